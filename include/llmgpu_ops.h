@@ -1,0 +1,48 @@
+/* Kernel-level C ABI of libllmgpu.so.
+ *
+ * These entry points run one hand-written sm_100a kernel on caller-owned device
+ * buffers (plain pointers, element strides, no framework types). They exist so
+ * that each kernel of the training step can be checked in isolation against the
+ * CPU oracle; the training step itself is driven through llmgpu.h.
+ *
+ * Conventions (shared with llmgpu.h): return 0 on success, a negative status on
+ * error; `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ * stream); every call is asynchronous on that stream.
+ */
+#ifndef LLMGPU_OPS_H
+#define LLMGPU_OPS_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* D[M,N] = A[M,K] * B[N,K]^T with bf16 operands and fp32 accumulation on the
+ * 5th-generation tensor cores. Replaces the fp32 contractions of
+ * Tensor::matmul (src/tensor.cpp:229-321) and the hand-written gradient loops
+ * (src/attention.cpp:234-241,322-334; src/transformer.cpp:129-181;
+ * src/model.cpp:249-270).
+ *   a_mn_major = 0: A is row-major [M][lda] (K contiguous); 1: A is [K][lda] (M contiguous)
+ *   b_mn_major = 0: B is row-major [N][ldb] (K contiguous); 1: B is [K][ldb] (N contiguous)
+ *   epi: 0 bf16 store, 1 f32 store (+= if accumulate), 2 f32 out = resid + acc,
+ *        3 gelu (aux = acc in bf16, out = gelu(acc) in bf16),
+ *        4 gelu backward (out = acc * gelu'(aux)) in bf16.
+ *   splits > 1 (epi 1 only) splits K; `workspace` must hold splits*M*N floats.
+ *   col_group/group_stride (epi 1): column n is written to
+ *        out + (n / col_group) * group_stride + m * ldo + n % col_group.
+ *   bn: tile width 64/128/256, 0 = automatic.
+ *   err: device int that receives a nonzero code if a device-side wait timed out. */
+int llmgpu_op_gemm(const void* A, long long lda, int a_mn_major, const void* B, long long ldb,
+                   int b_mn_major, int M, int N, int K, int epi, void* out, long long ldo,
+                   int accumulate, const float* resid, long long ldr, void* aux, long long ld_aux,
+                   int splits, float* workspace, int col_group, long long group_stride, int bn,
+                   int* err, void* stream);
+
+/* Number of SMs the library sizes persistent grids for (device 0 of the caller). */
+int llmgpu_op_num_sms(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

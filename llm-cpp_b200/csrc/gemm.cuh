@@ -1,0 +1,72 @@
+// Host-side interface of the tcgen05 GEMM used by every dense contraction of the
+// training step (projections, FFN, lm head, and all their gradients).
+//
+//   D[M,N] = A[M,K] * B[N,K]^T    (bf16 operands, fp32 accumulation in TMEM)
+//
+// A and B may each be stored K-major (row-major with K contiguous) or MN-major
+// (row-major with M/N contiguous), so that forward (x*W), data-gradient (dY*W^T)
+// and weight-gradient (X^T*dY) products all read the same bf16 buffers without
+// transposed copies.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace llmgpu {
+
+enum GemmEpilogue : int {
+    kEpiStoreBF16 = 0,   // out_bf16 = acc
+    kEpiStoreF32 = 1,    // out_f32 = acc (+ out_f32 if accumulate)
+    kEpiResidF32 = 2,    // out_f32 = resid + acc
+    kEpiGeluBF16 = 3,    // aux_bf16 = acc ; out_bf16 = gelu(acc)
+    kEpiDGeluBF16 = 4,   // out_bf16 = acc * gelu'(aux_bf16)
+    kEpiSplitPartial = 5 // out_f32[split][M][N] = partial acc (reduced by gemm_splitk_reduce)
+};
+
+struct GemmArgs {
+    int M, N, K;
+    int a_mn_major, b_mn_major;
+    int epi;
+    int accumulate;        // kEpiStoreF32: add into existing output
+    void* out;             // bf16 or f32
+    long long ldo;         // row stride of out (elements)
+    // Column grouping for f32 outputs: column n lands at
+    //   out + (n / col_group) * group_stride + m * ldo + (n % col_group)
+    // (used to write the gradients of adjacent same-shape parameters, e.g.
+    // Wq|Wk|Wv, from one GEMM). col_group == N disables grouping.
+    int col_group;
+    long long group_stride;
+    const float* resid;    // kEpiResidF32
+    long long ldr;
+    void* aux;             // bf16 pre-activation (written by Gelu, read by DGelu)
+    long long ld_aux;
+    int splits;            // >=1; kEpiSplitPartial writes `splits` partial planes
+    int* err;              // device error word
+};
+
+// Precomputed launch: tensor maps + args + tile config. Encoding tensor maps
+// costs host time, so the model builds one GemmPlan per call site at setup.
+struct GemmPlan {
+    CUtensorMap tmA;
+    CUtensorMap tmB;
+    GemmArgs args;
+    int bn;                // 64, 128 or 256
+    int grid;
+    size_t smem_bytes;
+};
+
+// Builds a plan. A is [M,K] (K-major, lda >= K) or [K,M] (MN-major, lda >= M);
+// B is [N,K] (K-major) or [K,N] (MN-major). Returns 0 on success.
+int gemm_make_plan(GemmPlan* plan, const void* A, long long lda, int a_mn_major, const void* B,
+                   long long ldb, int b_mn_major, int M, int N, int K, const GemmArgs& epi,
+                   int bn_hint, int num_sms);
+// Launches a plan on a stream.
+int gemm_run(const GemmPlan& plan, cudaStream_t stream);
+
+// Reduces split-K partials [splits][M][N] (fp32) into the final output with the
+// same epilogue options as kEpiStoreF32 (accumulate, column grouping).
+int gemm_splitk_reduce(const float* partial, int splits, int M, int N, float* out, long long ldo,
+                       int col_group, long long group_stride, int accumulate,
+                       cudaStream_t stream);
+
+}  // namespace llmgpu

@@ -1,0 +1,46 @@
+"""Loader for libllmgpu.so (built in-tree by `make -C llm-cpp_b200`).
+
+There is no fallback: if the shared library is missing, importing the binding
+raises, so a product path can never silently run on the CPU.
+"""
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+PKG_ROOT = os.path.abspath(os.path.join(_HERE, "..", ".."))
+LIB_PATH = os.path.join(PKG_ROOT, "libllmgpu.so")
+
+_lib = None
+
+c_int, c_ll, c_vp, c_float, c_size_t = (ctypes.c_int, ctypes.c_longlong, ctypes.c_void_p,
+                                       ctypes.c_float, ctypes.c_size_t)
+
+
+def _declare(lib):
+    lib.llmgpu_op_num_sms.argtypes = []
+    lib.llmgpu_op_num_sms.restype = c_int
+    lib.llmgpu_op_gemm.argtypes = [c_vp, c_ll, c_int, c_vp, c_ll, c_int, c_int, c_int, c_int,
+                                   c_int, c_vp, c_ll, c_int, c_vp, c_ll, c_vp, c_ll, c_int, c_vp,
+                                   c_int, c_ll, c_int, c_vp, c_vp]
+    lib.llmgpu_op_gemm.restype = c_int
+    try:
+        from . import _abi_decl
+        _abi_decl.declare(lib)
+    except ImportError:
+        pass
+
+
+def load(path=None):
+    """Load (once) and return the ctypes handle of libllmgpu.so."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    p = path or os.environ.get("LLMGPU_LIB", LIB_PATH)
+    if not os.path.exists(p):
+        raise FileNotFoundError(
+            f"libllmgpu.so not found at {p}; build it with `make -C llm-cpp_b200` "
+            "(there is no CPU fallback)")
+    lib = ctypes.CDLL(p)
+    _declare(lib)
+    _lib = lib
+    return lib
