@@ -1,0 +1,334 @@
+#!/usr/bin/env python3
+"""Training-step benchmark: GPT-2-small shape, train tokens/sec, MFU vs the measured bf16 peak.
+
+Workload (one step): 8 sequences x 1024 tokens per GPU of a 12-layer, n_embd 768, 12-head,
+GELU-FFN 3072, LayerNorm, learned positions, tied-embedding GPT with vocab 50257; seeded
+synthetic Zipf(1.1) token ids; forward -> cross-entropy -> backward -> clip -> AdamW
+(lr 3e-4, betas 0.9/0.95, wd 0.1). Data parallel over N GPUs (one process per GPU, NCCL
+gradient all-reduce), weak scaling (8 sequences per GPU).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`value` is the whole-job tokens/s with the token batches already resident in HBM
+(llmgpu_train_step_device); `e2e` is the same step through the public C ABI with host
+token buffers (host->device copy of the tokens and device->host read of loss/grad-norm
+inside every timed step). Timing: CUDA events on the library's stream, barrier +
+synchronize on both sides, max over ranks. The per-step working set (logits alone are
+0.82 GB) is far larger than the 126 MB L2, so no explicit L2 flush is needed.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "llm-cpp_b200", "python"))
+
+CFG = dict(vocab_size=50257, n_layers=12, n_heads=12, n_embd=768, block_size=1024,
+           weight_tying=True)
+B, T = 8, 1024
+HP = dict(lr=3e-4, b1=0.9, b2=0.95, eps=1e-8, wd=0.1)
+REF_T = 16          # tokens of the bounded CPU-reference sample (one sequence)
+PORT_T = 128        # tokens of the numpy-port CPU sample
+
+
+def algorithmic_flops_per_token(cfg=CFG, T=T):
+    """F_tok = 6*N_mm + 6*L*T*C (causal attention counted once; recompute not counted).
+    N_mm counts matmul weights incl. the lm head (tied or not), not the embeddings."""
+    C, L, V = cfg["n_embd"], cfg["n_layers"], cfg["vocab_size"]
+    F = 4 * C
+    n_mm = L * (4 * C * C + 2 * C * F) + C * V
+    return 6 * n_mm + 6 * L * T * C, n_mm
+
+
+def zipf_tokens(vocab, n, seed, s=1.1):
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    pk = np.arange(1, vocab + 1, dtype=np.float64) ** (-s)
+    pk /= pk.sum()
+    return rng.choice(vocab, size=n, p=pk).astype(np.int32)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), \
+            float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                                "sw_power_cap"], f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------ CPU baselines
+def ref_binary():
+    p = os.path.join(ROOT, "oracle", "_ref", "ref_step")
+    return p if os.path.exists(p) else None
+
+
+def run_reference_cpu(steps, T_sample):
+    """The unmodified reference train step (oracle/_ref/ref_step, built from the reference
+    sources) on the host cores: `steps` optimizer steps of one sequence of T_sample tokens,
+    reference initialisation, constant LR. Returns (seconds per step list, threads)."""
+    threads = os.cpu_count() or 1
+    with tempfile.TemporaryDirectory() as td:
+        env = dict(os.environ, OMP_NUM_THREADS=str(threads))
+        args = [ref_binary(), "-", "-", "1", str(T_sample), td, f"steps={steps}", "timing_only=1",
+                f"vocab={CFG['vocab_size']}", f"layers={CFG['n_layers']}",
+                f"heads={CFG['n_heads']}", f"embd={CFG['n_embd']}", f"block={CFG['block_size']}"]
+        args += [f"{k}={v}" for k, v in HP.items()]
+        subprocess.run(args, check=True, env=env, stdout=subprocess.DEVNULL,
+                       stderr=subprocess.DEVNULL)
+        with open(os.path.join(td, "timing.txt")) as f:
+            times = [float(x) for x in f.read().split()]
+    return times, threads
+
+
+def run_port_cpu(T_sample):
+    """numpy restatement of the reference step (oracle/gpt_oracle.py, fp32) on one sequence
+    of T_sample tokens of the same model: forward, backward, clip, AdamW. Returns seconds."""
+    import numpy as np
+    sys.path.insert(0, ROOT)
+    from oracle import gpt_oracle as go
+    cfg = go.Cfg(vocab=CFG["vocab_size"], n_layers=CFG["n_layers"], n_heads=CFG["n_heads"],
+                 n_embd=CFG["n_embd"], block_size=CFG["block_size"])
+    params = go.init_params(cfg, seed=1)
+    toks = zipf_tokens(cfg.vocab, T_sample, 7)
+    model = go.Model(cfg, params, dtype=np.float32)
+    st = go.AdamWState(**HP)
+    t0 = time.perf_counter()
+    go.train_step(model, [toks], st, clip=1.0)
+    return time.perf_counter() - t0
+
+
+# ------------------------------------------------------------------------------ reference arm
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    line = {"impl": "reference", "metric": "train_tokens_per_sec", "unit": "tokens/s",
+            "higher_is_better": True, "n_gpus": args.gpus, "data": "synthetic",
+            "dtype": "f32", "config": workload_config(args.gpus)}
+    if ref_binary() is None:
+        line["unavailable"] = "oracle/_ref/ref_step not built (needs the reference sources)"
+        print(json.dumps(line))
+        return 0
+    # One reference optimizer step over a single 16-token sequence of this model already
+    # takes ~80 s on 8 cores (naive single-threaded lm-head backward over V=50257 and an
+    # AdamW loop over 124M parameters), so the arm times at most 2 steps and no warm-up.
+    steps = max(1, min(args.steps, 2))
+    times, threads = run_reference_cpu(steps, REF_T)
+    per = sum(times) / len(times)
+    value = REF_T / per
+    sample = (f"{steps} reference optimizer step(s), each over 1 sequence of {REF_T} tokens of "
+              f"the full 12-layer/768/50257 model (warm-up skipped: one step takes {per:.0f} s)")
+    line.update({"value": value, "steps": steps, "warmup": 0, "ms_per_step": per * 1e3,
+                 "scaling": "weak", "vs_baseline": None,
+                 "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads,
+                                  "kind": "reference", "sample": sample},
+                 "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                         "d2h_bytes_per_step": 0}})
+    print(json.dumps(line))
+    return 0
+
+
+def workload_config(n):
+    return {"workload": "GPT-2-small train step (12L, n_embd 768, 12 heads, GELU FFN 3072, "
+                        "LayerNorm, learned pos, tied, vocab 50257), seq 1024, 8 seq/GPU",
+            "global_batch": 8 * n, "seq_len": T, "parallelism": f"dp{n}",
+            "tokens": "Zipf(1.1) synthetic ids, seeded",
+            "l2": "no flush: per-step working set (0.82 GB logits + 1.1 GB weights/state) >> L2"}
+
+
+# ------------------------------------------------------------------------------ our arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+
+    import numpy as np
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    uid = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+        from llmgpu.trainer import unique_id
+        obj = [unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        uid = obj[0]
+    from llmgpu.trainer import Trainer, make_config
+    cfg = make_config(**CFG)
+    tr = Trainer(cfg, B, T, rank=rank, world=world, uid=uid)
+    tr.set_adamw(**HP)
+    tr.set_train(grad_clip=1.0)
+    K, W = args.steps, args.warmup
+    toks = zipf_tokens(CFG["vocab_size"], (W + 2 * K) * B * T, 1234 + rank).reshape(-1, B, T)
+    stream = torch.cuda.ExternalStream(tr.stream())
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+
+    def maxed(x):
+        if not dist:
+            return x
+        t = torch.tensor([x], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for i in range(W):
+        tr.train_step(toks[i])
+    # ---------------- value: tokens resident in HBM
+    dev_toks = torch.from_numpy(toks[W:W + K].copy()).to(f"cuda:{local}")
+    step_bytes = B * T * 4
+    tr.set_profile(True)
+    tr.gemm_stats(reset=True)
+    sampler = ClockSampler(local)
+    sampler.start()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    launches = 0
+    for i in range(K):
+        tr.train_step_device(dev_toks[i].data_ptr(), B, T)
+        launches += tr.last_launches()
+    e1.record(stream)
+    barrier()
+    ms_dev = e0.elapsed_time(e1) / K
+    gflops, gms, glaunch = tr.gemm_stats(reset=True)
+    tr.set_profile(False)
+    # ---------------- e2e: host tokens through the public C ABI
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    losses = []
+    for i in range(K):
+        loss, gn, _ = tr.train_step(toks[W + K + i])
+        losses.append(loss)
+    e3.record(stream)
+    barrier()
+    clocks = sampler.stop()
+    ms_e2e = e2.elapsed_time(e3) / K
+    ms_dev, ms_e2e = maxed(ms_dev), maxed(ms_e2e)
+    timings = tr.last_timings()
+
+    peak, peak_sus, hbm, peak_kind = peaks()
+    f_tok, n_mm = algorithmic_flops_per_token()
+    tokens_step = world * B * T
+    value = tokens_step / (ms_dev / 1e3)
+    e2e = tokens_step / (ms_e2e / 1e3)
+    mfu = f_tok * value / (world * peak * 1e12)
+    gemm_tflops = gflops / (gms / 1e3) / 1e12 if gms > 0 else 0.0
+    if rank == 0:
+        line = {
+            "metric": "train_tokens_per_sec", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_dev,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic", "config": workload_config(world),
+            "mfu": {"value": mfu, "peak_tflops": peak, "peak": peak_kind,
+                    "flops_per_token": f_tok, "n_mm": n_mm},
+            "e2e": {"value": e2e, "unit": "tokens/s", "ms_per_step": ms_e2e,
+                    "h2d_bytes_per_step": step_bytes, "d2h_bytes_per_step": 32},
+            "gpu_launches": launches,
+            "roofline": {"kernel": "gemm_bf16_tc_kernel (tcgen05, all GEMMs of the step)",
+                         "bound": "tensor", "achieved": gemm_tflops, "peak": peak_sus,
+                         "unit": "TFLOP/s", "frac": gemm_tflops / peak_sus,
+                         "peak_kind": f"{peak_kind} sustained bf16 (kernel timed inside a long step)",
+                         "traffic": None, "launches_per_step": glaunch / max(K, 1),
+                         "gemm_ms_per_step": gms / max(K, 1),
+                         "flops_per_step": gflops / max(K, 1)},
+            "phase_ms": timings,
+            "clocks": clocks,
+            "loss_last": losses[-1],
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                secs = run_port_cpu(PORT_T)
+                line["cpu_baseline"] = {
+                    "value": PORT_T / secs, "unit": "tokens/s", "cores": os.cpu_count(),
+                    "kind": "port",
+                    "sample": f"numpy fp32 restatement (oracle/gpt_oracle.py) of one optimizer "
+                              f"step over 1 sequence of {PORT_T} tokens of the same model "
+                              f"({secs:.1f} s)"}
+            except Exception as ex:  # the baseline is reported, never fatal
+                line["cpu_baseline"] = {"value": None, "error": str(ex)[:200]}
+        print(json.dumps(line), flush=True)
+    tr.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -39,6 +39,32 @@ int llmgpu_op_gemm(const void* A, long long lda, int a_mn_major, const void* B, 
                    int splits, float* workspace, int col_group, long long group_stride, int bn,
                    int* err, void* stream);
 
+/* x[b*T+t,:] = wte[tok mod V,:] + wpe[t,:] in fp32 (src/model.cpp:149-157). */
+int llmgpu_op_embed(const int32_t* tokens, const float* wte, const float* wpe, float* x, int B,
+                    int T, int C, int V, void* stream);
+/* LayerNorm (rms=0, src/tensor.cpp:388-413) / RMSNorm (rms=1, :604-623): fp32 rows in,
+ * bf16 rows out, per-row mean and rstd saved. */
+int llmgpu_op_norm_fwd(const float* x, const float* gamma, const float* beta, void* y_bf16,
+                       float* mean, float* rstd, int rows, int C, int rms, void* stream);
+/* Norm backward (src/tensor.cpp:556-602 / :625-655): dx = resid + d/dx, written fp32 (and
+ * bf16 if dx_bf16 != NULL); dgamma, dbeta (nullable) and the column sums of dx (nullable)
+ * are written to their outputs. `work` must hold llmgpu_op_norm_bwd_work(rows, C) floats. */
+int llmgpu_op_norm_bwd(const float* dy, const float* x, const float* gamma, const float* mean,
+                       const float* rstd, const float* resid, float* dx, void* dx_bf16,
+                       float* dgamma, float* dbeta, float* dxsum, float* work, int rows, int C,
+                       int rms, void* stream);
+long long llmgpu_op_norm_bwd_work(int rows, int C);
+/* Fused softmax cross-entropy over bf16 logits [rows, Vp] (src/loss.cpp:6-40): per-row loss,
+ * logits overwritten by (softmax - y) * scale. */
+int llmgpu_op_cross_entropy(void* logits_bf16, int rows, int V, int Vp, const int32_t* tokens,
+                            float* row_loss, float scale, float smoothing, void* stream);
+/* Causal attention forward/backward over packed bf16 qkv [B*T, 3C]
+ * (src/attention.cpp:35-102, :183-363). dvec: B*H*T floats of scratch. */
+int llmgpu_op_attention_fwd(const void* qkv, void* out, float* lse, int B, int T, int H, int hd,
+                            void* stream);
+int llmgpu_op_attention_bwd(const void* qkv, const void* out, const void* dout, const float* lse,
+                            float* dvec, void* dqkv, int B, int T, int H, int hd, void* stream);
+
 /* Number of SMs the library sizes persistent grids for (device 0 of the caller). */
 int llmgpu_op_num_sms(void);
 

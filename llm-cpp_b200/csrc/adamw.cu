@@ -1,0 +1,171 @@
+// Global-norm clipping + non-finite guard + multi-tensor AdamW over one flat fp32
+// parameter arena, writing the bf16 shadow weights read by the GEMMs in the same pass.
+#include <cmath>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace llmgpu {
+
+namespace {
+
+constexpr int kNormBlocks = 592;  // 4 x 148 SMs
+constexpr int kNormThreads = 512;
+
+__global__ void __launch_bounds__(kNormThreads) grad_norm_kernel(const float* __restrict__ g,
+                                                                 long long n,
+                                                                 double* __restrict__ partial,
+                                                                 int* __restrict__ nonfinite) {
+    __shared__ double red[kNormThreads / 32];
+    float acc = 0.f;
+    int bad = 0;
+    const long long n4 = n >> 2;
+    const float4* g4 = reinterpret_cast<const float4*>(g);
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
+         i += (long long)gridDim.x * blockDim.x) {
+        float4 v = g4[i];
+        acc += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        bad |= !isfinite(v.x) | !isfinite(v.y) | !isfinite(v.z) | !isfinite(v.w);
+    }
+    for (long long i = (n4 << 2) + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        float v = g[i];
+        acc += v * v;
+        bad |= !isfinite(v);
+    }
+    double d = acc;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+    if (bad) atomicOr(nonfinite, 1);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = d;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0;
+        for (int w = 0; w < kNormThreads / 32; ++w) s += red[w];
+        partial[blockIdx.x] = s;
+    }
+}
+
+__global__ void grad_norm_final_kernel(const double* __restrict__ partial, int nblocks,
+                                       const int* __restrict__ nonfinite, float clip,
+                                       float* __restrict__ scal) {
+    __shared__ double red[32];
+    double s = 0;
+    for (int i = threadIdx.x; i < nblocks; i += blockDim.x) s += partial[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double tot = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
+        const double norm = sqrt(tot);
+        float sc = 1.0f;
+        if (norm > (double)clip && norm > 0) sc = clip / (float)norm;
+        scal[0] = (float)norm;
+        scal[1] = sc;
+        scal[2] = (float)(norm * (double)sc);
+        scal[3] = *nonfinite ? 1.0f : 0.0f;
+    }
+}
+
+__global__ void __launch_bounds__(256) adamw_kernel(const AdamParam* __restrict__ params,
+                                                    const AdamChunk* __restrict__ chunks,
+                                                    float* __restrict__ p,
+                                                    const float* __restrict__ g,
+                                                    float* __restrict__ m, float* __restrict__ v,
+                                                    const float* __restrict__ scal,
+                                                    const float* __restrict__ hp) {
+    if (scal[3] != 0.0f) return;  // non-finite gradient: the step is skipped
+    const AdamChunk ch = chunks[blockIdx.x];
+    const AdamParam pr = params[ch.param];
+    const float lr = hp[0], b1 = hp[1], b2 = hp[2], eps = hp[3], wd = hp[4];
+    const float c1 = hp[5], c2 = hp[6], gmul = hp[7] * scal[1];
+    const float decay = pr.decay ? lr * wd : 0.0f;
+    const long long base = pr.offset + ch.start;
+    for (int i = threadIdx.x; i < ch.len; i += blockDim.x) {
+        const long long e = base + i;
+        float pv = p[e];
+        const float gv = g[e] * gmul;
+        pv -= decay * pv;                                   // decoupled decay
+        float mv = b1 * m[e] + (1.0f - b1) * gv;
+        float vv = b2 * v[e] + (1.0f - b2) * gv * gv;
+        const float mhat = mv / c1, vhat = vv / c2;
+        pv -= lr * mhat / (sqrtf(vhat) + eps);
+        p[e] = pv;
+        m[e] = mv;
+        v[e] = vv;
+        if (pr.shadow) {
+            const long long k = ch.start + i;
+            long long off = k;
+            if (pr.shadow_ld != pr.cols) {
+                const long long r = k / pr.cols;
+                off = r * pr.shadow_ld + (k - r * pr.cols);
+            }
+            pr.shadow[off] = __float2bfloat16_rn(pv);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) shadow_kernel(const AdamParam* __restrict__ params,
+                                                     const AdamChunk* __restrict__ chunks,
+                                                     const float* __restrict__ p) {
+    const AdamChunk ch = chunks[blockIdx.x];
+    const AdamParam pr = params[ch.param];
+    if (!pr.shadow) return;
+    const long long base = pr.offset + ch.start;
+    for (int i = threadIdx.x; i < ch.len; i += blockDim.x) {
+        const long long k = ch.start + i;
+        long long off = k;
+        if (pr.shadow_ld != pr.cols) {
+            const long long r = k / pr.cols;
+            off = r * pr.shadow_ld + (k - r * pr.cols);
+        }
+        pr.shadow[off] = __float2bfloat16_rn(p[base + i]);
+    }
+}
+
+__global__ void scale_kernel(float* x, long long n, const float* scale) {
+    const float s = *scale;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x)
+        x[i] *= s;
+}
+
+}  // namespace
+
+int grad_norm_blocks() { return kNormBlocks; }
+
+int grad_norm_partials(const float* g, long long n, double* partial, int* nonfinite, int nblocks,
+                       cudaStream_t s) {
+    if (nblocks != kNormBlocks) return -1;
+    cudaMemsetAsync(nonfinite, 0, sizeof(int), s);
+    grad_norm_kernel<<<kNormBlocks, kNormThreads, 0, s>>>(g, n, partial, nonfinite);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int grad_norm_finalize(const double* partial, int nblocks, const int* nonfinite, float clip,
+                       float* scal, cudaStream_t s) {
+    grad_norm_final_kernel<<<1, 1024, 0, s>>>(partial, nblocks, nonfinite, clip, scal);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int adamw_update(const AdamParam* params, const AdamChunk* chunks, int nchunks, float* p,
+                 const float* g, float* m, float* v, const float* scal, const float* hp,
+                 cudaStream_t s) {
+    adamw_kernel<<<nchunks, 256, 0, s>>>(params, chunks, p, g, m, v, scal, hp);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int write_shadows(const AdamParam* params, const AdamChunk* chunks, int nchunks, const float* p,
+                  cudaStream_t s) {
+    shadow_kernel<<<nchunks, 256, 0, s>>>(params, chunks, p);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int scale_inplace(float* x, long long n, const float* scale, cudaStream_t s) {
+    scale_kernel<<<592, 256, 0, s>>>(x, n, scale);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+}  // namespace llmgpu

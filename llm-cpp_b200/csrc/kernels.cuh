@@ -1,0 +1,103 @@
+// Launchers of the memory-bound and attention kernels of the training step.
+// All launchers are asynchronous on `stream` and return 0 or a negative status.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace llmgpu {
+
+using bf16 = __nv_bfloat16;
+
+// ----------------------------------------------------------------- embedding
+// x[b*T+t, :] = wte[tok mod V, :] + wpe[t, :]   (src/model.cpp:149-157)
+int embed_forward(const int32_t* tokens, const float* wte, const float* wpe, float* x, int B,
+                  int T, int C, int V, cudaStream_t s);
+// Sorts (token mod V, row) pairs of the batch once per step so that the wte
+// gradient can be formed deterministically (each token's rows summed in row order).
+// `keys` holds n uint64 entries. n <= 16384.
+int embed_sort_keys(const int32_t* tokens, int n, int V, uint64_t* keys, cudaStream_t s);
+// wte_grad[tok, :] += dx[row, :] for every (tok,row) in sorted `keys`, and
+// wpe_grad[t, :] (+)= sum_b dx[b*T+t, :]   (src/model.cpp:314-322)
+int embed_backward(const uint64_t* keys, const float* dx, float* wte_grad, float* wpe_grad,
+                   int B, int T, int C, int accumulate_wpe, cudaStream_t s);
+
+// ----------------------------------------------------------------- norms
+// LayerNorm (rms=0, src/tensor.cpp:388-413) or RMSNorm (rms=1, :604-623) of fp32 rows into
+// bf16, saving mean (0 for RMSNorm) and rstd per row. beta may be null.
+int norm_forward(const float* x, const float* gamma, const float* beta, bf16* y, float* mean,
+                 float* rstd, int rows, int C, int rms, cudaStream_t s);
+// dx = resid_in + norm_backward(dy) (src/tensor.cpp:556-602 / :625-655), written as fp32
+// (dx_f32) and bf16 (dx_bf16, may be null). Per-CTA partial column sums are written to
+// `partial` [gridDim][3][C]: dgamma, dbeta, and the column sum of dx (used for the FFN
+// output-bias gradient of the block below). Returns the number of partial rows via *nparts.
+int norm_backward(const float* dy, const float* x, const float* gamma, const float* mean,
+                  const float* rstd, const float* resid_in, float* dx_f32, bf16* dx_bf16,
+                  float* partial, int rows, int C, int rms, int* nparts, cudaStream_t s);
+int norm_backward_grid(int rows);
+// out[j*C + c] (+)= sum_p partial[p][j][c] for the selected planes j (mask bit j set), out
+// pointers per plane (null = skip).
+int reduce_partials(const float* partial, int nparts, int C, float* out0, float* out1,
+                    float* out2, int accumulate, cudaStream_t s);
+// Column sums of a [rows, C] bf16 matrix into out (fp32, accumulate flag). Uses `work`
+// (>= colsum_work_floats(C) floats) for deterministic two-stage reduction.
+int colsum_bf16(const bf16* a, long long lda, int rows, int C, float* out, int accumulate,
+                float* work, cudaStream_t s);
+size_t colsum_work_floats(int C);
+
+// ----------------------------------------------------------------- cross-entropy
+// Per row of bf16 logits [rows, Vp] (first V columns valid): loss[row] = lse - logit[tgt],
+// and logits overwritten in place by dlogits = (softmax - y) * scale (0 in padded columns),
+// with y = 1 - smoothing at tgt and smoothing/(V-1) elsewhere (src/loss.cpp:6-40).
+// Targets are tokens mod V (the inputs themselves, src/trainer.cpp:39).
+int cross_entropy_fwd_bwd(bf16* logits, int rows, int V, int Vp, const int32_t* tokens,
+                          float* row_loss, float scale, float smoothing, cudaStream_t s);
+// out[0] = mean of v[0..n) (fixed summation order).
+int mean_reduce(const float* v, int n, float* out, cudaStream_t s);
+
+// ----------------------------------------------------------------- attention
+// Causal multi-head attention over qkv [B*T, 3C] bf16 (q | k | v, heads contiguous):
+// out [B*T, C] bf16, lse [B, H, T] fp32 (natural-log softmax normaliser of scaled scores).
+// src/attention.cpp:35-102 / src/flash_attention.cpp:88-123.
+int attention_forward(const bf16* qkv, bf16* out, float* lse, int B, int T, int H, int hd,
+                      cudaStream_t s);
+// Backward: dqkv [B*T, 3C] bf16 from dout [B*T, C]; dvec [B, H, T] fp32 scratch.
+// src/attention.cpp:183-363.
+int attention_backward(const bf16* qkv, const bf16* out, const bf16* dout, const float* lse,
+                       float* dvec, bf16* dqkv, int B, int T, int H, int hd, cudaStream_t s);
+
+// ----------------------------------------------------------------- optimizer
+struct AdamParam {
+    long long offset;    // into the flat fp32 buffers
+    long long numel;
+    int cols;            // row length of the parameter (for the bf16 shadow)
+    int decay;           // AdamW::default_decay (ndim > 1)
+    bf16* shadow;        // bf16 copy read by the GEMMs (null = none)
+    long long shadow_ld; // shadow row stride
+};
+struct AdamChunk {
+    int param;
+    int len;
+    long long start;     // element offset within the parameter
+};
+// Sum of squares (fp64 per block) and non-finite detection over n floats.
+int grad_norm_partials(const float* g, long long n, double* partial, int* nonfinite,
+                       int nblocks, cudaStream_t s);
+// Finalises: scal[0] = pre-clip norm, scal[1] = clip scale, scal[2] = post-clip norm,
+// scal[3] = 1 if the step must be skipped (non-finite). src/optimizer.cpp:90-101,
+// src/trainer.cpp:148-161.
+int grad_norm_finalize(const double* partial, int nblocks, const int* nonfinite, float clip,
+                       float* scal, cudaStream_t s);
+int grad_norm_blocks();
+// AdamW over all parameters (src/optimizer.cpp:54-89), skipped when scal[3] != 0.
+// hp: {lr, b1, b2, eps, wd, 1-b1^t, 1-b2^t, grad_mul}
+int adamw_update(const AdamParam* params, const AdamChunk* chunks, int nchunks, float* p,
+                 const float* g, float* m, float* v, const float* scal, const float* hp,
+                 cudaStream_t s);
+// Writes the bf16 shadows of all parameters from the fp32 master copy.
+int write_shadows(const AdamParam* params, const AdamChunk* chunks, int nchunks, const float* p,
+                  cudaStream_t s);
+// Multiplies n floats by a device scalar in place.
+int scale_inplace(float* x, long long n, const float* scale, cudaStream_t s);
+
+}  // namespace llmgpu

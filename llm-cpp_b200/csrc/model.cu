@@ -1,0 +1,1008 @@
+// Device-resident GPT training step: parameter arena, activations, forward/backward
+// orchestration over the sm_100a kernels, optimizer, checkpoints.
+//
+// Reference path (sergiorandria/llm-cpp): GPT::forward_with_hidden (src/model.cpp:144-171),
+// cross-entropy (src/loss.cpp:6-40), GPT::backward (src/model.cpp:175-323) through
+// TransformerBlock::backward (src/transformer.cpp:225-269), clip_by_global_norm and AdamW
+// (src/optimizer.cpp:53-101), orchestrated like Trainer::train_step_accum
+// (src/trainer.cpp:127-169).
+//
+// Differences of method (not of result): no recomputation (activations are kept), all B
+// sequences of a step form one [B*T, C] activation matrix, GEMMs take bf16 operands with
+// fp32 accumulation, and the weight gradients of a step are formed once for the whole batch.
+#include <nccl.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fcntl.h>
+#include <fstream>
+#include <random>
+#include <unistd.h>
+
+#include "model.h"
+
+namespace llmgpu {
+
+namespace {
+
+#define CK(x)                                                                  \
+    do {                                                                       \
+        cudaError_t e_ = (x);                                                  \
+        if (e_ != cudaSuccess) {                                               \
+            c->err = std::string(#x) + ": " + cudaGetErrorString(e_);          \
+            return LLMGPU_E_CUDA;                                              \
+        }                                                                      \
+    } while (0)
+#define KC(x)                                                                  \
+    do {                                                                       \
+        int r_ = (x);                                                          \
+        if (r_ != 0) {                                                         \
+            c->err = std::string(#x) + " failed with status " + std::to_string(r_); \
+            return LLMGPU_E_CUDA;                                              \
+        }                                                                      \
+        c->launches++;                                                         \
+    } while (0)
+
+inline int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+void add_param(Ctx* c, const std::string& name, std::vector<int64_t> shape) {
+    Param p;
+    p.name = name;
+    p.shape = shape;
+    p.numel = 1;
+    for (auto d : shape) p.numel *= d;
+    p.decay = shape.size() > 1 ? 1 : 0;  // AdamW::default_decay (include/llm/optimizer.h:70-72)
+    p.cols = (int)shape.back();
+    p.offset = c->n_floats;
+    c->n_floats = align_up(c->n_floats + p.numel, 64);
+    c->params.push_back(p);
+}
+
+// GPT::parameters() order (src/model.cpp:889-909), blocks per TransformerBlock::parameters
+// (src/transformer.cpp:279-290) or MambaBlock::parameters (src/mamba.cpp:415-420).
+void build_params(Ctx* c) {
+    const auto& k = c->cfg;
+    const int C = k.n_embd, V = k.vocab_size;
+    c->i_wte = (int)c->params.size();
+    add_param(c, "wte", {V, C});
+    c->i_wpe = (int)c->params.size();
+    add_param(c, "wpe", {k.block_size, C});
+    c->i_lnfg = (int)c->params.size();
+    add_param(c, "ln_f_gamma", {C});
+    c->i_lnfb = (int)c->params.size();
+    add_param(c, "ln_f_beta", {C});
+    if (!k.weight_tying) {
+        c->i_lm = (int)c->params.size();
+        add_param(c, "lm_head", {C, V});
+    }
+    for (int l = 0; l < k.n_layers; ++l) {
+        BlockIdx b;
+        const std::string p = "blk" + std::to_string(l) + ".";
+        auto idx = [&]() { return (int)c->params.size(); };
+        if (k.use_mamba) {
+            const int D = k.d_inner ? k.d_inner : 2 * C;
+            const int N = k.d_state;
+            const int R = k.dt_rank ? k.dt_rank : (C + 15) / 16;
+            const int K = k.conv_kernel;
+            b.norm_w = idx(); add_param(c, p + "norm_w", {C});
+            b.in_proj = idx(); add_param(c, p + "in_proj", {2 * D, C});
+            b.conv_w = idx(); add_param(c, p + "conv_w", {D, 1, K});
+            b.conv_b = idx(); add_param(c, p + "conv_b", {D});
+            b.x_proj = idx(); add_param(c, p + "x_proj", {R + 2 * N, D});
+            b.dt_proj = idx(); add_param(c, p + "dt_proj", {D, R});
+            b.a_log = idx(); add_param(c, p + "a_log", {D, N});
+            b.dskip = idx(); add_param(c, p + "d", {D});
+            b.out_proj = idx(); add_param(c, p + "out_proj", {C, D});
+        } else {
+            b.Wq = idx(); add_param(c, p + "Wq", {C, C});
+            b.Wk = idx(); add_param(c, p + "Wk", {C, C});
+            b.Wv = idx(); add_param(c, p + "Wv", {C, C});
+            b.Wo = idx(); add_param(c, p + "Wo", {C, C});
+            if (k.moe_experts > 0) {
+                const int E = k.moe_experts, Hd = 4 * C;
+                b.gate = idx(); add_param(c, p + "gate", {C, E});
+                b.W1e = idx(); add_param(c, p + "W1e", {E, C, Hd});
+                b.W2e = idx(); add_param(c, p + "W2e", {E, Hd, C});
+            } else {
+                const int F = c->F;
+                b.W1 = idx(); add_param(c, p + "W1", {C, F});
+                b.W2 = idx(); add_param(c, p + "W2", {F, C});
+                if (k.ffn_swiglu) { b.W3 = idx(); add_param(c, p + "W3", {C, F}); }
+                b.b1 = idx(); add_param(c, p + "b1", {F});
+                b.b2 = idx(); add_param(c, p + "b2", {C});
+            }
+            b.ln1g = idx(); add_param(c, p + "ln1_gamma", {C});
+            b.ln1b = idx(); add_param(c, p + "ln1_beta", {C});
+            b.ln2g = idx(); add_param(c, p + "ln2_gamma", {C});
+            b.ln2b = idx(); add_param(c, p + "ln2_beta", {C});
+        }
+        c->blocks.push_back(b);
+    }
+}
+
+// Host-side initialisation exactly like the reference constructors: every randn tensor
+// draws from a fresh std::mt19937(42) (src/tensor.cpp:147-156), gains 1, biases 0.
+void reference_init(Ctx* c, std::vector<float>& host) {
+    host.assign((size_t)c->n_floats, 0.0f);
+    auto randn = [&](int i, float stdv) {
+        std::mt19937 rng(42);
+        std::normal_distribution<float> dist(0.0f, stdv);
+        float* d = host.data() + c->params[i].offset;
+        for (int64_t j = 0; j < c->params[i].numel; ++j) d[j] = dist(rng);
+    };
+    auto fill = [&](int i, float v) {
+        float* d = host.data() + c->params[i].offset;
+        for (int64_t j = 0; j < c->params[i].numel; ++j) d[j] = v;
+    };
+    const auto& k = c->cfg;
+    randn(c->i_wte, 0.02f);
+    randn(c->i_wpe, 0.02f);
+    fill(c->i_lnfg, 1.0f);
+    if (c->i_lm >= 0) randn(c->i_lm, 0.02f);
+    for (auto& b : c->blocks) {
+        if (k.use_mamba) {
+            const int C = k.n_embd;
+            const int D = (int)c->params[b.in_proj].shape[0] / 2;
+            const int K = k.conv_kernel;
+            fill(b.norm_w, 1.0f);
+            randn(b.in_proj, 1.0f / std::sqrt((float)C));
+            randn(b.conv_w, 1.0f / std::sqrt((float)(D * K)));
+            randn(b.x_proj, 1.0f / std::sqrt((float)D));
+            randn(b.dt_proj, 0.001f);
+            fill(b.a_log, -1.0f);
+            fill(b.dskip, 1.0f);
+            // out_proj_weight_ is not randn'd by the reference constructor (src/mamba.cpp:26-34)
+        } else {
+            randn(b.Wq, 0.02f);
+            randn(b.Wk, 0.02f);
+            randn(b.Wv, 0.02f);
+            randn(b.Wo, 0.02f);
+            if (b.gate >= 0) {
+                randn(b.gate, 0.02f);
+                // experts: each W1/W2 is its own randn(0,0.02) from seed 42 (src/moe.cpp:8-22)
+                const int E = k.moe_experts;
+                const int64_t per1 = c->params[b.W1e].numel / E, per2 = c->params[b.W2e].numel / E;
+                for (int e = 0; e < E; ++e) {
+                    std::mt19937 r1(42), r2(42);
+                    std::normal_distribution<float> d1(0.0f, 0.02f), d2(0.0f, 0.02f);
+                    float* w1 = host.data() + c->params[b.W1e].offset + e * per1;
+                    float* w2 = host.data() + c->params[b.W2e].offset + e * per2;
+                    for (int64_t j = 0; j < per1; ++j) w1[j] = d1(r1);
+                    for (int64_t j = 0; j < per2; ++j) w2[j] = d2(r2);
+                }
+            } else {
+                randn(b.W1, 0.02f);
+                randn(b.W2, 0.02f);
+                if (b.W3 >= 0) randn(b.W3, 0.02f);
+            }
+            fill(b.ln1g, 1.0f);
+            fill(b.ln2g, 1.0f);
+        }
+    }
+}
+
+int choose_splits(Ctx* c, int M, int N, int K) {
+    const int bn = N >= 256 ? 256 : 128;
+    const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+    const int kb = (K + 63) / 64;
+    int best_s = 1;
+    double best = 1e30;
+    const int cand[6] = {1, 2, 3, 4, 6, 8};
+    for (int i = 0; i < 6; ++i) {
+        const int s = cand[i];
+        if (s > 1 && kb / s < 4) break;
+        const double waves = std::ceil((double)tiles * s / c->num_sms);
+        const double cost = waves * ((double)kb / s + 4.0) + (s > 1 ? 2.0 : 0.0);
+        if (cost < best - 1e-9) {
+            best = cost;
+            best_s = s;
+        }
+    }
+    return best_s;
+}
+
+// GEMM through the per-call-site plan cache.
+int gemm(Ctx* c, const void* A, long long lda, int amn, const void* B, long long ldb, int bmn,
+         int M, int N, int K, GemmArgs a, int splits = 1) {
+    a.err = c->d_err;
+    a.splits = 1;
+    void* final_out = a.out;
+    const long long final_ldo = a.ldo;
+    if (splits > 1) {
+        if ((size_t)splits * M * N > c->splitws_floats) splits = (int)(c->splitws_floats / ((size_t)M * N));
+        if (splits < 2) splits = 1;
+    }
+    if (splits > 1) {
+        a.epi = kEpiSplitPartial;
+        a.out = c->splitws;
+        a.ldo = N;
+        a.splits = splits;
+    }
+    struct Key {
+        const void *A, *B;
+        long long lda, ldb;
+        int amn, bmn, M, N, K;
+        GemmArgs args;
+    } key;
+    std::memset(&key, 0, sizeof(key));
+    key.A = A;
+    key.B = B;
+    key.lda = lda;
+    key.ldb = ldb;
+    key.amn = amn;
+    key.bmn = bmn;
+    key.M = M;
+    key.N = N;
+    key.K = K;
+    key.args = a;
+    std::vector<uint8_t> kb(sizeof(Key));
+    std::memcpy(kb.data(), &key, sizeof(Key));
+    const size_t i = c->plan_cursor++;
+    if (i >= c->plan_cache.size()) {
+        c->plan_cache.resize(i + 1);
+        c->plan_keys.resize(i + 1);
+    }
+    if (c->plan_keys[i] != kb) {
+        int rc = gemm_make_plan(&c->plan_cache[i], A, lda, amn, B, ldb, bmn, M, N, K, a, 0,
+                                c->num_sms);
+        if (rc) {
+            c->err = "gemm_make_plan failed (" + std::to_string(rc) + ") M=" + std::to_string(M) +
+                     " N=" + std::to_string(N) + " K=" + std::to_string(K);
+            c->plan_keys[i].clear();
+            return LLMGPU_E_ARG;
+        }
+        c->plan_keys[i] = kb;
+    }
+    if (c->profile) {
+        if (c->prof_ev.size() < 2 * (c->prof_n + 1)) {
+            cudaEvent_t e0, e1;
+            cudaEventCreate(&e0);
+            cudaEventCreate(&e1);
+            c->prof_ev.push_back(e0);
+            c->prof_ev.push_back(e1);
+            c->prof_flops.push_back(0);
+        }
+        c->prof_flops[c->prof_n] = 2.0 * M * N * (double)K;
+        cudaEventRecord(c->prof_ev[2 * c->prof_n], c->stream);
+    }
+    KC(gemm_run(c->plan_cache[i], c->stream));
+    if (c->profile) {
+        cudaEventRecord(c->prof_ev[2 * c->prof_n + 1], c->stream);
+        c->prof_n++;
+    }
+    if (splits > 1) {
+        KC(gemm_splitk_reduce(c->splitws, splits, M, N, reinterpret_cast<float*>(final_out),
+                              final_ldo, a.col_group > 0 ? a.col_group : N, a.group_stride,
+                              a.accumulate, c->stream));
+    }
+    return 0;
+}
+
+GemmArgs epi_args(int epi, void* out, long long ldo) {
+    GemmArgs a{};
+    a.epi = epi;
+    a.out = out;
+    a.ldo = ldo;
+    a.splits = 1;
+    return a;
+}
+
+template <typename T>
+int dalloc(Ctx* c, T** p, size_t n) {
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), n * sizeof(T) + 256);
+    if (e != cudaSuccess) {
+        c->err = std::string("cudaMalloc: ") + cudaGetErrorString(e);
+        return LLMGPU_E_CUDA;
+    }
+    // ordered on the context stream (a legacy-stream memset would not be ordered with it)
+    cudaMemsetAsync(*p, 0, n * sizeof(T), c->stream);
+    return 0;
+}
+
+}  // namespace
+
+// Host<->device copies ordered on the context stream and completed before returning.
+// (A plain cudaMemcpy runs on the legacy stream, which the context's non-blocking streams
+// do not wait for, and from pageable memory it may return before the DMA has landed.)
+int copy_sync(Ctx* c, void* dst, const void* src, size_t bytes, cudaMemcpyKind kind) {
+    if (bytes == 0) return 0;
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, kind, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) {
+        c->err = std::string("copy: ") + cudaGetErrorString(e);
+        return LLMGPU_E_CUDA;
+    }
+    return 0;
+}
+
+// ---------------------------------------------------------------------------- shadows
+void refresh_shadows(Ctx* c) {
+    write_shadows(c->d_aparams, c->d_chunks, c->nchunks, c->p, c->stream);
+}
+
+// ---------------------------------------------------------------------------- create
+Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, int world,
+                const void* uid, std::string* errout) {
+    auto fail = [&](Ctx* c, const std::string& m) -> Ctx* {
+        *errout = m.empty() ? c->err : m;
+        ctx_destroy(c);
+        return nullptr;
+    };
+    Ctx* c = new Ctx();
+    c->cfg = cfg;
+    c->rank = rank;
+    c->world = world;
+    if (cfg.vocab_size <= 0 || cfg.n_layers <= 0 || cfg.n_embd <= 0 || cfg.block_size <= 0 ||
+        max_batch <= 0 || max_seq <= 0 || max_seq > cfg.block_size)
+        return fail(c, "invalid configuration");
+    if (!cfg.use_mamba && (cfg.n_heads <= 0 || cfg.n_embd % cfg.n_heads != 0))
+        return fail(c, "n_heads must divide n_embd");  // src/config.cpp:39-68
+    c->C = cfg.n_embd;
+    c->V = cfg.vocab_size;
+    c->Vp = (int)align_up(c->V, 128);
+    c->L = cfg.n_layers;
+    c->H = cfg.use_mamba ? 1 : cfg.n_heads;
+    c->hd = c->C / c->H;
+    c->F = cfg.ffn_hidden > 0 ? cfg.ffn_hidden : 4 * c->C;
+    c->max_b = max_batch;
+    c->max_t = max_seq;
+    c->max_bt = max_batch * max_seq;
+    if (cfg.use_mamba || cfg.moe_experts > 0 || cfg.ffn_swiglu || cfg.rope_qk)
+        return fail(c, "configuration not supported yet by the device kernels");
+    if (c->hd != 32 && c->hd != 64) return fail(c, "head_dim must be 32 or 64");
+    if (c->C % 32 != 0 || c->F % 32 != 0) return fail(c, "n_embd and ffn hidden must be multiples of 32");
+    if (c->max_bt > 16384) return fail(c, "at most 16384 tokens per micro-batch");
+
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return fail(c, "no CUDA device");
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return fail(c, "no CUDA device");
+    if (prop.major != 10) return fail(c, "requires an sm_100 (B200) device");
+    c->device = dev;
+    c->num_sms = prop.multiProcessorCount;
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) != cudaSuccess)
+        return fail(c, "stream creation failed");
+    cudaEventCreateWithFlags(&c->ev_keys, cudaEventDisableTiming);
+    for (auto& e : c->ev) cudaEventCreate(&e);
+
+    build_params(c);
+    const int C = c->C, F = c->F, BT = c->max_bt, L = c->L;
+    if (dalloc(c, &c->p, c->n_floats) || dalloc(c, &c->g, c->n_floats) ||
+        dalloc(c, &c->m, c->n_floats) || dalloc(c, &c->v, c->n_floats))
+        return fail(c, "");
+
+    // bf16 shadows laid out for the GEMMs
+    size_t sh = (size_t)c->Vp * C;                            // wte16 [Vp, C]
+    if (!cfg.weight_tying) sh += (size_t)C * c->Vp;           // lm16 [C, Vp]
+    sh += (size_t)L * ((size_t)C * 3 * C + (size_t)C * C + 2 * (size_t)C * F + 64 * 4);
+    c->shadow_elems = sh;
+    if (dalloc(c, &c->shadow_arena, sh)) return fail(c, "");
+    {
+        bf16* q = c->shadow_arena;
+        auto take = [&](size_t n) {
+            bf16* r = q;
+            q += align_up((int64_t)n, 64);
+            return r;
+        };
+        c->wte16 = take((size_t)c->Vp * C);
+        c->params[c->i_wte].shadow = c->wte16;
+        c->params[c->i_wte].shadow_ld = C;
+        if (!cfg.weight_tying) {
+            c->lm16 = take((size_t)C * c->Vp);
+            c->params[c->i_lm].shadow = c->lm16;
+            c->params[c->i_lm].shadow_ld = c->Vp;
+        }
+        for (int l = 0; l < L; ++l) {
+            auto& b = c->blocks[l];
+            bf16* wqkv = take((size_t)C * 3 * C);
+            bf16* wo = take((size_t)C * C);
+            bf16* w1 = take((size_t)C * F);
+            bf16* w2 = take((size_t)F * C);
+            c->wqkv16.push_back(wqkv);
+            c->wo16.push_back(wo);
+            c->w1_16.push_back(w1);
+            c->w2_16.push_back(w2);
+            c->params[b.Wq].shadow = wqkv;
+            c->params[b.Wk].shadow = wqkv + C;
+            c->params[b.Wv].shadow = wqkv + 2 * C;
+            c->params[b.Wq].shadow_ld = c->params[b.Wk].shadow_ld = c->params[b.Wv].shadow_ld = 3 * C;
+            c->params[b.Wo].shadow = wo;
+            c->params[b.Wo].shadow_ld = C;
+            c->params[b.W1].shadow = w1;
+            c->params[b.W1].shadow_ld = F;
+            c->params[b.W2].shadow = w2;
+            c->params[b.W2].shadow_ld = C;
+        }
+    }
+
+    // activations
+    c->act.resize(L);
+    const int nparts = norm_backward_grid(BT);
+    for (int l = 0; l < L; ++l) {
+        auto& a = c->act[l];
+        if (dalloc(c, &a.x, (size_t)BT * C) || dalloc(c, &a.y, (size_t)BT * C) ||
+            dalloc(c, &a.ln1, (size_t)BT * C) || dalloc(c, &a.mean1, BT) ||
+            dalloc(c, &a.rstd1, BT) || dalloc(c, &a.qkv, (size_t)BT * 3 * C) ||
+            dalloc(c, &a.att, (size_t)BT * C) || dalloc(c, &a.lse, (size_t)BT * c->H) ||
+            dalloc(c, &a.ln2, (size_t)BT * C) || dalloc(c, &a.mean2, BT) ||
+            dalloc(c, &a.rstd2, BT) || dalloc(c, &a.h, (size_t)BT * F) ||
+            dalloc(c, &a.act, (size_t)BT * F))
+            return fail(c, "");
+    }
+    if (dalloc(c, &c->xL, (size_t)BT * C) || dalloc(c, &c->lnf, (size_t)BT * C) ||
+        dalloc(c, &c->meanf, BT) || dalloc(c, &c->rstdf, BT) ||
+        dalloc(c, &c->logits, (size_t)BT * c->Vp) || dalloc(c, &c->dres, (size_t)BT * C) ||
+        dalloc(c, &c->dy, (size_t)BT * C) || dalloc(c, &c->dln, (size_t)BT * C) ||
+        dalloc(c, &c->dres16, (size_t)BT * C) || dalloc(c, &c->dy16, (size_t)BT * C) ||
+        dalloc(c, &c->datt, (size_t)BT * C) || dalloc(c, &c->dqkv, (size_t)BT * 3 * C) ||
+        dalloc(c, &c->dh, (size_t)BT * F) || dalloc(c, &c->dvec, (size_t)BT * c->H) ||
+        dalloc(c, &c->partial, (size_t)nparts * 3 * C) ||
+        dalloc(c, &c->colwork, colsum_work_floats(F > C ? F : C)))
+        return fail(c, "");
+    c->splitws_floats = (size_t)8 * C * (F > 3 * C ? F : 3 * C);
+    if (dalloc(c, &c->splitws, c->splitws_floats)) return fail(c, "");
+    if (dalloc(c, &c->d_tokens, BT) || dalloc(c, &c->d_keys, BT) ||
+        dalloc(c, &c->d_row_loss, BT) || dalloc(c, &c->d_out, 8) || dalloc(c, &c->d_hp, 8) ||
+        dalloc(c, &c->d_normpart, grad_norm_blocks()) || dalloc(c, &c->d_nonfinite, 1) ||
+        dalloc(c, &c->d_err, 1) || dalloc(c, &c->d_kscale, 1))
+        return fail(c, "");
+    if (cudaMallocHost(&c->h_tokens, sizeof(int32_t) * BT) != cudaSuccess ||
+        cudaMallocHost(&c->h_out, sizeof(float) * 8) != cudaSuccess ||
+        cudaMallocHost(&c->h_hp, sizeof(float) * 8) != cudaSuccess ||
+        cudaMallocHost(&c->h_err, sizeof(int)) != cudaSuccess)
+        return fail(c, "cudaMallocHost failed");
+
+    // optimizer tables
+    {
+        std::vector<AdamParam> ap;
+        std::vector<AdamChunk> ch;
+        const int64_t CH = 16384;
+        for (size_t i = 0; i < c->params.size(); ++i) {
+            const auto& p = c->params[i];
+            AdamParam a{};
+            a.offset = p.offset;
+            a.numel = p.numel;
+            a.cols = p.cols;
+            a.decay = p.decay;
+            a.shadow = p.shadow;
+            a.shadow_ld = p.shadow ? p.shadow_ld : p.cols;
+            ap.push_back(a);
+            for (int64_t s = 0; s < p.numel; s += CH) {
+                AdamChunk k{};
+                k.param = (int)i;
+                k.start = s;
+                k.len = (int)std::min<int64_t>(CH, p.numel - s);
+                ch.push_back(k);
+            }
+        }
+        c->nchunks = (int)ch.size();
+        if (dalloc(c, &c->d_aparams, ap.size()) || dalloc(c, &c->d_chunks, ch.size()))
+            return fail(c, "");
+        if (copy_sync(c, c->d_aparams, ap.data(), ap.size() * sizeof(AdamParam), cudaMemcpyHostToDevice) ||
+            copy_sync(c, c->d_chunks, ch.data(), ch.size() * sizeof(AdamChunk), cudaMemcpyHostToDevice))
+            return fail(c, "");
+    }
+
+    // parameters initialised like the reference constructors
+    {
+        std::vector<float> host;
+        reference_init(c, host);
+        if (copy_sync(c, c->p, host.data(), host.size() * sizeof(float), cudaMemcpyHostToDevice))
+            return fail(c, "");
+        refresh_shadows(c);
+    }
+
+    if (world > 1) {
+        ncclUniqueId id;
+        std::memcpy(&id, uid, sizeof(id));
+        ncclComm_t comm;
+        ncclResult_t r = ncclCommInitRank(&comm, world, id, rank);
+        if (r != ncclSuccess) return fail(c, std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
+        c->nccl = comm;
+    }
+    if (cudaDeviceSynchronize() != cudaSuccess) return fail(c, "device error during setup");
+    return c;
+}
+
+void ctx_destroy(Ctx* c) {
+    if (!c) return;
+    cudaDeviceSynchronize();
+    if (c->graph) cudaGraphExecDestroy(c->graph);
+    if (c->nccl) ncclCommDestroy(reinterpret_cast<ncclComm_t>(c->nccl));
+    auto F = [](void* p) {
+        if (p) cudaFree(p);
+    };
+    F(c->p); F(c->g); F(c->m); F(c->v); F(c->shadow_arena);
+    for (auto& a : c->act) {
+        F(a.x); F(a.y); F(a.ln1); F(a.mean1); F(a.rstd1); F(a.qkv); F(a.att); F(a.lse);
+        F(a.ln2); F(a.mean2); F(a.rstd2); F(a.h); F(a.act);
+    }
+    F(c->xL); F(c->lnf); F(c->meanf); F(c->rstdf); F(c->logits); F(c->dres); F(c->dy);
+    F(c->dln); F(c->dres16); F(c->dy16); F(c->datt); F(c->dqkv); F(c->dh); F(c->dvec);
+    F(c->partial); F(c->colwork); F(c->splitws); F(c->d_tokens); F(c->d_keys);
+    F(c->d_row_loss); F(c->d_out); F(c->d_hp); F(c->d_normpart); F(c->d_nonfinite); F(c->d_err);
+    F(c->d_aparams); F(c->d_chunks); F(c->d_kscale);
+    if (c->h_tokens) cudaFreeHost(c->h_tokens);
+    if (c->h_out) cudaFreeHost(c->h_out);
+    if (c->h_hp) cudaFreeHost(c->h_hp);
+    if (c->h_err) cudaFreeHost(c->h_err);
+    if (c->ev_keys) cudaEventDestroy(c->ev_keys);
+    for (auto& e : c->ev)
+        if (e) cudaEventDestroy(e);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    if (c->side) cudaStreamDestroy(c->side);
+    delete c;
+}
+
+// ---------------------------------------------------------------------------- step
+int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
+    const int C = c->C, F = c->F, H = c->H, hd = c->hd, L = c->L, V = c->V, Vp = c->Vp;
+    const int BT = B * T;
+    const int rms = c->cfg.use_rmsnorm;
+    const bool tied = c->cfg.weight_tying != 0;
+    cudaStream_t s = c->stream;
+    float* G = c->g;
+    auto gp = [&](int i) { return G + c->params[i].offset; };
+    auto pp = [&](int i) { return c->p + c->params[i].offset; };
+
+    cudaEventRecord(c->ev[0], s);
+    // deterministic token sort for the embedding backward, overlapped on the side stream
+    if (backward) {
+        CK(cudaEventRecord(c->ev_keys, s));
+        CK(cudaStreamWaitEvent(c->side, c->ev_keys, 0));
+        int rc = embed_sort_keys(c->d_tokens, BT, V, c->d_keys, c->side);
+        if (rc) { c->err = "embed_sort_keys"; return LLMGPU_E_CUDA; }
+        c->launches++;
+        CK(cudaEventRecord(c->ev_keys, c->side));
+    }
+    // ------------------------------------------------------------------ forward
+    KC(embed_forward(c->d_tokens, pp(c->i_wte), pp(c->i_wpe), c->act[0].x, B, T, C, V, s));
+    for (int l = 0; l < L; ++l) {
+        auto& a = c->act[l];
+        auto& b = c->blocks[l];
+        float* xnext = (l + 1 < L) ? c->act[l + 1].x : c->xL;
+        KC(norm_forward(a.x, pp(b.ln1g), pp(b.ln1b), a.ln1, a.mean1, a.rstd1, BT, C, rms, s));
+        int rc = gemm(c, a.ln1, C, 0, c->wqkv16[l], 3 * C, 1, BT, 3 * C, C,
+                      epi_args(kEpiStoreBF16, a.qkv, 3 * C));
+        if (rc) return rc;
+        KC(attention_forward(a.qkv, a.att, a.lse, B, T, H, hd, s));
+        GemmArgs r = epi_args(kEpiResidF32, a.y, C);
+        r.resid = a.x;
+        r.ldr = C;
+        if ((rc = gemm(c, a.att, C, 0, c->wo16[l], C, 1, BT, C, C, r))) return rc;
+        KC(norm_forward(a.y, pp(b.ln2g), pp(b.ln2b), a.ln2, a.mean2, a.rstd2, BT, C, rms, s));
+        GemmArgs ge = epi_args(kEpiGeluBF16, a.act, F);
+        ge.aux = a.h;
+        ge.ld_aux = F;
+        if ((rc = gemm(c, a.ln2, C, 0, c->w1_16[l], F, 1, BT, F, C, ge))) return rc;
+        GemmArgs r2 = epi_args(kEpiResidF32, xnext, C);
+        r2.resid = a.y;
+        r2.ldr = C;
+        if ((rc = gemm(c, a.act, F, 0, c->w2_16[l], C, 1, BT, C, F, r2))) return rc;
+    }
+    KC(norm_forward(c->xL, pp(c->i_lnfg), pp(c->i_lnfb), c->lnf, c->meanf, c->rstdf, BT, C, rms, s));
+    {
+        int rc;
+        if (tied)
+            rc = gemm(c, c->lnf, C, 0, c->wte16, C, 0, BT, Vp, C,
+                      epi_args(kEpiStoreBF16, c->logits, Vp));
+        else
+            rc = gemm(c, c->lnf, C, 0, c->lm16, Vp, 1, BT, Vp, C,
+                      epi_args(kEpiStoreBF16, c->logits, Vp));
+        if (rc) return rc;
+    }
+    cudaEventRecord(c->ev[1], s);
+    // ------------------------------------------------------------------ loss
+    KC(cross_entropy_fwd_bwd(c->logits, BT, V, Vp, c->d_tokens, c->d_row_loss, 1.0f / (float)BT,
+                             c->smoothing, s));
+    KC(mean_reduce(c->d_row_loss, BT, c->d_out, s));
+    cudaEventRecord(c->ev[2], s);
+    if (!backward) return 0;
+    // ------------------------------------------------------------------ backward
+    int rc;
+    const int acc = accumulate;
+    // lm head: weight gradient (into wte when tied) and dHidden  (src/model.cpp:248-270)
+    if (tied) {
+        GemmArgs w = epi_args(kEpiStoreF32, gp(c->i_wte), C);
+        w.accumulate = acc;
+        if ((rc = gemm(c, c->logits, Vp, 1, c->lnf, C, 1, V, C, BT, w,
+                       choose_splits(c, V, C, BT))))
+            return rc;
+        if ((rc = gemm(c, c->logits, Vp, 0, c->wte16, C, 1, BT, C, Vp,
+                       epi_args(kEpiStoreF32, c->dln, C))))
+            return rc;
+    } else {
+        GemmArgs w = epi_args(kEpiStoreF32, gp(c->i_lm), V);
+        w.accumulate = acc;
+        if ((rc = gemm(c, c->lnf, C, 1, c->logits, Vp, 1, C, V, BT, w, choose_splits(c, C, V, BT))))
+            return rc;
+        if ((rc = gemm(c, c->logits, Vp, 0, c->lm16, Vp, 0, BT, C, Vp,
+                       epi_args(kEpiStoreF32, c->dln, C))))
+            return rc;
+        if (!acc) CK(cudaMemsetAsync(gp(c->i_wte), 0, sizeof(float) * c->params[c->i_wte].numel, s));
+    }
+    int nparts = 0;
+    KC(norm_backward(c->dln, c->xL, pp(c->i_lnfg), c->meanf, c->rstdf, nullptr, c->dres,
+                     c->dres16, c->partial, BT, C, rms, &nparts, s));
+    KC(reduce_partials(c->partial, nparts, C, gp(c->i_lnfg), rms ? nullptr : gp(c->i_lnfb),
+                       gp(c->blocks[L - 1].b2), acc, s));
+    for (int l = L - 1; l >= 0; --l) {
+        auto& a = c->act[l];
+        auto& b = c->blocks[l];
+        // ---- FFN  (src/transformer.cpp:120-183)
+        GemmArgs w2 = epi_args(kEpiStoreF32, gp(b.W2), C);
+        w2.accumulate = acc;
+        if ((rc = gemm(c, a.act, F, 1, c->dres16, C, 1, F, C, BT, w2, choose_splits(c, F, C, BT))))
+            return rc;
+        GemmArgs dg = epi_args(kEpiDGeluBF16, c->dh, F);
+        dg.aux = a.h;
+        dg.ld_aux = F;
+        if ((rc = gemm(c, c->dres16, C, 0, c->w2_16[l], C, 0, BT, F, C, dg))) return rc;
+        GemmArgs w1 = epi_args(kEpiStoreF32, gp(b.W1), F);
+        w1.accumulate = acc;
+        if ((rc = gemm(c, a.ln2, C, 1, c->dh, F, 1, C, F, BT, w1, choose_splits(c, C, F, BT))))
+            return rc;
+        KC(colsum_bf16(c->dh, F, BT, F, gp(b.b1), acc, c->colwork, s));
+        if ((rc = gemm(c, c->dh, F, 0, c->w1_16[l], F, 0, BT, C, F,
+                       epi_args(kEpiStoreF32, c->dln, C))))
+            return rc;
+        KC(norm_backward(c->dln, a.y, pp(b.ln2g), a.mean2, a.rstd2, c->dres, c->dy, c->dy16,
+                         c->partial, BT, C, rms, &nparts, s));
+        KC(reduce_partials(c->partial, nparts, C, gp(b.ln2g), rms ? nullptr : gp(b.ln2b), nullptr,
+                           acc, s));
+        // ---- attention  (src/attention.cpp:183-363)
+        GemmArgs wo = epi_args(kEpiStoreF32, gp(b.Wo), C);
+        wo.accumulate = acc;
+        if ((rc = gemm(c, a.att, C, 1, c->dy16, C, 1, C, C, BT, wo, choose_splits(c, C, C, BT))))
+            return rc;
+        if ((rc = gemm(c, c->dy16, C, 0, c->wo16[l], C, 0, BT, C, C,
+                       epi_args(kEpiStoreBF16, c->datt, C))))
+            return rc;
+        KC(attention_backward(a.qkv, a.att, c->datt, a.lse, c->dvec, c->dqkv, B, T, H, hd, s));
+        GemmArgs wq = epi_args(kEpiStoreF32, gp(b.Wq), C);
+        wq.accumulate = acc;
+        wq.col_group = C;
+        wq.group_stride = c->params[b.Wk].offset - c->params[b.Wq].offset;
+        if ((rc = gemm(c, a.ln1, C, 1, c->dqkv, 3 * C, 1, C, 3 * C, BT, wq,
+                       choose_splits(c, C, 3 * C, BT))))
+            return rc;
+        if ((rc = gemm(c, c->dqkv, 3 * C, 0, c->wqkv16[l], 3 * C, 0, BT, C, 3 * C,
+                       epi_args(kEpiStoreF32, c->dln, C))))
+            return rc;
+        KC(norm_backward(c->dln, a.x, pp(b.ln1g), a.mean1, a.rstd1, c->dy, c->dres, c->dres16,
+                         c->partial, BT, C, rms, &nparts, s));
+        KC(reduce_partials(c->partial, nparts, C, gp(b.ln1g), rms ? nullptr : gp(b.ln1b),
+                           l > 0 ? gp(c->blocks[l - 1].b2) : nullptr, acc, s));
+    }
+    // embedding scatter (src/model.cpp:314-322)
+    CK(cudaStreamWaitEvent(s, c->ev_keys, 0));
+    KC(embed_backward(c->d_keys, c->dres, gp(c->i_wte), gp(c->i_wpe), B, T, C, acc, s));
+    cudaEventRecord(c->ev[3], s);
+    return 0;
+}
+
+int run_optimizer(Ctx* c, int K) {
+    cudaStream_t s = c->stream;
+    if (K > 1) {
+        // train_step_accum averages the accumulated gradients (src/trainer.cpp:148-150)
+        const float inv = 1.0f / (float)K;
+        CK(cudaMemcpyAsync(c->d_kscale, &inv, sizeof(float), cudaMemcpyHostToDevice, s));
+        KC(scale_inplace(c->g, c->n_floats, c->d_kscale, s));
+    }
+    if (c->world > 1) {
+        ncclResult_t r = ncclAllReduce(c->g, c->g, (size_t)c->n_floats, ncclFloat, ncclAvg,
+                                       reinterpret_cast<ncclComm_t>(c->nccl), s);
+        if (r != ncclSuccess) {
+            c->err = std::string("ncclAllReduce: ") + ncclGetErrorString(r);
+            return LLMGPU_E_NCCL;
+        }
+        c->launches++;
+    }
+    cudaEventRecord(c->ev[4], s);
+    KC(grad_norm_partials(c->g, c->n_floats, c->d_normpart, c->d_nonfinite, grad_norm_blocks(), s));
+    KC(grad_norm_finalize(c->d_normpart, grad_norm_blocks(), c->d_nonfinite, c->clip, c->d_out + 1, s));
+    // Adam step counter advances only for steps that are not skipped; the bias corrections
+    // are prepared for t+1 and the host rolls t back if the device reports a skip.
+    c->adam_t += 1;
+    c->h_hp[0] = c->lr;
+    c->h_hp[1] = c->b1;
+    c->h_hp[2] = c->b2;
+    c->h_hp[3] = c->eps;
+    c->h_hp[4] = c->wd;
+    c->h_hp[5] = (float)(1.0 - std::pow((double)c->b1, (double)c->adam_t));
+    c->h_hp[6] = (float)(1.0 - std::pow((double)c->b2, (double)c->adam_t));
+    c->h_hp[7] = 1.0f;
+    CK(cudaMemcpyAsync(c->d_hp, c->h_hp, sizeof(float) * 8, cudaMemcpyHostToDevice, s));
+    KC(adamw_update(c->d_aparams, c->d_chunks, c->nchunks, c->p, c->g, c->m, c->v, c->d_out + 1,
+                    c->d_hp, s));
+    cudaEventRecord(c->ev[5], s);
+    return 0;
+}
+
+int ctx_sync_check(Ctx* c) {
+    CK(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    if (*c->h_err != 0) {
+        c->err = "device-side wait timed out (code " + std::to_string(*c->h_err) + ")";
+        return LLMGPU_E_DEVICE;
+    }
+    return 0;
+}
+
+// ---------------------------------------------------------------------------- checkpoints
+namespace {
+bool read_exact(std::ifstream& in, void* p, size_t n) {
+    in.read(reinterpret_cast<char*>(p), (std::streamsize)n);
+    return (size_t)in.gcount() == n;
+}
+}  // namespace
+
+// Binary checkpoint v3/v4 (src/model.cpp:568-635), written atomically (tmp + fsync + rename,
+// src/model.cpp:558-567).
+int save_binary(Ctx* c, const char* path) {
+    std::vector<float> host((size_t)c->n_floats);
+    if (copy_sync(c, host.data(), c->p, host.size() * sizeof(float), cudaMemcpyDeviceToHost))
+        return LLMGPU_E_CUDA;
+    const std::string tmp = std::string(path) + ".tmp";
+    {
+        std::ofstream out(tmp, std::ios::binary);
+        if (!out) {
+            c->err = "cannot open " + tmp;
+            return LLMGPU_E_IO;
+        }
+        auto& k = c->cfg;
+        const uint32_t magic = 0x4C4C4D00u, version = k.use_mamba ? 4 : 3;
+        out.write((const char*)&magic, 4);
+        out.write((const char*)&version, 4);
+        const uint64_t hdr[5] = {(uint64_t)k.vocab_size, (uint64_t)k.n_layers, (uint64_t)k.n_heads,
+                                 (uint64_t)k.n_embd, (uint64_t)k.block_size};
+        out.write((const char*)hdr, sizeof(hdr));
+        auto wt = [&](const std::vector<int64_t>& shape, const float* d, int64_t n) {
+            uint64_t nd = shape.size();
+            out.write((const char*)&nd, 8);
+            for (auto s : shape) {
+                uint64_t v = (uint64_t)s;
+                out.write((const char*)&v, 8);
+            }
+            uint64_t nn = (uint64_t)n;
+            out.write((const char*)&nn, 8);
+            out.write((const char*)d, n * sizeof(float));
+        };
+        auto wparam = [&](int i) {
+            const auto& p = c->params[i];
+            wt(p.shape, host.data() + p.offset, p.numel);
+        };
+        wparam(c->i_wte);
+        wparam(c->i_wpe);
+        wparam(c->i_lnfg);
+        wparam(c->i_lnfb);
+        if (c->i_lm >= 0) {
+            wparam(c->i_lm);
+        } else {  // tied: the reference's lm_head_ holds wte^T (tie_weights, src/model.cpp:931-939)
+            const int V = c->V, C = c->C;
+            std::vector<float> lm((size_t)C * V);
+            const float* w = host.data() + c->params[c->i_wte].offset;
+            for (int v = 0; v < V; ++v)
+                for (int j = 0; j < C; ++j) lm[(size_t)j * V + v] = w[(size_t)v * C + j];
+            wt({C, V}, lm.data(), (int64_t)lm.size());
+        }
+        if (k.use_mamba) {
+            const auto& b = c->blocks[0];
+            const uint64_t mh[4] = {(uint64_t)c->params[b.in_proj].shape[0] / 2,
+                                    (uint64_t)c->params[b.a_log].shape[1],
+                                    (uint64_t)c->params[b.dt_proj].shape[1],
+                                    (uint64_t)c->params[b.conv_w].shape[2]};
+            out.write((const char*)mh, sizeof(mh));
+        }
+        const uint64_t nb = (uint64_t)c->L;
+        out.write((const char*)&nb, 8);
+        const int first_block = c->i_lm >= 0 ? c->i_lm + 1 : c->i_lnfb + 1;
+        const int per = (int)((c->params.size() - first_block) / c->L);
+        for (int l = 0; l < c->L; ++l) {
+            const uint64_t np = (uint64_t)per;
+            out.write((const char*)&np, 8);
+            for (int j = 0; j < per; ++j) wparam(first_block + l * per + j);
+        }
+        if (!out) {
+            c->err = "write failed: " + tmp;
+            return LLMGPU_E_IO;
+        }
+    }
+    int fd = ::open(tmp.c_str(), O_RDONLY);
+    if (fd >= 0) {
+        ::fsync(fd);
+        ::close(fd);
+    }
+    if (std::rename(tmp.c_str(), path) != 0) {
+        c->err = std::string("rename failed: ") + path;
+        return LLMGPU_E_IO;
+    }
+    return 0;
+}
+
+// load_binary (src/model.cpp:636-811): header must match the configuration; unlike the
+// reference (which prints and keeps random init) a mismatch is reported as an error.
+int load_binary(Ctx* c, const char* path) {
+    std::ifstream in(path, std::ios::binary);
+    if (!in) {
+        c->err = std::string("cannot open ") + path;
+        return LLMGPU_E_IO;
+    }
+    uint32_t magic = 0, version = 0;
+    uint64_t hdr[5];
+    if (!read_exact(in, &magic, 4) || !read_exact(in, &version, 4) || magic != 0x4C4C4D00u ||
+        !read_exact(in, hdr, sizeof(hdr))) {
+        c->err = "bad checkpoint header";
+        return LLMGPU_E_IO;
+    }
+    auto& k = c->cfg;
+    if (hdr[0] != (uint64_t)k.vocab_size || hdr[1] != (uint64_t)k.n_layers ||
+        hdr[2] != (uint64_t)k.n_heads || hdr[3] != (uint64_t)k.n_embd ||
+        hdr[4] != (uint64_t)k.block_size) {
+        c->err = "checkpoint config mismatch";
+        return LLMGPU_E_ARG;
+    }
+    std::vector<float> host((size_t)c->n_floats, 0.0f);
+    if (copy_sync(c, host.data(), c->p, host.size() * sizeof(float), cudaMemcpyDeviceToHost))
+        return LLMGPU_E_CUDA;
+    auto rt = [&](std::vector<int64_t>* shape_out, std::vector<float>* data) -> bool {
+        uint64_t nd = 0;
+        if (!read_exact(in, &nd, 8) || nd > 8) return false;
+        shape_out->resize(nd);
+        for (uint64_t i = 0; i < nd; ++i) {
+            uint64_t v;
+            if (!read_exact(in, &v, 8)) return false;
+            (*shape_out)[i] = (int64_t)v;
+        }
+        uint64_t n = 0;
+        if (!read_exact(in, &n, 8)) return false;
+        data->resize(n);
+        return read_exact(in, data->data(), n * sizeof(float));
+    };
+    auto into = [&](int i, const std::vector<int64_t>& shape, const std::vector<float>& d) -> bool {
+        const auto& p = c->params[i];
+        if ((int64_t)d.size() != p.numel) return false;
+        (void)shape;
+        std::memcpy(host.data() + p.offset, d.data(), d.size() * sizeof(float));
+        return true;
+    };
+    std::vector<int64_t> shp;
+    std::vector<float> dat;
+    const int top[4] = {c->i_wte, c->i_wpe, c->i_lnfg, c->i_lnfb};
+    for (int t = 0; t < 4; ++t)
+        if (!rt(&shp, &dat) || !into(top[t], shp, dat)) {
+            c->err = "bad tensor in checkpoint";
+            return LLMGPU_E_IO;
+        }
+    if (!rt(&shp, &dat)) {
+        c->err = "bad lm_head";
+        return LLMGPU_E_IO;
+    }
+    if (c->i_lm >= 0 && !into(c->i_lm, shp, dat)) {
+        c->err = "lm_head size mismatch";
+        return LLMGPU_E_IO;
+    }
+    if (version >= 4) {
+        uint64_t mh[4];
+        if (!read_exact(in, mh, sizeof(mh))) {
+            c->err = "bad v4 header";
+            return LLMGPU_E_IO;
+        }
+    }
+    uint64_t nb = 0;
+    if (!read_exact(in, &nb, 8) || nb != (uint64_t)c->L) {
+        c->err = "block count mismatch";
+        return LLMGPU_E_ARG;
+    }
+    const int first_block = c->i_lm >= 0 ? c->i_lm + 1 : c->i_lnfb + 1;
+    const int per = (int)((c->params.size() - first_block) / c->L);
+    for (int l = 0; l < c->L; ++l) {
+        uint64_t np = 0;
+        if (!read_exact(in, &np, 8) || np != (uint64_t)per) {
+            c->err = "param count mismatch";
+            return LLMGPU_E_ARG;
+        }
+        for (int j = 0; j < per; ++j)
+            if (!rt(&shp, &dat) || !into(first_block + l * per + j, shp, dat)) {
+                c->err = "bad block tensor";
+                return LLMGPU_E_IO;
+            }
+    }
+    if (copy_sync(c, c->p, host.data(), host.size() * sizeof(float), cudaMemcpyHostToDevice))
+        return LLMGPU_E_CUDA;
+    refresh_shadows(c);
+    CK(cudaStreamSynchronize(c->stream));
+    return 0;
+}
+
+// Adam state persistence (src/optimizer.cpp:129-173): magic "ADAM", lr, b1, b2, eps, t,
+// then m[] and v[] as shape-prefixed tensors in parameters() order.
+int save_adam(Ctx* c, const char* path) {
+    std::ofstream os(path, std::ios::binary);
+    if (!os) {
+        c->err = std::string("cannot open ") + path;
+        return LLMGPU_E_IO;
+    }
+    std::vector<float> m((size_t)c->n_floats), v((size_t)c->n_floats);
+    if (copy_sync(c, m.data(), c->m, m.size() * 4, cudaMemcpyDeviceToHost) ||
+        copy_sync(c, v.data(), c->v, v.size() * 4, cudaMemcpyDeviceToHost))
+        return LLMGPU_E_CUDA;
+    const uint32_t magic = 0x4144414Du;
+    os.write((const char*)&magic, 4);
+    os.write((const char*)&c->lr, 4);
+    os.write((const char*)&c->b1, 4);
+    os.write((const char*)&c->b2, 4);
+    os.write((const char*)&c->eps, 4);
+    const int t = c->adam_t;
+    os.write((const char*)&t, 4);
+    for (int which = 0; which < 2; ++which) {
+        const uint64_t n = c->adam_t > 0 ? c->params.size() : 0;  // empty before the first step
+        os.write((const char*)&n, 8);
+        if (!n) continue;
+        const float* src = which == 0 ? m.data() : v.data();
+        for (const auto& p : c->params) {
+            uint64_t nd = p.shape.size();
+            os.write((const char*)&nd, 8);
+            for (auto s : p.shape) {
+                uint64_t d = (uint64_t)s;
+                os.write((const char*)&d, 8);
+            }
+            uint64_t nn = (uint64_t)p.numel;
+            os.write((const char*)&nn, 8);
+            os.write((const char*)(src + p.offset), p.numel * 4);
+        }
+    }
+    return os ? 0 : LLMGPU_E_IO;
+}
+
+int load_adam(Ctx* c, const char* path) {
+    std::ifstream is(path, std::ios::binary);
+    if (!is) {
+        c->err = std::string("cannot open ") + path;
+        return LLMGPU_E_IO;
+    }
+    uint32_t magic = 0;
+    if (!read_exact(is, &magic, 4) || magic != 0x4144414Du) {
+        c->err = "bad adam state magic";
+        return LLMGPU_E_IO;
+    }
+    int t = 0;
+    if (!read_exact(is, &c->lr, 4) || !read_exact(is, &c->b1, 4) || !read_exact(is, &c->b2, 4) ||
+        !read_exact(is, &c->eps, 4) || !read_exact(is, &t, 4)) {
+        c->err = "truncated adam state";
+        return LLMGPU_E_IO;
+    }
+    c->adam_t = t;
+    std::vector<float> m((size_t)c->n_floats, 0.f), v((size_t)c->n_floats, 0.f);
+    for (int which = 0; which < 2; ++which) {
+        uint64_t n = 0;
+        if (!read_exact(is, &n, 8)) {
+            c->err = "truncated adam state";
+            return LLMGPU_E_IO;
+        }
+        if (n != 0 && n != c->params.size()) {
+            c->err = "adam state tensor count mismatch";
+            return LLMGPU_E_ARG;
+        }
+        float* dst = which == 0 ? m.data() : v.data();
+        for (uint64_t i = 0; i < n; ++i) {
+            uint64_t nd = 0;
+            if (!read_exact(is, &nd, 8) || nd > 8) return LLMGPU_E_IO;
+            for (uint64_t d = 0; d < nd; ++d) {
+                uint64_t x;
+                if (!read_exact(is, &x, 8)) return LLMGPU_E_IO;
+            }
+            uint64_t nn = 0;
+            if (!read_exact(is, &nn, 8) || (int64_t)nn != c->params[i].numel) return LLMGPU_E_IO;
+            if (!read_exact(is, dst + c->params[i].offset, nn * 4)) return LLMGPU_E_IO;
+        }
+    }
+    if (copy_sync(c, c->m, m.data(), m.size() * 4, cudaMemcpyHostToDevice) ||
+        copy_sync(c, c->v, v.data(), v.size() * 4, cudaMemcpyHostToDevice))
+        return LLMGPU_E_CUDA;
+    return 0;
+}
+
+}  // namespace llmgpu

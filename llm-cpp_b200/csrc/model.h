@@ -1,0 +1,159 @@
+// Device-resident GPT training context behind the C ABI (include/llmgpu.h).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <string>
+#include <vector>
+
+#include "gemm.cuh"
+#include "kernels.cuh"
+#include "llmgpu.h"
+
+namespace llmgpu {
+
+struct Param {
+    std::string name;
+    std::vector<int64_t> shape;
+    int64_t offset = 0;  // floats, into the arena
+    int64_t numel = 0;
+    int decay = 0;
+    bf16* shadow = nullptr;
+    int64_t shadow_ld = 0;
+    int cols = 1;
+};
+
+// Indices into Ctx::params of one transformer / Mamba block.
+struct BlockIdx {
+    int Wq = -1, Wk = -1, Wv = -1, Wo = -1, W1 = -1, W2 = -1, W3 = -1, b1 = -1, b2 = -1;
+    int ln1g = -1, ln1b = -1, ln2g = -1, ln2b = -1;
+    int gate = -1, W1e = -1, W2e = -1;  // MoE
+    // Mamba
+    int norm_w = -1, in_proj = -1, conv_w = -1, conv_b = -1, x_proj = -1, dt_proj = -1,
+        a_log = -1, dskip = -1, out_proj = -1;
+};
+
+// Activations kept from the forward for the backward, per block.
+struct BlockAct {
+    float* x = nullptr;      // block input, fp32 [BT, C]
+    float* y = nullptr;      // after attention residual, fp32 [BT, C]
+    bf16* ln1 = nullptr;     // [BT, C]
+    float* mean1 = nullptr;
+    float* rstd1 = nullptr;
+    bf16* qkv = nullptr;     // [BT, 3C]
+    bf16* att = nullptr;     // [BT, C]
+    float* lse = nullptr;    // [B, H, T]
+    bf16* ln2 = nullptr;
+    float* mean2 = nullptr;
+    float* rstd2 = nullptr;
+    bf16* h = nullptr;       // FFN pre-activation [BT, F] (GELU) or [BT, 2F] (h1|h3, SwiGLU)
+    bf16* act = nullptr;     // FFN activation [BT, F]
+};
+
+struct Ctx {
+    llmgpu_config cfg{};
+    int rank = 0, world = 1;
+    int device = 0, num_sms = 148;
+    int max_bt = 0, max_b = 0, max_t = 0;
+    int C = 0, V = 0, Vp = 0, H = 0, hd = 0, F = 0, L = 0;
+    cudaStream_t stream = nullptr, side = nullptr;
+    cudaEvent_t ev_keys = nullptr;
+    cudaEvent_t ev[6] = {};
+    void* nccl = nullptr;  // ncclComm_t
+
+    std::vector<Param> params;
+    std::vector<BlockIdx> blocks;
+    int i_wte = -1, i_wpe = -1, i_lnfg = -1, i_lnfb = -1, i_lm = -1;
+    int64_t n_floats = 0;
+    float *p = nullptr, *g = nullptr, *m = nullptr, *v = nullptr;
+    bf16* shadow_arena = nullptr;
+    size_t shadow_elems = 0;
+    bf16* wte16 = nullptr;   // [Vp, C]   tied head / embedding shadow
+    bf16* lm16 = nullptr;    // [C, Vp]   untied head shadow
+    std::vector<bf16*> wqkv16, wo16, w1_16, w2_16;
+
+    // activations
+    std::vector<BlockAct> act;
+    float* xL = nullptr;
+    bf16* lnf = nullptr;
+    float *meanf = nullptr, *rstdf = nullptr;
+    bf16* logits = nullptr;
+    // backward scratch
+    float *dres = nullptr, *dy = nullptr, *dln = nullptr;
+    bf16 *dres16 = nullptr, *dy16 = nullptr, *datt = nullptr, *dqkv = nullptr, *dh = nullptr,
+         *dact = nullptr;
+    float* dvec = nullptr;
+    float* partial = nullptr;
+    float* colwork = nullptr;
+    float* splitws = nullptr;
+    size_t splitws_floats = 0;
+
+    // per-step device scalars / buffers
+    int32_t* d_tokens = nullptr;
+    uint64_t* d_keys = nullptr;
+    float* d_row_loss = nullptr;
+    float* d_out = nullptr;        // [0] loss [1] pre-clip norm [2] clip scale [3] post norm [4] skip
+    float* d_hp = nullptr;         // 8 AdamW scalars
+    double* d_normpart = nullptr;
+    int* d_nonfinite = nullptr;
+    int* d_err = nullptr;
+    AdamParam* d_aparams = nullptr;
+    AdamChunk* d_chunks = nullptr;
+    int nchunks = 0;
+    float* d_kscale = nullptr;
+
+    // pinned host staging
+    int32_t* h_tokens = nullptr;
+    float* h_out = nullptr;  // 8 floats
+    float* h_hp = nullptr;   // 8 floats
+    int* h_err = nullptr;
+
+    // optimizer / trainer state
+    float lr = 3e-4f, b1 = 0.9f, b2 = 0.95f, eps = 1e-8f, wd = 0.1f;
+    int adam_t = 0;
+    bool adam_init = false;
+    float clip = 1.0f, smoothing = 0.0f;
+    int accum_k = 1, accum_count = 0;
+    int step_count = 0, skipped = 0;
+    float last_loss = 0.f, last_gnorm = 0.f;
+    int last_T = -1;
+    float timings[6] = {};
+    int launches = 0;
+
+    // gemm plan cache (deterministic call order)
+    std::vector<GemmPlan> plan_cache;
+    std::vector<std::vector<uint8_t>> plan_keys;
+    size_t plan_cursor = 0;
+
+    // GEMM profiling (events around each GEMM launch)
+    bool profile = false;
+    std::vector<cudaEvent_t> prof_ev;
+    std::vector<double> prof_flops;
+    size_t prof_n = 0;
+    double prof_total_flops = 0, prof_total_ms = 0;
+    int prof_launches = 0;
+
+    // CUDA graph of the whole step
+    bool use_graph = true;
+    cudaGraphExec_t graph = nullptr;
+    int graph_B = -1, graph_T = -1, graph_acc = -1, graph_mode = -1;
+
+    std::string err;
+};
+
+// lifecycle
+Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, int world,
+                const void* uid, std::string* err);
+void ctx_destroy(Ctx* c);
+// one micro-batch forward+backward on device tokens (ctx->d_tokens) with accumulate flag
+int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward);
+// optimizer: (scale by 1/K) -> allreduce -> norm/clip -> AdamW
+int run_optimizer(Ctx* c, int K);
+int ctx_sync_check(Ctx* c);
+int save_binary(Ctx* c, const char* path);
+int load_binary(Ctx* c, const char* path);
+int save_adam(Ctx* c, const char* path);
+int load_adam(Ctx* c, const char* path);
+void refresh_shadows(Ctx* c);
+int copy_sync(Ctx* c, void* dst, const void* src, size_t bytes, cudaMemcpyKind kind);
+
+}  // namespace llmgpu

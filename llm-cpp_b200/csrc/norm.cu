@@ -1,0 +1,304 @@
+// LayerNorm / RMSNorm forward and backward (warp per row, 128-bit loads), deterministic
+// two-stage column reductions for the norm-parameter and bias gradients.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace llmgpu {
+
+namespace {
+
+constexpr float kNormEps = 1e-5f;  // include/llm/tensor.h:68-69
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+template <int MAXV>
+__global__ void __launch_bounds__(256) norm_fwd_kernel(const float* __restrict__ x,
+                                                       const float* __restrict__ gamma,
+                                                       const float* __restrict__ beta,
+                                                       bf16* __restrict__ y, float* __restrict__ mean,
+                                                       float* __restrict__ rstd, int rows, int C,
+                                                       int rms) {
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int nv = C >> 2;
+    const float4* xr = reinterpret_cast<const float4*>(x + (long long)row * C);
+    float4 v[MAXV];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int idx = lane + i * 32;
+        if (idx < nv) {
+            v[i] = xr[idx];
+            s += v[i].x + v[i].y + v[i].z + v[i].w;
+        } else {
+            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    s = warp_sum(s);
+    const float mu = rms ? 0.f : s / (float)C;
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int idx = lane + i * 32;
+        if (idx < nv) {
+            float a = v[i].x - mu, b = v[i].y - mu, c = v[i].z - mu, d = v[i].w - mu;
+            ss += a * a + b * b + c * c + d * d;
+        }
+    }
+    ss = warp_sum(ss);
+    const float r = 1.0f / sqrtf(ss / (float)C + kNormEps);
+    const float4* g4 = reinterpret_cast<const float4*>(gamma);
+    const float4* b4 = reinterpret_cast<const float4*>(beta);
+    uint2* yr = reinterpret_cast<uint2*>(y + (long long)row * C);
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int idx = lane + i * 32;
+        if (idx < nv) {
+            float4 g = g4[idx];
+            float4 b = (beta && !rms) ? b4[idx] : make_float4(0.f, 0.f, 0.f, 0.f);
+            float o0 = (v[i].x - mu) * r * g.x + b.x;
+            float o1 = (v[i].y - mu) * r * g.y + b.y;
+            float o2 = (v[i].z - mu) * r * g.z + b.z;
+            float o3 = (v[i].w - mu) * r * g.w + b.w;
+            yr[idx] = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
+        }
+    }
+    if (lane == 0) {
+        mean[row] = mu;
+        rstd[row] = r;
+    }
+}
+
+template <int MAXV>
+__global__ void __launch_bounds__(256) norm_bwd_kernel(
+    const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ gamma,
+    const float* __restrict__ mean, const float* __restrict__ rstd,
+    const float* __restrict__ resid_in, float* __restrict__ dx_f32, bf16* __restrict__ dx_bf16,
+    float* __restrict__ partial, int rows, int C, int rms) {
+    extern __shared__ float red[];  // [8][C]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nwarps_total = gridDim.x * 8;
+    const int nv = C >> 2;
+    const float4* g4 = reinterpret_cast<const float4*>(gamma);
+    float4 pg[MAXV], pb[MAXV], po[MAXV];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        pg[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        pb[i] = pg[i];
+        po[i] = pg[i];
+    }
+    const float invC = 1.0f / (float)C;
+    for (int row = blockIdx.x * 8 + warp; row < rows; row += nwarps_total) {
+        const float4* dyr = reinterpret_cast<const float4*>(dy + (long long)row * C);
+        const float4* xr = reinterpret_cast<const float4*>(x + (long long)row * C);
+        const float mu = mean[row], r = rstd[row];
+        float s1 = 0.f, s2 = 0.f;
+        float4 d[MAXV], xv[MAXV];
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+            const int idx = lane + i * 32;
+            if (idx < nv) {
+                d[i] = dyr[idx];
+                xv[i] = xr[idx];
+                float4 g = g4[idx];
+                if (!rms) {
+                    float gx = d[i].x * g.x, gy = d[i].y * g.y, gz = d[i].z * g.z,
+                          gw = d[i].w * g.w;
+                    s1 += gx + gy + gz + gw;
+                    s2 += gx * (xv[i].x - mu) * r + gy * (xv[i].y - mu) * r +
+                          gz * (xv[i].z - mu) * r + gw * (xv[i].w - mu) * r;
+                } else {
+                    s2 += d[i].x * g.x * xv[i].x + d[i].y * g.y * xv[i].y +
+                          d[i].z * g.z * xv[i].z + d[i].w * g.w * xv[i].w;
+                }
+            }
+        }
+        s1 = warp_sum(s1);
+        s2 = warp_sum(s2);
+        const float m1 = s1 * invC, m2 = s2 * invC;
+        const float coef = rms ? s2 * r * r * r * invC : 0.f;
+        const float4* rin = reinterpret_cast<const float4*>(resid_in + (long long)row * C);
+        float4* o32 = reinterpret_cast<float4*>(dx_f32 + (long long)row * C);
+        uint2* o16 = dx_bf16 ? reinterpret_cast<uint2*>(dx_bf16 + (long long)row * C) : nullptr;
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+            const int idx = lane + i * 32;
+            if (idx < nv) {
+                float4 g = g4[idx];
+                float dd[4] = {d[i].x, d[i].y, d[i].z, d[i].w};
+                float xx[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+                float gg[4] = {g.x, g.y, g.z, g.w};
+                float o[4], xh[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    xh[k] = (xx[k] - mu) * r;
+                    if (!rms)
+                        o[k] = r * (dd[k] * gg[k] - m1 - xh[k] * m2);
+                    else
+                        o[k] = dd[k] * gg[k] * r - xx[k] * coef;
+                }
+                if (resid_in) {
+                    float4 ri = rin[idx];
+                    o[0] += ri.x;
+                    o[1] += ri.y;
+                    o[2] += ri.z;
+                    o[3] += ri.w;
+                }
+                o32[idx] = make_float4(o[0], o[1], o[2], o[3]);
+                if (o16) o16[idx] = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+                pg[i].x += dd[0] * xh[0];
+                pg[i].y += dd[1] * xh[1];
+                pg[i].z += dd[2] * xh[2];
+                pg[i].w += dd[3] * xh[3];
+                pb[i].x += dd[0];
+                pb[i].y += dd[1];
+                pb[i].z += dd[2];
+                pb[i].w += dd[3];
+                po[i].x += o[0];
+                po[i].y += o[1];
+                po[i].z += o[2];
+                po[i].w += o[3];
+            }
+        }
+    }
+    // CTA-level reduction of the three partial planes (fixed order: warp 0..7)
+    for (int plane = 0; plane < 3; ++plane) {
+        float4* mine = reinterpret_cast<float4*>(red + warp * C);
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+            const int idx = lane + i * 32;
+            if (idx < nv) mine[idx] = plane == 0 ? pg[i] : (plane == 1 ? pb[i] : po[i]);
+        }
+        __syncthreads();
+        for (int c = threadIdx.x; c < C; c += blockDim.x) {
+            float acc = 0.f;
+            for (int w = 0; w < 8; ++w) acc += red[w * C + c];
+            partial[((long long)blockIdx.x * 3 + plane) * C + c] = acc;
+        }
+        __syncthreads();
+    }
+}
+
+__global__ void reduce_partials_kernel(const float* __restrict__ partial, int nparts, int C,
+                                       float* out0, float* out1, float* out2, int accumulate) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= 3 * C) return;
+    const int plane = i / C, c = i - plane * C;
+    float* out = plane == 0 ? out0 : (plane == 1 ? out1 : out2);
+    if (!out) return;
+    float acc = 0.f;
+    for (int p = 0; p < nparts; ++p) acc += partial[((long long)p * 3 + plane) * C + c];
+    out[c] = accumulate ? out[c] + acc : acc;
+}
+
+constexpr int kColsumGroups = 64;
+
+__global__ void colsum_stage1(const bf16* __restrict__ a, long long lda, int rows, int C,
+                              float* __restrict__ work) {
+    // blockIdx.x: 2048-column tile (256 threads x 8 columns); blockIdx.y: row group
+    const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    if (c0 >= C) return;
+    const int rg = blockIdx.y;
+    const int r0 = (int)((long long)rg * rows / kColsumGroups);
+    const int r1 = (int)((long long)(rg + 1) * rows / kColsumGroups);
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const bool vec = (c0 + 8 <= C) && ((lda & 7) == 0);
+    for (int r = r0; r < r1; ++r) {
+        const bf16* p = a + (long long)r * lda + c0;
+        if (vec) {
+            uint4 u = *reinterpret_cast<const uint4*>(p);
+            uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                acc[2 * k] += bf16_lo(w[k]);
+                acc[2 * k + 1] += bf16_hi(w[k]);
+            }
+        } else {
+            for (int k = 0; k < 8 && c0 + k < C; ++k) acc[k] += __bfloat162float(p[k]);
+        }
+    }
+    for (int k = 0; k < 8 && c0 + k < C; ++k) work[(long long)rg * C + c0 + k] = acc[k];
+}
+
+__global__ void colsum_stage2(const float* __restrict__ work, int C, float* out, int accumulate) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= C) return;
+    float acc = 0.f;
+    for (int g = 0; g < kColsumGroups; ++g) acc += work[(long long)g * C + c];
+    out[c] = accumulate ? out[c] + acc : acc;
+}
+
+}  // namespace
+
+int norm_forward(const float* x, const float* gamma, const float* beta, bf16* y, float* mean,
+                 float* rstd, int rows, int C, int rms, cudaStream_t s) {
+    if ((C & 3) != 0 || rows <= 0) return -1;
+    const int blocks = (rows + 7) / 8;
+    if (C <= 512)
+        norm_fwd_kernel<4><<<blocks, 256, 0, s>>>(x, gamma, beta, y, mean, rstd, rows, C, rms);
+    else if (C <= 1024)
+        norm_fwd_kernel<8><<<blocks, 256, 0, s>>>(x, gamma, beta, y, mean, rstd, rows, C, rms);
+    else if (C <= 2048)
+        norm_fwd_kernel<16><<<blocks, 256, 0, s>>>(x, gamma, beta, y, mean, rstd, rows, C, rms);
+    else
+        return -2;
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int norm_backward_grid(int rows) {
+    int g = (rows + 7) / 8;
+    return g < 296 ? g : 296;
+}
+
+int norm_backward(const float* dy, const float* x, const float* gamma, const float* mean,
+                  const float* rstd, const float* resid_in, float* dx_f32, bf16* dx_bf16,
+                  float* partial, int rows, int C, int rms, int* nparts, cudaStream_t s) {
+    if ((C & 3) != 0 || rows <= 0) return -1;
+    const int grid = norm_backward_grid(rows);
+    const size_t smem = 8 * (size_t)C * sizeof(float);
+    if (nparts) *nparts = grid;
+    if (C <= 512) {
+        norm_bwd_kernel<4><<<grid, 256, smem, s>>>(dy, x, gamma, mean, rstd, resid_in, dx_f32,
+                                                    dx_bf16, partial, rows, C, rms);
+    } else if (C <= 1024) {
+        norm_bwd_kernel<8><<<grid, 256, smem, s>>>(dy, x, gamma, mean, rstd, resid_in, dx_f32,
+                                                    dx_bf16, partial, rows, C, rms);
+    } else if (C <= 2048) {
+        static bool set = false;
+        if (!set) {
+            cudaFuncSetAttribute(norm_bwd_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 8 * 2048 * 4);
+            set = true;
+        }
+        norm_bwd_kernel<16><<<grid, 256, smem, s>>>(dy, x, gamma, mean, rstd, resid_in, dx_f32,
+                                                     dx_bf16, partial, rows, C, rms);
+    } else {
+        return -2;
+    }
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int reduce_partials(const float* partial, int nparts, int C, float* out0, float* out1,
+                    float* out2, int accumulate, cudaStream_t s) {
+    const int n = 3 * C;
+    reduce_partials_kernel<<<(n + 255) / 256, 256, 0, s>>>(partial, nparts, C, out0, out1, out2,
+                                                           accumulate);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+size_t colsum_work_floats(int C) { return (size_t)kColsumGroups * C; }
+
+int colsum_bf16(const bf16* a, long long lda, int rows, int C, float* out, int accumulate,
+                float* work, cudaStream_t s) {
+    dim3 g1((C + 2047) / 2048, kColsumGroups);
+    colsum_stage1<<<g1, 256, 0, s>>>(a, lda, rows, C, work);
+    colsum_stage2<<<(C + 255) / 256, 256, 0, s>>>(work, C, out, accumulate);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+}  // namespace llmgpu

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include "gemm.cuh"
+#include "kernels.cuh"
 #include "llmgpu_ops.h"
 
 using namespace llmgpu;
@@ -52,4 +53,55 @@ extern "C" int llmgpu_op_gemm(const void* A, long long lda, int a_mn_major, cons
         rc = gemm_splitk_reduce(workspace, g.splits, M, N, reinterpret_cast<float*>(out), ldo,
                                 col_group <= 0 ? N : col_group, group_stride, accumulate, st);
     return rc;
+}
+
+extern "C" int llmgpu_op_embed(const int32_t* tokens, const float* wte, const float* wpe, float* x,
+                               int B, int T, int C, int V, void* stream) {
+    return embed_forward(tokens, wte, wpe, x, B, T, C, V, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int llmgpu_op_norm_fwd(const float* x, const float* gamma, const float* beta,
+                                  void* y_bf16, float* mean, float* rstd, int rows, int C, int rms,
+                                  void* stream) {
+    return norm_forward(x, gamma, beta, reinterpret_cast<bf16*>(y_bf16), mean, rstd, rows, C, rms,
+                        reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" long long llmgpu_op_norm_bwd_work(int rows, int C) {
+    return (long long)norm_backward_grid(rows) * 3 * C;
+}
+
+extern "C" int llmgpu_op_norm_bwd(const float* dy, const float* x, const float* gamma,
+                                  const float* mean, const float* rstd, const float* resid,
+                                  float* dx, void* dx_bf16, float* dgamma, float* dbeta,
+                                  float* dxsum, float* work, int rows, int C, int rms,
+                                  void* stream) {
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    int nparts = 0;
+    int rc = norm_backward(dy, x, gamma, mean, rstd, resid, dx, reinterpret_cast<bf16*>(dx_bf16),
+                           work, rows, C, rms, &nparts, st);
+    if (rc) return rc;
+    return reduce_partials(work, nparts, C, dgamma, dbeta, dxsum, 0, st);
+}
+
+extern "C" int llmgpu_op_cross_entropy(void* logits_bf16, int rows, int V, int Vp,
+                                       const int32_t* tokens, float* row_loss, float scale,
+                                       float smoothing, void* stream) {
+    return cross_entropy_fwd_bwd(reinterpret_cast<bf16*>(logits_bf16), rows, V, Vp, tokens,
+                                 row_loss, scale, smoothing, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int llmgpu_op_attention_fwd(const void* qkv, void* out, float* lse, int B, int T,
+                                       int H, int hd, void* stream) {
+    return attention_forward(reinterpret_cast<const bf16*>(qkv), reinterpret_cast<bf16*>(out), lse,
+                             B, T, H, hd, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int llmgpu_op_attention_bwd(const void* qkv, const void* out, const void* dout,
+                                       const float* lse, float* dvec, void* dqkv, int B, int T,
+                                       int H, int hd, void* stream) {
+    return attention_backward(reinterpret_cast<const bf16*>(qkv), reinterpret_cast<const bf16*>(out),
+                              reinterpret_cast<const bf16*>(dout), lse, dvec,
+                              reinterpret_cast<bf16*>(dqkv), B, T, H, hd,
+                              reinterpret_cast<cudaStream_t>(stream));
 }

@@ -58,3 +58,72 @@ def gemm(A, B, M, N, K, *, a_mn=False, b_mn=False, lda=None, ldb=None, epi=EPI_F
         if int(err.item()) != 0:
             raise KernelError(f"gemm device error code {int(err.item())}")
     return out
+
+
+def _sync_check(rc, what):
+    _check(rc, what)
+    torch.cuda.synchronize()
+
+
+def embed(tokens, wte, wpe, B, T):
+    lib = load()
+    C, V = wte.shape[1], wte.shape[0]
+    x = torch.empty(B * T, C, dtype=torch.float32, device=wte.device)
+    _sync_check(lib.llmgpu_op_embed(_ptr(tokens), _ptr(wte), _ptr(wpe), _ptr(x), B, T, C, V,
+                                    _stream()), "embed")
+    return x
+
+
+def norm_fwd(x, gamma, beta, rms=False):
+    lib = load()
+    rows, C = x.shape
+    y = torch.empty(rows, C, dtype=torch.bfloat16, device=x.device)
+    mean = torch.empty(rows, device=x.device)
+    rstd = torch.empty(rows, device=x.device)
+    _sync_check(lib.llmgpu_op_norm_fwd(_ptr(x), _ptr(gamma), _ptr(beta), _ptr(y), _ptr(mean),
+                                       _ptr(rstd), rows, C, int(rms), _stream()), "norm_fwd")
+    return y, mean, rstd
+
+
+def norm_bwd(dy, x, gamma, mean, rstd, resid=None, rms=False):
+    lib = load()
+    rows, C = x.shape
+    dx = torch.empty_like(x)
+    dx16 = torch.empty(rows, C, dtype=torch.bfloat16, device=x.device)
+    dg, db, ds = (torch.empty(C, device=x.device) for _ in range(3))
+    work = torch.empty(int(lib.llmgpu_op_norm_bwd_work(rows, C)), device=x.device)
+    _sync_check(lib.llmgpu_op_norm_bwd(_ptr(dy), _ptr(x), _ptr(gamma), _ptr(mean), _ptr(rstd),
+                                       _ptr(resid), _ptr(dx), _ptr(dx16), _ptr(dg), _ptr(db),
+                                       _ptr(ds), _ptr(work), rows, C, int(rms), _stream()),
+                "norm_bwd")
+    return dx, dx16, dg, db, ds
+
+
+def cross_entropy(logits16, V, tokens, scale, smoothing=0.0):
+    lib = load()
+    rows, Vp = logits16.shape
+    loss = torch.empty(rows, device=logits16.device)
+    _sync_check(lib.llmgpu_op_cross_entropy(_ptr(logits16), rows, V, Vp, _ptr(tokens),
+                                            _ptr(loss), scale, smoothing, _stream()),
+                "cross_entropy")
+    return loss
+
+
+def attention_fwd(qkv, B, T, H, hd):
+    lib = load()
+    C = H * hd
+    out = torch.empty(B * T, C, dtype=torch.bfloat16, device=qkv.device)
+    lse = torch.empty(B, H, T, device=qkv.device)
+    _sync_check(lib.llmgpu_op_attention_fwd(_ptr(qkv), _ptr(out), _ptr(lse), B, T, H, hd,
+                                            _stream()), "attention_fwd")
+    return out, lse
+
+
+def attention_bwd(qkv, out, dout, lse, B, T, H, hd):
+    lib = load()
+    dqkv = torch.zeros_like(qkv)
+    dvec = torch.empty(B, H, T, device=qkv.device)
+    _sync_check(lib.llmgpu_op_attention_bwd(_ptr(qkv), _ptr(out), _ptr(dout), _ptr(lse),
+                                            _ptr(dvec), _ptr(dqkv), B, T, H, hd, _stream()),
+                "attention_bwd")
+    return dqkv

@@ -1,0 +1,239 @@
+"""Python mirror of the reference's training interface over libllmgpu.so.
+
+`GPT` + `Trainer` follow the names and argument meaning of llm::GPT / llm::Trainer /
+llm::AdamW (include/llm/model.h, include/llm/trainer.h, include/llm/optimizer.h); all
+compute runs in the CUDA kernels behind the C ABI. Errors raise `LlmgpuError` with the
+library's message (the reference asserts or throws at the same points).
+"""
+import ctypes
+
+import numpy as np
+
+from ._abi_decl import LlmgpuConfig
+from ._lib import load
+
+OK, SKIPPED = 0, 1
+
+
+class LlmgpuError(RuntimeError):
+    pass
+
+
+def make_config(vocab_size=50257, n_layers=12, n_heads=12, n_embd=768, block_size=1024,
+                weight_tying=True, use_rmsnorm=False, use_mamba=False, d_inner=0, d_state=16,
+                dt_rank=0, conv_kernel=4, ffn_swiglu=False, ffn_hidden=0, rope_qk=False,
+                rope_theta=10000.0, moe_experts=0, moe_top_k=2, moe_aux_coef=0.01):
+    lib = load()
+    c = LlmgpuConfig()
+    lib.llmgpu_config_default(ctypes.byref(c))
+    for k, v in dict(vocab_size=vocab_size, n_layers=n_layers, n_heads=n_heads, n_embd=n_embd,
+                     block_size=block_size, weight_tying=int(weight_tying),
+                     use_rmsnorm=int(use_rmsnorm), use_mamba=int(use_mamba), d_inner=d_inner,
+                     d_state=d_state, dt_rank=dt_rank, conv_kernel=conv_kernel,
+                     ffn_swiglu=int(ffn_swiglu), ffn_hidden=ffn_hidden, rope_qk=int(rope_qk),
+                     rope_theta=rope_theta, moe_experts=moe_experts, moe_top_k=moe_top_k,
+                     moe_aux_coef=moe_aux_coef).items():
+        setattr(c, k, v)
+    return c
+
+
+def unique_id():
+    buf = ctypes.create_string_buffer(128)
+    rc = load().llmgpu_get_unique_id(buf)
+    if rc != 0:
+        raise LlmgpuError(f"llmgpu_get_unique_id failed ({rc})")
+    return buf.raw
+
+
+class Trainer:
+    """Device training context: GPT parameters + AdamW state + Trainer counters."""
+
+    def __init__(self, cfg: LlmgpuConfig, max_batch, max_seq, rank=0, world=1, uid=None):
+        self.lib = load()
+        self.cfg = cfg
+        uidbuf = ctypes.create_string_buffer(uid, 128) if uid is not None else None
+        self.h = self.lib.llmgpu_create(ctypes.byref(cfg), max_batch, max_seq, rank, world,
+                                        uidbuf)
+        if not self.h:
+            raise LlmgpuError(self.lib.llmgpu_last_error(None).decode())
+
+    # ------------------------------------------------------------------ lifecycle
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.llmgpu_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def _err(self, what, rc):
+        msg = self.lib.llmgpu_last_error(self.h)
+        raise LlmgpuError(f"{what} failed ({rc}): {msg.decode() if msg else ''}")
+
+    # ------------------------------------------------------------------ hyper-parameters
+    def set_adamw(self, lr=3e-4, b1=0.9, b2=0.95, eps=1e-8, wd=0.1):
+        self.lib.llmgpu_set_adamw(self.h, lr, b1, b2, eps, wd)
+
+    def set_lr(self, lr):
+        self.lib.llmgpu_set_lr(self.h, lr)
+
+    def set_train(self, grad_clip=1.0, grad_accum_steps=1, label_smoothing=0.0):
+        rc = self.lib.llmgpu_set_train(self.h, grad_clip, grad_accum_steps, label_smoothing)
+        if rc:
+            self._err("set_train", rc)
+
+    def set_graph(self, enable):
+        self.lib.llmgpu_set_graph(self.h, int(enable))
+
+    # ------------------------------------------------------------------ steps
+    def train_step(self, tokens):
+        """tokens: int32 array [B, T]. Returns (loss, grad_norm, skipped)."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        B, T = t.shape
+        loss, gn = ctypes.c_float(), ctypes.c_float()
+        rc = self.lib.llmgpu_train_step(self.h, t.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                        B, T, ctypes.byref(loss), ctypes.byref(gn))
+        if rc < 0:
+            self._err("train_step", rc)
+        return loss.value, gn.value, rc == SKIPPED
+
+    def train_step_accum(self, tokens):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        B, T = t.shape
+        loss, stepped = ctypes.c_float(), ctypes.c_int()
+        rc = self.lib.llmgpu_train_step_accum(
+            self.h, t.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), B, T, ctypes.byref(loss),
+            ctypes.byref(stepped))
+        if rc < 0:
+            self._err("train_step_accum", rc)
+        return loss.value, bool(stepped.value), rc == SKIPPED
+
+    def train_step_device(self, dev_ptr, B, T):
+        loss, gn = ctypes.c_float(), ctypes.c_float()
+        rc = self.lib.llmgpu_train_step_device(self.h, ctypes.c_void_p(dev_ptr), B, T,
+                                               ctypes.byref(loss), ctypes.byref(gn))
+        if rc < 0:
+            self._err("train_step_device", rc)
+        return loss.value, gn.value, rc == SKIPPED
+
+    def eval_loss(self, tokens):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        B, T = t.shape
+        loss = ctypes.c_float()
+        rc = self.lib.llmgpu_eval_loss(self.h, t.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                       B, T, ctypes.byref(loss))
+        if rc < 0:
+            self._err("eval_loss", rc)
+        return loss.value
+
+    # ------------------------------------------------------------------ parameters
+    def num_params(self):
+        return self.lib.llmgpu_num_params(self.h)
+
+    def num_parameters(self):
+        return self.lib.llmgpu_num_parameters(self.h)
+
+    def param_info(self, i):
+        name = ctypes.create_string_buffer(128)
+        shape = (ctypes.c_int64 * 4)()
+        nd = self.lib.llmgpu_param_info(self.h, i, name, 128, shape)
+        if nd < 0:
+            self._err("param_info", nd)
+        return name.value.decode(), tuple(shape[j] for j in range(nd))
+
+    def _get(self, fn, i):
+        _, shape = self.param_info(i)
+        out = np.empty(int(np.prod(shape)), np.float32)
+        n = fn(self.h, i, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), out.size)
+        if n < 0:
+            self._err("get", n)
+        return out.reshape(shape)
+
+    def get_param(self, i):
+        return self._get(self.lib.llmgpu_get_param, i)
+
+    def get_grad(self, i):
+        return self._get(self.lib.llmgpu_get_grad, i)
+
+    def get_adam_state(self, i):
+        _, shape = self.param_info(i)
+        m = np.empty(int(np.prod(shape)), np.float32)
+        v = np.empty_like(m)
+        n = self.lib.llmgpu_get_adam_state(self.h, i, m.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                           v.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), m.size)
+        if n < 0:
+            self._err("get_adam_state", n)
+        return m.reshape(shape), v.reshape(shape)
+
+    def set_param(self, i, a):
+        a = np.ascontiguousarray(a, np.float32).ravel()
+        rc = self.lib.llmgpu_set_param(self.h, i, a.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                       a.size)
+        if rc:
+            self._err("set_param", rc)
+
+    def params(self):
+        return [self.get_param(i) for i in range(self.num_params())]
+
+    def grads(self):
+        return [self.get_grad(i) for i in range(self.num_params())]
+
+    def names(self):
+        return [self.param_info(i)[0] for i in range(self.num_params())]
+
+    # ------------------------------------------------------------------ checkpoints
+    def save_binary(self, path):
+        rc = self.lib.llmgpu_save_binary(self.h, path.encode())
+        if rc:
+            self._err("save_binary", rc)
+
+    def load_binary(self, path):
+        rc = self.lib.llmgpu_load_binary(self.h, path.encode())
+        if rc:
+            self._err("load_binary", rc)
+
+    def save_train_state(self, prefix):
+        rc = self.lib.llmgpu_save_train_state(self.h, prefix.encode())
+        if rc:
+            self._err("save_train_state", rc)
+
+    def load_train_state(self, prefix):
+        rc = self.lib.llmgpu_load_train_state(self.h, prefix.encode())
+        if rc:
+            self._err("load_train_state", rc)
+
+    # ------------------------------------------------------------------ counters
+    def step(self):
+        return self.lib.llmgpu_step(self.h)
+
+    def set_step(self, s):
+        self.lib.llmgpu_set_step(self.h, s)
+
+    def skipped_steps(self):
+        return self.lib.llmgpu_skipped_steps(self.h)
+
+    def last_loss(self):
+        return self.lib.llmgpu_last_loss(self.h)
+
+    def last_grad_norm(self):
+        return self.lib.llmgpu_last_grad_norm(self.h)
+
+    def last_timings(self):
+        t = (ctypes.c_float * 6)()
+        self.lib.llmgpu_last_timings(self.h, t)
+        return dict(zip(["forward", "loss", "backward", "allreduce", "optimizer", "total"], list(t)))
+
+    def last_launches(self):
+        return self.lib.llmgpu_last_launches(self.h)
+
+    def stream(self):
+        return self.lib.llmgpu_stream(self.h)
+
+    def set_profile(self, on):
+        self.lib.llmgpu_set_profile(self.h, int(on))
+
+    def gemm_stats(self, reset=False):
+        f, ms, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_int()
+        self.lib.llmgpu_gemm_stats(self.h, ctypes.byref(f), ctypes.byref(ms), ctypes.byref(n),
+                                   int(reset))
+        return f.value, ms.value, n.value

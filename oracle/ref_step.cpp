@@ -13,16 +13,21 @@
 //   gnorm.f32      Trainer::last_grad_norm() after each step
 //   timing.txt     wall seconds per optimizer step
 //
-// usage: ref_step <ckpt.bin> <tokens.i32> <B> <T> <outdir> [key=value ...]
+// usage: ref_step <ckpt.bin or -> <tokens.i32 or -> <B> <T> <outdir> [key=value ...]
+//   "-" as checkpoint keeps the reference initialisation (vocab/layers/heads/embd/block keys);
+//   "-" as token file draws seeded Zipf(1.1) ids (key seed).
 //   keys: steps, lr, b1, b2, eps, wd, clip, tied (0/1), rmsnorm (0/1), mamba (0/1),
 //         d_inner, d_state, dt_rank, conv_kernel, timing_only (0/1)
+#include <algorithm>
 #include <chrono>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <iostream>
 #include <map>
+#include <random>
 #include <string>
 #include <vector>
 
@@ -87,7 +92,19 @@ int main(int argc, char** argv) {
 
     uint32_t version = 0;
     size_t hdr[5] = {0}, mh[4] = {0};
-    if (!read_header(ckpt, version, hdr, mh)) {
+    const bool no_ckpt = (ckpt == "-");  // keep the reference constructors' initialisation
+    if (no_ckpt) {
+        version = getf("mamba", 0) != 0 ? 4 : 3;
+        hdr[0] = (size_t)getf("vocab", 50257);
+        hdr[1] = (size_t)getf("layers", 12);
+        hdr[2] = (size_t)getf("heads", 12);
+        hdr[3] = (size_t)getf("embd", 768);
+        hdr[4] = (size_t)getf("block", 1024);
+        mh[0] = (size_t)getf("d_inner", 0);
+        mh[1] = (size_t)getf("d_state", 16);
+        mh[2] = (size_t)getf("dt_rank", 0);
+        mh[3] = (size_t)getf("conv_kernel", 4);
+    } else if (!read_header(ckpt, version, hdr, mh)) {
         std::fprintf(stderr, "bad checkpoint %s\n", ckpt.c_str());
         return 3;
     }
@@ -107,10 +124,19 @@ int main(int argc, char** argv) {
         c.conv_kernel = mh[3];
     }
     llm::GPT model(c);
-    model.load_binary(ckpt);
+    if (!no_ckpt) model.load_binary(ckpt);
 
     std::vector<int> tokens(B * T * (size_t)steps);
-    {
+    if (tokpath == "-") {
+        // seeded Zipf(1.1) ids (rank k with probability ~ k^-1.1), when no token file is given
+        std::mt19937_64 rng((uint64_t)getf("seed", 1234));
+        std::vector<double> cdf(c.vocab_size);
+        double acc = 0;
+        for (size_t k = 0; k < c.vocab_size; ++k) cdf[k] = (acc += std::pow((double)(k + 1), -1.1));
+        std::uniform_real_distribution<double> u(0.0, acc);
+        for (auto& t : tokens)
+            t = (int)(std::lower_bound(cdf.begin(), cdf.end(), u(rng)) - cdf.begin());
+    } else {
         std::ifstream in(tokpath, std::ios::binary);
         std::vector<int32_t> raw;
         in.seekg(0, std::ios::end);

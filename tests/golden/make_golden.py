@@ -29,16 +29,17 @@ from oracle import gpt_oracle as go  # noqa: E402
 
 REF = os.path.join(ROOT, "oracle", "_ref", "ref_step")
 
+# Transformer cases use head_dim 32 so that the device kernels can run them directly.
 CASES = {
     # LayerNorm + GELU FFN + tied head: the transformer path of configs 1 and 2
-    "gpt_ln_gelu_tied": dict(cfg=dict(vocab=64, n_layers=2, n_heads=2, n_embd=32, block_size=16),
+    "gpt_ln_gelu_tied": dict(cfg=dict(vocab=64, n_layers=2, n_heads=1, n_embd=32, block_size=16),
                              B=3, T=16, steps=2, seed=1, tok_seed=0),
     # RMSNorm + untied lm_head
-    "gpt_rms_untied": dict(cfg=dict(vocab=48, n_layers=1, n_heads=2, n_embd=32, block_size=12,
+    "gpt_rms_untied": dict(cfg=dict(vocab=48, n_layers=1, n_heads=1, n_embd=32, block_size=12,
                                     tied=False, rmsnorm=True),
                            B=2, T=12, steps=2, seed=2, tok_seed=3),
     # T > 128: the forward takes flash_attention_full (src/attention.cpp:68-75)
-    "gpt_flash_t136": dict(cfg=dict(vocab=32, n_layers=1, n_heads=2, n_embd=16, block_size=136),
+    "gpt_flash_t136": dict(cfg=dict(vocab=32, n_layers=1, n_heads=1, n_embd=32, block_size=136),
                            B=1, T=136, steps=1, seed=4, tok_seed=5),
     # Mamba blocks (checkpoint v4), RMSNorm; larger x_proj/dt_proj so that softplus(dt)
     # falls both inside and outside the clamp range [1e-3, 0.1]

@@ -1,0 +1,118 @@
+"""Per-kernel parity on the GPU: embedding gather (bit-exact), LayerNorm/RMSNorm forward and
+backward, fused cross-entropy and causal attention forward/backward, each through the
+kernel-level C ABI and checked against a plain fp32/fp64 reference of the same op."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+def _rel(a, b):
+    a, b = a.double(), b.double()
+    return float((a - b).norm() / (b.norm() + 1e-30))
+
+
+def test_embedding_gather_bit_exact(cuda):
+    """x = wte[tok mod V] + wpe[t] (src/model.cpp:149-157), OOV ids wrap modulo V."""
+    from llmgpu import ops
+    g = torch.Generator().manual_seed(0)
+    B, T, C, V = 3, 37, 64, 101
+    wte = torch.randn(V, C, generator=g).to(cuda)
+    wpe = torch.randn(T, C, generator=g).to(cuda)
+    tok = torch.randint(-300, 300, (B, T), generator=g, dtype=torch.int32)
+    x = ops.embed(tok.to(cuda), wte, wpe, B, T)
+    t = tok.long() % V
+    want = wte.cpu()[t.reshape(-1)] + wpe.cpu().repeat(B, 1)
+    assert torch.equal(x.cpu(), want)
+
+
+@pytest.mark.parametrize("rms", [False, True])
+@pytest.mark.parametrize("C", [128, 768, 1024])
+def test_norm_forward_backward(cuda, rms, C):
+    from llmgpu import ops
+    g = torch.Generator().manual_seed(C + rms)
+    rows = 300
+    x = (torch.randn(rows, C, generator=g) * 2 + 0.5).to(cuda)
+    gamma = (1 + 0.1 * torch.randn(C, generator=g)).to(cuda)
+    beta = (0.1 * torch.randn(C, generator=g)).to(cuda)
+    y, mean, rstd = ops.norm_fwd(x, gamma, beta, rms)
+    xd = x.double().requires_grad_(True)
+    if rms:
+        ref = xd / torch.sqrt((xd * xd).mean(-1, keepdim=True) + 1e-5) * gamma.double()
+    else:
+        mu = xd.mean(-1, keepdim=True)
+        var = ((xd - mu) ** 2).mean(-1, keepdim=True)
+        ref = (xd - mu) / torch.sqrt(var + 1e-5) * gamma.double() + beta.double()
+    assert _rel(y.float(), ref.detach()) < 5e-3
+    dy = torch.randn(rows, C, generator=g).to(cuda)
+    resid = torch.randn(rows, C, generator=g).to(cuda)
+    dx, dx16, dg, db, ds = ops.norm_bwd(dy, x, gamma, mean, rstd, resid, rms)
+    ref.backward(dy.double())
+    want_dx = xd.grad + resid.double()
+    assert _rel(dx, want_dx) < 1e-5
+    assert _rel(dx16.float(), want_dx) < 5e-3
+    xh = (ref.detach() - (0 if rms else beta.double())) / gamma.double()
+    assert _rel(dg, (dy.double() * xh).sum(0)) < 1e-5
+    if not rms:
+        assert _rel(db, dy.double().sum(0)) < 1e-5
+    assert _rel(ds, want_dx.sum(0)) < 1e-5
+
+
+@pytest.mark.parametrize("V,Vp", [(256, 256), (50257, 50304), (300, 384)])
+def test_cross_entropy(cuda, V, Vp):
+    """loss = lse - logit[tgt]; dlogits = (softmax - onehot) * scale, zero in padding
+    (src/loss.cpp:6-40); targets are the tokens mod V."""
+    from llmgpu import ops
+    g = torch.Generator().manual_seed(V)
+    rows = 64
+    logits = torch.zeros(rows, Vp)
+    logits[:, :V] = torch.randn(rows, V, generator=g) * 2
+    l16 = logits.to(torch.bfloat16)
+    tok = torch.randint(-V, 2 * V, (rows,), generator=g, dtype=torch.int32)
+    scale = 1.0 / rows
+    d = l16.clone().to(cuda)
+    loss = ops.cross_entropy(d, V, tok.to(cuda), scale)
+    lf = l16.float()[:, :V].double()
+    tgt = tok.long() % V
+    lse = torch.logsumexp(lf, -1)
+    want_loss = lse - lf[torch.arange(rows), tgt]
+    assert torch.allclose(loss.cpu().double(), want_loss, rtol=1e-4, atol=1e-4)
+    p = torch.softmax(lf, -1)
+    p[torch.arange(rows), tgt] -= 1
+    want = p * scale
+    got = d.cpu().float()
+    assert _rel(got[:, :V], want) < 1e-2
+    assert torch.count_nonzero(got[:, V:]) == 0
+
+
+def _attn_ref(qkv, B, T, H, hd):
+    C = H * hd
+    q, k, v = qkv.double().reshape(B, T, 3, H, hd).permute(2, 0, 3, 1, 4)
+    s = q @ k.transpose(-1, -2) / np.sqrt(np.float32(hd))
+    mask = torch.triu(torch.ones(T, T, dtype=torch.bool, device=s.device), 1)
+    s = s.masked_fill(mask, float("-inf"))
+    a = torch.softmax(s, -1)
+    o = a @ v
+    return o.permute(0, 2, 1, 3).reshape(B * T, C), torch.logsumexp(s, -1)
+
+
+@pytest.mark.parametrize("B,T,H,hd", [(2, 128, 4, 32), (1, 200, 2, 64), (2, 64, 12, 64),
+                                      (1, 1024, 2, 64), (3, 33, 1, 32)])
+def test_attention_forward_backward(cuda, B, T, H, hd):
+    from llmgpu import ops
+    g = torch.Generator().manual_seed(T * H + hd)
+    C = H * hd
+    qkv = (torch.randn(B * T, 3 * C, generator=g)).to(torch.bfloat16).to(cuda)
+    out, lse = ops.attention_fwd(qkv, B, T, H, hd)
+    q = qkv.float().double().requires_grad_(True)
+    ref, ref_lse = _attn_ref(q, B, T, H, hd)
+    assert _rel(out.float(), ref.detach()) < 1e-2
+    assert torch.allclose(lse.double(), ref_lse.detach(), atol=2e-3, rtol=1e-3)
+    dout = torch.randn(B * T, C, generator=g).to(torch.bfloat16).to(cuda)
+    dqkv = ops.attention_bwd(qkv, out, dout, lse, B, T, H, hd)
+    ref.backward(dout.double())
+    want = q.grad
+    for part in range(3):
+        sl = slice(part * C, (part + 1) * C)
+        assert _rel(dqkv[:, sl].float(), want[:, sl]) < 2e-2, part
