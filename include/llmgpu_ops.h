@@ -39,6 +39,26 @@ int llmgpu_op_gemm(const void* A, long long lda, int a_mn_major, const void* B, 
                    int splits, float* workspace, int col_group, long long group_stride, int bn,
                    int* err, void* stream);
 
+/* Split-K form of llmgpu_op_gemm (f32 output, epi 1) that allocates no device memory.
+ * It has no counterpart in the reference.
+ * For callers that cannot call cudaMalloc: code that draws every byte from its own
+ * pre-reserved pool or custom allocator, or that runs under a fixed memory budget, and so
+ * cannot provide the `workspace` that llmgpu_op_gemm needs when splits > 1. Its split-K
+ * partial sums live in a fixed 16 MiB device array inside the library (4,194,304 floats),
+ * which every GPU that loads the library holds until the process exits.
+ *   - Requires splits * M * N <= 4194304; larger sizes return -101 and do nothing.
+ *   - The first call on a device looks up that array's device address (once per device);
+ *     make that first call before any stream capture.
+ *   - All calls share the one array: calls whose kernels overlap on the GPU (different
+ *     streams, concurrent threads) race and must be serialised by the caller. Each call
+ *     overwrites the part it uses, so no clearing is needed.
+ *   - No cudaMalloc, cudaFree or other allocating call is made.
+ * Same arguments and result as llmgpu_op_gemm with epi = 1. Returns 0 or a negative status. */
+int llmgpu_op_gemm_splitk_noalloc(const void* A, long long lda, int a_mn_major, const void* B,
+                                  long long ldb, int b_mn_major, int M, int N, int K, float* out,
+                                  long long ldo, int accumulate, int splits, int col_group,
+                                  long long group_stride, int* err, void* stream);
+
 /* x[b*T+t,:] = wte[tok mod V,:] + wpe[t,:] in fp32 (src/model.cpp:149-157). */
 int llmgpu_op_embed(const int32_t* tokens, const float* wte, const float* wpe, float* x, int B,
                     int T, int C, int V, void* stream);
