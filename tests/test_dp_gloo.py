@@ -1,0 +1,74 @@
+"""World-size-2 data-parallel semantics on CPU (gloo), with the oracle as the model.
+
+The device path shards the global batch over ranks (B sequences each) and all-reduces the
+mean gradient before a replicated clip + AdamW. That must equal the reference's
+train_step_accum over world*B sequences (src/trainer.cpp:127-169) and mean_reduce_grads
+(src/trainer.cpp:171-182). Here two gloo ranks run the oracle on their shards, average the
+flat gradients with all_reduce, step, and must end with the single-process result.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    from oracle import gpt_oracle as go
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    cfg = go.Cfg(vocab=64, n_layers=1, n_heads=2, n_embd=32, block_size=16)
+    params = go.init_params(cfg, seed=3)
+    toks = go.uniform_tokens(64, 4 * 16, seed=4).reshape(4, 16)
+    model = go.Model(cfg, params)
+    names = [n for n, _ in go.param_specs(cfg)]
+    shard = toks[rank * 2:(rank + 1) * 2]
+    acc = [np.zeros_like(model.p[n]) for n in names]
+    for seq in shard:
+        _, G, _ = model.forward_backward(seq)
+        for a, n in zip(acc, names):
+            a += G[n]
+    flat = torch.from_numpy(np.concatenate([a.ravel() / len(shard) for a in acc]))
+    dist.all_reduce(flat)
+    flat /= world
+    grads, off = [], 0
+    for n in names:
+        k = model.p[n].size
+        grads.append(flat[off:off + k].numpy().reshape(model.p[n].shape).copy())
+        off += k
+    go.clip_by_global_norm(grads, 1.0)
+    go.adamw_step([model.p[n] for n in names], grads, go.AdamWState(), go.decay_flags(cfg))
+    q.put((rank, np.concatenate([model.p[n].ravel() for n in names])))
+    dist.destroy_process_group()
+
+
+def test_two_rank_mean_allreduce_equals_accumulation():
+    import multiprocessing as mp
+    from oracle import gpt_oracle as go
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    cfg = go.Cfg(vocab=64, n_layers=1, n_heads=2, n_embd=32, block_size=16)
+    model = go.Model(cfg, go.init_params(cfg, seed=3))
+    toks = go.uniform_tokens(64, 4 * 16, seed=4).reshape(4, 16)
+    go.train_step(model, list(toks), go.AdamWState(), clip=1.0)
+    want = np.concatenate([model.p[n].ravel() for n, _ in go.param_specs(cfg)])
+    np.testing.assert_allclose(out[0], want, rtol=0, atol=1e-9)
+    np.testing.assert_array_equal(out[0], out[1])
