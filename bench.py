@@ -251,8 +251,6 @@ def main():
     # ---------------- value: tokens resident in HBM
     dev_toks = torch.from_numpy(toks[W:W + K].copy()).to(f"cuda:{local}")
     step_bytes = B * T * 4
-    tr.set_profile(True)
-    tr.gemm_stats(reset=True)
     sampler = ClockSampler(local)
     sampler.start()
     barrier()
@@ -265,8 +263,6 @@ def main():
     e1.record(stream)
     barrier()
     ms_dev = e0.elapsed_time(e1) / K
-    gflops, gms, glaunch = tr.gemm_stats(reset=True)
-    tr.set_profile(False)
     # ---------------- e2e: host tokens through the public C ABI
     barrier()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -281,6 +277,15 @@ def main():
     ms_e2e = e2.elapsed_time(e3) / K
     ms_dev, ms_e2e = maxed(ms_dev), maxed(ms_e2e)
     timings = tr.last_timings()
+    # ---------------- GEMM roofline: the same steps with every tcgen05 GEMM launch bracketed
+    # by CUDA events on the library stream (eager execution; not part of `value`)
+    tr.set_profile(True)
+    tr.gemm_stats(reset=True)
+    for i in range(K):
+        tr.train_step_device(dev_toks[i].data_ptr(), B, T)
+    barrier()
+    gflops, gms, glaunch = tr.gemm_stats(reset=True)
+    tr.set_profile(False)
 
     peak, peak_sus, hbm, peak_kind = peaks()
     f_tok, n_mm = algorithmic_flops_per_token()

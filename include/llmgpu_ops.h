@@ -79,11 +79,20 @@ long long llmgpu_op_norm_bwd_work(int rows, int C);
 int llmgpu_op_cross_entropy(void* logits_bf16, int rows, int V, int Vp, const int32_t* tokens,
                             float* row_loss, float scale, float smoothing, void* stream);
 /* Causal attention forward/backward over packed bf16 qkv [B*T, 3C]
- * (src/attention.cpp:35-102, :183-363). dvec: B*H*T floats of scratch. */
+ * (src/attention.cpp:35-102, :183-363). dvec: B*H*T floats of scratch.
+ * rope_cs (nullable): [T][hd/2][2] (cos, sin) of pos * theta^(-2j/hd); when given, Q and K
+ * are rotated per head on load (pairs 2j, 2j+1, as rope_cfg pairs them, src/model.cpp:88-100)
+ * and dQ/dK are returned for the unrotated inputs. */
 int llmgpu_op_attention_fwd(const void* qkv, void* out, float* lse, int B, int T, int H, int hd,
-                            void* stream);
+                            const float* rope_cs, void* stream);
 int llmgpu_op_attention_bwd(const void* qkv, const void* out, const void* dout, const float* lse,
-                            float* dvec, void* dqkv, int B, int T, int H, int hd, void* stream);
+                            float* dvec, void* dqkv, int B, int T, int H, int hd,
+                            const float* rope_cs, void* stream);
+/* SILU-gated FFN activation (src/transformer.cpp:22-30, 76-89) over h13 = [h1 | h3]
+ * ([rows, 2F] bf16): gated = silu(h1) * h3; backward gives dh13 = [dh1 | dh3]. */
+int llmgpu_op_swiglu_fwd(const void* h13, void* gated, int rows, int F, void* stream);
+int llmgpu_op_swiglu_bwd(const void* dgated, const void* h13, void* dh13, int rows, int F,
+                         void* stream);
 
 /* Number of SMs the library sizes persistent grids for (device 0 of the caller). */
 int llmgpu_op_num_sms(void);

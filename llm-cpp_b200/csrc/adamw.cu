@@ -141,31 +141,31 @@ int grad_norm_partials(const float* g, long long n, double* partial, int* nonfin
     if (nblocks != kNormBlocks) return -1;
     cudaMemsetAsync(nonfinite, 0, sizeof(int), s);
     grad_norm_kernel<<<kNormBlocks, kNormThreads, 0, s>>>(g, n, partial, nonfinite);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_status();
 }
 
 int grad_norm_finalize(const double* partial, int nblocks, const int* nonfinite, float clip,
                        float* scal, cudaStream_t s) {
     grad_norm_final_kernel<<<1, 1024, 0, s>>>(partial, nblocks, nonfinite, clip, scal);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_status();
 }
 
 int adamw_update(const AdamParam* params, const AdamChunk* chunks, int nchunks, float* p,
                  const float* g, float* m, float* v, const float* scal, const float* hp,
                  cudaStream_t s) {
     adamw_kernel<<<nchunks, 256, 0, s>>>(params, chunks, p, g, m, v, scal, hp);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_status();
 }
 
 int write_shadows(const AdamParam* params, const AdamChunk* chunks, int nchunks, const float* p,
                   cudaStream_t s) {
     shadow_kernel<<<nchunks, 256, 0, s>>>(params, chunks, p);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_status();
 }
 
 int scale_inplace(float* x, long long n, const float* scale, cudaStream_t s) {
     scale_kernel<<<592, 256, 0, s>>>(x, n, scale);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_status();
 }
 
 }  // namespace llmgpu

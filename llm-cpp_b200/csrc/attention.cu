@@ -143,12 +143,53 @@ __device__ __forceinline__ void mma_pt(float (&acc)[HD / 8][4], const float (&p)
     }
 }
 
+// RoPE on a 64 x HD tile in shared memory: row r holds sequence position pos0 + r; pairs
+// (2j, 2j+1) of every head vector are rotated by angle pos * theta^(-2j/HD), whose
+// (cos, sin) come from `tab` [T][HD/2] (the pairing and frequencies of rope_cfg,
+// src/model.cpp:88-100, with dim = head_dim).
+template <int HD>
+__device__ __forceinline__ void rope_tile(uint8_t* tile, int pos0, int T, const float2* tab) {
+    constexpr int P = HD / 2;
+    for (int i = threadIdx.x; i < BLK * P; i += ATT_THREADS) {
+        const int r = i / P, j = i - r * P;
+        const int pos = pos0 + r;
+        if (pos >= T) continue;
+        __nv_bfloat162* w =
+            reinterpret_cast<__nv_bfloat162*>(tile + swz<HD>(r, j >> 2) + ((j & 3) << 2));
+        const float2 v = __bfloat1622float2(*w);
+        const float2 cs = tab[(long long)pos * P + j];
+        *w = __floats2bfloat162_rn(v.x * cs.x - v.y * cs.y, v.x * cs.y + v.y * cs.x);
+    }
+}
+
+// Inverse RoPE of an accumulator fragment (16 rows x HD, rows row0 and row0 + 8 of this
+// thread): the pair (2j, 2j+1) of n8 block i at columns 2c, 2c+1 is held by one thread.
+template <int HD>
+__device__ __forceinline__ void rope_unrotate_acc(float (&acc)[HD / 8][4], int row0, int T,
+                                                  const float2* tab) {
+    const int c = threadIdx.x & 3;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int pos = row0 + r * 8;
+        if (pos >= T) continue;
+#pragma unroll
+        for (int i = 0; i < HD / 8; ++i) {
+            const int j = i * 4 + c;
+            const float2 cs = tab[(long long)pos * (HD / 2) + j];
+            const float y0 = acc[i][2 * r], y1 = acc[i][2 * r + 1];
+            acc[i][2 * r] = y0 * cs.x + y1 * cs.y;
+            acc[i][2 * r + 1] = -y0 * cs.y + y1 * cs.x;
+        }
+    }
+}
+
 // ---------------------------------------------------------------- forward
 template <int HD>
 __global__ void __launch_bounds__(ATT_THREADS) attn_fwd_kernel(const bf16* __restrict__ qkv,
                                                                bf16* __restrict__ out,
                                                                float* __restrict__ lse, int T,
-                                                               int H, float scale_log2) {
+                                                               int H, float scale_log2,
+                                                               const float2* __restrict__ rope) {
     extern __shared__ __align__(128) uint8_t sm[];
     constexpr int TILE = BLK * HD * 2;
     uint8_t* sQ = sm;
@@ -191,6 +232,11 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_fwd_kernel(const bf16* __res
             cp_async_wait<0>();
         }
         __syncthreads();
+        if (rope) {  // RoPE fused into the Q/K tile loads
+            if (kb == 0) rope_tile<HD>(sQ, q0, T, rope);
+            rope_tile<HD>(sK[cur], kb * BLK, T, rope);
+            __syncthreads();
+        }
         if (kb == 0) load_a_frags<HD>(sQ, warp * 16, qa);
         float s[8][4];
         mma_abt<HD>(s, qa, sK[cur]);
@@ -287,7 +333,8 @@ __global__ void attn_dvec_kernel(const bf16* __restrict__ out, const bf16* __res
 template <int HD>
 __global__ void __launch_bounds__(ATT_THREADS) attn_bwd_dkdv_kernel(
     const bf16* __restrict__ qkv, const bf16* __restrict__ dout, const float* __restrict__ lse,
-    const float* __restrict__ dvec, bf16* __restrict__ dqkv, int T, int H, float scale) {
+    const float* __restrict__ dvec, bf16* __restrict__ dqkv, int T, int H, float scale,
+    const float2* __restrict__ rope) {
     extern __shared__ __align__(128) uint8_t sm[];
     constexpr int TILE = BLK * HD * 2;
     uint8_t* sK = sm;
@@ -346,6 +393,11 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_bwd_dkdv_kernel(
             cp_async_wait<0>();
         }
         __syncthreads();
+        if (rope) {
+            if (qb == kb) rope_tile<HD>(sK, k0, T, rope);
+            rope_tile<HD>(sQ[cur], qb * BLK, T, rope);
+            __syncthreads();
+        }
         if (qb == kb) {
             load_a_frags<HD>(sK, warp * 16, ka);
             load_a_frags<HD>(sV, warp * 16, va);
@@ -380,6 +432,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_bwd_dkdv_kernel(
         mma_pt<HD>(dk, dp, sQ[cur]);
         __syncthreads();
     }
+    if (rope) rope_unrotate_acc<HD>(dk, key0, T, rope);
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
         const int key = key0 + r * 8;
@@ -400,7 +453,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_bwd_dkdv_kernel(
 template <int HD>
 __global__ void __launch_bounds__(ATT_THREADS) attn_bwd_dq_kernel(
     const bf16* __restrict__ qkv, const bf16* __restrict__ dout, const float* __restrict__ lse,
-    const float* __restrict__ dvec, bf16* __restrict__ dqkv, int T, int H, float scale) {
+    const float* __restrict__ dvec, bf16* __restrict__ dqkv, int T, int H, float scale,
+    const float2* __restrict__ rope) {
     extern __shared__ __align__(128) uint8_t sm[];
     constexpr int TILE = BLK * HD * 2;
     uint8_t* sQ = sm;
@@ -451,6 +505,11 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_bwd_dq_kernel(
             cp_async_wait<0>();
         }
         __syncthreads();
+        if (rope) {
+            if (kb == 0) rope_tile<HD>(sQ, q0, T, rope);
+            rope_tile<HD>(sK[cur], kb * BLK, T, rope);
+            __syncthreads();
+        }
         if (kb == 0) {
             load_a_frags<HD>(sQ, warp * 16, qa);
             load_a_frags<HD>(sO, warp * 16, oa);
@@ -473,6 +532,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_bwd_dq_kernel(
         mma_pt<HD>(dq, dp, sK[cur]);
         __syncthreads();
     }
+    if (rope) rope_unrotate_acc<HD>(dq, qrow0, T, rope);
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
         const int q = qrow0 + r * 8;
@@ -493,25 +553,26 @@ void set_smem(K kernel, int bytes) {
 }  // namespace
 
 int attention_forward(const bf16* qkv, bf16* out, float* lse, int B, int T, int H, int hd,
-                      cudaStream_t s) {
+                      const float2* rope, cudaStream_t s) {
     const float scale = 1.0f / sqrtf((float)hd);
     dim3 grid((T + BLK - 1) / BLK, H, B);
     if (hd == 64) {
         const int smem = 5 * BLK * 64 * 2;
         static bool set = false;
         if (!set) { set_smem(attn_fwd_kernel<64>, smem); set = true; }
-        attn_fwd_kernel<64><<<grid, ATT_THREADS, smem, s>>>(qkv, out, lse, T, H, scale * kLog2e);
+        attn_fwd_kernel<64><<<grid, ATT_THREADS, smem, s>>>(qkv, out, lse, T, H, scale * kLog2e, rope);
     } else if (hd == 32) {
         const int smem = 5 * BLK * 32 * 2;
-        attn_fwd_kernel<32><<<grid, ATT_THREADS, smem, s>>>(qkv, out, lse, T, H, scale * kLog2e);
+        attn_fwd_kernel<32><<<grid, ATT_THREADS, smem, s>>>(qkv, out, lse, T, H, scale * kLog2e, rope);
     } else {
         return -1;
     }
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_status();
 }
 
 int attention_backward(const bf16* qkv, const bf16* out, const bf16* dout, const float* lse,
-                       float* dvec, bf16* dqkv, int B, int T, int H, int hd, cudaStream_t s) {
+                       float* dvec, bf16* dqkv, int B, int T, int H, int hd, const float2* rope,
+                       cudaStream_t s) {
     const float scale = 1.0f / sqrtf((float)hd);
     const long long n = (long long)B * T * H;
     attn_dvec_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(out, dout, dvec, B, T, H, hd);
@@ -526,20 +587,20 @@ int attention_backward(const bf16* qkv, const bf16* out, const bf16* dout, const
             set = true;
         }
         attn_bwd_dkdv_kernel<64><<<grid, ATT_THREADS, smem1, s>>>(qkv, dout, lse, dvec, dqkv, T, H,
-                                                                  scale);
+                                                                  scale, rope);
         attn_bwd_dq_kernel<64><<<grid, ATT_THREADS, smem2, s>>>(qkv, dout, lse, dvec, dqkv, T, H,
-                                                                scale);
+                                                                scale, rope);
     } else if (hd == 32) {
         const int smem1 = 6 * BLK * 32 * 2 + 4 * BLK * 4;
         const int smem2 = 6 * BLK * 32 * 2;
         attn_bwd_dkdv_kernel<32><<<grid, ATT_THREADS, smem1, s>>>(qkv, dout, lse, dvec, dqkv, T, H,
-                                                                  scale);
+                                                                  scale, rope);
         attn_bwd_dq_kernel<32><<<grid, ATT_THREADS, smem2, s>>>(qkv, dout, lse, dvec, dqkv, T, H,
-                                                                scale);
+                                                                scale, rope);
     } else {
         return -1;
     }
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_status();
 }
 
 }  // namespace llmgpu

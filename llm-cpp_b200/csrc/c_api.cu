@@ -48,17 +48,71 @@ int validate_bt(Ctx* c, int B, int T) {
     return 0;
 }
 
-// Runs one micro-batch (+ optimizer when `do_step`), eagerly or through the step graph.
-int run_step(Ctx* c, int B, int T, int accumulate, bool do_step, int K) {
-    c->launches = 0;
+int enqueue_step(Ctx* c, int B, int T, int accumulate, bool do_step, int K) {
     c->plan_cursor = 0;
     c->prof_n = 0;
-    cudaMemsetAsync(c->d_out + 1, 0, sizeof(float) * 4, c->stream);
     int rc = run_fwd_bwd(c, B, T, accumulate, true);
     if (rc) return rc;
-    if (do_step) {
-        rc = run_optimizer(c, K);
+    if (do_step) rc = run_optimizer(c, K);
+    return rc;
+}
+
+// Captures the step for (B, T, accumulate, do_step, K) as a CUDA graph. The graph reads
+// the tokens from c->d_tokens and its per-step scalars from pinned host memory, so a
+// replay needs no host work besides the launch. On any capture problem the context falls
+// back to eager execution for good.
+void capture_step(Ctx* c, int B, int T, int accumulate, bool do_step, int K) {
+    if (c->graph) {
+        cudaGraphExecDestroy(c->graph);
+        c->graph = nullptr;
+    }
+    const int saved = c->launches;
+    c->launches = 0;
+    cudaGraph_t g = nullptr;
+    if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        c->use_graph = false;
+        c->launches = saved;
+        return;
+    }
+    const int rc = enqueue_step(c, B, T, accumulate, do_step, K);
+    const cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+    if (rc != 0 || e != cudaSuccess || !g ||
+        cudaGraphInstantiate(&c->graph, g, 0) != cudaSuccess) {
+        c->graph = nullptr;
+        c->use_graph = false;
+        cudaGetLastError();
+    } else {
+        c->graph_B = B;
+        c->graph_T = T;
+        c->graph_acc = accumulate;
+        c->graph_mode = do_step ? 1 : 0;
+        c->graph_K = K;
+        c->graph_launches = c->launches;
+    }
+    if (g) cudaGraphDestroy(g);
+    c->launches = saved;
+}
+
+// Runs one micro-batch (+ optimizer when `do_step`), eagerly or through the step graph.
+int run_step(Ctx* c, int B, int T, int accumulate, bool do_step, int K) {
+    cudaMemsetAsync(c->d_out + 1, 0, sizeof(float) * 4, c->stream);
+    if (do_step) prepare_step_scalars(c, K);
+    const bool graphable = c->use_graph && !c->profile;
+    const bool hit = graphable && c->graph && c->graph_B == B && c->graph_T == T &&
+                     c->graph_acc == accumulate && c->graph_mode == (do_step ? 1 : 0) &&
+                     c->graph_K == K;
+    int rc = 0;
+    if (hit) {
+        if (cudaGraphLaunch(c->graph, c->stream) != cudaSuccess) {
+            c->err = "cudaGraphLaunch failed";
+            return LLMGPU_E_CUDA;
+        }
+        c->launches = c->graph_launches;
+    } else {
+        c->launches = 0;
+        rc = enqueue_step(c, B, T, accumulate, do_step, K);
         if (rc) return rc;
+        if (graphable) capture_step(c, B, T, accumulate, do_step, K);
     }
     if (cudaMemcpyAsync(c->h_out, c->d_out, sizeof(float) * 8, cudaMemcpyDeviceToHost,
                         c->stream) != cudaSuccess)

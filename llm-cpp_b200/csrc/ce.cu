@@ -115,12 +115,12 @@ int cross_entropy_fwd_bwd(bf16* logits, int rows, int V, int Vp, const int32_t* 
         set = true;
     }
     ce_kernel<<<rows, kCeThreads, smem, s>>>(logits, V, Vp, tokens, row_loss, scale, smoothing);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_status();
 }
 
 int mean_reduce(const float* v, int n, float* out, cudaStream_t s) {
     mean_kernel<<<1, 1024, 0, s>>>(v, n, out);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_status();
 }
 
 }  // namespace llmgpu

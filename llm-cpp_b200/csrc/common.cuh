@@ -179,6 +179,12 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, int a_mn_ma
            | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Status of the last launch: 0, or -(1000 + cudaError_t) so callers can name the error.
+inline int launch_status() {
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : -(1000 + (int)e);
+}
+
 // ---------------------------------------------------------------- misc
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

@@ -56,30 +56,81 @@ __global__ void __launch_bounds__(1024) sort_keys_kernel(const int32_t* __restri
     for (int i = threadIdx.x; i < n; i += blockDim.x) keys[i] = sk[i];
 }
 
-// One warp per sorted position; the warp that starts a run of equal tokens sums the
-// run's rows in row order and adds the sum to that token's gradient row.
-__global__ void wte_grad_kernel(const uint64_t* __restrict__ keys, int n,
-                                const float* __restrict__ dx, float* __restrict__ wte_grad, int C) {
-    const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+// Deterministic scatter-add of dx rows into wte_grad, balanced for skewed token
+// frequencies (a Zipf batch repeats its most frequent id ~10% of the time).
+// Sorted positions are cut into pieces: a piece starts where the token changes or at a
+// multiple of kPiece. Stage 1 (one warp per piece start and 128-column slice) sums the
+// piece's rows in row order; a piece that is a whole run is added to its token's row
+// directly, otherwise its sum goes to scratch[piece start]. Stage 2 (one warp per run
+// start of a multi-piece run) sums those piece partials in order and adds the total.
+constexpr int kPiece = 16;
+
+__device__ __forceinline__ uint32_t key_tok(const uint64_t* keys, int i) {
+    return (uint32_t)(keys[i] >> 32);
+}
+
+__global__ void wte_grad_pieces(const uint64_t* __restrict__ keys, int n,
+                                const float* __restrict__ dx, float* __restrict__ wte_grad,
+                                float* __restrict__ scratch, int C) {
+    const int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
-    if (w >= n) return;
-    const uint32_t tok = (uint32_t)(keys[w] >> 32);
-    if (w > 0 && (uint32_t)(keys[w - 1] >> 32) == tok) return;
-    int end = w + 1;
-    while (end < n && (uint32_t)(keys[end] >> 32) == tok) ++end;
-    float* g = wte_grad + (long long)tok * C;
-    for (int c = lane * 4; c < C; c += 128) {
-        float4 acc = reinterpret_cast<float4*>(g + c)[0];
-        for (int k = w; k < end; ++k) {
-            const int row = (int)(keys[k] & 0xffffffffu);
-            float4 v = *reinterpret_cast<const float4*>(dx + (long long)row * C + c);
-            acc.x += v.x;
-            acc.y += v.y;
-            acc.z += v.z;
-            acc.w += v.w;
-        }
-        reinterpret_cast<float4*>(g + c)[0] = acc;
+    const int c = blockIdx.y * 128 + lane * 4;
+    if (p >= n || c >= C) return;
+    const uint32_t tok = key_tok(keys, p);
+    const bool run_start = (p == 0) || key_tok(keys, p - 1) != tok;
+    if (!run_start && (p % kPiece) != 0) return;  // not a piece start
+    const int block_end = min(n, (p / kPiece + 1) * kPiece);
+    int e = p + 1;
+    while (e < block_end && key_tok(keys, e) == tok) ++e;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = p; k < e; ++k) {
+        const int row = (int)(keys[k] & 0xffffffffu);
+        const float4 v = *reinterpret_cast<const float4*>(dx + (long long)row * C + c);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
     }
+    const bool run_end = (e == n) || key_tok(keys, e) != tok;
+    if (run_start && run_end) {
+        float4* g = reinterpret_cast<float4*>(wte_grad + (long long)tok * C + c);
+        float4 o = *g;
+        o.x += acc.x;
+        o.y += acc.y;
+        o.z += acc.z;
+        o.w += acc.w;
+        *g = o;
+    } else {
+        *reinterpret_cast<float4*>(scratch + (long long)p * C + c) = acc;
+    }
+}
+
+__global__ void wte_grad_runs(const uint64_t* __restrict__ keys, int n,
+                              const float* __restrict__ scratch, float* __restrict__ wte_grad,
+                              int C) {
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int c = blockIdx.y * 128 + lane * 4;
+    if (r >= n || c >= C) return;
+    const uint32_t tok = key_tok(keys, r);
+    if (r > 0 && key_tok(keys, r - 1) == tok) return;  // not a run start
+    const int first_end = min(n, (r / kPiece + 1) * kPiece);
+    if (first_end >= n || key_tok(keys, first_end) != tok) return;  // single-piece run
+    float4 acc = *reinterpret_cast<const float4*>(scratch + (long long)r * C + c);
+    for (int q = first_end; q < n && key_tok(keys, q) == tok; q += kPiece) {
+        const float4 v = *reinterpret_cast<const float4*>(scratch + (long long)q * C + c);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+    }
+    float4* g = reinterpret_cast<float4*>(wte_grad + (long long)tok * C + c);
+    float4 o = *g;
+    o.x += acc.x;
+    o.y += acc.y;
+    o.z += acc.z;
+    o.w += acc.w;
+    *g = o;
 }
 
 __global__ void wpe_grad_kernel(const float* __restrict__ dx, float* __restrict__ wpe_grad, int B,
@@ -106,7 +157,7 @@ int embed_forward(const int32_t* tokens, const float* wte, const float* wpe, flo
                   int T, int C, int V, cudaStream_t s) {
     if ((C & 3) != 0) return -1;
     embed_fwd_kernel<<<B * T, 128, 0, s>>>(tokens, wte, wpe, x, B, T, C, V);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_status();
 }
 
 int embed_sort_keys(const int32_t* tokens, int n, int V, uint64_t* keys, cudaStream_t s) {
@@ -121,17 +172,19 @@ int embed_sort_keys(const int32_t* tokens, int n, int V, uint64_t* keys, cudaStr
         set = true;
     }
     sort_keys_kernel<<<1, 1024, smem, s>>>(tokens, n, V, keys);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_status();
 }
 
 int embed_backward(const uint64_t* keys, const float* dx, float* wte_grad, float* wpe_grad, int B,
-                   int T, int C, int accumulate_wpe, cudaStream_t s) {
+                   int T, int C, int accumulate_wpe, float* scratch, cudaStream_t s) {
     if ((C & 3) != 0) return -1;
     const int n = B * T;
-    wte_grad_kernel<<<(n * 32 + 255) / 256, 256, 0, s>>>(keys, n, dx, wte_grad, C);
+    dim3 grid((n + 7) / 8, (C + 127) / 128);
+    wte_grad_pieces<<<grid, 256, 0, s>>>(keys, n, dx, wte_grad, scratch, C);
+    wte_grad_runs<<<grid, 256, 0, s>>>(keys, n, scratch, wte_grad, C);
     const long long m = (long long)T * C / 4;
     wpe_grad_kernel<<<(int)((m + 255) / 256), 256, 0, s>>>(dx, wpe_grad, B, T, C, accumulate_wpe);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_status();
 }
 
 }  // namespace llmgpu

@@ -474,7 +474,7 @@ int launch_bn(const GemmPlan& p, cudaStream_t stream) {
     }
     gemm_bf16_tc_kernel<BN><<<p.grid, kGemmThreads, GemmCfg<BN>::SMEM, stream>>>(p.tmA, p.tmB,
                                                                                 p.args);
-    return cudaGetLastError() == cudaSuccess ? 0 : -11;
+    return launch_status();
 }
 
 }  // namespace
@@ -573,7 +573,7 @@ int gemm_splitk_reduce(const float* partial, int splits, int M, int N, float* ou
     if (blocks > 148 * 16) blocks = 148 * 16;
     splitk_reduce_kernel<<<(int)blocks, threads, 0, stream>>>(partial, splits, M, N, out, ldo,
                                                              col_group, group_stride, accumulate);
-    return cudaGetLastError() == cudaSuccess ? 0 : -2;
+    return launch_status();
 }
 
 }  // namespace llmgpu

@@ -18,9 +18,10 @@ int embed_forward(const int32_t* tokens, const float* wte, const float* wpe, flo
 // `keys` holds n uint64 entries. n <= 16384.
 int embed_sort_keys(const int32_t* tokens, int n, int V, uint64_t* keys, cudaStream_t s);
 // wte_grad[tok, :] += dx[row, :] for every (tok,row) in sorted `keys`, and
-// wpe_grad[t, :] (+)= sum_b dx[b*T+t, :]   (src/model.cpp:314-322)
+// wpe_grad[t, :] (+)= sum_b dx[b*T+t, :]   (src/model.cpp:314-322). `scratch` holds
+// B*T*C floats of piece partial sums.
 int embed_backward(const uint64_t* keys, const float* dx, float* wte_grad, float* wpe_grad,
-                   int B, int T, int C, int accumulate_wpe, cudaStream_t s);
+                   int B, int T, int C, int accumulate_wpe, float* scratch, cudaStream_t s);
 
 // ----------------------------------------------------------------- norms
 // LayerNorm (rms=0, src/tensor.cpp:388-413) or RMSNorm (rms=1, :604-623) of fp32 rows into
@@ -59,12 +60,22 @@ int mean_reduce(const float* v, int n, float* out, cudaStream_t s);
 // Causal multi-head attention over qkv [B*T, 3C] bf16 (q | k | v, heads contiguous):
 // out [B*T, C] bf16, lse [B, H, T] fp32 (natural-log softmax normaliser of scaled scores).
 // src/attention.cpp:35-102 / src/flash_attention.cpp:88-123.
+// rope (nullable): [T][hd/2] (cos, sin) table; when given, Q and K are rotated per head as
+// they are loaded and dQ/dK are rotated back before they are stored.
 int attention_forward(const bf16* qkv, bf16* out, float* lse, int B, int T, int H, int hd,
-                      cudaStream_t s);
+                      const float2* rope, cudaStream_t s);
 // Backward: dqkv [B*T, 3C] bf16 from dout [B*T, C]; dvec [B, H, T] fp32 scratch.
 // src/attention.cpp:183-363.
 int attention_backward(const bf16* qkv, const bf16* out, const bf16* dout, const float* lse,
-                       float* dvec, bf16* dqkv, int B, int T, int H, int hd, cudaStream_t s);
+                       float* dvec, bf16* dqkv, int B, int T, int H, int hd, const float2* rope,
+                       cudaStream_t s);
+
+// ----------------------------------------------------------------- SwiGLU FFN
+// gated[r, j] = silu(h13[r, j]) * h13[r, F + j]   (src/transformer.cpp:22-30)
+int swiglu_forward(const bf16* h13, bf16* gated, int rows, int F, cudaStream_t s);
+// dh13 = [dgated * h3 * silu'(h1) | dgated * silu(h1)]   (src/transformer.cpp:76-89)
+int swiglu_backward(const bf16* dgated, const bf16* h13, bf16* dh13, int rows, int F,
+                    cudaStream_t s);
 
 // ----------------------------------------------------------------- optimizer
 struct AdamParam {

@@ -39,6 +39,9 @@ namespace {
         int r_ = (x);                                                          \
         if (r_ != 0) {                                                         \
             c->err = std::string(#x) + " failed with status " + std::to_string(r_); \
+            if (r_ <= -1000)                                                   \
+                c->err += std::string(" (") +                                  \
+                          cudaGetErrorName((cudaError_t)(-r_ - 1000)) + ")";   \
             return LLMGPU_E_CUDA;                                              \
         }                                                                      \
         c->launches++;                                                         \
@@ -333,6 +336,7 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
     c->cfg = cfg;
     c->rank = rank;
     c->world = world;
+    if (const char* e = std::getenv("LLMGPU_GRAPH")) c->use_graph = std::atoi(e) != 0;
     if (cfg.vocab_size <= 0 || cfg.n_layers <= 0 || cfg.n_embd <= 0 || cfg.block_size <= 0 ||
         max_batch <= 0 || max_seq <= 0 || max_seq > cfg.block_size)
         return fail(c, "invalid configuration");
@@ -348,8 +352,10 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
     c->max_b = max_batch;
     c->max_t = max_seq;
     c->max_bt = max_batch * max_seq;
-    if (cfg.use_mamba || cfg.moe_experts > 0 || cfg.ffn_swiglu || cfg.rope_qk)
+    if (cfg.use_mamba || cfg.moe_experts > 0)
         return fail(c, "configuration not supported yet by the device kernels");
+    c->swiglu = cfg.ffn_swiglu != 0;
+    const int FH = c->swiglu ? 2 * c->F : c->F;  // width of the FFN up-projection output
     if (c->hd != 32 && c->hd != 64) return fail(c, "head_dim must be 32 or 64");
     if (c->C % 32 != 0 || c->F % 32 != 0) return fail(c, "n_embd and ffn hidden must be multiples of 32");
     if (c->max_bt > 16384) return fail(c, "at most 16384 tokens per micro-batch");
@@ -376,7 +382,7 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
     // bf16 shadows laid out for the GEMMs
     size_t sh = (size_t)c->Vp * C;                            // wte16 [Vp, C]
     if (!cfg.weight_tying) sh += (size_t)C * c->Vp;           // lm16 [C, Vp]
-    sh += (size_t)L * ((size_t)C * 3 * C + (size_t)C * C + 2 * (size_t)C * F + 64 * 4);
+    sh += (size_t)L * ((size_t)C * 3 * C + (size_t)C * C + (size_t)C * FH + (size_t)C * F + 64 * 4);
     c->shadow_elems = sh;
     if (dalloc(c, &c->shadow_arena, sh)) return fail(c, "");
     {
@@ -398,7 +404,7 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
             auto& b = c->blocks[l];
             bf16* wqkv = take((size_t)C * 3 * C);
             bf16* wo = take((size_t)C * C);
-            bf16* w1 = take((size_t)C * F);
+            bf16* w1 = take((size_t)C * FH);  // [C, F] or, for SwiGLU, [W1 | W3] as [C, 2F]
             bf16* w2 = take((size_t)F * C);
             c->wqkv16.push_back(wqkv);
             c->wo16.push_back(wo);
@@ -411,10 +417,29 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
             c->params[b.Wo].shadow = wo;
             c->params[b.Wo].shadow_ld = C;
             c->params[b.W1].shadow = w1;
-            c->params[b.W1].shadow_ld = F;
+            c->params[b.W1].shadow_ld = FH;
+            if (b.W3 >= 0) {
+                c->params[b.W3].shadow = w1 + F;
+                c->params[b.W3].shadow_ld = FH;
+            }
             c->params[b.W2].shadow = w2;
             c->params[b.W2].shadow_ld = C;
         }
+    }
+    // RoPE (cos, sin) table [max_t][hd/2] for the rotation fused into the attention loads
+    if (cfg.rope_qk) {
+        const int P = c->hd / 2;
+        std::vector<float> tab((size_t)max_seq * P * 2);
+        for (int pos = 0; pos < max_seq; ++pos)
+            for (int j = 0; j < P; ++j) {
+                const double freq = std::pow((double)cfg.rope_theta, -2.0 * j / (double)c->hd);
+                const double ang = pos * freq;
+                tab[((size_t)pos * P + j) * 2] = (float)std::cos(ang);
+                tab[((size_t)pos * P + j) * 2 + 1] = (float)std::sin(ang);
+            }
+        if (dalloc(c, &c->rope, tab.size() / 2) ||
+            copy_sync(c, c->rope, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice))
+            return fail(c, "");
     }
 
     // activations
@@ -427,7 +452,7 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
             dalloc(c, &a.rstd1, BT) || dalloc(c, &a.qkv, (size_t)BT * 3 * C) ||
             dalloc(c, &a.att, (size_t)BT * C) || dalloc(c, &a.lse, (size_t)BT * c->H) ||
             dalloc(c, &a.ln2, (size_t)BT * C) || dalloc(c, &a.mean2, BT) ||
-            dalloc(c, &a.rstd2, BT) || dalloc(c, &a.h, (size_t)BT * F) ||
+            dalloc(c, &a.rstd2, BT) || dalloc(c, &a.h, (size_t)BT * FH) ||
             dalloc(c, &a.act, (size_t)BT * F))
             return fail(c, "");
     }
@@ -437,20 +462,21 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
         dalloc(c, &c->dy, (size_t)BT * C) || dalloc(c, &c->dln, (size_t)BT * C) ||
         dalloc(c, &c->dres16, (size_t)BT * C) || dalloc(c, &c->dy16, (size_t)BT * C) ||
         dalloc(c, &c->datt, (size_t)BT * C) || dalloc(c, &c->dqkv, (size_t)BT * 3 * C) ||
-        dalloc(c, &c->dh, (size_t)BT * F) || dalloc(c, &c->dvec, (size_t)BT * c->H) ||
+        dalloc(c, &c->dh, (size_t)BT * FH) || dalloc(c, &c->dvec, (size_t)BT * c->H) ||
+        (c->swiglu && dalloc(c, &c->dact, (size_t)BT * F)) ||
         dalloc(c, &c->partial, (size_t)nparts * 3 * C) ||
         dalloc(c, &c->colwork, colsum_work_floats(F > C ? F : C)))
         return fail(c, "");
-    c->splitws_floats = (size_t)8 * C * (F > 3 * C ? F : 3 * C);
+    c->splitws_floats = (size_t)8 * C * (FH > 3 * C ? FH : 3 * C);
     if (dalloc(c, &c->splitws, c->splitws_floats)) return fail(c, "");
     if (dalloc(c, &c->d_tokens, BT) || dalloc(c, &c->d_keys, BT) ||
-        dalloc(c, &c->d_row_loss, BT) || dalloc(c, &c->d_out, 8) || dalloc(c, &c->d_hp, 8) ||
+        dalloc(c, &c->d_row_loss, BT) || dalloc(c, &c->d_out, 8) || dalloc(c, &c->d_hp, 16) ||
         dalloc(c, &c->d_normpart, grad_norm_blocks()) || dalloc(c, &c->d_nonfinite, 1) ||
         dalloc(c, &c->d_err, 1) || dalloc(c, &c->d_kscale, 1))
         return fail(c, "");
     if (cudaMallocHost(&c->h_tokens, sizeof(int32_t) * BT) != cudaSuccess ||
         cudaMallocHost(&c->h_out, sizeof(float) * 8) != cudaSuccess ||
-        cudaMallocHost(&c->h_hp, sizeof(float) * 8) != cudaSuccess ||
+        cudaMallocHost(&c->h_hp, sizeof(float) * 16) != cudaSuccess ||
         cudaMallocHost(&c->h_err, sizeof(int)) != cudaSuccess)
         return fail(c, "cudaMallocHost failed");
 
@@ -522,6 +548,7 @@ void ctx_destroy(Ctx* c) {
     F(c->xL); F(c->lnf); F(c->meanf); F(c->rstdf); F(c->logits); F(c->dres); F(c->dy);
     F(c->dln); F(c->dres16); F(c->dy16); F(c->datt); F(c->dqkv); F(c->dh); F(c->dvec);
     F(c->partial); F(c->colwork); F(c->splitws); F(c->d_tokens); F(c->d_keys);
+    F(c->dact); F(c->rope);
     F(c->d_row_loss); F(c->d_out); F(c->d_hp); F(c->d_normpart); F(c->d_nonfinite); F(c->d_err);
     F(c->d_aparams); F(c->d_chunks); F(c->d_kscale);
     if (c->h_tokens) cudaFreeHost(c->h_tokens);
@@ -537,6 +564,20 @@ void ctx_destroy(Ctx* c) {
 }
 
 // ---------------------------------------------------------------------------- step
+namespace {
+// Phase timing events. While the step is being captured they are recorded as external
+// events so that they also fire at every replay (the external flag is only valid during
+// capture).
+void mark(Ctx* c, int i) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(c->stream, &st);
+    if (st == cudaStreamCaptureStatusActive)
+        cudaEventRecordWithFlags(c->ev[i], c->stream, cudaEventRecordExternal);
+    else
+        cudaEventRecord(c->ev[i], c->stream);
+}
+}  // namespace
+
 int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
     const int C = c->C, F = c->F, H = c->H, hd = c->hd, L = c->L, V = c->V, Vp = c->Vp;
     const int BT = B * T;
@@ -547,13 +588,18 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
     auto gp = [&](int i) { return G + c->params[i].offset; };
     auto pp = [&](int i) { return c->p + c->params[i].offset; };
 
-    cudaEventRecord(c->ev[0], s);
+    mark(c, 0);
     // deterministic token sort for the embedding backward, overlapped on the side stream
     if (backward) {
         CK(cudaEventRecord(c->ev_keys, s));
         CK(cudaStreamWaitEvent(c->side, c->ev_keys, 0));
-        int rc = embed_sort_keys(c->d_tokens, BT, V, c->d_keys, c->side);
-        if (rc) { c->err = "embed_sort_keys"; return LLMGPU_E_CUDA; }
+        const int rc = embed_sort_keys(c->d_tokens, BT, V, c->d_keys, c->side);
+        if (rc) {
+            c->err = "embed_sort_keys failed with status " + std::to_string(rc);
+            if (rc <= -1000)
+                c->err += std::string(" (") + cudaGetErrorName((cudaError_t)(-rc - 1000)) + ")";
+            return LLMGPU_E_CUDA;
+        }
         c->launches++;
         CK(cudaEventRecord(c->ev_keys, c->side));
     }
@@ -567,16 +613,23 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
         int rc = gemm(c, a.ln1, C, 0, c->wqkv16[l], 3 * C, 1, BT, 3 * C, C,
                       epi_args(kEpiStoreBF16, a.qkv, 3 * C));
         if (rc) return rc;
-        KC(attention_forward(a.qkv, a.att, a.lse, B, T, H, hd, s));
+        KC(attention_forward(a.qkv, a.att, a.lse, B, T, H, hd, c->rope, s));
         GemmArgs r = epi_args(kEpiResidF32, a.y, C);
         r.resid = a.x;
         r.ldr = C;
         if ((rc = gemm(c, a.att, C, 0, c->wo16[l], C, 1, BT, C, C, r))) return rc;
         KC(norm_forward(a.y, pp(b.ln2g), pp(b.ln2b), a.ln2, a.mean2, a.rstd2, BT, C, rms, s));
-        GemmArgs ge = epi_args(kEpiGeluBF16, a.act, F);
-        ge.aux = a.h;
-        ge.ld_aux = F;
-        if ((rc = gemm(c, a.ln2, C, 0, c->w1_16[l], F, 1, BT, F, C, ge))) return rc;
+        if (c->swiglu) {  // h13 = ln2 [W1 | W3]; act = silu(h1) * h3 (src/transformer.cpp:22-30)
+            if ((rc = gemm(c, a.ln2, C, 0, c->w1_16[l], 2 * F, 1, BT, 2 * F, C,
+                           epi_args(kEpiStoreBF16, a.h, 2 * F))))
+                return rc;
+            KC(swiglu_forward(a.h, a.act, BT, F, s));
+        } else {
+            GemmArgs ge = epi_args(kEpiGeluBF16, a.act, F);
+            ge.aux = a.h;
+            ge.ld_aux = F;
+            if ((rc = gemm(c, a.ln2, C, 0, c->w1_16[l], F, 1, BT, F, C, ge))) return rc;
+        }
         GemmArgs r2 = epi_args(kEpiResidF32, xnext, C);
         r2.resid = a.y;
         r2.ldr = C;
@@ -593,12 +646,12 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
                       epi_args(kEpiStoreBF16, c->logits, Vp));
         if (rc) return rc;
     }
-    cudaEventRecord(c->ev[1], s);
+    mark(c, 1);
     // ------------------------------------------------------------------ loss
     KC(cross_entropy_fwd_bwd(c->logits, BT, V, Vp, c->d_tokens, c->d_row_loss, 1.0f / (float)BT,
                              c->smoothing, s));
     KC(mean_reduce(c->d_row_loss, BT, c->d_out, s));
-    cudaEventRecord(c->ev[2], s);
+    mark(c, 2);
     if (!backward) return 0;
     // ------------------------------------------------------------------ backward
     int rc;
@@ -636,18 +689,38 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
         w2.accumulate = acc;
         if ((rc = gemm(c, a.act, F, 1, c->dres16, C, 1, F, C, BT, w2, choose_splits(c, F, C, BT))))
             return rc;
-        GemmArgs dg = epi_args(kEpiDGeluBF16, c->dh, F);
-        dg.aux = a.h;
-        dg.ld_aux = F;
-        if ((rc = gemm(c, c->dres16, C, 0, c->w2_16[l], C, 0, BT, F, C, dg))) return rc;
-        GemmArgs w1 = epi_args(kEpiStoreF32, gp(b.W1), F);
-        w1.accumulate = acc;
-        if ((rc = gemm(c, a.ln2, C, 1, c->dh, F, 1, C, F, BT, w1, choose_splits(c, C, F, BT))))
-            return rc;
-        KC(colsum_bf16(c->dh, F, BT, F, gp(b.b1), acc, c->colwork, s));
-        if ((rc = gemm(c, c->dh, F, 0, c->w1_16[l], F, 0, BT, C, F,
-                       epi_args(kEpiStoreF32, c->dln, C))))
-            return rc;
+        if (c->swiglu) {  // src/transformer.cpp:41-119
+            // dgated = dY W2^T, then dh13 = [dh1 | dh3]
+            if ((rc = gemm(c, c->dres16, C, 0, c->w2_16[l], C, 0, BT, F, C,
+                           epi_args(kEpiStoreBF16, c->dact, F))))
+                return rc;
+            KC(swiglu_backward(c->dact, a.h, c->dh, BT, F, s));
+            // dW1 | dW3 from one GEMM, written into the two parameter gradients
+            GemmArgs w13 = epi_args(kEpiStoreF32, gp(b.W1), F);
+            w13.accumulate = acc;
+            w13.col_group = F;
+            w13.group_stride = c->params[b.W3].offset - c->params[b.W1].offset;
+            if ((rc = gemm(c, a.ln2, C, 1, c->dh, 2 * F, 1, C, 2 * F, BT, w13,
+                           choose_splits(c, C, 2 * F, BT))))
+                return rc;
+            KC(colsum_bf16(c->dh, 2 * F, BT, F, gp(b.b1), acc, c->colwork, s));  // db1 = sum dh1
+            if ((rc = gemm(c, c->dh, 2 * F, 0, c->w1_16[l], 2 * F, 0, BT, C, 2 * F,
+                           epi_args(kEpiStoreF32, c->dln, C))))
+                return rc;
+        } else {
+            GemmArgs dg = epi_args(kEpiDGeluBF16, c->dh, F);
+            dg.aux = a.h;
+            dg.ld_aux = F;
+            if ((rc = gemm(c, c->dres16, C, 0, c->w2_16[l], C, 0, BT, F, C, dg))) return rc;
+            GemmArgs w1 = epi_args(kEpiStoreF32, gp(b.W1), F);
+            w1.accumulate = acc;
+            if ((rc = gemm(c, a.ln2, C, 1, c->dh, F, 1, C, F, BT, w1, choose_splits(c, C, F, BT))))
+                return rc;
+            KC(colsum_bf16(c->dh, F, BT, F, gp(b.b1), acc, c->colwork, s));
+            if ((rc = gemm(c, c->dh, F, 0, c->w1_16[l], F, 0, BT, C, F,
+                           epi_args(kEpiStoreF32, c->dln, C))))
+                return rc;
+        }
         KC(norm_backward(c->dln, a.y, pp(b.ln2g), a.mean2, a.rstd2, c->dres, c->dy, c->dy16,
                          c->partial, BT, C, rms, &nparts, s));
         KC(reduce_partials(c->partial, nparts, C, gp(b.ln2g), rms ? nullptr : gp(b.ln2b), nullptr,
@@ -660,7 +733,8 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
         if ((rc = gemm(c, c->dy16, C, 0, c->wo16[l], C, 0, BT, C, C,
                        epi_args(kEpiStoreBF16, c->datt, C))))
             return rc;
-        KC(attention_backward(a.qkv, a.att, c->datt, a.lse, c->dvec, c->dqkv, B, T, H, hd, s));
+        KC(attention_backward(a.qkv, a.att, c->datt, a.lse, c->dvec, c->dqkv, B, T, H, hd,
+                              c->rope, s));
         GemmArgs wq = epi_args(kEpiStoreF32, gp(b.Wq), C);
         wq.accumulate = acc;
         wq.col_group = C;
@@ -678,18 +752,21 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
     }
     // embedding scatter (src/model.cpp:314-322)
     CK(cudaStreamWaitEvent(s, c->ev_keys, 0));
-    KC(embed_backward(c->d_keys, c->dres, gp(c->i_wte), gp(c->i_wpe), B, T, C, acc, s));
-    cudaEventRecord(c->ev[3], s);
+    // c->dy is free once the last block's backward is done: piece partials go there
+    KC(embed_backward(c->d_keys, c->dres, gp(c->i_wte), gp(c->i_wpe), B, T, C, acc, c->dy, s));
+    mark(c, 3);
     return 0;
 }
 
 int run_optimizer(Ctx* c, int K) {
     cudaStream_t s = c->stream;
+    // Per-step scalars come from pinned host memory (c->h_hp, filled by
+    // prepare_step_scalars before the step is launched), so that a captured step graph
+    // reads the current values at every replay.
+    CK(cudaMemcpyAsync(c->d_hp, c->h_hp, sizeof(float) * 16, cudaMemcpyHostToDevice, s));
     if (K > 1) {
         // train_step_accum averages the accumulated gradients (src/trainer.cpp:148-150)
-        const float inv = 1.0f / (float)K;
-        CK(cudaMemcpyAsync(c->d_kscale, &inv, sizeof(float), cudaMemcpyHostToDevice, s));
-        KC(scale_inplace(c->g, c->n_floats, c->d_kscale, s));
+        KC(scale_inplace(c->g, c->n_floats, c->d_hp + 8, s));
     }
     if (c->world > 1) {
         ncclResult_t r = ncclAllReduce(c->g, c->g, (size_t)c->n_floats, ncclFloat, ncclAvg,
@@ -700,11 +777,19 @@ int run_optimizer(Ctx* c, int K) {
         }
         c->launches++;
     }
-    cudaEventRecord(c->ev[4], s);
+    mark(c, 4);
     KC(grad_norm_partials(c->g, c->n_floats, c->d_normpart, c->d_nonfinite, grad_norm_blocks(), s));
     KC(grad_norm_finalize(c->d_normpart, grad_norm_blocks(), c->d_nonfinite, c->clip, c->d_out + 1, s));
-    // Adam step counter advances only for steps that are not skipped; the bias corrections
-    // are prepared for t+1 and the host rolls t back if the device reports a skip.
+    KC(adamw_update(c->d_aparams, c->d_chunks, c->nchunks, c->p, c->g, c->m, c->v, c->d_out + 1,
+                    c->d_hp, s));
+    mark(c, 5);
+    return 0;
+}
+
+// Host-side scalars of the next optimizer step. The Adam step counter advances only for
+// steps that are not skipped: the bias corrections are prepared for t+1 and the caller
+// rolls t back if the device reports a skip.
+void prepare_step_scalars(Ctx* c, int K) {
     c->adam_t += 1;
     c->h_hp[0] = c->lr;
     c->h_hp[1] = c->b1;
@@ -714,11 +799,7 @@ int run_optimizer(Ctx* c, int K) {
     c->h_hp[5] = (float)(1.0 - std::pow((double)c->b1, (double)c->adam_t));
     c->h_hp[6] = (float)(1.0 - std::pow((double)c->b2, (double)c->adam_t));
     c->h_hp[7] = 1.0f;
-    CK(cudaMemcpyAsync(c->d_hp, c->h_hp, sizeof(float) * 8, cudaMemcpyHostToDevice, s));
-    KC(adamw_update(c->d_aparams, c->d_chunks, c->nchunks, c->p, c->g, c->m, c->v, c->d_out + 1,
-                    c->d_hp, s));
-    cudaEventRecord(c->ev[5], s);
-    return 0;
+    c->h_hp[8] = 1.0f / (float)(K > 0 ? K : 1);
 }
 
 int ctx_sync_check(Ctx* c) {

@@ -70,6 +70,8 @@ struct Ctx {
     bf16* wte16 = nullptr;   // [Vp, C]   tied head / embedding shadow
     bf16* lm16 = nullptr;    // [C, Vp]   untied head shadow
     std::vector<bf16*> wqkv16, wo16, w1_16, w2_16;
+    bool swiglu = false;
+    float2* rope = nullptr;  // [max_t][hd/2] (cos, sin) when rope_qk
 
     // activations
     std::vector<BlockAct> act;
@@ -92,7 +94,7 @@ struct Ctx {
     uint64_t* d_keys = nullptr;
     float* d_row_loss = nullptr;
     float* d_out = nullptr;        // [0] loss [1] pre-clip norm [2] clip scale [3] post norm [4] skip
-    float* d_hp = nullptr;         // 8 AdamW scalars
+    float* d_hp = nullptr;         // [0..7] AdamW scalars, [8] 1/K
     double* d_normpart = nullptr;
     int* d_nonfinite = nullptr;
     int* d_err = nullptr;
@@ -104,7 +106,7 @@ struct Ctx {
     // pinned host staging
     int32_t* h_tokens = nullptr;
     float* h_out = nullptr;  // 8 floats
-    float* h_hp = nullptr;   // 8 floats
+    float* h_hp = nullptr;   // 16 floats, mirrored into d_hp by every step
     int* h_err = nullptr;
 
     // optimizer / trainer state
@@ -135,7 +137,9 @@ struct Ctx {
     // CUDA graph of the whole step
     bool use_graph = true;
     cudaGraphExec_t graph = nullptr;
-    int graph_B = -1, graph_T = -1, graph_acc = -1, graph_mode = -1;
+    int graph_B = -1, graph_T = -1, graph_acc = -1, graph_mode = -1, graph_K = -1;
+    int graph_launches = 0;
+    int graph_seen = 0;  // consecutive eager runs with the current key (capture on the 2nd)
 
     std::string err;
 };
@@ -149,6 +153,7 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward);
 // optimizer: (scale by 1/K) -> allreduce -> norm/clip -> AdamW
 int run_optimizer(Ctx* c, int K);
 int ctx_sync_check(Ctx* c);
+void prepare_step_scalars(Ctx* c, int K);
 int save_binary(Ctx* c, const char* path);
 int load_binary(Ctx* c, const char* path);
 int save_adam(Ctx* c, const char* path);

@@ -74,24 +74,33 @@ __global__ void __launch_bounds__(256) norm_fwd_kernel(const float* __restrict__
     }
 }
 
+__device__ __forceinline__ void add4(float4* p, float a, float b, float c, float d) {
+    float4 v = *p;
+    v.x += a;
+    v.y += b;
+    v.z += c;
+    v.w += d;
+    *p = v;
+}
+
+// Column partial sums (dgamma, dbeta, colsum of dx) accumulate per warp in shared memory
+// ([8 warps][3][C] floats), which keeps registers low enough for several CTAs per SM.
 template <int MAXV>
 __global__ void __launch_bounds__(256) norm_bwd_kernel(
     const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ gamma,
     const float* __restrict__ mean, const float* __restrict__ rstd,
     const float* __restrict__ resid_in, float* __restrict__ dx_f32, bf16* __restrict__ dx_bf16,
     float* __restrict__ partial, int rows, int C, int rms) {
-    extern __shared__ float red[];  // [8][C]
+    extern __shared__ float red[];  // [8][3][C]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nwarps_total = gridDim.x * 8;
     const int nv = C >> 2;
     const float4* g4 = reinterpret_cast<const float4*>(gamma);
-    float4 pg[MAXV], pb[MAXV], po[MAXV];
-#pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-        pg[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        pb[i] = pg[i];
-        po[i] = pg[i];
-    }
+    for (int i = threadIdx.x; i < 8 * 3 * C; i += blockDim.x) red[i] = 0.f;
+    __syncthreads();
+    float4* sg = reinterpret_cast<float4*>(red + (warp * 3 + 0) * C);
+    float4* sb = reinterpret_cast<float4*>(red + (warp * 3 + 1) * C);
+    float4* so = reinterpret_cast<float4*>(red + (warp * 3 + 2) * C);
     const float invC = 1.0f / (float)C;
     for (int row = blockIdx.x * 8 + warp; row < rows; row += nwarps_total) {
         const float4* dyr = reinterpret_cast<const float4*>(dy + (long long)row * C);
@@ -151,52 +160,45 @@ __global__ void __launch_bounds__(256) norm_bwd_kernel(
                 }
                 o32[idx] = make_float4(o[0], o[1], o[2], o[3]);
                 if (o16) o16[idx] = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
-                pg[i].x += dd[0] * xh[0];
-                pg[i].y += dd[1] * xh[1];
-                pg[i].z += dd[2] * xh[2];
-                pg[i].w += dd[3] * xh[3];
-                pb[i].x += dd[0];
-                pb[i].y += dd[1];
-                pb[i].z += dd[2];
-                pb[i].w += dd[3];
-                po[i].x += o[0];
-                po[i].y += o[1];
-                po[i].z += o[2];
-                po[i].w += o[3];
+                add4(sg + idx, dd[0] * xh[0], dd[1] * xh[1], dd[2] * xh[2], dd[3] * xh[3]);
+                add4(sb + idx, dd[0], dd[1], dd[2], dd[3]);
+                add4(so + idx, o[0], o[1], o[2], o[3]);
             }
         }
     }
     // CTA-level reduction of the three partial planes (fixed order: warp 0..7)
-    for (int plane = 0; plane < 3; ++plane) {
-        float4* mine = reinterpret_cast<float4*>(red + warp * C);
-#pragma unroll
-        for (int i = 0; i < MAXV; ++i) {
-            const int idx = lane + i * 32;
-            if (idx < nv) mine[idx] = plane == 0 ? pg[i] : (plane == 1 ? pb[i] : po[i]);
-        }
-        __syncthreads();
-        for (int c = threadIdx.x; c < C; c += blockDim.x) {
-            float acc = 0.f;
-            for (int w = 0; w < 8; ++w) acc += red[w * C + c];
-            partial[((long long)blockIdx.x * 3 + plane) * C + c] = acc;
-        }
-        __syncthreads();
+    __syncthreads();
+    for (int i = threadIdx.x; i < 3 * C; i += blockDim.x) {
+        const int plane = i / C, c = i - plane * C;
+        float acc = 0.f;
+        for (int w = 0; w < 8; ++w) acc += red[(w * 3 + plane) * C + c];
+        partial[((long long)blockIdx.x * 3 + plane) * C + c] = acc;
     }
 }
 
+// grid (C/32, 3 planes), 256 threads = 8 part-groups x 32 columns; each group sums every
+// 8th part, then the 8 group sums are added in fixed order.
 __global__ void reduce_partials_kernel(const float* __restrict__ partial, int nparts, int C,
                                        float* out0, float* out1, float* out2, int accumulate) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= 3 * C) return;
-    const int plane = i / C, c = i - plane * C;
+    __shared__ float red[8][33];
+    const int plane = blockIdx.y;
     float* out = plane == 0 ? out0 : (plane == 1 ? out1 : out2);
     if (!out) return;
+    const int cc = threadIdx.x & 31, grp = threadIdx.x >> 5;
+    const int c = blockIdx.x * 32 + cc;
     float acc = 0.f;
-    for (int p = 0; p < nparts; ++p) acc += partial[((long long)p * 3 + plane) * C + c];
-    out[c] = accumulate ? out[c] + acc : acc;
+    if (c < C)
+        for (int p = grp; p < nparts; p += 8) acc += partial[((long long)p * 3 + plane) * C + c];
+    red[grp][cc] = acc;
+    __syncthreads();
+    if (grp == 0 && c < C) {
+        float t = 0.f;
+        for (int g = 0; g < 8; ++g) t += red[g][cc];
+        out[c] = accumulate ? out[c] + t : t;
+    }
 }
 
-constexpr int kColsumGroups = 64;
+constexpr int kColsumGroups = 256;
 
 __global__ void colsum_stage1(const bf16* __restrict__ a, long long lda, int rows, int C,
                               float* __restrict__ work) {
@@ -247,7 +249,7 @@ int norm_forward(const float* x, const float* gamma, const float* beta, bf16* y,
         norm_fwd_kernel<16><<<blocks, 256, 0, s>>>(x, gamma, beta, y, mean, rstd, rows, C, rms);
     else
         return -2;
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_status();
 }
 
 int norm_backward_grid(int rows) {
@@ -258,37 +260,45 @@ int norm_backward_grid(int rows) {
 int norm_backward(const float* dy, const float* x, const float* gamma, const float* mean,
                   const float* rstd, const float* resid_in, float* dx_f32, bf16* dx_bf16,
                   float* partial, int rows, int C, int rms, int* nparts, cudaStream_t s) {
-    if ((C & 3) != 0 || rows <= 0) return -1;
+    if ((C & 3) != 0 || rows <= 0 || C > 2048) return -1;
     const int grid = norm_backward_grid(rows);
-    const size_t smem = 8 * (size_t)C * sizeof(float);
+    const size_t smem = 8 * 3 * (size_t)C * sizeof(float);
     if (nparts) *nparts = grid;
-    if (C <= 512) {
-        norm_bwd_kernel<4><<<grid, 256, smem, s>>>(dy, x, gamma, mean, rstd, resid_in, dx_f32,
-                                                    dx_bf16, partial, rows, C, rms);
-    } else if (C <= 1024) {
-        norm_bwd_kernel<8><<<grid, 256, smem, s>>>(dy, x, gamma, mean, rstd, resid_in, dx_f32,
-                                                    dx_bf16, partial, rows, C, rms);
-    } else if (C <= 2048) {
-        static bool set = false;
-        if (!set) {
-            cudaFuncSetAttribute(norm_bwd_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 8 * 2048 * 4);
-            set = true;
-        }
-        norm_bwd_kernel<16><<<grid, 256, smem, s>>>(dy, x, gamma, mean, rstd, resid_in, dx_f32,
-                                                     dx_bf16, partial, rows, C, rms);
-    } else {
-        return -2;
+    static bool set = false;
+    if (!set) {
+        const int mx = 8 * 3 * 2048 * 4;
+        cudaFuncSetAttribute(norm_bwd_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+        cudaFuncSetAttribute(norm_bwd_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+        cudaFuncSetAttribute(norm_bwd_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+        cudaFuncSetAttribute(norm_bwd_kernel<6>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+        cudaFuncSetAttribute(norm_bwd_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+        cudaFuncSetAttribute(norm_bwd_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+        set = true;
     }
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+#define NB_LAUNCH(MV)                                                                      \
+    norm_bwd_kernel<MV><<<grid, 256, smem, s>>>(dy, x, gamma, mean, rstd, resid_in, dx_f32, \
+                                                dx_bf16, partial, rows, C, rms)
+    if (C <= 128)
+        NB_LAUNCH(1);
+    else if (C <= 256)
+        NB_LAUNCH(2);
+    else if (C <= 512)
+        NB_LAUNCH(4);
+    else if (C <= 768)
+        NB_LAUNCH(6);
+    else if (C <= 1024)
+        NB_LAUNCH(8);
+    else
+        NB_LAUNCH(16);
+#undef NB_LAUNCH
+    return launch_status();
 }
 
 int reduce_partials(const float* partial, int nparts, int C, float* out0, float* out1,
                     float* out2, int accumulate, cudaStream_t s) {
-    const int n = 3 * C;
-    reduce_partials_kernel<<<(n + 255) / 256, 256, 0, s>>>(partial, nparts, C, out0, out1, out2,
-                                                           accumulate);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    dim3 grid((C + 31) / 32, 3);
+    reduce_partials_kernel<<<grid, 256, 0, s>>>(partial, nparts, C, out0, out1, out2, accumulate);
+    return launch_status();
 }
 
 size_t colsum_work_floats(int C) { return (size_t)kColsumGroups * C; }
@@ -298,7 +308,7 @@ int colsum_bf16(const bf16* a, long long lda, int rows, int C, float* out, int a
     dim3 g1((C + 2047) / 2048, kColsumGroups);
     colsum_stage1<<<g1, 256, 0, s>>>(a, lda, rows, C, work);
     colsum_stage2<<<(C + 255) / 256, 256, 0, s>>>(work, C, out, accumulate);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_status();
 }
 
 }  // namespace llmgpu

@@ -92,16 +92,30 @@ extern "C" int llmgpu_op_cross_entropy(void* logits_bf16, int rows, int V, int V
 }
 
 extern "C" int llmgpu_op_attention_fwd(const void* qkv, void* out, float* lse, int B, int T,
-                                       int H, int hd, void* stream) {
+                                       int H, int hd, const float* rope_cs, void* stream) {
     return attention_forward(reinterpret_cast<const bf16*>(qkv), reinterpret_cast<bf16*>(out), lse,
-                             B, T, H, hd, reinterpret_cast<cudaStream_t>(stream));
+                             B, T, H, hd, reinterpret_cast<const float2*>(rope_cs),
+                             reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int llmgpu_op_attention_bwd(const void* qkv, const void* out, const void* dout,
                                        const float* lse, float* dvec, void* dqkv, int B, int T,
-                                       int H, int hd, void* stream) {
+                                       int H, int hd, const float* rope_cs, void* stream) {
     return attention_backward(reinterpret_cast<const bf16*>(qkv), reinterpret_cast<const bf16*>(out),
                               reinterpret_cast<const bf16*>(dout), lse, dvec,
                               reinterpret_cast<bf16*>(dqkv), B, T, H, hd,
+                              reinterpret_cast<const float2*>(rope_cs),
                               reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int llmgpu_op_swiglu_fwd(const void* h13, void* gated, int rows, int F, void* stream) {
+    return swiglu_forward(reinterpret_cast<const bf16*>(h13), reinterpret_cast<bf16*>(gated), rows,
+                          F, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int llmgpu_op_swiglu_bwd(const void* dgated, const void* h13, void* dh13, int rows,
+                                    int F, void* stream) {
+    return swiglu_backward(reinterpret_cast<const bf16*>(dgated), reinterpret_cast<const bf16*>(h13),
+                           reinterpret_cast<bf16*>(dh13), rows, F,
+                           reinterpret_cast<cudaStream_t>(stream));
 }

@@ -31,10 +31,14 @@ def _declare(lib):
     lib.llmgpu_op_norm_bwd_work.restype = c_ll
     lib.llmgpu_op_cross_entropy.argtypes = [c_vp, c_int, c_int, c_int, c_vp, c_vp, c_float,
                                             c_float, c_vp]
-    lib.llmgpu_op_attention_fwd.argtypes = [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp]
-    lib.llmgpu_op_attention_bwd.argtypes = [c_vp] * 6 + [c_int, c_int, c_int, c_int, c_vp]
+    lib.llmgpu_op_attention_fwd.argtypes = [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp,
+                                            c_vp]
+    lib.llmgpu_op_attention_bwd.argtypes = [c_vp] * 6 + [c_int, c_int, c_int, c_int, c_vp, c_vp]
+    lib.llmgpu_op_swiglu_fwd.argtypes = [c_vp, c_vp, c_int, c_int, c_vp]
+    lib.llmgpu_op_swiglu_bwd.argtypes = [c_vp, c_vp, c_vp, c_int, c_int, c_vp]
     for n in ("llmgpu_op_embed", "llmgpu_op_norm_fwd", "llmgpu_op_norm_bwd",
-              "llmgpu_op_cross_entropy", "llmgpu_op_attention_fwd", "llmgpu_op_attention_bwd"):
+              "llmgpu_op_cross_entropy", "llmgpu_op_attention_fwd", "llmgpu_op_attention_bwd",
+              "llmgpu_op_swiglu_fwd", "llmgpu_op_swiglu_bwd"):
         getattr(lib, n).restype = c_int
     try:
         from . import _abi_decl

@@ -109,21 +109,45 @@ def cross_entropy(logits16, V, tokens, scale, smoothing=0.0):
     return loss
 
 
-def attention_fwd(qkv, B, T, H, hd):
+def rope_table(T, hd, theta, device):
+    """(cos, sin) of pos * theta^(-2j/hd), shape [T, hd/2, 2] fp32."""
+    j = torch.arange(hd // 2, dtype=torch.float64)
+    ang = torch.arange(T, dtype=torch.float64)[:, None] * theta ** (-2.0 * j / hd)[None, :]
+    return torch.stack([ang.cos(), ang.sin()], -1).float().to(device).contiguous()
+
+
+def attention_fwd(qkv, B, T, H, hd, rope=None):
     lib = load()
     C = H * hd
     out = torch.empty(B * T, C, dtype=torch.bfloat16, device=qkv.device)
     lse = torch.empty(B, H, T, device=qkv.device)
     _sync_check(lib.llmgpu_op_attention_fwd(_ptr(qkv), _ptr(out), _ptr(lse), B, T, H, hd,
-                                            _stream()), "attention_fwd")
+                                            _ptr(rope), _stream()), "attention_fwd")
     return out, lse
 
 
-def attention_bwd(qkv, out, dout, lse, B, T, H, hd):
+def attention_bwd(qkv, out, dout, lse, B, T, H, hd, rope=None):
     lib = load()
     dqkv = torch.zeros_like(qkv)
     dvec = torch.empty(B, H, T, device=qkv.device)
     _sync_check(lib.llmgpu_op_attention_bwd(_ptr(qkv), _ptr(out), _ptr(dout), _ptr(lse),
-                                            _ptr(dvec), _ptr(dqkv), B, T, H, hd, _stream()),
-                "attention_bwd")
+                                            _ptr(dvec), _ptr(dqkv), B, T, H, hd, _ptr(rope),
+                                            _stream()), "attention_bwd")
     return dqkv
+
+
+def swiglu_fwd(h13, F):
+    lib = load()
+    rows = h13.shape[0]
+    g = torch.empty(rows, F, dtype=torch.bfloat16, device=h13.device)
+    _sync_check(lib.llmgpu_op_swiglu_fwd(_ptr(h13), _ptr(g), rows, F, _stream()), "swiglu_fwd")
+    return g
+
+
+def swiglu_bwd(dg, h13, F):
+    lib = load()
+    rows = h13.shape[0]
+    d = torch.empty_like(h13)
+    _sync_check(lib.llmgpu_op_swiglu_bwd(_ptr(dg), _ptr(h13), _ptr(d), rows, F, _stream()),
+                "swiglu_bwd")
+    return d

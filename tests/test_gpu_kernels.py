@@ -116,3 +116,51 @@ def test_attention_forward_backward(cuda, B, T, H, hd):
     for part in range(3):
         sl = slice(part * C, (part + 1) * C)
         assert _rel(dqkv[:, sl].float(), want[:, sl]) < 2e-2, part
+
+
+def _rope_ref(x, B, T, H, hd, theta=10000.0):
+    """Rotate pairs (2j, 2j+1) of each head by pos * theta^(-2j/hd); x: [B*T, H*hd]."""
+    j = torch.arange(hd // 2, dtype=torch.float64, device=x.device)
+    ang = torch.arange(T, dtype=torch.float64, device=x.device)[:, None] * theta ** (-2.0 * j / hd)
+    c, s = ang.cos()[None, :, None, :], ang.sin()[None, :, None, :]
+    v = x.reshape(B, T, H, hd // 2, 2)
+    x0, x1 = v[..., 0], v[..., 1]
+    return torch.stack([x0 * c - x1 * s, x0 * s + x1 * c], -1).reshape(B * T, H * hd)
+
+
+@pytest.mark.parametrize("B,T,H,hd", [(2, 128, 4, 64), (1, 200, 2, 64), (2, 96, 2, 32)])
+def test_attention_rope(cuda, B, T, H, hd):
+    """RoPE applied per head to Q and K inside the attention kernels (config 3)."""
+    from llmgpu import ops
+    g = torch.Generator().manual_seed(T + H)
+    C = H * hd
+    qkv = torch.randn(B * T, 3 * C, generator=g).to(torch.bfloat16).to(cuda)
+    tab = ops.rope_table(T, hd, 10000.0, cuda)
+    out, lse = ops.attention_fwd(qkv, B, T, H, hd, rope=tab)
+    q = qkv.double().requires_grad_(True)
+    rot = torch.cat([_rope_ref(q[:, :C], B, T, H, hd), _rope_ref(q[:, C:2 * C], B, T, H, hd),
+                     q[:, 2 * C:]], 1)
+    ref, _ = _attn_ref(rot, B, T, H, hd)
+    assert _rel(out.float(), ref.detach()) < 1e-2
+    dout = torch.randn(B * T, C, generator=g).to(torch.bfloat16).to(cuda)
+    dqkv = ops.attention_bwd(qkv, out, dout, lse, B, T, H, hd, rope=tab)
+    ref.backward(dout.double())
+    for part in range(3):
+        sl = slice(part * C, (part + 1) * C)
+        assert _rel(dqkv[:, sl].float(), q.grad[:, sl]) < 2e-2, part
+
+
+def test_swiglu_forward_backward(cuda):
+    """gated = silu(h1) * h3 and its backward (src/transformer.cpp:22-30, 76-89)."""
+    from llmgpu import ops
+    g = torch.Generator().manual_seed(2)
+    rows, F = 257, 704
+    h13 = (torch.randn(rows, 2 * F, generator=g) * 2).to(torch.bfloat16).to(cuda)
+    gated = ops.swiglu_fwd(h13, F)
+    h = h13.double().requires_grad_(True)
+    ref = torch.nn.functional.silu(h[:, :F]) * h[:, F:]
+    assert _rel(gated.float(), ref.detach()) < 5e-3
+    dg = torch.randn(rows, F, generator=g).to(torch.bfloat16).to(cuda)
+    d = ops.swiglu_bwd(dg, h13, F)
+    ref.backward(dg.double())
+    assert _rel(d.float(), h.grad) < 5e-3

@@ -125,6 +125,10 @@ ORACLE_CASES = {
     # RMSNorm everywhere
     "rms_hd64": (go.Cfg(vocab=512, n_layers=2, n_heads=4, n_embd=256, block_size=96,
                         rmsnorm=True), 3, 96),
+    # Llama-style: RMSNorm, SwiGLU FFN, RoPE on Q/K, untied head (config 3 shape, scaled down)
+    "llama_swiglu_rope": (go.Cfg(vocab=512, n_layers=2, n_heads=4, n_embd=256, block_size=128,
+                                 rmsnorm=True, tied=False, ffn="swiglu", ffn_hidden=704,
+                                 rope_qk=True), 2, 128),
 }
 
 
