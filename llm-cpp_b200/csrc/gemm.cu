@@ -63,7 +63,7 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* o, const float* v) 
 __device__ __forceinline__ void epi_store(const GemmArgs& a, int row, int col0, int split,
                                           float (&v)[32]) {
     const int nvalid = min(32, a.N - col0);
-    const bool full = (nvalid == 32);
+    const bool full = (nvalid == 32) && !a.scalar_store;
     switch (a.epi) {
         case kEpiStoreBF16: {
             __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.out) + row * a.ldo + col0;
@@ -431,6 +431,21 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
     }
 }
 
+__global__ void splitk_reduce_scalar_kernel(const float* __restrict__ part, int splits, int M,
+                                            int N, float* __restrict__ out, long long ldo,
+                                            int col_group, long long group_stride,
+                                            int accumulate) {
+    const long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    const long long plane = (long long)M * N;
+    if (e >= plane) return;
+    const int m = (int)(e / N), n = (int)(e - (long long)m * N);
+    float s = part[e];
+    for (int k = 1; k < splits; ++k) s += part[k * plane + e];
+    const int g = n / col_group;
+    float* o = out + g * group_stride + m * ldo + (n - g * col_group);
+    *o = accumulate ? *o + s : s;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -502,12 +517,12 @@ int gemm_make_plan(GemmPlan* plan, const void* A, long long lda, int a_mn_major,
             ((a.ld_aux % 8) != 0 || (reinterpret_cast<uintptr_t>(a.aux) & 15)))
             return -8;
     } else if (a.epi == kEpiStoreF32 || a.epi == kEpiResidF32) {
-        if ((a.ldo % 4) != 0 || (reinterpret_cast<uintptr_t>(a.out) & 15) ||
-            (a.group_stride % 4) != 0)
-            return -8;
+        // narrow or odd-strided fp32 outputs take the scalar store path
+        a.scalar_store = ((a.ldo % 4) != 0 || (reinterpret_cast<uintptr_t>(a.out) & 15) ||
+                          (a.group_stride % 4) != 0) ? 1 : 0;
         if (a.epi == kEpiResidF32 &&
             ((a.ldr % 4) != 0 || (reinterpret_cast<uintptr_t>(a.resid) & 15)))
-            return -8;
+            a.scalar_store = 1;
     } else if (a.epi == kEpiSplitPartial) {
         if (reinterpret_cast<uintptr_t>(a.out) & 15) return -8;
     }
@@ -564,9 +579,14 @@ int gemm_run(const GemmPlan& p, cudaStream_t stream) {
 int gemm_splitk_reduce(const float* partial, int splits, int M, int N, float* out, long long ldo,
                        int col_group, long long group_stride, int accumulate,
                        cudaStream_t stream) {
-    if ((N % 4) != 0 || (ldo % 4) != 0) return -1;
     if (col_group <= 0) col_group = N;
-    if (col_group != N && (col_group % 4) != 0) return -1;
+    if ((N % 4) != 0 || (ldo % 4) != 0 || (col_group != N && (col_group % 4) != 0) ||
+        (group_stride % 4) != 0) {
+        const long long total = (long long)M * N;
+        splitk_reduce_scalar_kernel<<<(int)((total + 255) / 256), 256, 0, stream>>>(
+            partial, splits, M, N, out, ldo, col_group, group_stride, accumulate);
+        return launch_status();
+    }
     long long total4 = (long long)M * N / 4;
     int threads = 256;
     long long blocks = (total4 + threads - 1) / threads;

@@ -41,6 +41,7 @@ struct GemmArgs {
     void* aux;             // bf16 pre-activation (written by Gelu, read by DGelu)
     long long ld_aux;
     int splits;            // >=1; kEpiSplitPartial writes `splits` partial planes
+    int scalar_store;      // set by the planner when the output is not 16-byte aligned
     int* err;              // device error word
 };
 

@@ -1,0 +1,594 @@
+// Mamba block kernels (MambaBlock::forward/backward, src/mamba.cpp:36-166, 179-413):
+// causal depthwise conv + SiLU, dt = clamp(softplus(xp[:, :R] dt_proj^T), 1e-3, 0.1), the
+// selective scan h = exp(A dt) h + B x dt, y = C.h + D x, the SiLU(z) gate, and their
+// backward. The in/x/out projections run on the tcgen05 GEMM (model.cu).
+//
+// Scan parallelisation: one thread per (sequence, channel d, state n); the L lanes of a
+// channel (L = next power of two >= N) reduce C.h with shuffles. The forward saves h every
+// kChunk steps; the backward walks chunks in reverse, recomputes the chunk's states from
+// the saved one (instead of storing the T x D x N trajectory the reference keeps,
+// src/mamba.cpp:215-229) and runs the reverse recurrence of src/mamba.cpp:277-308.
+// All cross-channel and cross-sequence sums go through partial buffers reduced in a fixed
+// order, so results are deterministic.
+#include "common.cuh"
+#include "mamba.cuh"
+
+namespace llmgpu {
+
+namespace {
+
+constexpr int kWarps = 8;
+
+__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
+__device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + __expf(-v)); }
+__device__ __forceinline__ float silu_grad_f(float v) {
+    const float s = sigmoid_f(v);
+    return s * (1.0f + v * (1.0f - s));
+}
+__device__ __forceinline__ float softplus_f(float v) { return log1pf(__expf(v)); }
+__device__ __forceinline__ float clamp_dt(float sp) { return fminf(fmaxf(sp, 0.001f), 0.1f); }
+
+// ---------------------------------------------------------------- conv forward
+// pre[t,d] = b[d] + sum_j w[d,j] x[t-(K-1)+j, d] within each sequence; u = silu(pre)
+__global__ void conv_fwd_kernel(const bf16* __restrict__ proj, long long ldp, int D, int T, int K,
+                                const float* __restrict__ w, const float* __restrict__ bias,
+                                float* __restrict__ u32, bf16* __restrict__ u16, long long rows) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= rows * D) return;
+    const long long row = i / D;
+    const int d = (int)(i - row * D);
+    const int t = (int)(row % T);
+    float acc = bias[d];
+    for (int j = 0; j < K; ++j) {
+        const int back = K - 1 - j;
+        if (t - back >= 0)
+            acc += w[d * K + j] * __bfloat162float(proj[(row - back) * ldp + D + d]);
+    }
+    const float uv = silu_f(acc);
+    u32[i] = uv;
+    u16[i] = __float2bfloat16_rn(uv);
+}
+
+// ---------------------------------------------------------------- dt forward
+// raw[row, d] = sum_r xp[row, r] * dt_proj[d, r]  (fp32; tiles of 32 rows x 64 channels)
+__global__ void dt_fwd_kernel(const float* __restrict__ xp, long long ldx,
+                              const float* __restrict__ dtp, float* __restrict__ raw,
+                              long long rows, int D, int R) {
+    extern __shared__ float sm[];
+    float* sx = sm;            // [32][R]
+    float* sw = sm + 32 * R;   // [64][R+1]
+    const long long r0 = blockIdx.y * 32LL;
+    const int d0 = blockIdx.x * 64;
+    for (int i = threadIdx.x; i < 32 * R; i += blockDim.x) {
+        const int rr = i / R, k = i - rr * R;
+        sx[i] = (r0 + rr < rows) ? xp[(r0 + rr) * ldx + k] : 0.f;
+    }
+    for (int i = threadIdx.x; i < 64 * R; i += blockDim.x) {
+        const int dd = i / R, k = i - dd * R;
+        sw[dd * (R + 1) + k] = (d0 + dd < D) ? dtp[(long long)(d0 + dd) * R + k] : 0.f;
+    }
+    __syncthreads();
+    const int dd = threadIdx.x & 63;       // channel within the tile
+    const int rg = threadIdx.x >> 6;       // 4 row groups of 8 rows
+    if (d0 + dd >= D) return;
+    for (int rr = rg * 8; rr < rg * 8 + 8; ++rr) {
+        if (r0 + rr >= rows) break;
+        float acc = 0.f;
+        for (int k = 0; k < R; ++k) acc += sx[rr * R + k] * sw[dd * (R + 1) + k];
+        raw[(r0 + rr) * D + d0 + dd] = acc;
+    }
+}
+
+// ---------------------------------------------------------------- scan forward
+template <int L>
+__global__ void __launch_bounds__(kWarps * 32) scan_fwd_kernel(
+    const float* __restrict__ raw, const float* __restrict__ u, const float* __restrict__ xp,
+    long long ldx, const float* __restrict__ alog, const float* __restrict__ dskip,
+    const bf16* __restrict__ proj, long long ldp, float* __restrict__ y32,
+    bf16* __restrict__ gated, float* __restrict__ hchk, int T, int D, int N, int R) {
+    constexpr int CPW = 32 / L;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = lane % L, ci = lane / L;
+    const int d = (blockIdx.x * kWarps + warp) * CPW + ci;
+    const int b = blockIdx.y;
+    const bool chan = d < D;
+    const bool active = chan && n < N;
+    const float A = active ? alog[(long long)d * N + n] : 0.f;
+    const float Ds = chan ? dskip[d] : 0.f;
+    const int nch = (T + kScanChunk - 1) / kScanChunk;
+    float h = 0.f;
+    for (int t = 0; t < T; ++t) {
+        const long long row = (long long)b * T + t;
+        if ((t % kScanChunk) == 0 && active)
+            hchk[(((long long)b * nch + t / kScanChunk) * D + d) * N + n] = h;
+        const float rv = chan ? raw[row * D + d] : 0.f;
+        const float dt = clamp_dt(softplus_f(rv));
+        const float uu = chan ? u[row * D + d] : 0.f;
+        const float Bv = active ? xp[row * ldx + R + n] : 0.f;
+        const float Cv = active ? xp[row * ldx + R + N + n] : 0.f;
+        const float a = __expf(A * dt);
+        h = a * h + Bv * uu * dt;
+        float c = Cv * h;
+#pragma unroll
+        for (int o = L / 2; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+        if (n == 0 && chan) {
+            const float yv = c + Ds * uu;
+            y32[row * D + d] = yv;
+            const float xz = __bfloat162float(proj[row * ldp + d]);
+            gated[row * D + d] = __float2bfloat16_rn(yv * silu_f(xz));
+        }
+    }
+}
+
+// ---------------------------------------------------------------- scan backward
+template <int L>
+__global__ void __launch_bounds__(kWarps * 32) scan_bwd_kernel(
+    const float* __restrict__ raw, const float* __restrict__ u, const float* __restrict__ xp,
+    long long ldx, const float* __restrict__ alog, const float* __restrict__ dskip,
+    const bf16* __restrict__ proj, long long ldp, const float* __restrict__ y32,
+    const float* __restrict__ dgated, const float* __restrict__ hchk, float* __restrict__ du,
+    float* __restrict__ ddt, bf16* __restrict__ dproj, float* __restrict__ dbc_part,
+    float* __restrict__ da_part, float* __restrict__ dd_part, int T, int D, int N, int R) {
+    constexpr int CPW = 32 / L;
+    constexpr int LC = kScanChunk;
+    __shared__ float sB[kWarps][LC][L];
+    __shared__ float sC[kWarps][LC][L];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = lane % L, ci = lane / L;
+    const int d = (blockIdx.x * kWarps + warp) * CPW + ci;
+    const int b = blockIdx.y;
+    const bool chan = d < D;
+    const bool active = chan && n < N;
+    const float A = active ? alog[(long long)d * N + n] : 0.f;
+    const float Ds = chan ? dskip[d] : 0.f;
+    const int nch = (T + LC - 1) / LC;
+    const long long BT = (long long)gridDim.y * T;
+    float dh_next = 0.f, dA_acc = 0.f, dD_acc = 0.f;
+    for (int ch = nch - 1; ch >= 0; --ch) {
+        const int t0 = ch * LC;
+        const float h_start = active ? hchk[(((long long)b * nch + ch) * D + d) * N + n] : 0.f;
+        float hs[LC], as[LC], dts[LC];
+        float h = h_start;
+#pragma unroll
+        for (int i = 0; i < LC; ++i) {
+            const int t = t0 + i;
+            float dt = 0.f, a = 1.f;
+            if (t < T) {
+                const long long row = (long long)b * T + t;
+                dt = clamp_dt(softplus_f(chan ? raw[row * D + d] : 0.f));
+                a = __expf(A * dt);
+                const float uu = chan ? u[row * D + d] : 0.f;
+                const float Bv = active ? xp[row * ldx + R + n] : 0.f;
+                h = a * h + Bv * uu * dt;
+            }
+            hs[i] = h;
+            as[i] = a;
+            dts[i] = dt;
+        }
+#pragma unroll
+        for (int i = LC - 1; i >= 0; --i) {
+            const int t = t0 + i;
+            float dB_c = 0.f, dC_c = 0.f;
+            if (t < T) {
+                const long long row = (long long)b * T + t;
+                const float uu = chan ? u[row * D + d] : 0.f;
+                const float Bv = active ? xp[row * ldx + R + n] : 0.f;
+                const float Cv = active ? xp[row * ldx + R + N + n] : 0.f;
+                const float dgv = chan ? dgated[row * D + d] : 0.f;
+                const float xz = chan ? __bfloat162float(proj[row * ldp + d]) : 0.f;
+                const float dyv = dgv * silu_f(xz);                // d(loss)/d(y)
+                const float h_t = hs[i];
+                const float h_prev = i > 0 ? hs[i - 1] : h_start;
+                const float a_t = as[i], dt_t = dts[i];
+                const float dh = dh_next + dyv * Cv;
+                dC_c = dyv * h_t;
+                dB_c = dh * uu * dt_t;
+                float du_c = dh * Bv * dt_t;
+                float ddt_c = dh * h_prev * a_t * A + dh * Bv * uu;
+                dA_acc += dh * h_prev * a_t * dt_t;
+                dh_next = dh * a_t;
+#pragma unroll
+                for (int o = L / 2; o > 0; o >>= 1) {
+                    du_c += __shfl_xor_sync(0xffffffffu, du_c, o);
+                    ddt_c += __shfl_xor_sync(0xffffffffu, ddt_c, o);
+                }
+                if (n == 0 && chan) {
+                    du[row * D + d] = du_c + dyv * Ds;
+                    ddt[row * D + d] = ddt_c;
+                    dD_acc += dyv * uu;
+                    const float yv = y32[row * D + d];
+                    dproj[row * ldp + d] = __float2bfloat16_rn(dgv * yv * silu_grad_f(xz));
+                }
+            }
+            // sum this warp's channels for every state n (fixed order)
+#pragma unroll
+            for (int o = L; o < 32; o <<= 1) {
+                dB_c += __shfl_xor_sync(0xffffffffu, dB_c, o);
+                dC_c += __shfl_xor_sync(0xffffffffu, dC_c, o);
+            }
+            if (ci == 0) {
+                sB[warp][i][n] = dB_c;
+                sC[warp][i][n] = dC_c;
+            }
+        }
+        __syncthreads();
+        // block partial over its warps (fixed order) -> dbc_part[blockIdx.x][2][B*T][N]
+        for (int k = threadIdx.x; k < LC * N; k += blockDim.x) {
+            const int i = k / N, nn = k - i * N;
+            const int t = t0 + i;
+            if (t >= T) continue;
+            float sb = 0.f, sc = 0.f;
+            for (int w = 0; w < kWarps; ++w) {
+                sb += sB[w][i][nn];
+                sc += sC[w][i][nn];
+            }
+            const long long row = (long long)b * T + t;
+            float* part = dbc_part + (long long)blockIdx.x * 2 * BT * N;
+            part[row * N + nn] = sb;
+            part[BT * N + row * N + nn] = sc;
+        }
+        __syncthreads();
+    }
+    if (active) da_part[((long long)b * D + d) * N + n] = dA_acc;
+    if (n == 0 && chan) dd_part[(long long)b * D + d] = dD_acc;
+}
+
+// dB, dC: sum over channel groups (fixed order) -> bf16 columns R.. of dxp
+__global__ void dbc_reduce_kernel(const float* __restrict__ part, int groups, long long BT, int N,
+                                  int R, bf16* __restrict__ dxp, long long ldx) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= BT * N) return;
+    const long long row = i / N;
+    const int n = (int)(i - row * N);
+    float sb = 0.f, sc = 0.f;
+    for (int g = 0; g < groups; ++g) {
+        sb += part[(long long)g * 2 * BT * N + i];
+        sc += part[(long long)g * 2 * BT * N + BT * N + i];
+    }
+    dxp[row * ldx + R + n] = __float2bfloat16_rn(sb);
+    dxp[row * ldx + R + N + n] = __float2bfloat16_rn(sc);
+}
+
+// out[j] (+)= sum_b part[b][j]
+__global__ void batch_reduce_kernel(const float* __restrict__ part, int B, long long n,
+                                    float* __restrict__ out, int accumulate) {
+    const long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    float s = 0.f;
+    for (int b = 0; b < B; ++b) s += part[(long long)b * n + j];
+    out[j] = accumulate ? out[j] + s : s;
+}
+
+// draw = ddt * [1e-3 <= softplus(raw) <= 0.1] * sigmoid(raw)   (src/mamba.cpp:318-328)
+__global__ void dt_bwd_kernel(const float* __restrict__ ddt, const float* __restrict__ raw,
+                              bf16* __restrict__ draw, long long n) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float r = raw[i];
+    const float sp = softplus_f(r);
+    const float in = (sp >= 0.001f && sp <= 0.1f) ? 1.f : 0.f;
+    draw[i] = __float2bfloat16_rn(ddt[i] * in * sigmoid_f(r));
+}
+
+// conv backward, stage 1: dpre = (du_scan + du_xp) * silu'(pre); per-block partial sums of
+// dconv_b and dconv_w over the block's rows (grid: D/256 x row blocks of kConvRows)
+constexpr int kConvRows = 64;
+__global__ void conv_bwd1_kernel(const bf16* __restrict__ proj, long long ldp, int D, int T,
+                                 int K, const float* __restrict__ w, const float* __restrict__ bias,
+                                 const float* __restrict__ du1, const float* __restrict__ du2,
+                                 float* __restrict__ dpre, float* __restrict__ part,
+                                 long long rows) {
+    const int d = blockIdx.x * blockDim.x + threadIdx.x;
+    if (d >= D) return;
+    const long long r0 = (long long)blockIdx.y * kConvRows;
+    float sb = 0.f, sw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (long long row = r0; row < r0 + kConvRows && row < rows; ++row) {
+        const int t = (int)(row % T);
+        float pre = bias[d];
+        float xin[8];
+        for (int j = 0; j < K; ++j) {
+            const int back = K - 1 - j;
+            xin[j] = (t - back >= 0) ? __bfloat162float(proj[(row - back) * ldp + D + d]) : 0.f;
+            pre += w[d * K + j] * xin[j];
+        }
+        const long long i = row * D + d;
+        const float g = (du1[i] + du2[i]) * silu_grad_f(pre);
+        dpre[i] = g;
+        sb += g;
+        for (int j = 0; j < K; ++j) sw[j] += g * xin[j];
+    }
+    float* p = part + ((long long)blockIdx.y * D + d) * (K + 1);
+    p[0] = sb;
+    for (int j = 0; j < K; ++j) p[1 + j] = sw[j];
+}
+
+// conv backward, stage 2: dxs[t,d] = sum_j dpre[t+(K-1-j), d] w[d,j] -> bf16 dproj[:, D+d]
+__global__ void conv_bwd2_kernel(const float* __restrict__ dpre, const float* __restrict__ w,
+                                 bf16* __restrict__ dproj, long long ldp, int D, int T, int K,
+                                 long long rows) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= rows * D) return;
+    const long long row = i / D;
+    const int d = (int)(i - row * D);
+    const int t = (int)(row % T);
+    float acc = 0.f;
+    for (int j = 0; j < K; ++j) {
+        const int fwd = K - 1 - j;
+        if (t + fwd < T) acc += dpre[(row + fwd) * D + d] * w[d * K + j];
+    }
+    dproj[row * ldp + D + d] = __float2bfloat16_rn(acc);
+}
+
+// conv weight/bias gradients: out_b[d] (+)= sum_blk part[blk][d][0], out_w[d,j] (+)= ...[1+j]
+__global__ void conv_reduce_kernel(const float* __restrict__ part, int nblk, int D, int K,
+                                   float* __restrict__ gw, float* __restrict__ gb, int accumulate) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= D * (K + 1)) return;
+    const int d = i / (K + 1), j = i - d * (K + 1);
+    float s = 0.f;
+    for (int k = 0; k < nblk; ++k) s += part[((long long)k * D + d) * (K + 1) + j];
+    float* o = j == 0 ? gb + d : gw + (long long)d * K + (j - 1);
+    *o = accumulate ? *o + s : s;
+}
+
+// draw = ddt * [1e-3 <= softplus(raw) <= 0.1] * sigmoid(raw), kept in fp32
+__global__ void dt_bwd_f32_kernel(const float* __restrict__ ddt, const float* __restrict__ raw,
+                                  float* __restrict__ draw, long long n) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float r = raw[i];
+    const float sp = softplus_f(r);
+    const float in = (sp >= 0.001f && sp <= 0.1f) ? 1.f : 0.f;
+    draw[i] = ddt[i] * in * sigmoid_f(r);
+}
+
+// Small fp32 GEMM for the dt_rank-wide contractions of the dt path: part[y][m][n] =
+// sum_{k in chunk y} A(m,k) B(k,n) with A(m,k) = A[m*sam + k*sak], B(k,n) = B[k*sbk + n*sbn],
+// N <= 64. 64 x 64 output tile per block, 4 x 4 per thread, k staged 32 at a time.
+constexpr int kSgM = 64, kSgK = 32;
+__global__ void __launch_bounds__(256) small_gemm_f32_kernel(
+    const float* __restrict__ A, long long sam, long long sak, const float* __restrict__ Bm,
+    long long sbk, long long sbn, int M, int N, int K, int kchunk, float* __restrict__ part) {
+    __shared__ float As[kSgK][kSgM + 1];
+    __shared__ float Bs[kSgK][64 + 1];
+    const int m0 = blockIdx.x * kSgM;
+    const int kbeg = blockIdx.y * kchunk;
+    const int kend = min(K, kbeg + kchunk);
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int k0 = kbeg; k0 < kend; k0 += kSgK) {
+        for (int i = threadIdx.x; i < kSgM * kSgK; i += blockDim.x) {
+            int mm, kk;
+            if (sam == 1) {
+                mm = i % kSgM;
+                kk = i / kSgM;
+            } else {
+                kk = i % kSgK;
+                mm = i / kSgK;
+            }
+            const int m = m0 + mm, k = k0 + kk;
+            As[kk][mm] = (m < M && k < kend) ? A[(long long)m * sam + (long long)k * sak] : 0.f;
+        }
+        for (int i = threadIdx.x; i < kSgK * 64; i += blockDim.x) {
+            int kk, nn;
+            if (sbn == 1) {
+                nn = i % 64;
+                kk = i / 64;
+            } else {
+                kk = i % kSgK;
+                nn = i / kSgK;
+            }
+            const int k = k0 + kk;
+            Bs[kk][nn] = (nn < N && k < kend) ? Bm[(long long)k * sbk + (long long)nn * sbn] : 0.f;
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int kk = 0; kk < kSgK; ++kk) {
+            float av[4], bv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] += av[i] * bv[j];
+        }
+        __syncthreads();
+    }
+    float* p = part + (long long)blockIdx.y * M * N;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int m = m0 + ty * 4 + i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int n = tx * 4 + j;
+            if (n < N) p[(long long)m * N + n] = acc[i][j];
+        }
+    }
+}
+
+// out (+)= sum_y part[y] (fixed order), fp32 [m*ldo + n] or, when out16 is given, bf16
+__global__ void small_gemm_reduce_kernel(const float* __restrict__ part, int splits, int M, int N,
+                                         float* __restrict__ out, bf16* __restrict__ out16,
+                                         long long ldo, int accumulate) {
+    const long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (e >= (long long)M * N) return;
+    const int m = (int)(e / N), n = (int)(e - (long long)m * N);
+    float s = 0.f;
+    for (int y = 0; y < splits; ++y) s += part[(long long)y * M * N + e];
+    if (out16) {
+        out16[(long long)m * ldo + n] = __float2bfloat16_rn(s);
+    } else {
+        float* o = out + (long long)m * ldo + n;
+        *o = accumulate ? *o + s : s;
+    }
+}
+
+__global__ void convert_kernel(const float* __restrict__ src, long long lds, bf16* __restrict__ dst,
+                               long long ldd, long long rows, int cols) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= rows * cols) return;
+    const long long r = i / cols;
+    const int c = (int)(i - r * cols);
+    dst[r * ldd + c] = __float2bfloat16_rn(src[r * lds + c]);
+}
+
+template <int L>
+int launch_scan_fwd(const MambaDims& m, const float* raw, const float* u, const float* xp,
+                    const float* alog, const float* dskip, const bf16* proj, float* y32,
+                    bf16* gated, float* hchk, cudaStream_t s) {
+    constexpr int CPB = kWarps * (32 / L);
+    dim3 grid((m.D + CPB - 1) / CPB, m.B);
+    scan_fwd_kernel<L><<<grid, kWarps * 32, 0, s>>>(raw, u, xp, m.ldx, alog, dskip, proj, m.ldp,
+                                                    y32, gated, hchk, m.T, m.D, m.N, m.R);
+    return launch_status();
+}
+
+template <int L>
+int launch_scan_bwd(const MambaDims& m, const float* raw, const float* u, const float* xp,
+                    const float* alog, const float* dskip, const bf16* proj, const float* y32,
+                    const float* dgated, const float* hchk, float* du, float* ddt, bf16* dproj,
+                    float* dbc_part, float* da_part, float* dd_part, cudaStream_t s) {
+    constexpr int CPB = kWarps * (32 / L);
+    dim3 grid((m.D + CPB - 1) / CPB, m.B);
+    scan_bwd_kernel<L><<<grid, kWarps * 32, 0, s>>>(raw, u, xp, m.ldx, alog, dskip, proj, m.ldp,
+                                                    y32, dgated, hchk, du, ddt, dproj, dbc_part,
+                                                    da_part, dd_part, m.T, m.D, m.N, m.R);
+    return launch_status();
+}
+
+// lanes per channel; d_state up to 16 (the scan's shared staging is sized for it)
+int lanes_for(int N) { return N <= 4 ? 4 : N <= 8 ? 8 : N <= 16 ? 16 : 0; }
+
+}  // namespace
+
+int mamba_dt_backward_f32(const MambaDims& m, const float* ddt, const float* raw, float* draw,
+                          cudaStream_t s) {
+    const long long n = (long long)m.B * m.T * m.D;
+    dt_bwd_f32_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(ddt, raw, draw, n);
+    return launch_status();
+}
+
+int small_gemm_f32(const float* A, long long sam, long long sak, const float* B, long long sbk,
+                   long long sbn, int M, int N, int K, int ksplit, float* part, float* out,
+                   bf16* out16, long long ldo, int accumulate, cudaStream_t s) {
+    if (N > 64 || ksplit < 1) return -1;
+    const int kchunk = ((K + ksplit - 1) / ksplit + kSgK - 1) / kSgK * kSgK;
+    const int ys = (K + kchunk - 1) / kchunk;
+    dim3 grid((M + kSgM - 1) / kSgM, ys);
+    small_gemm_f32_kernel<<<grid, 256, 0, s>>>(A, sam, sak, B, sbk, sbn, M, N, K, kchunk, part);
+    int rc = launch_status();
+    if (rc) return rc;
+    const long long n = (long long)M * N;
+    small_gemm_reduce_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(part, ys, M, N, out, out16, ldo,
+                                                                    accumulate);
+    return launch_status();
+}
+
+int convert_f32_bf16(const float* src, long long lds, bf16* dst, long long ldd, long long rows,
+                     int cols, cudaStream_t s) {
+    const long long n = rows * cols;
+    convert_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(src, lds, dst, ldd, rows, cols);
+    return launch_status();
+}
+
+int mamba_scan_groups(int D, int N) {
+    const int L = lanes_for(N);
+    if (!L) return 0;
+    const int cpb = kWarps * (32 / L);
+    return (D + cpb - 1) / cpb;
+}
+int mamba_conv_blocks(long long rows) { return (int)((rows + kConvRows - 1) / kConvRows); }
+
+int mamba_conv_forward(const MambaDims& m, const bf16* proj, const float* w, const float* bias,
+                       float* u32, bf16* u16, cudaStream_t s) {
+    if (m.K > 8) return -1;
+    const long long rows = (long long)m.B * m.T, n = rows * m.D;
+    conv_fwd_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(proj, m.ldp, m.D, m.T, m.K, w, bias, u32,
+                                                           u16, rows);
+    return launch_status();
+}
+
+int mamba_dt_forward(const MambaDims& m, const float* xp, const float* dt_proj, float* raw,
+                     cudaStream_t s) {
+    const long long rows = (long long)m.B * m.T;
+    dim3 grid((m.D + 63) / 64, (unsigned)((rows + 31) / 32));
+    const size_t smem = (32 * m.R + 64 * (m.R + 1)) * sizeof(float);
+    dt_fwd_kernel<<<grid, 256, smem, s>>>(xp, m.ldx, dt_proj, raw, rows, m.D, m.R);
+    return launch_status();
+}
+
+int mamba_scan_forward(const MambaDims& m, const float* raw, const float* u, const float* xp,
+                       const float* alog, const float* dskip, const bf16* proj, float* y32,
+                       bf16* gated, float* hchk, cudaStream_t s) {
+    switch (lanes_for(m.N)) {
+        case 4: return launch_scan_fwd<4>(m, raw, u, xp, alog, dskip, proj, y32, gated, hchk, s);
+        case 8: return launch_scan_fwd<8>(m, raw, u, xp, alog, dskip, proj, y32, gated, hchk, s);
+        case 16: return launch_scan_fwd<16>(m, raw, u, xp, alog, dskip, proj, y32, gated, hchk, s);
+        default: return -1;
+    }
+}
+
+int mamba_scan_backward(const MambaDims& m, const float* raw, const float* u, const float* xp,
+                        const float* alog, const float* dskip, const bf16* proj, const float* y32,
+                        const float* dgated, const float* hchk, float* du, float* ddt, bf16* dproj,
+                        float* dbc_part, float* da_part, float* dd_part, cudaStream_t s) {
+#define SB(L)                                                                                 \
+    launch_scan_bwd<L>(m, raw, u, xp, alog, dskip, proj, y32, dgated, hchk, du, ddt, dproj, \
+                       dbc_part, da_part, dd_part, s)
+    switch (lanes_for(m.N)) {
+        case 4: return SB(4);
+        case 8: return SB(8);
+        case 16: return SB(16);
+        default: return -1;
+    }
+#undef SB
+}
+
+int mamba_reduce_dbc(const MambaDims& m, const float* dbc_part, bf16* dxp, cudaStream_t s) {
+    const long long BT = (long long)m.B * m.T, n = BT * m.N;
+    dbc_reduce_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(dbc_part, mamba_scan_groups(m.D, m.N),
+                                                             BT, m.N, m.R, dxp, m.ldx);
+    return launch_status();
+}
+
+int mamba_batch_reduce(const float* part, int B, long long n, float* out, int accumulate,
+                       cudaStream_t s) {
+    batch_reduce_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(part, B, n, out, accumulate);
+    return launch_status();
+}
+
+int mamba_dt_backward(const MambaDims& m, const float* ddt, const float* raw, bf16* draw,
+                      cudaStream_t s) {
+    const long long n = (long long)m.B * m.T * m.D;
+    dt_bwd_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(ddt, raw, draw, n);
+    return launch_status();
+}
+
+int mamba_conv_backward(const MambaDims& m, const bf16* proj, const float* w, const float* bias,
+                        const float* du_scan, const float* du_xp, float* dpre, float* part,
+                        bf16* dproj, float* gw, float* gb, int accumulate, cudaStream_t s) {
+    if (m.K > 8) return -1;
+    const long long rows = (long long)m.B * m.T;
+    dim3 g1((m.D + 255) / 256, mamba_conv_blocks(rows));
+    conv_bwd1_kernel<<<g1, 256, 0, s>>>(proj, m.ldp, m.D, m.T, m.K, w, bias, du_scan, du_xp, dpre,
+                                        part, rows);
+    int rc = launch_status();
+    if (rc) return rc;
+    const long long n = rows * m.D;
+    conv_bwd2_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(dpre, w, dproj, m.ldp, m.D, m.T, m.K,
+                                                            rows);
+    if ((rc = launch_status())) return rc;
+    const int nr = m.D * (m.K + 1);
+    conv_reduce_kernel<<<(nr + 255) / 256, 256, 0, s>>>(part, mamba_conv_blocks(rows), m.D, m.K, gw,
+                                                        gb, accumulate);
+    return launch_status();
+}
+
+}  // namespace llmgpu

@@ -20,6 +20,7 @@
 #include <random>
 #include <unistd.h>
 
+#include "mamba.cuh"
 #include "model.h"
 
 namespace llmgpu {
@@ -352,12 +353,29 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
     c->max_b = max_batch;
     c->max_t = max_seq;
     c->max_bt = max_batch * max_seq;
-    if (cfg.use_mamba || cfg.moe_experts > 0)
+    if (cfg.moe_experts > 0)
         return fail(c, "configuration not supported yet by the device kernels");
+    c->mamba = cfg.use_mamba != 0;
     c->swiglu = cfg.ffn_swiglu != 0;
     const int FH = c->swiglu ? 2 * c->F : c->F;  // width of the FFN up-projection output
-    if (c->hd != 32 && c->hd != 64) return fail(c, "head_dim must be 32 or 64");
-    if (c->C % 32 != 0 || c->F % 32 != 0) return fail(c, "n_embd and ffn hidden must be multiples of 32");
+    if (c->mamba) {
+        // MambaBlock dims (src/model.cpp:44-47): d_inner 0 -> 2*n_embd, dt_rank 0 -> ceil(n_embd/16)
+        c->mD = cfg.d_inner ? cfg.d_inner : 2 * c->C;
+        c->mN = cfg.d_state;
+        c->mR = cfg.dt_rank ? cfg.dt_rank : (c->C + 15) / 16;
+        c->mK = cfg.conv_kernel;
+        c->mRP = c->mR + 2 * c->mN;
+        c->mRPp = (int)align_up(c->mRP, 8);
+        c->mRp = (int)align_up(c->mR, 8);
+        if (c->C % 8 != 0 || c->mD % 8 != 0 || c->mN < 1 || c->mN > 16 || c->mK < 1 ||
+            c->mK > 8 || c->mR < 1 || c->mR > 64)
+            return fail(c, "unsupported Mamba dimensions (n_embd, d_inner multiples of 8; "
+                           "d_state <= 16; conv_kernel <= 8)");
+    } else {
+        if (c->hd != 32 && c->hd != 64) return fail(c, "head_dim must be 32 or 64");
+        if (c->C % 32 != 0 || c->F % 32 != 0)
+            return fail(c, "n_embd and ffn hidden must be multiples of 32");
+    }
     if (c->max_bt > 16384) return fail(c, "at most 16384 tokens per micro-batch");
 
     int dev = 0;
@@ -382,7 +400,12 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
     // bf16 shadows laid out for the GEMMs
     size_t sh = (size_t)c->Vp * C;                            // wte16 [Vp, C]
     if (!cfg.weight_tying) sh += (size_t)C * c->Vp;           // lm16 [C, Vp]
-    sh += (size_t)L * ((size_t)C * 3 * C + (size_t)C * C + (size_t)C * FH + (size_t)C * F + 64 * 4);
+    if (c->mamba)
+        sh += (size_t)L * (2 * (size_t)c->mD * C + (size_t)c->mRP * c->mD +
+                           (size_t)c->mD * c->mRp + (size_t)C * c->mD + 64 * 4);
+    else
+        sh += (size_t)L * ((size_t)C * 3 * C + (size_t)C * C + (size_t)C * FH + (size_t)C * F +
+                           64 * 4);
     c->shadow_elems = sh;
     if (dalloc(c, &c->shadow_arena, sh)) return fail(c, "");
     {
@@ -400,7 +423,27 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
             c->params[c->i_lm].shadow = c->lm16;
             c->params[c->i_lm].shadow_ld = c->Vp;
         }
-        for (int l = 0; l < L; ++l) {
+        for (int l = 0; l < L && c->mamba; ++l) {
+            auto& b = c->blocks[l];
+            const int D = c->mD;
+            bf16* in = take((size_t)2 * D * C);           // in_proj  [2D, E]
+            bf16* xw = take((size_t)c->mRP * D);          // x_proj   [R+2N, D]
+            bf16* dw = take((size_t)D * c->mRp);          // dt_proj  [D, R] (row stride Rp)
+            bf16* ow = take((size_t)C * D);               // out_proj [E, D]
+            c->in16.push_back(in);
+            c->xproj16.push_back(xw);
+            c->dtp16.push_back(dw);
+            c->out16.push_back(ow);
+            c->params[b.in_proj].shadow = in;
+            c->params[b.in_proj].shadow_ld = C;
+            c->params[b.x_proj].shadow = xw;
+            c->params[b.x_proj].shadow_ld = D;
+            c->params[b.dt_proj].shadow = dw;
+            c->params[b.dt_proj].shadow_ld = c->mRp;
+            c->params[b.out_proj].shadow = ow;
+            c->params[b.out_proj].shadow_ld = D;
+        }
+        for (int l = 0; l < L && !c->mamba; ++l) {
             auto& b = c->blocks[l];
             bf16* wqkv = take((size_t)C * 3 * C);
             bf16* wo = take((size_t)C * C);
@@ -445,7 +488,36 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
     // activations
     c->act.resize(L);
     const int nparts = norm_backward_grid(BT);
-    for (int l = 0; l < L; ++l) {
+    if (c->mamba) {
+        const size_t D = c->mD;
+        const int nch = (max_seq + kScanChunk - 1) / kScanChunk;
+        c->mact.resize(L);
+        for (int l = 0; l < L; ++l) {
+            auto& a = c->act[l];
+            auto& m = c->mact[l];
+            if (dalloc(c, &a.x, (size_t)BT * C) || dalloc(c, &a.ln1, (size_t)BT * C) ||
+                dalloc(c, &a.mean1, BT) || dalloc(c, &a.rstd1, BT) ||
+                dalloc(c, &m.proj, (size_t)BT * 2 * D) || dalloc(c, &m.u32, (size_t)BT * D) ||
+                dalloc(c, &m.u16, (size_t)BT * D) || dalloc(c, &m.xp, (size_t)BT * c->mRPp) ||
+                dalloc(c, &m.xp16, (size_t)BT * c->mRPp) || dalloc(c, &m.raw, (size_t)BT * D) ||
+                dalloc(c, &m.y, (size_t)BT * D) || dalloc(c, &m.gated, (size_t)BT * D) ||
+                dalloc(c, &m.hchk, (size_t)max_batch * nch * D * c->mN))
+                return fail(c, "");
+        }
+        const int groups = mamba_scan_groups(c->mD, c->mN);
+        if (dalloc(c, &c->m_dgated, (size_t)BT * D) || dalloc(c, &c->m_du, (size_t)BT * D) ||
+            dalloc(c, &c->m_ddt, (size_t)BT * D) || dalloc(c, &c->m_duxp, (size_t)BT * D) ||
+            dalloc(c, &c->m_dpre, (size_t)BT * D) ||
+            dalloc(c, &c->m_dbc, (size_t)groups * 2 * BT * c->mN) ||
+            dalloc(c, &c->m_da, (size_t)max_batch * D * c->mN) ||
+            dalloc(c, &c->m_dd, (size_t)max_batch * D) ||
+            dalloc(c, &c->m_convpart, (size_t)mamba_conv_blocks(BT) * D * (c->mK + 1)) ||
+            dalloc(c, &c->m_dproj, (size_t)BT * 2 * D) || dalloc(c, &c->m_draw, (size_t)BT * D) ||
+            dalloc(c, &c->m_dxp, (size_t)BT * c->mRPp) ||
+            dalloc(c, &c->m_sgpart, std::max((size_t)BT, (size_t)16 * D) * c->mR))
+            return fail(c, "");
+    }
+    for (int l = 0; l < L && !c->mamba; ++l) {
         auto& a = c->act[l];
         if (dalloc(c, &a.x, (size_t)BT * C) || dalloc(c, &a.y, (size_t)BT * C) ||
             dalloc(c, &a.ln1, (size_t)BT * C) || dalloc(c, &a.mean1, BT) ||
@@ -468,6 +540,10 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
         dalloc(c, &c->colwork, colsum_work_floats(F > C ? F : C)))
         return fail(c, "");
     c->splitws_floats = (size_t)8 * C * (FH > 3 * C ? FH : 3 * C);
+    if (c->mamba) {  // largest Mamba weight gradient: in_proj [2D, E]
+        const size_t mx = std::max<size_t>((size_t)2 * c->mD * C, (size_t)c->mRP * c->mD);
+        c->splitws_floats = std::max(c->splitws_floats, (size_t)8 * mx);
+    }
     if (dalloc(c, &c->splitws, c->splitws_floats)) return fail(c, "");
     if (dalloc(c, &c->d_tokens, BT) || dalloc(c, &c->d_keys, BT) ||
         dalloc(c, &c->d_row_loss, BT) || dalloc(c, &c->d_out, 8) || dalloc(c, &c->d_hp, 16) ||
@@ -549,6 +625,13 @@ void ctx_destroy(Ctx* c) {
     F(c->dln); F(c->dres16); F(c->dy16); F(c->datt); F(c->dqkv); F(c->dh); F(c->dvec);
     F(c->partial); F(c->colwork); F(c->splitws); F(c->d_tokens); F(c->d_keys);
     F(c->dact); F(c->rope);
+    for (auto& m : c->mact) {
+        F(m.proj); F(m.u32); F(m.u16); F(m.xp); F(m.xp16); F(m.raw); F(m.y); F(m.gated);
+        F(m.hchk);
+    }
+    F(c->m_dgated); F(c->m_du); F(c->m_ddt); F(c->m_duxp); F(c->m_dpre); F(c->m_dbc);
+    F(c->m_da); F(c->m_dd); F(c->m_convpart); F(c->m_dproj); F(c->m_draw); F(c->m_dxp);
+    F(c->m_sgpart);
     F(c->d_row_loss); F(c->d_out); F(c->d_hp); F(c->d_normpart); F(c->d_nonfinite); F(c->d_err);
     F(c->d_aparams); F(c->d_chunks); F(c->d_kscale);
     if (c->h_tokens) cudaFreeHost(c->h_tokens);
@@ -576,6 +659,126 @@ void mark(Ctx* c, int i) {
     else
         cudaEventRecord(c->ev[i], c->stream);
 }
+}  // namespace
+
+namespace {
+
+MambaDims mamba_dims(const Ctx* c, int B, int T) {
+    MambaDims m;
+    m.B = B;
+    m.T = T;
+    m.D = c->mD;
+    m.N = c->mN;
+    m.R = c->mR;
+    m.K = c->mK;
+    m.ldp = 2LL * c->mD;
+    m.ldx = c->mRPp;
+    return m;
+}
+
+// MambaBlock::forward (src/mamba.cpp:60-166): norm -> in_proj -> conv+SiLU -> x_proj -> dt ->
+// selective scan -> SiLU(z) gate -> out_proj + residual.
+int mamba_forward_layer(Ctx* c, int l, int B, int T, float* xnext) {
+    const int C = c->C, D = c->mD, BT = B * T;
+    const int rms = c->cfg.use_rmsnorm;
+    cudaStream_t s = c->stream;
+    auto& a = c->act[l];
+    auto& m = c->mact[l];
+    auto& b = c->blocks[l];
+    auto pp = [&](int i) { return c->p + c->params[i].offset; };
+    const MambaDims md = mamba_dims(c, B, T);
+    int rc;
+    // the block's norm has no bias (src/mamba.cpp:67)
+    KC(norm_forward(a.x, pp(b.norm_w), nullptr, a.ln1, a.mean1, a.rstd1, BT, C, rms, s));
+    if ((rc = gemm(c, a.ln1, C, 0, c->in16[l], C, 0, BT, 2 * D, C,
+                   epi_args(kEpiStoreBF16, m.proj, 2 * D))))
+        return rc;
+    KC(mamba_conv_forward(md, m.proj, pp(b.conv_w), pp(b.conv_b), m.u32, m.u16, s));
+    // x_proj: the dt_rank columns feed softplus + a hard clamp whose mask gates the dt
+    // gradient (src/mamba.cpp:318-328); a bf16 operand moves dt_raw enough to flip that mask
+    // near its edges, so those columns are computed in fp32. B and C use the tensor cores.
+    KC(small_gemm_f32(m.u32, D, 1, pp(b.x_proj), 1, D, BT, c->mR, D, 1, c->m_sgpart, m.xp,
+                      nullptr, c->mRPp, 0, s));
+    if ((rc = gemm(c, m.u16, D, 0, c->xproj16[l] + (size_t)c->mR * D, D, 0, BT, 2 * c->mN, D,
+                   epi_args(kEpiStoreF32, m.xp + c->mR, c->mRPp))))
+        return rc;
+    KC(mamba_dt_forward(md, m.xp, pp(b.dt_proj), m.raw, s));
+    KC(mamba_scan_forward(md, m.raw, m.u32, m.xp, pp(b.a_log), pp(b.dskip), m.proj, m.y, m.gated,
+                          m.hchk, s));
+    GemmArgs r = epi_args(kEpiResidF32, xnext, C);
+    r.resid = a.x;
+    r.ldr = C;
+    return gemm(c, m.gated, D, 0, c->out16[l], D, 0, BT, C, D, r);
+}
+
+// MambaBlock::backward (src/mamba.cpp:179-413). On entry c->dres/c->dres16 hold the gradient
+// of the block output; on exit c->dres holds the gradient of the block input.
+int mamba_backward_layer(Ctx* c, int l, int B, int T, int acc) {
+    const int C = c->C, D = c->mD, BT = B * T, R = c->mR;
+    const int rms = c->cfg.use_rmsnorm;
+    cudaStream_t s = c->stream;
+    auto& a = c->act[l];
+    auto& m = c->mact[l];
+    auto& b = c->blocks[l];
+    auto pp = [&](int i) { return c->p + c->params[i].offset; };
+    auto gp = [&](int i) { return c->g + c->params[i].offset; };
+    const MambaDims md = mamba_dims(c, B, T);
+    int rc;
+    // out = x + gated out_proj^T: dgated = dY out_proj, dout_proj = dY^T gated
+    if ((rc = gemm(c, c->dres16, C, 0, c->out16[l], D, 1, BT, D, C,
+                   epi_args(kEpiStoreF32, c->m_dgated, D))))
+        return rc;
+    GemmArgs wo = epi_args(kEpiStoreF32, gp(b.out_proj), D);
+    wo.accumulate = acc;
+    if ((rc = gemm(c, c->dres16, C, 1, m.gated, D, 1, C, D, BT, wo, choose_splits(c, C, D, BT))))
+        return rc;
+    // gate + scan backward (dx_z goes straight into dproj[:, 0:D])
+    KC(mamba_scan_backward(md, m.raw, m.u32, m.xp, pp(b.a_log), pp(b.dskip), m.proj, m.y,
+                           c->m_dgated, m.hchk, c->m_du, c->m_ddt, c->m_dproj, c->m_dbc, c->m_da,
+                           c->m_dd, s));
+    KC(mamba_batch_reduce(c->m_da, B, (long long)D * c->mN, gp(b.a_log), acc, s));
+    KC(mamba_batch_reduce(c->m_dd, B, D, gp(b.dskip), acc, s));
+    KC(mamba_reduce_dbc(md, c->m_dbc, c->m_dxp, s));  // dB, dC -> dxp[:, R:R+2N]
+    // dt: clamp mask + softplus backward, then through dt_proj (src/mamba.cpp:310-329)
+    // These two dt_rank-wide contractions are sums with heavy cancellation, so they stay in
+    // fp32 (a bf16 operand costs ~5% on the dt_proj gradient).
+    float* draw = c->m_dpre;  // free until the conv backward below
+    KC(mamba_dt_backward_f32(md, c->m_ddt, m.raw, draw, s));
+    // dxp[:, :R] = draw dt_proj  ([BT, D] x [D, R]) -> bf16 columns [0, R) of dxp
+    KC(small_gemm_f32(draw, D, 1, pp(b.dt_proj), R, 1, BT, R, D, 1, c->m_sgpart, nullptr,
+                      c->m_dxp, c->mRPp, 0, s));
+    // ddt_proj = draw^T xp[:, :R]  ([D, BT] x [BT, R], K split 16 ways)
+    KC(small_gemm_f32(draw, 1, D, m.xp, c->mRPp, 1, D, R, BT, 16, c->m_sgpart, gp(b.dt_proj),
+                      nullptr, R, acc, s));
+    // x_proj (src/mamba.cpp:330-347)
+    if ((rc = gemm(c, c->m_dxp, c->mRPp, 0, c->xproj16[l], D, 1, BT, D, c->mRP,
+                   epi_args(kEpiStoreF32, c->m_duxp, D))))
+        return rc;
+    GemmArgs wx = epi_args(kEpiStoreF32, gp(b.x_proj), D);
+    wx.accumulate = acc;
+    if ((rc = gemm(c, c->m_dxp, c->mRPp, 1, m.u16, D, 1, c->mRP, D, BT, wx,
+                   choose_splits(c, c->mRP, D, BT))))
+        return rc;
+    // SiLU + causal conv backward; dx_ssm into dproj[:, D:2D] (src/mamba.cpp:348-371)
+    KC(mamba_conv_backward(md, m.proj, pp(b.conv_w), pp(b.conv_b), c->m_du, c->m_duxp, c->m_dpre,
+                           c->m_convpart, c->m_dproj, gp(b.conv_w), gp(b.conv_b), acc, s));
+    // in_proj (src/mamba.cpp:379-396)
+    if ((rc = gemm(c, c->m_dproj, 2 * D, 0, c->in16[l], C, 1, BT, C, 2 * D,
+                   epi_args(kEpiStoreF32, c->dln, C))))
+        return rc;
+    GemmArgs wi = epi_args(kEpiStoreF32, gp(b.in_proj), C);
+    wi.accumulate = acc;
+    if ((rc = gemm(c, c->m_dproj, 2 * D, 1, a.ln1, C, 1, 2 * D, C, BT, wi,
+                   choose_splits(c, 2 * D, C, BT))))
+        return rc;
+    // norm backward + residual (src/mamba.cpp:397-412); updates c->dres in place
+    int nparts = 0;
+    KC(norm_backward(c->dln, a.x, pp(b.norm_w), a.mean1, a.rstd1, c->dres, c->dres, c->dres16,
+                     c->partial, BT, C, rms, &nparts, s));
+    KC(reduce_partials(c->partial, nparts, C, gp(b.norm_w), nullptr, nullptr, acc, s));
+    return 0;
+}
+
 }  // namespace
 
 int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
@@ -609,6 +812,11 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
         auto& a = c->act[l];
         auto& b = c->blocks[l];
         float* xnext = (l + 1 < L) ? c->act[l + 1].x : c->xL;
+        if (c->mamba) {
+            const int rc = mamba_forward_layer(c, l, B, T, xnext);
+            if (rc) return rc;
+            continue;
+        }
         KC(norm_forward(a.x, pp(b.ln1g), pp(b.ln1b), a.ln1, a.mean1, a.rstd1, BT, C, rms, s));
         int rc = gemm(c, a.ln1, C, 0, c->wqkv16[l], 3 * C, 1, BT, 3 * C, C,
                       epi_args(kEpiStoreBF16, a.qkv, 3 * C));
@@ -680,10 +888,14 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
     KC(norm_backward(c->dln, c->xL, pp(c->i_lnfg), c->meanf, c->rstdf, nullptr, c->dres,
                      c->dres16, c->partial, BT, C, rms, &nparts, s));
     KC(reduce_partials(c->partial, nparts, C, gp(c->i_lnfg), rms ? nullptr : gp(c->i_lnfb),
-                       gp(c->blocks[L - 1].b2), acc, s));
+                       c->blocks[L - 1].b2 >= 0 ? gp(c->blocks[L - 1].b2) : nullptr, acc, s));
     for (int l = L - 1; l >= 0; --l) {
         auto& a = c->act[l];
         auto& b = c->blocks[l];
+        if (c->mamba) {
+            if ((rc = mamba_backward_layer(c, l, B, T, acc))) return rc;
+            continue;
+        }
         // ---- FFN  (src/transformer.cpp:120-183)
         GemmArgs w2 = epi_args(kEpiStoreF32, gp(b.W2), C);
         w2.accumulate = acc;

@@ -49,6 +49,19 @@ struct BlockAct {
     bf16* act = nullptr;     // FFN activation [BT, F]
 };
 
+// Mamba block activations kept for the backward (mamba.cuh has the layouts).
+struct MambaAct {
+    bf16* proj = nullptr;    // [BT, 2D]  x_z | x_ssm
+    float* u32 = nullptr;    // [BT, D]
+    bf16* u16 = nullptr;     // [BT, D]
+    float* xp = nullptr;     // [BT, RPp] dt_in | B | C (fp32)
+    bf16* xp16 = nullptr;    // [BT, RPp]
+    float* raw = nullptr;    // [BT, D]   dt before softplus/clamp
+    float* y = nullptr;      // [BT, D]
+    bf16* gated = nullptr;   // [BT, D]
+    float* hchk = nullptr;   // saved scan states
+};
+
 struct Ctx {
     llmgpu_config cfg{};
     int rank = 0, world = 1;
@@ -72,6 +85,15 @@ struct Ctx {
     std::vector<bf16*> wqkv16, wo16, w1_16, w2_16;
     bool swiglu = false;
     float2* rope = nullptr;  // [max_t][hd/2] (cos, sin) when rope_qk
+    // Mamba
+    bool mamba = false;
+    int mD = 0, mN = 0, mR = 0, mK = 0, mRP = 0, mRPp = 0, mRp = 0;
+    std::vector<bf16*> in16, xproj16, dtp16, out16;
+    std::vector<MambaAct> mact;
+    float *m_dgated = nullptr, *m_du = nullptr, *m_ddt = nullptr, *m_duxp = nullptr,
+          *m_dpre = nullptr, *m_dbc = nullptr, *m_da = nullptr, *m_dd = nullptr,
+          *m_convpart = nullptr, *m_sgpart = nullptr;
+    bf16 *m_dproj = nullptr, *m_draw = nullptr, *m_dxp = nullptr;
 
     // activations
     std::vector<BlockAct> act;
