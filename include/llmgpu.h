@@ -151,6 +151,12 @@ void* llmgpu_stream(const llmgpu_ctx* ctx);
  * milliseconds and launch count since the last reset (reset != 0 clears them). */
 int llmgpu_set_profile(llmgpu_ctx* ctx, int enable);
 int llmgpu_gemm_stats(llmgpu_ctx* ctx, double* flops, double* ms, int* launches, int reset);
+/* MoE routing of the last forward pass (introspection; the reference's MoEFFN keeps its
+ * choices internal, src/moe.cpp:36-45): the top-k expert indices [B*T, k] chosen by block
+ * `layer`'s router, in descending router probability (ties: lower index first). Copies at
+ * most n entries into idx and returns B*T*k, or a negative status (not an MoE model, layer
+ * out of range, n too small). Waits for the context stream. */
+int64_t llmgpu_moe_routing(llmgpu_ctx* ctx, int layer, int32_t* idx, int64_t n);
 
 #ifdef __cplusplus
 }

@@ -94,6 +94,36 @@ int llmgpu_op_swiglu_fwd(const void* h13, void* gated, int rows, int F, void* st
 int llmgpu_op_swiglu_bwd(const void* dgated, const void* h13, void* dh13, int rows, int F,
                          void* stream);
 
+/* Grouped (per-expert) GEMM for the MoE FFN experts (the per-token [1,C] matmuls of
+ * MoEFFN::forward, src/moe.cpp:46-56, batched by expert). grp is a device table of
+ * groups+1 ascending row offsets, each a multiple of 128.
+ *   mode 1 (rows): rows [off[g], off[g+1]) of A ([M = row capacity, K], K-major) times group
+ *     g of B, whose rows start at g * b_grp_rows of B's outer dimension; K a multiple of 64;
+ *     epi 0, 1, 3 or 4 as in llmgpu_op_gemm.
+ *   mode 2 (K): out + g * out_grp_stride (+)= A_g^T B_g over rows [off[g], off[g+1]) of
+ *     A ([K = row capacity, M]) and B ([K, N]), both MN-major; epi 1; empty groups write
+ *     zeros (or leave out as is when accumulating).
+ * Returns 0 or a negative status. */
+int llmgpu_op_gemm_grouped(const void* A, long long lda, int a_mn_major, const void* B,
+                           long long ldb, int b_mn_major, int M, int N, int K, int epi, void* out,
+                           long long ldo, int accumulate, void* aux, long long ld_aux,
+                           const int* grp, int groups, int mode, long long b_grp_rows,
+                           long long out_grp_stride, int* err, void* stream);
+/* MoE router (src/moe.cpp:28-45) on B*T rows: the norm output (y - mean) * rstd * gamma
+ * (+ beta unless rms) recomputed in fp32, probs = softmax(. gate) with gate [C, E] fp32,
+ * top-k experts by descending probability (ties: lower index first) and weights
+ * renormalised over the chosen k (sum below 1e-8 -> 1). Outputs probs [BT, E], idx [BT, k],
+ * wts [BT, k], ssum [BT]. */
+int llmgpu_op_moe_route(const float* y, const float* mean, const float* rstd, const float* gamma,
+                        const float* beta, int rms, const float* gate, int B, int T, int C, int E,
+                        int k, float* probs, int* idx, float* wts, float* ssum, void* stream);
+/* Dispatch of the (token, slot) assignments idx [BT, k] into per-expert row blocks:
+ * grp [2E+1] = row offsets off[0..E] (each block padded to a multiple of 128) then the row
+ * counts cnt[0..E-1]; row_of [BT, k] = expert row of each assignment, rows of one expert in
+ * token order; tok_of [BT*k + 128*E] = token of each expert row, -1 for padding rows. */
+int llmgpu_op_moe_dispatch(const int* idx, int B, int T, int E, int k, int* grp, int* row_of,
+                           int* tok_of, void* stream);
+
 /* Number of SMs the library sizes persistent grids for (device 0 of the caller). */
 int llmgpu_op_num_sms(void);
 

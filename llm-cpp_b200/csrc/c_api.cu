@@ -45,6 +45,7 @@ int validate_bt(Ctx* c, int B, int T) {
         cudaMemsetAsync(c->g + p.offset, 0, sizeof(float) * p.numel, c->stream);
         c->last_T = T;
     }
+    c->last_B = B;
     return 0;
 }
 
@@ -454,6 +455,18 @@ int llmgpu_gemm_stats(llmgpu_ctx* h, double* flops, double* ms, int* launches, i
         c->prof_launches = 0;
     }
     return 0;
+}
+
+int64_t llmgpu_moe_routing(llmgpu_ctx* h, int layer, int32_t* idx, int64_t n) {
+    if (check_ctx(h) || !idx) return LLMGPU_E_ARG;
+    Ctx* c = h->c;
+    if (!c->moe) return LLMGPU_E_UNSUPPORTED;
+    if (layer < 0 || layer >= c->L || c->last_B <= 0) return LLMGPU_E_ARG;
+    const int64_t total = (int64_t)c->last_B * c->last_T * c->moe_k;
+    if (n < total) return LLMGPU_E_ARG;
+    if (copy_sync(c, idx, c->moeact[layer].idx, sizeof(int32_t) * total, cudaMemcpyDeviceToHost))
+        return LLMGPU_E_CUDA;
+    return total;
 }
 
 }  // extern "C"

@@ -47,6 +47,30 @@ __device__ __forceinline__ void decode_tile(int t, int num_m, int num_n, int til
     n_blk = local / gm;
 }
 
+// Resolves tile t into block coordinates, group and k-block range [kb0, kb1). Returns false
+// for a tile with no rows in use (row-grouped products, past the last group).
+__device__ __forceinline__ bool tile_work(const GemmArgs& a, const int* s_grp, int t, int num_m,
+                                          int num_n, int tiles_mn, int kblocks, int& m_blk,
+                                          int& n_blk, int& split, int& g, int& kb0, int& kb1) {
+    decode_tile(t, num_m, num_n, tiles_mn, m_blk, n_blk, split);
+    g = 0;
+    if (a.grp_mode == kGroupRows) {
+        const int m0 = m_blk * BM;
+        if (m0 >= s_grp[a.groups]) return false;
+        while (g + 1 < a.groups && s_grp[g + 1] <= m0) ++g;
+        kb0 = 0;
+        kb1 = kblocks;
+    } else if (a.grp_mode == kGroupK) {
+        g = split;
+        kb0 = min(max(s_grp[g] / BK, 0), kblocks);
+        kb1 = min(max(s_grp[g + 1] / BK, kb0), kblocks);
+    } else {
+        kb0 = (int)((long long)split * kblocks / a.splits);
+        kb1 = (int)((long long)(split + 1) * kblocks / a.splits);
+    }
+    return true;
+}
+
 __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* o, const float* v) {
     uint4* o4 = reinterpret_cast<uint4*>(o);
 #pragma unroll
@@ -60,8 +84,9 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* o, const float* v) 
     }
 }
 
+// obase: element offset of the output (group g of a K-grouped product; kEpiStoreF32 only)
 __device__ __forceinline__ void epi_store(const GemmArgs& a, int row, int col0, int split,
-                                          float (&v)[32]) {
+                                          long long obase, float (&v)[32]) {
     const int nvalid = min(32, a.N - col0);
     const bool full = (nvalid == 32) && !a.scalar_store;
     switch (a.epi) {
@@ -79,7 +104,8 @@ __device__ __forceinline__ void epi_store(const GemmArgs& a, int row, int col0, 
         case kEpiStoreF32: {
             int g = col0 / a.col_group;
             int cc = col0 - g * a.col_group;
-            float* o = reinterpret_cast<float*>(a.out) + g * a.group_stride + row * a.ldo + cc;
+            float* o = reinterpret_cast<float*>(a.out) + obase + g * a.group_stride +
+                       (long long)row * a.ldo + cc;
             if (full) {
                 float4* o4 = reinterpret_cast<float4*>(o);
 #pragma unroll
@@ -233,6 +259,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
         tmem_relinquish();
     }
+    __shared__ int s_grp[kMaxGemmGroups + 1];
+    if (args.grp_mode != kGroupNone)
+        for (int i = threadIdx.x; i <= args.groups; i += blockDim.x) s_grp[i] = args.grp[i];
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -252,11 +281,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-                int m_blk, n_blk, split;
-                decode_tile(t, num_m, num_n, tiles_mn, m_blk, n_blk, split);
+                int m_blk, n_blk, split, g, kb0, kb1;
+                if (!tile_work(args, s_grp, t, num_m, num_n, tiles_mn, kblocks, m_blk, n_blk,
+                               split, g, kb0, kb1))
+                    continue;
                 const int m0 = m_blk * BM, n0 = n_blk * BN;
-                const int kb0 = (int)((long long)split * kblocks / splits);
-                const int kb1 = (int)((long long)(split + 1) * kblocks / splits);
+                // row-grouped products read group g of B from row g * b_grp_rows on
+                const int bg = (args.grp_mode == kGroupRows) ? (int)(g * args.b_grp_rows) : 0;
                 for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, args.err,
                                            kDevTimeoutEmpty)) {
@@ -286,11 +317,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         if (m0 + 64 < M) tma_load_2d(a + 8192, &tmA, &full[stage], m0 + 64, k0);
                     }
                     if (!args.b_mn_major) {
-                        tma_load_2d(b, &tmB, &full[stage], k0, n0);
+                        tma_load_2d(b, &tmB, &full[stage], k0, n0 + bg);
                     } else {
                         for (int j = 0; j < BN / 64; ++j)
                             if (n0 + 64 * j < N)
-                                tma_load_2d(b + j * 8192, &tmB, &full[stage], n0 + 64 * j, k0);
+                                tma_load_2d(b + j * 8192, &tmB, &full[stage], n0 + 64 * j,
+                                            k0 + bg);
                     }
                     last_phase[stage] = phase;
                     pending[stage] = true;
@@ -317,10 +349,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             uint32_t acc_phase = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-                int m_blk, n_blk, split;
-                decode_tile(t, num_m, num_n, tiles_mn, m_blk, n_blk, split);
-                const int kb0 = (int)((long long)split * kblocks / splits);
-                const int kb1 = (int)((long long)(split + 1) * kblocks / splits);
+                int m_blk, n_blk, split, g, kb0, kb1;
+                if (!tile_work(args, s_grp, t, num_m, num_n, tiles_mn, kblocks, m_blk, n_blk,
+                               split, g, kb0, kb1))
+                    continue;
                 if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u, args.err,
                                        kDevTimeoutAccFree)) {
                     ok = false;
@@ -353,7 +385,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     }
                 }
                 if (!ok) break;
-                umma_commit(&acc_full[acc]);
+                if (kb1 > kb0)
+                    umma_commit(&acc_full[acc]);
+                else
+                    mbar_arrive(&acc_full[acc]);  // empty group: the epilogue writes zeros
                 acc ^= 1;
                 if (acc == 0) acc_phase ^= 1u;
             }
@@ -364,9 +399,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
-            int m_blk, n_blk, split;
-            decode_tile(t, num_m, num_n, tiles_mn, m_blk, n_blk, split);
+            int m_blk, n_blk, split, g, kb0, kb1;
+            if (!tile_work(args, s_grp, t, num_m, num_n, tiles_mn, kblocks, m_blk, n_blk, split,
+                           g, kb0, kb1))
+                continue;
             const int m0 = m_blk * BM, n0 = n_blk * BN;
+            const bool empty = kb1 <= kb0;
+            const long long obase = (args.grp_mode == kGroupK) ? g * args.out_grp_stride : 0;
             if (!mbar_wait_bounded(&acc_full[acc], acc_phase, args.err, kDevTimeoutAcc)) break;
             tc_fence_after();
             const int row = m0 + q * 32 + lane;
@@ -375,14 +414,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t r[32];
-                tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), r);
-                tmem_ld_wait();
+                if (!empty) {
+                    tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), r);
+                    tmem_ld_wait();
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) r[j] = 0u;
+                }
                 const int col0 = n0 + c * 32;
                 if (row < M && col0 < N) {
                     float v[32];
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-                    epi_store(args, row, col0, split, v);
+                    epi_store(args, row, col0, split, obase, v);
                 }
             }
             tc_fence_before();
@@ -506,8 +550,21 @@ int gemm_make_plan(GemmPlan* plan, const void* A, long long lda, int a_mn_major,
     a.b_mn_major = b_mn_major;
     if (a.splits < 1) a.splits = 1;
     const int kblocks = (K + BK - 1) / BK;
-    if (a.splits > kblocks) return -5;
-    if (a.splits > 1 && a.epi != kEpiSplitPartial) return -6;
+    if (a.grp_mode != kGroupNone) {
+        if (!a.grp || a.groups < 1 || a.groups > kMaxGemmGroups || a.splits != 1) return -40;
+        if (a.grp_mode == kGroupRows) {
+            // a k-tail would run into the next group's rows of an MN-major B
+            if (a_mn_major || (K % BK) != 0 || a.b_grp_rows < (b_mn_major ? K : N)) return -41;
+        } else if (a.grp_mode == kGroupK) {
+            if (!a_mn_major || !b_mn_major || a.epi != kEpiStoreF32 || a.col_group > 0) return -42;
+            a.splits = a.groups;  // the split index of a tile is its group
+        } else {
+            return -43;
+        }
+    } else if (a.splits > kblocks) {
+        return -5;
+    }
+    if (a.splits > 1 && a.epi != kEpiSplitPartial && a.grp_mode != kGroupK) return -6;
     if (a.col_group <= 0) a.col_group = N;
     if (a.col_group != N && (a.col_group % 32) != 0) return -7;
     // alignment needed by the vectorised epilogue
@@ -519,7 +576,7 @@ int gemm_make_plan(GemmPlan* plan, const void* A, long long lda, int a_mn_major,
     } else if (a.epi == kEpiStoreF32 || a.epi == kEpiResidF32) {
         // narrow or odd-strided fp32 outputs take the scalar store path
         a.scalar_store = ((a.ldo % 4) != 0 || (reinterpret_cast<uintptr_t>(a.out) & 15) ||
-                          (a.group_stride % 4) != 0) ? 1 : 0;
+                          (a.group_stride % 4) != 0 || (a.out_grp_stride % 4) != 0) ? 1 : 0;
         if (a.epi == kEpiResidF32 &&
             ((a.ldr % 4) != 0 || (reinterpret_cast<uintptr_t>(a.resid) & 15)))
             a.scalar_store = 1;
@@ -551,11 +608,14 @@ int gemm_make_plan(GemmPlan* plan, const void* A, long long lda, int a_mn_major,
     else
         rc = make_tmap_bf16(&plan->tmA, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, 64, BK);
     if (rc) return -20 + rc;
+    // a row-grouped B stacks `groups` blocks of b_grp_rows rows along its outer dimension
+    const uint64_t b_rows = (a.grp_mode == kGroupRows)
+                                ? (uint64_t)a.groups * (uint64_t)a.b_grp_rows
+                                : (uint64_t)(b_mn_major ? K : N);
     if (!b_mn_major)
-        rc = make_tmap_bf16(&plan->tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK,
-                            (uint32_t)bn);
+        rc = make_tmap_bf16(&plan->tmB, B, (uint64_t)K, b_rows, (uint64_t)ldb, BK, (uint32_t)bn);
     else
-        rc = make_tmap_bf16(&plan->tmB, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, BK);
+        rc = make_tmap_bf16(&plan->tmB, B, (uint64_t)N, b_rows, (uint64_t)ldb, 64, BK);
     if (rc) return -30 + rc;
     long long tiles = (long long)num_m * ((N + bn - 1) / bn) * a.splits;
     plan->grid = (int)(tiles < num_sms ? tiles : num_sms);

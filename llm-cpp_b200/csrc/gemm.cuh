@@ -43,7 +43,25 @@ struct GemmArgs {
     int splits;            // >=1; kEpiSplitPartial writes `splits` partial planes
     int scalar_store;      // set by the planner when the output is not 16-byte aligned
     int* err;              // device error word
+    // Grouped (per-expert) products. `grp` is a device table of groups+1 ascending row
+    // offsets, each a multiple of 128 (entry `groups` = rows in use), written by an earlier
+    // kernel on the same stream, so the grouping needs no host synchronisation.
+    //   kGroupRows: A's rows (and out's) are the groups' rows stacked. A tile of rows in
+    //               [off[g], off[g+1]) multiplies group g of B, whose rows in B's tensor map
+    //               start at g * b_grp_rows. Tiles at or past off[groups] do nothing.
+    //   kGroupK:    A and B are both MN-major with the groups' rows stacked along K; group g
+    //               contracts rows [off[g], off[g+1]) into out + g * out_grp_stride (an
+    //               empty group writes zeros, or leaves `out` as is when accumulating).
+    const int* grp;
+    int groups;
+    int grp_mode;
+    long long b_grp_rows;
+    long long out_grp_stride;
 };
+
+enum GemmGroupMode : int { kGroupNone = 0, kGroupRows = 1, kGroupK = 2 };
+constexpr int kMaxGemmGroups = 64;
+constexpr int kGemmRowAlign = 128;  // group offsets are multiples of the tile height
 
 // Precomputed launch: tensor maps + args + tile config. Encoding tensor maps
 // costs host time, so the model builds one GemmPlan per call site at setup.
@@ -58,6 +76,8 @@ struct GemmPlan {
 
 // Builds a plan. A is [M,K] (K-major, lda >= K) or [K,M] (MN-major, lda >= M);
 // B is [N,K] (K-major) or [K,N] (MN-major). Returns 0 on success.
+// Grouped plans: kGroupRows takes M = row capacity of A/out and K a multiple of 64;
+// kGroupK takes M, N of one group's output and K = row capacity of A and B.
 int gemm_make_plan(GemmPlan* plan, const void* A, long long lda, int a_mn_major, const void* B,
                    long long ldb, int b_mn_major, int M, int N, int K, const GemmArgs& epi,
                    int bn_hint, int num_sms);

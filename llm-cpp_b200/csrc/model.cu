@@ -22,6 +22,7 @@
 
 #include "mamba.cuh"
 #include "model.h"
+#include "moe.cuh"
 
 namespace llmgpu {
 
@@ -353,8 +354,19 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
     c->max_b = max_batch;
     c->max_t = max_seq;
     c->max_bt = max_batch * max_seq;
-    if (cfg.moe_experts > 0)
-        return fail(c, "configuration not supported yet by the device kernels");
+    c->moe = cfg.moe_experts > 0 && !cfg.use_mamba;
+    if (c->moe) {
+        // MoEFFN (src/moe.cpp:8-22): experts of hidden 4 * n_embd, GELU, top-k routing
+        c->moe_E = cfg.moe_experts;
+        c->moe_k = cfg.moe_top_k > 0 ? cfg.moe_top_k : 2;
+        c->moe_He = 4 * cfg.n_embd;
+        c->moe_coef = cfg.moe_aux_coef;
+        if (c->moe_E > kMoeMaxExperts || c->moe_k > kMoeMaxTopK || c->moe_k > c->moe_E ||
+            cfg.ffn_swiglu || cfg.n_embd % 64 != 0)
+            return fail(c, "unsupported MoE configuration (at most 16 experts, top-k <= 4, "
+                           "n_embd a multiple of 64, GELU experts)");
+        c->moe_cap = moe_capacity(max_batch * max_seq, c->moe_E, c->moe_k);
+    }
     c->mamba = cfg.use_mamba != 0;
     c->swiglu = cfg.ffn_swiglu != 0;
     const int FH = c->swiglu ? 2 * c->F : c->F;  // width of the FFN up-projection output
@@ -403,6 +415,9 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
     if (c->mamba)
         sh += (size_t)L * (2 * (size_t)c->mD * C + (size_t)c->mRP * c->mD +
                            (size_t)c->mD * c->mRp + (size_t)C * c->mD + 64 * 4);
+    else if (c->moe)
+        sh += (size_t)L * ((size_t)C * 3 * C + (size_t)C * C +
+                           2 * (size_t)c->moe_E * C * c->moe_He + 64 * 4);
     else
         sh += (size_t)L * ((size_t)C * 3 * C + (size_t)C * C + (size_t)C * FH + (size_t)C * F +
                            64 * 4);
@@ -447,18 +462,31 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
             auto& b = c->blocks[l];
             bf16* wqkv = take((size_t)C * 3 * C);
             bf16* wo = take((size_t)C * C);
-            bf16* w1 = take((size_t)C * FH);  // [C, F] or, for SwiGLU, [W1 | W3] as [C, 2F]
-            bf16* w2 = take((size_t)F * C);
             c->wqkv16.push_back(wqkv);
             c->wo16.push_back(wo);
-            c->w1_16.push_back(w1);
-            c->w2_16.push_back(w2);
             c->params[b.Wq].shadow = wqkv;
             c->params[b.Wk].shadow = wqkv + C;
             c->params[b.Wv].shadow = wqkv + 2 * C;
             c->params[b.Wq].shadow_ld = c->params[b.Wk].shadow_ld = c->params[b.Wv].shadow_ld = 3 * C;
             c->params[b.Wo].shadow = wo;
             c->params[b.Wo].shadow_ld = C;
+            if (c->moe) {
+                // expert stacks, row-major like the parameters: W1e [E*C, He], W2e [E*He, C]
+                const size_t ne = (size_t)c->moe_E * C * c->moe_He;
+                bf16* w1e = take(ne);
+                bf16* w2e = take(ne);
+                c->w1e16.push_back(w1e);
+                c->w2e16.push_back(w2e);
+                c->params[b.W1e].shadow = w1e;
+                c->params[b.W1e].shadow_ld = c->moe_He;
+                c->params[b.W2e].shadow = w2e;
+                c->params[b.W2e].shadow_ld = C;
+                continue;
+            }
+            bf16* w1 = take((size_t)C * FH);  // [C, F] or, for SwiGLU, [W1 | W3] as [C, 2F]
+            bf16* w2 = take((size_t)F * C);
+            c->w1_16.push_back(w1);
+            c->w2_16.push_back(w2);
             c->params[b.W1].shadow = w1;
             c->params[b.W1].shadow_ld = FH;
             if (b.W3 >= 0) {
@@ -524,8 +552,29 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
             dalloc(c, &a.rstd1, BT) || dalloc(c, &a.qkv, (size_t)BT * 3 * C) ||
             dalloc(c, &a.att, (size_t)BT * C) || dalloc(c, &a.lse, (size_t)BT * c->H) ||
             dalloc(c, &a.ln2, (size_t)BT * C) || dalloc(c, &a.mean2, BT) ||
-            dalloc(c, &a.rstd2, BT) || dalloc(c, &a.h, (size_t)BT * FH) ||
-            dalloc(c, &a.act, (size_t)BT * F))
+            dalloc(c, &a.rstd2, BT))
+            return fail(c, "");
+        if (!c->moe && (dalloc(c, &a.h, (size_t)BT * FH) || dalloc(c, &a.act, (size_t)BT * F)))
+            return fail(c, "");
+    }
+    if (c->moe) {
+        const size_t E = c->moe_E, k = c->moe_k, He = c->moe_He, cap = c->moe_cap;
+        c->moeact.resize(L);
+        for (int l = 0; l < L; ++l) {
+            auto& e = c->moeact[l];
+            if (dalloc(c, &e.probs, (size_t)BT * E) || dalloc(c, &e.idx, (size_t)BT * k) ||
+                dalloc(c, &e.wts, (size_t)BT * k) || dalloc(c, &e.ssum, BT) ||
+                dalloc(c, &e.grp, 2 * E + 1) || dalloc(c, &e.row_of, (size_t)BT * k) ||
+                dalloc(c, &e.tok_of, cap) || dalloc(c, &e.xg, cap * C) ||
+                dalloc(c, &e.pre, cap * He) || dalloc(c, &e.act, cap * He) ||
+                dalloc(c, &e.yg, cap * C))
+                return fail(c, "");
+        }
+        if (dalloc(c, &c->moe_load, (size_t)L * max_batch * E) ||
+            dalloc(c, &c->moe_aux, (size_t)L * max_batch) || dalloc(c, &c->e_dyg, cap * C) ||
+            dalloc(c, &c->e_dpre, cap * He) || dalloc(c, &c->e_dxg, cap * C) ||
+            dalloc(c, &c->e_dscores, (size_t)BT * E) ||
+            dalloc(c, &c->e_gpart, (size_t)moe_gate_grad_parts(BT) * C * E))
             return fail(c, "");
     }
     if (dalloc(c, &c->xL, (size_t)BT * C) || dalloc(c, &c->lnf, (size_t)BT * C) ||
@@ -632,6 +681,12 @@ void ctx_destroy(Ctx* c) {
     F(c->m_dgated); F(c->m_du); F(c->m_ddt); F(c->m_duxp); F(c->m_dpre); F(c->m_dbc);
     F(c->m_da); F(c->m_dd); F(c->m_convpart); F(c->m_dproj); F(c->m_draw); F(c->m_dxp);
     F(c->m_sgpart);
+    for (auto& e : c->moeact) {
+        F(e.probs); F(e.idx); F(e.wts); F(e.ssum); F(e.grp); F(e.row_of); F(e.tok_of);
+        F(e.xg); F(e.pre); F(e.act); F(e.yg);
+    }
+    F(c->moe_load); F(c->moe_aux); F(c->e_dyg); F(c->e_dpre); F(c->e_dxg); F(c->e_dscores);
+    F(c->e_gpart);
     F(c->d_row_loss); F(c->d_out); F(c->d_hp); F(c->d_normpart); F(c->d_nonfinite); F(c->d_err);
     F(c->d_aparams); F(c->d_chunks); F(c->d_kscale);
     if (c->h_tokens) cudaFreeHost(c->h_tokens);
@@ -779,6 +834,101 @@ int mamba_backward_layer(Ctx* c, int l, int B, int T, int acc) {
     return 0;
 }
 
+MoeDims moe_dims(const Ctx* c, int B, int T) {
+    MoeDims m;
+    m.B = B;
+    m.T = T;
+    m.C = c->C;
+    m.E = c->moe_E;
+    m.k = c->moe_k;
+    m.cap = c->moe_cap;
+    return m;
+}
+
+// Grouped-GEMM arguments over the expert row blocks of table `grp`.
+GemmArgs grouped(GemmArgs a, const int* grp, int E, int mode, long long b_grp_rows,
+                 long long out_grp_stride) {
+    a.grp = grp;
+    a.groups = E;
+    a.grp_mode = mode;
+    a.b_grp_rows = b_grp_rows;
+    a.out_grp_stride = out_grp_stride;
+    return a;
+}
+
+// MoEFFN::forward (src/moe.cpp:23-62) and aux_loss (:64-75) on the norm output of block l:
+// route, dispatch into expert row blocks, expert GEMMs (GELU fused), weighted combine
+// + residual into xnext.
+int moe_forward_ffn(Ctx* c, int l, int B, int T, float* xnext) {
+    const int C = c->C, E = c->moe_E, He = c->moe_He, cap = c->moe_cap;
+    const int rms = c->cfg.use_rmsnorm;
+    cudaStream_t s = c->stream;
+    auto pp = [&](int i) { return c->p + c->params[i].offset; };
+    auto& a = c->act[l];
+    auto& b = c->blocks[l];
+    auto& e = c->moeact[l];
+    const MoeDims md = moe_dims(c, B, T);
+    KC(moe_router_forward(md, a.y, a.mean2, a.rstd2, pp(b.ln2g), pp(b.ln2b), rms, pp(b.gate),
+                          e.probs, e.idx, e.wts, e.ssum, s));
+    KC(moe_aux_forward(md, e.probs, c->moe_coef, c->moe_load + (size_t)l * B * E,
+                       c->moe_aux + (size_t)l * B, s));
+    KC(moe_dispatch(md, e.idx, e.grp, e.row_of, e.tok_of, s));
+    KC(moe_gather(md, a.ln2, e.tok_of, e.grp, e.xg, s));
+    int rc;
+    // h = GELU(xg W1e[g]): W1e[g] is [C, He] (MN-major B), group g from row g*C of the stack
+    GemmArgs g1 = grouped(epi_args(kEpiGeluBF16, e.act, He), e.grp, E, kGroupRows, C, 0);
+    g1.aux = e.pre;
+    g1.ld_aux = He;
+    if ((rc = gemm(c, e.xg, C, 0, c->w1e16[l], He, 1, cap, He, C, g1))) return rc;
+    // y = h W2e[g]: W2e[g] is [He, C], group g from row g*He
+    GemmArgs g2 = grouped(epi_args(kEpiStoreF32, e.yg, C), e.grp, E, kGroupRows, He, 0);
+    if ((rc = gemm(c, e.act, He, 0, c->w2e16[l], C, 1, cap, C, He, g2))) return rc;
+    KC(moe_combine(md, a.y, e.yg, e.row_of, e.wts, xnext, s));
+    return 0;
+}
+
+// Backward of moe_forward_ffn: c->dres is the gradient of the block output; writes the
+// gradient of the norm output into c->dln and the expert / gate parameter gradients.
+int moe_backward_ffn(Ctx* c, int l, int B, int T, int acc) {
+    const int C = c->C, E = c->moe_E, He = c->moe_He, cap = c->moe_cap;
+    const int rms = c->cfg.use_rmsnorm;
+    cudaStream_t s = c->stream;
+    auto pp = [&](int i) { return c->p + c->params[i].offset; };
+    auto gp = [&](int i) { return c->g + c->params[i].offset; };
+    auto& a = c->act[l];
+    auto& b = c->blocks[l];
+    auto& e = c->moeact[l];
+    const MoeDims md = moe_dims(c, B, T);
+    // each sequence's loss weighs 1/B in the micro-batch mean (src/trainer.cpp:148-150)
+    KC(moe_combine_backward(md, c->dres, e.yg, e.row_of, e.idx, e.wts, e.ssum, e.probs,
+                            c->moe_load + (size_t)l * B * E, c->moe_coef, 1.0f / (float)B,
+                            c->e_dyg, c->e_dscores, s));
+    KC(moe_zero_pad_rows(md, e.grp, c->e_dyg, C, s));
+    int rc;
+    // dW2e[g] = h_g^T dy_g over the rows of expert g
+    GemmArgs w2 = grouped(epi_args(kEpiStoreF32, gp(b.W2e), C), e.grp, E, kGroupK, 0,
+                          (long long)He * C);
+    w2.accumulate = acc;
+    if ((rc = gemm(c, e.act, He, 1, c->e_dyg, C, 1, He, C, cap, w2))) return rc;
+    // dpre = (dy W2e[g]^T) * GELU'(pre): W2e[g] read as [N=He, K=C]
+    GemmArgs dg = grouped(epi_args(kEpiDGeluBF16, c->e_dpre, He), e.grp, E, kGroupRows, He, 0);
+    dg.aux = e.pre;
+    dg.ld_aux = He;
+    if ((rc = gemm(c, c->e_dyg, C, 0, c->w2e16[l], C, 0, cap, He, C, dg))) return rc;
+    // dW1e[g] = xg_g^T dpre_g
+    GemmArgs w1 = grouped(epi_args(kEpiStoreF32, gp(b.W1e), He), e.grp, E, kGroupK, 0,
+                          (long long)C * He);
+    w1.accumulate = acc;
+    if ((rc = gemm(c, e.xg, C, 1, c->e_dpre, He, 1, C, He, cap, w1))) return rc;
+    // dxg = dpre W1e[g]^T: W1e[g] read as [N=C, K=He]
+    GemmArgs dx = grouped(epi_args(kEpiStoreF32, c->e_dxg, C), e.grp, E, kGroupRows, C, 0);
+    if ((rc = gemm(c, c->e_dpre, He, 0, c->w1e16[l], He, 0, cap, C, He, dx))) return rc;
+    KC(moe_scatter_sum(md, c->e_dxg, e.row_of, c->e_dscores, pp(b.gate), c->dln, s));
+    KC(moe_gate_grad(md, a.y, a.mean2, a.rstd2, pp(b.ln2g), pp(b.ln2b), rms, c->e_dscores,
+                     c->e_gpart, gp(b.gate), acc, s));
+    return 0;
+}
+
 }  // namespace
 
 int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
@@ -827,6 +977,10 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
         r.ldr = C;
         if ((rc = gemm(c, a.att, C, 0, c->wo16[l], C, 1, BT, C, C, r))) return rc;
         KC(norm_forward(a.y, pp(b.ln2g), pp(b.ln2b), a.ln2, a.mean2, a.rstd2, BT, C, rms, s));
+        if (c->moe) {
+            if ((rc = moe_forward_ffn(c, l, B, T, xnext))) return rc;
+            continue;
+        }
         if (c->swiglu) {  // h13 = ln2 [W1 | W3]; act = silu(h1) * h3 (src/transformer.cpp:22-30)
             if ((rc = gemm(c, a.ln2, C, 0, c->w1_16[l], 2 * F, 1, BT, 2 * F, C,
                            epi_args(kEpiStoreBF16, a.h, 2 * F))))
@@ -859,6 +1013,7 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
     KC(cross_entropy_fwd_bwd(c->logits, BT, V, Vp, c->d_tokens, c->d_row_loss, 1.0f / (float)BT,
                              c->smoothing, s));
     KC(mean_reduce(c->d_row_loss, BT, c->d_out, s));
+    if (c->moe) KC(moe_add_aux(c->moe_aux, L, B, c->d_out, s));
     mark(c, 2);
     if (!backward) return 0;
     // ------------------------------------------------------------------ backward
@@ -897,11 +1052,16 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
             continue;
         }
         // ---- FFN  (src/transformer.cpp:120-183)
-        GemmArgs w2 = epi_args(kEpiStoreF32, gp(b.W2), C);
-        w2.accumulate = acc;
-        if ((rc = gemm(c, a.act, F, 1, c->dres16, C, 1, F, C, BT, w2, choose_splits(c, F, C, BT))))
-            return rc;
-        if (c->swiglu) {  // src/transformer.cpp:41-119
+        if (!c->moe) {
+            GemmArgs w2 = epi_args(kEpiStoreF32, gp(b.W2), C);
+            w2.accumulate = acc;
+            if ((rc = gemm(c, a.act, F, 1, c->dres16, C, 1, F, C, BT, w2,
+                           choose_splits(c, F, C, BT))))
+                return rc;
+        }
+        if (c->moe) {
+            if ((rc = moe_backward_ffn(c, l, B, T, acc))) return rc;
+        } else if (c->swiglu) {  // src/transformer.cpp:41-119
             // dgated = dY W2^T, then dh13 = [dh1 | dh3]
             if ((rc = gemm(c, c->dres16, C, 0, c->w2_16[l], C, 0, BT, F, C,
                            epi_args(kEpiStoreBF16, c->dact, F))))
@@ -960,7 +1120,8 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
         KC(norm_backward(c->dln, a.x, pp(b.ln1g), a.mean1, a.rstd1, c->dy, c->dres, c->dres16,
                          c->partial, BT, C, rms, &nparts, s));
         KC(reduce_partials(c->partial, nparts, C, gp(b.ln1g), rms ? nullptr : gp(b.ln1b),
-                           l > 0 ? gp(c->blocks[l - 1].b2) : nullptr, acc, s));
+                           (l > 0 && c->blocks[l - 1].b2 >= 0) ? gp(c->blocks[l - 1].b2) : nullptr,
+                           acc, s));
     }
     // embedding scatter (src/model.cpp:314-322)
     CK(cudaStreamWaitEvent(s, c->ev_keys, 0));

@@ -62,6 +62,21 @@ struct MambaAct {
     float* hchk = nullptr;   // saved scan states
 };
 
+// MoE FFN activations kept for the backward, per block (moe.cuh has the layouts).
+struct MoeAct {
+    float* probs = nullptr;  // [BT, E]
+    int* idx = nullptr;      // [BT, k]
+    float* wts = nullptr;    // [BT, k]
+    float* ssum = nullptr;   // [BT]
+    int* grp = nullptr;      // [2E+1] expert row offsets and counts
+    int* row_of = nullptr;   // [BT, k]
+    int* tok_of = nullptr;   // [cap]
+    bf16* xg = nullptr;      // [cap, C]  gathered norm output
+    bf16* pre = nullptr;     // [cap, He] expert pre-activation
+    bf16* act = nullptr;     // [cap, He] GELU(pre)
+    float* yg = nullptr;     // [cap, C]  expert outputs
+};
+
 struct Ctx {
     llmgpu_config cfg{};
     int rank = 0, world = 1;
@@ -94,6 +109,15 @@ struct Ctx {
           *m_dpre = nullptr, *m_dbc = nullptr, *m_da = nullptr, *m_dd = nullptr,
           *m_convpart = nullptr, *m_sgpart = nullptr;
     bf16 *m_dproj = nullptr, *m_draw = nullptr, *m_dxp = nullptr;
+    // MoE FFN: E experts of hidden He = 4C, top-k, expert row capacity cap
+    bool moe = false;
+    int moe_E = 0, moe_k = 0, moe_He = 0, moe_cap = 0;
+    float moe_coef = 0.f;
+    std::vector<bf16*> w1e16, w2e16;  // [E*C, He], [E*He, C]
+    std::vector<MoeAct> moeact;
+    float *moe_load = nullptr, *moe_aux = nullptr;  // [L][B][E], [L][B]
+    bf16 *e_dyg = nullptr, *e_dpre = nullptr;       // [cap, C], [cap, He]
+    float *e_dxg = nullptr, *e_dscores = nullptr, *e_gpart = nullptr;
 
     // activations
     std::vector<BlockAct> act;
@@ -140,6 +164,7 @@ struct Ctx {
     int step_count = 0, skipped = 0;
     float last_loss = 0.f, last_gnorm = 0.f;
     int last_T = -1;
+    int last_B = 0;  // micro-batch of the last forward
     float timings[6] = {};
     int launches = 0;
 

@@ -5,6 +5,7 @@
 #include "gemm.cuh"
 #include "kernels.cuh"
 #include "llmgpu_ops.h"
+#include "moe.cuh"
 
 using namespace llmgpu;
 
@@ -118,4 +119,48 @@ extern "C" int llmgpu_op_swiglu_bwd(const void* dgated, const void* h13, void* d
     return swiglu_backward(reinterpret_cast<const bf16*>(dgated), reinterpret_cast<const bf16*>(h13),
                            reinterpret_cast<bf16*>(dh13), rows, F,
                            reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int llmgpu_op_gemm_grouped(const void* A, long long lda, int a_mn_major, const void* B,
+                                      long long ldb, int b_mn_major, int M, int N, int K, int epi,
+                                      void* out, long long ldo, int accumulate, void* aux,
+                                      long long ld_aux, const int* grp, int groups, int mode,
+                                      long long b_grp_rows, long long out_grp_stride, int* err,
+                                      void* stream) {
+    if (mode != kGroupRows && mode != kGroupK) return -100;
+    GemmArgs g{};
+    g.epi = epi;
+    g.accumulate = accumulate;
+    g.out = out;
+    g.ldo = ldo;
+    g.aux = aux;
+    g.ld_aux = ld_aux;
+    g.splits = 1;
+    g.err = err;
+    g.grp = grp;
+    g.groups = groups;
+    g.grp_mode = mode;
+    g.b_grp_rows = b_grp_rows;
+    g.out_grp_stride = out_grp_stride;
+    GemmPlan plan;
+    int rc = gemm_make_plan(&plan, A, lda, a_mn_major, B, ldb, b_mn_major, M, N, K, g, 0,
+                            device_num_sms());
+    if (rc) return rc;
+    return gemm_run(plan, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int llmgpu_op_moe_route(const float* y, const float* mean, const float* rstd,
+                                   const float* gamma, const float* beta, int rms,
+                                   const float* gate, int B, int T, int C, int E, int k,
+                                   float* probs, int* idx, float* wts, float* ssum,
+                                   void* stream) {
+    MoeDims m{B, T, C, E, k, moe_capacity(B * T, E, k)};
+    return moe_router_forward(m, y, mean, rstd, gamma, beta, rms, gate, probs, idx, wts, ssum,
+                              reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int llmgpu_op_moe_dispatch(const int* idx, int B, int T, int E, int k, int* grp,
+                                      int* row_of, int* tok_of, void* stream) {
+    MoeDims m{B, T, 8 /* C: unused by the dispatch */, E, k, moe_capacity(B * T, E, k)};
+    return moe_dispatch(m, idx, grp, row_of, tok_of, reinterpret_cast<cudaStream_t>(stream));
 }

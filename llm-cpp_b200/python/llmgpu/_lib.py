@@ -36,9 +36,16 @@ def _declare(lib):
     lib.llmgpu_op_attention_bwd.argtypes = [c_vp] * 6 + [c_int, c_int, c_int, c_int, c_vp, c_vp]
     lib.llmgpu_op_swiglu_fwd.argtypes = [c_vp, c_vp, c_int, c_int, c_vp]
     lib.llmgpu_op_swiglu_bwd.argtypes = [c_vp, c_vp, c_vp, c_int, c_int, c_vp]
+    lib.llmgpu_op_gemm_grouped.argtypes = [c_vp, c_ll, c_int, c_vp, c_ll, c_int, c_int, c_int,
+                                           c_int, c_int, c_vp, c_ll, c_int, c_vp, c_ll, c_vp,
+                                           c_int, c_int, c_ll, c_ll, c_vp, c_vp]
+    lib.llmgpu_op_moe_route.argtypes = [c_vp] * 5 + [c_int, c_vp] + [c_int] * 5 + [c_vp] * 5
+    lib.llmgpu_op_moe_dispatch.argtypes = [c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp,
+                                           c_vp]
     for n in ("llmgpu_op_embed", "llmgpu_op_norm_fwd", "llmgpu_op_norm_bwd",
               "llmgpu_op_cross_entropy", "llmgpu_op_attention_fwd", "llmgpu_op_attention_bwd",
-              "llmgpu_op_swiglu_fwd", "llmgpu_op_swiglu_bwd"):
+              "llmgpu_op_swiglu_fwd", "llmgpu_op_swiglu_bwd", "llmgpu_op_gemm_grouped",
+              "llmgpu_op_moe_route", "llmgpu_op_moe_dispatch"):
         getattr(lib, n).restype = c_int
     try:
         from . import _abi_decl

@@ -151,3 +151,58 @@ def swiglu_bwd(dg, h13, F):
     _sync_check(lib.llmgpu_op_swiglu_bwd(_ptr(dg), _ptr(h13), _ptr(d), rows, F, _stream()),
                 "swiglu_bwd")
     return d
+
+
+GROUP_ROWS, GROUP_K = 1, 2
+
+
+def gemm_grouped(A, B, M, N, K, grp, groups, mode, *, a_mn=False, b_mn=False, lda=None,
+                 ldb=None, epi=EPI_F32, out=None, ldo=None, accumulate=False, aux=None,
+                 ld_aux=None, b_grp_rows=0, out_grp_stride=0):
+    """Grouped (per-expert) GEMM; `grp` is an int32 device tensor of groups+1 row offsets."""
+    lib = load()
+    if lda is None:
+        lda = A.shape[-1]
+    if ldb is None:
+        ldb = B.shape[-1]
+    if ldo is None:
+        ldo = out.shape[-1]
+    err = torch.zeros(1, dtype=torch.int32, device=A.device)
+    rc = lib.llmgpu_op_gemm_grouped(_ptr(A), lda, int(a_mn), _ptr(B), ldb, int(b_mn), M, N, K,
+                                    epi, _ptr(out), ldo, int(accumulate), _ptr(aux), ld_aux or 0,
+                                    _ptr(grp), groups, mode, b_grp_rows, out_grp_stride,
+                                    _ptr(err), _stream())
+    _check(rc, "llmgpu_op_gemm_grouped")
+    torch.cuda.synchronize()
+    if int(err.item()) != 0:
+        raise KernelError(f"grouped gemm device error code {int(err.item())}")
+    return out
+
+
+def moe_route(y, mean, rstd, gamma, beta, gate, B, T, k, rms=False):
+    """Router: returns (probs [BT,E], idx [BT,k], wts [BT,k], ssum [BT])."""
+    lib = load()
+    C, E = gate.shape
+    dev = y.device
+    probs = torch.empty(B * T, E, dtype=torch.float32, device=dev)
+    idx = torch.empty(B * T, k, dtype=torch.int32, device=dev)
+    wts = torch.empty(B * T, k, dtype=torch.float32, device=dev)
+    ssum = torch.empty(B * T, dtype=torch.float32, device=dev)
+    _sync_check(lib.llmgpu_op_moe_route(_ptr(y), _ptr(mean), _ptr(rstd), _ptr(gamma), _ptr(beta),
+                                        int(rms), _ptr(gate), B, T, C, E, k, _ptr(probs),
+                                        _ptr(idx), _ptr(wts), _ptr(ssum), _stream()),
+                "moe_route")
+    return probs, idx, wts, ssum
+
+
+def moe_dispatch(idx, B, T, E):
+    """Dispatch: returns (grp [2E+1], row_of [BT,k], tok_of [BT*k + 128E])."""
+    lib = load()
+    k = idx.shape[1]
+    dev = idx.device
+    grp = torch.empty(2 * E + 1, dtype=torch.int32, device=dev)
+    row_of = torch.empty(B * T, k, dtype=torch.int32, device=dev)
+    tok_of = torch.empty(B * T * k + 128 * E, dtype=torch.int32, device=dev)
+    _sync_check(lib.llmgpu_op_moe_dispatch(_ptr(idx), B, T, E, k, _ptr(grp), _ptr(row_of),
+                                           _ptr(tok_of), _stream()), "moe_dispatch")
+    return grp, row_of, tok_of

@@ -237,3 +237,12 @@ class Trainer:
         self.lib.llmgpu_gemm_stats(self.h, ctypes.byref(f), ctypes.byref(ms), ctypes.byref(n),
                                    int(reset))
         return f.value, ms.value, n.value
+
+    def moe_routing(self, layer, B, T, k):
+        """Top-k expert indices [B*T, k] chosen by block `layer` in the last forward pass."""
+        out = np.empty((B * T, k), np.int32)
+        n = self.lib.llmgpu_moe_routing(self.h, layer, out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                        out.size)
+        if n < 0:
+            self._err("moe_routing", n)
+        return out

@@ -305,6 +305,14 @@ class Model:
         self.dtype = dtype
         self.names = [n for n, _ in param_specs(cfg)]
         self.p = {n: np.asarray(a, dtype) for n, a in zip(self.names, params)}
+        # MoE: optional routing given from outside, forced_routes[sequence][layer] = int
+        # [T, k] expert indices, consumed one sequence per forward_backward call. Lets a
+        # test evaluate the restatement under exactly the routing another implementation
+        # chose (routing is a discrete decision that rounding upstream can flip near ties).
+        self.forced_routes = None
+        self._seq = 0
+        self._layer = 0
+        self._routes = None
 
     # ------------------------------------------------------------------ norms
     def _norm(self, x, g, b):
@@ -400,8 +408,11 @@ class Model:
         cfg = self.cfg
         probs = softmax(h @ gate)
         k = cfg.moe_top_k
-        # stable sort on -p keeps the lower index first among equal probabilities
-        idx = np.argsort(-probs, axis=1, kind="stable")[:, :k]
+        if self._routes is not None:
+            idx = np.asarray(self._routes[self._layer], np.int64)
+        else:
+            # stable sort on -p keeps the lower index first among equal probabilities
+            idx = np.argsort(-probs, axis=1, kind="stable")[:, :k]
         top = np.take_along_axis(probs, idx, 1)
         s = top.sum(1, keepdims=True)
         s = np.where(s < 1e-8, 1.0, s)
@@ -566,9 +577,14 @@ class Model:
         G = {n: np.zeros_like(a) for n, a in p.items()}
         xs, caches = [], []
         aux_total = 0.0
+        self._routes = None
+        if self.forced_routes is not None:
+            self._routes = self.forced_routes[self._seq]
+            self._seq += 1
         for l in range(cfg.n_layers):
             P = self._blk(l)
             xs.append(x)
+            self._layer = l
             if cfg.mamba:
                 x, c = self._mamba_fwd(x, P)
                 caches.append(c)
