@@ -6,10 +6,11 @@
 //   warps 4..7  : epilogue (tcgen05.ld from TMEM lanes 32*(warp%4).., fused epilogue, global stores)
 // Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap the MMAs of tile i+1.
 //
-// No TMA multicast is used anywhere: every CTA loads its own tiles.
+// Every CTA loads its own operand tiles with plain TMA loads.
 #include <cudaTypedefs.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -31,7 +32,7 @@ struct GemmCfg {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
     static constexpr uint32_t TMEM_COLS = 2 * BN;
-    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 4 * 2 * 4096 + 256;
 };
 
 __device__ __forceinline__ void decode_tile(int t, int num_m, int num_n, int tiles_mn, int& m_blk,
@@ -213,10 +214,168 @@ __device__ __forceinline__ void epi_store(const GemmArgs& a, int row, int col0, 
     }
 }
 
+// ---------------------------------------------------------------------------- epilogue
+// Each epilogue warp owns 32 accumulator rows (TMEM lanes) and moves a tile out in chunks of
+// 32 columns. With TMA outputs (args.tma_epi) a chunk goes registers -> a swizzled 32x32
+// box in shared memory -> one bulk tensor store (or reduce-add), so every global write is a
+// full, coalesced line; inputs of the epilogue (residual, stored pre-activation) come in
+// through TMA loads into the same box. Two 4 KB boxes per warp alternate so the store of one
+// chunk overlaps the next. Outputs whose strides a tensor map cannot describe take the
+// per-thread row stores of epi_store.
+constexpr int kEpiSlotBytes = 4096;
+constexpr int kEpiStageBytes = 4 * 2 * kEpiSlotBytes;
+
+// byte offset of 16-byte chunk `ch` of row r in a box of 128-byte rows (fp32, 128-byte
+// swizzle: chunk ^= row % 8) or 64-byte rows (bf16, 64-byte swizzle: chunk ^= (row / 2) % 4)
+__device__ __forceinline__ uint32_t box_off_f32(int r, int ch) {
+    return (uint32_t)(r * 128 + ((ch ^ (r & 7)) << 4));
+}
+__device__ __forceinline__ uint32_t box_off_bf16(int r, int ch) {
+    return (uint32_t)(r * 64 + ((ch ^ ((r >> 1) & 3)) << 4));
+}
+__device__ __forceinline__ void box_put_f32(uint8_t* box, int r, const float* v) {
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch)
+        *reinterpret_cast<float4*>(box + box_off_f32(r, ch)) =
+            make_float4(v[4 * ch], v[4 * ch + 1], v[4 * ch + 2], v[4 * ch + 3]);
+}
+__device__ __forceinline__ void box_put_bf16(uint8_t* box, int r, const float* v) {
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch)
+        *reinterpret_cast<uint4*>(box + box_off_bf16(r, ch)) =
+            make_uint4(pack_bf16x2(v[8 * ch], v[8 * ch + 1]), pack_bf16x2(v[8 * ch + 2], v[8 * ch + 3]),
+                       pack_bf16x2(v[8 * ch + 4], v[8 * ch + 5]),
+                       pack_bf16x2(v[8 * ch + 6], v[8 * ch + 7]));
+}
+
+struct EpiWarp {
+    uint8_t* stage;   // this warp's two boxes
+    uint64_t* bar;    // completion of this warp's input loads
+    uint32_t phase;
+    int slot;
+};
+
+// One accumulator tile of one warp: rows [row0, row0+32), columns [n0, n0+NCOLS), TMEM
+// columns from tbase. `empty`: the tile had no k-blocks (writes zeros).
+template <int NCOLS>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorMap* tmO,
+                                              const CUtensorMap* tmX, uint32_t tbase, bool empty,
+                                              int row0, int n0, int split, int g, int lane,
+                                              EpiWarp& w) {
+#pragma unroll 1
+    for (int c = 0; c < NCOLS / 32; ++c) {
+        uint32_t r[32];
+        if (!empty) {
+            tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), r);
+            tmem_ld_wait();
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = 0u;
+        }
+        const int col0 = n0 + c * 32;
+        if (row0 >= a.M || col0 >= a.N) continue;  // uniform across the warp
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (!a.tma_epi) {
+            const long long obase = (a.grp_mode == kGroupK) ? g * a.out_grp_stride : 0;
+            if (row0 + lane < a.M) epi_store(a, row0 + lane, col0, split, obase, v);
+            continue;
+        }
+        uint8_t* box = w.stage + w.slot * kEpiSlotBytes;
+        if (lane == 0) bulk_wait_group_read<1>();  // this box's previous store has read it
+        __syncwarp();
+        if (a.epi == kEpiResidF32 || a.epi == kEpiDGeluBF16) {
+            if (lane == 0) {
+                mbar_arrive_expect_tx(w.bar, a.epi == kEpiResidF32 ? 4096u : 2048u);
+                tma_load_3d(box, tmX, w.bar, col0, row0, 0);
+            }
+            mbar_wait_bounded(w.bar, w.phase, a.err, kDevTimeoutFull);
+            w.phase ^= 1u;
+        }
+        int x = col0, z = 0;
+        bool reduce = false;
+        switch (a.epi) {
+            case kEpiStoreBF16:
+                box_put_bf16(box, lane, v);
+                break;
+            case kEpiStoreF32:
+                box_put_f32(box, lane, v);
+                if (a.grp_mode == kGroupK) {
+                    z = g;
+                } else if (a.col_group != a.N) {
+                    z = col0 / a.col_group;
+                    x = col0 - z * a.col_group;
+                }
+                reduce = a.accumulate != 0;
+                break;
+            case kEpiSplitPartial:
+                box_put_f32(box, lane, v);
+                z = split;
+                break;
+            case kEpiResidF32:
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) {
+                    float4* p = reinterpret_cast<float4*>(box + box_off_f32(lane, ch));
+                    float4 q = *p;
+                    q.x += v[4 * ch];
+                    q.y += v[4 * ch + 1];
+                    q.z += v[4 * ch + 2];
+                    q.w += v[4 * ch + 3];
+                    *p = q;
+                }
+                break;
+            case kEpiGeluBF16: {
+                box_put_bf16(box, lane, v);  // pre-activation -> aux
+                float gv[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) gv[j] = gelu_tanh(v[j]);
+                box_put_bf16(box + 2048, lane, gv);
+                break;
+            }
+            case kEpiDGeluBF16: {
+                float dv[32];
+#pragma unroll
+                for (int ch = 0; ch < 4; ++ch) {
+                    const uint4 p = *reinterpret_cast<const uint4*>(box + box_off_bf16(lane, ch));
+                    const uint32_t h[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        dv[8 * ch + 2 * k] = v[8 * ch + 2 * k] * gelu_tanh_grad(bf16_lo(h[k]));
+                        dv[8 * ch + 2 * k + 1] = v[8 * ch + 2 * k + 1] * gelu_tanh_grad(bf16_hi(h[k]));
+                    }
+                }
+                box_put_bf16(box + 2048, lane, dv);
+                break;
+            }
+            default:
+                break;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            if (a.epi == kEpiGeluBF16) {
+                tma_store_3d(tmX, box, col0, row0, 0);
+                tma_store_3d(tmO, box + 2048, col0, row0, 0);
+            } else if (a.epi == kEpiDGeluBF16) {
+                tma_store_3d(tmO, box + 2048, col0, row0, 0);
+            } else if (reduce) {
+                tma_reduce_add_3d(tmO, box, x, row0, z);
+            } else {
+                tma_store_3d(tmO, box, x, row0, z);
+            }
+            bulk_commit_group();
+        }
+        w.slot ^= 1;
+    }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmO,
+                        const __grid_constant__ CUtensorMap tmX, const GemmArgs args) {
     using Cfg = GemmCfg<BN>;
     constexpr int STAGES = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -224,11 +383,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint8_t* smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+    uint8_t* sEpi = smem + STAGES * Cfg::STAGE_BYTES;  // 2 boxes per epilogue warp
+    uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes);
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;
     uint64_t* acc_empty = acc_full + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    uint64_t* epi_bar = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + 4);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -249,6 +410,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(&acc_full[i], 1);
             mbar_init(&acc_empty[i], 128);
         }
+        for (int i = 0; i < 4; ++i) mbar_init(&epi_bar[i], 1);
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -396,6 +558,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     } else if (warp >= 4) {
         // ---------------- epilogue warpgroup
         const int q = warp - 4;
+        EpiWarp ew{sEpi + q * 2 * kEpiSlotBytes, &epi_bar[q], 0u, 0};
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
@@ -404,42 +567,264 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                            g, kb0, kb1))
                 continue;
             const int m0 = m_blk * BM, n0 = n_blk * BN;
-            const bool empty = kb1 <= kb0;
-            const long long obase = (args.grp_mode == kGroupK) ? g * args.out_grp_stride : 0;
             if (!mbar_wait_bounded(&acc_full[acc], acc_phase, args.err, kDevTimeoutAcc)) break;
             tc_fence_after();
-            const int row = m0 + q * 32 + lane;
             const uint32_t tbase =
                 tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(q * 32) << 16);
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                if (!empty) {
-                    tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), r);
-                    tmem_ld_wait();
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) r[j] = 0u;
-                }
-                const int col0 = n0 + c * 32;
-                if (row < M && col0 < N) {
-                    float v[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-                    epi_store(args, row, col0, split, obase, v);
-                }
-            }
+            epilogue_tile<BN>(args, &tmO, &tmX, tbase, kb1 <= kb0, m0 + q * 32, n0, split, g,
+                              lane, ew);
             tc_fence_before();
             mbar_arrive(&acc_empty[acc]);
             acc ^= 1;
             if (acc == 0) acc_phase ^= 1u;
         }
+        if (lane == 0) bulk_wait_group_all();  // stores complete before the CTA exits
     }
 
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+}
+
+// ---------------------------------------------------------------------------- CTA pairs
+// 256 x 256 output tiles on a cluster of two CTAs (two SMs) sharing each tcgen05 MMA
+// (cta_group::2). Per k-block each CTA stages its 128 rows of A and its 128 rows (N) of B,
+// so an SM streams 32 KB per 128x256x64 of MMA work instead of 48 KB, and six stages fit.
+// Each CTA holds rows [128*rank, 128*rank+128) of the tile in its own TMEM (two 256-column
+// accumulators) and runs its own epilogue. The leader CTA (rank 0) issues every MMA; its
+// commits arrive on the stage / accumulator barriers of both CTAs; both CTAs' loads count
+// their bytes on the leader's stage barrier; the follower's epilogue arrives remotely on
+// the leader's accumulator-free barrier.
+struct PairCfg {
+    static constexpr int BMP = 256;
+    static constexpr int BN = 256;
+    static constexpr int BNH = 128;
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BNH * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = 6;
+    static constexpr uint32_t TMEM_COLS = 2 * BN;
+    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + kEpiStageBytes + 256;
+};
+
+// Bytes one CTA of a pair loads per k-block (A rows from am, B rows from bn); boxes wholly
+// past M or N are not loaded (their rows or columns are discarded by the epilogue).
+__device__ __forceinline__ uint32_t pair_stage_bytes(const GemmArgs& a, int am, int bn) {
+    uint32_t bytes = 0;
+    if (!a.a_mn_major)
+        bytes += (am < a.M) ? (uint32_t)PairCfg::A_BYTES : 0u;
+    else
+        bytes += 8192u * ((am < a.M ? 1u : 0u) + (am + 64 < a.M ? 1u : 0u));
+    if (!a.b_mn_major)
+        bytes += (bn < a.N) ? (uint32_t)PairCfg::B_BYTES : 0u;
+    else
+        bytes += 8192u * ((bn < a.N ? 1u : 0u) + (bn + 64 < a.N ? 1u : 0u));
+    return bytes;
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                          const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ CUtensorMap tmO,
+                          const __grid_constant__ CUtensorMap tmX, const GemmArgs args) {
+    using Cfg = PairCfg;
+    constexpr int STAGES = Cfg::STAGES;
+    constexpr int BN = Cfg::BN;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_u32 = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+    uint8_t* sEpi = smem + STAGES * Cfg::STAGE_BYTES;  // 2 boxes per epilogue warp
+    uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes);
+    uint64_t* empty = full + STAGES;
+    uint64_t* acc_full = empty + STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* epi_bar = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + 4);
+
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int M = args.M, N = args.N, K = args.K;
+    const int num_m = (M + Cfg::BMP - 1) / Cfg::BMP;
+    const int num_n = (N + BN - 1) / BN;
+    const int kblocks = (K + BK - 1) / BK;
+    const int tiles_mn = num_m * num_n;
+    const int total = tiles_mn * args.splits;
+    const int cid = blockIdx.x >> 1;
+    const int nclusters = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 2 * 128);  // the epilogue threads of both CTAs
+        }
+        for (int i = 0; i < 4; ++i) mbar_init(&epi_bar[i], 1);
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    __shared__ int s_grp[kMaxGemmGroups + 1];
+    if (args.grp_mode != kGroupNone)
+        for (int i = threadIdx.x; i <= args.groups; i += blockDim.x) s_grp[i] = args.grp[i];
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // barriers of both CTAs initialised before any remote use
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer (both CTAs)
+            const uint32_t full_leader = mapa_shared(smem_u32(&full[0]), 0);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int t = cid; t < total && ok; t += nclusters) {
+                int m_blk, n_blk, split, g, kb0, kb1;
+                tile_work(args, s_grp, t, num_m, num_n, tiles_mn, kblocks, m_blk, n_blk, split, g,
+                          kb0, kb1);
+                const int m0 = m_blk * Cfg::BMP, n0 = n_blk * BN;
+                const int am = m0 + 128 * (int)rank, bn = n0 + Cfg::BNH * (int)rank;
+                const uint32_t all_bytes = leader ? pair_stage_bytes(args, m0, n0) +
+                                                        pair_stage_bytes(args, m0 + 128, n0 + Cfg::BNH)
+                                                  : 0u;
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait_bounded_cluster(&empty[stage], phase ^ 1u, args.err,
+                                                   kDevTimeoutEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_arrive_expect_tx(&full[stage], all_bytes);
+                    const uint32_t fb = full_leader + 8u * (uint32_t)stage;
+                    const int k0 = kb * BK;
+                    uint8_t* a = sA + stage * Cfg::A_BYTES;
+                    uint8_t* b = sB + stage * Cfg::B_BYTES;
+                    if (!args.a_mn_major) {
+                        if (am < M) tma_load_2d_pair(a, &tmA, fb, k0, am);
+                    } else {
+                        if (am < M) tma_load_2d_pair(a, &tmA, fb, am, k0);
+                        if (am + 64 < M) tma_load_2d_pair(a + 8192, &tmA, fb, am + 64, k0);
+                    }
+                    if (!args.b_mn_major) {
+                        if (bn < N) tma_load_2d_pair(b, &tmB, fb, k0, bn);
+                    } else {
+                        if (bn < N) tma_load_2d_pair(b, &tmB, fb, bn, k0);
+                        if (bn + 64 < N) tma_load_2d_pair(b + 8192, &tmB, fb, bn + 64, k0);
+                    }
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) spin_ns(100000);  // error path: let copies in flight land first
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            // ---------------- MMA issuer (leader only)
+            const uint32_t idesc = make_idesc_bf16(Cfg::BMP, BN, args.a_mn_major, args.b_mn_major);
+            const uint32_t acc_full_peer = mapa_shared(smem_u32(&acc_full[0]), 1);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int t = cid; t < total && ok; t += nclusters) {
+                int m_blk, n_blk, split, g, kb0, kb1;
+                tile_work(args, s_grp, t, num_m, num_n, tiles_mn, kblocks, m_blk, n_blk, split, g,
+                          kb0, kb1);
+                if (!mbar_wait_bounded_cluster(&acc_empty[acc], acc_phase ^ 1u, args.err,
+                                               kDevTimeoutAccFree)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait_bounded_cluster(&full[stage], phase, args.err,
+                                                   kDevTimeoutFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sA + stage * Cfg::A_BYTES);
+                    const uint32_t b_addr = smem_u32(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint64_t ad =
+                            args.a_mn_major ? make_sw128_desc(a_addr + kk * 2048, 8192, 1024)
+                                            : make_sw128_desc(a_addr + kk * 32, 16, 1024);
+                        const uint64_t bd =
+                            args.b_mn_major ? make_sw128_desc(b_addr + kk * 2048, 8192, 1024)
+                                            : make_sw128_desc(b_addr + kk * 32, 16, 1024);
+                        umma_bf16_pair(d, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+                    }
+                    umma_commit_pair(&empty[stage], 0x3);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                if (kb1 > kb0) {
+                    umma_commit_pair(&acc_full[acc], 0x3);
+                } else {  // empty group: both epilogues write zeros
+                    mbar_arrive(&acc_full[acc]);
+                    mbar_arrive_cluster(acc_full_peer + 8u * (uint32_t)acc);
+                }
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+        }
+    } else if (warp >= 4) {
+        // ---------------- epilogue warpgroup (both CTAs)
+        const int q = warp - 4;
+        const uint32_t acc_empty_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
+        EpiWarp ew{sEpi + q * 2 * kEpiSlotBytes, &epi_bar[q], 0u, 0};
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = cid; t < total; t += nclusters) {
+            int m_blk, n_blk, split, g, kb0, kb1;
+            tile_work(args, s_grp, t, num_m, num_n, tiles_mn, kblocks, m_blk, n_blk, split, g,
+                      kb0, kb1);
+            const int m0 = m_blk * Cfg::BMP + 128 * (int)rank, n0 = n_blk * BN;
+            if (!mbar_wait_bounded_cluster(&acc_full[acc], acc_phase, args.err, kDevTimeoutAcc))
+                break;
+            tc_fence_after();
+            const uint32_t tbase =
+                tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(q * 32) << 16);
+            epilogue_tile<BN>(args, &tmO, &tmX, tbase, kb1 <= kb0, m0 + q * 32, n0, split, g,
+                              lane, ew);
+            tc_fence_before();
+            if (leader)
+                mbar_arrive(&acc_empty[acc]);
+            else
+                mbar_arrive_cluster(acc_empty_leader + 8u * (uint32_t)acc);
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1u;
+        }
+        if (lane == 0) bulk_wait_group_all();  // stores complete before the CTA exits
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // neither CTA leaves while the other may still touch its memory
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
 }
 
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N,
@@ -522,6 +907,71 @@ int make_tmap_bf16(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t ou
     return r == CUDA_SUCCESS ? 0 : -4;
 }
 
+// 3-D tensor map of 32x32x1 boxes over an epilogue output or input: dims {x, y, z} with
+// row stride `ys` and plane stride `zs` in bytes; fp32 boxes use the 128-byte swizzle, bf16
+// boxes the 64-byte swizzle (the layouts box_off_f32 / box_off_bf16 write).
+int make_tmap_box(CUtensorMap* tm, const void* ptr, bool f32, uint64_t x, uint64_t y, uint64_t z,
+                  uint64_t ys, uint64_t zs) {
+    auto enc = get_encode_fn();
+    if (!enc) return -1;
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || (ys & 15) != 0 || (zs & 15) != 0)
+        return -2;
+    cuuint64_t dims[3] = {x, y, z};
+    cuuint64_t strides[2] = {ys, zs};
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(tm, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                     const_cast<void*>(ptr), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -4;
+}
+
+// Output (and epilogue input) tensor maps for the TMA epilogue; returns false when a stride
+// or base address cannot be described (the per-thread store path is used then).
+bool plan_tma_epilogue(GemmPlan* plan, const GemmArgs& a) {
+    if (a.scalar_store) return false;
+    const bool f32 = (a.epi == kEpiStoreF32 || a.epi == kEpiResidF32 || a.epi == kEpiSplitPartial);
+    const uint64_t elt = f32 ? 4 : 2;
+    const uint64_t ys = (uint64_t)a.ldo * elt;
+    uint64_t x = (uint64_t)a.N, z = 1, zs = ys * (uint64_t)a.M;
+    if (a.epi == kEpiStoreF32) {
+        if (a.grp_mode == kGroupK) {
+            z = (uint64_t)a.groups;
+            zs = (uint64_t)a.out_grp_stride * 4;
+        } else if (a.col_group != a.N) {
+            x = (uint64_t)a.col_group;
+            z = (uint64_t)(a.N / a.col_group);
+            zs = (uint64_t)a.group_stride * 4;
+        }
+    } else if (a.epi == kEpiSplitPartial) {
+        z = (uint64_t)a.splits;
+        zs = (uint64_t)a.M * (uint64_t)a.N * 4;  // planes [split][M][N], ldo == N
+        if (a.ldo != a.N) return false;
+    }
+    zs = (zs + 15) & ~(uint64_t)15;  // a single plane: any aligned stride
+    if (z > 1 && ((a.epi == kEpiStoreF32 && ((a.grp_mode == kGroupK ? a.out_grp_stride
+                                                                     : a.group_stride) * 4) % 16) ||
+                  (a.epi == kEpiSplitPartial && ((uint64_t)a.M * a.N * 4) % 16)))
+        return false;
+    if (make_tmap_box(&plan->tmO, a.out, f32, x, (uint64_t)a.M, z, ys, zs)) return false;
+    if (a.epi == kEpiResidF32) {
+        const uint64_t rs = (uint64_t)a.ldr * 4;
+        if (make_tmap_box(&plan->tmX, a.resid, true, (uint64_t)a.N, (uint64_t)a.M, 1, rs,
+                          (rs * a.M + 15) & ~(uint64_t)15))
+            return false;
+    } else if (a.epi == kEpiGeluBF16 || a.epi == kEpiDGeluBF16) {
+        const uint64_t xs = (uint64_t)a.ld_aux * 2;
+        if (make_tmap_box(&plan->tmX, a.aux, false, (uint64_t)a.N, (uint64_t)a.M, 1, xs,
+                          (xs * a.M + 15) & ~(uint64_t)15))
+            return false;
+    } else {
+        plan->tmX = plan->tmO;
+    }
+    return true;
+}
+
 template <int BN>
 int launch_bn(const GemmPlan& p, cudaStream_t stream) {
     static bool attr_set = false;
@@ -531,8 +981,66 @@ int launch_bn(const GemmPlan& p, cudaStream_t stream) {
             return -10;
         attr_set = true;
     }
-    gemm_bf16_tc_kernel<BN><<<p.grid, kGemmThreads, GemmCfg<BN>::SMEM, stream>>>(p.tmA, p.tmB,
-                                                                                p.args);
+    gemm_bf16_tc_kernel<BN><<<p.grid, kGemmThreads, GemmCfg<BN>::SMEM, stream>>>(
+        p.tmA, p.tmB, p.tmO, p.tmX, p.args);
+    return launch_status();
+}
+
+int pair_set_attr() {
+    static int rc = -1;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        rc = cudaFuncSetAttribute(gemm_bf16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)PairCfg::SMEM) == cudaSuccess
+                 ? 0
+                 : -10;
+    });
+    return rc;
+}
+
+// Clusters of two that can be resident at once (one CTA per SM).
+int pair_max_clusters(int num_sms) {
+    static int n = -1;
+    static std::once_flag once;
+    std::call_once(once, [num_sms] {
+        n = num_sms / 2;
+        if (pair_set_attr()) return;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
+        cfg.blockDim = dim3(kGemmThreads, 1, 1);
+        cfg.dynamicSmemBytes = PairCfg::SMEM;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int c = 0;
+        if (cudaOccupancyMaxActiveClusters(&c, gemm_bf16_pair_kernel, &cfg) == cudaSuccess && c > 0)
+            n = c < n ? c : n;
+        cudaGetLastError();
+    });
+    return n;
+}
+
+int launch_pair(const GemmPlan& p, cudaStream_t stream) {
+    if (pair_set_attr()) return -10;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.grid, 1, 1);
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = PairCfg::SMEM;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, gemm_bf16_pair_kernel, p.tmA, p.tmB, p.tmO, p.tmX, p.args) !=
+        cudaSuccess)
+        return launch_status();
     return launch_status();
 }
 
@@ -584,16 +1092,28 @@ int gemm_make_plan(GemmPlan* plan, const void* A, long long lda, int a_mn_major,
         if (reinterpret_cast<uintptr_t>(a.out) & 15) return -8;
     }
     const int num_m = (M + BM - 1) / BM;
+    const bool pair_ok = a.grp_mode != kGroupRows;  // a pair tile spans 256 rows of one group
     int bn = bn_hint;
-    if (bn != 64 && bn != 128 && bn != 256) {
-        // pick the tile width with the smallest estimated makespan
+    if (bn == kGemmPairTile && !pair_ok) return -44;
+    if (bn != 64 && bn != 128 && bn != 256 && bn != kGemmPairTile) {
+        // pick the tile with the smallest estimated makespan; a CTA pair streams a third
+        // less operand data per MMA than one CTA with a 128x256 tile, and runs about
+        // 1.6x faster per SM
         double best = 1e30;
-        const int cands[3] = {256, 128, 64};
-        for (int i = 0; i < 3; ++i) {
-            int c = cands[i];
-            long long tiles = (long long)num_m * ((N + c - 1) / c) * a.splits;
-            long long waves = (tiles + num_sms - 1) / num_sms;
-            double cost = (double)waves * (c + 48);
+        const int cands[4] = {kGemmPairTile, 256, 128, 64};
+        for (int i = pair_ok ? 0 : 1; i < 4; ++i) {
+            const int c = cands[i];
+            double cost;
+            if (c == kGemmPairTile) {
+                const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256) * a.splits;
+                const int slots = pair_max_clusters(num_sms);
+                const long long waves = (tiles + slots - 1) / slots;
+                cost = (double)waves * (256 + 48) / 1.6;
+            } else {
+                const long long tiles = (long long)num_m * ((N + c - 1) / c) * a.splits;
+                const long long waves = (tiles + num_sms - 1) / num_sms;
+                cost = (double)waves * (c + 48);
+            }
             if (cost < best - 1e-9) {
                 best = cost;
                 bn = c;
@@ -601,6 +1121,9 @@ int gemm_make_plan(GemmPlan* plan, const void* A, long long lda, int a_mn_major,
         }
     }
     plan->bn = bn;
+    a.tma_epi = 0;
+    if (std::getenv("LLMGPU_GEMM_DIRECT_EPILOGUE") == nullptr) a.tma_epi = plan_tma_epilogue(plan, a) ? 1 : 0;
+    if (!a.tma_epi) plan->tmO = plan->tmX = CUtensorMap{};
     plan->args = a;
     int rc;
     if (!a_mn_major)
@@ -612,11 +1135,20 @@ int gemm_make_plan(GemmPlan* plan, const void* A, long long lda, int a_mn_major,
     const uint64_t b_rows = (a.grp_mode == kGroupRows)
                                 ? (uint64_t)a.groups * (uint64_t)a.b_grp_rows
                                 : (uint64_t)(b_mn_major ? K : N);
+    // a CTA of a pair stages 128 of the tile's 256 B rows
+    const uint32_t b_box = (bn == kGemmPairTile) ? (uint32_t)PairCfg::BNH : (uint32_t)bn;
     if (!b_mn_major)
-        rc = make_tmap_bf16(&plan->tmB, B, (uint64_t)K, b_rows, (uint64_t)ldb, BK, (uint32_t)bn);
+        rc = make_tmap_bf16(&plan->tmB, B, (uint64_t)K, b_rows, (uint64_t)ldb, BK, b_box);
     else
         rc = make_tmap_bf16(&plan->tmB, B, (uint64_t)N, b_rows, (uint64_t)ldb, 64, BK);
     if (rc) return -30 + rc;
+    if (bn == kGemmPairTile) {
+        const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256) * a.splits;
+        const int slots = pair_max_clusters(num_sms);
+        plan->grid = 2 * (int)(tiles < slots ? tiles : slots);
+        plan->smem_bytes = PairCfg::SMEM;
+        return 0;
+    }
     long long tiles = (long long)num_m * ((N + bn - 1) / bn) * a.splits;
     plan->grid = (int)(tiles < num_sms ? tiles : num_sms);
     plan->smem_bytes = bn == 256 ? GemmCfg<256>::SMEM : (bn == 128 ? GemmCfg<128>::SMEM : GemmCfg<64>::SMEM);
@@ -631,6 +1163,8 @@ int gemm_run(const GemmPlan& p, cudaStream_t stream) {
             return launch_bn<128>(p, stream);
         case 64:
             return launch_bn<64>(p, stream);
+        case kGemmPairTile:
+            return launch_pair(p, stream);
         default:
             return -12;
     }

@@ -42,6 +42,7 @@ struct GemmArgs {
     long long ld_aux;
     int splits;            // >=1; kEpiSplitPartial writes `splits` partial planes
     int scalar_store;      // set by the planner when the output is not 16-byte aligned
+    int tma_epi;           // set by the planner: outputs (and epilogue inputs) go through TMA
     int* err;              // device error word
     // Grouped (per-expert) products. `grp` is a device table of groups+1 ascending row
     // offsets, each a multiple of 128 (entry `groups` = rows in use), written by an earlier
@@ -62,14 +63,17 @@ struct GemmArgs {
 enum GemmGroupMode : int { kGroupNone = 0, kGroupRows = 1, kGroupK = 2 };
 constexpr int kMaxGemmGroups = 64;
 constexpr int kGemmRowAlign = 128;  // group offsets are multiples of the tile height
+constexpr int kGemmPairTile = 512;  // plan tile code: 256x256 tiles on a cluster of two CTAs
 
 // Precomputed launch: tensor maps + args + tile config. Encoding tensor maps
 // costs host time, so the model builds one GemmPlan per call site at setup.
 struct GemmPlan {
     CUtensorMap tmA;
     CUtensorMap tmB;
+    CUtensorMap tmO;       // output boxes of 32x32 (3-D: column groups, splits or groups)
+    CUtensorMap tmX;       // epilogue input / second output (residual or pre-activation)
     GemmArgs args;
-    int bn;                // 64, 128 or 256
+    int bn;                // 64, 128, 256, or kGemmPairTile (256x256 on a CTA pair)
     int grid;
     size_t smem_bytes;
 };

@@ -26,8 +26,9 @@ def _rel(x, y):
 
 
 @pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
-@pytest.mark.parametrize("bn", [64, 128, 256])
-@pytest.mark.parametrize("M,N,K", [(256, 512, 192), (200, 100, 70), (128, 64, 64)])
+@pytest.mark.parametrize("bn", [64, 128, 256, 512])  # 512: 256x256 tiles on a CTA pair
+@pytest.mark.parametrize("M,N,K", [(256, 512, 192), (200, 100, 70), (128, 64, 64),
+                                   (520, 300, 136), (1024, 768, 512)])
 def test_gemm_majors_tiles(cuda, a_mn, b_mn, bn, M, N, K):
     from llmgpu import ops
     g = torch.Generator().manual_seed(M * 7 + N * 3 + K + 11 * bn + 2 * a_mn + b_mn)
@@ -48,7 +49,8 @@ def test_gemm_majors_tiles(cuda, a_mn, b_mn, bn, M, N, K):
     assert _rel(got, ref) < 1e-4, _rel(got, ref)
 
 
-def test_gemm_epilogues(cuda):
+@pytest.mark.parametrize("bn", [0, 512])  # planner's choice, CTA pair
+def test_gemm_epilogues(cuda, bn):
     from llmgpu import ops
     g = torch.Generator().manual_seed(5)
     M, N, K = 384, 320, 256
@@ -56,20 +58,20 @@ def test_gemm_epilogues(cuda):
     b = _mk((K, N), g, 0.5).to(cuda)          # MN-major B, like x @ W
     ref = a.float() @ b.float()
     # bf16 store
-    o = ops.gemm(a, b, M, N, K, b_mn=True, epi=ops.EPI_BF16)
+    o = ops.gemm(a, b, M, N, K, b_mn=True, bn=bn, epi=ops.EPI_BF16)
     assert _rel(o, ref) < 8e-3
     # residual add
     r = torch.randn(M, N, device=cuda)
-    o = ops.gemm(a, b, M, N, K, b_mn=True, epi=ops.EPI_RESID, resid=r, ldr=N)
+    o = ops.gemm(a, b, M, N, K, b_mn=True, bn=bn, epi=ops.EPI_RESID, resid=r, ldr=N)
     assert _rel(o, ref + r) < 1e-5
     # accumulate
     base = torch.randn(M, N, device=cuda)
     o = base.clone()
-    ops.gemm(a, b, M, N, K, b_mn=True, epi=ops.EPI_F32, out=o, accumulate=True)
+    ops.gemm(a, b, M, N, K, b_mn=True, bn=bn, epi=ops.EPI_F32, out=o, accumulate=True)
     assert _rel(o, ref + base) < 1e-5
     # gelu + stored pre-activation
     h = torch.zeros(M, N, dtype=torch.bfloat16, device=cuda)
-    o = ops.gemm(a, b, M, N, K, b_mn=True, epi=ops.EPI_GELU, aux=h, ld_aux=N)
+    o = ops.gemm(a, b, M, N, K, b_mn=True, bn=bn, epi=ops.EPI_GELU, aux=h, ld_aux=N)
     gelu = 0.5 * ref * (1 + torch.tanh(0.7978845608 * (ref + 0.044715 * ref ** 3)))
     assert _rel(h, ref) < 8e-3
     assert _rel(o, gelu) < 8e-3
@@ -77,11 +79,12 @@ def test_gemm_epilogues(cuda):
     hv = h.float()
     th = torch.tanh(0.7978845608 * (hv + 0.044715 * hv ** 3))
     dg = 0.5 * (1 + th) + 0.5 * hv * (1 - th * th) * 0.7978845608 * (1 + 3 * 0.044715 * hv * hv)
-    o = ops.gemm(a, b, M, N, K, b_mn=True, epi=ops.EPI_DGELU, aux=h, ld_aux=N)
+    o = ops.gemm(a, b, M, N, K, b_mn=True, bn=bn, epi=ops.EPI_DGELU, aux=h, ld_aux=N)
     assert _rel(o, ref * dg) < 8e-3
 
 
-def test_gemm_splitk_grouped(cuda):
+@pytest.mark.parametrize("bn", [0, 512])
+def test_gemm_splitk_grouped(cuda, bn):
     """Weight-gradient shape: X^T dY with K = tokens, split over K, written into
     three adjacent [C, C] parameter gradients (Wq|Wk|Wv layout)."""
     from llmgpu import ops
@@ -92,19 +95,20 @@ def test_gemm_splitk_grouped(cuda):
     ref = x.float().t() @ dy.float()     # [C, 3C]
     out = torch.zeros(3, C, C, device=cuda)
     ops.gemm(x, dy, C, 3 * C, T, a_mn=True, b_mn=True, epi=ops.EPI_F32, out=out, ldo=C,
-             splits=4, col_group=C, group_stride=C * C)
+             splits=4, col_group=C, group_stride=C * C, bn=bn)
     want = torch.stack([ref[:, i * C:(i + 1) * C] for i in range(3)])
     assert _rel(out, want) < 1e-5
 
 
-def test_gemm_large_persistent(cuda):
-    """More tiles than SMs: exercises the persistent tile loop and the
-    double-buffered accumulator hand-off."""
+@pytest.mark.parametrize("bn", [256, 512])
+def test_gemm_large_persistent(cuda, bn):
+    """More tiles than SMs (or SM pairs): exercises the persistent tile loop and the
+    double-buffered accumulator hand-off (across the two CTAs of a pair for 512)."""
     from llmgpu import ops
     g = torch.Generator().manual_seed(3)
-    M, N, K = 2048, 2304, 768
+    M, N, K = 8192, 2304, 768
     a = _mk((M, K), g).to(cuda)
     b = _mk((N, K), g).to(cuda)
-    o = ops.gemm(a, b, M, N, K, epi=ops.EPI_F32)
+    o = ops.gemm(a, b, M, N, K, epi=ops.EPI_F32, bn=bn)
     ref = a.float() @ b.float().t()
     assert _rel(o, ref) < 1e-4
