@@ -553,9 +553,14 @@ void set_smem(K kernel, int bytes) {
 }  // namespace
 
 int attention_forward(const bf16* qkv, bf16* out, float* lse, int B, int T, int H, int hd,
-                      const float2* rope, cudaStream_t s) {
+                      const float2* rope, cudaStream_t s, int* err) {
     const float scale = 1.0f / sqrtf((float)hd);
     dim3 grid((T + BLK - 1) / BLK, H, B);
+    if (hd == 64 && !rope) {
+        CUtensorMap tm;
+        if (attention_qkv_tmap(&tm, qkv, B, T, H * hd)) return -2;
+        return attention_forward_tc(tm, out, lse, B, T, H, hd, err, s);
+    }
     if (hd == 64) {
         const int smem = 5 * BLK * 64 * 2;
         static bool set = false;
@@ -567,6 +572,37 @@ int attention_forward(const bf16* qkv, bf16* out, float* lse, int B, int T, int 
     } else {
         return -1;
     }
+    return launch_status();
+}
+
+namespace {
+__global__ void rope_qk_kernel(bf16* __restrict__ qkv, int T, int C, int hd, long long pairs,
+                               const float2* __restrict__ tab, int inverse) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= pairs) return;
+    const int half = C / 2;
+    const long long row = i / half;
+    const int pc = (int)(i - row * half);       // pair index within the C columns
+    const int t = (int)(row % T);
+    const int j = pc % (hd / 2);                // pair within the head
+    const float2 cs = tab[(long long)t * (hd / 2) + j];
+    const float sn = inverse ? -cs.y : cs.y;
+    __nv_bfloat162* base = reinterpret_cast<__nv_bfloat162*>(qkv + row * 3LL * C) + pc;
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {      // q, then k
+        __nv_bfloat162* w = base + part * half;
+        const float2 v = __bfloat1622float2(*w);
+        *w = __floats2bfloat162_rn(v.x * cs.x - v.y * sn, v.x * sn + v.y * cs.x);
+    }
+}
+}  // namespace
+
+int rope_qk_inplace(bf16* qkv, int B, int T, int H, int hd, const float2* rope, int inverse,
+                    cudaStream_t s) {
+    if (!rope || (hd & 1)) return -1;
+    const int C = H * hd;
+    const long long pairs = (long long)B * T * (C / 2);
+    rope_qk_kernel<<<(int)((pairs + 255) / 256), 256, 0, s>>>(qkv, T, C, hd, pairs, rope, inverse);
     return launch_status();
 }
 

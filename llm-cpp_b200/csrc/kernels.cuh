@@ -1,6 +1,7 @@
 // Launchers of the memory-bound and attention kernels of the training step.
 // All launchers are asynchronous on `stream` and return 0 or a negative status.
 #pragma once
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -62,8 +63,19 @@ int mean_reduce(const float* v, int n, float* out, cudaStream_t s);
 // src/attention.cpp:35-102 / src/flash_attention.cpp:88-123.
 // rope (nullable): [T][hd/2] (cos, sin) table; when given, Q and K are rotated per head as
 // they are loaded and dQ/dK are rotated back before they are stored.
+// head_dim 64 without a fused rope runs on the tcgen05 kernel (attention_tc.cu); err
+// (nullable) receives the device error code of a timed-out wait.
 int attention_forward(const bf16* qkv, bf16* out, float* lse, int B, int T, int H, int hd,
-                      const float2* rope, cudaStream_t s);
+                      const float2* rope, cudaStream_t s, int* err = nullptr);
+// tcgen05 forward (head_dim 64) on a tensor map made by attention_qkv_tmap
+int attention_qkv_tmap(CUtensorMap* tm, const bf16* qkv, int B, int T, int C);
+int attention_forward_tc(const CUtensorMap& tm, bf16* out, float* lse, int B, int T, int H, int hd,
+                         int* err, cudaStream_t s);
+// In-place RoPE of the q and k parts of qkv [B*T, 3C] (pairs 2j, 2j+1 of every head, table
+// [T][hd/2] of (cos, sin)); inverse != 0 applies the transposed rotation, which maps
+// gradients with respect to rotated q / k back to the unrotated ones.
+int rope_qk_inplace(bf16* qkv, int B, int T, int H, int hd, const float2* rope, int inverse,
+                    cudaStream_t s);
 // Backward: dqkv [B*T, 3C] bf16 from dout [B*T, C]; dvec [B, H, T] fp32 scratch.
 // src/attention.cpp:183-363.
 int attention_backward(const bf16* qkv, const bf16* out, const bf16* dout, const float* lse,

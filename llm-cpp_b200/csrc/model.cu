@@ -971,7 +971,12 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
         int rc = gemm(c, a.ln1, C, 0, c->wqkv16[l], 3 * C, 1, BT, 3 * C, C,
                       epi_args(kEpiStoreBF16, a.qkv, 3 * C));
         if (rc) return rc;
-        KC(attention_forward(a.qkv, a.att, a.lse, B, T, H, hd, c->rope, s));
+        if (c->rope && hd == 64) {  // rotate q, k in place; the tcgen05 kernel takes them as is
+            KC(rope_qk_inplace(a.qkv, B, T, H, hd, c->rope, 0, s));
+            KC(attention_forward(a.qkv, a.att, a.lse, B, T, H, hd, nullptr, s, c->d_err));
+        } else {
+            KC(attention_forward(a.qkv, a.att, a.lse, B, T, H, hd, c->rope, s, c->d_err));
+        }
         GemmArgs r = epi_args(kEpiResidF32, a.y, C);
         r.resid = a.x;
         r.ldr = C;
@@ -1105,8 +1110,14 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
         if ((rc = gemm(c, c->dy16, C, 0, c->wo16[l], C, 0, BT, C, C,
                        epi_args(kEpiStoreBF16, c->datt, C))))
             return rc;
-        KC(attention_backward(a.qkv, a.att, c->datt, a.lse, c->dvec, c->dqkv, B, T, H, hd,
-                              c->rope, s));
+        if (c->rope && hd == 64) {  // q, k were rotated in place: rotate dq, dk back
+            KC(attention_backward(a.qkv, a.att, c->datt, a.lse, c->dvec, c->dqkv, B, T, H, hd,
+                                  nullptr, s));
+            KC(rope_qk_inplace(c->dqkv, B, T, H, hd, c->rope, 1, s));
+        } else {
+            KC(attention_backward(a.qkv, a.att, c->datt, a.lse, c->dvec, c->dqkv, B, T, H, hd,
+                                  c->rope, s));
+        }
         GemmArgs wq = epi_args(kEpiStoreF32, gp(b.Wq), C);
         wq.accumulate = acc;
         wq.col_group = C;

@@ -98,7 +98,8 @@ def _attn_ref(qkv, B, T, H, hd):
 
 
 @pytest.mark.parametrize("B,T,H,hd", [(2, 128, 4, 32), (1, 200, 2, 64), (2, 64, 12, 64),
-                                      (1, 1024, 2, 64), (3, 33, 1, 32)])
+                                      (1, 1024, 2, 64), (3, 33, 1, 32), (3, 300, 3, 64),
+                                      (2, 1024, 12, 64)])
 def test_attention_forward_backward(cuda, B, T, H, hd):
     from llmgpu import ops
     g = torch.Generator().manual_seed(T * H + hd)
