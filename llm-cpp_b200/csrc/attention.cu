@@ -608,10 +608,15 @@ int rope_qk_inplace(bf16* qkv, int B, int T, int H, int hd, const float2* rope, 
 
 int attention_backward(const bf16* qkv, const bf16* out, const bf16* dout, const float* lse,
                        float* dvec, bf16* dqkv, int B, int T, int H, int hd, const float2* rope,
-                       cudaStream_t s) {
+                       cudaStream_t s, int* err) {
     const float scale = 1.0f / sqrtf((float)hd);
     const long long n = (long long)B * T * H;
     attn_dvec_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(out, dout, dvec, B, T, H, hd);
+    if (hd == 64 && !rope && (T % 4) == 0) {
+        const int rc = launch_status();
+        if (rc) return rc;
+        return attention_backward_tc(qkv, dout, lse, dvec, dqkv, B, T, H, hd, err, s);
+    }
     dim3 grid((T + BLK - 1) / BLK, H, B);
     if (hd == 64) {
         const int smem1 = 6 * BLK * 64 * 2 + 4 * BLK * 4;

@@ -284,6 +284,429 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
+// ============================================================================ backward
+// Two deterministic kernels (no atomics), head_dim 64, 320 threads each:
+//   warp 0     TMA producer        warp 1     TMEM allocator + MMA issuer
+//   warps 2-9  elementwise: warp w handles TMEM lane quarter w % 4 (one row per thread) and
+//              column half (w - 2) / 4 of every 128-wide score tile, so two warps share each
+//              SM sub-partition.
+// With P = exp(S * scale - lse) (rows: queries) and D = rowsum(dO o O):
+//   dS = P o (dP - D), dP = dO V^T, dV = P^T dO, dK = scale dS^T Q, dQ = scale dS K.
+// dK/dV kernel (one 128-key tile per CTA, over the query tiles that see it): S^T = K Q^T and
+// dP^T = V dO^T in TMEM; P^T and dS^T (bf16) written back to TMEM feed dV += P^T dO and
+// dK += dS^T Q as A-from-TMEM MMAs. dQ kernel (one query tile per CTA, over key tiles 0..i):
+// S, dP as in the forward, dQ += dS K. The next tile's S / dP MMAs run while the elementwise
+// warps work on the current one; the inputs stream through 3-stage TMA rings.
+// TMEM (512 columns): S [0,128), dP [128,256), accumulators from 256, bf16 operands after.
+constexpr int kBwdThreads = 320;
+constexpr int kBwdStages = 3;
+constexpr uint32_t kBwdTmem = 512;
+constexpr float kLog2ef = 1.4426950408889634f;
+
+struct BwdSmem {
+    // two resident tiles (K, V or Q, dO), then kBwdStages stages of two streamed tiles
+    // (+ 512-byte lse and D vectors for the dK/dV kernel)
+    static constexpr int FIX0 = 0, FIX1 = kTile;
+    static constexpr int STAGE0 = 2 * kTile;
+    static constexpr int STAGE_BYTES = 2 * kTile + 1024;
+    static constexpr int BAR = STAGE0 + kBwdStages * STAGE_BYTES;
+    static constexpr int TOTAL = BAR + 256;
+};
+constexpr size_t kBwdSmemBytes = 1024 + BwdSmem::TOTAL;
+
+__device__ __forceinline__ void store_row64_bf16(bf16* dst, const uint32_t (&r)[32], float mul) {
+    uint4* o4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        o4[i] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * i]) * mul, __uint_as_float(r[8 * i + 1]) * mul),
+                           pack_bf16x2(__uint_as_float(r[8 * i + 2]) * mul, __uint_as_float(r[8 * i + 3]) * mul),
+                           pack_bf16x2(__uint_as_float(r[8 * i + 4]) * mul, __uint_as_float(r[8 * i + 5]) * mul),
+                           pack_bf16x2(__uint_as_float(r[8 * i + 6]) * mul, __uint_as_float(r[8 * i + 7]) * mul));
+}
+
+// ---------------------------------------------------------------- dK / dV
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv,
+                            const __grid_constant__ CUtensorMap tm_do,
+                            const __grid_constant__ CUtensorMap tm_lse,
+                            const __grid_constant__ CUtensorMap tm_d, bf16* __restrict__ dqkv,
+                            int T, int H, float scale, int* __restrict__ err) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_u32 = smem_u32(smem_raw);
+    uint8_t* sm = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + BwdSmem::BAR);
+    uint64_t* kv_full = bar;
+    uint64_t* st_full = bar + 1;                  // [kBwdStages]
+    uint64_t* st_empty = st_full + kBwdStages;    // [kBwdStages]
+    uint64_t* s_full = st_empty + kBwdStages;
+    uint64_t* s_free = s_full + 1;
+    uint64_t* p_full = s_free + 1;
+    uint64_t* mm_done = p_full + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mm_done + 1);
+
+    const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int nqb = (T + kRows - 1) / kRows;
+    const int ns = nqb - kt;                      // query tiles kt..nqb-1 see these keys
+    const int C = H * kHD;
+    const int k0 = kt * kRows;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float scale_log2 = scale * kLog2ef;
+    constexpr uint32_t kColDV = 256, kColDK = 320, kColP = 384, kColDS = 448;
+
+    if (threadIdx.x == 0) {
+        mbar_init(kv_full, 1);
+        for (int s = 0; s < kBwdStages; ++s) {
+            mbar_init(&st_full[s], 1);
+            mbar_init(&st_empty[s], 1);
+        }
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 256);
+        mbar_init(p_full, 256);
+        mbar_init(mm_done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kBwdTmem);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    auto stage = [&](int s) { return sm + BwdSmem::STAGE0 + (s % kBwdStages) * BwdSmem::STAGE_BYTES; };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            bool ok = true;
+            mbar_arrive_expect_tx(kv_full, 2 * kTile);
+            tma_load_3d(sm + BwdSmem::FIX0, &tm_qkv, kv_full, C + h * kHD, k0, b);      // K
+            tma_load_3d(sm + BwdSmem::FIX1, &tm_qkv, kv_full, 2 * C + h * kHD, k0, b);  // V
+            for (int s = 0; s < ns && ok; ++s) {
+                const int q0 = (kt + s) * kRows;
+                if (!mbar_wait_bounded(&st_empty[s % kBwdStages], ((s / kBwdStages) & 1) ^ 1u, err,
+                                       kDevTimeoutEmpty)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* st = stage(s);
+                uint64_t* f = &st_full[s % kBwdStages];
+                mbar_arrive_expect_tx(f, 2 * kTile + 1024);
+                tma_load_3d(st, &tm_qkv, f, h * kHD, q0, b);                  // Q_i
+                tma_load_3d(st + kTile, &tm_do, f, h * kHD, q0, b);           // dO_i
+                tma_load_2d(st + 2 * kTile, &tm_lse, f, q0, b * H + h);       // lse_i
+                tma_load_2d(st + 2 * kTile + 512, &tm_d, f, q0, b * H + h);   // D_i
+            }
+            if (!ok) spin_ns(100000);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc_s = make_idesc_bf16(kRows, kRows, 0, 0);
+            const uint32_t idesc_acc = make_idesc_bf16(kRows, kHD, 0, 1);
+            const uint32_t k_addr = smem_u32(sm + BwdSmem::FIX0), v_addr = smem_u32(sm + BwdSmem::FIX1);
+            bool ok = mbar_wait_bounded(kv_full, 0, err, kDevTimeoutFull);
+            auto issue_sdp = [&](int s) -> bool {
+                if (!mbar_wait_bounded(&st_full[s % kBwdStages], (s / kBwdStages) & 1, err,
+                                       kDevTimeoutFull))
+                    return false;
+                tc_fence_after();
+                const uint32_t q_addr = smem_u32(stage(s)), do_addr = q_addr + kTile;
+#pragma unroll
+                for (int kk = 0; kk < kHD / 16; ++kk)  // S^T = K Q^T
+                    umma_bf16(tmem, make_sw128_desc(k_addr + kk * 32, 16, 1024),
+                              make_sw128_desc(q_addr + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+#pragma unroll
+                for (int kk = 0; kk < kHD / 16; ++kk)  // dP^T = V dO^T
+                    umma_bf16(tmem + 128, make_sw128_desc(v_addr + kk * 32, 16, 1024),
+                              make_sw128_desc(do_addr + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+                umma_commit(s_full);
+                return true;
+            };
+            if (ok) ok = issue_sdp(0);
+            for (int s = 0; s < ns && ok; ++s) {
+                if (s + 1 < ns) {
+                    if (!mbar_wait_bounded(s_free, s & 1, err, kDevTimeoutAccFree) ||
+                        !issue_sdp(s + 1)) {
+                        ok = false;
+                        break;
+                    }
+                }
+                if (!mbar_wait_bounded(p_full, s & 1, err, kDevTimeoutFull)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t q_addr = smem_u32(stage(s)), do_addr = q_addr + kTile;
+#pragma unroll
+                for (int kk = 0; kk < kRows / 16; ++kk) {  // dV += P^T dO ; dK += dS^T Q
+                    umma_bf16_ts(tmem + kColDV, tmem + kColP + kk * 8,
+                                 make_sw128_desc(do_addr + kk * 2048, 8192, 1024), idesc_acc,
+                                 (s > 0 || kk > 0) ? 1u : 0u);
+                    umma_bf16_ts(tmem + kColDK, tmem + kColDS + kk * 8,
+                                 make_sw128_desc(q_addr + kk * 2048, 8192, 1024), idesc_acc,
+                                 (s > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(mm_done);
+                umma_commit(&st_empty[s % kBwdStages]);
+            }
+        }
+    } else {
+        // ---------------- elementwise warps: thread = key row, 64 query columns
+        const int lq = warp & 3, half = (warp - 2) >> 2;
+        const int kr = lq * 32 + lane;
+        const int key = k0 + kr;
+        const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
+        bool ok = true;
+        for (int s = 0; s < ns && ok; ++s) {
+            const int q0 = (kt + s) * kRows + half * 64;
+            if (!warp_wait(s_full, s & 1, err, kDevTimeoutAcc) ||
+                !warp_wait(&st_full[s % kBwdStages], (s / kBwdStages) & 1, err, kDevTimeoutAcc)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t sv[64], dp[64];
+            tmem_ld_32x32b_x32(tmem + lane_base + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+            tmem_ld_32x32b_x32(tmem + lane_base + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+            tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
+            tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[32]));
+            tmem_ld_wait();
+            tc_fence_before();
+            mbar_arrive(s_free);
+            const float* lse = reinterpret_cast<const float*>(stage(s) + 2 * kTile) + half * 64;
+            const float* dv = lse + 128;
+#pragma unroll
+            for (int c4 = 0; c4 < 16; ++c4) {
+                const float4 l4 = reinterpret_cast<const float4*>(lse)[c4];
+                const float4 d4 = reinterpret_cast<const float4*>(dv)[c4];
+                const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dd[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int c = c4 * 4 + u, q = q0 + c;
+                    float p = ex2_approx(fmaf(__uint_as_float(sv[c]), scale_log2, -lv[u] * kLog2ef));
+                    if (q < key || q >= T) p = 0.f;
+                    sv[c] = __float_as_uint(p);
+                    dp[c] = __float_as_uint(p * (__uint_as_float(dp[c]) - dd[u]));
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                sv[i] = pack_bf16x2(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1]));
+                dp[i] = pack_bf16x2(__uint_as_float(dp[2 * i]), __uint_as_float(dp[2 * i + 1]));
+            }
+            if (s >= 1 && !warp_wait(mm_done, (s - 1) & 1, err, kDevTimeoutAcc)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            tmem_st_32x32b_x32(tmem + lane_base + kColP + half * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+            tmem_st_32x32b_x32(tmem + lane_base + kColDS + half * 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        if (ok && warp_wait(mm_done, (ns - 1) & 1, err, kDevTimeoutAcc)) {
+            tc_fence_after();
+            // column half 0 writes dV, half 1 writes scale * dK
+            const uint32_t col = half == 0 ? kColDV : kColDK;
+            bf16* dst = dqkv + ((long long)b * T + key) * 3LL * C + (half == 0 ? 2 * C : C) + h * kHD;
+#pragma unroll
+            for (int c = 0; c < kHD / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem + lane_base + col + c * 32, r);
+                tmem_ld_wait();
+                if (key < T) store_row64_bf16(dst + c * 32, r, half == 0 ? 1.f : scale);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, kBwdTmem);
+}
+
+// ---------------------------------------------------------------- dQ
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv,
+                          const __grid_constant__ CUtensorMap tm_do,
+                          const float* __restrict__ lse_g, const float* __restrict__ dvec,
+                          bf16* __restrict__ dqkv, int T, int H, float scale,
+                          int* __restrict__ err) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_u32 = smem_u32(smem_raw);
+    uint8_t* sm = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + BwdSmem::BAR);
+    uint64_t* qd_full = bar;
+    uint64_t* st_full = bar + 1;
+    uint64_t* st_empty = st_full + kBwdStages;
+    uint64_t* s_full = st_empty + kBwdStages;
+    uint64_t* s_free = s_full + 1;
+    uint64_t* p_full = s_free + 1;
+    uint64_t* mm_done = p_full + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mm_done + 1);
+
+    const int nqb = (T + kRows - 1) / kRows;
+    const int qt = nqb - 1 - (int)blockIdx.x;     // longest tiles first
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int ns = qt + 1;                        // key tiles 0..qt
+    const int C = H * kHD;
+    const int q0 = qt * kRows;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float scale_log2 = scale * kLog2ef;
+    constexpr uint32_t kColDQ = 256, kColDS = 320;
+
+    if (threadIdx.x == 0) {
+        mbar_init(qd_full, 1);
+        for (int s = 0; s < kBwdStages; ++s) {
+            mbar_init(&st_full[s], 1);
+            mbar_init(&st_empty[s], 1);
+        }
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 256);
+        mbar_init(p_full, 256);
+        mbar_init(mm_done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kBwdTmem);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    auto stage = [&](int s) { return sm + BwdSmem::STAGE0 + (s % kBwdStages) * BwdSmem::STAGE_BYTES; };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            bool ok = true;
+            mbar_arrive_expect_tx(qd_full, 2 * kTile);
+            tma_load_3d(sm + BwdSmem::FIX0, &tm_qkv, qd_full, h * kHD, q0, b);  // Q
+            tma_load_3d(sm + BwdSmem::FIX1, &tm_do, qd_full, h * kHD, q0, b);   // dO
+            for (int s = 0; s < ns && ok; ++s) {
+                if (!mbar_wait_bounded(&st_empty[s % kBwdStages], ((s / kBwdStages) & 1) ^ 1u, err,
+                                       kDevTimeoutEmpty)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* st = stage(s);
+                uint64_t* f = &st_full[s % kBwdStages];
+                mbar_arrive_expect_tx(f, 2 * kTile);
+                tma_load_3d(st, &tm_qkv, f, C + h * kHD, s * kRows, b);              // K_j
+                tma_load_3d(st + kTile, &tm_qkv, f, 2 * C + h * kHD, s * kRows, b);  // V_j
+            }
+            if (!ok) spin_ns(100000);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc_s = make_idesc_bf16(kRows, kRows, 0, 0);
+            const uint32_t idesc_acc = make_idesc_bf16(kRows, kHD, 0, 1);
+            const uint32_t q_addr = smem_u32(sm + BwdSmem::FIX0), do_addr = smem_u32(sm + BwdSmem::FIX1);
+            bool ok = mbar_wait_bounded(qd_full, 0, err, kDevTimeoutFull);
+            auto issue_sdp = [&](int s) -> bool {
+                if (!mbar_wait_bounded(&st_full[s % kBwdStages], (s / kBwdStages) & 1, err,
+                                       kDevTimeoutFull))
+                    return false;
+                tc_fence_after();
+                const uint32_t k_addr = smem_u32(stage(s)), v_addr = k_addr + kTile;
+#pragma unroll
+                for (int kk = 0; kk < kHD / 16; ++kk)  // S = Q K^T
+                    umma_bf16(tmem, make_sw128_desc(q_addr + kk * 32, 16, 1024),
+                              make_sw128_desc(k_addr + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+#pragma unroll
+                for (int kk = 0; kk < kHD / 16; ++kk)  // dP = dO V^T
+                    umma_bf16(tmem + 128, make_sw128_desc(do_addr + kk * 32, 16, 1024),
+                              make_sw128_desc(v_addr + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+                umma_commit(s_full);
+                return true;
+            };
+            if (ok) ok = issue_sdp(0);
+            for (int s = 0; s < ns && ok; ++s) {
+                if (s + 1 < ns) {
+                    if (!mbar_wait_bounded(s_free, s & 1, err, kDevTimeoutAccFree) ||
+                        !issue_sdp(s + 1)) {
+                        ok = false;
+                        break;
+                    }
+                }
+                if (!mbar_wait_bounded(p_full, s & 1, err, kDevTimeoutFull)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t k_addr = smem_u32(stage(s));
+#pragma unroll
+                for (int kk = 0; kk < kRows / 16; ++kk)  // dQ += dS K
+                    umma_bf16_ts(tmem + kColDQ, tmem + kColDS + kk * 8,
+                                 make_sw128_desc(k_addr + kk * 2048, 8192, 1024), idesc_acc,
+                                 (s > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(mm_done);
+                umma_commit(&st_empty[s % kBwdStages]);
+            }
+        }
+    } else {
+        // ---------------- elementwise warps: thread = query row, 64 key columns
+        const int lq = warp & 3, half = (warp - 2) >> 2;
+        const int qr = lq * 32 + lane;
+        const int q = q0 + qr;
+        const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
+        const long long li = ((long long)b * H + h) * T + q;
+        const float lse_l2 = q < T ? lse_g[li] * kLog2ef : 0.f;
+        const float dq_row = q < T ? dvec[li] : 0.f;
+        bool ok = true;
+        for (int s = 0; s < ns && ok; ++s) {
+            const int kc0 = s * kRows + half * 64;
+            if (!warp_wait(s_full, s & 1, err, kDevTimeoutAcc)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t sv[64], dp[64];
+            tmem_ld_32x32b_x32(tmem + lane_base + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+            tmem_ld_32x32b_x32(tmem + lane_base + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+            tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
+            tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[32]));
+            tmem_ld_wait();
+            tc_fence_before();
+            mbar_arrive(s_free);
+#pragma unroll
+            for (int c = 0; c < 64; ++c) {
+                float p = ex2_approx(fmaf(__uint_as_float(sv[c]), scale_log2, -lse_l2));
+                if (kc0 + c > q || q >= T) p = 0.f;
+                dp[c] = __float_as_uint(p * (__uint_as_float(dp[c]) - dq_row));
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                dp[i] = pack_bf16x2(__uint_as_float(dp[2 * i]), __uint_as_float(dp[2 * i + 1]));
+            if (s >= 1 && !warp_wait(mm_done, (s - 1) & 1, err, kDevTimeoutAcc)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            tmem_st_32x32b_x32(tmem + lane_base + kColDS + half * 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        if (ok && warp_wait(mm_done, (ns - 1) & 1, err, kDevTimeoutAcc) && half == 0) {
+            tc_fence_after();
+            bf16* dst = dqkv + ((long long)b * T + q) * 3LL * C + h * kHD;
+#pragma unroll
+            for (int c = 0; c < kHD / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem + lane_base + kColDQ + c * 32, r);
+                tmem_ld_wait();
+                if (q < T) store_row64_bf16(dst + c * 32, r, scale);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, kBwdTmem);
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -331,6 +754,70 @@ int attention_forward_tc(const CUtensorMap& tm, bf16* out, float* lse, int B, in
     const dim3 grid((T + kRows - 1) / kRows, H, B);
     attn_fwd_tc_kernel<<<grid, kThreads, kSmemBytes, s>>>(tm, out, lse, T, H,
                                                          1.4426950408889634f / sqrtf((float)hd), err);
+    return launch_status();
+}
+
+namespace {
+int encode_map(CUtensorMap* tm, CUtensorMapDataType dt, int rank, const void* ptr,
+               const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
+               CUtensorMapSwizzle sw) {
+    auto enc = encode_fn();
+    if (!enc) return -1;
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0) return -2;
+    for (int i = 0; i + 1 < rank; ++i)
+        if ((strides[i] & 15) != 0) return -2;
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(tm, dt, rank, const_cast<void*>(ptr), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -4;
+}
+}  // namespace
+
+int attention_backward_tc(const bf16* qkv, const bf16* dout, const float* lse, const float* dvec,
+                          bf16* dqkv, int B, int T, int H, int hd, int* err, cudaStream_t s) {
+    if (hd != kHD || B <= 0 || T <= 0 || H <= 0 || (T % 4) != 0) return -1;
+    const int C = H * hd;
+    CUtensorMap tq, tdo, tl, td;
+    if (attention_qkv_tmap(&tq, qkv, B, T, C)) return -2;
+    {
+        const cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)T, (cuuint64_t)B};
+        const cuuint64_t strides[2] = {(cuuint64_t)C * 2, (cuuint64_t)C * 2 * T};
+        const cuuint32_t box[3] = {kHD, kRows, 1};
+        if (encode_map(&tdo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dout, dims, strides, box,
+                       CU_TENSOR_MAP_SWIZZLE_128B))
+            return -2;
+    }
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)T, (cuuint64_t)B * H};
+        const cuuint64_t strides[1] = {(cuuint64_t)T * 4};
+        const cuuint32_t box[2] = {kRows, 1};
+        if (encode_map(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, lse, dims, strides, box,
+                       CU_TENSOR_MAP_SWIZZLE_NONE) ||
+            encode_map(&td, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dvec, dims, strides, box,
+                       CU_TENSOR_MAP_SWIZZLE_NONE))
+            return -2;
+    }
+    static int attr = -1;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        attr = (cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kBwdSmemBytes) == cudaSuccess &&
+                cudaFuncSetAttribute(attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kBwdSmemBytes) == cudaSuccess)
+                   ? 0
+                   : -3;
+    });
+    if (attr) return attr;
+    const float scale = 1.0f / sqrtf((float)hd);
+    const dim3 grid((T + kRows - 1) / kRows, H, B);
+    attn_bwd_dkdv_tc_kernel<<<grid, kBwdThreads, kBwdSmemBytes, s>>>(tq, tdo, tl, td, dqkv, T, H,
+                                                                     scale, err);
+    int rc = launch_status();
+    if (rc) return rc;
+    attn_bwd_dq_tc_kernel<<<grid, kBwdThreads, kBwdSmemBytes, s>>>(tq, tdo, lse, dvec, dqkv, T, H,
+                                                                   scale, err);
     return launch_status();
 }
 

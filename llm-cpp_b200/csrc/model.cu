@@ -1112,11 +1112,11 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
             return rc;
         if (c->rope && hd == 64) {  // q, k were rotated in place: rotate dq, dk back
             KC(attention_backward(a.qkv, a.att, c->datt, a.lse, c->dvec, c->dqkv, B, T, H, hd,
-                                  nullptr, s));
+                                  nullptr, s, c->d_err));
             KC(rope_qk_inplace(c->dqkv, B, T, H, hd, c->rope, 1, s));
         } else {
             KC(attention_backward(a.qkv, a.att, c->datt, a.lse, c->dvec, c->dqkv, B, T, H, hd,
-                                  c->rope, s));
+                                  c->rope, s, c->d_err));
         }
         GemmArgs wq = epi_args(kEpiStoreF32, gp(b.Wq), C);
         wq.accumulate = acc;
