@@ -31,7 +31,7 @@ extern "C" {
  *   splits > 1 (epi 1 only) splits K; `workspace` must hold splits*M*N floats.
  *   col_group/group_stride (epi 1): column n is written to
  *        out + (n / col_group) * group_stride + m * ldo + n % col_group.
- *   bn: tile width 64/128/256, 0 = automatic.
+ *   bn: tile width 64/128/256, 512 = 256x256 tiles on a CTA pair, 0 = automatic.
  *   err: device int that receives a nonzero code if a device-side wait timed out. */
 int llmgpu_op_gemm(const void* A, long long lda, int a_mn_major, const void* B, long long ldb,
                    int b_mn_major, int M, int N, int K, int epi, void* out, long long ldo,
@@ -126,6 +126,8 @@ int llmgpu_op_moe_dispatch(const int* idx, int B, int T, int E, int k, int* grp,
 
 /* Number of SMs the library sizes persistent grids for (device 0 of the caller). */
 int llmgpu_op_num_sms(void);
+/* CTA pairs (clusters of two SMs) the 256x256-tile GEMM keeps resident at once. */
+int llmgpu_op_gemm_pair_slots(void);
 
 #ifdef __cplusplus
 }

@@ -1155,6 +1155,8 @@ int gemm_make_plan(GemmPlan* plan, const void* A, long long lda, int a_mn_major,
     return 0;
 }
 
+int gemm_pair_slots(int num_sms) { return pair_max_clusters(num_sms); }
+
 int gemm_run(const GemmPlan& p, cudaStream_t stream) {
     switch (p.bn) {
         case 256:

@@ -87,6 +87,8 @@ int gemm_make_plan(GemmPlan* plan, const void* A, long long lda, int a_mn_major,
                    int bn_hint, int num_sms);
 // Launches a plan on a stream.
 int gemm_run(const GemmPlan& plan, cudaStream_t stream);
+// CTA pairs of the pair-tile kernel that can be resident at once.
+int gemm_pair_slots(int num_sms);
 
 // Reduces split-K partials [splits][M][N] (fp32) into the final output with the
 // same epilogue options as kEpiStoreF32 (accumulate, column grouping).

@@ -187,18 +187,23 @@ void reference_init(Ctx* c, std::vector<float>& host) {
     }
 }
 
+// Split-K factor of a weight-gradient GEMM (K = tokens) on 256x256 CTA-pair tiles. Cost in
+// units of one 64-deep k-block of a tile (about 0.4 us): the waves of (tile, split) work
+// units over the resident pairs, each with ~6 units of tile overhead, plus the split-K
+// reduction's memory traffic ((s + 1) fp32 planes of M x N at ~6 TB/s).
 int choose_splits(Ctx* c, int M, int N, int K) {
-    const int bn = N >= 256 ? 256 : 128;
-    const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+    const int slots = gemm_pair_slots(c->num_sms);
+    const double tiles = (double)((M + 255) / 256) * ((N + 255) / 256);
     const int kb = (K + 63) / 64;
     int best_s = 1;
     double best = 1e30;
     const int cand[6] = {1, 2, 3, 4, 6, 8};
     for (int i = 0; i < 6; ++i) {
         const int s = cand[i];
-        if (s > 1 && kb / s < 4) break;
-        const double waves = std::ceil((double)tiles * s / c->num_sms);
-        const double cost = waves * ((double)kb / s + 4.0) + (s > 1 ? 2.0 : 0.0);
+        if (s > 1 && kb / s < 8) break;
+        const double waves = std::ceil(tiles * s / slots);
+        const double reduce_us = s > 1 ? (double)(s + 1) * M * N * 4.0 / 6.0e6 : 0.0;
+        const double cost = waves * ((double)kb / s + 6.0) + reduce_us / 0.41;
         if (cost < best - 1e-9) {
             best = cost;
             best_s = s;

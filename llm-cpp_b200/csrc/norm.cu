@@ -107,13 +107,22 @@ __global__ void __launch_bounds__(256) norm_bwd_kernel(
         const float4* xr = reinterpret_cast<const float4*>(x + (long long)row * C);
         const float mu = mean[row], r = rstd[row];
         float s1 = 0.f, s2 = 0.f;
-        float4 d[MAXV], xv[MAXV];
+        float4 d[MAXV], xv[MAXV], rv[MAXV];
+        const float4* rin = reinterpret_cast<const float4*>(resid_in + (long long)row * C);
+        // every load of the row is issued before the reductions need the first of them
 #pragma unroll
         for (int i = 0; i < MAXV; ++i) {
             const int idx = lane + i * 32;
             if (idx < nv) {
                 d[i] = dyr[idx];
                 xv[i] = xr[idx];
+                rv[i] = resid_in ? rin[idx] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+            const int idx = lane + i * 32;
+            if (idx < nv) {
                 float4 g = g4[idx];
                 if (!rms) {
                     float gx = d[i].x * g.x, gy = d[i].y * g.y, gz = d[i].z * g.z,
@@ -131,7 +140,6 @@ __global__ void __launch_bounds__(256) norm_bwd_kernel(
         s2 = warp_sum(s2);
         const float m1 = s1 * invC, m2 = s2 * invC;
         const float coef = rms ? s2 * r * r * r * invC : 0.f;
-        const float4* rin = reinterpret_cast<const float4*>(resid_in + (long long)row * C);
         float4* o32 = reinterpret_cast<float4*>(dx_f32 + (long long)row * C);
         uint2* o16 = dx_bf16 ? reinterpret_cast<uint2*>(dx_bf16 + (long long)row * C) : nullptr;
 #pragma unroll
@@ -151,13 +159,10 @@ __global__ void __launch_bounds__(256) norm_bwd_kernel(
                     else
                         o[k] = dd[k] * gg[k] * r - xx[k] * coef;
                 }
-                if (resid_in) {
-                    float4 ri = rin[idx];
-                    o[0] += ri.x;
-                    o[1] += ri.y;
-                    o[2] += ri.z;
-                    o[3] += ri.w;
-                }
+                o[0] += rv[i].x;
+                o[1] += rv[i].y;
+                o[2] += rv[i].z;
+                o[3] += rv[i].w;
                 o32[idx] = make_float4(o[0], o[1], o[2], o[3]);
                 if (o16) o16[idx] = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
                 add4(sg + idx, dd[0] * xh[0], dd[1] * xh[1], dd[2] * xh[2], dd[3] * xh[3]);
@@ -210,17 +215,36 @@ __global__ void colsum_stage1(const bf16* __restrict__ a, long long lda, int row
     const int r1 = (int)((long long)(rg + 1) * rows / kColsumGroups);
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     const bool vec = (c0 + 8 <= C) && ((lda & 7) == 0);
-    for (int r = r0; r < r1; ++r) {
-        const bf16* p = a + (long long)r * lda + c0;
-        if (vec) {
-            uint4 u = *reinterpret_cast<const uint4*>(p);
-            uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    if (vec) {
+        // rows in batches of 8 with all 8 loads in flight, summed in row order
+        int r = r0;
+        for (; r + 8 <= r1; r += 8) {
+            uint4 u[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                u[j] = *reinterpret_cast<const uint4*>(a + (long long)(r + j) * lda + c0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t w[4] = {u[j].x, u[j].y, u[j].z, u[j].w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    acc[2 * k] += bf16_lo(w[k]);
+                    acc[2 * k + 1] += bf16_hi(w[k]);
+                }
+            }
+        }
+        for (; r < r1; ++r) {
+            const uint4 u = *reinterpret_cast<const uint4*>(a + (long long)r * lda + c0);
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 acc[2 * k] += bf16_lo(w[k]);
                 acc[2 * k + 1] += bf16_hi(w[k]);
             }
-        } else {
+        }
+    } else {
+        for (int r = r0; r < r1; ++r) {
+            const bf16* p = a + (long long)r * lda + c0;
             for (int k = 0; k < 8 && c0 + k < C; ++k) acc[k] += __bfloat162float(p[k]);
         }
     }
@@ -231,7 +255,13 @@ __global__ void colsum_stage2(const float* __restrict__ work, int C, float* out,
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= C) return;
     float acc = 0.f;
-    for (int g = 0; g < kColsumGroups; ++g) acc += work[(long long)g * C + c];
+    for (int g = 0; g < kColsumGroups; g += 8) {  // 8 loads in flight, summed in group order
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = work[(long long)(g + j) * C + c];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc += v[j];
+    }
     out[c] = accumulate ? out[c] + acc : acc;
 }
 

@@ -18,6 +18,8 @@ static int device_num_sms() {
 
 extern "C" int llmgpu_op_num_sms(void) { return device_num_sms(); }
 
+extern "C" int llmgpu_op_gemm_pair_slots(void) { return gemm_pair_slots(device_num_sms()); }
+
 extern "C" int llmgpu_op_gemm(const void* A, long long lda, int a_mn_major, const void* B,
                               long long ldb, int b_mn_major, int M, int N, int K, int epi,
                               void* out, long long ldo, int accumulate, const float* resid,

@@ -19,6 +19,8 @@ c_int, c_ll, c_vp, c_float, c_size_t = (ctypes.c_int, ctypes.c_longlong, ctypes.
 def _declare(lib):
     lib.llmgpu_op_num_sms.argtypes = []
     lib.llmgpu_op_num_sms.restype = c_int
+    lib.llmgpu_op_gemm_pair_slots.argtypes = []
+    lib.llmgpu_op_gemm_pair_slots.restype = c_int
     lib.llmgpu_op_gemm.argtypes = [c_vp, c_ll, c_int, c_vp, c_ll, c_int, c_int, c_int, c_int,
                                    c_int, c_vp, c_ll, c_int, c_vp, c_ll, c_vp, c_ll, c_int, c_vp,
                                    c_int, c_ll, c_int, c_vp, c_vp]
