@@ -52,7 +52,7 @@ int validate_bt(Ctx* c, int B, int T) {
 int enqueue_step(Ctx* c, int B, int T, int accumulate, bool do_step, int K) {
     c->plan_cursor = 0;
     c->prof_n = 0;
-    int rc = run_fwd_bwd(c, B, T, accumulate, true);
+    int rc = run_fwd_bwd(c, B, T, accumulate, true, do_step && c->world > 1);
     if (rc) return rc;
     if (do_step) rc = run_optimizer(c, K);
     return rc;

@@ -650,11 +650,34 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
         refresh_shadows(c);
     }
 
+    // gradient buckets: block l's contiguous parameter range, then the rest (embeddings, ln_f,
+    // untied head) as bucket L
+    {
+        std::vector<int64_t> start(c->L + 1, c->n_floats);
+        for (size_t i = 0; i < c->params.size(); ++i) {
+            const std::string& n = c->params[i].name;
+            if (n.compare(0, 3, "blk") == 0) {
+                const int l = std::atoi(n.c_str() + 3);
+                start[l] = std::min(start[l], c->params[i].offset);
+            }
+        }
+        c->buckets.resize(c->L + 1);
+        for (int l = 0; l < c->L; ++l) c->buckets[l] = {start[l], l + 1 < c->L ? start[l + 1] : c->n_floats};
+        c->buckets[c->L] = {0, start[0]};
+    }
     if (world > 1) {
+        if (cudaStreamCreateWithFlags(&c->comm, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c->ev_grad, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c->ev_comm, cudaEventDisableTiming) != cudaSuccess)
+            return fail(c, "stream creation failed");
         ncclUniqueId id;
         std::memcpy(&id, uid, sizeof(id));
         ncclComm_t comm;
-        ncclResult_t r = ncclCommInitRank(&comm, world, id, rank);
+        // NCCL's own CTA count by default; LLMGPU_NCCL_MAX_CTAS caps it (fewer CTAs leave more
+        // SMs to the backward the buckets overlap, but slow the last, unoverlapped bucket)
+        ncclConfig_t ncfg = NCCL_CONFIG_INITIALIZER;
+        if (const char* e = std::getenv("LLMGPU_NCCL_MAX_CTAS")) ncfg.maxCTAs = std::atoi(e);
+        ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &ncfg);
         if (r != ncclSuccess) return fail(c, std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
         c->nccl = comm;
     }
@@ -703,6 +726,9 @@ void ctx_destroy(Ctx* c) {
         if (e) cudaEventDestroy(e);
     if (c->stream) cudaStreamDestroy(c->stream);
     if (c->side) cudaStreamDestroy(c->side);
+    if (c->comm) cudaStreamDestroy(c->comm);
+    if (c->ev_grad) cudaEventDestroy(c->ev_grad);
+    if (c->ev_comm) cudaEventDestroy(c->ev_comm);
     delete c;
 }
 
@@ -936,7 +962,23 @@ int moe_backward_ffn(Ctx* c, int l, int B, int T, int acc) {
 
 }  // namespace
 
-int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
+// All-reduce (average over ranks) of gradient floats [begin, end) on the comm stream, after
+// everything enqueued so far on the main stream.
+int allreduce_bucket(Ctx* c, int64_t begin, int64_t end) {
+    if (end <= begin) return 0;
+    CK(cudaEventRecord(c->ev_grad, c->stream));
+    CK(cudaStreamWaitEvent(c->comm, c->ev_grad, 0));
+    ncclResult_t r = ncclAllReduce(c->g + begin, c->g + begin, (size_t)(end - begin), ncclFloat,
+                                   ncclAvg, reinterpret_cast<ncclComm_t>(c->nccl), c->comm);
+    if (r != ncclSuccess) {
+        c->err = std::string("ncclAllReduce: ") + ncclGetErrorString(r);
+        return LLMGPU_E_NCCL;
+    }
+    c->launches++;
+    return 0;
+}
+
+int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce) {
     const int C = c->C, F = c->F, H = c->H, hd = c->hd, L = c->L, V = c->V, Vp = c->Vp;
     const int BT = B * T;
     const int rms = c->cfg.use_rmsnorm;
@@ -1059,6 +1101,8 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
         auto& b = c->blocks[l];
         if (c->mamba) {
             if ((rc = mamba_backward_layer(c, l, B, T, acc))) return rc;
+            if (reduce && (rc = allreduce_bucket(c, c->buckets[l].first, c->buckets[l].second)))
+                return rc;
             continue;
         }
         // ---- FFN  (src/transformer.cpp:120-183)
@@ -1138,12 +1182,20 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward) {
         KC(reduce_partials(c->partial, nparts, C, gp(b.ln1g), rms ? nullptr : gp(b.ln1b),
                            (l > 0 && c->blocks[l - 1].b2 >= 0) ? gp(c->blocks[l - 1].b2) : nullptr,
                            acc, s));
+        // every gradient of block l is final now (its b2 was reduced in block l+1's pass)
+        if (reduce && (rc = allreduce_bucket(c, c->buckets[l].first, c->buckets[l].second)))
+            return rc;
     }
     // embedding scatter (src/model.cpp:314-322)
     CK(cudaStreamWaitEvent(s, c->ev_keys, 0));
     // c->dy is free once the last block's backward is done: piece partials go there
     KC(embed_backward(c->d_keys, c->dres, gp(c->i_wte), gp(c->i_wpe), B, T, C, acc, c->dy, s));
     mark(c, 3);
+    if (reduce) {
+        // the embeddings / ln_f / head range, then hand the comm stream back to the step
+        if ((rc = allreduce_bucket(c, c->buckets[L].first, c->buckets[L].second))) return rc;
+        CK(cudaEventRecord(c->ev_comm, c->comm));
+    }
     return 0;
 }
 
@@ -1153,18 +1205,12 @@ int run_optimizer(Ctx* c, int K) {
     // prepare_step_scalars before the step is launched), so that a captured step graph
     // reads the current values at every replay.
     CK(cudaMemcpyAsync(c->d_hp, c->h_hp, sizeof(float) * 16, cudaMemcpyHostToDevice, s));
+    // data parallel: the gradient buckets were all-reduced (averaged) on the comm stream
+    // during the last micro-batch's backward
+    if (c->world > 1) CK(cudaStreamWaitEvent(s, c->ev_comm, 0));
     if (K > 1) {
         // train_step_accum averages the accumulated gradients (src/trainer.cpp:148-150)
         KC(scale_inplace(c->g, c->n_floats, c->d_hp + 8, s));
-    }
-    if (c->world > 1) {
-        ncclResult_t r = ncclAllReduce(c->g, c->g, (size_t)c->n_floats, ncclFloat, ncclAvg,
-                                       reinterpret_cast<ncclComm_t>(c->nccl), s);
-        if (r != ncclSuccess) {
-            c->err = std::string("ncclAllReduce: ") + ncclGetErrorString(r);
-            return LLMGPU_E_NCCL;
-        }
-        c->launches++;
     }
     mark(c, 4);
     KC(grad_norm_partials(c->g, c->n_floats, c->d_normpart, c->d_nonfinite, grad_norm_blocks(), s));

@@ -85,6 +85,11 @@ struct Ctx {
     int C = 0, V = 0, Vp = 0, H = 0, hd = 0, F = 0, L = 0;
     cudaStream_t stream = nullptr, side = nullptr;
     cudaEvent_t ev_keys = nullptr;
+    // data parallel: gradient buckets (one per block, then the embeddings/head range) are
+    // all-reduced on `comm` as soon as the backward has finished them
+    cudaStream_t comm = nullptr;
+    cudaEvent_t ev_grad = nullptr, ev_comm = nullptr;
+    std::vector<std::pair<int64_t, int64_t>> buckets;  // [begin, end) floats; index l = block l
     cudaEvent_t ev[6] = {};
     void* nccl = nullptr;  // ncclComm_t
 
@@ -195,9 +200,11 @@ struct Ctx {
 Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, int world,
                 const void* uid, std::string* err);
 void ctx_destroy(Ctx* c);
-// one micro-batch forward+backward on device tokens (ctx->d_tokens) with accumulate flag
-int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward);
-// optimizer: (scale by 1/K) -> allreduce -> norm/clip -> AdamW
+// one micro-batch forward+backward on device tokens (ctx->d_tokens) with accumulate flag;
+// `reduce` (data parallel, last micro-batch) all-reduces each gradient bucket on the comm
+// stream as soon as the backward has finished it
+int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce = false);
+// optimizer: (wait for the bucket all-reduces) -> scale by 1/K -> norm/clip -> AdamW
 int run_optimizer(Ctx* c, int K);
 int ctx_sync_check(Ctx* c);
 void prepare_step_scalars(Ctx* c, int K);
