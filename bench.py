@@ -46,6 +46,46 @@ def algorithmic_flops_per_token(cfg=CFG, T=T):
     return 6 * n_mm + 6 * L * T * C, n_mm
 
 
+# The other configurations of the path, for `--config` (reported in DESIGN.md; the default
+# line is GPT-2-small): model config, sequences per GPU, sequence length, workload text.
+OTHER_CONFIGS = {
+    "tiny": (dict(vocab_size=256, n_layers=4, n_heads=4, n_embd=128, block_size=128), 8, 128,
+             "tiny char-level GPT (4L, n_embd 128, 4 heads, GELU FFN 512, vocab 256), seq 128, 8 seq/GPU"),
+    "llama": (dict(vocab_size=32000, n_layers=24, n_heads=16, n_embd=1024, block_size=2048,
+                   weight_tying=False, use_rmsnorm=True, ffn_swiglu=True, ffn_hidden=2816,
+                   rope_qk=True), 4, 2048,
+              "Llama-style (24L, n_embd 1024, 16 heads, SwiGLU 2816, RoPE on Q/K, RMSNorm, untied, "
+              "vocab 32000), seq 2048, 4 seq/GPU"),
+    "mamba": (dict(vocab_size=32000, n_layers=12, n_heads=1, n_embd=768, block_size=2048,
+                   use_rmsnorm=True, use_mamba=True, d_inner=1536, d_state=16, dt_rank=48,
+                   conv_kernel=4), 4, 2048,
+              "Mamba (12 blocks, E 768, D 1536, N 16, R 48, K 4, RMSNorm, tied, vocab 32000), "
+              "seq 2048, 4 seq/GPU"),
+    "moe": (dict(vocab_size=32000, n_layers=12, n_heads=12, n_embd=768, block_size=1024,
+                 moe_experts=8, moe_top_k=2, moe_aux_coef=0.01), 8, 1024,
+            "MoE (12L, n_embd 768, 12 heads, 8 GELU experts of 3072, top-2, aux 0.01, tied, "
+            "vocab 32000), seq 1024, 8 seq/GPU"),
+}
+
+
+def flops_per_token(cfg, T):
+    """F_tok = 6*N_mm + (attention) 6*L*T*C, with N_mm the matmul weights one token passes
+    through (the active experts for MoE, the head counted even when tied)."""
+    C, L, V = cfg["n_embd"], cfg["n_layers"], cfg["vocab_size"]
+    if cfg.get("use_mamba"):
+        D, N, R = cfg["d_inner"], cfg["d_state"], cfg["dt_rank"]
+        n_mm = L * (2 * D * C + (R + 2 * N) * D + D * R + C * D) + C * V
+        return 6 * n_mm, n_mm
+    if cfg.get("moe_experts"):
+        k = cfg.get("moe_top_k", 2)
+        n_mm = L * (4 * C * C + k * 2 * C * 4 * C + C * cfg["moe_experts"]) + C * V
+    elif cfg.get("ffn_swiglu"):
+        n_mm = L * (4 * C * C + 3 * C * cfg["ffn_hidden"]) + C * V
+    else:
+        n_mm = L * (4 * C * C + 2 * C * 4 * C) + C * V
+    return 6 * n_mm + 6 * L * T * C, n_mm
+
+
 def zipf_tokens(vocab, n, seed, s=1.1):
     import numpy as np
     rng = np.random.default_rng(seed)
@@ -205,6 +245,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", default="gpt2-small", choices=["gpt2-small"] + sorted(OTHER_CONFIGS),
+                    help="workload (the headline line is gpt2-small)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -226,12 +268,15 @@ def main():
         dist.broadcast_object_list(obj, src=0)
         uid = obj[0]
     from llmgpu.trainer import Trainer, make_config
-    cfg = make_config(**CFG)
+    model_cfg, B, T, workload = (CFG, globals()["B"], globals()["T"], None)
+    if args.config != "gpt2-small":
+        model_cfg, B, T, workload = OTHER_CONFIGS[args.config]
+    cfg = make_config(**model_cfg)
     tr = Trainer(cfg, B, T, rank=rank, world=world, uid=uid)
     tr.set_adamw(**HP)
     tr.set_train(grad_clip=1.0)
     K, W = args.steps, args.warmup
-    toks = zipf_tokens(CFG["vocab_size"], (W + 2 * K) * B * T, 1234 + rank).reshape(-1, B, T)
+    toks = zipf_tokens(model_cfg["vocab_size"], (W + 2 * K) * B * T, 1234 + rank).reshape(-1, B, T)
     stream = torch.cuda.ExternalStream(tr.stream())
 
     def barrier():
@@ -288,7 +333,7 @@ def main():
     tr.set_profile(False)
 
     peak, peak_sus, hbm, peak_kind = peaks()
-    f_tok, n_mm = algorithmic_flops_per_token()
+    f_tok, n_mm = flops_per_token(model_cfg, T)
     tokens_step = world * B * T
     value = tokens_step / (ms_dev / 1e3)
     e2e = tokens_step / (ms_e2e / 1e3)
@@ -299,7 +344,10 @@ def main():
             "metric": "train_tokens_per_sec", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_dev,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic", "config": workload_config(world),
+            "dtype": "bf16", "data": "synthetic",
+            "config": workload_config(world) if workload is None else
+                      {"workload": workload, "global_batch": B * world, "seq_len": T,
+                       "parallelism": f"dp{world}", "tokens": "Zipf(1.1) synthetic ids, seeded"},
             "mfu": {"value": mfu, "peak_tflops": peak, "peak": peak_kind,
                     "flops_per_token": f_tok, "n_mm": n_mm},
             "e2e": {"value": e2e, "unit": "tokens/s", "ms_per_step": ms_e2e,
@@ -316,7 +364,7 @@ def main():
             "clocks": clocks,
             "loss_last": losses[-1],
         }
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and workload is None:
             try:
                 secs = run_port_cpu(PORT_T)
                 line["cpu_baseline"] = {
