@@ -79,6 +79,23 @@ __global__ void dt_fwd_kernel(const float* __restrict__ xp, long long ldx,
     }
 }
 
+// ---------------------------------------------------------------- scan staging
+// A block owns CPB = kWarps * 32 / L consecutive channels of one sequence. Time runs in
+// chunks of kScanChunk steps; the block loads a chunk's per-(step, channel) inputs and its
+// per-(step, state) B and C into shared memory with coalesced row segments, double
+// buffered: the loads of the next chunk are issued into registers before the recurrence of
+// the current one runs, so the serial part of the scan never waits on global memory.
+template <int L>
+struct ScanTile {
+    static constexpr int kThreads = kWarps * 32;
+    static constexpr int kCPW = 32 / L;                 // channels per warp
+    static constexpr int kCPB = kWarps * kCPW;          // channels per block
+    static constexpr int kTC = kScanChunk;              // steps per chunk
+    static constexpr int kEPT = kTC * kCPB / kThreads;  // (step, channel) slots per thread
+    static_assert(kTC * kCPB % kThreads == 0, "chunk tile must split evenly over the block");
+    static_assert(kTC * L <= kThreads, "one (step, state) slot per thread at most");
+};
+
 // ---------------------------------------------------------------- scan forward
 template <int L>
 __global__ void __launch_bounds__(kWarps * 32) scan_fwd_kernel(
@@ -86,36 +103,77 @@ __global__ void __launch_bounds__(kWarps * 32) scan_fwd_kernel(
     long long ldx, const float* __restrict__ alog, const float* __restrict__ dskip,
     const bf16* __restrict__ proj, long long ldp, float* __restrict__ y32,
     bf16* __restrict__ gated, float* __restrict__ hchk, int T, int D, int N, int R) {
-    constexpr int CPW = 32 / L;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n = lane % L, ci = lane / L;
-    const int d = (blockIdx.x * kWarps + warp) * CPW + ci;
+    using G = ScanTile<L>;
+    constexpr int CPB = G::kCPB, TC = G::kTC, EPT = G::kEPT, NT = G::kThreads;
+    __shared__ float sDt[2][TC][CPB], sU[2][TC][CPB], sZ[2][TC][CPB];
+    __shared__ float sB[2][TC][L], sC[2][TC][L];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n = lane % L, c = warp * G::kCPW + lane / L;
+    const int d0 = blockIdx.x * CPB, d = d0 + c;
     const int b = blockIdx.y;
     const bool chan = d < D;
     const bool active = chan && n < N;
     const float A = active ? alog[(long long)d * N + n] : 0.f;
     const float Ds = chan ? dskip[d] : 0.f;
-    const int nch = (T + kScanChunk - 1) / kScanChunk;
-    float h = 0.f;
-    for (int t = 0; t < T; ++t) {
-        const long long row = (long long)b * T + t;
-        if ((t % kScanChunk) == 0 && active)
-            hchk[(((long long)b * nch + t / kScanChunk) * D + d) * N + n] = h;
-        const float rv = chan ? raw[row * D + d] : 0.f;
-        const float dt = clamp_dt(softplus_f(rv));
-        const float uu = chan ? u[row * D + d] : 0.f;
-        const float Bv = active ? xp[row * ldx + R + n] : 0.f;
-        const float Cv = active ? xp[row * ldx + R + N + n] : 0.f;
-        const float a = __expf(A * dt);
-        h = a * h + Bv * uu * dt;
-        float c = Cv * h;
+    const int nch = (T + TC - 1) / TC;
+
+    float pr[EPT], pu[EPT], pz[EPT], pb = 0.f, pc = 0.f;
+    auto fetch = [&](int t0) {
 #pragma unroll
-        for (int o = L / 2; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
-        if (n == 0 && chan) {
-            const float yv = c + Ds * uu;
-            y32[row * D + d] = yv;
-            const float xz = __bfloat162float(proj[row * ldp + d]);
-            gated[row * D + d] = __float2bfloat16_rn(yv * silu_f(xz));
+        for (int e = 0; e < EPT; ++e) {
+            const int idx = tid + e * NT, i = idx / CPB, dd = d0 + idx % CPB;
+            const bool ok = t0 + i < T && dd < D;
+            const long long row = (long long)b * T + t0 + i;
+            pr[e] = ok ? raw[row * D + dd] : 0.f;
+            pu[e] = ok ? u[row * D + dd] : 0.f;
+            pz[e] = ok ? __bfloat162float(proj[row * ldp + dd]) : 0.f;
+        }
+        if (tid < TC * L) {
+            const int i = tid / L, nn = tid % L;
+            const bool ok = t0 + i < T && nn < N;
+            const long long row = (long long)b * T + t0 + i;
+            pb = ok ? xp[row * ldx + R + nn] : 0.f;
+            pc = ok ? xp[row * ldx + R + N + nn] : 0.f;
+        }
+    };
+    auto stage = [&](int buf, int t0) {
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) {
+            const int idx = tid + e * NT, i = idx / CPB, cc = idx % CPB;
+            const bool ok = t0 + i < T && d0 + cc < D;
+            sDt[buf][i][cc] = ok ? clamp_dt(softplus_f(pr[e])) : 0.f;
+            sU[buf][i][cc] = pu[e];
+            sZ[buf][i][cc] = pz[e];
+        }
+        if (tid < TC * L) {
+            sB[buf][tid / L][tid % L] = pb;
+            sC[buf][tid / L][tid % L] = pc;
+        }
+    };
+
+    fetch(0);
+    float h = 0.f;
+    for (int k = 0; k < nch; ++k) {
+        const int buf = k & 1, t0 = k * TC;
+        stage(buf, t0);
+        __syncthreads();
+        if (k + 1 < nch) fetch(t0 + TC);
+        if (active) hchk[(((long long)b * nch + k) * D + d) * N + n] = h;
+#pragma unroll
+        for (int i = 0; i < TC; ++i) {
+            const float dt = sDt[buf][i][c], uu = sU[buf][i][c];
+            const float Bv = sB[buf][i][n], Cv = sC[buf][i][n];
+            const float a = __expf(A * dt);
+            h = a * h + Bv * uu * dt;
+            float cs = Cv * h;
+#pragma unroll
+            for (int o = L / 2; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
+            if (n == 0 && chan && t0 + i < T) {
+                const long long row = (long long)b * T + t0 + i;
+                const float yv = cs + Ds * uu;
+                y32[row * D + d] = yv;
+                gated[row * D + d] = __float2bfloat16_rn(yv * silu_f(sZ[buf][i][c]));
+            }
         }
     }
 }
@@ -129,57 +187,93 @@ __global__ void __launch_bounds__(kWarps * 32) scan_bwd_kernel(
     const float* __restrict__ dgated, const float* __restrict__ hchk, float* __restrict__ du,
     float* __restrict__ ddt, bf16* __restrict__ dproj, float* __restrict__ dbc_part,
     float* __restrict__ da_part, float* __restrict__ dd_part, int T, int D, int N, int R) {
-    constexpr int CPW = 32 / L;
-    constexpr int LC = kScanChunk;
-    __shared__ float sB[kWarps][LC][L];
-    __shared__ float sC[kWarps][LC][L];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n = lane % L, ci = lane / L;
-    const int d = (blockIdx.x * kWarps + warp) * CPW + ci;
+    using G = ScanTile<L>;
+    constexpr int CPB = G::kCPB, TC = G::kTC, EPT = G::kEPT, NT = G::kThreads;
+    __shared__ float sDt[2][TC][CPB], sU[2][TC][CPB], sDy[2][TC][CPB];
+    __shared__ float sB[2][TC][L], sC[2][TC][L];
+    __shared__ float sPB[kWarps][TC][L], sPC[kWarps][TC][L];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n = lane % L, ci = lane / L, c = warp * G::kCPW + ci;
+    const int d0 = blockIdx.x * CPB, d = d0 + c;
     const int b = blockIdx.y;
     const bool chan = d < D;
     const bool active = chan && n < N;
     const float A = active ? alog[(long long)d * N + n] : 0.f;
     const float Ds = chan ? dskip[d] : 0.f;
-    const int nch = (T + LC - 1) / LC;
+    const int nch = (T + TC - 1) / TC;
     const long long BT = (long long)gridDim.y * T;
+
+    float pr[EPT], pu[EPT], pg[EPT], pz[EPT], py[EPT], pb = 0.f, pc = 0.f;
+    auto fetch = [&](int t0) {
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) {
+            const int idx = tid + e * NT, i = idx / CPB, dd = d0 + idx % CPB;
+            const bool ok = t0 + i < T && dd < D;
+            const long long row = (long long)b * T + t0 + i;
+            pr[e] = ok ? raw[row * D + dd] : 0.f;
+            pu[e] = ok ? u[row * D + dd] : 0.f;
+            pg[e] = ok ? dgated[row * D + dd] : 0.f;
+            pz[e] = ok ? __bfloat162float(proj[row * ldp + dd]) : 0.f;
+            py[e] = ok ? y32[row * D + dd] : 0.f;
+        }
+        if (tid < TC * L) {
+            const int i = tid / L, nn = tid % L;
+            const bool ok = t0 + i < T && nn < N;
+            const long long row = (long long)b * T + t0 + i;
+            pb = ok ? xp[row * ldx + R + nn] : 0.f;
+            pc = ok ? xp[row * ldx + R + N + nn] : 0.f;
+        }
+    };
+    // also writes the x_z gradient, which needs no scan state
+    auto stage = [&](int buf, int t0) {
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) {
+            const int idx = tid + e * NT, i = idx / CPB, cc = idx % CPB;
+            const bool ok = t0 + i < T && d0 + cc < D;
+            sDt[buf][i][cc] = ok ? clamp_dt(softplus_f(pr[e])) : 0.f;
+            sU[buf][i][cc] = pu[e];
+            sDy[buf][i][cc] = pg[e] * silu_f(pz[e]);      // d(loss)/d(y)
+            if (ok) {
+                const long long row = (long long)b * T + t0 + i;
+                dproj[row * ldp + d0 + cc] = __float2bfloat16_rn(pg[e] * py[e] * silu_grad_f(pz[e]));
+            }
+        }
+        if (tid < TC * L) {
+            sB[buf][tid / L][tid % L] = pb;
+            sC[buf][tid / L][tid % L] = pc;
+        }
+    };
+
     float dh_next = 0.f, dA_acc = 0.f, dD_acc = 0.f;
-    for (int ch = nch - 1; ch >= 0; --ch) {
-        const int t0 = ch * LC;
-        const float h_start = active ? hchk[(((long long)b * nch + ch) * D + d) * N + n] : 0.f;
-        float hs[LC], as[LC], dts[LC];
+    fetch((nch - 1) * TC);
+    for (int k = nch - 1; k >= 0; --k) {
+        const int buf = k & 1, t0 = k * TC;
+        stage(buf, t0);
+        __syncthreads();
+        if (k > 0) fetch(t0 - TC);
+        // the chunk's states, recomputed from the one saved at its start
+        const float h_start = active ? hchk[(((long long)b * nch + k) * D + d) * N + n] : 0.f;
+        float hs[TC];
         float h = h_start;
 #pragma unroll
-        for (int i = 0; i < LC; ++i) {
-            const int t = t0 + i;
-            float dt = 0.f, a = 1.f;
-            if (t < T) {
-                const long long row = (long long)b * T + t;
-                dt = clamp_dt(softplus_f(chan ? raw[row * D + d] : 0.f));
-                a = __expf(A * dt);
-                const float uu = chan ? u[row * D + d] : 0.f;
-                const float Bv = active ? xp[row * ldx + R + n] : 0.f;
-                h = a * h + Bv * uu * dt;
+        for (int i = 0; i < TC; ++i) {
+            if (t0 + i < T) {
+                const float dt = sDt[buf][i][c];
+                h = __expf(A * dt) * h + sB[buf][i][n] * sU[buf][i][c] * dt;
             }
             hs[i] = h;
-            as[i] = a;
-            dts[i] = dt;
         }
 #pragma unroll
-        for (int i = LC - 1; i >= 0; --i) {
+        for (int i = TC - 1; i >= 0; --i) {
             const int t = t0 + i;
             float dB_c = 0.f, dC_c = 0.f;
             if (t < T) {
                 const long long row = (long long)b * T + t;
-                const float uu = chan ? u[row * D + d] : 0.f;
-                const float Bv = active ? xp[row * ldx + R + n] : 0.f;
-                const float Cv = active ? xp[row * ldx + R + N + n] : 0.f;
-                const float dgv = chan ? dgated[row * D + d] : 0.f;
-                const float xz = chan ? __bfloat162float(proj[row * ldp + d]) : 0.f;
-                const float dyv = dgv * silu_f(xz);                // d(loss)/d(y)
+                const float dyv = sDy[buf][i][c], uu = sU[buf][i][c], dt_t = sDt[buf][i][c];
+                const float Bv = sB[buf][i][n], Cv = sC[buf][i][n];
+                const float a_t = __expf(A * dt_t);
                 const float h_t = hs[i];
                 const float h_prev = i > 0 ? hs[i - 1] : h_start;
-                const float a_t = as[i], dt_t = dts[i];
                 const float dh = dh_next + dyv * Cv;
                 dC_c = dyv * h_t;
                 dB_c = dh * uu * dt_t;
@@ -196,8 +290,6 @@ __global__ void __launch_bounds__(kWarps * 32) scan_bwd_kernel(
                     du[row * D + d] = du_c + dyv * Ds;
                     ddt[row * D + d] = ddt_c;
                     dD_acc += dyv * uu;
-                    const float yv = y32[row * D + d];
-                    dproj[row * ldp + d] = __float2bfloat16_rn(dgv * yv * silu_grad_f(xz));
                 }
             }
             // sum this warp's channels for every state n (fixed order)
@@ -207,27 +299,26 @@ __global__ void __launch_bounds__(kWarps * 32) scan_bwd_kernel(
                 dC_c += __shfl_xor_sync(0xffffffffu, dC_c, o);
             }
             if (ci == 0) {
-                sB[warp][i][n] = dB_c;
-                sC[warp][i][n] = dC_c;
+                sPB[warp][i][n] = dB_c;
+                sPC[warp][i][n] = dC_c;
             }
         }
         __syncthreads();
         // block partial over its warps (fixed order) -> dbc_part[blockIdx.x][2][B*T][N]
-        for (int k = threadIdx.x; k < LC * N; k += blockDim.x) {
-            const int i = k / N, nn = k - i * N;
+        for (int kk = tid; kk < TC * N; kk += NT) {
+            const int i = kk / N, nn = kk - i * N;
             const int t = t0 + i;
             if (t >= T) continue;
             float sb = 0.f, sc = 0.f;
             for (int w = 0; w < kWarps; ++w) {
-                sb += sB[w][i][nn];
-                sc += sC[w][i][nn];
+                sb += sPB[w][i][nn];
+                sc += sPC[w][i][nn];
             }
             const long long row = (long long)b * T + t;
             float* part = dbc_part + (long long)blockIdx.x * 2 * BT * N;
             part[row * N + nn] = sb;
             part[BT * N + row * N + nn] = sc;
         }
-        __syncthreads();
     }
     if (active) da_part[((long long)b * D + d) * N + n] = dA_acc;
     if (n == 0 && chan) dd_part[(long long)b * D + d] = dD_acc;

@@ -10,7 +10,7 @@
 
 namespace llmgpu {
 
-constexpr int kScanChunk = 32;  // steps between saved scan states
+constexpr int kScanChunk = 16;  // steps between saved scan states
 
 struct MambaDims {
     int B, T, D, N, R, K;
