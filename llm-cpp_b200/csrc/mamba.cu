@@ -94,7 +94,38 @@ struct ScanTile {
     static constexpr int kEPT = kTC * kCPB / kThreads;  // (step, channel) slots per thread
     static_assert(kTC * kCPB % kThreads == 0, "chunk tile must split evenly over the block");
     static_assert(kTC * L <= kThreads, "one (step, state) slot per thread at most");
+    static constexpr int kRow = kCPB + 1;               // padded row: lanes reading one channel
+                                                        // at different steps hit distinct banks
 };
+
+// v[M] held by each of the L lanes of a channel -> channel sums spread over the lanes:
+// lane n holds in v[0, kPer) the sums of entries [(n / kGroup) * kPer, ... + kPer), with
+// kPer = max(M / L, 1) and kGroup = max(L / M, 1) lanes holding each entry. Recursive
+// halving: every stage sends half of the remaining entries to the partner lane (M - M/L
+// shuffles for M >= L, instead of M*log2(L) for M butterflies), and the shuffles of a stage
+// are independent of one another.
+template <int L, int M>
+struct LaneSplit {
+    static constexpr int kPer = M >= L ? M / L : 1;
+    static constexpr int kGroup = M >= L ? 1 : L / M;
+};
+template <int L, int M>
+__device__ __forceinline__ void lane_reduce_scatter(float (&v)[M], int n) {
+#pragma unroll
+    for (int o = L / 2, h = M / 2; o >= 1 && h >= 1; o >>= 1, h >>= 1) {
+        const bool up = (n & o) != 0;
+#pragma unroll
+        for (int k = 0; k < h; ++k) {
+            const float send = up ? v[k] : v[k + h];
+            const float keep = up ? v[k + h] : v[k];
+            v[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    // M < L: lanes within a group still hold partial sums of the same entry
+#pragma unroll
+    for (int o = LaneSplit<L, M>::kGroup / 2; o >= 1; o >>= 1)
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+}
 
 // ---------------------------------------------------------------- scan forward
 template <int L>
@@ -104,8 +135,8 @@ __global__ void __launch_bounds__(kWarps * 32) scan_fwd_kernel(
     const bf16* __restrict__ proj, long long ldp, float* __restrict__ y32,
     bf16* __restrict__ gated, float* __restrict__ hchk, int T, int D, int N, int R) {
     using G = ScanTile<L>;
-    constexpr int CPB = G::kCPB, TC = G::kTC, EPT = G::kEPT, NT = G::kThreads;
-    __shared__ float sDt[2][TC][CPB], sU[2][TC][CPB], sZ[2][TC][CPB];
+    constexpr int CPB = G::kCPB, TC = G::kTC, EPT = G::kEPT, NT = G::kThreads, RW = G::kRow;
+    __shared__ float sDt[2][TC][RW], sU[2][TC][RW], sZ[2][TC][RW];
     __shared__ float sB[2][TC][L], sC[2][TC][L];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n = lane % L, c = warp * G::kCPW + lane / L;
@@ -159,18 +190,24 @@ __global__ void __launch_bounds__(kWarps * 32) scan_fwd_kernel(
         __syncthreads();
         if (k + 1 < nch) fetch(t0 + TC);
         if (active) hchk[(((long long)b * nch + k) * D + d) * N + n] = h;
+        // steps past T were staged as dt = u = B = 0, which leaves h unchanged
+        float cs[TC];
 #pragma unroll
         for (int i = 0; i < TC; ++i) {
             const float dt = sDt[buf][i][c], uu = sU[buf][i][c];
             const float Bv = sB[buf][i][n], Cv = sC[buf][i][n];
             const float a = __expf(A * dt);
             h = a * h + Bv * uu * dt;
-            float cs = Cv * h;
+            cs[i] = Cv * h;
+        }
+        lane_reduce_scatter<L, TC>(cs, n);
+        using S = LaneSplit<L, TC>;
 #pragma unroll
-            for (int o = L / 2; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
-            if (n == 0 && chan && t0 + i < T) {
+        for (int j = 0; j < S::kPer; ++j) {
+            const int i = (n / S::kGroup) * S::kPer + j;
+            if (chan && n % S::kGroup == 0 && t0 + i < T) {
                 const long long row = (long long)b * T + t0 + i;
-                const float yv = cs + Ds * uu;
+                const float yv = cs[j] + Ds * sU[buf][i][c];
                 y32[row * D + d] = yv;
                 gated[row * D + d] = __float2bfloat16_rn(yv * silu_f(sZ[buf][i][c]));
             }
@@ -188,8 +225,8 @@ __global__ void __launch_bounds__(kWarps * 32) scan_bwd_kernel(
     float* __restrict__ ddt, bf16* __restrict__ dproj, float* __restrict__ dbc_part,
     float* __restrict__ da_part, float* __restrict__ dd_part, int T, int D, int N, int R) {
     using G = ScanTile<L>;
-    constexpr int CPB = G::kCPB, TC = G::kTC, EPT = G::kEPT, NT = G::kThreads;
-    __shared__ float sDt[2][TC][CPB], sU[2][TC][CPB], sDy[2][TC][CPB];
+    constexpr int CPB = G::kCPB, TC = G::kTC, EPT = G::kEPT, NT = G::kThreads, RW = G::kRow;
+    __shared__ float sDt[2][TC][RW], sU[2][TC][RW], sDy[2][TC][RW];
     __shared__ float sB[2][TC][L], sC[2][TC][L];
     __shared__ float sPB[kWarps][TC][L], sPC[kWarps][TC][L];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -253,45 +290,38 @@ __global__ void __launch_bounds__(kWarps * 32) scan_bwd_kernel(
         if (k > 0) fetch(t0 - TC);
         // the chunk's states, recomputed from the one saved at its start
         const float h_start = active ? hchk[(((long long)b * nch + k) * D + d) * N + n] : 0.f;
+        // Steps past T were staged as dt = u = B = C = dy = 0: h and dh pass through them
+        // unchanged and they add nothing to dA, dD, dB or dC; their du and ddt are not stored.
         float hs[TC];
         float h = h_start;
 #pragma unroll
         for (int i = 0; i < TC; ++i) {
-            if (t0 + i < T) {
-                const float dt = sDt[buf][i][c];
-                h = __expf(A * dt) * h + sB[buf][i][n] * sU[buf][i][c] * dt;
-            }
+            const float dt = sDt[buf][i][c];
+            h = __expf(A * dt) * h + sB[buf][i][n] * sU[buf][i][c] * dt;
             hs[i] = h;
         }
+        // the reverse pass in two halves of the chunk, each reduced over the lanes at its end
+        constexpr int HS = TC / 2;
+        using S = LaneSplit<L, HS>;
 #pragma unroll
-        for (int i = TC - 1; i >= 0; --i) {
-            const int t = t0 + i;
-            float dB_c = 0.f, dC_c = 0.f;
-            if (t < T) {
-                const long long row = (long long)b * T + t;
-                const float dyv = sDy[buf][i][c], uu = sU[buf][i][c], dt_t = sDt[buf][i][c];
-                const float Bv = sB[buf][i][n], Cv = sC[buf][i][n];
-                const float a_t = __expf(A * dt_t);
-                const float h_t = hs[i];
-                const float h_prev = i > 0 ? hs[i - 1] : h_start;
-                const float dh = dh_next + dyv * Cv;
-                dC_c = dyv * h_t;
-                dB_c = dh * uu * dt_t;
-                float du_c = dh * Bv * dt_t;
-                float ddt_c = dh * h_prev * a_t * A + dh * Bv * uu;
-                dA_acc += dh * h_prev * a_t * dt_t;
-                dh_next = dh * a_t;
+        for (int half = 1; half >= 0; --half) {
+        float du_c[HS], ddt_c[HS];
 #pragma unroll
-                for (int o = L / 2; o > 0; o >>= 1) {
-                    du_c += __shfl_xor_sync(0xffffffffu, du_c, o);
-                    ddt_c += __shfl_xor_sync(0xffffffffu, ddt_c, o);
-                }
-                if (n == 0 && chan) {
-                    du[row * D + d] = du_c + dyv * Ds;
-                    ddt[row * D + d] = ddt_c;
-                    dD_acc += dyv * uu;
-                }
-            }
+        for (int j = HS - 1; j >= 0; --j) {
+            const int i = half * HS + j;
+            const float dyv = sDy[buf][i][c], uu = sU[buf][i][c], dt_t = sDt[buf][i][c];
+            const float Bv = sB[buf][i][n], Cv = sC[buf][i][n];
+            const float a_t = __expf(A * dt_t);
+            const float h_t = hs[i];
+            const float h_prev = i > 0 ? hs[i - 1] : h_start;
+            const float dh = dh_next + dyv * Cv;
+            float dC_c = dyv * h_t;
+            float dB_c = dh * uu * dt_t;
+            du_c[j] = dh * Bv * dt_t;
+            ddt_c[j] = dh * h_prev * a_t * A + dh * Bv * uu;
+            dA_acc += dh * h_prev * a_t * dt_t;
+            dD_acc += dyv * uu;
+            dh_next = dh * a_t;
             // sum this warp's channels for every state n (fixed order)
 #pragma unroll
             for (int o = L; o < 32; o <<= 1) {
@@ -302,6 +332,18 @@ __global__ void __launch_bounds__(kWarps * 32) scan_bwd_kernel(
                 sPB[warp][i][n] = dB_c;
                 sPC[warp][i][n] = dC_c;
             }
+        }
+        lane_reduce_scatter<L, HS>(du_c, n);
+        lane_reduce_scatter<L, HS>(ddt_c, n);
+#pragma unroll
+        for (int j = 0; j < S::kPer; ++j) {
+            const int i = half * HS + (n / S::kGroup) * S::kPer + j;
+            if (chan && n % S::kGroup == 0 && t0 + i < T) {
+                const long long row = (long long)b * T + t0 + i;
+                du[row * D + d] = du_c[j] + sDy[buf][i][c] * Ds;
+                ddt[row * D + d] = ddt_c[j];
+            }
+        }
         }
         __syncthreads();
         // block partial over its warps (fixed order) -> dbc_part[blockIdx.x][2][B*T][N]
