@@ -29,53 +29,44 @@ __device__ __forceinline__ float softplus_f(float v) { return log1pf(__expf(v));
 __device__ __forceinline__ float clamp_dt(float sp) { return fminf(fmaxf(sp, 0.001f), 0.1f); }
 
 // ---------------------------------------------------------------- conv forward
-// pre[t,d] = b[d] + sum_j w[d,j] x[t-(K-1)+j, d] within each sequence; u = silu(pre)
-__global__ void conv_fwd_kernel(const bf16* __restrict__ proj, long long ldp, int D, int T, int K,
+// pre[t,d] = b[d] + sum_j w[d,j] x[t-(K-1)+j, d] within each sequence; u = silu(pre).
+// A thread owns one channel over a run of kConvRows rows and slides a K-row window of x
+// down it, so each x is read once; the rows of a run are independent loads, the unrolled
+// loop keeps several in flight. Taps that reach before the sequence start are skipped.
+constexpr int kConvRows = 64;
+template <int K>
+__global__ void conv_fwd_kernel(const bf16* __restrict__ proj, long long ldp, int D, int T,
                                 const float* __restrict__ w, const float* __restrict__ bias,
                                 float* __restrict__ u32, bf16* __restrict__ u16, long long rows) {
-    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-    if (i >= rows * D) return;
-    const long long row = i / D;
-    const int d = (int)(i - row * D);
-    const int t = (int)(row % T);
-    float acc = bias[d];
-    for (int j = 0; j < K; ++j) {
+    const int d = blockIdx.x * blockDim.x + threadIdx.x;
+    if (d >= D) return;
+    const long long r0 = (long long)blockIdx.y * kConvRows;
+    const int nr = (int)min((long long)kConvRows, rows - r0);
+    float wk[K], win[K];  // win[j] = x[row - (K-1) + j]
+#pragma unroll
+    for (int j = 0; j < K; ++j) wk[j] = w[d * K + j];
+    const float bs = bias[d];
+    int t = (int)(r0 % T);
+#pragma unroll
+    for (int j = 0; j < K - 1; ++j) {
         const int back = K - 1 - j;
-        if (t - back >= 0)
-            acc += w[d * K + j] * __bfloat162float(proj[(row - back) * ldp + D + d]);
+        win[j] = t - back >= 0 ? __bfloat162float(proj[(r0 - back) * ldp + D + d]) : 0.f;
     }
-    const float uv = silu_f(acc);
-    u32[i] = uv;
-    u16[i] = __float2bfloat16_rn(uv);
-}
-
-// ---------------------------------------------------------------- dt forward
-// raw[row, d] = sum_r xp[row, r] * dt_proj[d, r]  (fp32; tiles of 32 rows x 64 channels)
-__global__ void dt_fwd_kernel(const float* __restrict__ xp, long long ldx,
-                              const float* __restrict__ dtp, float* __restrict__ raw,
-                              long long rows, int D, int R) {
-    extern __shared__ float sm[];
-    float* sx = sm;            // [32][R]
-    float* sw = sm + 32 * R;   // [64][R+1]
-    const long long r0 = blockIdx.y * 32LL;
-    const int d0 = blockIdx.x * 64;
-    for (int i = threadIdx.x; i < 32 * R; i += blockDim.x) {
-        const int rr = i / R, k = i - rr * R;
-        sx[i] = (r0 + rr < rows) ? xp[(r0 + rr) * ldx + k] : 0.f;
-    }
-    for (int i = threadIdx.x; i < 64 * R; i += blockDim.x) {
-        const int dd = i / R, k = i - dd * R;
-        sw[dd * (R + 1) + k] = (d0 + dd < D) ? dtp[(long long)(d0 + dd) * R + k] : 0.f;
-    }
-    __syncthreads();
-    const int dd = threadIdx.x & 63;       // channel within the tile
-    const int rg = threadIdx.x >> 6;       // 4 row groups of 8 rows
-    if (d0 + dd >= D) return;
-    for (int rr = rg * 8; rr < rg * 8 + 8; ++rr) {
-        if (r0 + rr >= rows) break;
-        float acc = 0.f;
-        for (int k = 0; k < R; ++k) acc += sx[rr * R + k] * sw[dd * (R + 1) + k];
-        raw[(r0 + rr) * D + d0 + dd] = acc;
+    const bf16* xs = proj + r0 * ldp + D + d;
+#pragma unroll 8
+    for (int r = 0; r < nr; ++r) {
+        win[K - 1] = __bfloat162float(xs[(long long)r * ldp]);
+        float acc = bs;
+#pragma unroll
+        for (int j = 0; j < K; ++j)
+            if (t >= K - 1 - j) acc += wk[j] * win[j];
+        const float uv = silu_f(acc);
+        const long long i = (r0 + r) * D + d;
+        u32[i] = uv;
+        u16[i] = __float2bfloat16_rn(uv);
+#pragma unroll
+        for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
+        t = t + 1 == T ? 0 : t + 1;
     }
 }
 
@@ -403,53 +394,80 @@ __global__ void dt_bwd_kernel(const float* __restrict__ ddt, const float* __rest
     draw[i] = __float2bfloat16_rn(ddt[i] * in * sigmoid_f(r));
 }
 
-// conv backward, stage 1: dpre = (du_scan + du_xp) * silu'(pre); per-block partial sums of
-// dconv_b and dconv_w over the block's rows (grid: D/256 x row blocks of kConvRows)
-constexpr int kConvRows = 64;
-__global__ void conv_bwd1_kernel(const bf16* __restrict__ proj, long long ldp, int D, int T,
-                                 int K, const float* __restrict__ w, const float* __restrict__ bias,
-                                 const float* __restrict__ du1, const float* __restrict__ du2,
-                                 float* __restrict__ dpre, float* __restrict__ part,
-                                 long long rows) {
+// conv backward, fused: g = (du_scan + du_xp) * silu'(pre) with pre recomputed from the x
+// window; per-run partial sums of dconv_b and dconv_w; and dx_ssm[t,d] =
+// sum_j g[t+(K-1-j), d] w[d,j] within the sequence, from a K-row window of g that runs K-1
+// rows ahead of the row it completes (those halo rows are recomputed, not stored).
+// Grid: D/256 x row runs of kConvRows; partials part[run][d][K+1].
+template <int K>
+__global__ void conv_bwd_kernel(const bf16* __restrict__ proj, long long ldp, int D, int T,
+                                const float* __restrict__ w, const float* __restrict__ bias,
+                                const float* __restrict__ du1, const float* __restrict__ du2,
+                                float* __restrict__ part, bf16* __restrict__ dproj,
+                                long long rows) {
     const int d = blockIdx.x * blockDim.x + threadIdx.x;
     if (d >= D) return;
     const long long r0 = (long long)blockIdx.y * kConvRows;
-    float sb = 0.f, sw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (long long row = r0; row < r0 + kConvRows && row < rows; ++row) {
-        const int t = (int)(row % T);
-        float pre = bias[d];
-        float xin[8];
-        for (int j = 0; j < K; ++j) {
-            const int back = K - 1 - j;
-            xin[j] = (t - back >= 0) ? __bfloat162float(proj[(row - back) * ldp + D + d]) : 0.f;
-            pre += w[d * K + j] * xin[j];
+    const int nr = (int)min((long long)kConvRows, rows - r0);
+    const int nh = (int)min((long long)nr + K - 1, rows - r0);  // rows incl. the halo
+    float wk[K], xw[K], gw[K];  // xw[j] = x[row'-(K-1)+j], gw[f] = g[row'-(K-1)+f]
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        wk[j] = w[d * K + j];
+        gw[j] = 0.f;
+    }
+    const float bs = bias[d];
+    int tp = (int)(r0 % T);  // position of row' in its sequence
+    int tr = tp;             // position of the row the window completes next
+#pragma unroll
+    for (int j = 0; j < K - 1; ++j) {
+        const int back = K - 1 - j;
+        xw[j] = tp - back >= 0 ? __bfloat162float(proj[(r0 - back) * ldp + D + d]) : 0.f;
+    }
+    float sb = 0.f, sw[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) sw[j] = 0.f;
+    const bf16* xs = proj + r0 * ldp + D + d;
+#pragma unroll 4
+    for (int r = 0; r < nr + K - 1; ++r) {
+        const bool in = r < nh;
+        xw[K - 1] = in ? __bfloat162float(xs[(long long)r * ldp]) : 0.f;
+        const long long i = (r0 + r) * D + d;
+        float pre = bs;
+#pragma unroll
+        for (int j = 0; j < K; ++j)
+            if (tp >= K - 1 - j) pre += wk[j] * xw[j];
+        const float g = in ? (du1[i] + du2[i]) * silu_grad_f(pre) : 0.f;
+        if (r < nr) {
+            sb += g;
+#pragma unroll
+            for (int j = 0; j < K; ++j)
+                if (tp >= K - 1 - j) sw[j] += g * xw[j];
         }
-        const long long i = row * D + d;
-        const float g = (du1[i] + du2[i]) * silu_grad_f(pre);
-        dpre[i] = g;
-        sb += g;
-        for (int j = 0; j < K; ++j) sw[j] += g * xin[j];
+        // g[row'] enters the window; the row K-1 above row' is now complete
+        gw[K - 1] = g;
+        const int rr = r - (K - 1);
+        if (rr >= 0) {
+            float acc = 0.f;
+#pragma unroll
+            for (int j = 0; j < K; ++j) {
+                const int f = K - 1 - j;
+                if (tr + f < T) acc += gw[f] * wk[j];
+            }
+            dproj[(r0 + rr) * ldp + D + d] = __float2bfloat16_rn(acc);
+            tr = tr + 1 == T ? 0 : tr + 1;
+        }
+#pragma unroll
+        for (int j = 0; j < K - 1; ++j) {
+            xw[j] = xw[j + 1];
+            gw[j] = gw[j + 1];
+        }
+        tp = tp + 1 == T ? 0 : tp + 1;
     }
     float* p = part + ((long long)blockIdx.y * D + d) * (K + 1);
     p[0] = sb;
+#pragma unroll
     for (int j = 0; j < K; ++j) p[1 + j] = sw[j];
-}
-
-// conv backward, stage 2: dxs[t,d] = sum_j dpre[t+(K-1-j), d] w[d,j] -> bf16 dproj[:, D+d]
-__global__ void conv_bwd2_kernel(const float* __restrict__ dpre, const float* __restrict__ w,
-                                 bf16* __restrict__ dproj, long long ldp, int D, int T, int K,
-                                 long long rows) {
-    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-    if (i >= rows * D) return;
-    const long long row = i / D;
-    const int d = (int)(i - row * D);
-    const int t = (int)(row % T);
-    float acc = 0.f;
-    for (int j = 0; j < K; ++j) {
-        const int fwd = K - 1 - j;
-        if (t + fwd < T) acc += dpre[(row + fwd) * D + d] * w[d * K + j];
-    }
-    dproj[row * ldp + D + d] = __float2bfloat16_rn(acc);
 }
 
 // conv weight/bias gradients: out_b[d] (+)= sum_blk part[blk][d][0], out_w[d,j] (+)= ...[1+j]
@@ -475,73 +493,112 @@ __global__ void dt_bwd_f32_kernel(const float* __restrict__ ddt, const float* __
     draw[i] = ddt[i] * in * sigmoid_f(r);
 }
 
-// Small fp32 GEMM for the dt_rank-wide contractions of the dt path: part[y][m][n] =
-// sum_{k in chunk y} A(m,k) B(k,n) with A(m,k) = A[m*sam + k*sak], B(k,n) = B[k*sbk + n*sbn],
-// N <= 64. 64 x 64 output tile per block, 4 x 4 per thread, k staged 32 at a time.
-constexpr int kSgM = 64, kSgK = 32;
-__global__ void __launch_bounds__(256) small_gemm_f32_kernel(
+// fp32 GEMM on the CUDA cores for the dt_rank-wide contractions of the dt path (the clamp
+// mask after softplus needs fp32 operands): C = A B with A(m,k) = A[m*sam + k*sak] and
+// B(k,n) = B[k*sbk + n*sbn]. 128 x BN output tile per block (8 x BN/16 per thread), k staged
+// 16 at a time in double-buffered shared memory, the next stage's loads in flight during the
+// current stage's math. blockIdx.z splits K into chunks of kchunk: with one chunk the tile
+// goes straight to out (fp32, += when accumulate) or out16 (bf16); with several, to
+// part[z][M][N] for a fixed-order reduction.
+constexpr int kSgM = 128, kSgK = 16;
+template <int BN>
+__global__ void __launch_bounds__(256) sgemm_f32_kernel(
     const float* __restrict__ A, long long sam, long long sak, const float* __restrict__ Bm,
-    long long sbk, long long sbn, int M, int N, int K, int kchunk, float* __restrict__ part) {
-    __shared__ float As[kSgK][kSgM + 1];
-    __shared__ float Bs[kSgK][64 + 1];
-    const int m0 = blockIdx.x * kSgM;
-    const int kbeg = blockIdx.y * kchunk;
-    const int kend = min(K, kbeg + kchunk);
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-    float acc[4][4];
+    long long sbk, long long sbn, int M, int N, int K, int kchunk, float* __restrict__ part,
+    float* __restrict__ out, bf16* __restrict__ out16, long long ldo, int accumulate) {
+    constexpr int TM = 8, TN = BN / 16;
+    constexpr int AE = kSgM * kSgK / 256, BE = kSgK * BN / 256;
+    static_assert(BN % 16 == 0 && kSgK * BN % 256 == 0, "B stage must split over the block");
+    __shared__ __align__(16) float As[2][kSgK][kSgM + 4];
+    __shared__ __align__(16) float Bs[2][kSgK][BN + 4];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int m0 = blockIdx.x * kSgM, n0 = blockIdx.y * BN;
+    const int kbeg = blockIdx.z * kchunk, kend = min(K, kbeg + kchunk);
+    const bool a_kfast = sak == 1, b_nfast = sbn == 1;
+    float ra[AE], rb[BE];
+    auto gload = [&](int k0) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-    for (int k0 = kbeg; k0 < kend; k0 += kSgK) {
-        for (int i = threadIdx.x; i < kSgM * kSgK; i += blockDim.x) {
-            int mm, kk;
-            if (sam == 1) {
-                mm = i % kSgM;
-                kk = i / kSgM;
-            } else {
-                kk = i % kSgK;
-                mm = i / kSgK;
-            }
+        for (int e = 0; e < AE; ++e) {
+            const int idx = tid + e * 256;
+            const int mm = a_kfast ? idx / kSgK : idx % kSgM;
+            const int kk = a_kfast ? idx % kSgK : idx / kSgM;
             const int m = m0 + mm, k = k0 + kk;
-            As[kk][mm] = (m < M && k < kend) ? A[(long long)m * sam + (long long)k * sak] : 0.f;
+            ra[e] = (m < M && k < kend) ? A[(long long)m * sam + (long long)k * sak] : 0.f;
         }
-        for (int i = threadIdx.x; i < kSgK * 64; i += blockDim.x) {
-            int kk, nn;
-            if (sbn == 1) {
-                nn = i % 64;
-                kk = i / 64;
-            } else {
-                kk = i % kSgK;
-                nn = i / kSgK;
-            }
-            const int k = k0 + kk;
-            Bs[kk][nn] = (nn < N && k < kend) ? Bm[(long long)k * sbk + (long long)nn * sbn] : 0.f;
+#pragma unroll
+        for (int e = 0; e < BE; ++e) {
+            const int idx = tid + e * 256;
+            const int nn = b_nfast ? idx % BN : idx / kSgK;
+            const int kk = b_nfast ? idx / BN : idx % kSgK;
+            const int n = n0 + nn, k = k0 + kk;
+            rb[e] = (n < N && k < kend) ? Bm[(long long)k * sbk + (long long)n * sbn] : 0.f;
         }
-        __syncthreads();
-#pragma unroll 4
-        for (int kk = 0; kk < kSgK; ++kk) {
-            float av[4], bv[4];
+    };
+    auto sstore = [&](int buf) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx * 4 + j];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] += av[i] * bv[j];
+        for (int e = 0; e < AE; ++e) {
+            const int idx = tid + e * 256;
+            const int mm = a_kfast ? idx / kSgK : idx % kSgM;
+            const int kk = a_kfast ? idx % kSgK : idx / kSgM;
+            As[buf][kk][mm] = ra[e];
         }
-        __syncthreads();
+#pragma unroll
+        for (int e = 0; e < BE; ++e) {
+            const int idx = tid + e * 256;
+            const int nn = b_nfast ? idx % BN : idx / kSgK;
+            const int kk = b_nfast ? idx / BN : idx % kSgK;
+            Bs[buf][kk][nn] = rb[e];
+        }
+    };
+    float acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+    if (kbeg < kend) {
+        gload(kbeg);
+        sstore(0);
     }
-    float* p = part + (long long)blockIdx.y * M * N;
+    __syncthreads();
+    int buf = 0;
+    for (int k0 = kbeg; k0 < kend; k0 += kSgK) {
+        const bool more = k0 + kSgK < kend;
+        if (more) gload(k0 + kSgK);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int m = m0 + ty * 4 + i;
+        for (int kk = 0; kk < kSgK; ++kk) {
+            float av[TM], bv[TN];
+            const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * TM]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * TM + 4]);
+            av[0] = a0.x; av[1] = a0.y; av[2] = a0.z; av[3] = a0.w;
+            av[4] = a1.x; av[5] = a1.y; av[6] = a1.z; av[7] = a1.w;
+#pragma unroll
+            for (int j = 0; j < TN; ++j) bv[j] = Bs[buf][kk][tx * TN + j];
+#pragma unroll
+            for (int i = 0; i < TM; ++i)
+#pragma unroll
+                for (int j = 0; j < TN; ++j) acc[i][j] += av[i] * bv[j];
+        }
+        if (more) sstore(buf ^ 1);
+        __syncthreads();
+        buf ^= 1;
+    }
+    const bool split = gridDim.z > 1;
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+        const int m = m0 + ty * TM + i;
         if (m >= M) continue;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int n = tx * 4 + j;
-            if (n < N) p[(long long)m * N + n] = acc[i][j];
+        for (int j = 0; j < TN; ++j) {
+            const int n = n0 + tx * TN + j;
+            if (n >= N) continue;
+            if (split) {
+                part[((long long)blockIdx.z * M + m) * N + n] = acc[i][j];
+            } else if (out16) {
+                out16[(long long)m * ldo + n] = __float2bfloat16_rn(acc[i][j]);
+            } else {
+                float* o = out + (long long)m * ldo + n;
+                *o = accumulate ? *o + acc[i][j] : acc[i][j];
+            }
         }
     }
 }
@@ -611,15 +668,23 @@ int mamba_dt_backward_f32(const MambaDims& m, const float* ddt, const float* raw
 int small_gemm_f32(const float* A, long long sam, long long sak, const float* B, long long sbk,
                    long long sbn, int M, int N, int K, int ksplit, float* part, float* out,
                    bf16* out16, long long ldo, int accumulate, cudaStream_t s) {
-    if (N > 64 || ksplit < 1) return -1;
+    if (ksplit < 1 || M < 1 || N < 1 || K < 1) return -1;
     const int kchunk = ((K + ksplit - 1) / ksplit + kSgK - 1) / kSgK * kSgK;
-    const int ys = (K + kchunk - 1) / kchunk;
-    dim3 grid((M + kSgM - 1) / kSgM, ys);
-    small_gemm_f32_kernel<<<grid, 256, 0, s>>>(A, sam, sak, B, sbk, sbn, M, N, K, kchunk, part);
+    const int zs = (K + kchunk - 1) / kchunk;
+    if (zs > 1 && !part) return -1;
+    const bool narrow = N <= 48;  // the dt_rank-wide outputs fit one 48-column tile
+    const int bn = narrow ? 48 : 64;
+    dim3 grid((M + kSgM - 1) / kSgM, (N + bn - 1) / bn, zs);
+    if (narrow)
+        sgemm_f32_kernel<48><<<grid, 256, 0, s>>>(A, sam, sak, B, sbk, sbn, M, N, K, kchunk, part,
+                                                  out, out16, ldo, accumulate);
+    else
+        sgemm_f32_kernel<64><<<grid, 256, 0, s>>>(A, sam, sak, B, sbk, sbn, M, N, K, kchunk, part,
+                                                  out, out16, ldo, accumulate);
     int rc = launch_status();
-    if (rc) return rc;
+    if (rc || zs == 1) return rc;
     const long long n = (long long)M * N;
-    small_gemm_reduce_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(part, ys, M, N, out, out16, ldo,
+    small_gemm_reduce_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(part, zs, M, N, out, out16, ldo,
                                                                     accumulate);
     return launch_status();
 }
@@ -639,22 +704,47 @@ int mamba_scan_groups(int D, int N) {
 }
 int mamba_conv_blocks(long long rows) { return (int)((rows + kConvRows - 1) / kConvRows); }
 
-int mamba_conv_forward(const MambaDims& m, const bf16* proj, const float* w, const float* bias,
-                       float* u32, bf16* u16, cudaStream_t s) {
-    if (m.K > 8) return -1;
-    const long long rows = (long long)m.B * m.T, n = rows * m.D;
-    conv_fwd_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(proj, m.ldp, m.D, m.T, m.K, w, bias, u32,
-                                                           u16, rows);
+template <int K>
+int launch_conv_fwd(const MambaDims& m, const bf16* proj, const float* w, const float* bias,
+                    float* u32, bf16* u16, cudaStream_t s) {
+    const long long rows = (long long)m.B * m.T;
+    dim3 grid((m.D + 255) / 256, mamba_conv_blocks(rows));
+    conv_fwd_kernel<K><<<grid, 256, 0, s>>>(proj, m.ldp, m.D, m.T, w, bias, u32, u16, rows);
     return launch_status();
 }
 
+template <int K>
+int launch_conv_bwd(const MambaDims& m, const bf16* proj, const float* w, const float* bias,
+                    const float* du_scan, const float* du_xp, float* part, bf16* dproj,
+                    cudaStream_t s) {
+    const long long rows = (long long)m.B * m.T;
+    dim3 grid((m.D + 255) / 256, mamba_conv_blocks(rows));
+    conv_bwd_kernel<K><<<grid, 256, 0, s>>>(proj, m.ldp, m.D, m.T, w, bias, du_scan, du_xp, part,
+                                            dproj, rows);
+    return launch_status();
+}
+
+int mamba_conv_forward(const MambaDims& m, const bf16* proj, const float* w, const float* bias,
+                       float* u32, bf16* u16, cudaStream_t s) {
+    switch (m.K) {
+        case 1: return launch_conv_fwd<1>(m, proj, w, bias, u32, u16, s);
+        case 2: return launch_conv_fwd<2>(m, proj, w, bias, u32, u16, s);
+        case 3: return launch_conv_fwd<3>(m, proj, w, bias, u32, u16, s);
+        case 4: return launch_conv_fwd<4>(m, proj, w, bias, u32, u16, s);
+        case 5: return launch_conv_fwd<5>(m, proj, w, bias, u32, u16, s);
+        case 6: return launch_conv_fwd<6>(m, proj, w, bias, u32, u16, s);
+        case 7: return launch_conv_fwd<7>(m, proj, w, bias, u32, u16, s);
+        case 8: return launch_conv_fwd<8>(m, proj, w, bias, u32, u16, s);
+        default: return -1;
+    }
+}
+
+// raw = xp[:, :R] dt_proj^T, fp32 (rows x D, K = R)
 int mamba_dt_forward(const MambaDims& m, const float* xp, const float* dt_proj, float* raw,
                      cudaStream_t s) {
-    const long long rows = (long long)m.B * m.T;
-    dim3 grid((m.D + 63) / 64, (unsigned)((rows + 31) / 32));
-    const size_t smem = (32 * m.R + 64 * (m.R + 1)) * sizeof(float);
-    dt_fwd_kernel<<<grid, 256, smem, s>>>(xp, m.ldx, dt_proj, raw, rows, m.D, m.R);
-    return launch_status();
+    const int rows = m.B * m.T;
+    return small_gemm_f32(xp, m.ldx, 1, dt_proj, 1, m.R, rows, m.D, m.R, 1, nullptr, raw, nullptr,
+                          m.D, 0, s);
 }
 
 int mamba_scan_forward(const MambaDims& m, const float* raw, const float* u, const float* xp,
@@ -705,19 +795,22 @@ int mamba_dt_backward(const MambaDims& m, const float* ddt, const float* raw, bf
 }
 
 int mamba_conv_backward(const MambaDims& m, const bf16* proj, const float* w, const float* bias,
-                        const float* du_scan, const float* du_xp, float* dpre, float* part,
-                        bf16* dproj, float* gw, float* gb, int accumulate, cudaStream_t s) {
-    if (m.K > 8) return -1;
-    const long long rows = (long long)m.B * m.T;
-    dim3 g1((m.D + 255) / 256, mamba_conv_blocks(rows));
-    conv_bwd1_kernel<<<g1, 256, 0, s>>>(proj, m.ldp, m.D, m.T, m.K, w, bias, du_scan, du_xp, dpre,
-                                        part, rows);
-    int rc = launch_status();
+                        const float* du_scan, const float* du_xp, float* part, bf16* dproj,
+                        float* gw, float* gb, int accumulate, cudaStream_t s) {
+    int rc;
+    switch (m.K) {
+        case 1: rc = launch_conv_bwd<1>(m, proj, w, bias, du_scan, du_xp, part, dproj, s); break;
+        case 2: rc = launch_conv_bwd<2>(m, proj, w, bias, du_scan, du_xp, part, dproj, s); break;
+        case 3: rc = launch_conv_bwd<3>(m, proj, w, bias, du_scan, du_xp, part, dproj, s); break;
+        case 4: rc = launch_conv_bwd<4>(m, proj, w, bias, du_scan, du_xp, part, dproj, s); break;
+        case 5: rc = launch_conv_bwd<5>(m, proj, w, bias, du_scan, du_xp, part, dproj, s); break;
+        case 6: rc = launch_conv_bwd<6>(m, proj, w, bias, du_scan, du_xp, part, dproj, s); break;
+        case 7: rc = launch_conv_bwd<7>(m, proj, w, bias, du_scan, du_xp, part, dproj, s); break;
+        case 8: rc = launch_conv_bwd<8>(m, proj, w, bias, du_scan, du_xp, part, dproj, s); break;
+        default: return -1;
+    }
     if (rc) return rc;
-    const long long n = rows * m.D;
-    conv_bwd2_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(dpre, w, dproj, m.ldp, m.D, m.T, m.K,
-                                                            rows);
-    if ((rc = launch_status())) return rc;
+    const long long rows = (long long)m.B * m.T;
     const int nr = m.D * (m.K + 1);
     conv_reduce_kernel<<<(nr + 255) / 256, 256, 0, s>>>(part, mamba_conv_blocks(rows), m.D, m.K, gw,
                                                         gb, accumulate);

@@ -43,15 +43,18 @@ int mamba_dt_backward(const MambaDims& m, const float* ddt, const float* raw, bf
                       cudaStream_t s);
 // part: mamba_conv_blocks(rows) * D * (K+1) floats; writes dx_ssm into dproj[:, D:2D]
 int mamba_conv_backward(const MambaDims& m, const bf16* proj, const float* w, const float* bias,
-                        const float* du_scan, const float* du_xp, float* dpre, float* part,
-                        bf16* dproj, float* gw, float* gb, int accumulate, cudaStream_t s);
+                        const float* du_scan, const float* du_xp, float* part, bf16* dproj,
+                        float* gw, float* gb, int accumulate, cudaStream_t s);
 
 // fp32 draw = ddt * clamp-mask * sigmoid(raw)   (src/mamba.cpp:318-328)
 int mamba_dt_backward_f32(const MambaDims& m, const float* ddt, const float* raw, float* draw,
                           cudaStream_t s);
-// out = A B for the dt_rank-wide fp32 contractions (N <= 64), K split `ksplit` ways through
-// `part` (ksplit * M * N floats) and reduced in order; writes fp32 `out` (+= if accumulate)
-// or bf16 `out16` when given. A(m,k) = A[m*sam + k*sak], B(k,n) = B[k*sbk + n*sbn].
+// out = A B in fp32 on the CUDA cores (the dt path's contractions), K split `ksplit` ways
+// through `part` (ksplit * M * N floats, unused when ksplit is 1) and reduced in order;
+// writes fp32 `out` (+= if accumulate) or bf16 `out16` when given.
+// A(m,k) = A[m*sam + k*sak], B(k,n) = B[k*sbk + n*sbn].
+constexpr int kSgSplitRows = 4;   // K split of the rows x dt_rank products (K = d_inner)
+constexpr int kSgSplitCols = 32;  // K split of the d_inner x dt_rank product (K = rows)
 int small_gemm_f32(const float* A, long long sam, long long sak, const float* B, long long sbk,
                    long long sbn, int M, int N, int K, int ksplit, float* part, float* out,
                    bf16* out16, long long ldo, int accumulate, cudaStream_t s);

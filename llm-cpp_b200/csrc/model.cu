@@ -547,7 +547,8 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
             dalloc(c, &c->m_convpart, (size_t)mamba_conv_blocks(BT) * D * (c->mK + 1)) ||
             dalloc(c, &c->m_dproj, (size_t)BT * 2 * D) || dalloc(c, &c->m_draw, (size_t)BT * D) ||
             dalloc(c, &c->m_dxp, (size_t)BT * c->mRPp) ||
-            dalloc(c, &c->m_sgpart, std::max((size_t)BT, (size_t)16 * D) * c->mR))
+            dalloc(c, &c->m_sgpart,
+                   std::max((size_t)kSgSplitRows * BT, (size_t)kSgSplitCols * D) * c->mR))
             return fail(c, "");
     }
     for (int l = 0; l < L && !c->mamba; ++l) {
@@ -783,8 +784,8 @@ int mamba_forward_layer(Ctx* c, int l, int B, int T, float* xnext) {
     // x_proj: the dt_rank columns feed softplus + a hard clamp whose mask gates the dt
     // gradient (src/mamba.cpp:318-328); a bf16 operand moves dt_raw enough to flip that mask
     // near its edges, so those columns are computed in fp32. B and C use the tensor cores.
-    KC(small_gemm_f32(m.u32, D, 1, pp(b.x_proj), 1, D, BT, c->mR, D, 1, c->m_sgpart, m.xp,
-                      nullptr, c->mRPp, 0, s));
+    KC(small_gemm_f32(m.u32, D, 1, pp(b.x_proj), 1, D, BT, c->mR, D, kSgSplitRows, c->m_sgpart,
+                      m.xp, nullptr, c->mRPp, 0, s));
     if ((rc = gemm(c, m.u16, D, 0, c->xproj16[l] + (size_t)c->mR * D, D, 0, BT, 2 * c->mN, D,
                    epi_args(kEpiStoreF32, m.xp + c->mR, c->mRPp))))
         return rc;
@@ -828,14 +829,14 @@ int mamba_backward_layer(Ctx* c, int l, int B, int T, int acc) {
     // dt: clamp mask + softplus backward, then through dt_proj (src/mamba.cpp:310-329)
     // These two dt_rank-wide contractions are sums with heavy cancellation, so they stay in
     // fp32 (a bf16 operand costs ~5% on the dt_proj gradient).
-    float* draw = c->m_dpre;  // free until the conv backward below
+    float* draw = c->m_dpre;  // fp32 scratch of the dt path
     KC(mamba_dt_backward_f32(md, c->m_ddt, m.raw, draw, s));
     // dxp[:, :R] = draw dt_proj  ([BT, D] x [D, R]) -> bf16 columns [0, R) of dxp
-    KC(small_gemm_f32(draw, D, 1, pp(b.dt_proj), R, 1, BT, R, D, 1, c->m_sgpart, nullptr,
-                      c->m_dxp, c->mRPp, 0, s));
-    // ddt_proj = draw^T xp[:, :R]  ([D, BT] x [BT, R], K split 16 ways)
-    KC(small_gemm_f32(draw, 1, D, m.xp, c->mRPp, 1, D, R, BT, 16, c->m_sgpart, gp(b.dt_proj),
-                      nullptr, R, acc, s));
+    KC(small_gemm_f32(draw, D, 1, pp(b.dt_proj), R, 1, BT, R, D, kSgSplitRows, c->m_sgpart,
+                      nullptr, c->m_dxp, c->mRPp, 0, s));
+    // ddt_proj = draw^T xp[:, :R]  ([D, BT] x [BT, R], K split)
+    KC(small_gemm_f32(draw, 1, D, m.xp, c->mRPp, 1, D, R, BT, kSgSplitCols, c->m_sgpart,
+                      gp(b.dt_proj), nullptr, R, acc, s));
     // x_proj (src/mamba.cpp:330-347)
     if ((rc = gemm(c, c->m_dxp, c->mRPp, 0, c->xproj16[l], D, 1, BT, D, c->mRP,
                    epi_args(kEpiStoreF32, c->m_duxp, D))))
@@ -846,7 +847,7 @@ int mamba_backward_layer(Ctx* c, int l, int B, int T, int acc) {
                    choose_splits(c, c->mRP, D, BT))))
         return rc;
     // SiLU + causal conv backward; dx_ssm into dproj[:, D:2D] (src/mamba.cpp:348-371)
-    KC(mamba_conv_backward(md, m.proj, pp(b.conv_w), pp(b.conv_b), c->m_du, c->m_duxp, c->m_dpre,
+    KC(mamba_conv_backward(md, m.proj, pp(b.conv_w), pp(b.conv_b), c->m_du, c->m_duxp,
                            c->m_convpart, c->m_dproj, gp(b.conv_w), gp(b.conv_b), acc, s));
     // in_proj (src/mamba.cpp:379-396)
     if ((rc = gemm(c, c->m_dproj, 2 * D, 0, c->in16[l], C, 1, BT, C, 2 * D,

@@ -156,6 +156,11 @@ ORACLE_CASES = {
     "mamba_n16": (go.Cfg(vocab=256, n_layers=2, n_heads=1, n_embd=64, block_size=128,
                          rmsnorm=True, mamba=True, d_inner=128, d_state=16, dt_rank=8,
                          conv_kernel=4), 2, 128),
+    # ragged Mamba: T not a multiple of the scan chunk or the conv row run (runs cross
+    # sequence starts), d_state 8, d_inner not a multiple of the scan's channel block, K = 3
+    "mamba_ragged_n8": (go.Cfg(vocab=256, n_layers=1, n_heads=1, n_embd=64, block_size=100,
+                               rmsnorm=True, mamba=True, d_inner=80, d_state=8, dt_rank=6,
+                               conv_kernel=3), 3, 100),
 }
 
 
