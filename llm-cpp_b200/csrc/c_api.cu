@@ -51,6 +51,7 @@ int validate_bt(Ctx* c, int B, int T) {
 
 int enqueue_step(Ctx* c, int B, int T, int accumulate, bool do_step, int K) {
     c->plan_cursor = 0;
+    c->plan2_cursor = 0;
     c->prof_n = 0;
     int rc = run_fwd_bwd(c, B, T, accumulate, true, do_step && c->world > 1);
     if (rc) return rc;
@@ -291,6 +292,7 @@ int llmgpu_eval_loss(llmgpu_ctx* h, const int32_t* tokens, int B, int T, float* 
     int rc = stage_tokens(c, tokens, B, T);
     if (rc) return rc;
     c->plan_cursor = 0;
+    c->plan2_cursor = 0;
     c->launches = 0;
     if ((rc = run_fwd_bwd(c, B, T, 0, false))) return rc;
     if (cudaMemcpyAsync(c->h_out, c->d_out, sizeof(float), cudaMemcpyDeviceToHost, c->stream) !=

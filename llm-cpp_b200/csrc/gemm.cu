@@ -12,6 +12,8 @@
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
+#include <vector>
+#include <algorithm>
 
 #include "common.cuh"
 #include "gemm.cuh"
@@ -623,11 +625,57 @@ __device__ __forceinline__ uint32_t pair_stage_bytes(const GemmArgs& a, int am, 
     return bytes;
 }
 
+// Launch parameters of the pair kernel for NG co-scheduled products (NG = 2: the data- and
+// weight-gradient products of one layer, which read the same upstream gradient but not each
+// other's results). With NG = 1 cluster c takes tiles c, c + clusters, ...; with NG = 2 the
+// host's per-cluster lists in `sched` ([cluster][stride]: count, then items g << 24 | tile)
+// balance the two products' tiles over the pairs.
+template <int NG>
+struct PairParams {
+    CUtensorMap tmA[NG];
+    CUtensorMap tmB[NG];
+    CUtensorMap tmO[NG];
+    CUtensorMap tmX[NG];
+    GemmArgs args[NG];
+    const int* sched;
+    int sched_stride;
+};
+
+// Tile geometry of one product on 256 x 256 pair tiles.
+struct PairShape {
+    int num_m, num_n, tiles_mn, kblocks;
+};
+__device__ __forceinline__ PairShape pair_shape(const GemmArgs& a) {
+    PairShape s;
+    s.num_m = (a.M + PairCfg::BMP - 1) / PairCfg::BMP;
+    s.num_n = (a.N + PairCfg::BN - 1) / PairCfg::BN;
+    s.tiles_mn = s.num_m * s.num_n;
+    s.kblocks = (a.K + BK - 1) / BK;
+    return s;
+}
+
+// Item i of cluster cid's work: product g, tile t of that product (split-major).
+template <int NG>
+__device__ __forceinline__ bool pair_item(const PairParams<NG>& P, int cid, int nclusters, int i,
+                                          int& g, int& t) {
+    if constexpr (NG == 1) {
+        const PairShape s = pair_shape(P.args[0]);
+        g = 0;
+        t = cid + i * nclusters;
+        return t < s.tiles_mn * P.args[0].splits;
+    } else {
+        const int* l = P.sched + (size_t)cid * P.sched_stride;
+        if (i >= l[0]) return false;
+        const int v = l[1 + i];
+        g = v >> 24;
+        t = v & 0xffffff;
+        return true;
+    }
+}
+
+template <int NG>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
-                          const __grid_constant__ CUtensorMap tmB,
-                          const __grid_constant__ CUtensorMap tmO,
-                          const __grid_constant__ CUtensorMap tmX, const GemmArgs args) {
+    gemm_bf16_pair_kernel(const __grid_constant__ PairParams<NG> P) {
     using Cfg = PairCfg;
     constexpr int STAGES = Cfg::STAGES;
     constexpr int BN = Cfg::BN;
@@ -648,14 +696,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const bool leader = rank == 0;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int M = args.M, N = args.N, K = args.K;
-    const int num_m = (M + Cfg::BMP - 1) / Cfg::BMP;
-    const int num_n = (N + BN - 1) / BN;
-    const int kblocks = (K + BK - 1) / BK;
-    const int tiles_mn = num_m * num_n;
-    const int total = tiles_mn * args.splits;
     const int cid = blockIdx.x >> 1;
     const int nclusters = gridDim.x >> 1;
+    int* const err = P.args[0].err;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -670,16 +713,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
-        tma_prefetch_desc(&tmA);
-        tma_prefetch_desc(&tmB);
+        for (int g = 0; g < NG; ++g) {
+            tma_prefetch_desc(&P.tmA[g]);
+            tma_prefetch_desc(&P.tmB[g]);
+        }
     }
     if (warp == 1) {
         tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
         tmem_relinquish_pair();
     }
+    // row-group table of a grouped product (single products only)
     __shared__ int s_grp[kMaxGemmGroups + 1];
-    if (args.grp_mode != kGroupNone)
-        for (int i = threadIdx.x; i <= args.groups; i += blockDim.x) s_grp[i] = args.grp[i];
+    if (NG == 1 && P.args[0].grp_mode != kGroupNone)
+        for (int i = threadIdx.x; i <= P.args[0].groups; i += blockDim.x) s_grp[i] = P.args[0].grp[i];
     tc_fence_before();
     __syncthreads();
     cluster_sync_all();  // barriers of both CTAs initialised before any remote use
@@ -693,17 +739,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int t = cid; t < total && ok; t += nclusters) {
-                int m_blk, n_blk, split, g, kb0, kb1;
-                tile_work(args, s_grp, t, num_m, num_n, tiles_mn, kblocks, m_blk, n_blk, split, g,
-                          kb0, kb1);
+            int g, t;
+            for (int i = 0; ok && pair_item(P, cid, nclusters, i, g, t); ++i) {
+                const GemmArgs& args = P.args[g];
+                const PairShape sh = pair_shape(args);
+                const CUtensorMap* tmA = &P.tmA[g];
+                const CUtensorMap* tmB = &P.tmB[g];
+                int m_blk, n_blk, split, gi, kb0, kb1;
+                tile_work(args, s_grp, t, sh.num_m, sh.num_n, sh.tiles_mn, sh.kblocks, m_blk,
+                          n_blk, split, gi, kb0, kb1);
+                const int M = args.M, N = args.N;
                 const int m0 = m_blk * Cfg::BMP, n0 = n_blk * BN;
                 const int am = m0 + 128 * (int)rank, bn = n0 + Cfg::BNH * (int)rank;
                 const uint32_t all_bytes = leader ? pair_stage_bytes(args, m0, n0) +
                                                         pair_stage_bytes(args, m0 + 128, n0 + Cfg::BNH)
                                                   : 0u;
                 for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!mbar_wait_bounded_cluster(&empty[stage], phase ^ 1u, args.err,
+                    if (!mbar_wait_bounded_cluster(&empty[stage], phase ^ 1u, err,
                                                    kDevTimeoutEmpty)) {
                         ok = false;
                         break;
@@ -714,16 +766,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     uint8_t* a = sA + stage * Cfg::A_BYTES;
                     uint8_t* b = sB + stage * Cfg::B_BYTES;
                     if (!args.a_mn_major) {
-                        if (am < M) tma_load_2d_pair(a, &tmA, fb, k0, am);
+                        if (am < M) tma_load_2d_pair(a, tmA, fb, k0, am);
                     } else {
-                        if (am < M) tma_load_2d_pair(a, &tmA, fb, am, k0);
-                        if (am + 64 < M) tma_load_2d_pair(a + 8192, &tmA, fb, am + 64, k0);
+                        if (am < M) tma_load_2d_pair(a, tmA, fb, am, k0);
+                        if (am + 64 < M) tma_load_2d_pair(a + 8192, tmA, fb, am + 64, k0);
                     }
                     if (!args.b_mn_major) {
-                        if (bn < N) tma_load_2d_pair(b, &tmB, fb, k0, bn);
+                        if (bn < N) tma_load_2d_pair(b, tmB, fb, k0, bn);
                     } else {
-                        if (bn < N) tma_load_2d_pair(b, &tmB, fb, bn, k0);
-                        if (bn + 64 < N) tma_load_2d_pair(b + 8192, &tmB, fb, bn + 64, k0);
+                        if (bn < N) tma_load_2d_pair(b, tmB, fb, bn, k0);
+                        if (bn + 64 < N) tma_load_2d_pair(b + 8192, tmB, fb, bn + 64, k0);
                     }
                     if (++stage == STAGES) {
                         stage = 0;
@@ -736,18 +788,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     } else if (warp == 1) {
         if (lane == 0 && leader) {
             // ---------------- MMA issuer (leader only)
-            const uint32_t idesc = make_idesc_bf16(Cfg::BMP, BN, args.a_mn_major, args.b_mn_major);
             const uint32_t acc_full_peer = mapa_shared(smem_u32(&acc_full[0]), 1);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
-            for (int t = cid; t < total && ok; t += nclusters) {
-                int m_blk, n_blk, split, g, kb0, kb1;
-                tile_work(args, s_grp, t, num_m, num_n, tiles_mn, kblocks, m_blk, n_blk, split, g,
-                          kb0, kb1);
-                if (!mbar_wait_bounded_cluster(&acc_empty[acc], acc_phase ^ 1u, args.err,
+            int g, t;
+            for (int i = 0; ok && pair_item(P, cid, nclusters, i, g, t); ++i) {
+                const GemmArgs& args = P.args[g];
+                const PairShape sh = pair_shape(args);
+                const uint32_t idesc =
+                    make_idesc_bf16(Cfg::BMP, BN, args.a_mn_major, args.b_mn_major);
+                int m_blk, n_blk, split, gi, kb0, kb1;
+                tile_work(args, s_grp, t, sh.num_m, sh.num_n, sh.tiles_mn, sh.kblocks, m_blk,
+                          n_blk, split, gi, kb0, kb1);
+                if (!mbar_wait_bounded_cluster(&acc_empty[acc], acc_phase ^ 1u, err,
                                                kDevTimeoutAccFree)) {
                     ok = false;
                     break;
@@ -755,8 +811,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(acc * BN);
                 for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!mbar_wait_bounded_cluster(&full[stage], phase, args.err,
-                                                   kDevTimeoutFull)) {
+                    if (!mbar_wait_bounded_cluster(&full[stage], phase, err, kDevTimeoutFull)) {
                         ok = false;
                         break;
                     }
@@ -797,18 +852,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         EpiWarp ew{sEpi + q * 2 * kEpiSlotBytes, &epi_bar[q], 0u, 0};
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int t = cid; t < total; t += nclusters) {
-            int m_blk, n_blk, split, g, kb0, kb1;
-            tile_work(args, s_grp, t, num_m, num_n, tiles_mn, kblocks, m_blk, n_blk, split, g,
-                      kb0, kb1);
+        int g, t;
+        for (int i = 0; pair_item(P, cid, nclusters, i, g, t); ++i) {
+            const GemmArgs& args = P.args[g];
+            const PairShape sh = pair_shape(args);
+            int m_blk, n_blk, split, gi, kb0, kb1;
+            tile_work(args, s_grp, t, sh.num_m, sh.num_n, sh.tiles_mn, sh.kblocks, m_blk, n_blk,
+                      split, gi, kb0, kb1);
             const int m0 = m_blk * Cfg::BMP + 128 * (int)rank, n0 = n_blk * BN;
-            if (!mbar_wait_bounded_cluster(&acc_full[acc], acc_phase, args.err, kDevTimeoutAcc))
-                break;
+            if (!mbar_wait_bounded_cluster(&acc_full[acc], acc_phase, err, kDevTimeoutAcc)) break;
             tc_fence_after();
             const uint32_t tbase =
                 tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(q * 32) << 16);
-            epilogue_tile<BN>(args, &tmO, &tmX, tbase, kb1 <= kb0, m0 + q * 32, n0, split, g,
-                              lane, ew);
+            epilogue_tile<BN>(args, &P.tmO[g], &P.tmX[g], tbase, kb1 <= kb0, m0 + q * 32, n0,
+                              split, gi, lane, ew);
             tc_fence_before();
             if (leader)
                 mbar_arrive(&acc_empty[acc]);
@@ -990,8 +1047,12 @@ int pair_set_attr() {
     static int rc = -1;
     static std::once_flag once;
     std::call_once(once, [] {
-        rc = cudaFuncSetAttribute(gemm_bf16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)PairCfg::SMEM) == cudaSuccess
+        rc = (cudaFuncSetAttribute(gemm_bf16_pair_kernel<1>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)PairCfg::SMEM) == cudaSuccess &&
+              cudaFuncSetAttribute(gemm_bf16_pair_kernel<2>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)PairCfg::SMEM) == cudaSuccess)
                  ? 0
                  : -10;
     });
@@ -1017,17 +1078,19 @@ int pair_max_clusters(int num_sms) {
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         int c = 0;
-        if (cudaOccupancyMaxActiveClusters(&c, gemm_bf16_pair_kernel, &cfg) == cudaSuccess && c > 0)
+        if (cudaOccupancyMaxActiveClusters(&c, gemm_bf16_pair_kernel<1>, &cfg) == cudaSuccess &&
+            c > 0)
             n = c < n ? c : n;
         cudaGetLastError();
     });
     return n;
 }
 
-int launch_pair(const GemmPlan& p, cudaStream_t stream) {
+template <int NG>
+int launch_pair_params(const PairParams<NG>& P, int grid, cudaStream_t stream) {
     if (pair_set_attr()) return -10;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.grid, 1, 1);
+    cfg.gridDim = dim3(grid, 1, 1);
     cfg.blockDim = dim3(kGemmThreads, 1, 1);
     cfg.dynamicSmemBytes = PairCfg::SMEM;
     cfg.stream = stream;
@@ -1038,10 +1101,21 @@ int launch_pair(const GemmPlan& p, cudaStream_t stream) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, gemm_bf16_pair_kernel, p.tmA, p.tmB, p.tmO, p.tmX, p.args) !=
-        cudaSuccess)
+    if (cudaLaunchKernelEx(&cfg, gemm_bf16_pair_kernel<NG>, P) != cudaSuccess)
         return launch_status();
     return launch_status();
+}
+
+int launch_pair(const GemmPlan& p, cudaStream_t stream) {
+    PairParams<1> P;
+    P.tmA[0] = p.tmA;
+    P.tmB[0] = p.tmB;
+    P.tmO[0] = p.tmO;
+    P.tmX[0] = p.tmX;
+    P.args[0] = p.args;
+    P.sched = nullptr;
+    P.sched_stride = 0;
+    return launch_pair_params<1>(P, p.grid, stream);
 }
 
 }  // namespace
@@ -1156,6 +1230,89 @@ int gemm_make_plan(GemmPlan* plan, const void* A, long long lda, int a_mn_major,
 }
 
 int gemm_pair_slots(int num_sms) { return pair_max_clusters(num_sms); }
+
+// Longest-first list scheduling of the two products' tiles (split units included) over the
+// resident pairs: each tile, longest first, goes to the pair with the least work so far
+// (ties: the lower pair), and every pair runs its tiles in the order they were given.
+// Cost of a tile: its k-blocks plus 4 for pipeline fill and epilogue.
+int gemm_make_plan2(GemmPlan2* plan, const GemmPlan& p0, const GemmPlan& p1, int num_sms) {
+    plan->sched = nullptr;
+    const GemmPlan* ps[2] = {&p0, &p1};
+    struct Unit {
+        int cost, g, t;
+    };
+    std::vector<Unit> units;
+    for (int g = 0; g < 2; ++g) {
+        const GemmArgs& a = ps[g]->args;
+        if (ps[g]->bn != kGemmPairTile || a.grp_mode != kGroupNone) return -50;
+        const int num_m = (a.M + PairCfg::BMP - 1) / PairCfg::BMP;
+        const int num_n = (a.N + PairCfg::BN - 1) / PairCfg::BN;
+        const int kblocks = (a.K + BK - 1) / BK;
+        const int tiles = num_m * num_n * a.splits;
+        if (tiles >= (1 << 24)) return -51;
+        for (int t = 0; t < tiles; ++t) {
+            const int split = t / (num_m * num_n);
+            const int kb0 = (int)((long long)split * kblocks / a.splits);
+            const int kb1 = (int)((long long)(split + 1) * kblocks / a.splits);
+            units.push_back(Unit{kb1 - kb0 + 4, g, t});
+        }
+    }
+    std::stable_sort(units.begin(), units.end(),
+                     [](const Unit& x, const Unit& y) { return x.cost > y.cost; });
+    const int ncl = std::min<int>(pair_max_clusters(num_sms), (int)units.size());
+    std::vector<std::vector<int>> lists(ncl);
+    std::vector<long long> load(ncl, 0);
+    for (const Unit& u : units) {
+        int best = 0;
+        for (int c = 1; c < ncl; ++c)
+            if (load[c] < load[best]) best = c;
+        load[best] += u.cost;
+        lists[best].push_back((u.g << 24) | u.t);
+    }
+    size_t stride = 1;
+    for (const auto& l : lists) stride = std::max(stride, l.size() + 1);
+    std::vector<int> table((size_t)ncl * stride, 0);
+    for (int c = 0; c < ncl; ++c) {
+        table[(size_t)c * stride] = (int)lists[c].size();
+        for (size_t i = 0; i < lists[c].size(); ++i) table[(size_t)c * stride + 1 + i] = lists[c][i];
+    }
+    int* d = nullptr;
+    if (cudaMalloc(&d, table.size() * sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        return -52;
+    }
+    if (cudaMemcpy(d, table.data(), table.size() * sizeof(int), cudaMemcpyHostToDevice) !=
+        cudaSuccess) {
+        cudaFree(d);
+        cudaGetLastError();
+        return -53;
+    }
+    plan->p[0] = p0;
+    plan->p[1] = p1;
+    plan->sched = d;
+    plan->sched_stride = (int)stride;
+    plan->grid = 2 * ncl;
+    return 0;
+}
+
+int gemm_run2(const GemmPlan2& plan, cudaStream_t stream) {
+    PairParams<2> P;
+    for (int g = 0; g < 2; ++g) {
+        P.tmA[g] = plan.p[g].tmA;
+        P.tmB[g] = plan.p[g].tmB;
+        P.tmO[g] = plan.p[g].tmO;
+        P.tmX[g] = plan.p[g].tmX;
+        P.args[g] = plan.p[g].args;
+    }
+    P.sched = plan.sched;
+    P.sched_stride = plan.sched_stride;
+    return launch_pair_params<2>(P, plan.grid, stream);
+}
+
+void gemm_free_plan2(GemmPlan2* plan) {
+    if (plan->sched) cudaFree(plan->sched);
+    plan->sched = nullptr;
+}
 
 int gemm_run(const GemmPlan& p, cudaStream_t stream) {
     switch (p.bn) {

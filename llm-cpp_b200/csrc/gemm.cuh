@@ -90,6 +90,21 @@ int gemm_run(const GemmPlan& plan, cudaStream_t stream);
 // CTA pairs of the pair-tile kernel that can be resident at once.
 int gemm_pair_slots(int num_sms);
 
+// Two independent products in one launch of the pair-tile kernel (both plans bn =
+// kGemmPairTile, ungrouped; split-K partials allowed): the data- and weight-gradient products
+// of a layer, whose tiles alone leave pairs idle in their last wave. The tiles of both,
+// longest first, are spread over the resident pairs by a host-built table (device memory
+// owned by the plan: gemm_free_plan2).
+struct GemmPlan2 {
+    GemmPlan p[2];
+    int grid;
+    int* sched;
+    int sched_stride;
+};
+int gemm_make_plan2(GemmPlan2* plan, const GemmPlan& p0, const GemmPlan& p1, int num_sms);
+int gemm_run2(const GemmPlan2& plan, cudaStream_t stream);
+void gemm_free_plan2(GemmPlan2* plan);
+
 // Reduces split-K partials [splits][M][N] (fp32) into the final output with the
 // same epilogue options as kEpiStoreF32 (accumulate, column grouping).
 int gemm_splitk_reduce(const float* partial, int splits, int M, int N, float* out, long long ldo,

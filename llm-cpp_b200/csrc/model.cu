@@ -212,22 +212,40 @@ int choose_splits(Ctx* c, int M, int N, int K) {
     return best_s;
 }
 
-// GEMM through the per-call-site plan cache.
-int gemm(Ctx* c, const void* A, long long lda, int amn, const void* B, long long ldb, int bmn,
-         int M, int N, int K, GemmArgs a, int splits = 1) {
+// One product at a call site: operands, shape, epilogue and split-K factor; the plan index,
+// final output and stride are filled in by gemm_prepare.
+struct GemmCall {
+    const void* A;
+    long long lda;
+    int amn;
+    const void* B;
+    long long ldb;
+    int bmn;
+    int M, N, K;
+    GemmArgs a;
+    int splits;
+    size_t plan;
+    void* final_out;
+    long long final_ldo;
+};
+
+// Resolves the split-K factor (partials in c->splitws) and the call site's cached plan.
+int gemm_prepare(Ctx* c, GemmCall& g) {
+    GemmArgs& a = g.a;
     a.err = c->d_err;
     a.splits = 1;
-    void* final_out = a.out;
-    const long long final_ldo = a.ldo;
-    if (splits > 1) {
-        if ((size_t)splits * M * N > c->splitws_floats) splits = (int)(c->splitws_floats / ((size_t)M * N));
-        if (splits < 2) splits = 1;
+    g.final_out = a.out;
+    g.final_ldo = a.ldo;
+    if (g.splits > 1) {
+        if ((size_t)g.splits * g.M * g.N > c->splitws_floats)
+            g.splits = (int)(c->splitws_floats / ((size_t)g.M * g.N));
+        if (g.splits < 2) g.splits = 1;
     }
-    if (splits > 1) {
+    if (g.splits > 1) {
         a.epi = kEpiSplitPartial;
         a.out = c->splitws;
-        a.ldo = N;
-        a.splits = splits;
+        a.ldo = g.N;
+        a.splits = g.splits;
     }
     struct Key {
         const void *A, *B;
@@ -236,15 +254,15 @@ int gemm(Ctx* c, const void* A, long long lda, int amn, const void* B, long long
         GemmArgs args;
     } key;
     std::memset(&key, 0, sizeof(key));
-    key.A = A;
-    key.B = B;
-    key.lda = lda;
-    key.ldb = ldb;
-    key.amn = amn;
-    key.bmn = bmn;
-    key.M = M;
-    key.N = N;
-    key.K = K;
+    key.A = g.A;
+    key.B = g.B;
+    key.lda = g.lda;
+    key.ldb = g.ldb;
+    key.amn = g.amn;
+    key.bmn = g.bmn;
+    key.M = g.M;
+    key.N = g.N;
+    key.K = g.K;
     key.args = a;
     std::vector<uint8_t> kb(sizeof(Key));
     std::memcpy(kb.data(), &key, sizeof(Key));
@@ -254,38 +272,91 @@ int gemm(Ctx* c, const void* A, long long lda, int amn, const void* B, long long
         c->plan_keys.resize(i + 1);
     }
     if (c->plan_keys[i] != kb) {
-        int rc = gemm_make_plan(&c->plan_cache[i], A, lda, amn, B, ldb, bmn, M, N, K, a, 0,
-                                c->num_sms);
+        int rc = gemm_make_plan(&c->plan_cache[i], g.A, g.lda, g.amn, g.B, g.ldb, g.bmn, g.M, g.N,
+                                g.K, a, 0, c->num_sms);
         if (rc) {
-            c->err = "gemm_make_plan failed (" + std::to_string(rc) + ") M=" + std::to_string(M) +
-                     " N=" + std::to_string(N) + " K=" + std::to_string(K);
+            c->err = "gemm_make_plan failed (" + std::to_string(rc) + ") M=" +
+                     std::to_string(g.M) + " N=" + std::to_string(g.N) +
+                     " K=" + std::to_string(g.K);
             c->plan_keys[i].clear();
             return LLMGPU_E_ARG;
         }
         c->plan_keys[i] = kb;
     }
-    if (c->profile) {
-        if (c->prof_ev.size() < 2 * (c->prof_n + 1)) {
-            cudaEvent_t e0, e1;
-            cudaEventCreate(&e0);
-            cudaEventCreate(&e1);
-            c->prof_ev.push_back(e0);
-            c->prof_ev.push_back(e1);
-            c->prof_flops.push_back(0);
-        }
-        c->prof_flops[c->prof_n] = 2.0 * M * N * (double)K;
-        cudaEventRecord(c->prof_ev[2 * c->prof_n], c->stream);
+    g.plan = i;
+    return 0;
+}
+
+void prof_begin(Ctx* c, double flops) {
+    if (!c->profile) return;
+    if (c->prof_ev.size() < 2 * (c->prof_n + 1)) {
+        cudaEvent_t e0, e1;
+        cudaEventCreate(&e0);
+        cudaEventCreate(&e1);
+        c->prof_ev.push_back(e0);
+        c->prof_ev.push_back(e1);
+        c->prof_flops.push_back(0);
     }
-    KC(gemm_run(c->plan_cache[i], c->stream));
-    if (c->profile) {
-        cudaEventRecord(c->prof_ev[2 * c->prof_n + 1], c->stream);
-        c->prof_n++;
+    c->prof_flops[c->prof_n] = flops;
+    cudaEventRecord(c->prof_ev[2 * c->prof_n], c->stream);
+}
+void prof_end(Ctx* c) {
+    if (!c->profile) return;
+    cudaEventRecord(c->prof_ev[2 * c->prof_n + 1], c->stream);
+    c->prof_n++;
+}
+
+int gemm_finish(Ctx* c, const GemmCall& g) {
+    if (g.splits > 1)
+        KC(gemm_splitk_reduce(c->splitws, g.splits, g.M, g.N,
+                              reinterpret_cast<float*>(g.final_out), g.final_ldo,
+                              g.a.col_group > 0 ? g.a.col_group : g.N, g.a.group_stride,
+                              g.a.accumulate, c->stream));
+    return 0;
+}
+
+// GEMM through the per-call-site plan cache.
+int gemm(Ctx* c, const void* A, long long lda, int amn, const void* B, long long ldb, int bmn,
+         int M, int N, int K, GemmArgs a, int splits = 1) {
+    GemmCall g{A, lda, amn, B, ldb, bmn, M, N, K, a, splits, 0, nullptr, 0};
+    int rc = gemm_prepare(c, g);
+    if (rc) return rc;
+    prof_begin(c, 2.0 * M * N * (double)K);
+    KC(gemm_run(c->plan_cache[g.plan], c->stream));
+    prof_end(c);
+    return gemm_finish(c, g);
+}
+
+// The data- and weight-gradient products of one layer (independent: both read the upstream
+// gradient) in one launch of the pair kernel, their tiles balanced over all pairs. Falls back
+// to two launches when either plan is not on pair tiles. At most one of them may split K.
+int gemm_dual(Ctx* c, GemmCall g0, GemmCall g1) {
+    int rc;
+    if ((rc = gemm_prepare(c, g0)) || (rc = gemm_prepare(c, g1))) return rc;
+    if (g0.splits > 1 && g1.splits > 1) return LLMGPU_E_ARG;  // one split-K workspace
+    const size_t i = c->plan2_cursor++;
+    if (i >= c->plan2_cache.size()) {
+        c->plan2_cache.resize(i + 1);
+        c->plan2_keys.resize(i + 1);
+        c->plan2_ok.resize(i + 1, 0);
     }
-    if (splits > 1) {
-        KC(gemm_splitk_reduce(c->splitws, splits, M, N, reinterpret_cast<float*>(final_out),
-                              final_ldo, a.col_group > 0 ? a.col_group : N, a.group_stride,
-                              a.accumulate, c->stream));
+    std::vector<uint8_t> key = c->plan_keys[g0.plan];
+    key.insert(key.end(), c->plan_keys[g1.plan].begin(), c->plan_keys[g1.plan].end());
+    if (c->plan2_keys[i] != key) {
+        gemm_free_plan2(&c->plan2_cache[i]);
+        c->plan2_ok[i] = gemm_make_plan2(&c->plan2_cache[i], c->plan_cache[g0.plan],
+                                         c->plan_cache[g1.plan], c->num_sms) == 0;
+        c->plan2_keys[i] = key;
     }
+    prof_begin(c, 2.0 * g0.M * g0.N * (double)g0.K + 2.0 * g1.M * g1.N * (double)g1.K);
+    if (c->plan2_ok[i]) {
+        KC(gemm_run2(c->plan2_cache[i], c->stream));
+    } else {
+        KC(gemm_run(c->plan_cache[g0.plan], c->stream));
+        KC(gemm_run(c->plan_cache[g1.plan], c->stream));
+    }
+    prof_end(c);
+    if ((rc = gemm_finish(c, g0)) || (rc = gemm_finish(c, g1))) return rc;
     return 0;
 }
 
@@ -701,6 +772,7 @@ void ctx_destroy(Ctx* c) {
     }
     F(c->xL); F(c->lnf); F(c->meanf); F(c->rstdf); F(c->logits); F(c->dres); F(c->dy);
     F(c->dln); F(c->dres16); F(c->dy16); F(c->datt); F(c->dqkv); F(c->dh); F(c->dvec);
+    for (auto& p2 : c->plan2_cache) gemm_free_plan2(&p2);
     F(c->partial); F(c->colwork); F(c->splitws); F(c->d_tokens); F(c->d_keys);
     F(c->dact); F(c->rope);
     for (auto& m : c->mact) {
@@ -1076,19 +1148,20 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
     if (tied) {
         GemmArgs w = epi_args(kEpiStoreF32, gp(c->i_wte), C);
         w.accumulate = acc;
-        if ((rc = gemm(c, c->logits, Vp, 1, c->lnf, C, 1, V, C, BT, w,
-                       choose_splits(c, V, C, BT))))
-            return rc;
-        if ((rc = gemm(c, c->logits, Vp, 0, c->wte16, C, 1, BT, C, Vp,
-                       epi_args(kEpiStoreF32, c->dln, C))))
+        if ((rc = gemm_dual(c,
+                            GemmCall{c->logits, Vp, 1, c->lnf, C, 1, V, C, BT, w,
+                                     choose_splits(c, V, C, BT)},
+                            GemmCall{c->logits, Vp, 0, c->wte16, C, 1, BT, C, Vp,
+                                     epi_args(kEpiStoreF32, c->dln, C), 1})))
             return rc;
     } else {
         GemmArgs w = epi_args(kEpiStoreF32, gp(c->i_lm), V);
         w.accumulate = acc;
-        if ((rc = gemm(c, c->lnf, C, 1, c->logits, Vp, 1, C, V, BT, w, choose_splits(c, C, V, BT))))
-            return rc;
-        if ((rc = gemm(c, c->logits, Vp, 0, c->lm16, Vp, 0, BT, C, Vp,
-                       epi_args(kEpiStoreF32, c->dln, C))))
+        if ((rc = gemm_dual(c,
+                            GemmCall{c->lnf, C, 1, c->logits, Vp, 1, C, V, BT, w,
+                                     choose_splits(c, C, V, BT)},
+                            GemmCall{c->logits, Vp, 0, c->lm16, Vp, 0, BT, C, Vp,
+                                     epi_args(kEpiStoreF32, c->dln, C), 1})))
             return rc;
         if (!acc) CK(cudaMemsetAsync(gp(c->i_wte), 0, sizeof(float) * c->params[c->i_wte].numel, s));
     }
@@ -1107,19 +1180,20 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
             continue;
         }
         // ---- FFN  (src/transformer.cpp:120-183)
-        if (!c->moe) {
+        // Each layer's weight-gradient product runs in one launch with its data-gradient
+        // product (both read the same upstream gradient).
+        auto dw2 = [&]() {
             GemmArgs w2 = epi_args(kEpiStoreF32, gp(b.W2), C);
             w2.accumulate = acc;
-            if ((rc = gemm(c, a.act, F, 1, c->dres16, C, 1, F, C, BT, w2,
-                           choose_splits(c, F, C, BT))))
-                return rc;
-        }
+            return GemmCall{a.act, F, 1, c->dres16, C, 1, F, C, BT, w2, choose_splits(c, F, C, BT)};
+        };
         if (c->moe) {
             if ((rc = moe_backward_ffn(c, l, B, T, acc))) return rc;
         } else if (c->swiglu) {  // src/transformer.cpp:41-119
             // dgated = dY W2^T, then dh13 = [dh1 | dh3]
-            if ((rc = gemm(c, c->dres16, C, 0, c->w2_16[l], C, 0, BT, F, C,
-                           epi_args(kEpiStoreBF16, c->dact, F))))
+            if ((rc = gemm_dual(c, dw2(),
+                                GemmCall{c->dres16, C, 0, c->w2_16[l], C, 0, BT, F, C,
+                                         epi_args(kEpiStoreBF16, c->dact, F), 1})))
                 return rc;
             KC(swiglu_backward(c->dact, a.h, c->dh, BT, F, s));
             // dW1 | dW3 from one GEMM, written into the two parameter gradients
@@ -1127,26 +1201,29 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
             w13.accumulate = acc;
             w13.col_group = F;
             w13.group_stride = c->params[b.W3].offset - c->params[b.W1].offset;
-            if ((rc = gemm(c, a.ln2, C, 1, c->dh, 2 * F, 1, C, 2 * F, BT, w13,
-                           choose_splits(c, C, 2 * F, BT))))
+            if ((rc = gemm_dual(c,
+                                GemmCall{a.ln2, C, 1, c->dh, 2 * F, 1, C, 2 * F, BT, w13,
+                                         choose_splits(c, C, 2 * F, BT)},
+                                GemmCall{c->dh, 2 * F, 0, c->w1_16[l], 2 * F, 0, BT, C, 2 * F,
+                                         epi_args(kEpiStoreF32, c->dln, C), 1})))
                 return rc;
             KC(colsum_bf16(c->dh, 2 * F, BT, F, gp(b.b1), acc, c->colwork, s));  // db1 = sum dh1
-            if ((rc = gemm(c, c->dh, 2 * F, 0, c->w1_16[l], 2 * F, 0, BT, C, 2 * F,
-                           epi_args(kEpiStoreF32, c->dln, C))))
-                return rc;
         } else {
             GemmArgs dg = epi_args(kEpiDGeluBF16, c->dh, F);
             dg.aux = a.h;
             dg.ld_aux = F;
-            if ((rc = gemm(c, c->dres16, C, 0, c->w2_16[l], C, 0, BT, F, C, dg))) return rc;
+            if ((rc = gemm_dual(c, dw2(),
+                                GemmCall{c->dres16, C, 0, c->w2_16[l], C, 0, BT, F, C, dg, 1})))
+                return rc;
             GemmArgs w1 = epi_args(kEpiStoreF32, gp(b.W1), F);
             w1.accumulate = acc;
-            if ((rc = gemm(c, a.ln2, C, 1, c->dh, F, 1, C, F, BT, w1, choose_splits(c, C, F, BT))))
+            if ((rc = gemm_dual(c,
+                                GemmCall{a.ln2, C, 1, c->dh, F, 1, C, F, BT, w1,
+                                         choose_splits(c, C, F, BT)},
+                                GemmCall{c->dh, F, 0, c->w1_16[l], F, 0, BT, C, F,
+                                         epi_args(kEpiStoreF32, c->dln, C), 1})))
                 return rc;
             KC(colsum_bf16(c->dh, F, BT, F, gp(b.b1), acc, c->colwork, s));
-            if ((rc = gemm(c, c->dh, F, 0, c->w1_16[l], F, 0, BT, C, F,
-                           epi_args(kEpiStoreF32, c->dln, C))))
-                return rc;
         }
         KC(norm_backward(c->dln, a.y, pp(b.ln2g), a.mean2, a.rstd2, c->dres, c->dy, c->dy16,
                          c->partial, BT, C, rms, &nparts, s));
@@ -1155,10 +1232,11 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
         // ---- attention  (src/attention.cpp:183-363)
         GemmArgs wo = epi_args(kEpiStoreF32, gp(b.Wo), C);
         wo.accumulate = acc;
-        if ((rc = gemm(c, a.att, C, 1, c->dy16, C, 1, C, C, BT, wo, choose_splits(c, C, C, BT))))
-            return rc;
-        if ((rc = gemm(c, c->dy16, C, 0, c->wo16[l], C, 0, BT, C, C,
-                       epi_args(kEpiStoreBF16, c->datt, C))))
+        if ((rc = gemm_dual(c,
+                            GemmCall{a.att, C, 1, c->dy16, C, 1, C, C, BT, wo,
+                                     choose_splits(c, C, C, BT)},
+                            GemmCall{c->dy16, C, 0, c->wo16[l], C, 0, BT, C, C,
+                                     epi_args(kEpiStoreBF16, c->datt, C), 1})))
             return rc;
         if (c->rope && hd == 64) {  // q, k were rotated in place: rotate dq, dk back
             KC(attention_backward(a.qkv, a.att, c->datt, a.lse, c->dvec, c->dqkv, B, T, H, hd,
@@ -1172,11 +1250,11 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
         wq.accumulate = acc;
         wq.col_group = C;
         wq.group_stride = c->params[b.Wk].offset - c->params[b.Wq].offset;
-        if ((rc = gemm(c, a.ln1, C, 1, c->dqkv, 3 * C, 1, C, 3 * C, BT, wq,
-                       choose_splits(c, C, 3 * C, BT))))
-            return rc;
-        if ((rc = gemm(c, c->dqkv, 3 * C, 0, c->wqkv16[l], 3 * C, 0, BT, C, 3 * C,
-                       epi_args(kEpiStoreF32, c->dln, C))))
+        if ((rc = gemm_dual(c,
+                            GemmCall{a.ln1, C, 1, c->dqkv, 3 * C, 1, C, 3 * C, BT, wq,
+                                     choose_splits(c, C, 3 * C, BT)},
+                            GemmCall{c->dqkv, 3 * C, 0, c->wqkv16[l], 3 * C, 0, BT, C, 3 * C,
+                                     epi_args(kEpiStoreF32, c->dln, C), 1})))
             return rc;
         KC(norm_backward(c->dln, a.x, pp(b.ln1g), a.mean1, a.rstd1, c->dy, c->dres, c->dres16,
                          c->partial, BT, C, rms, &nparts, s));

@@ -177,6 +177,10 @@ struct Ctx {
     std::vector<GemmPlan> plan_cache;
     std::vector<std::vector<uint8_t>> plan_keys;
     size_t plan_cursor = 0;
+    std::vector<GemmPlan2> plan2_cache;  // co-scheduled data/weight-gradient products
+    std::vector<std::vector<uint8_t>> plan2_keys;
+    std::vector<char> plan2_ok;
+    size_t plan2_cursor = 0;
 
     // GEMM profiling (events around each GEMM launch)
     bool profile = false;
