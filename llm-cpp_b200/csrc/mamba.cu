@@ -17,7 +17,6 @@ namespace llmgpu {
 
 namespace {
 
-constexpr int kWarps = 8;
 
 __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
 __device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + __expf(-v)); }
@@ -71,20 +70,25 @@ __global__ void conv_fwd_kernel(const bf16* __restrict__ proj, long long ldp, in
 }
 
 // ---------------------------------------------------------------- scan staging
-// A block owns CPB = kWarps * 32 / L consecutive channels of one sequence. Time runs in
-// chunks of kScanChunk steps; the block loads a chunk's per-(step, channel) inputs and its
-// per-(step, state) B and C into shared memory with coalesced row segments, double
-// buffered: the loads of the next chunk are issued into registers before the recurrence of
-// the current one runs, so the serial part of the scan never waits on global memory.
-template <int L>
+// A block of kScanWarps warps owns CPB = kScanWarps * 32 / L consecutive channels of one
+// sequence; the L lanes of a channel hold S states each (state n*S + s in lane n), so
+// d_state 16 runs as 8 lanes x 2 states and all (sequence, channel) pairs of a Mamba layer
+// fit on the GPU at once. Time runs in chunks of kScanChunk steps; the block loads a chunk's
+// per-(step, channel) inputs and its per-(step, state) B and C into shared memory with
+// coalesced row segments, double buffered: the loads of the next chunk are issued into
+// registers before the recurrence of the current one runs, so the serial part of the scan
+// never waits on global memory.
+constexpr int kScanWarps = 4;
+template <int L, int S>
 struct ScanTile {
-    static constexpr int kThreads = kWarps * 32;
+    static constexpr int kThreads = kScanWarps * 32;
     static constexpr int kCPW = 32 / L;                 // channels per warp
-    static constexpr int kCPB = kWarps * kCPW;          // channels per block
+    static constexpr int kCPB = kScanWarps * kCPW;      // channels per block
+    static constexpr int kNS = L * S;                   // state slots per channel
     static constexpr int kTC = kScanChunk;              // steps per chunk
     static constexpr int kEPT = kTC * kCPB / kThreads;  // (step, channel) slots per thread
+    static constexpr int kBPT = (kTC * kNS + kThreads - 1) / kThreads;  // (step, state) slots
     static_assert(kTC * kCPB % kThreads == 0, "chunk tile must split evenly over the block");
-    static_assert(kTC * L <= kThreads, "one (step, state) slot per thread at most");
     static constexpr int kRow = kCPB + 1;               // padded row: lanes reading one channel
                                                         // at different steps hit distinct banks
 };
@@ -119,27 +123,32 @@ __device__ __forceinline__ void lane_reduce_scatter(float (&v)[M], int n) {
 }
 
 // ---------------------------------------------------------------- scan forward
-template <int L>
-__global__ void __launch_bounds__(kWarps * 32) scan_fwd_kernel(
+template <int L, int S>
+__global__ void __launch_bounds__(kScanWarps * 32) scan_fwd_kernel(
     const float* __restrict__ raw, const float* __restrict__ u, const float* __restrict__ xp,
     long long ldx, const float* __restrict__ alog, const float* __restrict__ dskip,
     const bf16* __restrict__ proj, long long ldp, float* __restrict__ y32,
     bf16* __restrict__ gated, float* __restrict__ hchk, int T, int D, int N, int R) {
-    using G = ScanTile<L>;
+    using G = ScanTile<L, S>;
     constexpr int CPB = G::kCPB, TC = G::kTC, EPT = G::kEPT, NT = G::kThreads, RW = G::kRow;
+    constexpr int NS = G::kNS, BPT = G::kBPT;
     __shared__ float sDt[2][TC][RW], sU[2][TC][RW], sZ[2][TC][RW];
-    __shared__ float sB[2][TC][L], sC[2][TC][L];
+    __shared__ __align__(16) float sB[2][TC][NS], sC[2][TC][NS];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n = lane % L, c = warp * G::kCPW + lane / L;
     const int d0 = blockIdx.x * CPB, d = d0 + c;
     const int b = blockIdx.y;
     const bool chan = d < D;
-    const bool active = chan && n < N;
-    const float A = active ? alog[(long long)d * N + n] : 0.f;
+    float A[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        const int k = n * S + s;
+        A[s] = (chan && k < N) ? alog[(long long)d * N + k] : 0.f;
+    }
     const float Ds = chan ? dskip[d] : 0.f;
     const int nch = (T + TC - 1) / TC;
 
-    float pr[EPT], pu[EPT], pz[EPT], pb = 0.f, pc = 0.f;
+    float pr[EPT], pu[EPT], pz[EPT], pb[BPT], pc[BPT];
     auto fetch = [&](int t0) {
 #pragma unroll
         for (int e = 0; e < EPT; ++e) {
@@ -150,12 +159,13 @@ __global__ void __launch_bounds__(kWarps * 32) scan_fwd_kernel(
             pu[e] = ok ? u[row * D + dd] : 0.f;
             pz[e] = ok ? __bfloat162float(proj[row * ldp + dd]) : 0.f;
         }
-        if (tid < TC * L) {
-            const int i = tid / L, nn = tid % L;
-            const bool ok = t0 + i < T && nn < N;
+#pragma unroll
+        for (int e = 0; e < BPT; ++e) {
+            const int idx = tid + e * NT, i = idx / NS, k = idx % NS;
+            const bool ok = idx < TC * NS && t0 + i < T && k < N;
             const long long row = (long long)b * T + t0 + i;
-            pb = ok ? xp[row * ldx + R + nn] : 0.f;
-            pc = ok ? xp[row * ldx + R + N + nn] : 0.f;
+            pb[e] = ok ? xp[row * ldx + R + k] : 0.f;
+            pc[e] = ok ? xp[row * ldx + R + N + k] : 0.f;
         }
     };
     auto stage = [&](int buf, int t0) {
@@ -167,36 +177,49 @@ __global__ void __launch_bounds__(kWarps * 32) scan_fwd_kernel(
             sU[buf][i][cc] = pu[e];
             sZ[buf][i][cc] = pz[e];
         }
-        if (tid < TC * L) {
-            sB[buf][tid / L][tid % L] = pb;
-            sC[buf][tid / L][tid % L] = pc;
+#pragma unroll
+        for (int e = 0; e < BPT; ++e) {
+            const int idx = tid + e * NT;
+            if (idx < TC * NS) {
+                sB[buf][idx / NS][idx % NS] = pb[e];
+                sC[buf][idx / NS][idx % NS] = pc[e];
+            }
         }
     };
 
     fetch(0);
-    float h = 0.f;
+    float h[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) h[s] = 0.f;
     for (int k = 0; k < nch; ++k) {
         const int buf = k & 1, t0 = k * TC;
         stage(buf, t0);
         __syncthreads();
         if (k + 1 < nch) fetch(t0 + TC);
-        if (active) hchk[(((long long)b * nch + k) * D + d) * N + n] = h;
+#pragma unroll
+        for (int s = 0; s < S; ++s)
+            if (chan && n * S + s < N)
+                hchk[(((long long)b * nch + k) * D + d) * N + n * S + s] = h[s];
         // steps past T were staged as dt = u = B = 0, which leaves h unchanged
         float cs[TC];
 #pragma unroll
         for (int i = 0; i < TC; ++i) {
             const float dt = sDt[buf][i][c], uu = sU[buf][i][c];
-            const float Bv = sB[buf][i][n], Cv = sC[buf][i][n];
-            const float a = __expf(A * dt);
-            h = a * h + Bv * uu * dt;
-            cs[i] = Cv * h;
+            float acc = 0.f;
+#pragma unroll
+            for (int s = 0; s < S; ++s) {
+                const float a = __expf(A[s] * dt);
+                h[s] = a * h[s] + sB[buf][i][n * S + s] * uu * dt;
+                acc += sC[buf][i][n * S + s] * h[s];
+            }
+            cs[i] = acc;
         }
         lane_reduce_scatter<L, TC>(cs, n);
-        using S = LaneSplit<L, TC>;
+        using SP = LaneSplit<L, TC>;
 #pragma unroll
-        for (int j = 0; j < S::kPer; ++j) {
-            const int i = (n / S::kGroup) * S::kPer + j;
-            if (chan && n % S::kGroup == 0 && t0 + i < T) {
+        for (int j = 0; j < SP::kPer; ++j) {
+            const int i = (n / SP::kGroup) * SP::kPer + j;
+            if (chan && n % SP::kGroup == 0 && t0 + i < T) {
                 const long long row = (long long)b * T + t0 + i;
                 const float yv = cs[j] + Ds * sU[buf][i][c];
                 y32[row * D + d] = yv;
@@ -207,31 +230,37 @@ __global__ void __launch_bounds__(kWarps * 32) scan_fwd_kernel(
 }
 
 // ---------------------------------------------------------------- scan backward
-template <int L>
-__global__ void __launch_bounds__(kWarps * 32) scan_bwd_kernel(
+template <int L, int S>
+__global__ void __launch_bounds__(kScanWarps * 32) scan_bwd_kernel(
     const float* __restrict__ raw, const float* __restrict__ u, const float* __restrict__ xp,
     long long ldx, const float* __restrict__ alog, const float* __restrict__ dskip,
     const bf16* __restrict__ proj, long long ldp, const float* __restrict__ y32,
     const float* __restrict__ dgated, const float* __restrict__ hchk, float* __restrict__ du,
     float* __restrict__ ddt, bf16* __restrict__ dproj, float* __restrict__ dbc_part,
     float* __restrict__ da_part, float* __restrict__ dd_part, int T, int D, int N, int R) {
-    using G = ScanTile<L>;
+    using G = ScanTile<L, S>;
     constexpr int CPB = G::kCPB, TC = G::kTC, EPT = G::kEPT, NT = G::kThreads, RW = G::kRow;
+    constexpr int NS = G::kNS, BPT = G::kBPT;
     __shared__ float sDt[2][TC][RW], sU[2][TC][RW], sDy[2][TC][RW];
-    __shared__ float sB[2][TC][L], sC[2][TC][L];
-    __shared__ float sPB[kWarps][TC][L], sPC[kWarps][TC][L];
+    __shared__ __align__(16) float sB[2][TC][NS], sC[2][TC][NS];
+    // per-channel dB, dC terms of the chunk, summed over the block's channels after it
+    __shared__ float sPB[TC][CPB][NS], sPC[TC][CPB][NS];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n = lane % L, ci = lane / L, c = warp * G::kCPW + ci;
+    const int n = lane % L, c = warp * G::kCPW + lane / L;
     const int d0 = blockIdx.x * CPB, d = d0 + c;
     const int b = blockIdx.y;
     const bool chan = d < D;
-    const bool active = chan && n < N;
-    const float A = active ? alog[(long long)d * N + n] : 0.f;
+    float A[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        const int k = n * S + s;
+        A[s] = (chan && k < N) ? alog[(long long)d * N + k] : 0.f;
+    }
     const float Ds = chan ? dskip[d] : 0.f;
     const int nch = (T + TC - 1) / TC;
     const long long BT = (long long)gridDim.y * T;
 
-    float pr[EPT], pu[EPT], pg[EPT], pz[EPT], py[EPT], pb = 0.f, pc = 0.f;
+    float pr[EPT], pu[EPT], pg[EPT], pz[EPT], py[EPT], pb[BPT], pc[BPT];
     auto fetch = [&](int t0) {
 #pragma unroll
         for (int e = 0; e < EPT; ++e) {
@@ -244,12 +273,13 @@ __global__ void __launch_bounds__(kWarps * 32) scan_bwd_kernel(
             pz[e] = ok ? __bfloat162float(proj[row * ldp + dd]) : 0.f;
             py[e] = ok ? y32[row * D + dd] : 0.f;
         }
-        if (tid < TC * L) {
-            const int i = tid / L, nn = tid % L;
-            const bool ok = t0 + i < T && nn < N;
+#pragma unroll
+        for (int e = 0; e < BPT; ++e) {
+            const int idx = tid + e * NT, i = idx / NS, k = idx % NS;
+            const bool ok = idx < TC * NS && t0 + i < T && k < N;
             const long long row = (long long)b * T + t0 + i;
-            pb = ok ? xp[row * ldx + R + nn] : 0.f;
-            pc = ok ? xp[row * ldx + R + N + nn] : 0.f;
+            pb[e] = ok ? xp[row * ldx + R + k] : 0.f;
+            pc[e] = ok ? xp[row * ldx + R + N + k] : 0.f;
         }
     };
     // also writes the x_z gradient, which needs no scan state
@@ -266,86 +296,93 @@ __global__ void __launch_bounds__(kWarps * 32) scan_bwd_kernel(
                 dproj[row * ldp + d0 + cc] = __float2bfloat16_rn(pg[e] * py[e] * silu_grad_f(pz[e]));
             }
         }
-        if (tid < TC * L) {
-            sB[buf][tid / L][tid % L] = pb;
-            sC[buf][tid / L][tid % L] = pc;
+#pragma unroll
+        for (int e = 0; e < BPT; ++e) {
+            const int idx = tid + e * NT;
+            if (idx < TC * NS) {
+                sB[buf][idx / NS][idx % NS] = pb[e];
+                sC[buf][idx / NS][idx % NS] = pc[e];
+            }
         }
     };
 
-    float dh_next = 0.f, dA_acc = 0.f, dD_acc = 0.f;
+    float dh_next[S], dA_acc[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) dh_next[s] = dA_acc[s] = 0.f;
+    float dD_acc = 0.f;
     fetch((nch - 1) * TC);
     for (int k = nch - 1; k >= 0; --k) {
         const int buf = k & 1, t0 = k * TC;
         stage(buf, t0);
         __syncthreads();
         if (k > 0) fetch(t0 - TC);
-        // the chunk's states, recomputed from the one saved at its start
-        const float h_start = active ? hchk[(((long long)b * nch + k) * D + d) * N + n] : 0.f;
-        // Steps past T were staged as dt = u = B = C = dy = 0: h and dh pass through them
-        // unchanged and they add nothing to dA, dD, dB or dC; their du and ddt are not stored.
-        float hs[TC];
-        float h = h_start;
+        // the chunk's states, recomputed from the ones saved at its start. Steps past T
+        // were staged as dt = u = B = C = dy = 0: h and dh pass through them unchanged and
+        // they add nothing to dA, dD, dB or dC; their du and ddt are not stored.
+        float h_start[S], hs[S][TC];
 #pragma unroll
-        for (int i = 0; i < TC; ++i) {
-            const float dt = sDt[buf][i][c];
-            h = __expf(A * dt) * h + sB[buf][i][n] * sU[buf][i][c] * dt;
-            hs[i] = h;
+        for (int s = 0; s < S; ++s) {
+            const int kk = n * S + s;
+            h_start[s] = (chan && kk < N) ? hchk[(((long long)b * nch + k) * D + d) * N + kk] : 0.f;
+            float h = h_start[s];
+#pragma unroll
+            for (int i = 0; i < TC; ++i) {
+                const float dt = sDt[buf][i][c];
+                h = __expf(A[s] * dt) * h + sB[buf][i][n * S + s] * sU[buf][i][c] * dt;
+                hs[s][i] = h;
+            }
         }
         // the reverse pass in two halves of the chunk, each reduced over the lanes at its end
         constexpr int HS = TC / 2;
-        using S = LaneSplit<L, HS>;
+        using SP = LaneSplit<L, HS>;
 #pragma unroll
         for (int half = 1; half >= 0; --half) {
-        float du_c[HS], ddt_c[HS];
+            float du_c[HS], ddt_c[HS];
 #pragma unroll
-        for (int j = HS - 1; j >= 0; --j) {
-            const int i = half * HS + j;
-            const float dyv = sDy[buf][i][c], uu = sU[buf][i][c], dt_t = sDt[buf][i][c];
-            const float Bv = sB[buf][i][n], Cv = sC[buf][i][n];
-            const float a_t = __expf(A * dt_t);
-            const float h_t = hs[i];
-            const float h_prev = i > 0 ? hs[i - 1] : h_start;
-            const float dh = dh_next + dyv * Cv;
-            float dC_c = dyv * h_t;
-            float dB_c = dh * uu * dt_t;
-            du_c[j] = dh * Bv * dt_t;
-            ddt_c[j] = dh * h_prev * a_t * A + dh * Bv * uu;
-            dA_acc += dh * h_prev * a_t * dt_t;
-            dD_acc += dyv * uu;
-            dh_next = dh * a_t;
-            // sum this warp's channels for every state n (fixed order)
+            for (int j = HS - 1; j >= 0; --j) {
+                const int i = half * HS + j;
+                const float dyv = sDy[buf][i][c], uu = sU[buf][i][c], dt_t = sDt[buf][i][c];
+                float du_s = 0.f, ddt_s = 0.f;
 #pragma unroll
-            for (int o = L; o < 32; o <<= 1) {
-                dB_c += __shfl_xor_sync(0xffffffffu, dB_c, o);
-                dC_c += __shfl_xor_sync(0xffffffffu, dC_c, o);
+                for (int s = 0; s < S; ++s) {
+                    const float Bv = sB[buf][i][n * S + s], Cv = sC[buf][i][n * S + s];
+                    const float a_t = __expf(A[s] * dt_t);
+                    const float h_t = hs[s][i];
+                    const float h_prev = i > 0 ? hs[s][i - 1] : h_start[s];
+                    const float dh = dh_next[s] + dyv * Cv;
+                    sPC[i][c][n * S + s] = dyv * h_t;
+                    sPB[i][c][n * S + s] = dh * uu * dt_t;
+                    du_s += dh * Bv * dt_t;
+                    ddt_s += dh * h_prev * a_t * A[s] + dh * Bv * uu;
+                    dA_acc[s] += dh * h_prev * a_t * dt_t;
+                    dh_next[s] = dh * a_t;
+                }
+                du_c[j] = du_s;
+                ddt_c[j] = ddt_s;
+                dD_acc += dyv * uu;
             }
-            if (ci == 0) {
-                sPB[warp][i][n] = dB_c;
-                sPC[warp][i][n] = dC_c;
-            }
-        }
-        lane_reduce_scatter<L, HS>(du_c, n);
-        lane_reduce_scatter<L, HS>(ddt_c, n);
+            lane_reduce_scatter<L, HS>(du_c, n);
+            lane_reduce_scatter<L, HS>(ddt_c, n);
 #pragma unroll
-        for (int j = 0; j < S::kPer; ++j) {
-            const int i = half * HS + (n / S::kGroup) * S::kPer + j;
-            if (chan && n % S::kGroup == 0 && t0 + i < T) {
-                const long long row = (long long)b * T + t0 + i;
-                du[row * D + d] = du_c[j] + sDy[buf][i][c] * Ds;
-                ddt[row * D + d] = ddt_c[j];
+            for (int j = 0; j < SP::kPer; ++j) {
+                const int i = half * HS + (n / SP::kGroup) * SP::kPer + j;
+                if (chan && n % SP::kGroup == 0 && t0 + i < T) {
+                    const long long row = (long long)b * T + t0 + i;
+                    du[row * D + d] = du_c[j] + sDy[buf][i][c] * Ds;
+                    ddt[row * D + d] = ddt_c[j];
+                }
             }
-        }
         }
         __syncthreads();
-        // block partial over its warps (fixed order) -> dbc_part[blockIdx.x][2][B*T][N]
+        // block partial over its channels (fixed order) -> dbc_part[blockIdx.x][2][B*T][N]
         for (int kk = tid; kk < TC * N; kk += NT) {
             const int i = kk / N, nn = kk - i * N;
             const int t = t0 + i;
             if (t >= T) continue;
             float sb = 0.f, sc = 0.f;
-            for (int w = 0; w < kWarps; ++w) {
-                sb += sPB[w][i][nn];
-                sc += sPC[w][i][nn];
+            for (int cc = 0; cc < CPB; ++cc) {
+                sb += sPB[i][cc][nn];
+                sc += sPC[i][cc][nn];
             }
             const long long row = (long long)b * T + t;
             float* part = dbc_part + (long long)blockIdx.x * 2 * BT * N;
@@ -353,7 +390,9 @@ __global__ void __launch_bounds__(kWarps * 32) scan_bwd_kernel(
             part[BT * N + row * N + nn] = sc;
         }
     }
-    if (active) da_part[((long long)b * D + d) * N + n] = dA_acc;
+#pragma unroll
+    for (int s = 0; s < S; ++s)
+        if (chan && n * S + s < N) da_part[((long long)b * D + d) * N + n * S + s] = dA_acc[s];
     if (n == 0 && chan) dd_part[(long long)b * D + d] = dD_acc;
 }
 
@@ -629,32 +668,35 @@ __global__ void convert_kernel(const float* __restrict__ src, long long lds, bf1
     dst[r * ldd + c] = __float2bfloat16_rn(src[r * lds + c]);
 }
 
-template <int L>
+template <int L, int S>
 int launch_scan_fwd(const MambaDims& m, const float* raw, const float* u, const float* xp,
                     const float* alog, const float* dskip, const bf16* proj, float* y32,
                     bf16* gated, float* hchk, cudaStream_t s) {
-    constexpr int CPB = kWarps * (32 / L);
+    constexpr int CPB = ScanTile<L, S>::kCPB;
     dim3 grid((m.D + CPB - 1) / CPB, m.B);
-    scan_fwd_kernel<L><<<grid, kWarps * 32, 0, s>>>(raw, u, xp, m.ldx, alog, dskip, proj, m.ldp,
-                                                    y32, gated, hchk, m.T, m.D, m.N, m.R);
+    scan_fwd_kernel<L, S><<<grid, kScanWarps * 32, 0, s>>>(raw, u, xp, m.ldx, alog, dskip, proj,
+                                                           m.ldp, y32, gated, hchk, m.T, m.D,
+                                                           m.N, m.R);
     return launch_status();
 }
 
-template <int L>
+template <int L, int S>
 int launch_scan_bwd(const MambaDims& m, const float* raw, const float* u, const float* xp,
                     const float* alog, const float* dskip, const bf16* proj, const float* y32,
                     const float* dgated, const float* hchk, float* du, float* ddt, bf16* dproj,
                     float* dbc_part, float* da_part, float* dd_part, cudaStream_t s) {
-    constexpr int CPB = kWarps * (32 / L);
+    constexpr int CPB = ScanTile<L, S>::kCPB;
     dim3 grid((m.D + CPB - 1) / CPB, m.B);
-    scan_bwd_kernel<L><<<grid, kWarps * 32, 0, s>>>(raw, u, xp, m.ldx, alog, dskip, proj, m.ldp,
-                                                    y32, dgated, hchk, du, ddt, dproj, dbc_part,
-                                                    da_part, dd_part, m.T, m.D, m.N, m.R);
+    scan_bwd_kernel<L, S><<<grid, kScanWarps * 32, 0, s>>>(
+        raw, u, xp, m.ldx, alog, dskip, proj, m.ldp, y32, dgated, hchk, du, ddt, dproj, dbc_part,
+        da_part, dd_part, m.T, m.D, m.N, m.R);
     return launch_status();
 }
 
-// lanes per channel; d_state up to 16 (the scan's shared staging is sized for it)
-int lanes_for(int N) { return N <= 4 ? 4 : N <= 8 ? 8 : N <= 16 ? 16 : 0; }
+// Scan layout for d_state N: lanes per channel (L) and states per lane (S), L * S >= N;
+// 0 when N is above 16 (the staging is sized for it).
+int scan_layout(int N) { return N <= 4 ? 41 : N <= 8 ? 81 : N <= 16 ? 82 : 0; }
+int scan_cpb(int layout) { return kScanWarps * (32 / (layout / 10)); }
 
 }  // namespace
 
@@ -697,9 +739,9 @@ int convert_f32_bf16(const float* src, long long lds, bf16* dst, long long ldd, 
 }
 
 int mamba_scan_groups(int D, int N) {
-    const int L = lanes_for(N);
-    if (!L) return 0;
-    const int cpb = kWarps * (32 / L);
+    const int layout = scan_layout(N);
+    if (!layout) return 0;
+    const int cpb = scan_cpb(layout);
     return (D + cpb - 1) / cpb;
 }
 int mamba_conv_blocks(long long rows) { return (int)((rows + kConvRows - 1) / kConvRows); }
@@ -750,25 +792,27 @@ int mamba_dt_forward(const MambaDims& m, const float* xp, const float* dt_proj, 
 int mamba_scan_forward(const MambaDims& m, const float* raw, const float* u, const float* xp,
                        const float* alog, const float* dskip, const bf16* proj, float* y32,
                        bf16* gated, float* hchk, cudaStream_t s) {
-    switch (lanes_for(m.N)) {
-        case 4: return launch_scan_fwd<4>(m, raw, u, xp, alog, dskip, proj, y32, gated, hchk, s);
-        case 8: return launch_scan_fwd<8>(m, raw, u, xp, alog, dskip, proj, y32, gated, hchk, s);
-        case 16: return launch_scan_fwd<16>(m, raw, u, xp, alog, dskip, proj, y32, gated, hchk, s);
+#define SF(L, S) launch_scan_fwd<L, S>(m, raw, u, xp, alog, dskip, proj, y32, gated, hchk, s)
+    switch (scan_layout(m.N)) {
+        case 41: return SF(4, 1);
+        case 81: return SF(8, 1);
+        case 82: return SF(8, 2);
         default: return -1;
     }
+#undef SF
 }
 
 int mamba_scan_backward(const MambaDims& m, const float* raw, const float* u, const float* xp,
                         const float* alog, const float* dskip, const bf16* proj, const float* y32,
                         const float* dgated, const float* hchk, float* du, float* ddt, bf16* dproj,
                         float* dbc_part, float* da_part, float* dd_part, cudaStream_t s) {
-#define SB(L)                                                                                 \
-    launch_scan_bwd<L>(m, raw, u, xp, alog, dskip, proj, y32, dgated, hchk, du, ddt, dproj, \
-                       dbc_part, da_part, dd_part, s)
-    switch (lanes_for(m.N)) {
-        case 4: return SB(4);
-        case 8: return SB(8);
-        case 16: return SB(16);
+#define SB(L, S)                                                                            \
+    launch_scan_bwd<L, S>(m, raw, u, xp, alog, dskip, proj, y32, dgated, hchk, du, ddt, dproj, \
+                          dbc_part, da_part, dd_part, s)
+    switch (scan_layout(m.N)) {
+        case 41: return SB(4, 1);
+        case 81: return SB(8, 1);
+        case 82: return SB(8, 2);
         default: return -1;
     }
 #undef SB

@@ -884,12 +884,13 @@ int mamba_backward_layer(Ctx* c, int l, int B, int T, int acc) {
     const MambaDims md = mamba_dims(c, B, T);
     int rc;
     // out = x + gated out_proj^T: dgated = dY out_proj, dout_proj = dY^T gated
-    if ((rc = gemm(c, c->dres16, C, 0, c->out16[l], D, 1, BT, D, C,
-                   epi_args(kEpiStoreF32, c->m_dgated, D))))
-        return rc;
     GemmArgs wo = epi_args(kEpiStoreF32, gp(b.out_proj), D);
     wo.accumulate = acc;
-    if ((rc = gemm(c, c->dres16, C, 1, m.gated, D, 1, C, D, BT, wo, choose_splits(c, C, D, BT))))
+    if ((rc = gemm_dual(c,
+                        GemmCall{c->dres16, C, 0, c->out16[l], D, 1, BT, D, C,
+                                 epi_args(kEpiStoreF32, c->m_dgated, D), 1},
+                        GemmCall{c->dres16, C, 1, m.gated, D, 1, C, D, BT, wo,
+                                 choose_splits(c, C, D, BT)})))
         return rc;
     // gate + scan backward (dx_z goes straight into dproj[:, 0:D])
     KC(mamba_scan_backward(md, m.raw, m.u32, m.xp, pp(b.a_log), pp(b.dskip), m.proj, m.y,
@@ -910,25 +911,25 @@ int mamba_backward_layer(Ctx* c, int l, int B, int T, int acc) {
     KC(small_gemm_f32(draw, 1, D, m.xp, c->mRPp, 1, D, R, BT, kSgSplitCols, c->m_sgpart,
                       gp(b.dt_proj), nullptr, R, acc, s));
     // x_proj (src/mamba.cpp:330-347)
-    if ((rc = gemm(c, c->m_dxp, c->mRPp, 0, c->xproj16[l], D, 1, BT, D, c->mRP,
-                   epi_args(kEpiStoreF32, c->m_duxp, D))))
-        return rc;
     GemmArgs wx = epi_args(kEpiStoreF32, gp(b.x_proj), D);
     wx.accumulate = acc;
-    if ((rc = gemm(c, c->m_dxp, c->mRPp, 1, m.u16, D, 1, c->mRP, D, BT, wx,
-                   choose_splits(c, c->mRP, D, BT))))
+    if ((rc = gemm_dual(c,
+                        GemmCall{c->m_dxp, c->mRPp, 0, c->xproj16[l], D, 1, BT, D, c->mRP,
+                                 epi_args(kEpiStoreF32, c->m_duxp, D), 1},
+                        GemmCall{c->m_dxp, c->mRPp, 1, m.u16, D, 1, c->mRP, D, BT, wx,
+                                 choose_splits(c, c->mRP, D, BT)})))
         return rc;
     // SiLU + causal conv backward; dx_ssm into dproj[:, D:2D] (src/mamba.cpp:348-371)
     KC(mamba_conv_backward(md, m.proj, pp(b.conv_w), pp(b.conv_b), c->m_du, c->m_duxp,
                            c->m_convpart, c->m_dproj, gp(b.conv_w), gp(b.conv_b), acc, s));
     // in_proj (src/mamba.cpp:379-396)
-    if ((rc = gemm(c, c->m_dproj, 2 * D, 0, c->in16[l], C, 1, BT, C, 2 * D,
-                   epi_args(kEpiStoreF32, c->dln, C))))
-        return rc;
     GemmArgs wi = epi_args(kEpiStoreF32, gp(b.in_proj), C);
     wi.accumulate = acc;
-    if ((rc = gemm(c, c->m_dproj, 2 * D, 1, a.ln1, C, 1, 2 * D, C, BT, wi,
-                   choose_splits(c, 2 * D, C, BT))))
+    if ((rc = gemm_dual(c,
+                        GemmCall{c->m_dproj, 2 * D, 0, c->in16[l], C, 1, BT, C, 2 * D,
+                                 epi_args(kEpiStoreF32, c->dln, C), 1},
+                        GemmCall{c->m_dproj, 2 * D, 1, a.ln1, C, 1, 2 * D, C, BT, wi,
+                                 choose_splits(c, 2 * D, C, BT)})))
         return rc;
     // norm backward + residual (src/mamba.cpp:397-412); updates c->dres in place
     int nparts = 0;
