@@ -30,9 +30,10 @@ __device__ __forceinline__ float clamp_dt(float sp) { return fminf(fmaxf(sp, 0.0
 // ---------------------------------------------------------------- conv forward
 // pre[t,d] = b[d] + sum_j w[d,j] x[t-(K-1)+j, d] within each sequence; u = silu(pre).
 // A thread owns one channel over a run of kConvRows rows and slides a K-row window of x
-// down it, so each x is read once; the rows of a run are independent loads, the unrolled
-// loop keeps several in flight. Taps that reach before the sequence start are skipped.
+// down it, so each x is read once; the loads of kConvBatch rows are issued together before
+// their arithmetic. Taps that reach before the sequence start are skipped.
 constexpr int kConvRows = 64;
+constexpr int kConvBatch = 8;
 template <int K>
 __global__ void conv_fwd_kernel(const bf16* __restrict__ proj, long long ldp, int D, int T,
                                 const float* __restrict__ w, const float* __restrict__ bias,
@@ -52,20 +53,28 @@ __global__ void conv_fwd_kernel(const bf16* __restrict__ proj, long long ldp, in
         win[j] = t - back >= 0 ? __bfloat162float(proj[(r0 - back) * ldp + D + d]) : 0.f;
     }
     const bf16* xs = proj + r0 * ldp + D + d;
-#pragma unroll 8
-    for (int r = 0; r < nr; ++r) {
-        win[K - 1] = __bfloat162float(xs[(long long)r * ldp]);
-        float acc = bs;
+    for (int rb = 0; rb < nr; rb += kConvBatch) {
+        float xg[kConvBatch];
 #pragma unroll
-        for (int j = 0; j < K; ++j)
-            if (t >= K - 1 - j) acc += wk[j] * win[j];
-        const float uv = silu_f(acc);
-        const long long i = (r0 + r) * D + d;
-        u32[i] = uv;
-        u16[i] = __float2bfloat16_rn(uv);
+        for (int q = 0; q < kConvBatch; ++q)
+            xg[q] = rb + q < nr ? __bfloat162float(xs[(long long)(rb + q) * ldp]) : 0.f;
 #pragma unroll
-        for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
-        t = t + 1 == T ? 0 : t + 1;
+        for (int q = 0; q < kConvBatch; ++q) {
+            win[K - 1] = xg[q];
+            float acc = bs;
+#pragma unroll
+            for (int j = 0; j < K; ++j)
+                if (t >= K - 1 - j) acc += wk[j] * win[j];
+            if (rb + q < nr) {
+                const float uv = silu_f(acc);
+                const long long i = (r0 + rb + q) * D + d;
+                u32[i] = uv;
+                u16[i] = __float2bfloat16_rn(uv);
+            }
+#pragma unroll
+            for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
+            t = t + 1 == T ? 0 : t + 1;
+        }
     }
 }
 
@@ -231,17 +240,20 @@ __global__ void __launch_bounds__(kScanWarps * 32) scan_fwd_kernel(
 
 // ---------------------------------------------------------------- scan backward
 template <int L, int S>
-__global__ void __launch_bounds__(kScanWarps * 32) scan_bwd_kernel(
+__global__ void __launch_bounds__(kScanWarps * 32, 3) scan_bwd_kernel(
     const float* __restrict__ raw, const float* __restrict__ u, const float* __restrict__ xp,
     long long ldx, const float* __restrict__ alog, const float* __restrict__ dskip,
     const bf16* __restrict__ proj, long long ldp, const float* __restrict__ y32,
     const float* __restrict__ dgated, const float* __restrict__ hchk, float* __restrict__ du,
-    float* __restrict__ ddt, bf16* __restrict__ dproj, float* __restrict__ dbc_part,
+    float* __restrict__ draw, bf16* __restrict__ dproj, float* __restrict__ dbc_part,
     float* __restrict__ da_part, float* __restrict__ dd_part, int T, int D, int N, int R) {
     using G = ScanTile<L, S>;
     constexpr int CPB = G::kCPB, TC = G::kTC, EPT = G::kEPT, NT = G::kThreads, RW = G::kRow;
     constexpr int NS = G::kNS, BPT = G::kBPT;
     __shared__ float sDt[2][TC][RW], sU[2][TC][RW], sDy[2][TC][RW];
+    // d(dt)/d(dt_raw): sigmoid(dt_raw) where softplus(dt_raw) lies inside the clamp, else 0
+    // (src/mamba.cpp:318-328)
+    __shared__ float sDf[2][TC][RW];
     __shared__ __align__(16) float sB[2][TC][NS], sC[2][TC][NS];
     // per-channel dB, dC terms of the chunk, summed over the block's channels after it
     __shared__ float sPB[TC][CPB][NS], sPC[TC][CPB][NS];
@@ -288,7 +300,9 @@ __global__ void __launch_bounds__(kScanWarps * 32) scan_bwd_kernel(
         for (int e = 0; e < EPT; ++e) {
             const int idx = tid + e * NT, i = idx / CPB, cc = idx % CPB;
             const bool ok = t0 + i < T && d0 + cc < D;
-            sDt[buf][i][cc] = ok ? clamp_dt(softplus_f(pr[e])) : 0.f;
+            const float sp = softplus_f(pr[e]);
+            sDt[buf][i][cc] = ok ? clamp_dt(sp) : 0.f;
+            sDf[buf][i][cc] = (ok && sp >= 0.001f && sp <= 0.1f) ? sigmoid_f(pr[e]) : 0.f;
             sU[buf][i][cc] = pu[e];
             sDy[buf][i][cc] = pg[e] * silu_f(pz[e]);      // d(loss)/d(y)
             if (ok) {
@@ -369,7 +383,7 @@ __global__ void __launch_bounds__(kScanWarps * 32) scan_bwd_kernel(
                 if (chan && n % SP::kGroup == 0 && t0 + i < T) {
                     const long long row = (long long)b * T + t0 + i;
                     du[row * D + d] = du_c[j] + sDy[buf][i][c] * Ds;
-                    ddt[row * D + d] = ddt_c[j];
+                    draw[row * D + d] = ddt_c[j] * sDf[buf][i][c];
                 }
             }
         }
@@ -422,16 +436,6 @@ __global__ void batch_reduce_kernel(const float* __restrict__ part, int B, long 
     out[j] = accumulate ? out[j] + s : s;
 }
 
-// draw = ddt * [1e-3 <= softplus(raw) <= 0.1] * sigmoid(raw)   (src/mamba.cpp:318-328)
-__global__ void dt_bwd_kernel(const float* __restrict__ ddt, const float* __restrict__ raw,
-                              bf16* __restrict__ draw, long long n) {
-    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const float r = raw[i];
-    const float sp = softplus_f(r);
-    const float in = (sp >= 0.001f && sp <= 0.1f) ? 1.f : 0.f;
-    draw[i] = __float2bfloat16_rn(ddt[i] * in * sigmoid_f(r));
-}
 
 // conv backward, fused: g = (du_scan + du_xp) * silu'(pre) with pre recomputed from the x
 // window; per-run partial sums of dconv_b and dconv_w; and dx_ssm[t,d] =
@@ -467,41 +471,51 @@ __global__ void conv_bwd_kernel(const bf16* __restrict__ proj, long long ldp, in
 #pragma unroll
     for (int j = 0; j < K; ++j) sw[j] = 0.f;
     const bf16* xs = proj + r0 * ldp + D + d;
-#pragma unroll 4
-    for (int r = 0; r < nr + K - 1; ++r) {
-        const bool in = r < nh;
-        xw[K - 1] = in ? __bfloat162float(xs[(long long)r * ldp]) : 0.f;
-        const long long i = (r0 + r) * D + d;
-        float pre = bs;
+    for (int rb = 0; rb < nr + K - 1; rb += kConvBatch) {
+        float xg[kConvBatch], gg[kConvBatch];
 #pragma unroll
-        for (int j = 0; j < K; ++j)
-            if (tp >= K - 1 - j) pre += wk[j] * xw[j];
-        const float g = in ? (du1[i] + du2[i]) * silu_grad_f(pre) : 0.f;
-        if (r < nr) {
-            sb += g;
+        for (int q = 0; q < kConvBatch; ++q) {
+            const bool in = rb + q < nh;
+            const long long i = (r0 + rb + q) * D + d;
+            xg[q] = in ? __bfloat162float(xs[(long long)(rb + q) * ldp]) : 0.f;
+            gg[q] = in ? du1[i] + du2[i] : 0.f;
+        }
+#pragma unroll
+        for (int q = 0; q < kConvBatch; ++q) {
+            const int r = rb + q;
+            if (r >= nr + K - 1) break;
+            xw[K - 1] = xg[q];
+            float pre = bs;
 #pragma unroll
             for (int j = 0; j < K; ++j)
-                if (tp >= K - 1 - j) sw[j] += g * xw[j];
-        }
-        // g[row'] enters the window; the row K-1 above row' is now complete
-        gw[K - 1] = g;
-        const int rr = r - (K - 1);
-        if (rr >= 0) {
-            float acc = 0.f;
+                if (tp >= K - 1 - j) pre += wk[j] * xw[j];
+            const float g = gg[q] * silu_grad_f(pre);
+            if (r < nr) {
+                sb += g;
 #pragma unroll
-            for (int j = 0; j < K; ++j) {
-                const int f = K - 1 - j;
-                if (tr + f < T) acc += gw[f] * wk[j];
+                for (int j = 0; j < K; ++j)
+                    if (tp >= K - 1 - j) sw[j] += g * xw[j];
             }
-            dproj[(r0 + rr) * ldp + D + d] = __float2bfloat16_rn(acc);
-            tr = tr + 1 == T ? 0 : tr + 1;
-        }
+            // g[row'] enters the window; the row K-1 above row' is now complete
+            gw[K - 1] = g;
+            const int rr = r - (K - 1);
+            if (rr >= 0) {
+                float acc = 0.f;
 #pragma unroll
-        for (int j = 0; j < K - 1; ++j) {
-            xw[j] = xw[j + 1];
-            gw[j] = gw[j + 1];
+                for (int j = 0; j < K; ++j) {
+                    const int f = K - 1 - j;
+                    if (tr + f < T) acc += gw[f] * wk[j];
+                }
+                dproj[(r0 + rr) * ldp + D + d] = __float2bfloat16_rn(acc);
+                tr = tr + 1 == T ? 0 : tr + 1;
+            }
+#pragma unroll
+            for (int j = 0; j < K - 1; ++j) {
+                xw[j] = xw[j + 1];
+                gw[j] = gw[j + 1];
+            }
+            tp = tp + 1 == T ? 0 : tp + 1;
         }
-        tp = tp + 1 == T ? 0 : tp + 1;
     }
     float* p = part + ((long long)blockIdx.y * D + d) * (K + 1);
     p[0] = sb;
@@ -521,16 +535,6 @@ __global__ void conv_reduce_kernel(const float* __restrict__ part, int nblk, int
     *o = accumulate ? *o + s : s;
 }
 
-// draw = ddt * [1e-3 <= softplus(raw) <= 0.1] * sigmoid(raw), kept in fp32
-__global__ void dt_bwd_f32_kernel(const float* __restrict__ ddt, const float* __restrict__ raw,
-                                  float* __restrict__ draw, long long n) {
-    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const float r = raw[i];
-    const float sp = softplus_f(r);
-    const float in = (sp >= 0.001f && sp <= 0.1f) ? 1.f : 0.f;
-    draw[i] = ddt[i] * in * sigmoid_f(r);
-}
 
 // fp32 GEMM on the CUDA cores for the dt_rank-wide contractions of the dt path (the clamp
 // mask after softplus needs fp32 operands): C = A B with A(m,k) = A[m*sam + k*sak] and
@@ -622,10 +626,18 @@ __global__ void __launch_bounds__(256) sgemm_f32_kernel(
         buf ^= 1;
     }
     const bool split = gridDim.z > 1;
+    // whole 4-column groups of a plain fp32 output go out as one 16-byte store
+    const bool vec = TN == 4 && !split && !out16 && !accumulate && n0 + tx * 4 + 4 <= N &&
+                     (ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
         const int m = m0 + ty * TM + i;
         if (m >= M) continue;
+        if (vec) {
+            *reinterpret_cast<float4*>(out + (long long)m * ldo + n0 + tx * 4) =
+                make_float4(acc[i][0], acc[i][1 % TN], acc[i][2 % TN], acc[i][3 % TN]);
+            continue;
+        }
 #pragma unroll
         for (int j = 0; j < TN; ++j) {
             const int n = n0 + tx * TN + j;
@@ -683,12 +695,12 @@ int launch_scan_fwd(const MambaDims& m, const float* raw, const float* u, const 
 template <int L, int S>
 int launch_scan_bwd(const MambaDims& m, const float* raw, const float* u, const float* xp,
                     const float* alog, const float* dskip, const bf16* proj, const float* y32,
-                    const float* dgated, const float* hchk, float* du, float* ddt, bf16* dproj,
+                    const float* dgated, const float* hchk, float* du, float* draw, bf16* dproj,
                     float* dbc_part, float* da_part, float* dd_part, cudaStream_t s) {
     constexpr int CPB = ScanTile<L, S>::kCPB;
     dim3 grid((m.D + CPB - 1) / CPB, m.B);
     scan_bwd_kernel<L, S><<<grid, kScanWarps * 32, 0, s>>>(
-        raw, u, xp, m.ldx, alog, dskip, proj, m.ldp, y32, dgated, hchk, du, ddt, dproj, dbc_part,
+        raw, u, xp, m.ldx, alog, dskip, proj, m.ldp, y32, dgated, hchk, du, draw, dproj, dbc_part,
         da_part, dd_part, m.T, m.D, m.N, m.R);
     return launch_status();
 }
@@ -699,13 +711,6 @@ int scan_layout(int N) { return N <= 4 ? 41 : N <= 8 ? 81 : N <= 16 ? 82 : 0; }
 int scan_cpb(int layout) { return kScanWarps * (32 / (layout / 10)); }
 
 }  // namespace
-
-int mamba_dt_backward_f32(const MambaDims& m, const float* ddt, const float* raw, float* draw,
-                          cudaStream_t s) {
-    const long long n = (long long)m.B * m.T * m.D;
-    dt_bwd_f32_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(ddt, raw, draw, n);
-    return launch_status();
-}
 
 int small_gemm_f32(const float* A, long long sam, long long sak, const float* B, long long sbk,
                    long long sbn, int M, int N, int K, int ksplit, float* part, float* out,
@@ -804,10 +809,10 @@ int mamba_scan_forward(const MambaDims& m, const float* raw, const float* u, con
 
 int mamba_scan_backward(const MambaDims& m, const float* raw, const float* u, const float* xp,
                         const float* alog, const float* dskip, const bf16* proj, const float* y32,
-                        const float* dgated, const float* hchk, float* du, float* ddt, bf16* dproj,
+                        const float* dgated, const float* hchk, float* du, float* draw, bf16* dproj,
                         float* dbc_part, float* da_part, float* dd_part, cudaStream_t s) {
-#define SB(L, S)                                                                            \
-    launch_scan_bwd<L, S>(m, raw, u, xp, alog, dskip, proj, y32, dgated, hchk, du, ddt, dproj, \
+#define SB(L, S)                                                                             \
+    launch_scan_bwd<L, S>(m, raw, u, xp, alog, dskip, proj, y32, dgated, hchk, du, draw, dproj, \
                           dbc_part, da_part, dd_part, s)
     switch (scan_layout(m.N)) {
         case 41: return SB(4, 1);
@@ -828,13 +833,6 @@ int mamba_reduce_dbc(const MambaDims& m, const float* dbc_part, bf16* dxp, cudaS
 int mamba_batch_reduce(const float* part, int B, long long n, float* out, int accumulate,
                        cudaStream_t s) {
     batch_reduce_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(part, B, n, out, accumulate);
-    return launch_status();
-}
-
-int mamba_dt_backward(const MambaDims& m, const float* ddt, const float* raw, bf16* draw,
-                      cudaStream_t s) {
-    const long long n = (long long)m.B * m.T * m.D;
-    dt_bwd_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(ddt, raw, draw, n);
     return launch_status();
 }
 

@@ -29,32 +29,28 @@ int mamba_dt_forward(const MambaDims& m, const float* xp, const float* dt_proj, 
 int mamba_scan_forward(const MambaDims& m, const float* raw, const float* u, const float* xp,
                        const float* alog, const float* dskip, const bf16* proj, float* y32,
                        bf16* gated, float* hchk, cudaStream_t s);
-// dgated: fp32 gradient of the gated output. Writes du (scan + skip part), ddt, the x_z
-// gradient into dproj[:, 0:D], and partials: dbc_part [groups][2][rows][N],
-// da_part [B][D][N], dd_part [B][D].
+// dgated: fp32 gradient of the gated output. Writes du (scan + skip part), draw (the
+// gradient of dt_raw: through the clamp mask and softplus), the x_z gradient into
+// dproj[:, 0:D], and partials: dbc_part [groups][2][rows][N], da_part [B][D][N],
+// dd_part [B][D].
 int mamba_scan_backward(const MambaDims& m, const float* raw, const float* u, const float* xp,
                         const float* alog, const float* dskip, const bf16* proj, const float* y32,
-                        const float* dgated, const float* hchk, float* du, float* ddt, bf16* dproj,
+                        const float* dgated, const float* hchk, float* du, float* draw, bf16* dproj,
                         float* dbc_part, float* da_part, float* dd_part, cudaStream_t s);
 int mamba_reduce_dbc(const MambaDims& m, const float* dbc_part, bf16* dxp, cudaStream_t s);
 int mamba_batch_reduce(const float* part, int B, long long n, float* out, int accumulate,
                        cudaStream_t s);
-int mamba_dt_backward(const MambaDims& m, const float* ddt, const float* raw, bf16* draw,
-                      cudaStream_t s);
 // part: mamba_conv_blocks(rows) * D * (K+1) floats; writes dx_ssm into dproj[:, D:2D]
 int mamba_conv_backward(const MambaDims& m, const bf16* proj, const float* w, const float* bias,
                         const float* du_scan, const float* du_xp, float* part, bf16* dproj,
                         float* gw, float* gb, int accumulate, cudaStream_t s);
 
-// fp32 draw = ddt * clamp-mask * sigmoid(raw)   (src/mamba.cpp:318-328)
-int mamba_dt_backward_f32(const MambaDims& m, const float* ddt, const float* raw, float* draw,
-                          cudaStream_t s);
 // out = A B in fp32 on the CUDA cores (the dt path's contractions), K split `ksplit` ways
 // through `part` (ksplit * M * N floats, unused when ksplit is 1) and reduced in order;
 // writes fp32 `out` (+= if accumulate) or bf16 `out16` when given.
 // A(m,k) = A[m*sam + k*sak], B(k,n) = B[k*sbk + n*sbn].
-constexpr int kSgSplitRows = 4;   // K split of the rows x dt_rank products (K = d_inner)
-constexpr int kSgSplitCols = 32;  // K split of the d_inner x dt_rank product (K = rows)
+constexpr int kSgSplitRows = 8;   // K split of the rows x dt_rank products (K = d_inner)
+constexpr int kSgSplitCols = 64;  // K split of the d_inner x dt_rank product (K = rows)
 int small_gemm_f32(const float* A, long long sam, long long sak, const float* B, long long sbk,
                    long long sbn, int M, int N, int K, int ksplit, float* part, float* out,
                    bf16* out16, long long ldo, int accumulate, cudaStream_t s);

@@ -610,13 +610,13 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
         }
         const int groups = mamba_scan_groups(c->mD, c->mN);
         if (dalloc(c, &c->m_dgated, (size_t)BT * D) || dalloc(c, &c->m_du, (size_t)BT * D) ||
-            dalloc(c, &c->m_ddt, (size_t)BT * D) || dalloc(c, &c->m_duxp, (size_t)BT * D) ||
+            dalloc(c, &c->m_duxp, (size_t)BT * D) ||
             dalloc(c, &c->m_dpre, (size_t)BT * D) ||
             dalloc(c, &c->m_dbc, (size_t)groups * 2 * BT * c->mN) ||
             dalloc(c, &c->m_da, (size_t)max_batch * D * c->mN) ||
             dalloc(c, &c->m_dd, (size_t)max_batch * D) ||
             dalloc(c, &c->m_convpart, (size_t)mamba_conv_blocks(BT) * D * (c->mK + 1)) ||
-            dalloc(c, &c->m_dproj, (size_t)BT * 2 * D) || dalloc(c, &c->m_draw, (size_t)BT * D) ||
+            dalloc(c, &c->m_dproj, (size_t)BT * 2 * D) ||
             dalloc(c, &c->m_dxp, (size_t)BT * c->mRPp) ||
             dalloc(c, &c->m_sgpart,
                    std::max((size_t)kSgSplitRows * BT, (size_t)kSgSplitCols * D) * c->mR))
@@ -779,8 +779,8 @@ void ctx_destroy(Ctx* c) {
         F(m.proj); F(m.u32); F(m.u16); F(m.xp); F(m.xp16); F(m.raw); F(m.y); F(m.gated);
         F(m.hchk);
     }
-    F(c->m_dgated); F(c->m_du); F(c->m_ddt); F(c->m_duxp); F(c->m_dpre); F(c->m_dbc);
-    F(c->m_da); F(c->m_dd); F(c->m_convpart); F(c->m_dproj); F(c->m_draw); F(c->m_dxp);
+    F(c->m_dgated); F(c->m_du); F(c->m_duxp); F(c->m_dpre); F(c->m_dbc);
+    F(c->m_da); F(c->m_dd); F(c->m_convpart); F(c->m_dproj); F(c->m_dxp);
     F(c->m_sgpart);
     for (auto& e : c->moeact) {
         F(e.probs); F(e.idx); F(e.wts); F(e.ssum); F(e.grp); F(e.row_of); F(e.tok_of);
@@ -892,18 +892,17 @@ int mamba_backward_layer(Ctx* c, int l, int B, int T, int acc) {
                         GemmCall{c->dres16, C, 1, m.gated, D, 1, C, D, BT, wo,
                                  choose_splits(c, C, D, BT)})))
         return rc;
-    // gate + scan backward (dx_z goes straight into dproj[:, 0:D])
+    // gate + scan backward (dx_z goes straight into dproj[:, 0:D]); the dt gradient comes out
+    // through the clamp mask and softplus (src/mamba.cpp:310-329) as draw, fp32
+    float* draw = c->m_dpre;
     KC(mamba_scan_backward(md, m.raw, m.u32, m.xp, pp(b.a_log), pp(b.dskip), m.proj, m.y,
-                           c->m_dgated, m.hchk, c->m_du, c->m_ddt, c->m_dproj, c->m_dbc, c->m_da,
+                           c->m_dgated, m.hchk, c->m_du, draw, c->m_dproj, c->m_dbc, c->m_da,
                            c->m_dd, s));
     KC(mamba_batch_reduce(c->m_da, B, (long long)D * c->mN, gp(b.a_log), acc, s));
     KC(mamba_batch_reduce(c->m_dd, B, D, gp(b.dskip), acc, s));
     KC(mamba_reduce_dbc(md, c->m_dbc, c->m_dxp, s));  // dB, dC -> dxp[:, R:R+2N]
-    // dt: clamp mask + softplus backward, then through dt_proj (src/mamba.cpp:310-329)
-    // These two dt_rank-wide contractions are sums with heavy cancellation, so they stay in
-    // fp32 (a bf16 operand costs ~5% on the dt_proj gradient).
-    float* draw = c->m_dpre;  // fp32 scratch of the dt path
-    KC(mamba_dt_backward_f32(md, c->m_ddt, m.raw, draw, s));
+    // draw through dt_proj. These two dt_rank-wide contractions are sums with heavy
+    // cancellation, so they stay in fp32 (a bf16 operand costs ~5% on the dt_proj gradient).
     // dxp[:, :R] = draw dt_proj  ([BT, D] x [D, R]) -> bf16 columns [0, R) of dxp
     KC(small_gemm_f32(draw, D, 1, pp(b.dt_proj), R, 1, BT, R, D, kSgSplitRows, c->m_sgpart,
                       nullptr, c->m_dxp, c->mRPp, 0, s));

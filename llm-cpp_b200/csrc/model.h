@@ -110,10 +110,10 @@ struct Ctx {
     int mD = 0, mN = 0, mR = 0, mK = 0, mRP = 0, mRPp = 0, mRp = 0;
     std::vector<bf16*> in16, xproj16, dtp16, out16;
     std::vector<MambaAct> mact;
-    float *m_dgated = nullptr, *m_du = nullptr, *m_ddt = nullptr, *m_duxp = nullptr,
+    float *m_dgated = nullptr, *m_du = nullptr, *m_duxp = nullptr,
           *m_dpre = nullptr, *m_dbc = nullptr, *m_da = nullptr, *m_dd = nullptr,
           *m_convpart = nullptr, *m_sgpart = nullptr;
-    bf16 *m_dproj = nullptr, *m_draw = nullptr, *m_dxp = nullptr;
+    bf16 *m_dproj = nullptr, *m_dxp = nullptr;
     // MoE FFN: E experts of hidden He = 4C, top-k, expert row capacity cap
     bool moe = false;
     int moe_E = 0, moe_k = 0, moe_He = 0, moe_cap = 0;
