@@ -69,6 +69,28 @@ __global__ void grad_norm_final_kernel(const double* __restrict__ partial, int n
     }
 }
 
+struct AdamHp {
+    float lr, b1, b2, eps, c1, c2, gmul, decay;
+};
+// One element of AdamW (src/optimizer.cpp:54-89): decoupled decay, then the Adam step.
+__device__ __forceinline__ void adam_elem(const AdamHp& h, float& pv, float gv, float& mv,
+                                          float& vv) {
+    gv *= h.gmul;
+    pv -= h.decay * pv;
+    mv = h.b1 * mv + (1.0f - h.b1) * gv;
+    vv = h.b2 * vv + (1.0f - h.b2) * gv * gv;
+    const float mhat = mv / h.c1, vhat = vv / h.c2;
+    pv -= h.lr * mhat / (sqrtf(vhat) + h.eps);
+}
+__device__ __forceinline__ long long shadow_off(const AdamParam& pr, long long k) {
+    if (pr.shadow_ld == pr.cols) return k;
+    const long long r = k / pr.cols;
+    return r * pr.shadow_ld + (k - r * pr.cols);
+}
+
+// A chunk of one parameter per block: 16-byte loads and stores of p, g, m and v (parameter
+// offsets are multiples of 64 floats, chunk starts of 16384), four in flight per thread, and
+// the bf16 shadow written 4 values at a time when its rows keep 4-element groups aligned.
 __global__ void __launch_bounds__(256) adamw_kernel(const AdamParam* __restrict__ params,
                                                     const AdamChunk* __restrict__ chunks,
                                                     float* __restrict__ p,
@@ -79,31 +101,57 @@ __global__ void __launch_bounds__(256) adamw_kernel(const AdamParam* __restrict_
     if (scal[3] != 0.0f) return;  // non-finite gradient: the step is skipped
     const AdamChunk ch = chunks[blockIdx.x];
     const AdamParam pr = params[ch.param];
-    const float lr = hp[0], b1 = hp[1], b2 = hp[2], eps = hp[3], wd = hp[4];
-    const float c1 = hp[5], c2 = hp[6], gmul = hp[7] * scal[1];
-    const float decay = pr.decay ? lr * wd : 0.0f;
+    AdamHp h;
+    h.lr = hp[0];
+    h.b1 = hp[1];
+    h.b2 = hp[2];
+    h.eps = hp[3];
+    h.c1 = hp[5];
+    h.c2 = hp[6];
+    h.gmul = hp[7] * scal[1];
+    h.decay = pr.decay ? hp[0] * hp[4] : 0.0f;
     const long long base = pr.offset + ch.start;
-    for (int i = threadIdx.x; i < ch.len; i += blockDim.x) {
+    const int n4 = ch.len >> 2;
+    const bool vec_shadow = pr.shadow && (pr.cols & 3) == 0 && (pr.shadow_ld & 3) == 0;
+    float4* p4 = reinterpret_cast<float4*>(p + base);
+    const float4* g4 = reinterpret_cast<const float4*>(g + base);
+    float4* m4 = reinterpret_cast<float4*>(m + base);
+    float4* v4 = reinterpret_cast<float4*>(v + base);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        float4 pv = p4[i];
+        const float4 gv = g4[i];
+        float4 mv = m4[i], vv = v4[i];
+        adam_elem(h, pv.x, gv.x, mv.x, vv.x);
+        adam_elem(h, pv.y, gv.y, mv.y, vv.y);
+        adam_elem(h, pv.z, gv.z, mv.z, vv.z);
+        adam_elem(h, pv.w, gv.w, mv.w, vv.w);
+        p4[i] = pv;
+        m4[i] = mv;
+        v4[i] = vv;
+        if (pr.shadow) {
+            const long long k = ch.start + 4LL * i;
+            if (vec_shadow) {
+                uint2 w;
+                w.x = pack_bf16x2(pv.x, pv.y);
+                w.y = pack_bf16x2(pv.z, pv.w);
+                *reinterpret_cast<uint2*>(pr.shadow + shadow_off(pr, k)) = w;
+            } else {
+                pr.shadow[shadow_off(pr, k)] = __float2bfloat16_rn(pv.x);
+                pr.shadow[shadow_off(pr, k + 1)] = __float2bfloat16_rn(pv.y);
+                pr.shadow[shadow_off(pr, k + 2)] = __float2bfloat16_rn(pv.z);
+                pr.shadow[shadow_off(pr, k + 3)] = __float2bfloat16_rn(pv.w);
+            }
+        }
+    }
+    for (int i = 4 * n4 + threadIdx.x; i < ch.len; i += blockDim.x) {
         const long long e = base + i;
-        float pv = p[e];
-        const float gv = g[e] * gmul;
-        pv -= decay * pv;                                   // decoupled decay
-        float mv = b1 * m[e] + (1.0f - b1) * gv;
-        float vv = b2 * v[e] + (1.0f - b2) * gv * gv;
-        const float mhat = mv / c1, vhat = vv / c2;
-        pv -= lr * mhat / (sqrtf(vhat) + eps);
+        float pv = p[e], mv = m[e], vv = v[e];
+        adam_elem(h, pv, g[e], mv, vv);
         p[e] = pv;
         m[e] = mv;
         v[e] = vv;
-        if (pr.shadow) {
-            const long long k = ch.start + i;
-            long long off = k;
-            if (pr.shadow_ld != pr.cols) {
-                const long long r = k / pr.cols;
-                off = r * pr.shadow_ld + (k - r * pr.cols);
-            }
-            pr.shadow[off] = __float2bfloat16_rn(pv);
-        }
+        if (pr.shadow) pr.shadow[shadow_off(pr, ch.start + i)] = __float2bfloat16_rn(pv);
     }
 }
 
