@@ -1,6 +1,6 @@
-// Fused softmax cross-entropy forward + backward over bf16 logits, one CTA per row:
-// the row is read from HBM once into shared memory, the loss is emitted and the
-// row is overwritten in place by dlogits (src/loss.cpp:6-40).
+// Fused softmax cross-entropy forward + backward over bf16 logits: each row is read from
+// HBM once into shared memory, the loss is emitted and the row is overwritten in place by
+// dlogits (src/loss.cpp:6-40).
 #include <cfloat>
 
 #include "common.cuh"
@@ -10,7 +10,7 @@ namespace llmgpu {
 
 namespace {
 
-constexpr int kCeThreads = 512;
+constexpr int kCeThreads = 1024;
 
 __device__ __forceinline__ float block_reduce(float v, float* sh, bool is_max) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -35,63 +35,137 @@ __device__ __forceinline__ float block_reduce(float v, float* sh, bool is_max) {
     return sh[32];
 }
 
-__global__ void __launch_bounds__(kCeThreads) ce_kernel(bf16* __restrict__ logits, int V, int Vp,
-                                                         const int32_t* __restrict__ tokens,
-                                                         float* __restrict__ row_loss, float scale,
-                                                         float smoothing) {
-    extern __shared__ uint4 srow[];  // Vp bf16 (Vp % 8 == 0)
+// Persistent over rows: CTA b takes rows b, b + grid, ... A row (Vp bf16) arrives by one
+// bulk copy into a shared buffer, is overwritten in place by its gradient, and leaves by one
+// bulk store, so the threads only do arithmetic. With two buffers (nbuf 2, rows up to half
+// the shared memory) the next row's copy runs while the current one is computed.
+__global__ void __launch_bounds__(kCeThreads, 1) ce_kernel(bf16* __restrict__ logits, int rows,
+                                                            int V, int Vp,
+                                                            const int32_t* __restrict__ tokens,
+                                                            float* __restrict__ row_loss,
+                                                            float scale, float smoothing,
+                                                            int nbuf, int* err) {
+    extern __shared__ __align__(128) uint8_t ce_smem[];  // nbuf x Vp bf16 (Vp % 8 == 0)
     __shared__ float red[33];
-    const int row = blockIdx.x;
-    uint4* g = reinterpret_cast<uint4*>(logits + (long long)row * Vp);
+    __shared__ float s_tgt;
+    __shared__ __align__(8) uint64_t bar[2];
+    const uint32_t row_bytes = (uint32_t)Vp * 2u;
     const int n8 = Vp >> 3;
-    float mx = -FLT_MAX;
-    for (int i = threadIdx.x; i < n8; i += blockDim.x) {
-        uint4 u = g[i];
-        srow[i] = u;
-        uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int c = i * 8 + 2 * k;
-            if (c < V) mx = fmaxf(mx, bf16_lo(w[k]));
-            if (c + 1 < V) mx = fmaxf(mx, bf16_hi(w[k]));
-        }
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        fence_barrier_init();
     }
-    mx = block_reduce(mx, red, true);
-    float se = 0.f;
-    for (int i = threadIdx.x; i < n8; i += blockDim.x) {
-        uint4 u = srow[i];
-        uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int c = i * 8 + 2 * k;
-            if (c < V) se += __expf(bf16_lo(w[k]) - mx);
-            if (c + 1 < V) se += __expf(bf16_hi(w[k]) - mx);
-        }
+    __syncthreads();
+    int row = blockIdx.x;
+    if (row >= rows) return;
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bar[0], row_bytes);
+        bulk_load_g2s(ce_smem, logits + (long long)row * Vp, row_bytes, &bar[0]);
     }
-    se = block_reduce(se, red, false);
-    const float lse = mx + logf(se);
-    int tgt = tokens[row] % V;
-    if (tgt < 0) tgt += V;
     const float off = (smoothing > 0.f && V > 1) ? smoothing / (float)(V - 1) : 0.f;
     const float on = 1.0f - smoothing;
-    if (threadIdx.x == 0) {
-        const bf16* sb = reinterpret_cast<const bf16*>(srow);
-        row_loss[row] = lse - __bfloat162float(sb[tgt]);
-    }
-    for (int i = threadIdx.x; i < n8; i += blockDim.x) {
-        uint4 u = srow[i];
-        uint32_t w[4] = {u.x, u.y, u.z, u.w};
-        uint32_t o[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int c = i * 8 + 2 * k;
-            float a = 0.f, b = 0.f;
-            if (c < V) a = (__expf(bf16_lo(w[k]) - lse) - (c == tgt ? on : off)) * scale;
-            if (c + 1 < V) b = (__expf(bf16_hi(w[k]) - lse) - (c + 1 == tgt ? on : off)) * scale;
-            o[k] = pack_bf16x2(a, b);
+    for (int it = 0; row < rows; ++it, row += gridDim.x) {
+        const int b = nbuf == 2 ? (it & 1) : 0;
+        uint4* srow = reinterpret_cast<uint4*>(ce_smem + (size_t)b * row_bytes);
+        if (threadIdx.x == 0) {
+            // a buffer is refilled once the gradient store of its previous row has read it
+            const int next = row + gridDim.x;
+            if (nbuf == 2 && next < rows) {
+                bulk_wait_group_read<0>();
+                mbar_arrive_expect_tx(&bar[b ^ 1], row_bytes);
+                bulk_load_g2s(ce_smem + (size_t)(b ^ 1) * row_bytes,
+                              logits + (long long)next * Vp, row_bytes, &bar[b ^ 1]);
+            } else if (nbuf == 1 && it > 0) {
+                bulk_wait_group_read<0>();
+                mbar_arrive_expect_tx(&bar[0], row_bytes);
+                bulk_load_g2s(ce_smem, logits + (long long)row * Vp, row_bytes, &bar[0]);
+            }
         }
-        g[i] = make_uint4(o[0], o[1], o[2], o[3]);
+        mbar_wait_bounded(&bar[b], (uint32_t)(nbuf == 2 ? (it >> 1) & 1 : it & 1), err,
+                          kDevTimeoutFull);
+        int tgt = tokens[row] % V;
+        if (tgt < 0) tgt += V;
+        // groups of 8 columns: [0, nfull) all valid, then at most one partly valid group,
+        // then padding up to Vp
+        const int nfull = V >> 3, nval = (V + 7) >> 3;
+        float mx = -FLT_MAX;
+        for (int i = threadIdx.x; i < nfull; i += blockDim.x) {
+            const uint4 u = srow[i];
+            mx = fmaxf(mx, fmaxf(fmaxf(fmaxf(bf16_lo(u.x), bf16_hi(u.x)),
+                                       fmaxf(bf16_lo(u.y), bf16_hi(u.y))),
+                                 fmaxf(fmaxf(bf16_lo(u.z), bf16_hi(u.z)),
+                                       fmaxf(bf16_lo(u.w), bf16_hi(u.w)))));
+        }
+        if (threadIdx.x == 0 && nval > nfull) {
+            const bf16* t = reinterpret_cast<const bf16*>(srow + nfull);
+            for (int c = nfull * 8; c < V; ++c) mx = fmaxf(mx, __bfloat162float(t[c - nfull * 8]));
+        }
+        if (threadIdx.x == 0) s_tgt = __bfloat162float(reinterpret_cast<const bf16*>(srow)[tgt]);
+        mx = block_reduce(mx, red, true);
+        // exp(x - m) = 2^(x log2e - m log2e)
+        constexpr float kLog2e = 1.4426950408889634f;
+        const float mxl = mx * kLog2e;
+        float se = 0.f;
+        for (int i = threadIdx.x; i < nfull; i += blockDim.x) {
+            const uint4 u = srow[i];
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                se += ex2_approx(fmaf(bf16_lo(w[k]), kLog2e, -mxl)) +
+                      ex2_approx(fmaf(bf16_hi(w[k]), kLog2e, -mxl));
+        }
+        if (threadIdx.x == 0 && nval > nfull) {
+            const bf16* t = reinterpret_cast<const bf16*>(srow + nfull);
+            for (int c = nfull * 8; c < V; ++c)
+                se += ex2_approx(fmaf(__bfloat162float(t[c - nfull * 8]), kLog2e, -mxl));
+        }
+        se = block_reduce(se, red, false);
+        const float lse = mx + logf(se);
+        const float lsel = lse * kLog2e;
+        if (threadIdx.x == 0) row_loss[row] = lse - s_tgt;
+        // dlogits = (softmax - y) * scale; y = off everywhere but `on` at the target, and the
+        // padding columns get 0
+        const float offs = off * scale;
+        for (int i = threadIdx.x; i < n8; i += blockDim.x) {
+            const uint4 u = srow[i];
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+            uint32_t o[4];
+            if (i < nfull) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    o[k] = pack_bf16x2(ex2_approx(fmaf(bf16_lo(w[k]), kLog2e, -lsel)) * scale - offs,
+                                       ex2_approx(fmaf(bf16_hi(w[k]), kLog2e, -lsel)) * scale - offs);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int c = i * 8 + 2 * k;
+                    const float a =
+                        c < V ? ex2_approx(fmaf(bf16_lo(w[k]), kLog2e, -lsel)) * scale - offs : 0.f;
+                    const float bb =
+                        c + 1 < V ? ex2_approx(fmaf(bf16_hi(w[k]), kLog2e, -lsel)) * scale - offs
+                                  : 0.f;
+                    o[k] = pack_bf16x2(a, bb);
+                }
+            }
+            if (i == (tgt >> 3)) {  // the target column takes `on` instead of `off`
+                const int k = (tgt & 7) >> 1;
+                const float x = (tgt & 1) ? bf16_hi(w[k]) : bf16_lo(w[k]);
+                const float gt = (ex2_approx(fmaf(x, kLog2e, -lsel)) - on) * scale;
+                const float lo = (tgt & 1) ? bf16_lo(o[k]) : gt;
+                const float hi = (tgt & 1) ? gt : bf16_hi(o[k]);
+                o[k] = pack_bf16x2(lo, hi);
+            }
+            srow[i] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        fence_proxy_async_smem();  // this thread's gradient writes before the bulk store
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            bulk_store_s2g(logits + (long long)row * Vp, srow, row_bytes);
+            bulk_commit_group();
+        }
     }
+    if (threadIdx.x == 0) bulk_wait_group_all();
 }
 
 __global__ void mean_kernel(const float* __restrict__ v, int n, float* out) {
@@ -105,16 +179,26 @@ __global__ void mean_kernel(const float* __restrict__ v, int n, float* out) {
 }  // namespace
 
 int cross_entropy_fwd_bwd(bf16* logits, int rows, int V, int Vp, const int32_t* tokens,
-                          float* row_loss, float scale, float smoothing, cudaStream_t s) {
-    if ((Vp & 7) != 0 || V > Vp) return -1;
-    const size_t smem = (size_t)Vp * sizeof(bf16);
-    if (smem > 200 * 1024) return -2;
+                          float* row_loss, float scale, float smoothing, cudaStream_t s,
+                          int* err) {
+    if ((Vp & 7) != 0 || V > Vp || rows <= 0) return -1;
+    if ((reinterpret_cast<uintptr_t>(logits) & 15) != 0) return -3;
+    constexpr size_t kMaxSmem = 220 * 1024;
+    const size_t row = (size_t)Vp * sizeof(bf16);
+    if (row > kMaxSmem) return -2;
+    const int nbuf = 2 * row <= kMaxSmem ? 2 : 1;
+    const size_t smem = nbuf * row;
     static bool set = false;
     if (!set) {
-        cudaFuncSetAttribute(ce_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(ce_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
         set = true;
     }
-    ce_kernel<<<rows, kCeThreads, smem, s>>>(logits, V, Vp, tokens, row_loss, scale, smoothing);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = rows < sms ? rows : sms;
+    ce_kernel<<<grid, kCeThreads, smem, s>>>(logits, rows, V, Vp, tokens, row_loss, scale,
+                                             smoothing, nbuf, err);
     return launch_status();
 }
 

@@ -195,6 +195,25 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, ui
         : "memory");
 }
 
+// Contiguous bulk copy global -> this CTA's shared memory (16-byte aligned, size a multiple
+// of 16), completion counted in bytes on `bar`.
+__device__ __forceinline__ void bulk_load_g2s(void* smem_dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes),
+        "r"(smem_u32(bar))
+        : "memory");
+}
+// Contiguous bulk copy of this CTA's shared memory to global memory (16-byte aligned, size a
+// multiple of 16), tracked by the bulk groups.
+__device__ __forceinline__ void bulk_store_s2g(void* gdst, const void* smem_src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                     reinterpret_cast<uint64_t>(gdst)),
+                 "r"(smem_u32(smem_src)), "r"(bytes)
+                 : "memory");
+}
+
 // ---------------------------------------------------------------- TMA stores (epilogues)
 // Shared-memory writes of the generic proxy made visible to the TMA (async proxy).
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -51,9 +51,11 @@ size_t colsum_work_floats(int C);
 // Per row of bf16 logits [rows, Vp] (first V columns valid): loss[row] = lse - logit[tgt],
 // and logits overwritten in place by dlogits = (softmax - y) * scale (0 in padded columns),
 // with y = 1 - smoothing at tgt and smoothing/(V-1) elsewhere (src/loss.cpp:6-40).
-// Targets are tokens mod V (the inputs themselves, src/trainer.cpp:39).
+// Targets are tokens mod V (the inputs themselves, src/trainer.cpp:39). Vp * 4 bytes (two
+// rows) must fit in shared memory; `err` receives a code if a row's copy times out.
 int cross_entropy_fwd_bwd(bf16* logits, int rows, int V, int Vp, const int32_t* tokens,
-                          float* row_loss, float scale, float smoothing, cudaStream_t s);
+                          float* row_loss, float scale, float smoothing, cudaStream_t s,
+                          int* err = nullptr);
 // out[0] = mean of v[0..n) (fixed summation order).
 int mean_reduce(const float* v, int n, float* out, cudaStream_t s);
 

@@ -1136,7 +1136,7 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
     mark(c, 1);
     // ------------------------------------------------------------------ loss
     KC(cross_entropy_fwd_bwd(c->logits, BT, V, Vp, c->d_tokens, c->d_row_loss, 1.0f / (float)BT,
-                             c->smoothing, s));
+                             c->smoothing, s, c->d_err));
     KC(mean_reduce(c->d_row_loss, BT, c->d_out, s));
     if (c->moe) KC(moe_add_aux(c->moe_aux, L, B, c->d_out, s));
     mark(c, 2);

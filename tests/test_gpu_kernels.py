@@ -59,13 +59,15 @@ def test_norm_forward_backward(cuda, rms, C):
     assert _rel(ds, want_dx.sum(0)) < 1e-5
 
 
-@pytest.mark.parametrize("V,Vp", [(256, 256), (50257, 50304), (300, 384)])
-def test_cross_entropy(cuda, V, Vp):
+# rows above the SM count run several rows per CTA through both shared buffers; a row wider
+# than half the shared memory (60032 bf16) takes the single-buffer path
+@pytest.mark.parametrize("V,Vp,rows", [(256, 256, 64), (50257, 50304, 64), (300, 384, 64),
+                                       (50257, 50304, 700), (60001, 60032, 400)])
+def test_cross_entropy(cuda, V, Vp, rows):
     """loss = lse - logit[tgt]; dlogits = (softmax - onehot) * scale, zero in padding
     (src/loss.cpp:6-40); targets are the tokens mod V."""
     from llmgpu import ops
-    g = torch.Generator().manual_seed(V)
-    rows = 64
+    g = torch.Generator().manual_seed(V + rows)
     logits = torch.zeros(rows, Vp)
     logits[:, :V] = torch.randn(rows, V, generator=g) * 2
     l16 = logits.to(torch.bfloat16)
