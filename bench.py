@@ -353,7 +353,8 @@ def main():
             "e2e": {"value": e2e, "unit": "tokens/s", "ms_per_step": ms_e2e,
                     "h2d_bytes_per_step": step_bytes, "d2h_bytes_per_step": 32},
             "gpu_launches": launches,
-            "roofline": {"kernel": "gemm_bf16_tc_kernel (tcgen05, all GEMMs of the step)",
+            "roofline": {"kernel": "tcgen05 GEMMs (gemm_bf16_pair_kernel, gemm_bf16_tc_kernel): "
+                                   "every GEMM launch of the step",
                          "bound": "tensor", "achieved": gemm_tflops, "peak": peak_sus,
                          "unit": "TFLOP/s", "frac": gemm_tflops / peak_sus,
                          "peak_kind": f"{peak_kind} sustained bf16 (kernel timed inside a long step)",
