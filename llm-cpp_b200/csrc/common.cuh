@@ -403,13 +403,20 @@ __device__ __forceinline__ int elect_one_sync() {
 }
 
 // GELU (tanh form) exactly as the reference writes it: sqrt(2/3.14159265).
+// tanh on the special-function unit (PTX tanh.approx.f32: relative error about 2^-11, well
+// inside the bf16 rounding of the GELU epilogues' outputs)
+__device__ __forceinline__ float tanh_approx(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 __device__ __forceinline__ float gelu_tanh(float v) {
     const float k = 0.7978845608f;  // sqrtf(2.0f / 3.14159265f)
-    return 0.5f * v * (1.0f + tanhf(k * (v + 0.044715f * v * v * v)));
+    return 0.5f * v * (1.0f + tanh_approx(k * (v + 0.044715f * v * v * v)));
 }
 __device__ __forceinline__ float gelu_tanh_grad(float v) {
     const float k = 0.7978845608f;
-    float th = tanhf(k * (v + 0.044715f * v * v * v));
+    float th = tanh_approx(k * (v + 0.044715f * v * v * v));
     float sech2 = 1.0f - th * th;
     float inner = k * (1.0f + 3.0f * 0.044715f * v * v);
     return 0.5f * (1.0f + th) + 0.5f * v * sech2 * inner;
