@@ -25,6 +25,10 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kGemmThreads = 256;
+// CTA-pair kernel: warp 0 TMA, warp 1 MMA, warps 4..11 epilogue (two warps per TMEM lane
+// quarter, each draining half of a tile's columns)
+constexpr int kPairThreads = 384;
+constexpr int kPairEpiWarps = 8;
 constexpr int kGroupM = 16;  // tile raster: groups of 16 m-blocks share B tiles in L2
 
 template <int BN>
@@ -226,6 +230,7 @@ __device__ __forceinline__ void epi_store(const GemmArgs& a, int row, int col0, 
 // per-thread row stores of epi_store.
 constexpr int kEpiSlotBytes = 4096;
 constexpr int kEpiStageBytes = 4 * 2 * kEpiSlotBytes;
+constexpr int kPairEpiStageBytes = kPairEpiWarps * 2 * kEpiSlotBytes;
 
 // byte offset of 16-byte chunk `ch` of row r in a box of 128-byte rows (fp32, 128-byte
 // swizzle: chunk ^= row % 8) or 64-byte rows (bf16, 64-byte swizzle: chunk ^= (row / 2) % 4)
@@ -263,9 +268,10 @@ template <int NCOLS>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorMap* tmO,
                                               const CUtensorMap* tmX, uint32_t tbase, bool empty,
                                               int row0, int n0, int split, int g, int lane,
-                                              EpiWarp& w) {
+                                              EpiWarp& w, int c_begin = 0,
+                                              int c_end = NCOLS / 32) {
 #pragma unroll 1
-    for (int c = 0; c < NCOLS / 32; ++c) {
+    for (int c = c_begin; c < c_end; ++c) {
         uint32_t r[32];
         if (!empty) {
             tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), r);
@@ -605,9 +611,9 @@ struct PairCfg {
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BNH * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = 6;
+    static constexpr int STAGES = 5;
     static constexpr uint32_t TMEM_COLS = 2 * BN;
-    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + kEpiStageBytes + 256;
+    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + kPairEpiStageBytes + 256;
 };
 
 // Bytes one CTA of a pair loads per k-block (A rows from am, B rows from bn); boxes wholly
@@ -674,7 +680,7 @@ __device__ __forceinline__ bool pair_item(const PairParams<NG>& P, int cid, int 
 }
 
 template <int NG>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kPairThreads, 1)
     gemm_bf16_pair_kernel(const __grid_constant__ PairParams<NG> P) {
     using Cfg = PairCfg;
     constexpr int STAGES = Cfg::STAGES;
@@ -685,12 +691,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
     uint8_t* sEpi = smem + STAGES * Cfg::STAGE_BYTES;  // 2 boxes per epilogue warp
-    uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kPairEpiStageBytes);
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* epi_bar = acc_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + kPairEpiWarps);
 
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
@@ -707,9 +713,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], 2 * 128);  // the epilogue threads of both CTAs
+            mbar_init(&acc_empty[i], 2 * 32 * kPairEpiWarps);  // epilogue threads, both CTAs
         }
-        for (int i = 0; i < 4; ++i) mbar_init(&epi_bar[i], 1);
+        for (int i = 0; i < kPairEpiWarps; ++i) mbar_init(&epi_bar[i], 1);
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -846,10 +852,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
         }
     } else if (warp >= 4) {
-        // ---------------- epilogue warpgroup (both CTAs)
-        const int q = warp - 4;
+        // ---------------- epilogue warps (both CTAs): warp 4 + e drains TMEM lane quarter
+        // e % 4, columns [half * BN/2, (half + 1) * BN/2) with half = e / 4
+        const int e = warp - 4;
+        const int q = e & 3, half = e >> 2;
         const uint32_t acc_empty_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
-        EpiWarp ew{sEpi + q * 2 * kEpiSlotBytes, &epi_bar[q], 0u, 0};
+        EpiWarp ew{sEpi + e * 2 * kEpiSlotBytes, &epi_bar[e], 0u, 0};
         int acc = 0;
         uint32_t acc_phase = 0;
         int g, t;
@@ -865,7 +873,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t tbase =
                 tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(q * 32) << 16);
             epilogue_tile<BN>(args, &P.tmO[g], &P.tmX[g], tbase, kb1 <= kb0, m0 + q * 32, n0,
-                              split, gi, lane, ew);
+                              split, gi, lane, ew, half * (BN / 64), (half + 1) * (BN / 64));
             tc_fence_before();
             if (leader)
                 mbar_arrive(&acc_empty[acc]);
@@ -1068,7 +1076,7 @@ int pair_max_clusters(int num_sms) {
         if (pair_set_attr()) return;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
-        cfg.blockDim = dim3(kGemmThreads, 1, 1);
+        cfg.blockDim = dim3(kPairThreads, 1, 1);
         cfg.dynamicSmemBytes = PairCfg::SMEM;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1091,7 +1099,7 @@ int launch_pair_params(const PairParams<NG>& P, int grid, cudaStream_t stream) {
     if (pair_set_attr()) return -10;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
-    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.blockDim = dim3(kPairThreads, 1, 1);
     cfg.dynamicSmemBytes = PairCfg::SMEM;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
