@@ -34,15 +34,17 @@ constexpr int kHD = 64;
 constexpr int kTile = kRows * kHD * 2;        // 16 KB: a Q, K or V tile (128 rows x 128 B)
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColS = 0, kColO = 128, kColP = 192;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr float kLn2f = 0.6931471805599453f;
 constexpr float kRescaleLog2 = 8.0f;          // rescale O when the max grows by more than 2^8
+constexpr int kPolyEvery = 4;                 // one pair of exponentials in 4 on the FMA pipe
 
 struct Smem {
     static constexpr int Q = 0;
     static constexpr int K = kTile;           // two K slots
     static constexpr int V = K + 2 * kTile;   // two V slots
-    static constexpr int BAR = V + 2 * kTile;
+    static constexpr int XCH = V + 2 * kTile; // row maxima [2][2][128] and sums [2][128]
+    static constexpr int BAR = XCH + 6 * kRows * 4;
     static constexpr int TOTAL = BAR + 256;
 };
 constexpr size_t kSmemBytes = 1024 + Smem::TOTAL;
@@ -91,8 +93,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             mbar_init(&v_empty[s], 1);
         }
         mbar_init(s_full, 1);
-        mbar_init(s_free, 128);
-        mbar_init(p_full, 128);
+        mbar_init(s_free, 256);
+        mbar_init(p_full, 256);
         mbar_init(pv_done, 1);
         fence_barrier_init();
     }
@@ -174,41 +176,51 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (ok) issue_pv(nkv - 1);
         }
     } else {
-        // ---------------- softmax warps 2-5: thread = query row
-        const int q = warp & 3;
+        // ---------------- softmax warps 2-9: warp w reads TMEM lane quarter w % 4 (one query
+        // row per thread) and column half hf = (w - 2) / 4 of each 128-key score tile; the two
+        // threads of a row exchange their block maxima through shared memory
+        const int q = warp & 3, hf = (warp - 2) >> 2;
         const int row = q * 32 + lane;
         const int qrow = q0 + row;
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        float* sMax = reinterpret_cast<float*>(sm + Smem::XCH);  // [2][128]
+        const int bar_id = 1 + q;   // named barrier of the two warps of lane quarter q
+        constexpr int kHalf = kRows / 2;
         float m_run = -INFINITY, l = 0.f;
+        // Both warps of a quarter take every block's exchange barrier, also after a timed-out
+        // wait (ok false: later waits are skipped and the results are discarded), so neither
+        // can be left waiting at a barrier its partner will not reach.
         bool ok = true;
-        for (int j = 0; j < nkv && ok; ++j) {
-            if (!warp_wait(s_full, j & 1, err, kDevTimeoutAcc)) {
-                ok = false;
-                break;
-            }
+        for (int j = 0; j < nkv; ++j) {
+            if (ok && !warp_wait(s_full, j & 1, err, kDevTimeoutAcc)) ok = false;
             tc_fence_after();
-            uint32_t v[kRows];
+            uint32_t v[kHalf];
 #pragma unroll
-            for (int c = 0; c < kRows / 32; ++c)
-                tmem_ld_32x32b_x32(tmem + lane_base + kColS + c * 32,
+            for (int c = 0; c < kHalf / 32; ++c)
+                tmem_ld_32x32b_x32(tmem + lane_base + kColS + hf * kHalf + c * 32,
                                    *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
             tmem_ld_wait();
             tc_fence_before();
             mbar_arrive(s_free);
-            const int k0 = j * kRows;
-            if ((k0 + kRows - 1 > qrow) || (k0 + kRows > T)) {  // causal / sequence-end mask
+            const int k0 = j * kRows + hf * kHalf;
+            if ((k0 + kHalf - 1 > qrow) || (k0 + kHalf > T)) {  // causal / sequence-end mask
 #pragma unroll
-                for (int i = 0; i < kRows; ++i)
+                for (int i = 0; i < kHalf; ++i)
                     if (k0 + i > qrow || k0 + i >= T) v[i] = __float_as_uint(-INFINITY);
             }
-            // 8 independent partial maxima / sums keep the dependency chains short
+            // 8 independent partial maxima keep the dependency chains short
             float pm[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) pm[u] = __uint_as_float(v[u]);
 #pragma unroll
-            for (int i = 8; i < kRows; ++i) pm[i & 7] = fmaxf(pm[i & 7], __uint_as_float(v[i]));
+            for (int i = 8; i < kHalf; ++i) pm[i & 7] = fmaxf(pm[i & 7], __uint_as_float(v[i]));
             float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
                              fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+            // row maximum over both halves (buffer j & 1: the partner may already be one
+            // block ahead when this thread reads)
+            sMax[((j & 1) * 2 + hf) * kRows + row] = mx;
+            named_barrier_sync(bar_id, 64);
+            mx = fmaxf(mx, sMax[((j & 1) * 2 + (hf ^ 1)) * kRows + row]);
             mx *= scale_log2;
             float alpha = 1.f;
             bool rescale = false;
@@ -219,62 +231,68 @@ __global__ void __launch_bounds__(kThreads, 2)
                 m_run = mx;
                 rescale = true;
             }
-            // P_j = 2^(s * scale - m_run) as bf16 pairs, packed in place of the scores
-            float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            // P_j = 2^(s * scale - m_run) as bf16 pairs, packed in place of the scores; one
+            // pair in kPolyEvery on the FMA pipe (ex2_poly), the rest on the special-function
+            // unit; scale, shift and sum run as packed pairs
+            const float2 sc2 = make_float2(scale_log2, scale_log2);
+            const float2 nm2 = make_float2(-m_run, -m_run);
+            float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                            make_float2(0.f, 0.f)};
 #pragma unroll
-            for (int i = 0; i < kRows / 2; ++i) {
-                const float p0 = ex2_approx(fmaf(__uint_as_float(v[2 * i]), scale_log2, -m_run));
-                const float p1 = ex2_approx(fmaf(__uint_as_float(v[2 * i + 1]), scale_log2, -m_run));
-                ps[i & 7] += p0 + p1;
-                v[i] = pack_bf16x2(p0, p1);
+            for (int i = 0; i < kHalf / 2; ++i) {
+                const float2 x = ffma2(make_float2(__uint_as_float(v[2 * i]),
+                                                   __uint_as_float(v[2 * i + 1])), sc2, nm2);
+                float2 pp;
+                if (i % kPolyEvery == kPolyEvery - 1)
+                    pp = make_float2(ex2_poly(x.x), ex2_poly(x.y));
+                else
+                    pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                ps[i & 3] = fadd2(ps[i & 3], pp);
+                v[i] = pack_bf16x2(pp.x, pp.y);
             }
-            const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+            const float2 s4 = fadd2(fadd2(ps[0], ps[1]), fadd2(ps[2], ps[3]));
+            const float sum = s4.x + s4.y;
             // PV_{j-1} has read the previous P and finished adding into O
-            if (j >= 1 && !warp_wait(pv_done, (j - 1) & 1, err, kDevTimeoutAcc)) {
-                ok = false;
-                break;
-            }
+            if (ok && j >= 1 && !warp_wait(pv_done, (j - 1) & 1, err, kDevTimeoutAcc)) ok = false;
             tc_fence_after();
-            if (__any_sync(0xffffffffu, rescale)) {
+            if (__any_sync(0xffffffffu, rescale)) {  // this half's 32 columns of O
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem + lane_base + kColO + hf * 32, r);
+                tmem_ld_wait();
 #pragma unroll
-                for (int c = 0; c < kHD / 32; ++c) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(tmem + lane_base + kColO + c * 32, r);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-                    tmem_st_32x32b_x32(tmem + lane_base + kColO + c * 32, r);
-                }
+                for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                tmem_st_32x32b_x32(tmem + lane_base + kColO + hf * 32, r);
             }
-            tmem_st_32x32b_x32(tmem + lane_base + kColP, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-            tmem_st_32x32b_x32(tmem + lane_base + kColP + 32,
-                               *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+            tmem_st_32x32b_x32(tmem + lane_base + kColP + hf * 32,
+                               *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
             tmem_st_wait();
             l = l * alpha + sum;
             tc_fence_before();
             mbar_arrive(p_full);
         }
+        // the row's sum over both halves
+        float* sSum = sMax + 4 * kRows;
+        sSum[hf * kRows + row] = l;
+        named_barrier_sync(bar_id, 64);
+        l += sSum[(hf ^ 1) * kRows + row];
         if (ok && warp_wait(pv_done, (nkv - 1) & 1, err, kDevTimeoutAcc)) {
             tc_fence_after();
             const float inv = 1.f / l;
-            bf16* o = out + ((long long)b * T + qrow) * C + h * kHD;
+            bf16* o = out + ((long long)b * T + qrow) * C + h * kHD + hf * 32;
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem + lane_base + kColO + hf * 32, r);
+            tmem_ld_wait();
+            if (qrow < T) {
+                uint4* o4 = reinterpret_cast<uint4*>(o);
 #pragma unroll
-            for (int c = 0; c < kHD / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem + lane_base + kColO + c * 32, r);
-                tmem_ld_wait();
-                if (qrow < T) {
-                    uint4* o4 = reinterpret_cast<uint4*>(o + c * 32);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        o4[i] = make_uint4(
-                            pack_bf16x2(__uint_as_float(r[8 * i]) * inv, __uint_as_float(r[8 * i + 1]) * inv),
-                            pack_bf16x2(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv),
-                            pack_bf16x2(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv),
-                            pack_bf16x2(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv));
-                }
+                for (int i = 0; i < 4; ++i)
+                    o4[i] = make_uint4(
+                        pack_bf16x2(__uint_as_float(r[8 * i]) * inv, __uint_as_float(r[8 * i + 1]) * inv),
+                        pack_bf16x2(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv),
+                        pack_bf16x2(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv),
+                        pack_bf16x2(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv));
+                if (hf == 0) lse[((long long)b * H + h) * T + qrow] = (m_run + log2f(l)) * kLn2f;
             }
-            if (qrow < T) lse[((long long)b * H + h) * T + qrow] = (m_run + log2f(l)) * kLn2f;
         }
     }
 

@@ -185,6 +185,48 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
+// 2^x on the FMA pipe, for softmax kernels whose special-function unit is the bottleneck:
+// x = j + f with j = round(x) (from the mantissa of x + 1.5 * 2^23) and f in [-0.5, 0.5];
+// 2^f by a cubic fitted here to minimise the relative error on that interval (max relative
+// error 7.5e-5); 2^j added to the exponent field. x is clamped below at -126, where the
+// result (about 1e-38) is negligible next to the row maximum's 1.
+__device__ __forceinline__ float ex2_poly(float x) {
+    x = fmaxf(x, -126.0f);
+    const float t = __fadd_rn(x, 12582912.0f);
+    const float f = __fsub_rn(x, __fsub_rn(t, 12582912.0f));
+    const float p = fmaf(fmaf(fmaf(0.055171646f, f, 0.24261113f), f, 0.69326097f), f, 0.99992806f);
+    const int j = __float_as_int(t) - 0x4B400000;
+    return __int_as_float(__float_as_int(p) + (j << 23));
+}
+// Barrier `id` (1..15; 0 is __syncthreads) over `count` threads, a multiple of 32.
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+// Packed fp32 pairs (sm_100 f32x2 instructions: one issue for two lanes of work).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "mov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+        "mov.b64 {%0, %1}, rd;}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
 // 3-D tiled TMA load into this CTA (c2 the outermost coordinate).
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, uint64_t* bar,
                                             int c0, int c1, int c2) {
