@@ -310,11 +310,17 @@ __global__ void __launch_bounds__(kThreads, 2)
 //              SM sub-partition.
 // With P = exp(S * scale - lse) (rows: queries) and D = rowsum(dO o O):
 //   dS = P o (dP - D), dP = dO V^T, dV = P^T dO, dK = scale dS^T Q, dQ = scale dS K.
-// dK/dV kernel (one 128-key tile per CTA, over the query tiles that see it): S^T = K Q^T and
-// dP^T = V dO^T in TMEM; P^T and dS^T (bf16) written back to TMEM feed dV += P^T dO and
-// dK += dS^T Q as A-from-TMEM MMAs. dQ kernel (one query tile per CTA, over key tiles 0..i):
-// S, dP as in the forward, dQ += dS K. The next tile's S / dP MMAs run while the elementwise
-// warps work on the current one; the inputs stream through 3-stage TMA rings.
+// dK/dV kernel (work item: a 128-key tile of one head, over the query tiles that see it):
+// S^T = K Q^T and dP^T = V dO^T in TMEM; P^T and dS^T (bf16) written back to TMEM feed
+// dV += P^T dO and dK += dS^T Q as A-from-TMEM MMAs. dQ kernel (work item: a query tile over
+// key tiles 0..i): S, dP as in the forward, dQ += dS K. The next tile's S / dP MMAs run while
+// the elementwise warps work on the current one; the streamed inputs pass through 3-stage
+// TMA rings.
+// Both kernels are persistent: one CTA per SM walks the work items from the longest (most
+// tiles) down, CTA c taking items c, c + grid, ...; every role counts tiles across items, the
+// fixed tiles of an item (K, V or Q, dO) are double buffered so that the next item's load
+// overlaps the current one, and the next item's first S / dP MMAs run while the current
+// item's accumulators are drained.
 // TMEM (512 columns): S [0,128), dP [128,256), accumulators from 256, bf16 operands after.
 constexpr int kBwdThreads = 320;
 constexpr int kBwdStages = 3;
@@ -322,10 +328,10 @@ constexpr uint32_t kBwdTmem = 512;
 constexpr float kLog2ef = 1.4426950408889634f;
 
 struct BwdSmem {
-    // two resident tiles (K, V or Q, dO), then kBwdStages stages of two streamed tiles
-    // (+ 512-byte lse and D vectors for the dK/dV kernel)
-    static constexpr int FIX0 = 0, FIX1 = kTile;
-    static constexpr int STAGE0 = 2 * kTile;
+    // two buffers of the two fixed tiles (K, V or Q, dO), then kBwdStages stages of two
+    // streamed tiles (+ 512-byte lse and D vectors for the dK/dV kernel)
+    static constexpr int FIX = 0;                  // [buffer][tile]
+    static constexpr int STAGE0 = 4 * kTile;
     static constexpr int STAGE_BYTES = 2 * kTile + 1024;
     static constexpr int BAR = STAGE0 + kBwdStages * STAGE_BYTES;
     static constexpr int TOTAL = BAR + 256;
@@ -342,118 +348,188 @@ __device__ __forceinline__ void store_row64_bf16(bf16* dst, const uint32_t (&r)[
                            pack_bf16x2(__uint_as_float(r[8 * i + 6]) * mul, __uint_as_float(r[8 * i + 7]) * mul));
 }
 
+// Work item `it` of a backward kernel: tile index counted from the longest end (the tile
+// with the most partner tiles first), head and sequence.
+struct BwdItem {
+    int tile, h, b;
+};
+__device__ __forceinline__ BwdItem bwd_item(int it, int H, int B) {
+    const int hb = H * B;
+    BwdItem w;
+    w.tile = it / hb;
+    const int r = it - w.tile * hb;
+    w.h = r % H;
+    w.b = r / H;
+    return w;
+}
+
+// Barriers of a persistent backward kernel.
+struct BwdBars {
+    uint64_t* fix_full;   // [2] fixed tiles of an item loaded
+    uint64_t* fix_empty;  // [2] an item's last MMA reading its fixed tiles done
+    uint64_t* st_full;    // [kBwdStages]
+    uint64_t* st_empty;   // [kBwdStages]
+    uint64_t* s_full;     // S / dP of a tile in TMEM
+    uint64_t* s_free;     // S / dP read by the elementwise warps
+    uint64_t* p_full;     // the tile's bf16 operands written to TMEM
+    uint64_t* mm_done;    // the tile's accumulating MMAs done
+    uint64_t* acc_free;   // an item's accumulators read out of TMEM
+    uint32_t* tmem_slot;
+};
+__device__ __forceinline__ BwdBars bwd_bars(uint8_t* sm) {
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + BwdSmem::BAR);
+    BwdBars r;
+    r.fix_full = bar;
+    r.fix_empty = bar + 2;
+    r.st_full = bar + 4;
+    r.st_empty = r.st_full + kBwdStages;
+    r.s_full = r.st_empty + kBwdStages;
+    r.s_free = r.s_full + 1;
+    r.p_full = r.s_free + 1;
+    r.mm_done = r.p_full + 1;
+    r.acc_free = r.mm_done + 1;
+    r.tmem_slot = reinterpret_cast<uint32_t*>(r.acc_free + 1);
+    return r;
+}
+__device__ __forceinline__ void bwd_init(const BwdBars& k, int acc_readers) {
+    for (int i = 0; i < 2; ++i) {
+        mbar_init(&k.fix_full[i], 1);
+        mbar_init(&k.fix_empty[i], 1);
+    }
+    for (int s = 0; s < kBwdStages; ++s) {
+        mbar_init(&k.st_full[s], 1);
+        mbar_init(&k.st_empty[s], 1);
+    }
+    mbar_init(k.s_full, 1);
+    mbar_init(k.s_free, 256);
+    mbar_init(k.p_full, 256);
+    mbar_init(k.mm_done, 1);
+    mbar_init(k.acc_free, acc_readers);
+    fence_barrier_init();
+}
+
 // ---------------------------------------------------------------- dK / dV
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv,
                             const __grid_constant__ CUtensorMap tm_do,
                             const __grid_constant__ CUtensorMap tm_lse,
                             const __grid_constant__ CUtensorMap tm_d, bf16* __restrict__ dqkv,
-                            int T, int H, float scale, int* __restrict__ err) {
+                            int B, int T, int H, float scale, int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_u32 = smem_u32(smem_raw);
     uint8_t* sm = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + BwdSmem::BAR);
-    uint64_t* kv_full = bar;
-    uint64_t* st_full = bar + 1;                  // [kBwdStages]
-    uint64_t* st_empty = st_full + kBwdStages;    // [kBwdStages]
-    uint64_t* s_full = st_empty + kBwdStages;
-    uint64_t* s_free = s_full + 1;
-    uint64_t* p_full = s_free + 1;
-    uint64_t* mm_done = p_full + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mm_done + 1);
-
-    const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const BwdBars k = bwd_bars(sm);
     const int nqb = (T + kRows - 1) / kRows;
-    const int ns = nqb - kt;                      // query tiles kt..nqb-1 see these keys
+    const int items = nqb * H * B;
     const int C = H * kHD;
-    const int k0 = kt * kRows;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float scale_log2 = scale * kLog2ef;
     constexpr uint32_t kColDV = 256, kColDK = 320, kColP = 384, kColDS = 448;
 
-    if (threadIdx.x == 0) {
-        mbar_init(kv_full, 1);
-        for (int s = 0; s < kBwdStages; ++s) {
-            mbar_init(&st_full[s], 1);
-            mbar_init(&st_empty[s], 1);
-        }
-        mbar_init(s_full, 1);
-        mbar_init(s_free, 256);
-        mbar_init(p_full, 256);
-        mbar_init(mm_done, 1);
-        fence_barrier_init();
-    }
+    if (threadIdx.x == 0) bwd_init(k, 256);
     if (warp == 1) {
-        tmem_alloc(tmem_slot, kBwdTmem);
+        tmem_alloc(k.tmem_slot, kBwdTmem);
         tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-    auto stage = [&](int s) { return sm + BwdSmem::STAGE0 + (s % kBwdStages) * BwdSmem::STAGE_BYTES; };
+    const uint32_t tmem = *k.tmem_slot;
+    auto stage = [&](int g) { return sm + BwdSmem::STAGE0 + (g % kBwdStages) * BwdSmem::STAGE_BYTES; };
+    auto fix = [&](int buf, int t) { return sm + BwdSmem::FIX + (2 * buf + t) * kTile; };
 
     if (warp == 0) {
         if (lane == 0) {
+            // ---------------- TMA producer: K, V of each item, then Q, dO, lse, D per tile
             bool ok = true;
-            mbar_arrive_expect_tx(kv_full, 2 * kTile);
-            tma_load_3d(sm + BwdSmem::FIX0, &tm_qkv, kv_full, C + h * kHD, k0, b);      // K
-            tma_load_3d(sm + BwdSmem::FIX1, &tm_qkv, kv_full, 2 * C + h * kHD, k0, b);  // V
-            for (int s = 0; s < ns && ok; ++s) {
-                const int q0 = (kt + s) * kRows;
-                if (!mbar_wait_bounded(&st_empty[s % kBwdStages], ((s / kBwdStages) & 1) ^ 1u, err,
+            int g = 0;
+            for (int it = blockIdx.x, n = 0; it < items && ok; it += gridDim.x, ++n) {
+                const BwdItem w = bwd_item(it, H, B);
+                const int kt = w.tile, ns = nqb - kt, fb = n & 1;
+                if (!mbar_wait_bounded(&k.fix_empty[fb], ((n >> 1) & 1) ^ 1u, err,
                                        kDevTimeoutEmpty)) {
                     ok = false;
                     break;
                 }
-                uint8_t* st = stage(s);
-                uint64_t* f = &st_full[s % kBwdStages];
-                mbar_arrive_expect_tx(f, 2 * kTile + 1024);
-                tma_load_3d(st, &tm_qkv, f, h * kHD, q0, b);                  // Q_i
-                tma_load_3d(st + kTile, &tm_do, f, h * kHD, q0, b);           // dO_i
-                tma_load_2d(st + 2 * kTile, &tm_lse, f, q0, b * H + h);       // lse_i
-                tma_load_2d(st + 2 * kTile + 512, &tm_d, f, q0, b * H + h);   // D_i
+                mbar_arrive_expect_tx(&k.fix_full[fb], 2 * kTile);
+                tma_load_3d(fix(fb, 0), &tm_qkv, &k.fix_full[fb], C + w.h * kHD, kt * kRows, w.b);
+                tma_load_3d(fix(fb, 1), &tm_qkv, &k.fix_full[fb], 2 * C + w.h * kHD, kt * kRows,
+                            w.b);
+                for (int s = 0; s < ns; ++s, ++g) {
+                    const int q0 = (kt + s) * kRows;
+                    if (!mbar_wait_bounded(&k.st_empty[g % kBwdStages], ((g / kBwdStages) & 1) ^ 1u,
+                                           err, kDevTimeoutEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = stage(g);
+                    uint64_t* f = &k.st_full[g % kBwdStages];
+                    mbar_arrive_expect_tx(f, 2 * kTile + 1024);
+                    tma_load_3d(st, &tm_qkv, f, w.h * kHD, q0, w.b);                  // Q_i
+                    tma_load_3d(st + kTile, &tm_do, f, w.h * kHD, q0, w.b);           // dO_i
+                    tma_load_2d(st + 2 * kTile, &tm_lse, f, q0, w.b * H + w.h);       // lse_i
+                    tma_load_2d(st + 2 * kTile + 512, &tm_d, f, q0, w.b * H + w.h);   // D_i
+                }
             }
             if (!ok) spin_ns(100000);
         }
     } else if (warp == 1) {
         if (lane == 0) {
+            // ---------------- MMA issuer; tiles are counted across items (g), so the next
+            // tile's S^T / dP^T can be issued before the current tile's dV / dK
             const uint32_t idesc_s = make_idesc_bf16(kRows, kRows, 0, 0);
             const uint32_t idesc_acc = make_idesc_bf16(kRows, kHD, 0, 1);
-            const uint32_t k_addr = smem_u32(sm + BwdSmem::FIX0), v_addr = smem_u32(sm + BwdSmem::FIX1);
-            bool ok = mbar_wait_bounded(kv_full, 0, err, kDevTimeoutFull);
-            auto issue_sdp = [&](int s) -> bool {
-                if (!mbar_wait_bounded(&st_full[s % kBwdStages], (s / kBwdStages) & 1, err,
+            bool ok = true;
+            // issue S^T = K Q^T and dP^T = V dO^T of tile g (item slot n, tile s of ns)
+            auto issue_sdp = [&](int g, int n, int s, int ns) -> bool {
+                const int fb = n & 1;
+                if (s == 0 && !mbar_wait_bounded(&k.fix_full[fb], (n >> 1) & 1, err, kDevTimeoutFull))
+                    return false;
+                if (!mbar_wait_bounded(&k.st_full[g % kBwdStages], (g / kBwdStages) & 1, err,
                                        kDevTimeoutFull))
                     return false;
                 tc_fence_after();
-                const uint32_t q_addr = smem_u32(stage(s)), do_addr = q_addr + kTile;
+                const uint32_t k_addr = smem_u32(fix(fb, 0)), v_addr = smem_u32(fix(fb, 1));
+                const uint32_t q_addr = smem_u32(stage(g)), do_addr = q_addr + kTile;
 #pragma unroll
-                for (int kk = 0; kk < kHD / 16; ++kk)  // S^T = K Q^T
+                for (int kk = 0; kk < kHD / 16; ++kk)
                     umma_bf16(tmem, make_sw128_desc(k_addr + kk * 32, 16, 1024),
                               make_sw128_desc(q_addr + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
 #pragma unroll
-                for (int kk = 0; kk < kHD / 16; ++kk)  // dP^T = V dO^T
+                for (int kk = 0; kk < kHD / 16; ++kk)
                     umma_bf16(tmem + 128, make_sw128_desc(v_addr + kk * 32, 16, 1024),
                               make_sw128_desc(do_addr + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
-                umma_commit(s_full);
+                umma_commit(k.s_full);
+                if (s == ns - 1) umma_commit(&k.fix_empty[fb]);  // K, V of the item read
                 return true;
             };
-            if (ok) ok = issue_sdp(0);
-            for (int s = 0; s < ns && ok; ++s) {
-                if (s + 1 < ns) {
-                    if (!mbar_wait_bounded(s_free, s & 1, err, kDevTimeoutAccFree) ||
-                        !issue_sdp(s + 1)) {
+            // walk the tiles: (n, s) of tile g, and of tile g + 1
+            int it = blockIdx.x, n = 0, s = 0;
+            int ns = it < items ? nqb - bwd_item(it, H, B).tile : 0;
+            if (it < items) ok = issue_sdp(0, 0, 0, ns);
+            for (int g = 0; it < items && ok; ++g) {
+                int it1 = it, n1 = n, s1 = s + 1, ns1 = ns;
+                if (s1 == ns) {
+                    it1 = it + gridDim.x;
+                    n1 = n + 1;
+                    s1 = 0;
+                    ns1 = it1 < items ? nqb - bwd_item(it1, H, B).tile : 0;
+                }
+                if (it1 < items) {
+                    if (!mbar_wait_bounded(k.s_free, g & 1, err, kDevTimeoutAccFree) ||
+                        !issue_sdp(g + 1, n1, s1, ns1)) {
                         ok = false;
                         break;
                     }
                 }
-                if (!mbar_wait_bounded(p_full, s & 1, err, kDevTimeoutFull)) {
+                if (!mbar_wait_bounded(k.p_full, g & 1, err, kDevTimeoutFull) ||
+                    (s == 0 && n > 0 &&
+                     !mbar_wait_bounded(k.acc_free, (n - 1) & 1, err, kDevTimeoutAccFree))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t q_addr = smem_u32(stage(s)), do_addr = q_addr + kTile;
+                const uint32_t q_addr = smem_u32(stage(g)), do_addr = q_addr + kTile;
 #pragma unroll
                 for (int kk = 0; kk < kRows / 16; ++kk) {  // dV += P^T dO ; dK += dS^T Q
                     umma_bf16_ts(tmem + kColDV, tmem + kColP + kk * 8,
@@ -463,76 +539,93 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                  make_sw128_desc(q_addr + kk * 2048, 8192, 1024), idesc_acc,
                                  (s > 0 || kk > 0) ? 1u : 0u);
                 }
-                umma_commit(mm_done);
-                umma_commit(&st_empty[s % kBwdStages]);
+                umma_commit(k.mm_done);
+                umma_commit(&k.st_empty[g % kBwdStages]);
+                it = it1;
+                n = n1;
+                s = s1;
+                ns = ns1;
             }
         }
     } else {
         // ---------------- elementwise warps: thread = key row, 64 query columns
         const int lq = warp & 3, half = (warp - 2) >> 2;
         const int kr = lq * 32 + lane;
-        const int key = k0 + kr;
         const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
         bool ok = true;
-        for (int s = 0; s < ns && ok; ++s) {
-            const int q0 = (kt + s) * kRows + half * 64;
-            if (!warp_wait(s_full, s & 1, err, kDevTimeoutAcc) ||
-                !warp_wait(&st_full[s % kBwdStages], (s / kBwdStages) & 1, err, kDevTimeoutAcc)) {
+        int g = 0;
+        for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+            const BwdItem w = bwd_item(it, H, B);
+            const int kt = w.tile, ns = nqb - kt;
+            const int key = kt * kRows + kr;
+            for (int s = 0; s < ns && ok; ++s, ++g) {
+                const int q0 = (kt + s) * kRows + half * 64;
+                if (!warp_wait(k.s_full, g & 1, err, kDevTimeoutAcc) ||
+                    !warp_wait(&k.st_full[g % kBwdStages], (g / kBwdStages) & 1, err,
+                               kDevTimeoutAcc)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                uint32_t sv[64], dp[64];
+                tmem_ld_32x32b_x32(tmem + lane_base + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+                tmem_ld_32x32b_x32(tmem + lane_base + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+                tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
+                tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[32]));
+                tmem_ld_wait();
+                tc_fence_before();
+                mbar_arrive(k.s_free);
+                const float* lse = reinterpret_cast<const float*>(stage(g) + 2 * kTile) + half * 64;
+                const float* dv = lse + 128;
+#pragma unroll
+                for (int c4 = 0; c4 < 16; ++c4) {
+                    const float4 l4 = reinterpret_cast<const float4*>(lse)[c4];
+                    const float4 d4 = reinterpret_cast<const float4*>(dv)[c4];
+                    const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dd[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int c = c4 * 4 + u, q = q0 + c;
+                        float p = ex2_approx(fmaf(__uint_as_float(sv[c]), scale_log2, -lv[u] * kLog2ef));
+                        if (q < key || q >= T) p = 0.f;
+                        sv[c] = __float_as_uint(p);
+                        dp[c] = __float_as_uint(p * (__uint_as_float(dp[c]) - dd[u]));
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    sv[i] = pack_bf16x2(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1]));
+                    dp[i] = pack_bf16x2(__uint_as_float(dp[2 * i]), __uint_as_float(dp[2 * i + 1]));
+                }
+                if (g >= 1 && !warp_wait(k.mm_done, (g - 1) & 1, err, kDevTimeoutAcc)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                tmem_st_32x32b_x32(tmem + lane_base + kColP + half * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+                tmem_st_32x32b_x32(tmem + lane_base + kColDS + half * 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(k.p_full);
+            }
+            if (!ok || !warp_wait(k.mm_done, (g - 1) & 1, err, kDevTimeoutAcc)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            uint32_t sv[64], dp[64];
-            tmem_ld_32x32b_x32(tmem + lane_base + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-            tmem_ld_32x32b_x32(tmem + lane_base + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-            tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
-            tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[32]));
+            // column half 0 writes dV, half 1 writes scale * dK; the accumulators are free
+            // for the next item once read
+            const uint32_t col = half == 0 ? kColDV : kColDK;
+            uint32_t r0[32], r1[32];
+            tmem_ld_32x32b_x32(tmem + lane_base + col, r0);
+            tmem_ld_32x32b_x32(tmem + lane_base + col + 32, r1);
             tmem_ld_wait();
             tc_fence_before();
-            mbar_arrive(s_free);
-            const float* lse = reinterpret_cast<const float*>(stage(s) + 2 * kTile) + half * 64;
-            const float* dv = lse + 128;
-#pragma unroll
-            for (int c4 = 0; c4 < 16; ++c4) {
-                const float4 l4 = reinterpret_cast<const float4*>(lse)[c4];
-                const float4 d4 = reinterpret_cast<const float4*>(dv)[c4];
-                const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dd[4] = {d4.x, d4.y, d4.z, d4.w};
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int c = c4 * 4 + u, q = q0 + c;
-                    float p = ex2_approx(fmaf(__uint_as_float(sv[c]), scale_log2, -lv[u] * kLog2ef));
-                    if (q < key || q >= T) p = 0.f;
-                    sv[c] = __float_as_uint(p);
-                    dp[c] = __float_as_uint(p * (__uint_as_float(dp[c]) - dd[u]));
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                sv[i] = pack_bf16x2(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1]));
-                dp[i] = pack_bf16x2(__uint_as_float(dp[2 * i]), __uint_as_float(dp[2 * i + 1]));
-            }
-            if (s >= 1 && !warp_wait(mm_done, (s - 1) & 1, err, kDevTimeoutAcc)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            tmem_st_32x32b_x32(tmem + lane_base + kColP + half * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-            tmem_st_32x32b_x32(tmem + lane_base + kColDS + half * 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
-            tmem_st_wait();
-            tc_fence_before();
-            mbar_arrive(p_full);
-        }
-        if (ok && warp_wait(mm_done, (ns - 1) & 1, err, kDevTimeoutAcc)) {
-            tc_fence_after();
-            // column half 0 writes dV, half 1 writes scale * dK
-            const uint32_t col = half == 0 ? kColDV : kColDK;
-            bf16* dst = dqkv + ((long long)b * T + key) * 3LL * C + (half == 0 ? 2 * C : C) + h * kHD;
-#pragma unroll
-            for (int c = 0; c < kHD / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem + lane_base + col + c * 32, r);
-                tmem_ld_wait();
-                if (key < T) store_row64_bf16(dst + c * 32, r, half == 0 ? 1.f : scale);
+            mbar_arrive(k.acc_free);
+            if (key < T) {
+                bf16* dst = dqkv + ((long long)w.b * T + key) * 3LL * C + (half == 0 ? 2 * C : C) +
+                            w.h * kHD;
+                store_row64_bf16(dst, r0, half == 0 ? 1.f : scale);
+                store_row64_bf16(dst + 32, r1, half == 0 ? 1.f : scale);
             }
         }
     }
@@ -548,70 +641,59 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv,
                           const __grid_constant__ CUtensorMap tm_do,
                           const float* __restrict__ lse_g, const float* __restrict__ dvec,
-                          bf16* __restrict__ dqkv, int T, int H, float scale,
+                          bf16* __restrict__ dqkv, int B, int T, int H, float scale,
                           int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_u32 = smem_u32(smem_raw);
     uint8_t* sm = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + BwdSmem::BAR);
-    uint64_t* qd_full = bar;
-    uint64_t* st_full = bar + 1;
-    uint64_t* st_empty = st_full + kBwdStages;
-    uint64_t* s_full = st_empty + kBwdStages;
-    uint64_t* s_free = s_full + 1;
-    uint64_t* p_full = s_free + 1;
-    uint64_t* mm_done = p_full + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mm_done + 1);
-
+    const BwdBars k = bwd_bars(sm);
     const int nqb = (T + kRows - 1) / kRows;
-    const int qt = nqb - 1 - (int)blockIdx.x;     // longest tiles first
-    const int h = blockIdx.y, b = blockIdx.z;
-    const int ns = qt + 1;                        // key tiles 0..qt
+    const int items = nqb * H * B;
     const int C = H * kHD;
-    const int q0 = qt * kRows;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float scale_log2 = scale * kLog2ef;
     constexpr uint32_t kColDQ = 256, kColDS = 320;
 
-    if (threadIdx.x == 0) {
-        mbar_init(qd_full, 1);
-        for (int s = 0; s < kBwdStages; ++s) {
-            mbar_init(&st_full[s], 1);
-            mbar_init(&st_empty[s], 1);
-        }
-        mbar_init(s_full, 1);
-        mbar_init(s_free, 256);
-        mbar_init(p_full, 256);
-        mbar_init(mm_done, 1);
-        fence_barrier_init();
-    }
+    if (threadIdx.x == 0) bwd_init(k, 128);  // half 0 of the elementwise warps reads dQ
     if (warp == 1) {
-        tmem_alloc(tmem_slot, kBwdTmem);
+        tmem_alloc(k.tmem_slot, kBwdTmem);
         tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-    auto stage = [&](int s) { return sm + BwdSmem::STAGE0 + (s % kBwdStages) * BwdSmem::STAGE_BYTES; };
+    const uint32_t tmem = *k.tmem_slot;
+    auto stage = [&](int g) { return sm + BwdSmem::STAGE0 + (g % kBwdStages) * BwdSmem::STAGE_BYTES; };
+    auto fix = [&](int buf, int t) { return sm + BwdSmem::FIX + (2 * buf + t) * kTile; };
+    // item tile index counted from the longest: query tile nqb - 1 - tile, key tiles 0..that
 
     if (warp == 0) {
         if (lane == 0) {
             bool ok = true;
-            mbar_arrive_expect_tx(qd_full, 2 * kTile);
-            tma_load_3d(sm + BwdSmem::FIX0, &tm_qkv, qd_full, h * kHD, q0, b);  // Q
-            tma_load_3d(sm + BwdSmem::FIX1, &tm_do, qd_full, h * kHD, q0, b);   // dO
-            for (int s = 0; s < ns && ok; ++s) {
-                if (!mbar_wait_bounded(&st_empty[s % kBwdStages], ((s / kBwdStages) & 1) ^ 1u, err,
+            int g = 0;
+            for (int it = blockIdx.x, n = 0; it < items && ok; it += gridDim.x, ++n) {
+                const BwdItem w = bwd_item(it, H, B);
+                const int qt = nqb - 1 - w.tile, ns = qt + 1, fb = n & 1;
+                if (!mbar_wait_bounded(&k.fix_empty[fb], ((n >> 1) & 1) ^ 1u, err,
                                        kDevTimeoutEmpty)) {
                     ok = false;
                     break;
                 }
-                uint8_t* st = stage(s);
-                uint64_t* f = &st_full[s % kBwdStages];
-                mbar_arrive_expect_tx(f, 2 * kTile);
-                tma_load_3d(st, &tm_qkv, f, C + h * kHD, s * kRows, b);              // K_j
-                tma_load_3d(st + kTile, &tm_qkv, f, 2 * C + h * kHD, s * kRows, b);  // V_j
+                mbar_arrive_expect_tx(&k.fix_full[fb], 2 * kTile);
+                tma_load_3d(fix(fb, 0), &tm_qkv, &k.fix_full[fb], w.h * kHD, qt * kRows, w.b);  // Q
+                tma_load_3d(fix(fb, 1), &tm_do, &k.fix_full[fb], w.h * kHD, qt * kRows, w.b);   // dO
+                for (int s = 0; s < ns; ++s, ++g) {
+                    if (!mbar_wait_bounded(&k.st_empty[g % kBwdStages], ((g / kBwdStages) & 1) ^ 1u,
+                                           err, kDevTimeoutEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = stage(g);
+                    uint64_t* f = &k.st_full[g % kBwdStages];
+                    mbar_arrive_expect_tx(f, 2 * kTile);
+                    tma_load_3d(st, &tm_qkv, f, C + w.h * kHD, s * kRows, w.b);              // K_j
+                    tma_load_3d(st + kTile, &tm_qkv, f, 2 * C + w.h * kHD, s * kRows, w.b);  // V_j
+                }
             }
             if (!ok) spin_ns(100000);
         }
@@ -619,14 +701,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (lane == 0) {
             const uint32_t idesc_s = make_idesc_bf16(kRows, kRows, 0, 0);
             const uint32_t idesc_acc = make_idesc_bf16(kRows, kHD, 0, 1);
-            const uint32_t q_addr = smem_u32(sm + BwdSmem::FIX0), do_addr = smem_u32(sm + BwdSmem::FIX1);
-            bool ok = mbar_wait_bounded(qd_full, 0, err, kDevTimeoutFull);
-            auto issue_sdp = [&](int s) -> bool {
-                if (!mbar_wait_bounded(&st_full[s % kBwdStages], (s / kBwdStages) & 1, err,
+            bool ok = true;
+            auto issue_sdp = [&](int g, int n, int s, int ns) -> bool {
+                const int fb = n & 1;
+                if (s == 0 && !mbar_wait_bounded(&k.fix_full[fb], (n >> 1) & 1, err, kDevTimeoutFull))
+                    return false;
+                if (!mbar_wait_bounded(&k.st_full[g % kBwdStages], (g / kBwdStages) & 1, err,
                                        kDevTimeoutFull))
                     return false;
                 tc_fence_after();
-                const uint32_t k_addr = smem_u32(stage(s)), v_addr = k_addr + kTile;
+                const uint32_t q_addr = smem_u32(fix(fb, 0)), do_addr = smem_u32(fix(fb, 1));
+                const uint32_t k_addr = smem_u32(stage(g)), v_addr = k_addr + kTile;
 #pragma unroll
                 for (int kk = 0; kk < kHD / 16; ++kk)  // S = Q K^T
                     umma_bf16(tmem, make_sw128_desc(q_addr + kk * 32, 16, 1024),
@@ -635,86 +720,114 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 for (int kk = 0; kk < kHD / 16; ++kk)  // dP = dO V^T
                     umma_bf16(tmem + 128, make_sw128_desc(do_addr + kk * 32, 16, 1024),
                               make_sw128_desc(v_addr + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
-                umma_commit(s_full);
+                umma_commit(k.s_full);
+                if (s == ns - 1) umma_commit(&k.fix_empty[fb]);  // Q, dO of the item read
                 return true;
             };
-            if (ok) ok = issue_sdp(0);
-            for (int s = 0; s < ns && ok; ++s) {
-                if (s + 1 < ns) {
-                    if (!mbar_wait_bounded(s_free, s & 1, err, kDevTimeoutAccFree) ||
-                        !issue_sdp(s + 1)) {
+            auto item_ns = [&](int it) { return it < items ? nqb - bwd_item(it, H, B).tile : 0; };
+            int it = blockIdx.x, n = 0, s = 0, ns = item_ns(it);
+            if (it < items) ok = issue_sdp(0, 0, 0, ns);
+            for (int g = 0; it < items && ok; ++g) {
+                int it1 = it, n1 = n, s1 = s + 1, ns1 = ns;
+                if (s1 == ns) {
+                    it1 = it + gridDim.x;
+                    n1 = n + 1;
+                    s1 = 0;
+                    ns1 = item_ns(it1);
+                }
+                if (it1 < items) {
+                    if (!mbar_wait_bounded(k.s_free, g & 1, err, kDevTimeoutAccFree) ||
+                        !issue_sdp(g + 1, n1, s1, ns1)) {
                         ok = false;
                         break;
                     }
                 }
-                if (!mbar_wait_bounded(p_full, s & 1, err, kDevTimeoutFull)) {
+                if (!mbar_wait_bounded(k.p_full, g & 1, err, kDevTimeoutFull) ||
+                    (s == 0 && n > 0 &&
+                     !mbar_wait_bounded(k.acc_free, (n - 1) & 1, err, kDevTimeoutAccFree))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t k_addr = smem_u32(stage(s));
+                const uint32_t k_addr = smem_u32(stage(g));
 #pragma unroll
                 for (int kk = 0; kk < kRows / 16; ++kk)  // dQ += dS K
                     umma_bf16_ts(tmem + kColDQ, tmem + kColDS + kk * 8,
                                  make_sw128_desc(k_addr + kk * 2048, 8192, 1024), idesc_acc,
                                  (s > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(mm_done);
-                umma_commit(&st_empty[s % kBwdStages]);
+                umma_commit(k.mm_done);
+                umma_commit(&k.st_empty[g % kBwdStages]);
+                it = it1;
+                n = n1;
+                s = s1;
+                ns = ns1;
             }
         }
     } else {
         // ---------------- elementwise warps: thread = query row, 64 key columns
         const int lq = warp & 3, half = (warp - 2) >> 2;
         const int qr = lq * 32 + lane;
-        const int q = q0 + qr;
         const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
-        const long long li = ((long long)b * H + h) * T + q;
-        const float lse_l2 = q < T ? lse_g[li] * kLog2ef : 0.f;
-        const float dq_row = q < T ? dvec[li] : 0.f;
         bool ok = true;
-        for (int s = 0; s < ns && ok; ++s) {
-            const int kc0 = s * kRows + half * 64;
-            if (!warp_wait(s_full, s & 1, err, kDevTimeoutAcc)) {
+        int g = 0;
+        for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+            const BwdItem w = bwd_item(it, H, B);
+            const int qt = nqb - 1 - w.tile, ns = qt + 1;
+            const int q = qt * kRows + qr;
+            const long long li = ((long long)w.b * H + w.h) * T + q;
+            const float lse_l2 = q < T ? lse_g[li] * kLog2ef : 0.f;
+            const float dq_row = q < T ? dvec[li] : 0.f;
+            for (int s = 0; s < ns && ok; ++s, ++g) {
+                const int kc0 = s * kRows + half * 64;
+                if (!warp_wait(k.s_full, g & 1, err, kDevTimeoutAcc)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                uint32_t sv[64], dp[64];
+                tmem_ld_32x32b_x32(tmem + lane_base + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+                tmem_ld_32x32b_x32(tmem + lane_base + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+                tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
+                tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[32]));
+                tmem_ld_wait();
+                tc_fence_before();
+                mbar_arrive(k.s_free);
+#pragma unroll
+                for (int c = 0; c < 64; ++c) {
+                    float p = ex2_approx(fmaf(__uint_as_float(sv[c]), scale_log2, -lse_l2));
+                    if (kc0 + c > q || q >= T) p = 0.f;
+                    dp[c] = __float_as_uint(p * (__uint_as_float(dp[c]) - dq_row));
+                }
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    dp[i] = pack_bf16x2(__uint_as_float(dp[2 * i]), __uint_as_float(dp[2 * i + 1]));
+                if (g >= 1 && !warp_wait(k.mm_done, (g - 1) & 1, err, kDevTimeoutAcc)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                tmem_st_32x32b_x32(tmem + lane_base + kColDS + half * 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(k.p_full);
+            }
+            if (half != 0) continue;
+            // half 0 drains dQ; the accumulator is free for the next item once read
+            if (!ok || !warp_wait(k.mm_done, (g - 1) & 1, err, kDevTimeoutAcc)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            uint32_t sv[64], dp[64];
-            tmem_ld_32x32b_x32(tmem + lane_base + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-            tmem_ld_32x32b_x32(tmem + lane_base + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-            tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
-            tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[32]));
+            uint32_t r0[32], r1[32];
+            tmem_ld_32x32b_x32(tmem + lane_base + kColDQ, r0);
+            tmem_ld_32x32b_x32(tmem + lane_base + kColDQ + 32, r1);
             tmem_ld_wait();
             tc_fence_before();
-            mbar_arrive(s_free);
-#pragma unroll
-            for (int c = 0; c < 64; ++c) {
-                float p = ex2_approx(fmaf(__uint_as_float(sv[c]), scale_log2, -lse_l2));
-                if (kc0 + c > q || q >= T) p = 0.f;
-                dp[c] = __float_as_uint(p * (__uint_as_float(dp[c]) - dq_row));
-            }
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-                dp[i] = pack_bf16x2(__uint_as_float(dp[2 * i]), __uint_as_float(dp[2 * i + 1]));
-            if (s >= 1 && !warp_wait(mm_done, (s - 1) & 1, err, kDevTimeoutAcc)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            tmem_st_32x32b_x32(tmem + lane_base + kColDS + half * 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
-            tmem_st_wait();
-            tc_fence_before();
-            mbar_arrive(p_full);
-        }
-        if (ok && warp_wait(mm_done, (ns - 1) & 1, err, kDevTimeoutAcc) && half == 0) {
-            tc_fence_after();
-            bf16* dst = dqkv + ((long long)b * T + q) * 3LL * C + h * kHD;
-#pragma unroll
-            for (int c = 0; c < kHD / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem + lane_base + kColDQ + c * 32, r);
-                tmem_ld_wait();
-                if (q < T) store_row64_bf16(dst + c * 32, r, scale);
+            mbar_arrive(k.acc_free);
+            if (q < T) {
+                bf16* dst = dqkv + ((long long)w.b * T + q) * 3LL * C + w.h * kHD;
+                store_row64_bf16(dst, r0, scale);
+                store_row64_bf16(dst + 32, r1, scale);
             }
         }
     }
@@ -829,13 +942,17 @@ int attention_backward_tc(const bf16* qkv, const bf16* dout, const float* lse, c
     });
     if (attr) return attr;
     const float scale = 1.0f / sqrtf((float)hd);
-    const dim3 grid((T + kRows - 1) / kRows, H, B);
-    attn_bwd_dkdv_tc_kernel<<<grid, kBwdThreads, kBwdSmemBytes, s>>>(tq, tdo, tl, td, dqkv, T, H,
-                                                                     scale, err);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int items = ((T + kRows - 1) / kRows) * H * B;
+    const int grid = items < sms ? items : sms;
+    attn_bwd_dkdv_tc_kernel<<<grid, kBwdThreads, kBwdSmemBytes, s>>>(tq, tdo, tl, td, dqkv, B, T,
+                                                                     H, scale, err);
     int rc = launch_status();
     if (rc) return rc;
-    attn_bwd_dq_tc_kernel<<<grid, kBwdThreads, kBwdSmemBytes, s>>>(tq, tdo, lse, dvec, dqkv, T, H,
-                                                                   scale, err);
+    attn_bwd_dq_tc_kernel<<<grid, kBwdThreads, kBwdSmemBytes, s>>>(tq, tdo, lse, dvec, dqkv, B, T,
+                                                                   H, scale, err);
     return launch_status();
 }
 
