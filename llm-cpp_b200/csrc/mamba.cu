@@ -132,12 +132,20 @@ __device__ __forceinline__ void lane_reduce_scatter(float (&v)[M], int n) {
 }
 
 // ---------------------------------------------------------------- scan forward
-template <int L, int S>
+// The sequence is cut into gridDim.z segments of whole chunks, scanned side by side. The
+// recurrence is linear, so a segment's states are its own scan from h = 0 plus the state
+// entering it decayed by exp(A * (sum of dt so far in the segment)). PASS 0 scans each
+// segment from zero and keeps only its final state and its dt sum (seg_h [B][P][D][N],
+// seg_dt [B][P][D]); PASS 1 folds the earlier segments' results into the state entering its
+// segment, then scans it again writing y, the gated output and the saved chunk states. With
+// one segment, PASS 1 alone is the plain scan.
+template <int L, int S, int PASS>
 __global__ void __launch_bounds__(kScanWarps * 32) scan_fwd_kernel(
     const float* __restrict__ raw, const float* __restrict__ u, const float* __restrict__ xp,
     long long ldx, const float* __restrict__ alog, const float* __restrict__ dskip,
     const bf16* __restrict__ proj, long long ldp, float* __restrict__ y32,
-    bf16* __restrict__ gated, float* __restrict__ hchk, int T, int D, int N, int R) {
+    bf16* __restrict__ gated, float* __restrict__ hchk, float* __restrict__ seg_h,
+    float* __restrict__ seg_dt, int T, int D, int N, int R) {
     using G = ScanTile<L, S>;
     constexpr int CPB = G::kCPB, TC = G::kTC, EPT = G::kEPT, NT = G::kThreads, RW = G::kRow;
     constexpr int NS = G::kNS, BPT = G::kBPT;
@@ -166,7 +174,7 @@ __global__ void __launch_bounds__(kScanWarps * 32) scan_fwd_kernel(
             const long long row = (long long)b * T + t0 + i;
             pr[e] = ok ? raw[row * D + dd] : 0.f;
             pu[e] = ok ? u[row * D + dd] : 0.f;
-            pz[e] = ok ? __bfloat162float(proj[row * ldp + dd]) : 0.f;
+            if (PASS == 1) pz[e] = ok ? __bfloat162float(proj[row * ldp + dd]) : 0.f;
         }
 #pragma unroll
         for (int e = 0; e < BPT; ++e) {
@@ -174,7 +182,7 @@ __global__ void __launch_bounds__(kScanWarps * 32) scan_fwd_kernel(
             const bool ok = idx < TC * NS && t0 + i < T && k < N;
             const long long row = (long long)b * T + t0 + i;
             pb[e] = ok ? xp[row * ldx + R + k] : 0.f;
-            pc[e] = ok ? xp[row * ldx + R + N + k] : 0.f;
+            if (PASS == 1) pc[e] = ok ? xp[row * ldx + R + N + k] : 0.f;
         }
     };
     auto stage = [&](int buf, int t0) {
@@ -184,57 +192,94 @@ __global__ void __launch_bounds__(kScanWarps * 32) scan_fwd_kernel(
             const bool ok = t0 + i < T && d0 + cc < D;
             sDt[buf][i][cc] = ok ? clamp_dt(softplus_f(pr[e])) : 0.f;
             sU[buf][i][cc] = pu[e];
-            sZ[buf][i][cc] = pz[e];
+            if (PASS == 1) sZ[buf][i][cc] = pz[e];
         }
 #pragma unroll
         for (int e = 0; e < BPT; ++e) {
             const int idx = tid + e * NT;
             if (idx < TC * NS) {
                 sB[buf][idx / NS][idx % NS] = pb[e];
-                sC[buf][idx / NS][idx % NS] = pc[e];
+                if (PASS == 1) sC[buf][idx / NS][idx % NS] = pc[e];
             }
         }
     };
 
-    fetch(0);
+    // this block's segment: chunks [k_begin, k_end)
+    const int seg = blockIdx.z, nseg = gridDim.z;
+    const int cps = (nch + nseg - 1) / nseg;
+    const int k_begin = seg * cps, k_end = min(nch, k_begin + cps);
     float h[S];
 #pragma unroll
     for (int s = 0; s < S; ++s) h[s] = 0.f;
-    for (int k = 0; k < nch; ++k) {
+    if (PASS == 1) {
+        // the state entering the segment, from the earlier segments' zero-start scans
+        for (int p = 0; p < seg; ++p) {
+            const long long bp = (long long)b * nseg + p;
+            const float dts = chan ? seg_dt[bp * D + d] : 0.f;
+#pragma unroll
+            for (int s = 0; s < S; ++s) {
+                const int kk = n * S + s;
+                const float he = (chan && kk < N) ? seg_h[(bp * D + d) * N + kk] : 0.f;
+                h[s] = __expf(A[s] * dts) * h[s] + he;
+            }
+        }
+    }
+    float dtsum = 0.f;
+    if (k_begin < k_end) fetch(k_begin * TC);
+    for (int k = k_begin; k < k_end; ++k) {
         const int buf = k & 1, t0 = k * TC;
         stage(buf, t0);
         __syncthreads();
-        if (k + 1 < nch) fetch(t0 + TC);
+        if (k + 1 < k_end) fetch(t0 + TC);
+        if constexpr (PASS == 0) {
+            // h from zero and the segment's dt sum only
+#pragma unroll
+            for (int i = 0; i < TC; ++i) {
+                const float dt = sDt[buf][i][c], uu = sU[buf][i][c];
+                dtsum += dt;
+#pragma unroll
+                for (int s = 0; s < S; ++s)
+                    h[s] = __expf(A[s] * dt) * h[s] + sB[buf][i][n * S + s] * uu * dt;
+            }
+        } else {
+#pragma unroll
+            for (int s = 0; s < S; ++s)
+                if (chan && n * S + s < N)
+                    hchk[(((long long)b * nch + k) * D + d) * N + n * S + s] = h[s];
+            // steps past T were staged as dt = u = B = 0, which leaves h unchanged
+            float cs[TC];
+#pragma unroll
+            for (int i = 0; i < TC; ++i) {
+                const float dt = sDt[buf][i][c], uu = sU[buf][i][c];
+                float acc = 0.f;
+#pragma unroll
+                for (int s = 0; s < S; ++s) {
+                    const float a = __expf(A[s] * dt);
+                    h[s] = a * h[s] + sB[buf][i][n * S + s] * uu * dt;
+                    acc += sC[buf][i][n * S + s] * h[s];
+                }
+                cs[i] = acc;
+            }
+            lane_reduce_scatter<L, TC>(cs, n);
+            using SP = LaneSplit<L, TC>;
+#pragma unroll
+            for (int j = 0; j < SP::kPer; ++j) {
+                const int i = (n / SP::kGroup) * SP::kPer + j;
+                if (chan && n % SP::kGroup == 0 && t0 + i < T) {
+                    const long long row = (long long)b * T + t0 + i;
+                    const float yv = cs[j] + Ds * sU[buf][i][c];
+                    y32[row * D + d] = yv;
+                    gated[row * D + d] = __float2bfloat16_rn(yv * silu_f(sZ[buf][i][c]));
+                }
+            }
+        }
+    }
+    if (PASS == 0) {
+        const long long bp = (long long)b * nseg + seg;
 #pragma unroll
         for (int s = 0; s < S; ++s)
-            if (chan && n * S + s < N)
-                hchk[(((long long)b * nch + k) * D + d) * N + n * S + s] = h[s];
-        // steps past T were staged as dt = u = B = 0, which leaves h unchanged
-        float cs[TC];
-#pragma unroll
-        for (int i = 0; i < TC; ++i) {
-            const float dt = sDt[buf][i][c], uu = sU[buf][i][c];
-            float acc = 0.f;
-#pragma unroll
-            for (int s = 0; s < S; ++s) {
-                const float a = __expf(A[s] * dt);
-                h[s] = a * h[s] + sB[buf][i][n * S + s] * uu * dt;
-                acc += sC[buf][i][n * S + s] * h[s];
-            }
-            cs[i] = acc;
-        }
-        lane_reduce_scatter<L, TC>(cs, n);
-        using SP = LaneSplit<L, TC>;
-#pragma unroll
-        for (int j = 0; j < SP::kPer; ++j) {
-            const int i = (n / SP::kGroup) * SP::kPer + j;
-            if (chan && n % SP::kGroup == 0 && t0 + i < T) {
-                const long long row = (long long)b * T + t0 + i;
-                const float yv = cs[j] + Ds * sU[buf][i][c];
-                y32[row * D + d] = yv;
-                gated[row * D + d] = __float2bfloat16_rn(yv * silu_f(sZ[buf][i][c]));
-            }
-        }
+            if (chan && n * S + s < N) seg_h[(bp * D + d) * N + n * S + s] = h[s];
+        if (chan && n == 0) seg_dt[bp * D + d] = dtsum;
     }
 }
 
@@ -246,7 +291,8 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) scan_bwd_kernel(
     const bf16* __restrict__ proj, long long ldp, const float* __restrict__ y32,
     const float* __restrict__ dgated, const float* __restrict__ hchk, float* __restrict__ du,
     float* __restrict__ draw, bf16* __restrict__ dproj, float* __restrict__ dbc_part,
-    float* __restrict__ da_part, float* __restrict__ dd_part, int T, int D, int N, int R) {
+    float* __restrict__ da_part, float* __restrict__ dd_part, const float* __restrict__ seg_dh,
+    const float* __restrict__ seg_dt, int T, int D, int N, int R) {
     using G = ScanTile<L, S>;
     constexpr int CPB = G::kCPB, TC = G::kTC, EPT = G::kEPT, NT = G::kThreads, RW = G::kRow;
     constexpr int NS = G::kNS, BPT = G::kBPT;
@@ -320,16 +366,31 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) scan_bwd_kernel(
         }
     };
 
+    // this block's segment: chunks [k_begin, k_end), walked from the right; dh entering it
+    // from the right folds the later segments' zero-start results (scan_bwd_carry_kernel)
+    const int seg = blockIdx.z, nseg = gridDim.z;
+    const int cps = (nch + nseg - 1) / nseg;
+    const int k_begin = seg * cps, k_end = min(nch, k_begin + cps);
     float dh_next[S], dA_acc[S];
 #pragma unroll
     for (int s = 0; s < S; ++s) dh_next[s] = dA_acc[s] = 0.f;
+    for (int p = nseg - 1; p > seg; --p) {
+        const long long bp = (long long)b * nseg + p;
+        const float dts = chan ? seg_dt[bp * D + d] : 0.f;
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            const int kk = n * S + s;
+            const float he = (chan && kk < N) ? seg_dh[(bp * D + d) * N + kk] : 0.f;
+            dh_next[s] = __expf(A[s] * dts) * dh_next[s] + he;
+        }
+    }
     float dD_acc = 0.f;
-    fetch((nch - 1) * TC);
-    for (int k = nch - 1; k >= 0; --k) {
+    if (k_begin < k_end) fetch((k_end - 1) * TC);
+    for (int k = k_end - 1; k >= k_begin; --k) {
         const int buf = k & 1, t0 = k * TC;
         stage(buf, t0);
         __syncthreads();
-        if (k > 0) fetch(t0 - TC);
+        if (k > k_begin) fetch(t0 - TC);
         // the chunk's states, recomputed from the ones saved at its start. Steps past T
         // were staged as dt = u = B = C = dy = 0: h and dh pass through them unchanged and
         // they add nothing to dA, dD, dB or dC; their du and ddt are not stored.
@@ -404,10 +465,100 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) scan_bwd_kernel(
             part[BT * N + row * N + nn] = sc;
         }
     }
+    // per (sequence, segment) partials [B * nseg][D][N] and [B * nseg][D]
+    const long long bs = (long long)b * nseg + seg;
 #pragma unroll
     for (int s = 0; s < S; ++s)
-        if (chan && n * S + s < N) da_part[((long long)b * D + d) * N + n * S + s] = dA_acc[s];
-    if (n == 0 && chan) dd_part[(long long)b * D + d] = dD_acc;
+        if (chan && n * S + s < N) da_part[(bs * D + d) * N + n * S + s] = dA_acc[s];
+    if (n == 0 && chan) dd_part[bs * D + d] = dD_acc;
+}
+
+// dh entering each segment's left end from a zero carry at its right end, and the segment's
+// dt sum: dh_t = dh_(t+1) exp(A dt_(t+1)) + dy_t C_t over the segment, from the right. These
+// are what the segments to the left need to start their reverse scans from the true dh.
+template <int L, int S>
+__global__ void __launch_bounds__(kScanWarps * 32) scan_bwd_carry_kernel(
+    const float* __restrict__ raw, const float* __restrict__ xp, long long ldx,
+    const float* __restrict__ alog, const bf16* __restrict__ proj, long long ldp,
+    const float* __restrict__ dgated, float* __restrict__ seg_dh, float* __restrict__ seg_dt,
+    int T, int D, int N, int R) {
+    using G = ScanTile<L, S>;
+    constexpr int CPB = G::kCPB, TC = G::kTC, EPT = G::kEPT, NT = G::kThreads, RW = G::kRow;
+    constexpr int NS = G::kNS, BPT = G::kBPT;
+    __shared__ float sDt[2][TC][RW], sDy[2][TC][RW];
+    __shared__ __align__(16) float sC[2][TC][NS];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n = lane % L, c = warp * G::kCPW + lane / L;
+    const int d0 = blockIdx.x * CPB, d = d0 + c;
+    const int b = blockIdx.y;
+    const bool chan = d < D;
+    float A[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        const int k = n * S + s;
+        A[s] = (chan && k < N) ? alog[(long long)d * N + k] : 0.f;
+    }
+    const int nch = (T + TC - 1) / TC;
+    float pr[EPT], pg[EPT], pz[EPT], pc[BPT];
+    auto fetch = [&](int t0) {
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) {
+            const int idx = tid + e * NT, i = idx / CPB, dd = d0 + idx % CPB;
+            const bool ok = t0 + i < T && dd < D;
+            const long long row = (long long)b * T + t0 + i;
+            pr[e] = ok ? raw[row * D + dd] : 0.f;
+            pg[e] = ok ? dgated[row * D + dd] : 0.f;
+            pz[e] = ok ? __bfloat162float(proj[row * ldp + dd]) : 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < BPT; ++e) {
+            const int idx = tid + e * NT, i = idx / NS, k = idx % NS;
+            const bool ok = idx < TC * NS && t0 + i < T && k < N;
+            const long long row = (long long)b * T + t0 + i;
+            pc[e] = ok ? xp[row * ldx + R + N + k] : 0.f;
+        }
+    };
+    auto stage = [&](int buf, int t0) {
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) {
+            const int idx = tid + e * NT, i = idx / CPB, cc = idx % CPB;
+            const bool ok = t0 + i < T && d0 + cc < D;
+            sDt[buf][i][cc] = ok ? clamp_dt(softplus_f(pr[e])) : 0.f;
+            sDy[buf][i][cc] = pg[e] * silu_f(pz[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < BPT; ++e) {
+            const int idx = tid + e * NT;
+            if (idx < TC * NS) sC[buf][idx / NS][idx % NS] = pc[e];
+        }
+    };
+    const int seg = blockIdx.z, nseg = gridDim.z;
+    const int cps = (nch + nseg - 1) / nseg;
+    const int k_begin = seg * cps, k_end = min(nch, k_begin + cps);
+    float dh_next[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) dh_next[s] = 0.f;
+    float dtsum = 0.f;
+    if (k_begin < k_end) fetch((k_end - 1) * TC);
+    for (int k = k_end - 1; k >= k_begin; --k) {
+        const int buf = k & 1, t0 = k * TC;
+        stage(buf, t0);
+        __syncthreads();
+        if (k > k_begin) fetch(t0 - TC);
+#pragma unroll
+        for (int i = TC - 1; i >= 0; --i) {
+            const float dyv = sDy[buf][i][c], dt = sDt[buf][i][c];
+            dtsum += dt;
+#pragma unroll
+            for (int s = 0; s < S; ++s)
+                dh_next[s] = (dh_next[s] + dyv * sC[buf][i][n * S + s]) * __expf(A[s] * dt);
+        }
+    }
+    const long long bp = (long long)b * nseg + seg;
+#pragma unroll
+    for (int s = 0; s < S; ++s)
+        if (chan && n * S + s < N) seg_dh[(bp * D + d) * N + n * S + s] = dh_next[s];
+    if (chan && n == 0) seg_dt[bp * D + d] = dtsum;
 }
 
 // dB, dC: sum over channel groups (fixed order) -> bf16 columns R.. of dxp
@@ -683,12 +834,22 @@ __global__ void convert_kernel(const float* __restrict__ src, long long lds, bf1
 template <int L, int S>
 int launch_scan_fwd(const MambaDims& m, const float* raw, const float* u, const float* xp,
                     const float* alog, const float* dskip, const bf16* proj, float* y32,
-                    bf16* gated, float* hchk, cudaStream_t s) {
+                    bf16* gated, float* hchk, float* seg_work, cudaStream_t s) {
     constexpr int CPB = ScanTile<L, S>::kCPB;
-    dim3 grid((m.D + CPB - 1) / CPB, m.B);
-    scan_fwd_kernel<L, S><<<grid, kScanWarps * 32, 0, s>>>(raw, u, xp, m.ldx, alog, dskip, proj,
-                                                           m.ldp, y32, gated, hchk, m.T, m.D,
-                                                           m.N, m.R);
+    const int nseg = mamba_scan_segments(m.B, m.T, m.D, m.N);
+    dim3 grid((m.D + CPB - 1) / CPB, m.B, nseg);
+    float* seg_h = seg_work;
+    float* seg_dt = seg_work + (size_t)m.B * nseg * m.D * m.N;
+    if (nseg > 1) {
+        scan_fwd_kernel<L, S, 0><<<grid, kScanWarps * 32, 0, s>>>(
+            raw, u, xp, m.ldx, alog, dskip, proj, m.ldp, y32, gated, hchk, seg_h, seg_dt, m.T,
+            m.D, m.N, m.R);
+        int rc = launch_status();
+        if (rc) return rc;
+    }
+    scan_fwd_kernel<L, S, 1><<<grid, kScanWarps * 32, 0, s>>>(raw, u, xp, m.ldx, alog, dskip, proj,
+                                                              m.ldp, y32, gated, hchk, seg_h,
+                                                              seg_dt, m.T, m.D, m.N, m.R);
     return launch_status();
 }
 
@@ -696,12 +857,22 @@ template <int L, int S>
 int launch_scan_bwd(const MambaDims& m, const float* raw, const float* u, const float* xp,
                     const float* alog, const float* dskip, const bf16* proj, const float* y32,
                     const float* dgated, const float* hchk, float* du, float* draw, bf16* dproj,
-                    float* dbc_part, float* da_part, float* dd_part, cudaStream_t s) {
+                    float* dbc_part, float* da_part, float* dd_part, float* seg_work,
+                    cudaStream_t s) {
     constexpr int CPB = ScanTile<L, S>::kCPB;
-    dim3 grid((m.D + CPB - 1) / CPB, m.B);
+    const int nseg = mamba_scan_segments(m.B, m.T, m.D, m.N);
+    dim3 grid((m.D + CPB - 1) / CPB, m.B, nseg);
+    float* seg_dh = seg_work;
+    float* seg_dt = seg_work + (size_t)m.B * nseg * m.D * m.N;
+    if (nseg > 1) {
+        scan_bwd_carry_kernel<L, S><<<grid, kScanWarps * 32, 0, s>>>(
+            raw, xp, m.ldx, alog, proj, m.ldp, dgated, seg_dh, seg_dt, m.T, m.D, m.N, m.R);
+        int rc = launch_status();
+        if (rc) return rc;
+    }
     scan_bwd_kernel<L, S><<<grid, kScanWarps * 32, 0, s>>>(
         raw, u, xp, m.ldx, alog, dskip, proj, m.ldp, y32, dgated, hchk, du, draw, dproj, dbc_part,
-        da_part, dd_part, m.T, m.D, m.N, m.R);
+        da_part, dd_part, seg_dh, seg_dt, m.T, m.D, m.N, m.R);
     return launch_status();
 }
 
@@ -794,10 +965,57 @@ int mamba_dt_forward(const MambaDims& m, const float* xp, const float* dt_proj, 
                           m.D, 0, s);
 }
 
+static int scan_channels_per_block(int N) {
+    switch (scan_layout(N)) {
+        case 41: return ScanTile<4, 1>::kCPB;
+        case 81: return ScanTile<8, 1>::kCPB;
+        case 82: return ScanTile<8, 2>::kCPB;
+        default: return 1;
+    }
+}
+
+static int device_sms() {
+    static int sms = [] {
+        int dev = 0, n = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        return n > 0 ? n : 148;
+    }();
+    return sms;
+}
+
+// Splitting the sequence costs a carry pass, so it only pays when the (channel group, sequence)
+// grid leaves SMs idle: fewer blocks than SMs. Then enough segments of at least 32 chunks
+// (512 steps) each to reach two blocks per SM, at most 8.
+int mamba_scan_segments(int B, int T, int D, int N) {
+    const int sms = device_sms();
+    const int cpb = scan_channels_per_block(N);
+    const long long blocks = (long long)B * ((D + cpb - 1) / cpb);
+    if (blocks <= 0 || blocks >= sms) return 1;
+    const int nch = (T + kScanChunk - 1) / kScanChunk;
+    long long p = (2LL * sms + blocks - 1) / blocks;
+    if (p > T / 512) p = T / 512;
+    if (p > 8) p = 8;
+    if (p > nch) p = nch;
+    return p < 1 ? 1 : (int)p;
+}
+int mamba_scan_parts_max(int max_batch, int max_seq, int D, int N) {
+    int best = 0;
+    for (int b = 1; b <= max_batch; ++b) {
+        const int parts = b * mamba_scan_segments(b, max_seq, D, N);
+        best = parts > best ? parts : best;
+    }
+    return best;
+}
+size_t mamba_scan_seg_floats(int max_batch, int max_seq, int D, int N) {
+    return (size_t)mamba_scan_parts_max(max_batch, max_seq, D, N) * D * (N + 1);
+}
+
 int mamba_scan_forward(const MambaDims& m, const float* raw, const float* u, const float* xp,
                        const float* alog, const float* dskip, const bf16* proj, float* y32,
-                       bf16* gated, float* hchk, cudaStream_t s) {
-#define SF(L, S) launch_scan_fwd<L, S>(m, raw, u, xp, alog, dskip, proj, y32, gated, hchk, s)
+                       bf16* gated, float* hchk, float* seg_work, cudaStream_t s) {
+#define SF(L, S) \
+    launch_scan_fwd<L, S>(m, raw, u, xp, alog, dskip, proj, y32, gated, hchk, seg_work, s)
     switch (scan_layout(m.N)) {
         case 41: return SF(4, 1);
         case 81: return SF(8, 1);
@@ -810,10 +1028,11 @@ int mamba_scan_forward(const MambaDims& m, const float* raw, const float* u, con
 int mamba_scan_backward(const MambaDims& m, const float* raw, const float* u, const float* xp,
                         const float* alog, const float* dskip, const bf16* proj, const float* y32,
                         const float* dgated, const float* hchk, float* du, float* draw, bf16* dproj,
-                        float* dbc_part, float* da_part, float* dd_part, cudaStream_t s) {
+                        float* dbc_part, float* da_part, float* dd_part, float* seg_work,
+                        cudaStream_t s) {
 #define SB(L, S)                                                                             \
     launch_scan_bwd<L, S>(m, raw, u, xp, alog, dskip, proj, y32, dgated, hchk, du, draw, dproj, \
-                          dbc_part, da_part, dd_part, s)
+                          dbc_part, da_part, dd_part, seg_work, s)
     switch (scan_layout(m.N)) {
         case 41: return SB(4, 1);
         case 81: return SB(8, 1);

@@ -25,18 +25,25 @@ int mamba_conv_forward(const MambaDims& m, const bf16* proj, const float* w, con
                        float* u32, bf16* u16, cudaStream_t s);
 int mamba_dt_forward(const MambaDims& m, const float* xp, const float* dt_proj, float* raw,
                      cudaStream_t s);
-// hchk: B * ceil(T/kScanChunk) * D * N floats
+// hchk: B * ceil(T/kScanChunk) * D * N floats. Each sequence is scanned in
+// mamba_scan_segments(B, T, D, N) segments side by side (one unless the grid would leave SMs
+// idle); seg_work: mamba_scan_seg_floats(max batch, max length, D, N) floats, and
+// mamba_scan_parts_max(...) bounds B x segments over batches up to max batch.
+int mamba_scan_segments(int B, int T, int D, int N);
+int mamba_scan_parts_max(int max_batch, int max_seq, int D, int N);
+size_t mamba_scan_seg_floats(int max_batch, int max_seq, int D, int N);
 int mamba_scan_forward(const MambaDims& m, const float* raw, const float* u, const float* xp,
                        const float* alog, const float* dskip, const bf16* proj, float* y32,
-                       bf16* gated, float* hchk, cudaStream_t s);
+                       bf16* gated, float* hchk, float* seg_work, cudaStream_t s);
 // dgated: fp32 gradient of the gated output. Writes du (scan + skip part), draw (the
 // gradient of dt_raw: through the clamp mask and softplus), the x_z gradient into
-// dproj[:, 0:D], and partials: dbc_part [groups][2][rows][N], da_part [B][D][N],
-// dd_part [B][D].
+// dproj[:, 0:D], and partials: dbc_part [groups][2][rows][N], da_part [B * nseg][D][N],
+// dd_part [B * nseg][D] with nseg = mamba_scan_segments(B, T, D, N); seg_work as for the forward.
 int mamba_scan_backward(const MambaDims& m, const float* raw, const float* u, const float* xp,
                         const float* alog, const float* dskip, const bf16* proj, const float* y32,
                         const float* dgated, const float* hchk, float* du, float* draw, bf16* dproj,
-                        float* dbc_part, float* da_part, float* dd_part, cudaStream_t s);
+                        float* dbc_part, float* da_part, float* dd_part, float* seg_work,
+                        cudaStream_t s);
 int mamba_reduce_dbc(const MambaDims& m, const float* dbc_part, bf16* dxp, cudaStream_t s);
 int mamba_batch_reduce(const float* part, int B, long long n, float* out, int accumulate,
                        cudaStream_t s);

@@ -613,13 +613,15 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
             dalloc(c, &c->m_duxp, (size_t)BT * D) ||
             dalloc(c, &c->m_dpre, (size_t)BT * D) ||
             dalloc(c, &c->m_dbc, (size_t)groups * 2 * BT * c->mN) ||
-            dalloc(c, &c->m_da, (size_t)max_batch * D * c->mN) ||
-            dalloc(c, &c->m_dd, (size_t)max_batch * D) ||
+            dalloc(c, &c->m_da,
+                   (size_t)mamba_scan_parts_max(max_batch, max_seq, D, c->mN) * D * c->mN) ||
+            dalloc(c, &c->m_dd, (size_t)mamba_scan_parts_max(max_batch, max_seq, D, c->mN) * D) ||
             dalloc(c, &c->m_convpart, (size_t)mamba_conv_blocks(BT) * D * (c->mK + 1)) ||
             dalloc(c, &c->m_dproj, (size_t)BT * 2 * D) ||
             dalloc(c, &c->m_dxp, (size_t)BT * c->mRPp) ||
             dalloc(c, &c->m_sgpart,
-                   std::max((size_t)kSgSplitRows * BT, (size_t)kSgSplitCols * D) * c->mR))
+                   std::max((size_t)kSgSplitRows * BT, (size_t)kSgSplitCols * D) * c->mR) ||
+            dalloc(c, &c->m_segwork, mamba_scan_seg_floats(max_batch, max_seq, D, c->mN)))
             return fail(c, "");
     }
     for (int l = 0; l < L && !c->mamba; ++l) {
@@ -780,7 +782,7 @@ void ctx_destroy(Ctx* c) {
         F(m.hchk);
     }
     F(c->m_dgated); F(c->m_du); F(c->m_duxp); F(c->m_dpre); F(c->m_dbc);
-    F(c->m_da); F(c->m_dd); F(c->m_convpart); F(c->m_dproj); F(c->m_dxp);
+    F(c->m_da); F(c->m_dd); F(c->m_convpart); F(c->m_segwork); F(c->m_dproj); F(c->m_dxp);
     F(c->m_sgpart);
     for (auto& e : c->moeact) {
         F(e.probs); F(e.idx); F(e.wts); F(e.ssum); F(e.grp); F(e.row_of); F(e.tok_of);
@@ -863,7 +865,7 @@ int mamba_forward_layer(Ctx* c, int l, int B, int T, float* xnext) {
         return rc;
     KC(mamba_dt_forward(md, m.xp, pp(b.dt_proj), m.raw, s));
     KC(mamba_scan_forward(md, m.raw, m.u32, m.xp, pp(b.a_log), pp(b.dskip), m.proj, m.y, m.gated,
-                          m.hchk, s));
+                          m.hchk, c->m_segwork, s));
     GemmArgs r = epi_args(kEpiResidF32, xnext, C);
     r.resid = a.x;
     r.ldr = C;
@@ -897,9 +899,10 @@ int mamba_backward_layer(Ctx* c, int l, int B, int T, int acc) {
     float* draw = c->m_dpre;
     KC(mamba_scan_backward(md, m.raw, m.u32, m.xp, pp(b.a_log), pp(b.dskip), m.proj, m.y,
                            c->m_dgated, m.hchk, c->m_du, draw, c->m_dproj, c->m_dbc, c->m_da,
-                           c->m_dd, s));
-    KC(mamba_batch_reduce(c->m_da, B, (long long)D * c->mN, gp(b.a_log), acc, s));
-    KC(mamba_batch_reduce(c->m_dd, B, D, gp(b.dskip), acc, s));
+                           c->m_dd, c->m_segwork, s));
+    const int parts = B * mamba_scan_segments(B, T, D, c->mN);
+    KC(mamba_batch_reduce(c->m_da, parts, (long long)D * c->mN, gp(b.a_log), acc, s));
+    KC(mamba_batch_reduce(c->m_dd, parts, D, gp(b.dskip), acc, s));
     KC(mamba_reduce_dbc(md, c->m_dbc, c->m_dxp, s));  // dB, dC -> dxp[:, R:R+2N]
     // draw through dt_proj. These two dt_rank-wide contractions are sums with heavy
     // cancellation, so they stay in fp32 (a bf16 operand costs ~5% on the dt_proj gradient).

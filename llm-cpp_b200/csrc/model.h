@@ -112,7 +112,7 @@ struct Ctx {
     std::vector<MambaAct> mact;
     float *m_dgated = nullptr, *m_du = nullptr, *m_duxp = nullptr,
           *m_dpre = nullptr, *m_dbc = nullptr, *m_da = nullptr, *m_dd = nullptr,
-          *m_convpart = nullptr, *m_sgpart = nullptr;
+          *m_convpart = nullptr, *m_sgpart = nullptr, *m_segwork = nullptr;
     bf16 *m_dproj = nullptr, *m_dxp = nullptr;
     // MoE FFN: E experts of hidden He = 4C, top-k, expert row capacity cap
     bool moe = false;

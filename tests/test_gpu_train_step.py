@@ -161,6 +161,11 @@ ORACLE_CASES = {
     "mamba_ragged_n8": (go.Cfg(vocab=256, n_layers=1, n_heads=1, n_embd=64, block_size=100,
                                rmsnorm=True, mamba=True, d_inner=80, d_state=8, dt_rank=6,
                                conv_kernel=3), 3, 100),
+    # long Mamba sequence: the forward scan runs as two segments side by side (T >= 1024),
+    # the second starting from the state the first hands over; ragged chunk split
+    "mamba_long_segments": (go.Cfg(vocab=256, n_layers=1, n_heads=1, n_embd=64,
+                                   block_size=1100, rmsnorm=True, mamba=True, d_inner=64,
+                                   d_state=16, dt_rank=8, conv_kernel=4), 1, 1100),
 }
 
 
