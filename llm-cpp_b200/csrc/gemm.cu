@@ -270,6 +270,49 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
                                               int row0, int n0, int split, int g, int lane,
                                               EpiWarp& w, int c_begin = 0,
                                               int c_end = NCOLS / 32) {
+    if (a.tma_epi && a.epi == kEpiStoreBF16) {
+        // two chunks per 32 x 64 box (128-byte rows): half the bulk stores of 32 x 32 boxes.
+        // A warp's chunk range has even length; a second chunk past N is clipped by the store.
+        if (row0 >= a.M) return;
+        const int lim = (a.N - n0 + 31) / 32;
+        const int ce = c_end < lim ? c_end : lim;
+#pragma unroll 1
+        for (int c = c_begin; c < ce; c += 2) {
+            uint32_t ra[32], rb[32];
+            if (!empty) {
+                tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), ra);
+                tmem_ld_32x32b_x32(tbase + (uint32_t)((c + 1) * 32), rb);
+                tmem_ld_wait();
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) ra[j] = rb[j] = 0u;
+            }
+            uint8_t* box = w.stage + w.slot * kEpiSlotBytes;
+            if (lane == 0) bulk_wait_group_read<1>();  // this box's previous store has read it
+            __syncwarp();
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+                *reinterpret_cast<uint4*>(box + box_off_f32(lane, ch)) = make_uint4(
+                    pack_bf16x2(__uint_as_float(ra[8 * ch]), __uint_as_float(ra[8 * ch + 1])),
+                    pack_bf16x2(__uint_as_float(ra[8 * ch + 2]), __uint_as_float(ra[8 * ch + 3])),
+                    pack_bf16x2(__uint_as_float(ra[8 * ch + 4]), __uint_as_float(ra[8 * ch + 5])),
+                    pack_bf16x2(__uint_as_float(ra[8 * ch + 6]), __uint_as_float(ra[8 * ch + 7])));
+                *reinterpret_cast<uint4*>(box + box_off_f32(lane, ch + 4)) = make_uint4(
+                    pack_bf16x2(__uint_as_float(rb[8 * ch]), __uint_as_float(rb[8 * ch + 1])),
+                    pack_bf16x2(__uint_as_float(rb[8 * ch + 2]), __uint_as_float(rb[8 * ch + 3])),
+                    pack_bf16x2(__uint_as_float(rb[8 * ch + 4]), __uint_as_float(rb[8 * ch + 5])),
+                    pack_bf16x2(__uint_as_float(rb[8 * ch + 6]), __uint_as_float(rb[8 * ch + 7])));
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_3d(tmO, box, n0 + c * 32, row0, 0);
+                bulk_commit_group();
+            }
+            w.slot ^= 1;
+        }
+        return;
+    }
 #pragma unroll 1
     for (int c = c_begin; c < c_end; ++c) {
         uint32_t r[32];
@@ -975,20 +1018,23 @@ int make_tmap_bf16(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t ou
 // 3-D tensor map of 32x32x1 boxes over an epilogue output or input: dims {x, y, z} with
 // row stride `ys` and plane stride `zs` in bytes; fp32 boxes use the 128-byte swizzle, bf16
 // boxes the 64-byte swizzle (the layouts box_off_f32 / box_off_bf16 write).
+// Boxes of 32 rows: 32 fp32 or 32 bf16 columns, or (wide) 64 bf16 columns; rows of 128
+// bytes take the 128-byte swizzle, 64-byte rows the 64-byte one.
 int make_tmap_box(CUtensorMap* tm, const void* ptr, bool f32, uint64_t x, uint64_t y, uint64_t z,
-                  uint64_t ys, uint64_t zs) {
+                  uint64_t ys, uint64_t zs, bool wide = false) {
     auto enc = get_encode_fn();
     if (!enc) return -1;
     if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || (ys & 15) != 0 || (zs & 15) != 0)
         return -2;
+    const bool rows128 = f32 || wide;
     cuuint64_t dims[3] = {x, y, z};
     cuuint64_t strides[2] = {ys, zs};
-    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t box[3] = {(!f32 && wide) ? 64u : 32u, 32, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(tm, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
                      const_cast<void*>(ptr), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                     rows128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : -4;
 }
@@ -1020,7 +1066,10 @@ bool plan_tma_epilogue(GemmPlan* plan, const GemmArgs& a) {
                                                                      : a.group_stride) * 4) % 16) ||
                   (a.epi == kEpiSplitPartial && ((uint64_t)a.M * a.N * 4) % 16)))
         return false;
-    if (make_tmap_box(&plan->tmO, a.out, f32, x, (uint64_t)a.M, z, ys, zs)) return false;
+    // plain bf16 outputs leave in 32 x 64 boxes (two chunks per store)
+    if (make_tmap_box(&plan->tmO, a.out, f32, x, (uint64_t)a.M, z, ys, zs,
+                      a.epi == kEpiStoreBF16))
+        return false;
     if (a.epi == kEpiResidF32) {
         const uint64_t rs = (uint64_t)a.ldr * 4;
         if (make_tmap_box(&plan->tmX, a.resid, true, (uint64_t)a.N, (uint64_t)a.M, 1, rs,
