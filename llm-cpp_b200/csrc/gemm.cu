@@ -39,6 +39,7 @@ struct GemmCfg {
     static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
     static constexpr uint32_t TMEM_COLS = 2 * BN;
     static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 4 * 2 * 4096 + 256;
+    static_assert((2 * STAGES + 4 + 8) * 8 + 4 <= 256, "barrier area");
 };
 
 __device__ __forceinline__ void decode_tile(int t, int num_m, int num_n, int tiles_mn, int& m_blk,
@@ -256,11 +257,132 @@ __device__ __forceinline__ void box_put_bf16(uint8_t* box, int r, const float* v
 }
 
 struct EpiWarp {
-    uint8_t* stage;   // this warp's two boxes
-    uint64_t* bar;    // completion of this warp's input loads
-    uint32_t phase;
-    int slot;
+    uint8_t* stage;   // this warp's two 4 KB boxes
+    uint64_t* bar;    // [2]: completion of the input load into each box
+    uint32_t phase;   // bit s: parity of bar[s]
+    int slot;         // box of the next chunk
+    uint32_t pend;    // bit s: an input load into box s not yet waited for
 };
+
+// Epilogues that read an input: the residual (fp32, a unit is one 32-column chunk) and the
+// stored pre-activation of dGELU (bf16, a unit is two chunks in one 32 x 64 box). A unit's
+// input is loaded one unit ahead, the first two before the accumulator is ready, so the
+// HBM latency of the input is not paid once per chunk.
+__device__ __forceinline__ bool epi_has_input(const GemmArgs& a) {
+    return a.tma_epi && (a.epi == kEpiResidF32 || a.epi == kEpiDGeluBF16);
+}
+__device__ __forceinline__ int epi_unit_chunks(const GemmArgs& a) {
+    return a.epi == kEpiDGeluBF16 ? 2 : 1;
+}
+// End of the chunks of [c_begin, c_end) a TMA epilogue writes: none when the rows are past
+// M; none from the first chunk whose columns start at or past N.
+__device__ __forceinline__ int epi_chunk_end(const GemmArgs& a, int row0, int n0, int c_begin,
+                                             int c_end) {
+    if (row0 >= a.M) return c_begin;
+    const int lim = (a.N - n0 + 31) / 32;
+    return c_end < lim ? c_end : (lim > c_begin ? lim : c_begin);
+}
+// lane 0: the 4 KB input box of the unit starting at column col0 into box s
+__device__ __forceinline__ void epi_load_unit(const CUtensorMap* tmX, EpiWarp& w, int s,
+                                              int col0, int row0) {
+    mbar_arrive_expect_tx(&w.bar[s], (uint32_t)kEpiSlotBytes);
+    tma_load_3d(w.stage + s * kEpiSlotBytes, tmX, &w.bar[s], col0, row0, 0);
+    w.pend |= 1u << s;
+}
+// Issued before the accumulator wait: the inputs of the tile's first two units.
+__device__ __forceinline__ void epilogue_prefetch(const GemmArgs& a, const CUtensorMap* tmX,
+                                                  int row0, int n0, int lane, EpiWarp& w,
+                                                  int c_begin, int c_end) {
+    if (!epi_has_input(a)) return;
+    const int ce = epi_chunk_end(a, row0, n0, c_begin, c_end);
+    const int u = epi_unit_chunks(a);
+    if (lane == 0 && ce > c_begin) {
+        bulk_wait_group_read<0>();  // earlier stores have read both boxes
+        epi_load_unit(tmX, w, w.slot, n0 + c_begin * 32, row0);
+        if (c_begin + u < ce) epi_load_unit(tmX, w, w.slot ^ 1, n0 + (c_begin + u) * 32, row0);
+    }
+    __syncwarp();
+}
+// Error exit: wait (bounded) for input loads still landing in this warp's boxes.
+__device__ __forceinline__ void epilogue_drain(const GemmArgs& a, int lane, EpiWarp& w) {
+    if (lane == 0)
+        for (int s = 0; s < 2; ++s)
+            if (w.pend & (1u << s))
+                mbar_wait_bounded(&w.bar[s], (w.phase >> s) & 1u, a.err, kDevTimeoutFull);
+    __syncwarp();
+}
+
+// The input epilogues (epilogue_prefetch has issued the first two units' loads).
+__device__ __forceinline__ void epilogue_input_tile(const GemmArgs& a, const CUtensorMap* tmO,
+                                                    const CUtensorMap* tmX, uint32_t tbase,
+                                                    bool empty, int row0, int n0, int lane,
+                                                    EpiWarp& w, int c_begin, int c_end) {
+    const int u = epi_unit_chunks(a);
+    const int ce = epi_chunk_end(a, row0, n0, c_begin, c_end);
+#pragma unroll 1
+    for (int c = c_begin; c < ce; c += u) {
+        uint32_t ra[32], rb[32];
+        if (!empty) {
+            tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), ra);
+            if (u == 2) tmem_ld_32x32b_x32(tbase + (uint32_t)((c + 1) * 32), rb);
+        }
+        // the next unit's input goes into the box the previous unit stored from
+        if (c > c_begin && c + u < ce) {
+            if (lane == 0) {
+                bulk_wait_group_read<0>();
+                epi_load_unit(tmX, w, w.slot ^ 1, n0 + (c + u) * 32, row0);
+            }
+            __syncwarp();
+        }
+        if (!empty) {
+            tmem_ld_wait();
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) ra[j] = rb[j] = 0u;
+        }
+        uint8_t* box = w.stage + w.slot * kEpiSlotBytes;
+        mbar_wait_bounded(&w.bar[w.slot], (w.phase >> w.slot) & 1u, a.err, kDevTimeoutFull);
+        w.phase ^= 1u << w.slot;
+        w.pend &= ~(1u << w.slot);
+        if (a.epi == kEpiResidF32) {
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch) {
+                float4* p = reinterpret_cast<float4*>(box + box_off_f32(lane, ch));
+                float4 q = *p;
+                q.x += __uint_as_float(ra[4 * ch]);
+                q.y += __uint_as_float(ra[4 * ch + 1]);
+                q.z += __uint_as_float(ra[4 * ch + 2]);
+                q.w += __uint_as_float(ra[4 * ch + 3]);
+                *p = q;
+            }
+        } else {
+            // dGELU in place: 16-byte chunks 0-3 of a row hold columns c*32.., 4-7 the next 32
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch) {
+                uint4* p = reinterpret_cast<uint4*>(box + box_off_f32(lane, ch));
+                const uint4 hp = *p;
+                const uint32_t h[4] = {hp.x, hp.y, hp.z, hp.w};
+                uint32_t o[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int j = 8 * (ch & 3) + 2 * k;
+                    const float x0 = __uint_as_float(ch < 4 ? ra[j] : rb[j]);
+                    const float x1 = __uint_as_float(ch < 4 ? ra[j + 1] : rb[j + 1]);
+                    o[k] = pack_bf16x2(x0 * gelu_tanh_grad(bf16_lo(h[k])),
+                                       x1 * gelu_tanh_grad(bf16_hi(h[k])));
+                }
+                *p = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            tma_store_3d(tmO, box, n0 + c * 32, row0, 0);
+            bulk_commit_group();
+        }
+        w.slot ^= 1;
+    }
+}
 
 // One accumulator tile of one warp: rows [row0, row0+32), columns [n0, n0+NCOLS), TMEM
 // columns from tbase. `empty`: the tile had no k-blocks (writes zeros).
@@ -270,6 +392,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
                                               int row0, int n0, int split, int g, int lane,
                                               EpiWarp& w, int c_begin = 0,
                                               int c_end = NCOLS / 32) {
+    if (epi_has_input(a)) {
+        epilogue_input_tile(a, tmO, tmX, tbase, empty, row0, n0, lane, w, c_begin, c_end);
+        return;
+    }
     if (a.tma_epi && a.epi == kEpiStoreBF16) {
         // two chunks per 32 x 64 box (128-byte rows): half the bulk stores of 32 x 32 boxes.
         // A warp's chunk range has even length; a second chunk past N is clipped by the store.
@@ -336,14 +462,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
         uint8_t* box = w.stage + w.slot * kEpiSlotBytes;
         if (lane == 0) bulk_wait_group_read<1>();  // this box's previous store has read it
         __syncwarp();
-        if (a.epi == kEpiResidF32 || a.epi == kEpiDGeluBF16) {
-            if (lane == 0) {
-                mbar_arrive_expect_tx(w.bar, a.epi == kEpiResidF32 ? 4096u : 2048u);
-                tma_load_3d(box, tmX, w.bar, col0, row0, 0);
-            }
-            mbar_wait_bounded(w.bar, w.phase, a.err, kDevTimeoutFull);
-            w.phase ^= 1u;
-        }
         int x = col0, z = 0;
         bool reduce = false;
         switch (a.epi) {
@@ -364,39 +482,12 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
                 box_put_f32(box, lane, v);
                 z = split;
                 break;
-            case kEpiResidF32:
-#pragma unroll
-                for (int ch = 0; ch < 8; ++ch) {
-                    float4* p = reinterpret_cast<float4*>(box + box_off_f32(lane, ch));
-                    float4 q = *p;
-                    q.x += v[4 * ch];
-                    q.y += v[4 * ch + 1];
-                    q.z += v[4 * ch + 2];
-                    q.w += v[4 * ch + 3];
-                    *p = q;
-                }
-                break;
             case kEpiGeluBF16: {
                 box_put_bf16(box, lane, v);  // pre-activation -> aux
                 float gv[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) gv[j] = gelu_tanh(v[j]);
                 box_put_bf16(box + 2048, lane, gv);
-                break;
-            }
-            case kEpiDGeluBF16: {
-                float dv[32];
-#pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {
-                    const uint4 p = *reinterpret_cast<const uint4*>(box + box_off_bf16(lane, ch));
-                    const uint32_t h[4] = {p.x, p.y, p.z, p.w};
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        dv[8 * ch + 2 * k] = v[8 * ch + 2 * k] * gelu_tanh_grad(bf16_lo(h[k]));
-                        dv[8 * ch + 2 * k + 1] = v[8 * ch + 2 * k + 1] * gelu_tanh_grad(bf16_hi(h[k]));
-                    }
-                }
-                box_put_bf16(box + 2048, lane, dv);
                 break;
             }
             default:
@@ -407,8 +498,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
         if (lane == 0) {
             if (a.epi == kEpiGeluBF16) {
                 tma_store_3d(tmX, box, col0, row0, 0);
-                tma_store_3d(tmO, box + 2048, col0, row0, 0);
-            } else if (a.epi == kEpiDGeluBF16) {
                 tma_store_3d(tmO, box + 2048, col0, row0, 0);
             } else if (reduce) {
                 tma_reduce_add_3d(tmO, box, x, row0, z);
@@ -439,8 +528,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;
     uint64_t* acc_empty = acc_full + 2;
-    uint64_t* epi_bar = acc_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + 4);
+    uint64_t* epi_bar = acc_empty + 2;  // two per epilogue warp
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + 8);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -461,7 +550,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(&acc_full[i], 1);
             mbar_init(&acc_empty[i], 128);
         }
-        for (int i = 0; i < 4; ++i) mbar_init(&epi_bar[i], 1);
+        for (int i = 0; i < 8; ++i) mbar_init(&epi_bar[i], 1);
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -609,7 +698,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     } else if (warp >= 4) {
         // ---------------- epilogue warpgroup
         const int q = warp - 4;
-        EpiWarp ew{sEpi + q * 2 * kEpiSlotBytes, &epi_bar[q], 0u, 0};
+        EpiWarp ew{sEpi + q * 2 * kEpiSlotBytes, &epi_bar[2 * q], 0u, 0, 0u};
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
@@ -618,7 +707,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                            g, kb0, kb1))
                 continue;
             const int m0 = m_blk * BM, n0 = n_blk * BN;
-            if (!mbar_wait_bounded(&acc_full[acc], acc_phase, args.err, kDevTimeoutAcc)) break;
+            epilogue_prefetch(args, &tmX, m0 + q * 32, n0, lane, ew, 0, BN / 32);
+            if (!mbar_wait_bounded(&acc_full[acc], acc_phase, args.err, kDevTimeoutAcc)) {
+                epilogue_drain(args, lane, ew);
+                break;
+            }
             tc_fence_after();
             const uint32_t tbase =
                 tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(q * 32) << 16);
@@ -657,6 +750,8 @@ struct PairCfg {
     static constexpr int STAGES = 5;
     static constexpr uint32_t TMEM_COLS = 2 * BN;
     static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + kPairEpiStageBytes + 256;
+    // the last 256 bytes: stage, accumulator and epilogue barriers, then the TMEM address
+    static_assert((2 * STAGES + 4 + 2 * kPairEpiWarps) * 8 + 4 <= 256, "barrier area");
 };
 
 // Bytes one CTA of a pair loads per k-block (A rows from am, B rows from bn); boxes wholly
@@ -738,8 +833,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;
     uint64_t* acc_empty = acc_full + 2;
-    uint64_t* epi_bar = acc_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + kPairEpiWarps);
+    uint64_t* epi_bar = acc_empty + 2;  // two per epilogue warp
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + 2 * kPairEpiWarps);
 
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
@@ -758,7 +853,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             mbar_init(&acc_full[i], 1);
             mbar_init(&acc_empty[i], 2 * 32 * kPairEpiWarps);  // epilogue threads, both CTAs
         }
-        for (int i = 0; i < kPairEpiWarps; ++i) mbar_init(&epi_bar[i], 1);
+        for (int i = 0; i < 2 * kPairEpiWarps; ++i) mbar_init(&epi_bar[i], 1);
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -900,7 +995,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const int e = warp - 4;
         const int q = e & 3, half = e >> 2;
         const uint32_t acc_empty_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
-        EpiWarp ew{sEpi + e * 2 * kEpiSlotBytes, &epi_bar[e], 0u, 0};
+        EpiWarp ew{sEpi + e * 2 * kEpiSlotBytes, &epi_bar[2 * e], 0u, 0, 0u};
         int acc = 0;
         uint32_t acc_phase = 0;
         int g, t;
@@ -911,7 +1006,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             tile_work(args, s_grp, t, sh.num_m, sh.num_n, sh.tiles_mn, sh.kblocks, m_blk, n_blk,
                       split, gi, kb0, kb1);
             const int m0 = m_blk * Cfg::BMP + 128 * (int)rank, n0 = n_blk * BN;
-            if (!mbar_wait_bounded_cluster(&acc_full[acc], acc_phase, err, kDevTimeoutAcc)) break;
+            epilogue_prefetch(args, &P.tmX[g], m0 + q * 32, n0, lane, ew, half * (BN / 64),
+                              (half + 1) * (BN / 64));
+            if (!mbar_wait_bounded_cluster(&acc_full[acc], acc_phase, err, kDevTimeoutAcc)) {
+                epilogue_drain(args, lane, ew);
+                break;
+            }
             tc_fence_after();
             const uint32_t tbase =
                 tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(q * 32) << 16);
@@ -1068,7 +1168,7 @@ bool plan_tma_epilogue(GemmPlan* plan, const GemmArgs& a) {
         return false;
     // plain bf16 outputs leave in 32 x 64 boxes (two chunks per store)
     if (make_tmap_box(&plan->tmO, a.out, f32, x, (uint64_t)a.M, z, ys, zs,
-                      a.epi == kEpiStoreBF16))
+                      a.epi == kEpiStoreBF16 || a.epi == kEpiDGeluBF16))
         return false;
     if (a.epi == kEpiResidF32) {
         const uint64_t rs = (uint64_t)a.ldr * 4;
@@ -1078,7 +1178,7 @@ bool plan_tma_epilogue(GemmPlan* plan, const GemmArgs& a) {
     } else if (a.epi == kEpiGeluBF16 || a.epi == kEpiDGeluBF16) {
         const uint64_t xs = (uint64_t)a.ld_aux * 2;
         if (make_tmap_box(&plan->tmX, a.aux, false, (uint64_t)a.N, (uint64_t)a.M, 1, xs,
-                          (xs * a.M + 15) & ~(uint64_t)15))
+                          (xs * a.M + 15) & ~(uint64_t)15, a.epi == kEpiDGeluBF16))
             return false;
     } else {
         plan->tmX = plan->tmO;

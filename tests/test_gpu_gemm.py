@@ -49,11 +49,14 @@ def test_gemm_majors_tiles(cuda, a_mn, b_mn, bn, M, N, K):
     assert _rel(got, ref) < 1e-4, _rel(got, ref)
 
 
-@pytest.mark.parametrize("bn", [0, 512])  # planner's choice, CTA pair
-def test_gemm_epilogues(cuda, bn):
+@pytest.mark.parametrize("bn", [0, 128, 256, 512])  # planner's choice, one CTA, CTA pair
+@pytest.mark.parametrize("M,N,K", [(384, 320, 256),
+                                   # several tiles per CTA or pair; the last tile column ends
+                                   # inside a 32-column chunk and after an odd chunk count
+                                   (8192, 968, 128)])
+def test_gemm_epilogues(cuda, bn, M, N, K):
     from llmgpu import ops
     g = torch.Generator().manual_seed(5)
-    M, N, K = 384, 320, 256
     a = _mk((M, K), g, 0.5).to(cuda)
     b = _mk((K, N), g, 0.5).to(cuda)          # MN-major B, like x @ W
     ref = a.float() @ b.float()
