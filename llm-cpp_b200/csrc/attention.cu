@@ -329,6 +329,47 @@ __global__ void attn_dvec_kernel(const bf16* __restrict__ out, const bf16* __res
     dvec[((long long)b * H + h) * T + t] = acc;
 }
 
+// The same by token rows: a warp per row, lanes reading consecutive 16-byte pieces (all ITER
+// loads of a lane in flight at once), and the LPH = HD/8 lanes of a head adding their parts
+// with shuffles. Needs LPH to divide 32 and H * LPH <= 32 * ITER.
+template <int LPH, int ITER>
+__global__ void __launch_bounds__(256) attn_dvec_rows_kernel(const bf16* __restrict__ out,
+                                                             const bf16* __restrict__ dout,
+                                                             float* __restrict__ dvec, int B,
+                                                             int T, int H) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long row = blockIdx.x * 8LL + warp;  // b*T + t
+    if (row >= (long long)B * T) return;
+    const int C8 = H * LPH;  // 16-byte pieces per row
+    const uint4* o4 = reinterpret_cast<const uint4*>(out) + row * C8;
+    const uint4* d4 = reinterpret_cast<const uint4*>(dout) + row * C8;
+    uint4 a[ITER], d[ITER];
+#pragma unroll
+    for (int k = 0; k < ITER; ++k) {
+        const int u = lane + 32 * k;
+        if (u < C8) {
+            a[k] = o4[u];
+            d[k] = d4[u];
+        } else {
+            a[k] = d[k] = make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
+    const int b = (int)(row / T), t = (int)(row % T);
+#pragma unroll
+    for (int k = 0; k < ITER; ++k) {
+        const uint32_t aw[4] = {a[k].x, a[k].y, a[k].z, a[k].w};
+        const uint32_t dw[4] = {d[k].x, d[k].y, d[k].z, d[k].w};
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            acc += bf16_lo(aw[j]) * bf16_lo(dw[j]) + bf16_hi(aw[j]) * bf16_hi(dw[j]);
+#pragma unroll
+        for (int off = LPH / 2; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        const int u = lane + 32 * k;
+        if (u < C8 && (lane % LPH) == 0) dvec[((long long)b * H + u / LPH) * T + t] = acc;
+    }
+}
+
 // dK, dV for one 64-key block; warps own 16 keys each and loop over query blocks.
 template <int HD>
 __global__ void __launch_bounds__(ATT_THREADS) attn_bwd_dkdv_kernel(
@@ -611,7 +652,19 @@ int attention_backward(const bf16* qkv, const bf16* out, const bf16* dout, const
                        cudaStream_t s, int* err) {
     const float scale = 1.0f / sqrtf((float)hd);
     const long long n = (long long)B * T * H;
-    attn_dvec_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(out, dout, dvec, B, T, H, hd);
+    const int rows_blocks = (int)(((long long)B * T + 7) / 8);
+    if (hd == 64 && H * 8 <= 128) {
+        if (H * 8 <= 32)
+            attn_dvec_rows_kernel<8, 1><<<rows_blocks, 256, 0, s>>>(out, dout, dvec, B, T, H);
+        else if (H * 8 <= 64)
+            attn_dvec_rows_kernel<8, 2><<<rows_blocks, 256, 0, s>>>(out, dout, dvec, B, T, H);
+        else if (H * 8 <= 96)
+            attn_dvec_rows_kernel<8, 3><<<rows_blocks, 256, 0, s>>>(out, dout, dvec, B, T, H);
+        else
+            attn_dvec_rows_kernel<8, 4><<<rows_blocks, 256, 0, s>>>(out, dout, dvec, B, T, H);
+    } else {
+        attn_dvec_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(out, dout, dvec, B, T, H, hd);
+    }
     if (hd == 64 && !rope && (T % 4) == 0) {
         const int rc = launch_status();
         if (rc) return rc;

@@ -181,24 +181,42 @@ __global__ void __launch_bounds__(256) norm_bwd_kernel(
     }
 }
 
-// grid (C/32, 3 planes), 256 threads = 8 part-groups x 32 columns; each group sums every
-// 8th part, then the 8 group sums are added in fixed order.
-__global__ void reduce_partials_kernel(const float* __restrict__ partial, int nparts, int C,
-                                       float* out0, float* out1, float* out2, int accumulate) {
-    __shared__ float red[8][33];
+// Sums nparts partial rows of C floats: out_y[c] = sum_p part[p * pstride + y * plane_off + c]
+// for planes y = blockIdx.y (a null output skips its plane). A block is 32 columns x 32 part
+// groups; group g adds parts g, g + 32, ... in order with four loads in flight, then the 32
+// group sums are added in group order: a fixed order, so the result is deterministic.
+__global__ void __launch_bounds__(1024) sum_parts_kernel(const float* __restrict__ part,
+                                                         int nparts, long long pstride,
+                                                         long long plane_off, int C, float* out0,
+                                                         float* out1, float* out2,
+                                                         int accumulate) {
+    __shared__ float red[32][33];
     const int plane = blockIdx.y;
     float* out = plane == 0 ? out0 : (plane == 1 ? out1 : out2);
-    if (!out) return;
+    if (!out) return;  // uniform across the block
     const int cc = threadIdx.x & 31, grp = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + cc;
     float acc = 0.f;
-    if (c < C)
-        for (int p = grp; p < nparts; p += 8) acc += partial[((long long)p * 3 + plane) * C + c];
+    if (c < C) {
+        const float* base = part + plane * plane_off + c;
+        int p = grp;
+        for (; p + 96 < nparts; p += 128) {
+            const float v0 = base[(long long)p * pstride];
+            const float v1 = base[(long long)(p + 32) * pstride];
+            const float v2 = base[(long long)(p + 64) * pstride];
+            const float v3 = base[(long long)(p + 96) * pstride];
+            acc += v0;
+            acc += v1;
+            acc += v2;
+            acc += v3;
+        }
+        for (; p < nparts; p += 32) acc += base[(long long)p * pstride];
+    }
     red[grp][cc] = acc;
     __syncthreads();
     if (grp == 0 && c < C) {
         float t = 0.f;
-        for (int g = 0; g < 8; ++g) t += red[g][cc];
+        for (int g = 0; g < 32; ++g) t += red[g][cc];
         out[c] = accumulate ? out[c] + t : t;
     }
 }
@@ -249,20 +267,6 @@ __global__ void colsum_stage1(const bf16* __restrict__ a, long long lda, int row
         }
     }
     for (int k = 0; k < 8 && c0 + k < C; ++k) work[(long long)rg * C + c0 + k] = acc[k];
-}
-
-__global__ void colsum_stage2(const float* __restrict__ work, int C, float* out, int accumulate) {
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    if (c >= C) return;
-    float acc = 0.f;
-    for (int g = 0; g < kColsumGroups; g += 8) {  // 8 loads in flight, summed in group order
-        float v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = work[(long long)(g + j) * C + c];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc += v[j];
-    }
-    out[c] = accumulate ? out[c] + acc : acc;
 }
 
 }  // namespace
@@ -326,8 +330,9 @@ int norm_backward(const float* dy, const float* x, const float* gamma, const flo
 
 int reduce_partials(const float* partial, int nparts, int C, float* out0, float* out1,
                     float* out2, int accumulate, cudaStream_t s) {
-    dim3 grid((C + 31) / 32, 3);
-    reduce_partials_kernel<<<grid, 256, 0, s>>>(partial, nparts, C, out0, out1, out2, accumulate);
+    dim3 grid((C + 31) / 32, 3);  // partials are [part][3][C]
+    sum_parts_kernel<<<grid, 1024, 0, s>>>(partial, nparts, 3LL * C, C, C, out0, out1, out2,
+                                           accumulate);
     return launch_status();
 }
 
@@ -337,7 +342,8 @@ int colsum_bf16(const bf16* a, long long lda, int rows, int C, float* out, int a
                 float* work, cudaStream_t s) {
     dim3 g1((C + 2047) / 2048, kColsumGroups);
     colsum_stage1<<<g1, 256, 0, s>>>(a, lda, rows, C, work);
-    colsum_stage2<<<(C + 255) / 256, 256, 0, s>>>(work, C, out, accumulate);
+    sum_parts_kernel<<<dim3((C + 31) / 32, 1), 1024, 0, s>>>(work, kColsumGroups, C, 0, C, out,
+                                                             nullptr, nullptr, accumulate);
     return launch_status();
 }
 
