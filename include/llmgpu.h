@@ -151,6 +151,10 @@ void* llmgpu_stream(const llmgpu_ctx* ctx);
  * milliseconds and launch count since the last reset (reset != 0 clears them). */
 int llmgpu_set_profile(llmgpu_ctx* ctx, int enable);
 int llmgpu_gemm_stats(llmgpu_ctx* ctx, double* flops, double* ms, int* launches, int reset);
+/* Per GEMM launch of the last profiled step, in launch order: shapes[6*i..6*i+5] = M, N, K of
+ * the launch's first product and of its second (zeros for a single product), ms[i] its
+ * device time. Fills at most cap entries (either pointer may be null); returns the count. */
+int llmgpu_gemm_last_step(llmgpu_ctx* ctx, int32_t* shapes, float* ms, int cap);
 /* MoE routing of the last forward pass (introspection; the reference's MoEFFN keeps its
  * choices internal, src/moe.cpp:36-45): the top-k expert indices [B*T, k] chosen by block
  * `layer`'s router, in descending router probability (ties: lower index first). Copies at

@@ -133,9 +133,11 @@ int run_step(Ctx* c, int B, int T, int accumulate, bool do_step, int K) {
         cudaEventElapsedTime(&c->timings[5], c->ev[0], c->ev[3]);
     }
     if (c->profile) {
+        c->prof_last_ms.assign(c->prof_n, 0.f);
         for (size_t i = 0; i < c->prof_n; ++i) {
             float ms = 0.f;
             cudaEventElapsedTime(&ms, c->prof_ev[2 * i], c->prof_ev[2 * i + 1]);
+            c->prof_last_ms[i] = ms;
             c->prof_total_ms += ms;
             c->prof_total_flops += c->prof_flops[i];
         }
@@ -457,6 +459,18 @@ int llmgpu_gemm_stats(llmgpu_ctx* h, double* flops, double* ms, int* launches, i
         c->prof_launches = 0;
     }
     return 0;
+}
+
+int llmgpu_gemm_last_step(llmgpu_ctx* h, int32_t* shapes, float* ms, int cap) {
+    if (check_ctx(h) || cap < 0) return LLMGPU_E_ARG;
+    Ctx* c = h->c;
+    const int n = (int)c->prof_last_ms.size();
+    for (int i = 0; i < n && i < cap; ++i) {
+        if (shapes)
+            for (int j = 0; j < 6; ++j) shapes[6 * i + j] = c->prof_shape[6 * i + j];
+        if (ms) ms[i] = c->prof_last_ms[i];
+    }
+    return n;
 }
 
 int64_t llmgpu_moe_routing(llmgpu_ctx* h, int layer, int32_t* idx, int64_t n) {

@@ -287,7 +287,7 @@ int gemm_prepare(Ctx* c, GemmCall& g) {
     return 0;
 }
 
-void prof_begin(Ctx* c, double flops) {
+void prof_begin(Ctx* c, const GemmCall& g0, const GemmCall* g1 = nullptr) {
     if (!c->profile) return;
     if (c->prof_ev.size() < 2 * (c->prof_n + 1)) {
         cudaEvent_t e0, e1;
@@ -296,6 +296,14 @@ void prof_begin(Ctx* c, double flops) {
         c->prof_ev.push_back(e0);
         c->prof_ev.push_back(e1);
         c->prof_flops.push_back(0);
+        c->prof_shape.resize(c->prof_shape.size() + 6, 0);
+    }
+    double flops = 2.0 * g0.M * g0.N * (double)g0.K;
+    int* sh = &c->prof_shape[6 * c->prof_n];
+    sh[0] = g0.M, sh[1] = g0.N, sh[2] = g0.K, sh[3] = sh[4] = sh[5] = 0;
+    if (g1) {
+        flops += 2.0 * g1->M * g1->N * (double)g1->K;
+        sh[3] = g1->M, sh[4] = g1->N, sh[5] = g1->K;
     }
     c->prof_flops[c->prof_n] = flops;
     cudaEventRecord(c->prof_ev[2 * c->prof_n], c->stream);
@@ -321,7 +329,7 @@ int gemm(Ctx* c, const void* A, long long lda, int amn, const void* B, long long
     GemmCall g{A, lda, amn, B, ldb, bmn, M, N, K, a, splits, 0, nullptr, 0};
     int rc = gemm_prepare(c, g);
     if (rc) return rc;
-    prof_begin(c, 2.0 * M * N * (double)K);
+    prof_begin(c, g);
     KC(gemm_run(c->plan_cache[g.plan], c->stream));
     prof_end(c);
     return gemm_finish(c, g);
@@ -348,7 +356,7 @@ int gemm_dual(Ctx* c, GemmCall g0, GemmCall g1) {
                                          c->plan_cache[g1.plan], c->num_sms) == 0;
         c->plan2_keys[i] = key;
     }
-    prof_begin(c, 2.0 * g0.M * g0.N * (double)g0.K + 2.0 * g1.M * g1.N * (double)g1.K);
+    prof_begin(c, g0, &g1);
     if (c->plan2_ok[i]) {
         KC(gemm_run2(c->plan2_cache[i], c->stream));
     } else {

@@ -186,6 +186,8 @@ struct Ctx {
     bool profile = false;
     std::vector<cudaEvent_t> prof_ev;
     std::vector<double> prof_flops;
+    std::vector<int> prof_shape;     // per launch: M, N, K of each product (zeros: none)
+    std::vector<float> prof_last_ms; // per launch of the last profiled step
     size_t prof_n = 0;
     double prof_total_flops = 0, prof_total_ms = 0;
     int prof_launches = 0;

@@ -56,6 +56,7 @@ SIGS = {
     "llmgpu_set_profile": ([c_vp, c_int], c_int),
     "llmgpu_gemm_stats": ([c_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
                            P_int, c_int], c_int),
+    "llmgpu_gemm_last_step": ([c_vp, P_i32, P_f32, c_int], c_int),
     "llmgpu_moe_routing": ([c_vp, c_int, P_i32, ctypes.c_int64], ctypes.c_int64),
 }
 

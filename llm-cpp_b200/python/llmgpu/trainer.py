@@ -238,6 +238,18 @@ class Trainer:
                                    int(reset))
         return f.value, ms.value, n.value
 
+    def gemm_last_step(self):
+        """Per GEMM launch of the last profiled step: (shapes [n, 6] = M, N, K of the first and
+        second product, device ms [n])."""
+        n = self.lib.llmgpu_gemm_last_step(self.h, None, None, 0)
+        shapes = np.zeros((max(n, 0), 6), np.int32)
+        ms = np.zeros(max(n, 0), np.float32)
+        if n > 0:
+            self.lib.llmgpu_gemm_last_step(
+                self.h, shapes.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                ms.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), n)
+        return shapes, ms
+
     def moe_routing(self, layer, B, T, k):
         """Top-k expert indices [B*T, k] chosen by block `layer` in the last forward pass."""
         out = np.empty((B * T, k), np.int32)
