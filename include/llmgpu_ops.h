@@ -85,9 +85,13 @@ int llmgpu_op_cross_entropy(void* logits_bf16, int rows, int V, int Vp, const in
  * and dQ/dK are returned for the unrotated inputs. */
 int llmgpu_op_attention_fwd(const void* qkv, void* out, float* lse, int B, int T, int H, int hd,
                             const float* rope_cs, void* stream);
+/* The backward's `work` must hold llmgpu_op_attention_bwd_work(B, T, H, hd) bytes (the dS
+ * tiles that the dK/dV kernel stores and the dQ kernel reads; 0 bytes when head_dim or the
+ * rotation keep it off the tcgen05 kernels), 256-byte aligned. */
 int llmgpu_op_attention_bwd(const void* qkv, const void* out, const void* dout, const float* lse,
                             float* dvec, void* dqkv, int B, int T, int H, int hd,
-                            const float* rope_cs, void* stream);
+                            const float* rope_cs, void* work, void* stream);
+long long llmgpu_op_attention_bwd_work(int B, int T, int H, int hd);
 /* SILU-gated FFN activation (src/transformer.cpp:22-30, 76-89) over h13 = [h1 | h3]
  * ([rows, 2F] bf16): gated = silu(h1) * h3; backward gives dh13 = [dh1 | dh3]. */
 int llmgpu_op_swiglu_fwd(const void* h13, void* gated, int rows, int F, void* stream);

@@ -336,7 +336,13 @@ struct BwdSmem {
     static constexpr int BAR = STAGE0 + kBwdStages * STAGE_BYTES;
     static constexpr int TOTAL = BAR + 256;
 };
-constexpr size_t kBwdSmemBytes = 1024 + BwdSmem::TOTAL;
+// The dK/dV kernel also stages each elementwise warp's 32 x 64 block of dS^T (4 KB, 128-byte
+// swizzle) for a bulk store to the dS tiles the dQ kernel reads.
+constexpr int kDsBoxOff = (BwdSmem::TOTAL + 1023) & ~1023;
+constexpr size_t kDkdvSmemBytes = 1024 + kDsBoxOff + 8 * 4096;
+
+// Compact causal tile index of (query tile qi, key tile kj), kj <= qi.
+__device__ __forceinline__ int ds_tile(int qi, int kj) { return qi * (qi + 1) / 2 + kj; }
 
 __device__ __forceinline__ void store_row64_bf16(bf16* dst, const uint32_t (&r)[32], float mul) {
     uint4* o4 = reinterpret_cast<uint4*>(dst);
@@ -413,7 +419,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv,
                             const __grid_constant__ CUtensorMap tm_do,
                             const __grid_constant__ CUtensorMap tm_lse,
-                            const __grid_constant__ CUtensorMap tm_d, bf16* __restrict__ dqkv,
+                            const __grid_constant__ CUtensorMap tm_d,
+                            const __grid_constant__ CUtensorMap tm_ds, bf16* __restrict__ dqkv,
                             int B, int T, int H, float scale, int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -424,6 +431,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int C = H * kHD;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float scale_log2 = scale * kLog2ef;
+    const int ntiles = nqb * (nqb + 1) / 2;
     constexpr uint32_t kColDV = 256, kColDK = 320, kColP = 384, kColDS = 448;
 
     if (threadIdx.x == 0) bwd_init(k, 256);
@@ -596,6 +604,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     sv[i] = pack_bf16x2(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1]));
                     dp[i] = pack_bf16x2(__uint_as_float(dp[2 * i]), __uint_as_float(dp[2 * i + 1]));
                 }
+                {
+                    // this warp's 32 keys x 64 queries of dS^T also go to the dS tiles
+                    uint8_t* box = sm + kDsBoxOff + (warp - 2) * 4096;
+                    if (lane == 0) bulk_wait_group_read<0>();  // the box's last store has read it
+                    __syncwarp();
+#pragma unroll
+                    for (int ch = 0; ch < 8; ++ch)
+                        *reinterpret_cast<uint4*>(box + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
+                            make_uint4(dp[4 * ch], dp[4 * ch + 1], dp[4 * ch + 2], dp[4 * ch + 3]);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_3d(&tm_ds, box, half * 64, lq * 32,
+                                     (w.b * H + w.h) * ntiles + ds_tile(kt + s, kt));
+                        bulk_commit_group();
+                    }
+                }
                 if (g >= 1 && !warp_wait(k.mm_done, (g - 1) & 1, err, kDevTimeoutAcc)) {
                     ok = false;
                     break;
@@ -630,6 +655,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
     }
 
+    if (warp >= 2 && lane == 0) bulk_wait_group_all();  // dS stores done before exit
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -637,193 +663,132 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 }
 
 // ---------------------------------------------------------------- dQ
-__global__ void __launch_bounds__(kBwdThreads, 1)
+// dQ_i = scale * sum_j dS_ij K_j over the dS tiles the dK/dV kernel stored (no recompute of S
+// and dP). Persistent: one CTA per SM walks the query tiles, longest first. Warp 0 loads per
+// key tile the stored dS^T (two 128-key x 64-query boxes: the MN-major A operand) and K_j
+// (the MN-major B operand), warp 1 accumulates in TMEM (two 64-column accumulators, so an
+// item's MMAs overlap the previous item's read-out), warps 2-5 write dQ. The sum over j runs
+// in key-tile order: deterministic.
+constexpr int kDqThreads = 192;
+constexpr int kDqStages = 4;
+constexpr int kDqStageBytes = 3 * kTile;
+constexpr int kDqBarOff = kDqStages * kDqStageBytes;
+constexpr size_t kDqSmemBytes = 1024 + kDqBarOff + 256;
+
+__global__ void __launch_bounds__(kDqThreads, 1)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv,
-                          const __grid_constant__ CUtensorMap tm_do,
-                          const float* __restrict__ lse_g, const float* __restrict__ dvec,
-                          bf16* __restrict__ dqkv, int B, int T, int H, float scale,
-                          int* __restrict__ err) {
+                          const __grid_constant__ CUtensorMap tm_ds, bf16* __restrict__ dqkv,
+                          int B, int T, int H, float scale, int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_u32 = smem_u32(smem_raw);
     uint8_t* sm = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
-    const BwdBars k = bwd_bars(sm);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + kDqBarOff);
+    uint64_t* empty = full + kDqStages;
+    uint64_t* acc_full = empty + kDqStages;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     const int nqb = (T + kRows - 1) / kRows;
+    const int ntiles = nqb * (nqb + 1) / 2;
     const int items = nqb * H * B;
     const int C = H * kHD;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const float scale_log2 = scale * kLog2ef;
-    constexpr uint32_t kColDQ = 256, kColDS = 320;
 
-    if (threadIdx.x == 0) bwd_init(k, 128);  // half 0 of the elementwise warps reads dQ
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kDqStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 128);
+        }
+        fence_barrier_init();
+    }
     if (warp == 1) {
-        tmem_alloc(k.tmem_slot, kBwdTmem);
+        tmem_alloc(tmem_slot, 2 * kHD);
         tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *k.tmem_slot;
-    auto stage = [&](int g) { return sm + BwdSmem::STAGE0 + (g % kBwdStages) * BwdSmem::STAGE_BYTES; };
-    auto fix = [&](int buf, int t) { return sm + BwdSmem::FIX + (2 * buf + t) * kTile; };
-    // item tile index counted from the longest: query tile nqb - 1 - tile, key tiles 0..that
+    const uint32_t tmem = *tmem_slot;
+    auto stage = [&](int g) { return sm + (g % kDqStages) * kDqStageBytes; };
 
     if (warp == 0) {
         if (lane == 0) {
             bool ok = true;
             int g = 0;
-            for (int it = blockIdx.x, n = 0; it < items && ok; it += gridDim.x, ++n) {
+            for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
                 const BwdItem w = bwd_item(it, H, B);
-                const int qt = nqb - 1 - w.tile, ns = qt + 1, fb = n & 1;
-                if (!mbar_wait_bounded(&k.fix_empty[fb], ((n >> 1) & 1) ^ 1u, err,
-                                       kDevTimeoutEmpty)) {
-                    ok = false;
-                    break;
-                }
-                mbar_arrive_expect_tx(&k.fix_full[fb], 2 * kTile);
-                tma_load_3d(fix(fb, 0), &tm_qkv, &k.fix_full[fb], w.h * kHD, qt * kRows, w.b);  // Q
-                tma_load_3d(fix(fb, 1), &tm_do, &k.fix_full[fb], w.h * kHD, qt * kRows, w.b);   // dO
-                for (int s = 0; s < ns; ++s, ++g) {
-                    if (!mbar_wait_bounded(&k.st_empty[g % kBwdStages], ((g / kBwdStages) & 1) ^ 1u,
-                                           err, kDevTimeoutEmpty)) {
+                const int qt = nqb - 1 - w.tile;
+                const int z0 = (w.b * H + w.h) * ntiles + ds_tile(qt, 0);
+                for (int j = 0; j <= qt; ++j, ++g) {
+                    if (!mbar_wait_bounded(&empty[g % kDqStages], ((g / kDqStages) & 1) ^ 1u, err,
+                                           kDevTimeoutEmpty)) {
                         ok = false;
                         break;
                     }
                     uint8_t* st = stage(g);
-                    uint64_t* f = &k.st_full[g % kBwdStages];
-                    mbar_arrive_expect_tx(f, 2 * kTile);
-                    tma_load_3d(st, &tm_qkv, f, C + w.h * kHD, s * kRows, w.b);              // K_j
-                    tma_load_3d(st + kTile, &tm_qkv, f, 2 * C + w.h * kHD, s * kRows, w.b);  // V_j
+                    uint64_t* f = &full[g % kDqStages];
+                    mbar_arrive_expect_tx(f, 3 * kTile);
+                    tma_load_3d(st, &tm_ds, f, 0, 0, z0 + j);           // dS^T, queries 0-63
+                    tma_load_3d(st + kTile, &tm_ds, f, 64, 0, z0 + j);  // queries 64-127
+                    tma_load_3d(st + 2 * kTile, &tm_qkv, f, C + w.h * kHD, j * kRows, w.b);  // K_j
                 }
             }
-            if (!ok) spin_ns(100000);
+            if (!ok) spin_ns(100000);  // error path: let copies in flight land first
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc_s = make_idesc_bf16(kRows, kRows, 0, 0);
-            const uint32_t idesc_acc = make_idesc_bf16(kRows, kHD, 0, 1);
+            const uint32_t idesc = make_idesc_bf16(kRows, kHD, 1, 1);
             bool ok = true;
-            auto issue_sdp = [&](int g, int n, int s, int ns) -> bool {
-                const int fb = n & 1;
-                if (s == 0 && !mbar_wait_bounded(&k.fix_full[fb], (n >> 1) & 1, err, kDevTimeoutFull))
-                    return false;
-                if (!mbar_wait_bounded(&k.st_full[g % kBwdStages], (g / kBwdStages) & 1, err,
-                                       kDevTimeoutFull))
-                    return false;
-                tc_fence_after();
-                const uint32_t q_addr = smem_u32(fix(fb, 0)), do_addr = smem_u32(fix(fb, 1));
-                const uint32_t k_addr = smem_u32(stage(g)), v_addr = k_addr + kTile;
-#pragma unroll
-                for (int kk = 0; kk < kHD / 16; ++kk)  // S = Q K^T
-                    umma_bf16(tmem, make_sw128_desc(q_addr + kk * 32, 16, 1024),
-                              make_sw128_desc(k_addr + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
-#pragma unroll
-                for (int kk = 0; kk < kHD / 16; ++kk)  // dP = dO V^T
-                    umma_bf16(tmem + 128, make_sw128_desc(do_addr + kk * 32, 16, 1024),
-                              make_sw128_desc(v_addr + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
-                umma_commit(k.s_full);
-                if (s == ns - 1) umma_commit(&k.fix_empty[fb]);  // Q, dO of the item read
-                return true;
-            };
-            auto item_ns = [&](int it) { return it < items ? nqb - bwd_item(it, H, B).tile : 0; };
-            int it = blockIdx.x, n = 0, s = 0, ns = item_ns(it);
-            if (it < items) ok = issue_sdp(0, 0, 0, ns);
-            for (int g = 0; it < items && ok; ++g) {
-                int it1 = it, n1 = n, s1 = s + 1, ns1 = ns;
-                if (s1 == ns) {
-                    it1 = it + gridDim.x;
-                    n1 = n + 1;
-                    s1 = 0;
-                    ns1 = item_ns(it1);
+            int g = 0;
+            for (int it = blockIdx.x, n = 0; it < items && ok; it += gridDim.x, ++n) {
+                const int qt = nqb - 1 - bwd_item(it, H, B).tile;
+                const int acc = n & 1;
+                if (!mbar_wait_bounded(&acc_empty[acc], ((n >> 1) & 1) ^ 1u, err,
+                                       kDevTimeoutAccFree)) {
+                    ok = false;
+                    break;
                 }
-                if (it1 < items) {
-                    if (!mbar_wait_bounded(k.s_free, g & 1, err, kDevTimeoutAccFree) ||
-                        !issue_sdp(g + 1, n1, s1, ns1)) {
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(acc * kHD);
+                for (int j = 0; j <= qt; ++j, ++g) {
+                    if (!mbar_wait_bounded(&full[g % kDqStages], (g / kDqStages) & 1, err,
+                                           kDevTimeoutFull)) {
                         ok = false;
                         break;
                     }
-                }
-                if (!mbar_wait_bounded(k.p_full, g & 1, err, kDevTimeoutFull) ||
-                    (s == 0 && n > 0 &&
-                     !mbar_wait_bounded(k.acc_free, (n - 1) & 1, err, kDevTimeoutAccFree))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t k_addr = smem_u32(stage(g));
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(stage(g)), b_addr = a_addr + 2 * kTile;
 #pragma unroll
-                for (int kk = 0; kk < kRows / 16; ++kk)  // dQ += dS K
-                    umma_bf16_ts(tmem + kColDQ, tmem + kColDS + kk * 8,
-                                 make_sw128_desc(k_addr + kk * 2048, 8192, 1024), idesc_acc,
-                                 (s > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(k.mm_done);
-                umma_commit(&k.st_empty[g % kBwdStages]);
-                it = it1;
-                n = n1;
-                s = s1;
-                ns = ns1;
+                    for (int kk = 0; kk < kRows / 16; ++kk)  // 16 keys per MMA
+                        umma_bf16(d, make_sw128_desc(a_addr + kk * 2048, kTile, 1024),
+                                  make_sw128_desc(b_addr + kk * 2048, 8192, 1024), idesc,
+                                  (j > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit(&empty[g % kDqStages]);
+                }
+                if (!ok) break;
+                umma_commit(&acc_full[acc]);
             }
         }
     } else {
-        // ---------------- elementwise warps: thread = query row, 64 key columns
-        const int lq = warp & 3, half = (warp - 2) >> 2;
-        const int qr = lq * 32 + lane;
+        // ---------------- warps 2-5: TMEM lane quarter warp % 4, one query row per thread
+        const int lq = warp & 3;
         const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
-        bool ok = true;
-        int g = 0;
-        for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+        for (int it = blockIdx.x, n = 0; it < items; it += gridDim.x, ++n) {
             const BwdItem w = bwd_item(it, H, B);
-            const int qt = nqb - 1 - w.tile, ns = qt + 1;
-            const int q = qt * kRows + qr;
-            const long long li = ((long long)w.b * H + w.h) * T + q;
-            const float lse_l2 = q < T ? lse_g[li] * kLog2ef : 0.f;
-            const float dq_row = q < T ? dvec[li] : 0.f;
-            for (int s = 0; s < ns && ok; ++s, ++g) {
-                const int kc0 = s * kRows + half * 64;
-                if (!warp_wait(k.s_full, g & 1, err, kDevTimeoutAcc)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                uint32_t sv[64], dp[64];
-                tmem_ld_32x32b_x32(tmem + lane_base + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-                tmem_ld_32x32b_x32(tmem + lane_base + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-                tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
-                tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[32]));
-                tmem_ld_wait();
-                tc_fence_before();
-                mbar_arrive(k.s_free);
-#pragma unroll
-                for (int c = 0; c < 64; ++c) {
-                    float p = ex2_approx(fmaf(__uint_as_float(sv[c]), scale_log2, -lse_l2));
-                    if (kc0 + c > q || q >= T) p = 0.f;
-                    dp[c] = __float_as_uint(p * (__uint_as_float(dp[c]) - dq_row));
-                }
-#pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    dp[i] = pack_bf16x2(__uint_as_float(dp[2 * i]), __uint_as_float(dp[2 * i + 1]));
-                if (g >= 1 && !warp_wait(k.mm_done, (g - 1) & 1, err, kDevTimeoutAcc)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                tmem_st_32x32b_x32(tmem + lane_base + kColDS + half * 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
-                tmem_st_wait();
-                tc_fence_before();
-                mbar_arrive(k.p_full);
-            }
-            if (half != 0) continue;
-            // half 0 drains dQ; the accumulator is free for the next item once read
-            if (!ok || !warp_wait(k.mm_done, (g - 1) & 1, err, kDevTimeoutAcc)) {
-                ok = false;
-                break;
-            }
+            const int qt = nqb - 1 - w.tile;
+            const int acc = n & 1;
+            if (!warp_wait(&acc_full[acc], (n >> 1) & 1, err, kDevTimeoutAcc)) break;
             tc_fence_after();
             uint32_t r0[32], r1[32];
-            tmem_ld_32x32b_x32(tmem + lane_base + kColDQ, r0);
-            tmem_ld_32x32b_x32(tmem + lane_base + kColDQ + 32, r1);
+            tmem_ld_32x32b_x32(tmem + lane_base + (uint32_t)(acc * kHD), r0);
+            tmem_ld_32x32b_x32(tmem + lane_base + (uint32_t)(acc * kHD + 32), r1);
             tmem_ld_wait();
             tc_fence_before();
-            mbar_arrive(k.acc_free);
+            mbar_arrive(&acc_empty[acc]);
+            const int q = qt * kRows + lq * 32 + lane;
             if (q < T) {
                 bf16* dst = dqkv + ((long long)w.b * T + q) * 3LL * C + w.h * kHD;
                 store_row64_bf16(dst, r0, scale);
@@ -835,7 +800,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, kBwdTmem);
+    if (warp == 1) tmem_dealloc(tmem, 2 * kHD);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -905,12 +870,31 @@ int encode_map(CUtensorMap* tm, CUtensorMapDataType dt, int rank, const void* pt
 }
 }  // namespace
 
+size_t attention_ds_bytes(int B, int T, int H) {
+    const long long nqb = (T + kRows - 1) / kRows;
+    return (size_t)B * H * (nqb * (nqb + 1) / 2) * kRows * kRows * sizeof(bf16);
+}
+
 int attention_backward_tc(const bf16* qkv, const bf16* dout, const float* lse, const float* dvec,
-                          bf16* dqkv, int B, int T, int H, int hd, int* err, cudaStream_t s) {
-    if (hd != kHD || B <= 0 || T <= 0 || H <= 0 || (T % 4) != 0) return -1;
+                          bf16* dqkv, int B, int T, int H, int hd, void* ds_work, int* err,
+                          cudaStream_t s) {
+    if (hd != kHD || B <= 0 || T <= 0 || H <= 0 || (T % 4) != 0 || !ds_work) return -1;
     const int C = H * hd;
-    CUtensorMap tq, tdo, tl, td;
+    CUtensorMap tq, tdo, tl, td, tds_st, tds_ld;
     if (attention_qkv_tmap(&tq, qkv, B, T, C)) return -2;
+    {
+        // dS^T tiles: [B*H*tiles][128 keys][128 queries] bf16
+        const int nqb = (T + kRows - 1) / kRows;
+        const cuuint64_t dims[3] = {(cuuint64_t)kRows, (cuuint64_t)kRows,
+                                    (cuuint64_t)B * H * (nqb * (nqb + 1) / 2)};
+        const cuuint64_t strides[2] = {(cuuint64_t)kRows * 2, (cuuint64_t)kRows * kRows * 2};
+        const cuuint32_t box_st[3] = {64, 32, 1}, box_ld[3] = {64, kRows, 1};
+        if (encode_map(&tds_st, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ds_work, dims, strides,
+                       box_st, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            encode_map(&tds_ld, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ds_work, dims, strides,
+                       box_ld, CU_TENSOR_MAP_SWIZZLE_128B))
+            return -2;
+    }
     {
         const cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)T, (cuuint64_t)B};
         const cuuint64_t strides[2] = {(cuuint64_t)C * 2, (cuuint64_t)C * 2 * T};
@@ -934,9 +918,9 @@ int attention_backward_tc(const bf16* qkv, const bf16* dout, const float* lse, c
     std::call_once(once, [] {
         attr = (cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)kBwdSmemBytes) == cudaSuccess &&
+                                     (int)kDkdvSmemBytes) == cudaSuccess &&
                 cudaFuncSetAttribute(attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)kBwdSmemBytes) == cudaSuccess)
+                                     (int)kDqSmemBytes) == cudaSuccess)
                    ? 0
                    : -3;
     });
@@ -947,12 +931,12 @@ int attention_backward_tc(const bf16* qkv, const bf16* dout, const float* lse, c
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int items = ((T + kRows - 1) / kRows) * H * B;
     const int grid = items < sms ? items : sms;
-    attn_bwd_dkdv_tc_kernel<<<grid, kBwdThreads, kBwdSmemBytes, s>>>(tq, tdo, tl, td, dqkv, B, T,
-                                                                     H, scale, err);
+    attn_bwd_dkdv_tc_kernel<<<grid, kBwdThreads, kDkdvSmemBytes, s>>>(tq, tdo, tl, td, tds_st, dqkv,
+                                                                      B, T, H, scale, err);
     int rc = launch_status();
     if (rc) return rc;
-    attn_bwd_dq_tc_kernel<<<grid, kBwdThreads, kBwdSmemBytes, s>>>(tq, tdo, lse, dvec, dqkv, B, T,
-                                                                   H, scale, err);
+    attn_bwd_dq_tc_kernel<<<grid, kDqThreads, kDqSmemBytes, s>>>(tq, tds_ld, dqkv, B, T, H, scale,
+                                                                 err);
     return launch_status();
 }
 

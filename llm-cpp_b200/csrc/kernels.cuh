@@ -80,12 +80,15 @@ int rope_qk_inplace(bf16* qkv, int B, int T, int H, int hd, const float2* rope, 
                     cudaStream_t s);
 // Backward: dqkv [B*T, 3C] bf16 from dout [B*T, C]; dvec [B, H, T] fp32 scratch.
 // src/attention.cpp:183-363.
-// head_dim 64 without a fused rope and T % 4 == 0 runs on the tcgen05 kernels.
+// head_dim 64 without a fused rope and T % 4 == 0 runs on the tcgen05 kernels, which need
+// ds_work: attention_ds_bytes(B, T, H) bytes of scratch for the dS tiles.
 int attention_backward(const bf16* qkv, const bf16* out, const bf16* dout, const float* lse,
                        float* dvec, bf16* dqkv, int B, int T, int H, int hd, const float2* rope,
-                       cudaStream_t s, int* err = nullptr);
+                       cudaStream_t s, int* err = nullptr, void* ds_work = nullptr);
+size_t attention_ds_bytes(int B, int T, int H);
 int attention_backward_tc(const bf16* qkv, const bf16* dout, const float* lse, const float* dvec,
-                          bf16* dqkv, int B, int T, int H, int hd, int* err, cudaStream_t s);
+                          bf16* dqkv, int B, int T, int H, int hd, void* ds_work, int* err,
+                          cudaStream_t s);
 
 // ----------------------------------------------------------------- SwiGLU FFN
 // gated[r, j] = silu(h13[r, j]) * h13[r, F + j]   (src/transformer.cpp:22-30)

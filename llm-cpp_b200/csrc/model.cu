@@ -671,6 +671,8 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
         dalloc(c, &c->dres16, (size_t)BT * C) || dalloc(c, &c->dy16, (size_t)BT * C) ||
         dalloc(c, &c->datt, (size_t)BT * C) || dalloc(c, &c->dqkv, (size_t)BT * 3 * C) ||
         dalloc(c, &c->dh, (size_t)BT * FH) || dalloc(c, &c->dvec, (size_t)BT * c->H) ||
+        (!c->mamba &&
+         dalloc(c, &c->attn_ds, attention_ds_bytes(max_batch, max_seq, c->H) / sizeof(bf16))) ||
         (c->swiglu && dalloc(c, &c->dact, (size_t)BT * F)) ||
         dalloc(c, &c->partial, (size_t)nparts * 3 * C) ||
         dalloc(c, &c->colwork, colsum_work_floats(F > C ? F : C)))
@@ -782,6 +784,7 @@ void ctx_destroy(Ctx* c) {
     }
     F(c->xL); F(c->lnf); F(c->meanf); F(c->rstdf); F(c->logits); F(c->dres); F(c->dy);
     F(c->dln); F(c->dres16); F(c->dy16); F(c->datt); F(c->dqkv); F(c->dh); F(c->dvec);
+    F(c->attn_ds);
     for (auto& p2 : c->plan2_cache) gemm_free_plan2(&p2);
     F(c->partial); F(c->colwork); F(c->splitws); F(c->d_tokens); F(c->d_keys);
     F(c->dact); F(c->rope);
@@ -1251,11 +1254,11 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
             return rc;
         if (c->rope && hd == 64) {  // q, k were rotated in place: rotate dq, dk back
             KC(attention_backward(a.qkv, a.att, c->datt, a.lse, c->dvec, c->dqkv, B, T, H, hd,
-                                  nullptr, s, c->d_err));
+                                  nullptr, s, c->d_err, c->attn_ds));
             KC(rope_qk_inplace(c->dqkv, B, T, H, hd, c->rope, 1, s));
         } else {
             KC(attention_backward(a.qkv, a.att, c->datt, a.lse, c->dvec, c->dqkv, B, T, H, hd,
-                                  c->rope, s, c->d_err));
+                                  c->rope, s, c->d_err, c->attn_ds));
         }
         GemmArgs wq = epi_args(kEpiStoreF32, gp(b.Wq), C);
         wq.accumulate = acc;

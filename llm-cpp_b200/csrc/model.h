@@ -132,6 +132,7 @@ struct Ctx {
     bf16* logits = nullptr;
     // backward scratch
     float *dres = nullptr, *dy = nullptr, *dln = nullptr;
+    bf16* attn_ds = nullptr;  // dS tiles of the attention backward (attention_ds_bytes)
     bf16 *dres16 = nullptr, *dy16 = nullptr, *datt = nullptr, *dqkv = nullptr, *dh = nullptr,
          *dact = nullptr;
     float* dvec = nullptr;

@@ -103,12 +103,18 @@ extern "C" int llmgpu_op_attention_fwd(const void* qkv, void* out, float* lse, i
 
 extern "C" int llmgpu_op_attention_bwd(const void* qkv, const void* out, const void* dout,
                                        const float* lse, float* dvec, void* dqkv, int B, int T,
-                                       int H, int hd, const float* rope_cs, void* stream) {
+                                       int H, int hd, const float* rope_cs, void* work,
+                                       void* stream) {
     return attention_backward(reinterpret_cast<const bf16*>(qkv), reinterpret_cast<const bf16*>(out),
                               reinterpret_cast<const bf16*>(dout), lse, dvec,
                               reinterpret_cast<bf16*>(dqkv), B, T, H, hd,
                               reinterpret_cast<const float2*>(rope_cs),
-                              reinterpret_cast<cudaStream_t>(stream));
+                              reinterpret_cast<cudaStream_t>(stream), nullptr, work);
+}
+
+extern "C" long long llmgpu_op_attention_bwd_work(int B, int T, int H, int hd) {
+    if (B <= 0 || T <= 0 || H <= 0 || hd != 64) return 0;
+    return (long long)attention_ds_bytes(B, T, H);
 }
 
 extern "C" int llmgpu_op_swiglu_fwd(const void* h13, void* gated, int rows, int F, void* stream) {

@@ -35,7 +35,10 @@ def _declare(lib):
                                             c_float, c_vp]
     lib.llmgpu_op_attention_fwd.argtypes = [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp,
                                             c_vp]
-    lib.llmgpu_op_attention_bwd.argtypes = [c_vp] * 6 + [c_int, c_int, c_int, c_int, c_vp, c_vp]
+    lib.llmgpu_op_attention_bwd.argtypes = [c_vp] * 6 + [c_int, c_int, c_int, c_int, c_vp, c_vp,
+                                                         c_vp]
+    lib.llmgpu_op_attention_bwd_work.argtypes = [c_int, c_int, c_int, c_int]
+    lib.llmgpu_op_attention_bwd_work.restype = c_ll
     lib.llmgpu_op_swiglu_fwd.argtypes = [c_vp, c_vp, c_int, c_int, c_vp]
     lib.llmgpu_op_swiglu_bwd.argtypes = [c_vp, c_vp, c_vp, c_int, c_int, c_vp]
     lib.llmgpu_op_gemm_grouped.argtypes = [c_vp, c_ll, c_int, c_vp, c_ll, c_int, c_int, c_int,

@@ -130,9 +130,11 @@ def attention_bwd(qkv, out, dout, lse, B, T, H, hd, rope=None):
     lib = load()
     dqkv = torch.zeros_like(qkv)
     dvec = torch.empty(B, H, T, device=qkv.device)
+    nbytes = int(lib.llmgpu_op_attention_bwd_work(B, T, H, hd))
+    work = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=qkv.device)
     _sync_check(lib.llmgpu_op_attention_bwd(_ptr(qkv), _ptr(out), _ptr(dout), _ptr(lse),
                                             _ptr(dvec), _ptr(dqkv), B, T, H, hd, _ptr(rope),
-                                            _stream()), "attention_bwd")
+                                            _ptr(work), _stream()), "attention_bwd")
     return dqkv
 
 
