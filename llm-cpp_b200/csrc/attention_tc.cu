@@ -303,25 +303,26 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 // ============================================================================ backward
-// Two deterministic kernels (no atomics), head_dim 64, 320 threads each:
-//   warp 0     TMA producer        warp 1     TMEM allocator + MMA issuer
-//   warps 2-9  elementwise: warp w handles TMEM lane quarter w % 4 (one row per thread) and
-//              column half (w - 2) / 4 of every 128-wide score tile, so two warps share each
-//              SM sub-partition.
-// With P = exp(S * scale - lse) (rows: queries) and D = rowsum(dO o O):
+// Two deterministic kernels (no atomics), head_dim 64. With P = exp(S * scale - lse) (rows:
+// queries) and D = rowsum(dO o O):
 //   dS = P o (dP - D), dP = dO V^T, dV = P^T dO, dK = scale dS^T Q, dQ = scale dS K.
-// dK/dV kernel (work item: a 128-key tile of one head, over the query tiles that see it):
+// dK/dV kernel (320 threads; work item: a 128-key tile of one head, over the query tiles
+// that see it):
+//   warp 0     TMA producer        warp 1     TMEM allocator + MMA issuer
+//   warps 2-9  elementwise: warp w handles TMEM lane quarter w % 4 (one key row per thread)
+//              and column half (w - 2) / 4 of every 128-wide score tile, so two warps share
+//              each SM sub-partition.
 // S^T = K Q^T and dP^T = V dO^T in TMEM; P^T and dS^T (bf16) written back to TMEM feed
-// dV += P^T dO and dK += dS^T Q as A-from-TMEM MMAs. dQ kernel (work item: a query tile over
-// key tiles 0..i): S, dP as in the forward, dQ += dS K. The next tile's S / dP MMAs run while
-// the elementwise warps work on the current one; the streamed inputs pass through 3-stage
-// TMA rings.
-// Both kernels are persistent: one CTA per SM walks the work items from the longest (most
-// tiles) down, CTA c taking items c, c + grid, ...; every role counts tiles across items, the
-// fixed tiles of an item (K, V or Q, dO) are double buffered so that the next item's load
-// overlaps the current one, and the next item's first S / dP MMAs run while the current
-// item's accumulators are drained.
-// TMEM (512 columns): S [0,128), dP [128,256), accumulators from 256, bf16 operands after.
+// dV += P^T dO and dK += dS^T Q as A-from-TMEM MMAs, and dS^T also goes out to a table of
+// dS tiles in global memory. The next tile's S / dP MMAs run while the elementwise warps
+// work on the current one; Q, dO, lse and D stream through a 3-stage TMA ring. The kernel is
+// persistent: one CTA per SM walks the work items from the longest (most tiles) down, CTA c
+// taking items c, c + grid, ...; every role counts tiles across items, the fixed K and V
+// tiles of an item are double buffered so that the next item's load overlaps the current
+// one, and the next item's first S / dP MMAs run while the current item's accumulators are
+// drained. TMEM (512 columns): S [0,128), dP [128,256), dV and dK accumulators [256,384),
+// bf16 P and dS operands [384,512).
+// dQ kernel (further down): dQ_i = scale * sum_j dS_ij K_j from the stored dS tiles.
 constexpr int kBwdThreads = 320;
 constexpr int kBwdStages = 3;
 constexpr uint32_t kBwdTmem = 512;
