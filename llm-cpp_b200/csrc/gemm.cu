@@ -223,12 +223,15 @@ __device__ __forceinline__ void epi_store(const GemmArgs& a, int row, int col0, 
 
 // ---------------------------------------------------------------------------- epilogue
 // Each epilogue warp owns 32 accumulator rows (TMEM lanes) and moves a tile out in chunks of
-// 32 columns. With TMA outputs (args.tma_epi) a chunk goes registers -> a swizzled 32x32
-// box in shared memory -> one bulk tensor store (or reduce-add), so every global write is a
-// full, coalesced line; inputs of the epilogue (residual, stored pre-activation) come in
-// through TMA loads into the same box. Two 4 KB boxes per warp alternate so the store of one
-// chunk overlaps the next. Outputs whose strides a tensor map cannot describe take the
-// per-thread row stores of epi_store.
+// 32 columns. With TMA outputs (args.tma_epi) values go registers -> a swizzled box of 32
+// rows in shared memory -> one bulk tensor store (or reduce-add), so every global write is a
+// full, coalesced line. Plain bf16 outputs and dGELU pack two chunks per 32 x 64 box
+// (128-byte rows: half the bulk operations); fp32 outputs use 32 x 32 boxes, GELU's two bf16
+// outputs 32 x 32 boxes with 64-byte rows. Inputs of the epilogue (residual, stored
+// pre-activation) come in through TMA loads into the box they are combined in, one unit
+// ahead. Two 4 KB boxes per warp alternate so the store of one unit overlaps the next.
+// Outputs whose strides a tensor map cannot describe take the per-thread row stores of
+// epi_store.
 constexpr int kEpiSlotBytes = 4096;
 constexpr int kEpiStageBytes = 4 * 2 * kEpiSlotBytes;
 constexpr int kPairEpiStageBytes = kPairEpiWarps * 2 * kEpiSlotBytes;
@@ -1115,11 +1118,10 @@ int make_tmap_bf16(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t ou
     return r == CUDA_SUCCESS ? 0 : -4;
 }
 
-// 3-D tensor map of 32x32x1 boxes over an epilogue output or input: dims {x, y, z} with
-// row stride `ys` and plane stride `zs` in bytes; fp32 boxes use the 128-byte swizzle, bf16
-// boxes the 64-byte swizzle (the layouts box_off_f32 / box_off_bf16 write).
-// Boxes of 32 rows: 32 fp32 or 32 bf16 columns, or (wide) 64 bf16 columns; rows of 128
-// bytes take the 128-byte swizzle, 64-byte rows the 64-byte one.
+// 3-D tensor map over an epilogue output or input: dims {x, y, z} with row stride `ys` and
+// plane stride `zs` in bytes. Boxes are 32 rows of 32 fp32 or 32 bf16 columns, or (wide) 64
+// bf16 columns; rows of 128 bytes take the 128-byte swizzle (the layout box_off_f32
+// addresses), 64-byte rows the 64-byte one (box_off_bf16).
 int make_tmap_box(CUtensorMap* tm, const void* ptr, bool f32, uint64_t x, uint64_t y, uint64_t z,
                   uint64_t ys, uint64_t zs, bool wide = false) {
     auto enc = get_encode_fn();
