@@ -1,0 +1,68 @@
+// ORACLE harness (test infrastructure only): drives the reference's own data-feed pieces
+// (read in place from the reference tree and linked unmodified) and prints what they produce,
+// for the parity tests of the host-side feed in llm-cpp_b200/python/llmgpu/feed.py.
+//   ref_feed lr                      -> "lr base warmup max_iters min_lr cycles step value" lines
+//   ref_feed data TEXT_FILE BS       -> "tokens ...", then "loader ..." / "prefetch ..." batches
+//   ref_feed log OUT_FILE            -> MetricsLogger lines written to OUT_FILE
+// Calls: CosineScheduler::get_lr (src/scheduler.cpp:13-28), Dataset / DataLoader
+// (src/dataset.cpp:41-84), PrefetchLoader (src/prefetch.cpp), MetricsLogger::log_step
+// (src/logging.cpp:49-55).
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "llm/dataset.h"
+#include "llm/logging.h"
+#include "llm/prefetch.h"
+#include "llm/scheduler.h"
+
+static void print_batch(const char* tag, const std::vector<int>& b) {
+    std::printf("%s %zu", tag, b.size());
+    for (int t : b) std::printf(" %d", t);
+    std::printf("\n");
+}
+
+int main(int argc, char** argv) {
+    if (argc < 2) return 2;
+    if (!std::strcmp(argv[1], "lr")) {
+        struct Cfg { float base; int warmup, max_iters; float min_lr; int cycles; };
+        const Cfg cfgs[] = {{3e-4f, 100, 1000, 0.f, 1}, {1e-3f, 0, 500, 1e-5f, 1},
+                            {6e-4f, 50, 1050, 6e-5f, 4}, {1e-3f, 10, 10, 1e-4f, 1},
+                            {2e-4f, 7, 93, 0.f, 3}};
+        for (const Cfg& c : cfgs) {
+            llm::CosineScheduler s(c.base, c.warmup, c.max_iters, c.min_lr, c.cycles);
+            for (int step = 0; step <= c.max_iters + 20; step += (step < 120 ? 1 : 37))
+                std::printf("lr %.9g %d %d %.9g %d %d %.9g\n", c.base, c.warmup, c.max_iters,
+                            c.min_lr, c.cycles, step, s.get_lr(step));
+        }
+        return 0;
+    }
+    if (!std::strcmp(argv[1], "data") && argc >= 4) {
+        const size_t bs = std::strtoul(argv[3], nullptr, 10);
+        llm::Dataset ds(argv[2], bs);
+        print_batch("tokens", ds.tokens());
+        llm::DataLoader dl(ds, bs);
+        while (dl.has_next()) {
+            auto b = dl.next_batch();
+            if (b.empty()) break;
+            print_batch("loader", b[0]);
+        }
+        llm::PrefetchLoader pl(ds, bs, 2);
+        while (true) {
+            auto b = pl.next();
+            if (b.empty()) break;
+            print_batch("prefetch", b[0]);
+        }
+        return 0;
+    }
+    if (!std::strcmp(argv[1], "log") && argc >= 3) {
+        llm::MetricsLogger log(argv[2]);
+        log.log_step(1, 2.3614869f, 10.60655f, 3e-4f, 0.8754321f, 756960.19f);
+        log.log_step(20, 0.125f, 1.1331485f, 1.5e-5f, 12.5f, 1e-3f);
+        log.log_step(300, 7.0f, 1096.6332f, 0.f, 0.f, 0.f);
+        return 0;
+    }
+    return 2;
+}
