@@ -6,6 +6,7 @@ compute runs in the CUDA kernels behind the C ABI. Errors raise `LlmgpuError` wi
 library's message (the reference asserts or throws at the same points).
 """
 import ctypes
+import math
 
 import numpy as np
 
@@ -56,6 +57,8 @@ class Trainer:
                                         uidbuf)
         if not self.h:
             raise LlmgpuError(self.lib.llmgpu_last_error(None).decode())
+        self._lr = 3e-4  # the library's AdamW default
+        self._last_good = None
 
     # ------------------------------------------------------------------ lifecycle
     def close(self):
@@ -73,9 +76,31 @@ class Trainer:
     # ------------------------------------------------------------------ hyper-parameters
     def set_adamw(self, lr=3e-4, b1=0.9, b2=0.95, eps=1e-8, wd=0.1):
         self.lib.llmgpu_set_adamw(self.h, lr, b1, b2, eps, wd)
+        self._lr = float(lr)
 
     def set_lr(self, lr):
         self.lib.llmgpu_set_lr(self.h, lr)
+        self._lr = float(lr)
+
+    def get_lr(self):
+        """Optimizer::get_lr: the learning rate last set through this object."""
+        return self._lr
+
+    def snapshot_params(self):
+        """Trainer::snapshot_params (src/trainer.cpp:234-238): keep a host copy of every
+        parameter as the last good state."""
+        self._last_good = [self.get_param(i) for i in range(self.num_params())]
+
+    def rollback_if_nonfinite(self, loss):
+        """Trainer::rollback_if_nonfinite (src/trainer.cpp:239-246): if `loss` is not finite
+        and a snapshot exists, restore the snapshot's parameters and halve the learning rate.
+        Returns whether it rolled back. (Adam's moments are left as they are, as there.)"""
+        if math.isfinite(loss) or self._last_good is None:
+            return False
+        for i, p in enumerate(self._last_good):
+            self.set_param(i, p)
+        self.set_lr(self._lr * 0.5)
+        return True
 
     def set_train(self, grad_clip=1.0, grad_accum_steps=1, label_smoothing=0.0):
         rc = self.lib.llmgpu_set_train(self.h, grad_clip, grad_accum_steps, label_smoothing)
