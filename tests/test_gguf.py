@@ -1,0 +1,50 @@
+"""GGUF F32 export/import (llmgpu.gguf) against the reference's own save_gguf / load_gguf,
+run by oracle/_ref/ref_gguf on the same parameters (passed as a reference binary
+checkpoint): the files must be byte-identical, and each side must read the other's."""
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from llmgpu import gguf
+from oracle import gpt_oracle as go
+
+ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+REF = os.path.join(ROOT, "oracle", "_ref", "ref_gguf")
+
+
+def _ref(*args):
+    if not os.path.exists(REF):
+        pytest.skip("oracle/_ref/ref_gguf not built (needs the reference sources)")
+    subprocess.run([REF, *map(str, args)], check=True, capture_output=True)
+
+
+@pytest.mark.parametrize("tied,rms", [(True, False), (False, True)])
+def test_gguf_matches_reference(tmp_path, tied, rms):
+    cfg = go.Cfg(vocab=96, n_layers=2, n_heads=4, n_embd=64, block_size=48, tied=tied,
+                 rmsnorm=rms)
+    params = go.init_params(cfg, seed=5)
+    shapes = [p.shape for p in params]
+    ckpt = tmp_path / "model.bin"
+    go.write_ckpt(str(ckpt), cfg, params)
+    args = (cfg.vocab, cfg.n_layers, cfg.n_heads, cfg.n_embd, cfg.block_size, int(tied), int(rms))
+    ref_file, our_file = tmp_path / "ref.gguf", tmp_path / "ours.gguf"
+    _ref("save", *args, ckpt, ref_file)
+    gguf.write_gguf(str(our_file), params)
+    assert our_file.read_bytes() == ref_file.read_bytes()
+    arrays, kvs = gguf.read_gguf(str(ref_file), shapes)
+    assert kvs["llm.tensor_count"] == str(len(params))
+    assert all(np.array_equal(a, p) for a, p in zip(arrays, params))
+    back = tmp_path / "back.bin"
+    _ref("load", *args, our_file, back)
+    assert all(np.array_equal(a, p) for a, p in zip(go.read_ckpt(str(back), cfg), params))
+
+
+def test_gguf_rejects_a_shape_mismatch(tmp_path):
+    f = tmp_path / "x.gguf"
+    gguf.write_gguf(str(f), [np.zeros((4, 3), np.float32), np.ones((2, 3), np.float32)])
+    with pytest.raises(ValueError):
+        gguf.read_gguf(str(f), [(4, 3), (3, 3)])
+    with pytest.raises(ValueError):
+        gguf.read_gguf(str(f), [(4, 3)])
