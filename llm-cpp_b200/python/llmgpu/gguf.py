@@ -10,8 +10,12 @@
   data from the start of the data section, offsets aligned to 32 bytes;
 - zero padding to a 32-byte boundary, then each tensor's fp32 data at its offset.
 
-Reading accepts F32 tensors only (the reference's Q8_0 / Q4_0 / Q4_K storage is not read
-here) and checks the tensor count and every shape against the model.
+Reading accepts F32 tensors only and checks the tensor count and every shape against the
+model. `write_gguf_quant` writes the reference's quantized export (save_gguf_quant,
+src/gguf.cpp:499-581) for qtype 0 (F32), 8 (Q8_0: per 32 values an f32 scale
+max|x| / 127 + 1e-8 and 32 int8) and 4 (Q4_0: scale max|x| / 7 + 1e-8 and 16 bytes of
+nibbles, value + 8, even index in the low nibble), with the extra KV llm.quant_type; values
+are rounded half away from zero as std::round does. Q4_K (qtype 12) is not written.
 """
 import struct
 
@@ -61,6 +65,68 @@ def write_gguf(path, arrays):
     for a, off in zip(arrays, offsets):
         out += bytes(data_start + off - len(out))
         out += a.tobytes()
+    with open(path, "wb") as f:
+        f.write(out)
+
+
+GGUF_Q4_0 = 2
+GGUF_Q8_0 = 8
+_QBLK = 32
+
+
+def _round_away(v):
+    """std::round of float32 values (half away from zero), exact in float64."""
+    v64 = v.astype(np.float64)
+    return (np.sign(v64) * np.floor(np.abs(v64) + 0.5)).astype(np.float32)
+
+
+def _encode(a, qtype):
+    x = np.ascontiguousarray(a, dtype=np.float32).ravel()
+    if qtype == 0:
+        return x.tobytes()
+    x = np.concatenate([x, np.zeros((-x.size) % _QBLK, np.float32)]).reshape(-1, _QBLK)
+    mx = np.abs(x).max(axis=1)
+    top = np.float32(127.0 if qtype == 8 else 7.0)
+    sc = (mx / top).astype(np.float32) + np.float32(1e-8)
+    q = _round_away((x / sc[:, None]).astype(np.float32))
+    if qtype == 8:
+        body = np.clip(q, -127, 127).astype(np.int8).view(np.uint8)
+    else:
+        q = np.clip(q, -8, 7).astype(np.int32) + 8
+        body = ((q[:, 1::2] << 4) | (q[:, 0::2] & 0xF)).astype(np.uint8)
+    return np.concatenate([sc[:, None].view(np.uint8), body], axis=1).tobytes()
+
+
+def write_gguf_quant(path, arrays, qtype):
+    """The reference's save_gguf_quant for qtype 0 (F32), 8 (Q8_0) or 4 (Q4_0)."""
+    dtype = {0: GGUF_F32, 8: GGUF_Q8_0, 4: GGUF_Q4_0}.get(qtype)
+    if dtype is None:
+        raise ValueError(f"gguf: quant type {qtype} is not written here (0, 8 and 4 are)")
+    arrays = [np.asarray(a, dtype=np.float32) for a in arrays]
+    vocab = arrays[0].shape[0] if arrays else 0
+    n_embd = arrays[0].shape[1] if arrays else 0
+    block = arrays[1].shape[0] if len(arrays) >= 2 else 0
+    kvs = [("general.architecture", "llm"), ("general.name", "llm-cpp"),
+           ("llm.vocab_size", str(vocab)), ("llm.n_embd", str(n_embd)),
+           ("llm.block_size", str(block)), ("llm.tensor_count", str(len(arrays))),
+           ("llm.quant_type", str(qtype))]
+    out = bytearray(struct.pack("<IIQQ", GGUF_MAGIC, GGUF_VERSION, len(arrays), len(kvs)))
+    for k, v in kvs:
+        out += _string(k) + struct.pack("<I", GGUF_TYPE_STRING) + _string(v)
+    blobs = [_encode(a, qtype) for a in arrays]
+    offsets, cur = [], 0
+    for b in blobs:
+        cur = _align(cur)
+        offsets.append(cur)
+        cur += len(b)
+    for i, (a, off) in enumerate(zip(arrays, offsets)):
+        out += _string(f"tensor_{i}") + struct.pack("<I", a.ndim)
+        out += struct.pack(f"<{a.ndim}Q", *a.shape) + struct.pack("<IQ", dtype, off)
+    out += bytes(_align(len(out)) - len(out))
+    data_start = len(out)
+    for b, off in zip(blobs, offsets):
+        out += bytes(data_start + off - len(out))
+        out += b
     with open(path, "wb") as f:
         f.write(out)
 
@@ -124,6 +190,11 @@ def read_gguf(path, shapes=None):
 def save_gguf(trainer, path):
     """GPT save_gguf for the model on the device."""
     write_gguf(path, [trainer.get_param(i) for i in range(trainer.num_params())])
+
+
+def save_gguf_quant(trainer, path, qtype):
+    """GPT save_gguf_quant for the model on the device (qtype 0, 8 or 4)."""
+    write_gguf_quant(path, [trainer.get_param(i) for i in range(trainer.num_params())], qtype)
 
 
 def load_gguf(trainer, path):
