@@ -14,8 +14,18 @@ Reading accepts F32 tensors only and checks the tensor count and every shape aga
 model. `write_gguf_quant` writes the reference's quantized export (save_gguf_quant,
 src/gguf.cpp:499-581) for qtype 0 (F32), 8 (Q8_0: per 32 values an f32 scale
 max|x| / 127 + 1e-8 and 32 int8) and 4 (Q4_0: scale max|x| / 7 + 1e-8 and 16 bytes of
-nibbles, value + 8, even index in the low nibble), with the extra KV llm.quant_type; values
-are rounded half away from zero as std::round does. Q4_K (qtype 12) is not written.
+nibbles, value + 8, even index in the low nibble) and 12 (Q4_K: 144-byte super-blocks of
+256 values, below), with the extra KV llm.quant_type; values are rounded half away from zero
+as std::round does.
+
+Q4_K super-block (encode_q4k_block, src/gguf.cpp:160-245): per 32-value sub-block j its
+min mn_j and scale (max_j - mn_j) / 15; d = max scale / 63 and dmin = (largest -mn_j over
+negative mins, else minus the largest min) / 63, both stored as f16 by the reference's own
+f32 -> f16 rounding (round half to even, overflow saturating to 0x7BFF, its subnormal path
+masked to 10 bits); 6-bit sub-block scales and mins packed into 12 bytes; each value
+round((x + dmin_f * qmn_j) / (d_f * qsc_j)) clamped to 0..15 against the stored f16 scales,
+value i of 64-value group g at byte 32 g + i % 32, low nibble for i % 64 < 32. A super-block
+with a non-finite value is written as zeros.
 """
 import struct
 
@@ -71,6 +81,7 @@ def write_gguf(path, arrays):
 
 GGUF_Q4_0 = 2
 GGUF_Q8_0 = 8
+GGUF_Q4_K = 12
 _QBLK = 32
 
 
@@ -80,15 +91,95 @@ def _round_away(v):
     return (np.sign(v64) * np.floor(np.abs(v64) + 0.5)).astype(np.float32)
 
 
+def _f32_to_f16_bits(v):
+    """The reference's f32 -> f16 bit conversion (src/gguf.cpp:92-119), elementwise."""
+    b = np.asarray(v, np.float32).view(np.uint32).astype(np.int64)
+    sign = (b >> 16) & 0x8000
+    exp = ((b >> 23) & 0xFF) - 112
+    mant = b & 0x7FFFFF
+    out = np.zeros_like(b)
+    # normal range
+    half = mant >> 13
+    rest = mant & 0x1FFF
+    up = (rest > 0x1000) | ((rest == 0x1000) & ((half & 1) == 1))
+    half = half + up
+    e2 = exp + (half == 0x400)
+    half = np.where(half == 0x400, 0, half)
+    normal = sign | (np.clip(e2, 0, 31) << 10) | half
+    normal = np.where(e2 >= 31, sign | 0x7BFF, normal)
+    # subnormal range (exp in [-10, 0])
+    shift = np.clip(1 - exp, 1, 31)
+    m = mant | 0x800000
+    hs = m >> shift
+    rs = m & ((np.int64(1) << shift) - 1)
+    hw = np.int64(1) << (shift - 1)
+    hs = hs + ((rs > hw) | ((rs == hw) & ((hs & 1) == 1)))
+    sub = sign | (hs & 0x3FF)
+    out = np.where(exp >= 31, sign | 0x7BFF,
+                   np.where(exp >= 1, normal, np.where(exp < -10, sign, sub)))
+    return out.astype(np.uint16)
+
+
+def _f16_bits_to_f32(h):
+    return np.asarray(h, np.uint16).view(np.float16).astype(np.float32)
+
+
+def _encode_q4k(x):
+    """x: float32 [nb, 256] -> uint8 [nb, 144]."""
+    f32 = np.float32
+    nb = x.shape[0]
+    finite = np.isfinite(x).all(axis=1)
+    xs = np.where(finite[:, None], x, f32(0)).reshape(nb, 8, 32)
+    mn = xs.min(axis=2)
+    mx = xs.max(axis=2)
+    sc_true = ((mx - mn) / f32(15)).astype(f32)
+    dall_anchor = np.maximum(f32(0), sc_true.max(axis=1))
+    dall = (dall_anchor / f32(63)).astype(f32)
+    neg_max = np.where(mn < 0, -mn, f32(0)).max(axis=1)
+    pos_max = np.where(mn >= 0, mn, f32(0)).max(axis=1)
+    dmin_anchor = np.where(neg_max > 0, neg_max, -pos_max).astype(f32)
+    dmin = (dmin_anchor / f32(63)).astype(f32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        qsc = np.where(dall_anchor[:, None] > 0,
+                       np.clip(_round_away(((f32(63) * sc_true) / dall_anchor[:, None]).astype(f32)), 0, 63),
+                       0).astype(np.int64)
+        qmn = np.where(dmin_anchor[:, None] != 0,
+                       np.clip(_round_away(((f32(63) * (-mn)) / dmin_anchor[:, None]).astype(f32)), 0, 63),
+                       0).astype(np.int64)
+    out = np.zeros((nb, 144), np.uint8)
+    dh, mh = _f32_to_f16_bits(dall), _f32_to_f16_bits(dmin)
+    out[:, 0:2] = dh[:, None].view(np.uint8).reshape(nb, 2)
+    out[:, 2:4] = mh[:, None].view(np.uint8).reshape(nb, 2)
+    for j in range(4):
+        out[:, 4 + j] = (qsc[:, j] & 63) | ((qsc[:, j + 4] >> 4) << 6)
+        out[:, 8 + j] = (qmn[:, j] & 63) | ((qmn[:, j + 4] >> 4) << 6)
+        out[:, 12 + j] = (qsc[:, j + 4] & 0xF) | ((qmn[:, j + 4] & 0xF) << 4)
+    dall_f, dmin_f = _f16_bits_to_f32(dh), _f16_bits_to_f32(mh)
+    dj = (dall_f[:, None] * qsc.astype(f32)).astype(f32)  # [nb, 8]
+    dmj = (dmin_f[:, None] * qmn.astype(f32)).astype(f32)
+    xv = xs.reshape(nb, 8, 32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        q = _round_away(((xv + dmj[:, :, None]).astype(f32) / dj[:, :, None]).astype(f32))
+    q = np.where(dj[:, :, None] != 0, np.clip(q, 0, 15), 0).astype(np.int64).reshape(nb, 4, 64)
+    out[:, 16:] = (q[:, :, :32] | (q[:, :, 32:] << 4)).reshape(nb, 128).astype(np.uint8)
+    return out
+
+
 def _encode(a, qtype):
     x = np.ascontiguousarray(a, dtype=np.float32).ravel()
     if qtype == 0:
         return x.tobytes()
+    if qtype == 12:
+        x = np.concatenate([x, np.zeros((-x.size) % 256, np.float32)]).reshape(-1, 256)
+        return _encode_q4k(x).tobytes()
     x = np.concatenate([x, np.zeros((-x.size) % _QBLK, np.float32)]).reshape(-1, _QBLK)
-    mx = np.abs(x).max(axis=1)
+    # std::max(mx, |x|) from mx = 0 passes over NaN; a NaN quotient clamps to the top code
+    mx = np.where(np.isnan(x), np.float32(0), np.abs(x)).max(axis=1)
     top = np.float32(127.0 if qtype == 8 else 7.0)
     sc = (mx / top).astype(np.float32) + np.float32(1e-8)
-    q = _round_away((x / sc[:, None]).astype(np.float32))
+    with np.errstate(invalid="ignore"):
+        q = _round_away((x / sc[:, None]).astype(np.float32))
+    q = np.where(np.isnan(q), top, q)
     if qtype == 8:
         body = np.clip(q, -127, 127).astype(np.int8).view(np.uint8)
     else:
@@ -98,10 +189,10 @@ def _encode(a, qtype):
 
 
 def write_gguf_quant(path, arrays, qtype):
-    """The reference's save_gguf_quant for qtype 0 (F32), 8 (Q8_0) or 4 (Q4_0)."""
-    dtype = {0: GGUF_F32, 8: GGUF_Q8_0, 4: GGUF_Q4_0}.get(qtype)
+    """The reference's save_gguf_quant for qtype 0 (F32), 8 (Q8_0), 4 (Q4_0) or 12 (Q4_K)."""
+    dtype = {0: GGUF_F32, 8: GGUF_Q8_0, 4: GGUF_Q4_0, 12: GGUF_Q4_K}.get(qtype)
     if dtype is None:
-        raise ValueError(f"gguf: quant type {qtype} is not written here (0, 8 and 4 are)")
+        raise ValueError(f"gguf: unknown quant type {qtype} (0, 8, 4 or 12)")
     arrays = [np.asarray(a, dtype=np.float32) for a in arrays]
     vocab = arrays[0].shape[0] if arrays else 0
     n_embd = arrays[0].shape[1] if arrays else 0
@@ -193,7 +284,7 @@ def save_gguf(trainer, path):
 
 
 def save_gguf_quant(trainer, path, qtype):
-    """GPT save_gguf_quant for the model on the device (qtype 0, 8 or 4)."""
+    """GPT save_gguf_quant for the model on the device (qtype 0, 8, 4 or 12)."""
     write_gguf_quant(path, [trainer.get_param(i) for i in range(trainer.num_params())], qtype)
 
 

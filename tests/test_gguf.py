@@ -50,13 +50,16 @@ def test_gguf_rejects_a_shape_mismatch(tmp_path):
         gguf.read_gguf(str(f), [(4, 3)])
 
 
-@pytest.mark.parametrize("qtype", [0, 8, 4])
+@pytest.mark.parametrize("qtype", [0, 8, 4, 12])
 def test_quantized_gguf_matches_reference(tmp_path, qtype):
     cfg = go.Cfg(vocab=96, n_layers=2, n_heads=4, n_embd=64, block_size=48)
     params = go.init_params(cfg, seed=9)
     # an evenly spread block (both signs, the extremes at +-1) and an all-zero block
     params[0].ravel()[:32] = np.linspace(-1, 1, 32, dtype=np.float32)
     params[0].ravel()[32:64] = 0.0
+    big = next(i for i, p in enumerate(params) if i > 1 and p.size >= 1024)
+    params[big].ravel()[3] = np.nan     # non-finite values: NaN and inf in separate blocks
+    params[big].ravel()[700] = np.inf
     ckpt = tmp_path / "model.bin"
     go.write_ckpt(str(ckpt), cfg, params)
     ref_file, our_file = tmp_path / "ref.gguf", tmp_path / "ours.gguf"
@@ -66,6 +69,6 @@ def test_quantized_gguf_matches_reference(tmp_path, qtype):
     assert our_file.read_bytes() == ref_file.read_bytes()
 
 
-def test_quant_type_12_is_refused(tmp_path):
+def test_unknown_quant_type_is_refused(tmp_path):
     with pytest.raises(ValueError):
-        gguf.write_gguf_quant(str(tmp_path / "q.gguf"), [np.zeros((2, 2), np.float32)], 12)
+        gguf.write_gguf_quant(str(tmp_path / "q.gguf"), [np.zeros((2, 2), np.float32)], 5)
