@@ -4,6 +4,9 @@ Host-side mirror of the reference's feed and loop, with the reference's names an
 semantics:
 - `CosineScheduler` (src/scheduler.cpp:13-28): linear warmup, then a cosine from base_lr to
   min_lr, optionally restarted `cycles` times; fp32 arithmetic as the reference does it.
+  `StepScheduler` (:29-33): base_lr * gamma^(step // step_size).
+- `pack_with_eos`, `train_val_split` (src/dataset.cpp:86-115): rows of block_size tokens, the
+  last padded with eos_id, with 1/0 masks; a contiguous split at floor(n * train_ratio).
 - `Dataset` (src/dataset.cpp:41-58): a flat token stream; `get_batch(idx, n)` is the run
   tokens[idx:idx+n] (shorter at the end). `Dataset.from_file` reads a text file the way the
   reference does with its default tokenizer, which has no merges: one id per byte.
@@ -56,6 +59,37 @@ class CosineScheduler:
             progress = min(_F32(step - self.warmup) / _F32(span), _F32(1.0))
         c = np.cos(_F32(3.14159265) * _F32(progress), dtype=_F32)
         return float(self.min_lr + (self.base_lr - self.min_lr) * _F32(0.5) * (_F32(1.0) + c))
+
+
+class StepScheduler:
+    """get_lr(step) of the reference's StepScheduler: the power in double, the product in
+    float, as std::pow(float, int) and the float return give it."""
+
+    def __init__(self, base_lr, step_size, gamma):
+        self.base_lr, self.step_size, self.gamma = _F32(base_lr), int(step_size), _F32(gamma)
+
+    def get_lr(self, step):
+        return float(_F32(float(self.base_lr) * float(self.gamma) ** (int(step) // self.step_size)))
+
+
+def pack_with_eos(tokens, block_size, eos_id):
+    """(input rows, mask rows): the tokens in rows of block_size, the last row padded with
+    eos_id and masked 0 there."""
+    t = np.asarray(tokens, dtype=np.int32).ravel()
+    n = -(-t.size // block_size)
+    rows = np.full((n, block_size), eos_id, np.int32)
+    mask = np.zeros((n, block_size), np.int32)
+    rows.ravel()[:t.size] = t
+    mask.ravel()[:t.size] = 1
+    return rows, mask
+
+
+def train_val_split(tokens, train_ratio, seed=0):
+    """(train, val): the first floor(n * train_ratio) tokens and the rest (the seed is unused,
+    as in the reference)."""
+    t = np.asarray(tokens, dtype=np.int32).ravel()
+    k = int(t.size * float(train_ratio))
+    return t[:k], t[k:]
 
 
 class Dataset:

@@ -4,6 +4,7 @@
 //   ref_feed lr                      -> "lr base warmup max_iters min_lr cycles step value" lines
 //   ref_feed data TEXT_FILE BS       -> "tokens ...", then "loader ..." / "prefetch ..." batches
 //   ref_feed log OUT_FILE            -> MetricsLogger lines written to OUT_FILE
+//   ref_feed pack TEXT_FILE BLOCK EOS RATIO -> pack_with_eos rows/masks, train_val_split sizes
 // Calls: CosineScheduler::get_lr (src/scheduler.cpp:13-28), Dataset / DataLoader
 // (src/dataset.cpp:41-84), PrefetchLoader (src/prefetch.cpp), MetricsLogger::log_step
 // (src/logging.cpp:49-55).
@@ -37,6 +38,17 @@ int main(int argc, char** argv) {
                 std::printf("lr %.9g %d %d %.9g %d %d %.9g\n", c.base, c.warmup, c.max_iters,
                             c.min_lr, c.cycles, step, s.get_lr(step));
         }
+        const float bases[] = {3e-4f, 1e-2f};
+        const int sizes[] = {1, 7, 100};
+        const float gammas[] = {0.5f, 0.9f, 0.33f};
+        for (float base : bases)
+            for (int size : sizes)
+                for (float gamma : gammas) {
+                    llm::StepScheduler s(base, size, gamma);
+                    for (int step = 0; step < 400; step += 13)
+                        std::printf("steplr %.9g %d %.9g %d %.9g\n", base, size, gamma, step,
+                                    s.get_lr(step));
+                }
         return 0;
     }
     if (!std::strcmp(argv[1], "data") && argc >= 4) {
@@ -55,6 +67,20 @@ int main(int argc, char** argv) {
             if (b.empty()) break;
             print_batch("prefetch", b[0]);
         }
+        return 0;
+    }
+    if (!std::strcmp(argv[1], "pack") && argc >= 6) {
+        llm::Dataset ds(argv[2], 0);
+        auto packed = llm::pack_with_eos(ds.tokens(), std::strtoul(argv[3], nullptr, 10),
+                                         std::atoi(argv[4]));
+        for (size_t i = 0; i < packed.input.size(); ++i) {
+            print_batch("row", packed.input[i]);
+            print_batch("mask", packed.mask[i]);
+        }
+        std::vector<int> tr, va;
+        llm::train_val_split(ds.tokens(), std::atof(argv[5]), 7, tr, va);
+        print_batch("train", tr);
+        print_batch("val", va);
         return 0;
     }
     if (!std::strcmp(argv[1], "log") && argc >= 3) {

@@ -26,6 +26,8 @@ def _ref(*args):
 def test_cosine_scheduler_matches_reference():
     n = 0
     for line in _ref("lr").splitlines():
+        if not line.startswith("lr "):
+            continue
         _, base, warm, mx, mn, cyc, step, val = line.split()
         s = feed.CosineScheduler(float(base), int(warm), int(mx), float(mn), int(cyc))
         got, want = s.get_lr(int(step)), float(val)
@@ -90,3 +92,28 @@ def test_shuffled_loader_covers_the_same_runs():
     assert a.order.tolist() != b.order.tolist()
     c = feed.DataLoader(ds, 64, shuffle=True, seed=3)
     assert a.order.tolist() == c.order.tolist()  # seeded
+
+
+def test_step_scheduler_matches_reference():
+    n = 0
+    for line in _ref("lr").splitlines():
+        if not line.startswith("steplr"):
+            continue
+        _, base, size, gamma, step, val = line.split()
+        got = feed.StepScheduler(float(base), int(size), float(gamma)).get_lr(int(step))
+        want = float(val)
+        assert got == pytest.approx(want, rel=1e-7, abs=1e-30), line
+        n += 1
+    assert n > 100
+
+
+@pytest.mark.parametrize("block,eos,ratio", [(8, 0, 0.9), (5, 50256, 0.5), (64, 7, 1.0)])
+def test_pack_and_split_match_reference(tmp_path, block, eos, ratio):
+    p = tmp_path / "text.txt"
+    p.write_bytes(b"Some text to pack into rows, with a ragged tail.\n" * 3)
+    out = _ref("pack", str(p), str(block), str(eos), str(ratio))
+    rows, mask = feed.pack_with_eos(feed.Dataset.from_file(str(p)).tokens, block, eos)
+    assert rows.tolist() == _runs(out, "row")
+    assert mask.tolist() == _runs(out, "mask")
+    tr, va = feed.train_val_split(feed.Dataset.from_file(str(p)).tokens, ratio, 7)
+    assert [tr.tolist()] == _runs(out, "train") and [va.tolist()] == _runs(out, "val")
