@@ -103,6 +103,12 @@ int llmgpu_train_step_device(llmgpu_ctx* ctx, const int32_t* d_tokens, int B, in
                              float* loss_out, float* grad_norm_out);
 /* Forward + loss only (no gradient, no step): mean loss over B sequences. */
 int llmgpu_eval_loss(llmgpu_ctx* ctx, const int32_t* tokens, int B, int T, float* loss_out);
+/* Forward without the loss: the logits of each sequence's last position (GPT::forward,
+ * src/model.cpp:144-170, row T-1; what GPT::generate samples from). Writes B*V floats to
+ * `logits` (capacity `cap` floats; the device holds bf16 logits) and returns B*V, or a
+ * negative status. */
+int64_t llmgpu_forward_logits(llmgpu_ctx* ctx, const int32_t* tokens, int B, int T,
+                              float* logits, int64_t cap);
 
 /* Parameters in GPT::parameters() order (src/model.cpp:889-909). */
 int llmgpu_num_params(const llmgpu_ctx* ctx);           /* number of parameter tensors */

@@ -305,6 +305,35 @@ int llmgpu_eval_loss(llmgpu_ctx* h, const int32_t* tokens, int B, int T, float* 
     return 0;
 }
 
+int64_t llmgpu_forward_logits(llmgpu_ctx* h, const int32_t* tokens, int B, int T, float* logits,
+                              int64_t cap) {
+    if (check_ctx(h) || !tokens || !logits) return LLMGPU_E_ARG;
+    Ctx* c = h->c;
+    if (B <= 0 || T <= 0 || (long long)B * T > c->max_bt || T > c->max_t) return LLMGPU_E_ARG;
+    if (cap < (int64_t)B * c->V) return LLMGPU_E_ARG;
+    int rc = stage_tokens(c, tokens, B, T);
+    if (rc) return rc;
+    c->plan_cursor = 0;
+    c->plan2_cursor = 0;
+    c->launches = 0;
+    c->logits_only = true;  // stop after the lm head: the fused loss would overwrite the logits
+    rc = run_fwd_bwd(c, B, T, 0, false);
+    c->logits_only = false;
+    if (rc) return rc;
+    // row T-1 of each sequence: B rows of V bf16, T * Vp apart
+    std::vector<uint16_t> rows((size_t)B * c->V);
+    if (cudaMemcpy2DAsync(rows.data(), (size_t)c->V * 2, c->logits + (size_t)(T - 1) * c->Vp,
+                          (size_t)T * c->Vp * 2, (size_t)c->V * 2, (size_t)B,
+                          cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+        return LLMGPU_E_CUDA;
+    if ((rc = ctx_sync_check(c))) return rc;
+    for (size_t i = 0; i < rows.size(); ++i) {
+        const uint32_t bits = (uint32_t)rows[i] << 16;
+        std::memcpy(&logits[i], &bits, sizeof(float));
+    }
+    return (int64_t)B * c->V;
+}
+
 int llmgpu_num_params(const llmgpu_ctx* h) {
     if (check_ctx(h)) return LLMGPU_E_ARG;
     return (int)h->c->params.size();

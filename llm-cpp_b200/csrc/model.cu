@@ -1148,6 +1148,7 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
         if (rc) return rc;
     }
     mark(c, 1);
+    if (c->logits_only) return 0;  // llmgpu_forward_logits reads them
     // ------------------------------------------------------------------ loss
     KC(cross_entropy_fwd_bwd(c->logits, BT, V, Vp, c->d_tokens, c->d_row_loss, 1.0f / (float)BT,
                              c->smoothing, s, c->d_err));

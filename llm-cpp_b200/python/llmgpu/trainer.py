@@ -57,6 +57,7 @@ class Trainer:
                                         uidbuf)
         if not self.h:
             raise LlmgpuError(self.lib.llmgpu_last_error(None).decode())
+        self.max_batch, self.max_seq = max_batch, max_seq
         self._lr = 3e-4  # the library's AdamW default
         self._last_good = None
 
@@ -150,6 +151,29 @@ class Trainer:
         if rc < 0:
             self._err("eval_loss", rc)
         return loss.value
+
+    def forward_logits(self, tokens):
+        """tokens int32 [B, T] -> float32 [B, V]: the logits of each sequence's last position
+        (GPT::forward, row T-1)."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        B, T = t.shape
+        out = np.empty((B, self.cfg.vocab_size), np.float32)
+        n = self.lib.llmgpu_forward_logits(self.h, t.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                           B, T, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                           out.size)
+        if n < 0:
+            self._err("forward_logits", n)
+        return out
+
+    def generate(self, prompt, max_new_tokens):
+        """Greedy GPT::generate (temperature 0, src/model.cpp): append the argmax of the last
+        position's logits max_new_tokens times. Each token re-runs the forward over the last
+        max_seq tokens (no KV cache). Returns prompt + generated ids."""
+        out = [int(t) for t in prompt]
+        for _ in range(int(max_new_tokens)):
+            ctx = np.asarray(out[-self.max_seq:] or [0], np.int32)[None, :]
+            out.append(int(np.argmax(self.forward_logits(ctx)[0])))
+        return out
 
     # ------------------------------------------------------------------ parameters
     def num_params(self):
