@@ -165,15 +165,14 @@ class Trainer:
             self._err("forward_logits", n)
         return out
 
-    def generate(self, prompt, max_new_tokens):
-        """Greedy GPT::generate (temperature 0, src/model.cpp): append the argmax of the last
-        position's logits max_new_tokens times. Each token re-runs the forward over the last
-        max_seq tokens (no KV cache). Returns prompt + generated ids."""
-        out = [int(t) for t in prompt]
-        for _ in range(int(max_new_tokens)):
-            ctx = np.asarray(out[-self.max_seq:] or [0], np.int32)[None, :]
-            out.append(int(np.argmax(self.forward_logits(ctx)[0])))
-        return out
+    def generate(self, prompt, max_new_tokens, **sampling_args):
+        """GPT::generate (src/model.cpp) on the device forward: greedy by default; the
+        reference's temperature / top-k / top-p / repetition-penalty options as in
+        llmgpu.sampling.generate. Each token re-runs the forward over the last max_seq
+        tokens (no KV cache). Returns prompt + generated ids."""
+        from . import sampling
+        return sampling.generate(self.forward_logits, prompt, max_new_tokens, self.max_seq,
+                                 **sampling_args)
 
     # ------------------------------------------------------------------ parameters
     def num_params(self):

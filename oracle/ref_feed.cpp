@@ -5,6 +5,7 @@
 //   ref_feed data TEXT_FILE BS       -> "tokens ...", then "loader ..." / "prefetch ..." batches
 //   ref_feed log OUT_FILE            -> MetricsLogger lines written to OUT_FILE
 //   ref_feed pack TEXT_FILE BLOCK EOS RATIO -> pack_with_eos rows/masks, train_val_split sizes
+//   ref_feed sample                  -> logits rows, then seeded sampler picks (src/sampling.cpp)
 // Calls: CosineScheduler::get_lr (src/scheduler.cpp:13-28), Dataset / DataLoader
 // (src/dataset.cpp:41-84), PrefetchLoader (src/prefetch.cpp), MetricsLogger::log_step
 // (src/logging.cpp:49-55).
@@ -17,6 +18,7 @@
 #include "llm/dataset.h"
 #include "llm/logging.h"
 #include "llm/prefetch.h"
+#include "llm/sampling.h"
 #include "llm/scheduler.h"
 
 static void print_batch(const char* tag, const std::vector<int>& b) {
@@ -66,6 +68,42 @@ int main(int argc, char** argv) {
             auto b = pl.next();
             if (b.empty()) break;
             print_batch("prefetch", b[0]);
+        }
+        return 0;
+    }
+    if (!std::strcmp(argv[1], "sample")) {
+        // rows of logits from a fixed LCG (printed exactly), then the samplers' picks
+        uint64_t st = 12345;
+        auto rnd = [&]() {
+            st = st * 6364136223846793005ull + 1442695040888963407ull;
+            return (float)((double)(st >> 40) / (double)(1ull << 24)) * 8.0f - 4.0f;
+        };
+        const int V = 50;
+        for (int r = 0; r < 6; ++r) {
+            std::vector<float> l(V);
+            for (auto& v : l) v = rnd();
+            std::printf("logits");
+            for (float v : l) std::printf(" %.9g", v);
+            std::printf("\n");
+            const float temps[] = {0.7f, 1.0f, 1.6f};
+            for (float t : temps)
+                for (uint64_t seed = 0; seed < 40; ++seed) {
+                    std::printf("temp %d %.9g %llu %d\n", r, t, (unsigned long long)seed,
+                                llm::sample_temperature_seeded(l, t, seed));
+                    std::printf("topk %d %.9g %llu %d\n", r, t, (unsigned long long)seed,
+                                llm::sample_top_k_seeded(l, 5 + (int)(seed % 7), t, seed));
+                    std::printf("topp %d %.9g %llu %d\n", r, t, (unsigned long long)seed,
+                                llm::sample_top_p_seeded(l, 0.5f + 0.01f * (float)seed, t, seed));
+                }
+            std::printf("greedy %d %d\n", r, llm::sample_greedy(l));
+            const std::vector<int> gen = {3, 7, 7, 49, 0, 3, 3};
+            auto rp = llm::apply_repetition_penalty(l, gen, 1.3f);
+            auto fp = llm::apply_freq_presence(l, gen, 0.25f, 0.5f);
+            std::printf("reppen");
+            for (float v : rp) std::printf(" %.9g", v);
+            std::printf("\nfreqpres");
+            for (float v : fp) std::printf(" %.9g", v);
+            std::printf("\n");
         }
         return 0;
     }

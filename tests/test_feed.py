@@ -117,3 +117,56 @@ def test_pack_and_split_match_reference(tmp_path, block, eos, ratio):
     assert mask.tolist() == _runs(out, "mask")
     tr, va = feed.train_val_split(feed.Dataset.from_file(str(p)).tokens, ratio, 7)
     assert [tr.tolist()] == _runs(out, "train") and [va.tolist()] == _runs(out, "val")
+
+
+def test_samplers_match_reference():
+    from llmgpu import sampling
+    rows, n = [], 0
+    gen = [3, 7, 7, 49, 0, 3, 3]
+    for line in _ref("sample").splitlines():
+        f = line.split()
+        if f[0] == "logits":
+            rows.append(np.array([float(v) for v in f[1:]], np.float32))
+        elif f[0] in ("temp", "topk", "topp"):
+            r, t, seed, want = int(f[1]), float(f[2]), int(f[3]), int(f[4])
+            l = rows[r]
+            if f[0] == "temp":
+                got = sampling.sample_temperature_seeded(l, t, seed)
+            elif f[0] == "topk":
+                got = sampling.sample_top_k_seeded(l, 5 + seed % 7, t, seed)
+            else:
+                got = sampling.sample_top_p_seeded(l, np.float32(0.5) + np.float32(0.01) * np.float32(seed), t, seed)
+            assert got == want, line
+            n += 1
+        elif f[0] == "greedy":
+            assert sampling.sample_greedy(rows[int(f[1])]) == int(f[2])
+        elif f[0] == "reppen":
+            want = np.array([float(v) for v in f[1:]], np.float32)
+            assert np.array_equal(sampling.apply_repetition_penalty(rows[-1], gen, 1.3), want)
+        elif f[0] == "freqpres":
+            want = np.array([float(v) for v in f[1:]], np.float32)
+            assert np.array_equal(sampling.apply_freq_presence(rows[-1], gen, 0.25, 0.5), want)
+    assert n == 6 * 3 * 40 * 3
+
+
+def test_generate_loop_with_a_stand_in_model():
+    """sampling.generate over a fixed logits function (no GPU): greedy follows argmax,
+    seeded sampling is reproducible, eos stops, the context window is the last max_seq."""
+    from llmgpu import sampling
+    V = 32
+    seen = []
+
+    def logits(ctx):
+        seen.append(ctx.shape[1])
+        r = np.random.default_rng(int(ctx.sum()) + ctx.shape[1])
+        return r.standard_normal((1, V)).astype(np.float32)
+
+    out = sampling.generate(logits, [1, 2, 3], 5, max_seq=4)
+    assert len(out) == 8 and max(seen) == 4
+    for k in range(3, 8):
+        assert out[k] == sampling.sample_greedy(logits(np.asarray(out[:k][-4:], np.int32)[None]))
+    a = sampling.generate(logits, [5], 6, 16, temperature=0.9, top_k=5, seed=3)
+    b = sampling.generate(logits, [5], 6, 16, temperature=0.9, top_k=5, seed=3)
+    assert a == b
+    c = sampling.generate(logits, [5], 20, 16, temperature=1.0, top_p=0.9, eos_id=a[1])
+    assert len(c) >= 2 and (len(c) == 21 or c[-1] == a[1])
