@@ -125,7 +125,6 @@ class Dataset:
 class DataLoader:
     def __init__(self, ds, batch_size, shuffle=False, seed=0):
         self.ds, self.batch_size, self.shuffle, self.seed = ds, int(batch_size), shuffle, seed
-        self._epoch = 0
         self._build_order()
 
     def _build_order(self):

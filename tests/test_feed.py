@@ -170,3 +170,36 @@ def test_generate_loop_with_a_stand_in_model():
     assert a == b
     c = sampling.generate(logits, [5], 20, 16, temperature=1.0, top_p=0.9, eos_id=a[1])
     assert len(c) >= 2 and (len(c) == 21 or c[-1] == a[1])
+
+
+def test_train_loop_with_a_stand_in_trainer(tmp_path):
+    """feed.train on the host path (no GPU): each step gets the next B runs of T tokens,
+    the scheduler's rate for that step is set first, a short tail ends the loop, and one
+    metrics line is written per step."""
+    B, T = 3, 8
+    toks = np.arange(10 * B * T + 5, dtype=np.int32)
+
+    class Stand:
+        def __init__(self):
+            self.lrs, self.blocks = [], []
+
+        def set_lr(self, lr):
+            self.lrs.append(lr)
+
+        def train_step(self, block):
+            self.blocks.append(np.array(block))
+            return float(len(self.blocks)), 0.5, False
+
+    st = Stand()
+    sched = feed.CosineScheduler(1e-3, 2, 20, 1e-4)
+    log = tmp_path / "m.jsonl"
+    losses = feed.train(st, feed.Dataset(toks), B, T, 100, scheduler=sched,
+                        logger=feed.MetricsLogger(str(log)), device_feed=False)
+    assert len(losses) == 10  # 10 full steps; the 5-token tail is not a full run
+    for s, blk in enumerate(st.blocks):
+        assert np.array_equal(blk, toks[s * B * T:(s + 1) * B * T].reshape(B, T))
+    assert st.lrs == [sched.get_lr(s) for s in range(10)]
+    lines = [json.loads(x) for x in log.read_text().splitlines()]
+    assert [x["step"] for x in lines] == list(range(10)) and lines[3]["loss"] == 4
+    st2 = Stand()
+    assert len(feed.train(st2, feed.Dataset(toks), B, T, 4, device_feed=False)) == 4
