@@ -10,8 +10,8 @@
   data from the start of the data section, offsets aligned to 32 bytes;
 - zero padding to a 32-byte boundary, then each tensor's fp32 data at its offset.
 
-Reading accepts F32 tensors only and checks the tensor count and every shape against the
-model. `write_gguf_quant` writes the reference's quantized export (save_gguf_quant,
+Reading decodes F32, Q8_0, Q4_0 and Q4_K tensors as the reference's load_gguf does
+(src/gguf.cpp:315-353) and checks the tensor count and every shape against the model. `write_gguf_quant` writes the reference's quantized export (save_gguf_quant,
 src/gguf.cpp:499-581) for qtype 0 (F32), 8 (Q8_0: per 32 values an f32 scale
 max|x| / 127 + 1e-8 and 32 int8) and 4 (Q4_0: scale max|x| / 7 + 1e-8 and 16 bytes of
 nibbles, value + 8, even index in the low nibble) and 12 (Q4_K: 144-byte super-blocks of
@@ -222,9 +222,46 @@ def write_gguf_quant(path, arrays, qtype):
         f.write(out)
 
 
+def _decode(buf, start, n, dtype):
+    f32 = np.float32
+    if dtype == GGUF_F32:
+        return np.frombuffer(buf, f32, n, start).copy()
+    if dtype == GGUF_Q4_K:
+        nb = -(-n // 256)
+        blk = np.frombuffer(buf, np.uint8, nb * 144, start).reshape(nb, 144)
+        dall = _f16_bits_to_f32(blk[:, 0:2].copy().view(np.uint16)[:, 0])
+        dmin = _f16_bits_to_f32(blk[:, 2:4].copy().view(np.uint16)[:, 0])
+        sc8 = blk[:, 4:16].astype(np.int64)
+        sc = np.empty((nb, 8), np.int64)
+        mn = np.empty((nb, 8), np.int64)
+        for j in range(4):  # ggml get_scale_min_k4 order
+            sc[:, j], mn[:, j] = sc8[:, j] & 63, sc8[:, j + 4] & 63
+            sc[:, j + 4] = (sc8[:, j + 8] & 0xF) | ((sc8[:, j] >> 6) << 4)
+            mn[:, j + 4] = (sc8[:, j + 8] >> 4) | ((sc8[:, j + 4] >> 6) << 4)
+        qs = blk[:, 16:].reshape(nb, 4, 32).astype(np.int64)
+        q = np.concatenate([qs & 0xF, qs >> 4], axis=2).reshape(nb, 8, 32).astype(f32)
+        a = (dall[:, None] * sc.astype(f32)).astype(f32)
+        b = (dmin[:, None] * mn.astype(f32)).astype(f32)
+        with np.errstate(invalid="ignore"):
+            out = (a[:, :, None] * q).astype(f32) - b[:, :, None]
+        return out.reshape(-1)[:n].astype(f32)
+    nb = -(-n // _QBLK)
+    width = 4 + (_QBLK if dtype == GGUF_Q8_0 else _QBLK // 2)
+    blk = np.frombuffer(buf, np.uint8, nb * width, start).reshape(nb, width)
+    sc = blk[:, :4].copy().view(f32)[:, 0]
+    if dtype == GGUF_Q8_0:
+        q = blk[:, 4:].view(np.int8).astype(f32)
+    else:
+        p = blk[:, 4:].astype(np.int64)
+        q = np.stack([(p & 0xF) - 8, ((p >> 4) & 0xF) - 8], axis=2).reshape(nb, _QBLK).astype(f32)
+    with np.errstate(invalid="ignore"):  # an inf scale times a zero code is NaN, as there
+        return (q * sc[:, None]).astype(f32).reshape(-1)[:n]
+
+
 def read_gguf(path, shapes=None):
-    """Reads an F32 GGUF written in the reference's layout; returns (arrays, kvs). With
-    `shapes`, the tensor count and every shape must match (as load_gguf checks)."""
+    """Reads a GGUF written in the reference's layout (F32, Q8_0, Q4_0 or Q4_K tensors,
+    decoded to float32); returns (arrays, kvs). With `shapes`, the tensor count and every
+    shape must match (as load_gguf checks)."""
     with open(path, "rb") as f:
         buf = f.read()
     pos = 0
@@ -264,17 +301,16 @@ def read_gguf(path, shapes=None):
         (nd,) = take("<I")
         dims = take(f"<{nd}Q")
         dtype, off = take("<IQ")
-        if dtype != GGUF_F32:
-            raise ValueError(f"gguf: tensor {i} has type {dtype}; only F32 (0) is read here")
+        if dtype not in (GGUF_F32, GGUF_Q8_0, GGUF_Q4_0, GGUF_Q4_K):
+            raise ValueError(f"gguf: tensor {i} has unsupported type {dtype}")
         if shapes is not None and tuple(dims) != tuple(shapes[i]):
             raise ValueError(f"gguf: tensor {i} shape {dims}, model {tuple(shapes[i])}")
-        infos.append((dims, off))
+        infos.append((dims, off, dtype))
     data_start = _align(pos)
     arrays = []
-    for dims, off in infos:
+    for dims, off, dtype in infos:
         n = int(np.prod(dims)) if dims else 1
-        start = data_start + off
-        arrays.append(np.frombuffer(buf, np.float32, n, start).reshape(dims).copy())
+        arrays.append(_decode(buf, data_start + off, n, dtype).reshape(dims))
     return arrays, kvs
 
 

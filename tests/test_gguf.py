@@ -67,6 +67,14 @@ def test_quantized_gguf_matches_reference(tmp_path, qtype):
          ref_file, qtype)
     gguf.write_gguf_quant(str(our_file), params, qtype)
     assert our_file.read_bytes() == ref_file.read_bytes()
+    # decoding: the values the reference's load_gguf puts into its model
+    back = tmp_path / "back.bin"
+    _ref("load", cfg.vocab, cfg.n_layers, cfg.n_heads, cfg.n_embd, cfg.block_size, 1, 0,
+         our_file, back)
+    want = go.read_ckpt(str(back), cfg)
+    got, _ = gguf.read_gguf(str(our_file), [p.shape for p in params])
+    for a, b in zip(got, want):
+        assert np.array_equal(a, b, equal_nan=True)
 
 
 def test_unknown_quant_type_is_refused(tmp_path):
