@@ -18,7 +18,11 @@ semantics:
   number formatting (6 significant digits).
 - `train` (src/trainer.cpp:23-36): the loop. One device step takes B runs of T tokens (the
   reference's train_step_accum over B sequences), with the learning rate of
-  `scheduler.get_lr(step)` set before it, as Trainer::train_step_accum does.
+  `scheduler.get_lr(step)` set before it, as Trainer::train_step_accum does; every
+  eval_interval steps the step's loss and rate are printed, with `evaluate` on a
+  validation set when one is given.
+- `evaluate` (Trainer::evaluate): the loss of the dataset's first min(n, 128) tokens as one
+  sequence.
 
 `DeviceFeed` is what the device adds: each step's [B, T] token block is staged in pinned
 host memory and copied to the GPU on a copy stream while the previous step runs; the step's
@@ -271,8 +275,16 @@ class DeviceFeed:
         self._launched[s] = True
 
 
+def evaluate(trainer, dataset):
+    """Trainer::evaluate: the loss of the first min(n, 128) tokens, one sequence."""
+    t = dataset.tokens[:128]
+    if t.size == 0:
+        return 0.0
+    return trainer.eval_loss(t[None, :])
+
+
 def train(trainer, dataset, B, T, max_iters, scheduler=None, logger=None, prefetch=2,
-          device_feed=True, log_every=1):
+          device_feed=True, log_every=1, val_ds=None, eval_interval=500, print_fn=print):
     """Trainer::train over the device step: each step takes the next B runs of T tokens
     (a short last run ends the loop), sets lr = scheduler.get_lr(step) first, and logs loss,
     perplexity, lr, grad norm and tokens/s. Returns the list of step losses."""
@@ -310,10 +322,14 @@ def train(trainer, dataset, B, T, max_iters, scheduler=None, logger=None, prefet
                 loss, gn, _ = trainer.train_step(block)
             dt = time.perf_counter() - t0
             losses.append(loss)
+            lr = scheduler.get_lr(step) if scheduler is not None else trainer.get_lr()
             if logger is not None and step % max(log_every, 1) == 0:
-                lr = scheduler.get_lr(step) if scheduler is not None else 0.0
                 ppl = math.exp(min(loss, 80.0))
                 logger.log_step(step, loss, ppl, lr, gn, B * T / dt if dt > 0 else 0.0)
+            if print_fn is not None and eval_interval > 0 and step % eval_interval == 0:
+                print_fn(f"[trainer] step {step} loss {_num(loss)} lr {_num(lr)}")
+                if val_ds is not None:
+                    print_fn(f"[trainer] val loss {_num(evaluate(trainer, val_ds))}")
             block = nxt
             step += 1
     finally:

@@ -190,6 +190,13 @@ def test_train_loop_with_a_stand_in_trainer(tmp_path):
             self.blocks.append(np.array(block))
             return float(len(self.blocks)), 0.5, False
 
+        def get_lr(self):
+            return self.lrs[-1] if self.lrs else 3e-4
+
+        def eval_loss(self, tokens):
+            self.evaluated = tokens.copy()
+            return 1.25
+
     st = Stand()
     sched = feed.CosineScheduler(1e-3, 2, 20, 1e-4)
     log = tmp_path / "m.jsonl"
@@ -202,4 +209,10 @@ def test_train_loop_with_a_stand_in_trainer(tmp_path):
     lines = [json.loads(x) for x in log.read_text().splitlines()]
     assert [x["step"] for x in lines] == list(range(10)) and lines[3]["loss"] == 4
     st2 = Stand()
-    assert len(feed.train(st2, feed.Dataset(toks), B, T, 4, device_feed=False)) == 4
+    printed = []
+    assert len(feed.train(st2, feed.Dataset(toks), B, T, 4, device_feed=False,
+                          val_ds=feed.Dataset(toks[:300]), eval_interval=2,
+                          print_fn=printed.append)) == 4
+    assert printed == ["[trainer] step 0 loss 1 lr 0.0003", "[trainer] val loss 1.25",
+                       "[trainer] step 2 loss 3 lr 0.0003", "[trainer] val loss 1.25"]
+    assert np.array_equal(st2.evaluated, toks[:128][None, :])  # Trainer::evaluate's window
