@@ -245,6 +245,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="sequences per GPU (0: the workload's own); smaller cases for profiling")
     ap.add_argument("--config", default="gpt2-small", choices=["gpt2-small"] + sorted(OTHER_CONFIGS),
                     help="workload (the headline line is gpt2-small)")
     args = ap.parse_args()
@@ -271,6 +273,10 @@ def main():
     model_cfg, B, T, workload = (CFG, globals()["B"], globals()["T"], None)
     if args.config != "gpt2-small":
         model_cfg, B, T, workload = OTHER_CONFIGS[args.config]
+    if args.batch > 0:
+        B = args.batch
+        workload = (workload or workload_config(1)["workload"]).replace("8 seq/GPU", "") + \
+            f" [profiling case: {B} seq/GPU]"
     cfg = make_config(**model_cfg)
     tr = Trainer(cfg, B, T, rank=rank, world=world, uid=uid)
     tr.set_adamw(**HP)

@@ -59,7 +59,21 @@ typedef struct llmgpu_config {
     int moe_experts;    /* >0: MoEFFN (src/moe.cpp) replaces the FFN */
     int moe_top_k;
     float moe_aux_coef;
+    /* Config::pos_encoding and its RoPE options (include/llm/model.h:15-33):
+     * LLMGPU_POS_LEARNED, LLMGPU_POS_SINUSOIDAL (wpe initialised with sin/cos,
+     * src/model.cpp:34-41) or LLMGPU_POS_ROPE (rope_cfg rotates the embedding sum,
+     * src/model.cpp:81-104,158; the backward scatters the gradient of the rotated sum into
+     * wte/wpe unrotated, as src/model.cpp:314-322 does). rope_theta above is Config::rope_theta. */
+    int pos_encoding;
+    float rope_scaling; /* Config::rope_scaling (values below 1 act as 1, as rope_cfg clamps) */
+    int rope_mode;      /* Config::rope_mode: 0 NTK (base * scaling), 1 YaRN ramp */
+    float yarn_alpha;   /* Config::yarn_alpha (multiplies every angle) */
+    float yarn_beta;    /* Config::yarn_beta (ramp between beta/2 and beta) */
 } llmgpu_config;
+
+#define LLMGPU_POS_LEARNED 0
+#define LLMGPU_POS_SINUSOIDAL 1
+#define LLMGPU_POS_ROPE 2
 
 /* Fills `cfg` with the reference defaults (Config{} of include/llm/model.h). */
 void llmgpu_config_default(llmgpu_config* cfg);

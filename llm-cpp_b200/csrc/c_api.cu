@@ -173,6 +173,11 @@ void llmgpu_config_default(llmgpu_config* cfg) {
     cfg->rope_theta = 10000.0f;
     cfg->moe_top_k = 2;
     cfg->moe_aux_coef = 0.01f;
+    cfg->pos_encoding = LLMGPU_POS_LEARNED;
+    cfg->rope_scaling = 1.0f;
+    cfg->rope_mode = 0;
+    cfg->yarn_alpha = 1.0f;
+    cfg->yarn_beta = 32.0f;
 }
 
 int llmgpu_get_unique_id(void* uid128) {

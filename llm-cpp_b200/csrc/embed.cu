@@ -12,18 +12,31 @@ __device__ __forceinline__ int wrap_token(int tok, int V) {
     return r < 0 ? r + V : r;
 }
 
+// `rope` (nullable): per position t, the (cos, sin) of every column pair (2j, 2j+1) as
+// [T][C/2] float2, i.e. one float4 per group of four columns. With it the sum is rotated
+// pairwise and scaled by rope_scale, as rope_cfg does to the embedding sum
+// (src/model.cpp:81-104,158): (x0 cos - x1 sin, x0 sin + x1 cos) * scale.
 __global__ void embed_fwd_kernel(const int32_t* __restrict__ tokens, const float* __restrict__ wte,
                                  const float* __restrict__ wpe, float* __restrict__ x, int B, int T,
-                                 int C, int V) {
+                                 int C, int V, const float4* __restrict__ rope, float rope_scale) {
     const int row = blockIdx.x;  // b*T + t
     const int t = row % T;
     const int tok = wrap_token(tokens[row], V);
     const float4* a = reinterpret_cast<const float4*>(wte + (long long)tok * C);
     const float4* p = reinterpret_cast<const float4*>(wpe + (long long)t * C);
     float4* o = reinterpret_cast<float4*>(x + (long long)row * C);
+    const float4* r = rope ? rope + (long long)t * (C >> 2) : nullptr;
     for (int i = threadIdx.x; i < (C >> 2); i += blockDim.x) {
         float4 u = a[i], w = p[i];
-        o[i] = make_float4(u.x + w.x, u.y + w.y, u.z + w.z, u.w + w.w);
+        float4 v = make_float4(u.x + w.x, u.y + w.y, u.z + w.z, u.w + w.w);
+        if (r) {
+            const float4 cs = r[i];  // (cos, sin) of pair 2i, then of pair 2i+1
+            v = make_float4((v.x * cs.x - v.y * cs.y) * rope_scale,
+                            (v.x * cs.y + v.y * cs.x) * rope_scale,
+                            (v.z * cs.z - v.w * cs.w) * rope_scale,
+                            (v.z * cs.w + v.w * cs.z) * rope_scale);
+        }
+        o[i] = v;
     }
 }
 
@@ -154,9 +167,10 @@ __global__ void wpe_grad_kernel(const float* __restrict__ dx, float* __restrict_
 }  // namespace
 
 int embed_forward(const int32_t* tokens, const float* wte, const float* wpe, float* x, int B,
-                  int T, int C, int V, cudaStream_t s) {
+                  int T, int C, int V, cudaStream_t s, const float* rope, float rope_scale) {
     if ((C & 3) != 0) return -1;
-    embed_fwd_kernel<<<B * T, 128, 0, s>>>(tokens, wte, wpe, x, B, T, C, V);
+    embed_fwd_kernel<<<B * T, 128, 0, s>>>(tokens, wte, wpe, x, B, T, C, V,
+                                           reinterpret_cast<const float4*>(rope), rope_scale);
     return launch_status();
 }
 

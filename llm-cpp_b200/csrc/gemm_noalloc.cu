@@ -57,6 +57,9 @@ extern "C" int llmgpu_op_gemm_splitk_noalloc(const void* A, long long lda, int a
                                              int accumulate, int splits, int col_group,
                                              long long group_stride, int* err, void* stream) {
     if (M <= 0 || N <= 0 || K <= 0 || splits < 1 || !out) return -1;
+    // the column-group rule of llmgpu_op_gemm (its plan sees col_group, this one's partial
+    // tiles are ungrouped), so that both entry points accept the same arguments
+    if (col_group > 0 && col_group != N && (col_group % 32) != 0) return -7;
     if ((long long)splits * M * N > kNoAllocScratchFloats) return -101;  // beyond the scratch
     float* scratch = nullptr;
     int rc = scratch_for_current_device(&scratch);

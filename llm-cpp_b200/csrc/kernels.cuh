@@ -11,9 +11,12 @@ namespace llmgpu {
 using bf16 = __nv_bfloat16;
 
 // ----------------------------------------------------------------- embedding
-// x[b*T+t, :] = wte[tok mod V, :] + wpe[t, :]   (src/model.cpp:149-157)
+// x[b*T+t, :] = wte[tok mod V, :] + wpe[t, :]   (src/model.cpp:149-157), then, when `rope`
+// is given ([T][C/2] (cos, sin) pairs), rotated pairwise and scaled by rope_scale like
+// rope_cfg (src/model.cpp:81-104,158).
 int embed_forward(const int32_t* tokens, const float* wte, const float* wpe, float* x, int B,
-                  int T, int C, int V, cudaStream_t s);
+                  int T, int C, int V, cudaStream_t s, const float* rope = nullptr,
+                  float rope_scale = 1.0f);
 // Sorts (token mod V, row) pairs of the batch once per step so that the wte
 // gradient can be formed deterministically (each token's rows summed in row order).
 // `keys` holds n uint64 entries. n <= 16384.

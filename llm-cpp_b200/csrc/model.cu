@@ -143,6 +143,16 @@ void reference_init(Ctx* c, std::vector<float>& host) {
     const auto& k = c->cfg;
     randn(c->i_wte, 0.02f);
     randn(c->i_wpe, 0.02f);
+    if (k.pos_encoding == LLMGPU_POS_SINUSOIDAL) {
+        // wpe[pos][i] = sin / cos(pos / 10000^(2*(i/2)/C)) for even / odd i (src/model.cpp:34-41)
+        float* d = host.data() + c->params[c->i_wpe].offset;
+        const int C = k.n_embd;
+        for (int pos = 0; pos < k.block_size; ++pos)
+            for (int i = 0; i < C; ++i) {
+                const float angle = (float)pos / std::pow(10000.0f, (float)(2 * (i / 2)) / (float)C);
+                d[(size_t)pos * C + i] = (i % 2 == 0) ? std::sin(angle) : std::cos(angle);
+            }
+    }
     fill(c->i_lnfg, 1.0f);
     if (c->i_lm >= 0) randn(c->i_lm, 0.02f);
     for (auto& b : c->blocks) {
@@ -426,6 +436,8 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
     if (cfg.vocab_size <= 0 || cfg.n_layers <= 0 || cfg.n_embd <= 0 || cfg.block_size <= 0 ||
         max_batch <= 0 || max_seq <= 0 || max_seq > cfg.block_size)
         return fail(c, "invalid configuration");
+    if (cfg.pos_encoding < LLMGPU_POS_LEARNED || cfg.pos_encoding > LLMGPU_POS_ROPE)
+        return fail(c, "pos_encoding must be 0 (learned), 1 (sinusoidal) or 2 (RoPE)");
     if (!cfg.use_mamba && (cfg.n_heads <= 0 || cfg.n_embd % cfg.n_heads != 0))
         return fail(c, "n_heads must divide n_embd");  // src/config.cpp:39-68
     c->C = cfg.n_embd;
@@ -594,6 +606,40 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
             }
         if (dalloc(c, &c->rope, tab.size() / 2) ||
             copy_sync(c, c->rope, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice))
+            return fail(c, "");
+    }
+
+    // Config::pos_encoding == RoPE: rope_cfg (src/model.cpp:71-104) evaluated once per position
+    // and column pair with the reference's own float expressions (NTK base * scaling, or the
+    // YaRN ramp with its attention scale), applied by the embedding gather
+    if (cfg.pos_encoding == LLMGPU_POS_ROPE) {
+        const float scaling = cfg.rope_scaling < 1.0f ? 1.0f : cfg.rope_scaling;
+        const float base = cfg.rope_theta * (cfg.rope_mode == 0 ? scaling : 1.0f);
+        const bool yarn = cfg.rope_mode == 1 && scaling > 1.0f;
+        c->emb_rope_scale = yarn ? std::sqrt(1.0f + 0.1f * std::log(scaling)) : 1.0f;
+        auto ramp = [&](int dim) {  // yarn_ramp (src/model.cpp:71-78)
+            const float d = (float)dim / (float)C * cfg.yarn_beta;
+            const float low = cfg.yarn_beta / 2.0f, high = cfg.yarn_beta;
+            if (d < low) return 0.0f;
+            if (d > high) return 1.0f;
+            return (d - low) / (high - low);
+        };
+        const int P = C / 2;
+        std::vector<float> tab((size_t)max_seq * P * 2);
+        for (int pos = 0; pos < max_seq; ++pos)
+            for (int j = 0; j < P; ++j) {
+                const int i = 2 * j;
+                float freq = std::pow(base, -(float)i / (float)C);
+                if (yarn) {
+                    const float m = ramp(i);
+                    freq = ((1.0f - m) / scaling + m) * std::pow(cfg.rope_theta, -(float)i / (float)C);
+                }
+                const float angle = (float)pos * freq * cfg.yarn_alpha;
+                tab[((size_t)pos * P + j) * 2] = std::cos(angle);
+                tab[((size_t)pos * P + j) * 2 + 1] = std::sin(angle);
+            }
+        if (dalloc(c, &c->emb_rope, tab.size() / 2) ||
+            copy_sync(c, c->emb_rope, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice))
             return fail(c, "");
     }
 
@@ -787,7 +833,7 @@ void ctx_destroy(Ctx* c) {
     F(c->attn_ds);
     for (auto& p2 : c->plan2_cache) gemm_free_plan2(&p2);
     F(c->partial); F(c->colwork); F(c->splitws); F(c->d_tokens); F(c->d_keys);
-    F(c->dact); F(c->rope);
+    F(c->dact); F(c->rope); F(c->emb_rope);
     for (auto& m : c->mact) {
         F(m.proj); F(m.u32); F(m.u16); F(m.xp); F(m.xp16); F(m.raw); F(m.y); F(m.gated);
         F(m.hchk);
@@ -1091,7 +1137,8 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
         CK(cudaEventRecord(c->ev_keys, c->side));
     }
     // ------------------------------------------------------------------ forward
-    KC(embed_forward(c->d_tokens, pp(c->i_wte), pp(c->i_wpe), c->act[0].x, B, T, C, V, s));
+    KC(embed_forward(c->d_tokens, pp(c->i_wte), pp(c->i_wpe), c->act[0].x, B, T, C, V, s,
+                     reinterpret_cast<const float*>(c->emb_rope), c->emb_rope_scale));
     for (int l = 0; l < L; ++l) {
         auto& a = c->act[l];
         auto& b = c->blocks[l];

@@ -105,6 +105,10 @@ struct Ctx {
     std::vector<bf16*> wqkv16, wo16, w1_16, w2_16;
     bool swiglu = false;
     float2* rope = nullptr;  // [max_t][hd/2] (cos, sin) when rope_qk
+    // Config::pos_encoding == RoPE: rope_cfg's (cos, sin) per position and column pair of the
+    // embedding sum, [max_t][C/2], and its attention scale
+    float2* emb_rope = nullptr;
+    float emb_rope_scale = 1.0f;
     // Mamba
     bool mamba = false;
     int mD = 0, mN = 0, mR = 0, mK = 0, mRP = 0, mRPp = 0, mRp = 0;

@@ -17,7 +17,8 @@ class LlmgpuConfig(ctypes.Structure):
                 ("d_state", c_int), ("dt_rank", c_int), ("conv_kernel", c_int),
                 ("ffn_swiglu", c_int), ("ffn_hidden", c_int), ("rope_qk", c_int),
                 ("rope_theta", c_float), ("moe_experts", c_int), ("moe_top_k", c_int),
-                ("moe_aux_coef", c_float)]
+                ("moe_aux_coef", c_float), ("pos_encoding", c_int), ("rope_scaling", c_float),
+                ("rope_mode", c_int), ("yarn_alpha", c_float), ("yarn_beta", c_float)]
 
 
 SIGS = {

@@ -17,15 +17,40 @@ import numpy as np
 _F32 = np.float32
 
 
-def _mt_draw(seed):
-    bg = np.random.MT19937(0)
-    bg._legacy_seeding(int(seed) & 0xFFFFFFFF)  # init_genrand, as std::mt19937(seed)
-    g1, g2 = (int(v) for v in bg.random_raw(2))
-    p = (float(g1) + float(g2) * 4294967296.0) / 18446744073709551616.0
-    return p if p < 1.0 else float(np.nextafter(1.0, 0.0))
+class MT19937:
+    """std::mt19937: the standard 32-bit Mersenne Twister with its standard seeding, as one
+    stream of outputs (the reference's GPT::generate draws every token from one stream)."""
+
+    def __init__(self, seed):
+        self.bg = np.random.MT19937(0)
+        self.bg._legacy_seeding(int(seed) & 0xFFFFFFFF)  # init_genrand, as std::mt19937(seed)
+
+    def next_u32(self):
+        return int(self.bg.random_raw())
+
+    def canonical(self):
+        """generate_canonical<double, 53> (libstdc++): two outputs, low word first."""
+        g1, g2 = self.next_u32(), self.next_u32()
+        p = (float(g1) + float(g2) * 4294967296.0) / 18446744073709551616.0
+        return p if p < 1.0 else float(np.nextafter(1.0, 0.0))
+
+    def uniform_int(self, a, b):
+        """std::uniform_int_distribution<int>(a, b) over a 32-bit engine (libstdc++): Lemire's
+        multiply-and-reject downscaling of one output (more only on a rejection)."""
+        r = b - a + 1
+        if r == 1 << 32:
+            return self.next_u32() + a
+        prod = self.next_u32() * r
+        low = prod & 0xFFFFFFFF
+        if low < r:
+            threshold = ((1 << 32) - r) % r
+            while low < threshold:
+                prod = self.next_u32() * r
+                low = prod & 0xFFFFFFFF
+        return (prod >> 32) + a
 
 
-def _discrete(weights, seed):
+def _discrete_draw(weights, p):
     w = [float(v) for v in weights]
     s = 0.0
     for v in w:
@@ -35,7 +60,12 @@ def _discrete(weights, seed):
         acc += v / s
         cp.append(acc)
     cp[-1] = 1.0
-    return int(np.searchsorted(np.asarray(cp), _mt_draw(seed), side="left"))
+    return int(np.searchsorted(np.asarray(cp), p, side="left"))
+
+
+def _discrete(weights, seed):
+    """std::discrete_distribution drawn once from a fresh std::mt19937(seed)."""
+    return _discrete_draw(weights, MT19937(seed).canonical())
 
 
 def _softmax32(l):
@@ -99,28 +129,47 @@ def should_stop(next_id, eos_id, stop_ids=()):
     return next_id == eos_id or next_id in stop_ids
 
 
-def generate(forward_logits, prompt, max_new_tokens, max_seq, temperature=0.0, top_k=0,
-             top_p=1.0, rep_penalty=1.0, seed=42, eos_id=None, stop_ids=()):
-    """GPT::generate's loop over a logits function (tokens [1, T] -> [1, V]): per new token,
-    the logits of the last position over the last max_seq tokens, the repetition penalty,
-    then greedy (temperature 0), top-k (k > 0), top-p (p < 1) or temperature sampling.
-    Token i draws with seed + i (GPT::generate draws every token from one std::mt19937
-    stream instead). Stops early at eos_id / stop_ids."""
+def generate(forward_logits, prompt, max_new_tokens, max_seq, vocab, temperature=0.0, top_k=0,
+             top_p=1.0, rep_penalty=1.0, seed=42, global_seed=42, eos_id=None, stop_ids=()):
+    """GPT::generate (src/model.cpp:393-474) over a logits function (tokens [1, T] -> [1, V]):
+
+    - the logits of the last position over the last max_seq tokens (zeros, i.e. uniform,
+      for an empty prompt), then the repetition penalty;
+    - temperature 0: the first maximum;
+    - otherwise the logits are divided by the temperature, then
+      * top_p < 1 with top_k == 0: sample_top_p with the global seed (every token draws from
+        a fresh std::mt19937(global_seed), as the reference's sample_top_p does);
+      * top_k > 0: one of the k largest logits, uniformly (std::uniform_int_distribution on
+        the generator stream);
+      * else: softmax, then std::discrete_distribution on the generator stream;
+    - the generator stream is one std::mt19937(seed) for the whole call (42 in the
+      reference).
+    Among equal logits, the top-k order here is index order (std::partial_sort leaves it
+    unspecified). Stops early at eos_id / stop_ids (generate_with_stop's rule)."""
     out = [int(t) for t in prompt]
-    for i in range(int(max_new_tokens)):
-        ctx = np.asarray(out[-max_seq:] or [0], np.int32)[None, :]
-        l = np.asarray(forward_logits(ctx)[0], _F32)
+    rng = MT19937(seed)
+    last = np.asarray(forward_logits(np.asarray(out[-max_seq:], np.int32)[None, :])[0], _F32) \
+        if out else np.zeros(int(vocab), _F32)
+    for step in range(int(max_new_tokens)):
+        cur = np.array(last, _F32)
         if rep_penalty != 1.0:
-            l = apply_repetition_penalty(l, out, rep_penalty)
+            cur = apply_repetition_penalty(cur, out, rep_penalty)
         if temperature == 0.0:
-            nxt = sample_greedy(l)
-        elif top_k > 0:
-            nxt = sample_top_k_seeded(l, top_k, temperature, seed + i)
-        elif top_p < 1.0:
-            nxt = sample_top_p_seeded(l, top_p, temperature, seed + i)
+            nxt = sample_greedy(cur)
         else:
-            nxt = sample_temperature_seeded(l, temperature, seed + i)
+            if temperature != 1.0:
+                cur = (cur / _F32(temperature)).astype(_F32)
+            if top_p < 1.0 and top_k == 0:
+                nxt = sample_top_p_seeded(cur, top_p, 1.0, global_seed)
+            elif top_k > 0:
+                idx = np.argsort(-cur, kind="stable")[:top_k]
+                nxt = int(idx[rng.uniform_int(0, top_k - 1)])
+            else:
+                nxt = _discrete_draw(_softmax32(cur), rng.canonical())
         out.append(nxt)
         if eos_id is not None and should_stop(nxt, eos_id, stop_ids):
             break
+        if step + 1 >= max_new_tokens:
+            break
+        last = np.asarray(forward_logits(np.asarray(out[-max_seq:], np.int32)[None, :])[0], _F32)
     return out

@@ -23,7 +23,8 @@ class LlmgpuError(RuntimeError):
 def make_config(vocab_size=50257, n_layers=12, n_heads=12, n_embd=768, block_size=1024,
                 weight_tying=True, use_rmsnorm=False, use_mamba=False, d_inner=0, d_state=16,
                 dt_rank=0, conv_kernel=4, ffn_swiglu=False, ffn_hidden=0, rope_qk=False,
-                rope_theta=10000.0, moe_experts=0, moe_top_k=2, moe_aux_coef=0.01):
+                rope_theta=10000.0, moe_experts=0, moe_top_k=2, moe_aux_coef=0.01,
+                pos_encoding=0, rope_scaling=1.0, rope_mode=0, yarn_alpha=1.0, yarn_beta=32.0):
     lib = load()
     c = LlmgpuConfig()
     lib.llmgpu_config_default(ctypes.byref(c))
@@ -33,7 +34,9 @@ def make_config(vocab_size=50257, n_layers=12, n_heads=12, n_embd=768, block_siz
                      d_state=d_state, dt_rank=dt_rank, conv_kernel=conv_kernel,
                      ffn_swiglu=int(ffn_swiglu), ffn_hidden=ffn_hidden, rope_qk=int(rope_qk),
                      rope_theta=rope_theta, moe_experts=moe_experts, moe_top_k=moe_top_k,
-                     moe_aux_coef=moe_aux_coef).items():
+                     moe_aux_coef=moe_aux_coef, pos_encoding=int(pos_encoding),
+                     rope_scaling=rope_scaling, rope_mode=rope_mode, yarn_alpha=yarn_alpha,
+                     yarn_beta=yarn_beta).items():
         setattr(c, k, v)
     return c
 
@@ -166,13 +169,13 @@ class Trainer:
         return out
 
     def generate(self, prompt, max_new_tokens, **sampling_args):
-        """GPT::generate (src/model.cpp) on the device forward: greedy by default; the
-        reference's temperature / top-k / top-p / repetition-penalty options as in
-        llmgpu.sampling.generate. Each token re-runs the forward over the last max_seq
-        tokens (no KV cache). Returns prompt + generated ids."""
+        """GPT::generate (src/model.cpp:393-474) on the device forward: greedy by default;
+        the reference's temperature / top-k / top-p / repetition-penalty options and its
+        one std::mt19937(42) stream, as in llmgpu.sampling.generate. Each token re-runs the
+        forward over the last max_seq tokens. Returns prompt + generated ids."""
         from . import sampling
         return sampling.generate(self.forward_logits, prompt, max_new_tokens, self.max_seq,
-                                 **sampling_args)
+                                 self.cfg.vocab_size, **sampling_args)
 
     # ------------------------------------------------------------------ parameters
     def num_params(self):

@@ -55,6 +55,14 @@ class Cfg:
     moe_experts: int = 0       # >0 replaces the FFN by MoEFFN
     moe_top_k: int = 2
     moe_aux_coef: float = 0.01
+    # Config::pos_encoding (include/llm/model.h:15-33): "learned", "sinusoidal" (wpe init
+    # only) or "rope" (rope_cfg on the embedding sum, with the options below; rope_theta
+    # above is Config::rope_theta)
+    pos_encoding: str = "learned"
+    rope_scaling: float = 1.0
+    rope_mode: int = 0
+    yarn_alpha: float = 1.0
+    yarn_beta: float = 32.0
 
     @property
     def hidden(self):
@@ -121,6 +129,8 @@ def init_params(cfg: Cfg, seed: int) -> List[np.ndarray]:
         else:
             a = (rng.standard_normal(shape) * 0.02).astype(np.float32)
         out.append(a)
+    if cfg.pos_encoding == "sinusoidal":
+        out[1] = sinusoidal_wpe(cfg.block_size, cfg.n_embd)
     return out
 
 
@@ -286,6 +296,48 @@ def rope_tables(T, hd, theta):
     freq = theta ** (-i / hd)
     ang = np.arange(T, dtype=np.float64)[:, None] * freq[None, :]
     return np.cos(ang), np.sin(ang)
+
+
+def rope_cfg_tables(T, C, theta, scaling, mode, alpha, beta):
+    """rope_cfg (src/model.cpp:71-104) in its own float32 arithmetic: per position and column
+    pair (i, i+1), i even, the (cos, sin) of pos * freq * yarn_alpha with freq = base^(-i/C),
+    base = theta * scaling for NTK (mode 0); for YaRN (mode 1, scaling > 1) freq =
+    ((1 - m)/scaling + m) * theta^(-i/C) with the ramp m of yarn_ramp and the output scale
+    sqrt(1 + 0.1 ln scaling). Returns cos, sin [T, C//2] and the scale."""
+    f = np.float32
+    sc = f(1.0) if f(scaling) < f(1.0) else f(scaling)
+    base = f(theta) * (sc if mode == 0 else f(1.0))
+    yarn = mode == 1 and sc > f(1.0)
+    scale = f(np.sqrt(f(1.0) + f(0.1) * f(np.log(sc)))) if yarn else f(1.0)
+    i = np.arange(0, C - 1, 2).astype(f)
+    expo = (-i / f(C)).astype(f)
+    freq = np.power(base, expo).astype(f)
+    if yarn:
+        d = (i / f(C) * f(beta)).astype(f)
+        low, high = f(beta) / f(2.0), f(beta)
+        m = np.where(d < low, f(0.0), np.where(d > high, f(1.0), (d - low) / (high - low))).astype(f)
+        freq = (((f(1.0) - m) / sc + m) * np.power(f(theta), expo)).astype(f)
+    ang = (np.arange(T, dtype=f)[:, None] * freq[None, :] * f(alpha)).astype(f)
+    return np.cos(ang), np.sin(ang), scale
+
+
+def rope_cfg_apply(x, cos, sin, scale):
+    """Rotates column pairs (2j, 2j+1) of x [T, C] and scales, as rope_cfg writes `out`."""
+    out = x.copy()
+    n = cos.shape[1]
+    x0, x1 = x[:, 0:2 * n:2], x[:, 1:2 * n:2]
+    out[:, 0:2 * n:2] = (x0 * cos - x1 * sin) * scale
+    out[:, 1:2 * n:2] = (x0 * sin + x1 * cos) * scale
+    return out
+
+
+def sinusoidal_wpe(block_size, C):
+    """GPT::GPT's sinusoidal wpe fill (src/model.cpp:34-41), float32."""
+    f = np.float32
+    pos = np.arange(block_size, dtype=f)[:, None]
+    i = np.arange(C)
+    angle = (pos / np.power(f(10000.0), ((2 * (i // 2)).astype(f) / f(C)).astype(f))).astype(f)
+    return np.where(i % 2 == 0, np.sin(angle), np.cos(angle)).astype(f)
 
 
 def rope_apply(x, cos, sin, inverse=False):
@@ -566,6 +618,39 @@ class Model:
         pre = f"blk{l}."
         return {n[len(pre):]: v for n, v in self.p.items() if n.startswith(pre)}
 
+    def _embed(self, tok):
+        """wte[tok] + wpe[t] (src/model.cpp:149-157), rotated by rope_cfg under RoPE (:158).
+        The backward scatters the gradient of the rotated sum into wte/wpe as it is
+        (src/model.cpp:314-322): the reference does not rotate it back."""
+        cfg, p = self.cfg, self.p
+        x = p["wte"][tok] + p["wpe"][:len(tok)]
+        if cfg.pos_encoding == "rope":
+            cos, sin, sc = rope_cfg_tables(len(tok), cfg.n_embd, cfg.rope_theta, cfg.rope_scaling,
+                                           cfg.rope_mode, cfg.yarn_alpha, cfg.yarn_beta)
+            x = rope_cfg_apply(x, cos.astype(x.dtype), sin.astype(x.dtype), x.dtype.type(sc))
+        return x
+
+    def logits(self, tokens):
+        """GPT::forward (src/model.cpp:140-171): logits [T, V] of one sequence."""
+        cfg = self.cfg
+        tok = np.asarray(tokens, np.int64) % cfg.vocab
+        p = self.p
+        x = self._embed(tok)
+        self._routes = None
+        for l in range(cfg.n_layers):
+            P = self._blk(l)
+            self._layer = l
+            if cfg.mamba:
+                x, _ = self._mamba_fwd(x, P)
+                continue
+            h1 = self._norm(x, P["ln1_gamma"], P["ln1_beta"])
+            att, _ = self._attn_fwd(h1, P)
+            y = x + att
+            f, _ = self._ffn_fwd(self._norm(y, P["ln2_gamma"], P["ln2_beta"]), P)
+            x = y + f
+        hid = self._norm(x, p["ln_f_gamma"], p["ln_f_beta"])
+        return hid @ (p["wte"].T if cfg.tied else p["lm_head"])
+
     def forward_backward(self, tokens):
         """One sequence: loss and gradients (dict name -> array), src/model.cpp:144-323."""
         cfg = self.cfg
@@ -573,7 +658,7 @@ class Model:
         V, C = cfg.vocab, cfg.n_embd
         tok = np.asarray(tokens, np.int64) % V
         p = self.p
-        x = p["wte"][tok] + p["wpe"][:T]
+        x = self._embed(tok)
         G = {n: np.zeros_like(a) for n, a in p.items()}
         xs, caches = [], []
         aux_total = 0.0

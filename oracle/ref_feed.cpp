@@ -6,6 +6,10 @@
 //   ref_feed log OUT_FILE            -> MetricsLogger lines written to OUT_FILE
 //   ref_feed pack TEXT_FILE BLOCK EOS RATIO -> pack_with_eos rows/masks, train_val_split sizes
 //   ref_feed sample                  -> logits rows, then seeded sampler picks (src/sampling.cpp)
+//   ref_feed rng                     -> draws of std::uniform_int_distribution and
+//                                       std::discrete_distribution sharing one std::mt19937(42)
+//   ref_feed generate CKPT TEMP TOPK TOPP REP N PROMPT... -> GPT::generate (src/model.cpp:393-474)
+//                                       on a v3 checkpoint (tied, LayerNorm, learned positions)
 // Calls: CosineScheduler::get_lr (src/scheduler.cpp:13-28), Dataset / DataLoader
 // (src/dataset.cpp:41-84), PrefetchLoader (src/prefetch.cpp), MetricsLogger::log_step
 // (src/logging.cpp:49-55).
@@ -15,7 +19,11 @@
 #include <string>
 #include <vector>
 
+#include <fstream>
+#include <random>
+
 #include "llm/dataset.h"
+#include "llm/model.h"
 #include "llm/logging.h"
 #include "llm/prefetch.h"
 #include "llm/sampling.h"
@@ -105,6 +113,46 @@ int main(int argc, char** argv) {
             for (float v : fp) std::printf(" %.9g", v);
             std::printf("\n");
         }
+        return 0;
+    }
+    if (!std::strcmp(argv[1], "rng")) {
+        std::mt19937 rng(42);
+        for (int i = 0; i < 400; ++i) {
+            const int k = 1 + (int)((i * 7919u + 13u) % 5000u);
+            if (i % 3 == 2) {
+                std::vector<float> w(17);
+                for (int j = 0; j < 17; ++j) w[j] = (float)((j * 31 + i) % 11 + 1);
+                std::discrete_distribution<int> d(w.begin(), w.end());
+                std::printf("disc %d %d\n", i, d(rng));
+            } else {
+                std::uniform_int_distribution<int> d(0, k - 1);
+                std::printf("uni %d %d %d\n", i, k, d(rng));
+            }
+        }
+        return 0;
+    }
+    if (!std::strcmp(argv[1], "generate") && argc >= 8) {
+        std::ifstream in(argv[2], std::ios::binary);
+        uint32_t magic = 0, version = 0;
+        size_t hdr[5] = {0};
+        in.read((char*)&magic, 4);
+        in.read((char*)&version, 4);
+        for (auto& h : hdr) in.read((char*)&h, sizeof(size_t));
+        if (!in || magic != 0x4C4C4D00u) return 3;
+        llm::Config c;
+        c.vocab_size = hdr[0];
+        c.n_layers = hdr[1];
+        c.n_heads = hdr[2];
+        c.n_embd = hdr[3];
+        c.block_size = hdr[4];
+        llm::GPT model(c);
+        model.load_binary(argv[2]);
+        std::vector<int> prompt;
+        for (int i = 8; i < argc; ++i) prompt.push_back(std::atoi(argv[i]));
+        auto out = model.generate(prompt, std::strtoul(argv[7], nullptr, 10),
+                                  (float)std::atof(argv[3]), std::atoi(argv[4]),
+                                  (float)std::atof(argv[5]), (float)std::atof(argv[6]));
+        print_batch("gen", out);
         return 0;
     }
     if (!std::strcmp(argv[1], "pack") && argc >= 6) {

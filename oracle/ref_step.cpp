@@ -17,7 +17,9 @@
 //   "-" as checkpoint keeps the reference initialisation (vocab/layers/heads/embd/block keys);
 //   "-" as token file draws seeded Zipf(1.1) ids (key seed).
 //   keys: steps, lr, b1, b2, eps, wd, clip, tied (0/1), rmsnorm (0/1), mamba (0/1),
-//         d_inner, d_state, dt_rank, conv_kernel, timing_only (0/1)
+//         d_inner, d_state, dt_rank, conv_kernel, timing_only (0/1),
+//         pos (0 learned, 1 sinusoidal, 2 RoPE), rope_theta, rope_scaling, rope_mode,
+//         yarn_alpha, yarn_beta (Config fields of include/llm/model.h:25-33)
 #include <algorithm>
 #include <chrono>
 #include <cmath>
@@ -117,6 +119,14 @@ int main(int argc, char** argv) {
     c.weight_tying = getf("tied", 1) != 0;
     c.use_rmsnorm = getf("rmsnorm", 0) != 0;
     c.use_mamba = version >= 4;
+    const int pos = (int)getf("pos", 0);
+    c.pos_encoding = pos == 2 ? llm::PosEncoding::RoPE
+                   : pos == 1 ? llm::PosEncoding::Sinusoidal : llm::PosEncoding::Learned;
+    c.rope_theta = (float)getf("rope_theta", 10000.0);
+    c.rope_scaling = (float)getf("rope_scaling", 1.0);
+    c.rope_mode = (int)getf("rope_mode", 0);
+    c.yarn_alpha = (float)getf("yarn_alpha", 1.0);
+    c.yarn_beta = (float)getf("yarn_beta", 32.0);
     if (c.use_mamba) {
         c.d_inner = mh[0];
         c.d_state = mh[1];

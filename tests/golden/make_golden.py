@@ -12,9 +12,14 @@ in <case>.npz:
   gnorm     float32 [steps]     Trainer::last_grad_norm()
   meta      json string         config and hyper-parameters
 
+Cases marked compact (the config-1 step, 840 K parameters) store no `init` (it is
+regenerated from meta["seed"] by gpt_oracle.init_params and checked against meta["init_sha256"])
+and store `params_delta` = params - init instead of `params`; oracle/golden.py reads both forms.
+
 Run from the repository root (needs the reference sources to build oracle/_ref):
-    make -C oracle ref && python tests/golden/make_golden.py
+    make -C oracle ref && python tests/golden/make_golden.py [case ...]
 """
+import hashlib
 import json
 import os
 import subprocess
@@ -47,7 +52,34 @@ CASES = {
                                rmsnorm=True, mamba=True, d_inner=32, d_state=4, dt_rank=2,
                                conv_kernel=4),
                       B=2, T=12, steps=2, seed=6, tok_seed=7, dt_scale=True),
+    # several heads: the per-head slicing of MultiHeadAttention (src/attention.cpp:35-102,
+    # 183-363) at head_dim 32 and 64 (the tcgen05 attention path), naive and flash forward
+    "gpt_mh4_hd32": dict(cfg=dict(vocab=96, n_layers=1, n_heads=4, n_embd=128, block_size=64),
+                         B=3, T=64, steps=2, seed=8, tok_seed=9, compact=True),
+    "gpt_mh2_hd64_t200": dict(cfg=dict(vocab=80, n_layers=1, n_heads=2, n_embd=128,
+                                       block_size=200),
+                              B=2, T=200, steps=1, seed=10, tok_seed=11, compact=True),
+    # Config::pos_encoding = RoPE: rope_cfg on the embedding sum (src/model.cpp:81-104,158),
+    # NTK base scaling and the YaRN ramp with its attention scale
+    "gpt_rope_ntk": dict(cfg=dict(vocab=64, n_layers=2, n_heads=2, n_embd=64, block_size=48,
+                                  pos_encoding="rope", rope_theta=10000.0, rope_scaling=2.0,
+                                  rope_mode=0),
+                         B=2, T=48, steps=2, seed=12, tok_seed=13, compact=True),
+    "gpt_rope_yarn": dict(cfg=dict(vocab=64, n_layers=1, n_heads=2, n_embd=64, block_size=40,
+                                   tied=False, rmsnorm=True, pos_encoding="rope",
+                                   rope_theta=500.0, rope_scaling=4.0, rope_mode=1,
+                                   yarn_alpha=1.5, yarn_beta=32.0),
+                          B=2, T=40, steps=2, seed=14, tok_seed=15, compact=True),
+    "mamba_rope": dict(cfg=dict(vocab=40, n_layers=1, n_heads=1, n_embd=16, block_size=12,
+                                rmsnorm=True, mamba=True, d_inner=32, d_state=4, dt_rank=2,
+                                conv_kernel=4, pos_encoding="rope", rope_scaling=3.0),
+                       B=2, T=12, steps=1, seed=16, tok_seed=17),
+    # the tiny char-level configuration exactly: 4 layers, n_embd 128, 4 heads, vocab 256,
+    # T 128, batch 8, ids uniform over [0, 256) from PCG64 seed 0, weights from seed 1
+    "gpt_config1": dict(cfg=dict(vocab=256, n_layers=4, n_heads=4, n_embd=128, block_size=128),
+                        B=8, T=128, steps=1, seed=1, tok_seed=0, compact=True, threads=8),
 }
+POS = {"learned": 0, "sinusoidal": 1, "rope": 2}
 HP = dict(lr=3e-4, b1=0.9, b2=0.95, eps=1e-8, wd=0.1, clip=1.0)
 
 
@@ -76,23 +108,31 @@ def run_case(name, spec, outdir):
         go.write_ckpt(ck, cfg, params)
         tokens.tofile(tk)
         args = [REF, ck, tk, str(B), str(T), td, f"steps={steps}",
-                f"tied={int(cfg.tied)}", f"rmsnorm={int(cfg.rmsnorm)}"]
+                f"tied={int(cfg.tied)}", f"rmsnorm={int(cfg.rmsnorm)}",
+                f"pos={POS[cfg.pos_encoding]}", f"rope_theta={cfg.rope_theta!r}",
+                f"rope_scaling={cfg.rope_scaling!r}", f"rope_mode={cfg.rope_mode}",
+                f"yarn_alpha={cfg.yarn_alpha!r}", f"yarn_beta={cfg.yarn_beta!r}"]
         args += [f"{k}={v}" for k, v in HP.items()]
-        env = dict(os.environ, OMP_NUM_THREADS="1")
+        env = dict(os.environ, OMP_NUM_THREADS=str(spec.get("threads", 1)))
         subprocess.run(args, check=True, env=env, stdout=subprocess.DEVNULL)
         rd = lambda f: np.fromfile(os.path.join(td, f), np.float32)  # noqa: E731
-        out = dict(init=np.concatenate([p.ravel() for p in params]), tokens=tokens,
-                   losses=rd("losses.f32"), grads=rd("grads.f32"), params=rd("params.f32"),
-                   gnorm=rd("gnorm.f32"))
+        init = np.concatenate([p.ravel() for p in params])
+        out = dict(init=init, tokens=tokens, losses=rd("losses.f32"), grads=rd("grads.f32"),
+                   params=rd("params.f32"), gnorm=rd("gnorm.f32"))
     meta = dict(cfg=spec["cfg"], B=B, T=T, steps=steps, hp=HP)
+    if spec.get("compact"):
+        meta.update(seed=spec["seed"], init_sha256=hashlib.sha256(init.tobytes()).hexdigest())
+        out["params_delta"] = out.pop("params") - init
+        del out["init"]
     np.savez_compressed(os.path.join(outdir, name + ".npz"), meta=json.dumps(meta), **out)
-    print(name, "loss0", out["losses"][0], "n_params", out["params"].size)
+    print(name, "loss0", out["losses"][0], "n_params", out["grads"].size)
 
 
 def main():
     outdir = os.path.dirname(os.path.abspath(__file__))
-    for name, spec in CASES.items():
-        run_case(name, spec, outdir)
+    names = sys.argv[1:] or list(CASES)
+    for name in names:
+        run_case(name, CASES[name], outdir)
 
 
 if __name__ == "__main__":

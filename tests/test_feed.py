@@ -161,15 +161,67 @@ def test_generate_loop_with_a_stand_in_model():
         r = np.random.default_rng(int(ctx.sum()) + ctx.shape[1])
         return r.standard_normal((1, V)).astype(np.float32)
 
-    out = sampling.generate(logits, [1, 2, 3], 5, max_seq=4)
+    out = sampling.generate(logits, [1, 2, 3], 5, max_seq=4, vocab=V)
     assert len(out) == 8 and max(seen) == 4
     for k in range(3, 8):
         assert out[k] == sampling.sample_greedy(logits(np.asarray(out[:k][-4:], np.int32)[None]))
-    a = sampling.generate(logits, [5], 6, 16, temperature=0.9, top_k=5, seed=3)
-    b = sampling.generate(logits, [5], 6, 16, temperature=0.9, top_k=5, seed=3)
+    a = sampling.generate(logits, [5], 6, 16, V, temperature=0.9, top_k=5, seed=3)
+    b = sampling.generate(logits, [5], 6, 16, V, temperature=0.9, top_k=5, seed=3)
     assert a == b
-    c = sampling.generate(logits, [5], 20, 16, temperature=1.0, top_p=0.9, eos_id=a[1])
+    c = sampling.generate(logits, [5], 20, 16, V, temperature=1.0, top_p=0.9, eos_id=a[1])
     assert len(c) >= 2 and (len(c) == 21 or c[-1] == a[1])
+    # an empty prompt starts from zero logits (uniform), as GPT::generate does
+    assert sampling.generate(logits, [], 1, 16, V) == [0]
+
+
+def test_shared_generator_stream_matches_reference():
+    """MT19937.uniform_int / canonical: std::uniform_int_distribution and
+    std::discrete_distribution drawing from one std::mt19937(42), interleaved."""
+    from llmgpu import sampling
+    rng = sampling.MT19937(42)
+    n = 0
+    for line in _ref("rng").splitlines():
+        f = line.split()
+        if f[0] == "uni":
+            assert rng.uniform_int(0, int(f[2]) - 1) == int(f[3]), line
+        else:
+            i = int(f[1])
+            w = [float((j * 31 + i) % 11 + 1) for j in range(17)]
+            assert sampling._discrete_draw(w, rng.canonical()) == int(f[2]), line
+        n += 1
+    assert n == 400
+
+
+@pytest.mark.parametrize("opts", [
+    dict(temp=0.0, top_k=0, top_p=1.0, rep=1.0, prompt=[3, 1, 4, 1, 5]),
+    dict(temp=0.8, top_k=0, top_p=1.0, rep=1.0, prompt=[3, 1, 4]),
+    dict(temp=1.3, top_k=7, top_p=1.0, rep=1.0, prompt=[2, 7]),
+    dict(temp=0.9, top_k=0, top_p=0.8, rep=1.0, prompt=[9]),
+    dict(temp=1.0, top_k=0, top_p=1.0, rep=1.4, prompt=[5, 5, 6]),
+    dict(temp=0.7, top_k=3, top_p=1.0, rep=1.2, prompt=[]),
+])
+def test_generate_matches_reference(tmp_path, opts):
+    """sampling.generate, run over the oracle's logits, picks the reference's GPT::generate
+    tokens (one std::mt19937(42) stream; uniform pick among the top k; top-p with the
+    global seed; zero logits for an empty prompt; repetition penalty)."""
+    import sys
+    sys.path.insert(0, ROOT)
+    from llmgpu import sampling
+    from oracle import gpt_oracle as go
+    cfg = go.Cfg(vocab=40, n_layers=1, n_heads=2, n_embd=32, block_size=32)
+    params = go.init_params(cfg, seed=21)
+    params[0] = params[0] * 50.0  # sharp logits: the top-k order has no near-ties
+    ck = str(tmp_path / "m.bin")
+    go.write_ckpt(ck, cfg, params)
+    n = 12
+    line = _ref("generate", ck, str(opts["temp"]), str(opts["top_k"]), str(opts["top_p"]),
+                str(opts["rep"]), str(n), *[str(t) for t in opts["prompt"]]).split()
+    want = [int(t) for t in line[2:]]
+    model = go.Model(cfg, params)
+    got = sampling.generate(lambda ctx: model.logits(ctx[0])[-1:], opts["prompt"], n,
+                            cfg.block_size, cfg.vocab, temperature=opts["temp"],
+                            top_k=opts["top_k"], top_p=opts["top_p"], rep_penalty=opts["rep"])
+    assert got == want
 
 
 def test_train_loop_with_a_stand_in_trainer(tmp_path):

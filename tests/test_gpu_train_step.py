@@ -14,6 +14,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
+from oracle import golden  # noqa: E402
 from oracle import gpt_oracle as go  # noqa: E402
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
@@ -45,7 +46,10 @@ def _trainer(cfg: go.Cfg, B, T, params, hp=None, clip=1.0):
                     ffn_swiglu=cfg.ffn == "swiglu", ffn_hidden=cfg.ffn_hidden,
                     rope_qk=cfg.rope_qk, rope_theta=cfg.rope_theta,
                     moe_experts=cfg.moe_experts, moe_top_k=cfg.moe_top_k,
-                    moe_aux_coef=cfg.moe_aux_coef)
+                    moe_aux_coef=cfg.moe_aux_coef,
+                    pos_encoding={"learned": 0, "sinusoidal": 1, "rope": 2}[cfg.pos_encoding],
+                    rope_scaling=cfg.rope_scaling, rope_mode=cfg.rope_mode,
+                    yarn_alpha=cfg.yarn_alpha, yarn_beta=cfg.yarn_beta)
     tr = Trainer(c, B, T)
     hp = hp or dict(lr=3e-4, b1=0.9, b2=0.95, eps=1e-8, wd=0.1)
     tr.set_adamw(**hp)
@@ -112,12 +116,13 @@ def _check_params(tr, ref, names, init=None, ref_m=None, steps=1, lr=3e-4, tol=G
     assert not bad, bad
 
 
-@pytest.mark.parametrize("name", ["gpt_ln_gelu_tied", "gpt_rms_untied", "gpt_flash_t136",
-                                  "mamba_rms"])
+GOLDEN_STEPS = sorted(f[:-4] for f in os.listdir(GOLDEN)
+                      if f.endswith(".npz") and not f.startswith("moe_"))
+
+
+@pytest.mark.parametrize("name", GOLDEN_STEPS)
 def test_golden_train_step(cuda, name):
-    z = np.load(os.path.join(GOLDEN, name + ".npz"))
-    meta = json.loads(str(z["meta"]))
-    cfg = go.Cfg(**meta["cfg"])
+    z, meta, cfg = golden.load(os.path.join(GOLDEN, name + ".npz"))
     B, T, steps = meta["B"], meta["T"], meta["steps"]
     names = [n for n, _ in go.param_specs(cfg)]
     hp = {k: v for k, v in meta["hp"].items() if k != "clip"}
@@ -161,6 +166,15 @@ ORACLE_CASES = {
     "mamba_ragged_n8": (go.Cfg(vocab=256, n_layers=1, n_heads=1, n_embd=64, block_size=100,
                                rmsnorm=True, mamba=True, d_inner=80, d_state=8, dt_rank=6,
                                conv_kernel=3), 3, 100),
+    # the GPT-2-small width (n_embd 768, 12 heads of 64, vocab 50257, T 1024) with two
+    # layers and one sequence: the tcgen05 GEMM/attention tiles and the padded 50304-wide
+    # logits at the configuration of record, against the oracle on Zipf(1.1) ids
+    "gpt2_width_2l": (go.Cfg(vocab=50257, n_layers=2, n_heads=12, n_embd=768,
+                             block_size=1024), 1, 1024),
+    # Config::pos_encoding = RoPE with the YaRN ramp (rope_cfg on the embedding sum) at
+    # head_dim 64 with several heads; the reference fixtures pin head_dim 32
+    "rope_cfg_yarn_hd64": (go.Cfg(vocab=300, n_layers=2, n_heads=4, n_embd=256, block_size=160,
+                                  pos_encoding="rope", rope_scaling=4.0, rope_mode=1), 2, 160),
     # long Mamba sequence: the forward scan runs as two segments side by side (T >= 1024),
     # the second starting from the state the first hands over; ragged chunk split
     "mamba_long_segments": (go.Cfg(vocab=256, n_layers=1, n_heads=1, n_embd=64,
@@ -186,7 +200,10 @@ def _case_params(case, cfg):
 def test_oracle_train_step(cuda, case):
     cfg, B, T = ORACLE_CASES[case]
     params = _case_params(case, cfg)
-    toks = go.uniform_tokens(cfg.vocab, 2 * B * T, seed=12).reshape(2, B, T)
+    if cfg.vocab > 10000:  # the configurations of record draw Zipf(1.1) ids
+        toks = go.zipf_tokens(cfg.vocab, 2 * B * T, seed=12).reshape(2, B, T)
+    else:
+        toks = go.uniform_tokens(cfg.vocab, 2 * B * T, seed=12).reshape(2, B, T)
     names = [n for n, _ in go.param_specs(cfg)]
     tr = _trainer(cfg, B, T, params)
     model = go.Model(cfg, params)

@@ -59,6 +59,32 @@ def test_noalloc_splitk_matches_workspace_gemm(cuda):
         torch.cuda.synchronize()
         assert int(err.item()) == 0
         assert _rel(got, want) < 1e-5
+        # and against a plain fp32 product of the same bf16 operands
+        ref = a.float().t() @ b.float()
+        if grouped:
+            ref = ref.reshape(M, N // c["group"], c["group"]).permute(1, 0, 2)
+        ref = ref + base if c["acc"] else ref
+        assert _rel(got, ref) < 1e-5
+
+
+def test_noalloc_rejects_what_the_workspace_gemm_rejects(cuda):
+    """A column group that is neither N nor a multiple of 32 is refused by both entry points
+    with the same status."""
+    from llmgpu import load, ops
+    lib = load()
+    noalloc = _noalloc(lib)
+    M, N, K, S, group = 64, 96, 256, 2, 48
+    a = torch.zeros(K, M, dtype=torch.bfloat16, device=cuda)
+    b = torch.zeros(K, N, dtype=torch.bfloat16, device=cuda)
+    out = torch.zeros(N // group, M, group, device=cuda)
+    ws = torch.zeros(S * M * N, device=cuda)
+    stream = torch.cuda.current_stream().cuda_stream
+    rc_ws = lib.llmgpu_op_gemm(a.data_ptr(), M, 1, b.data_ptr(), N, 1, M, N, K, ops.EPI_F32,
+                               out.data_ptr(), group, 0, None, 0, None, 0, S, ws.data_ptr(),
+                               group, M * group, 0, None, stream)
+    rc_na = noalloc(a.data_ptr(), M, 1, b.data_ptr(), N, 1, M, N, K, out.data_ptr(), group, 0, S,
+                    group, M * group, None, stream)
+    assert rc_ws == rc_na == -7
 
 
 def test_noalloc_rejects_oversize(cuda):
