@@ -98,6 +98,11 @@ int llmgpu_set_adamw(llmgpu_ctx* ctx, float lr, float b1, float b2, float eps, f
 int llmgpu_set_lr(llmgpu_ctx* ctx, float lr); /* Optimizer::set_lr */
 int llmgpu_set_train(llmgpu_ctx* ctx, float grad_clip, int grad_accum_steps,
                      float label_smoothing);
+/* TrainConfig::loss_scale (src/trainer.cpp:91,103-105): the loss gradient is multiplied by
+ * `scale` and the parameter gradients are divided by it before the non-finite check and the
+ * clip. 1 (the default) leaves the step unchanged; a power of two gives the same result bit
+ * for bit (the scale is exact in fp32 and bf16). Returns 0 or LLMGPU_E_ARG (scale <= 0). */
+int llmgpu_set_loss_scale(llmgpu_ctx* ctx, float scale);
 
 /* One optimizer step over B sequences of T tokens (targets = inputs, src/trainer.cpp:39),
  * equal to the reference's train_step_accum with K = B micro-batches of one sequence
@@ -123,6 +128,11 @@ int llmgpu_eval_loss(llmgpu_ctx* ctx, const int32_t* tokens, int B, int T, float
  * negative status. */
 int64_t llmgpu_forward_logits(llmgpu_ctx* ctx, const int32_t* tokens, int B, int T,
                               float* logits, int64_t cap);
+/* The same forward, returning the logits of every position (GPT::forward, src/model.cpp:140-171):
+ * B*T*V floats in sequence-major order, capacity `cap` floats. Returns B*T*V or a negative
+ * status. */
+int64_t llmgpu_forward_logits_all(llmgpu_ctx* ctx, const int32_t* tokens, int B, int T,
+                                  float* logits, int64_t cap);
 
 /* Parameters in GPT::parameters() order (src/model.cpp:889-909). */
 int llmgpu_num_params(const llmgpu_ctx* ctx);           /* number of parameter tensors */

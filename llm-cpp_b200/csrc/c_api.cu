@@ -33,6 +33,16 @@ int stage_tokens(Ctx* c, const int32_t* tokens, int B, int T) {
     return 0;
 }
 
+// Forgets the captured step, so that the next step is captured again with the current
+// kernel arguments.
+void drop_graph(Ctx* c) {
+    if (c->graph) {
+        cudaGraphExecDestroy(c->graph);
+        c->graph = nullptr;
+    }
+    c->graph_B = -1;
+}
+
 int validate_bt(Ctx* c, int B, int T) {
     if (B <= 0 || T <= 0 || B > c->max_b || T > c->max_t || (long long)B * T > c->max_bt) {
         c->err = "B x T outside the context's capacity";
@@ -239,10 +249,20 @@ int llmgpu_set_lr(llmgpu_ctx* h, float lr) {
 
 int llmgpu_set_train(llmgpu_ctx* h, float grad_clip, int grad_accum_steps, float label_smoothing) {
     if (check_ctx(h) || grad_accum_steps < 1) return LLMGPU_E_ARG;
-    h->c->clip = grad_clip;
-    h->c->accum_k = grad_accum_steps;
-    h->c->accum_count = 0;
-    h->c->smoothing = label_smoothing;
+    Ctx* c = h->c;
+    // the clip and the smoothing are arguments of kernels inside the captured step
+    if (grad_clip != c->clip || label_smoothing != c->smoothing) drop_graph(c);
+    c->clip = grad_clip;
+    c->accum_k = grad_accum_steps;
+    c->accum_count = 0;
+    c->smoothing = label_smoothing;
+    return 0;
+}
+
+int llmgpu_set_loss_scale(llmgpu_ctx* h, float scale) {
+    if (check_ctx(h) || !(scale > 0.0f)) return LLMGPU_E_ARG;
+    if (scale != h->c->loss_scale) drop_graph(h->c);
+    h->c->loss_scale = scale;
     return 0;
 }
 
@@ -310,12 +330,15 @@ int llmgpu_eval_loss(llmgpu_ctx* h, const int32_t* tokens, int B, int T, float* 
     return 0;
 }
 
-int64_t llmgpu_forward_logits(llmgpu_ctx* h, const int32_t* tokens, int B, int T, float* logits,
-                              int64_t cap) {
+// Forward up to the lm head, then rows of the bf16 logits to host floats: the last position
+// of each sequence (all_rows false) or every position.
+static int64_t forward_rows(llmgpu_ctx* h, const int32_t* tokens, int B, int T, float* logits,
+                            int64_t cap, bool all_rows) {
     if (check_ctx(h) || !tokens || !logits) return LLMGPU_E_ARG;
     Ctx* c = h->c;
     if (B <= 0 || T <= 0 || (long long)B * T > c->max_bt || T > c->max_t) return LLMGPU_E_ARG;
-    if (cap < (int64_t)B * c->V) return LLMGPU_E_ARG;
+    const int64_t nrows = all_rows ? (int64_t)B * T : B;
+    if (cap < nrows * c->V) return LLMGPU_E_ARG;
     int rc = stage_tokens(c, tokens, B, T);
     if (rc) return rc;
     c->plan_cursor = 0;
@@ -325,18 +348,29 @@ int64_t llmgpu_forward_logits(llmgpu_ctx* h, const int32_t* tokens, int B, int T
     rc = run_fwd_bwd(c, B, T, 0, false);
     c->logits_only = false;
     if (rc) return rc;
-    // row T-1 of each sequence: B rows of V bf16, T * Vp apart
-    std::vector<uint16_t> rows((size_t)B * c->V);
-    if (cudaMemcpy2DAsync(rows.data(), (size_t)c->V * 2, c->logits + (size_t)(T - 1) * c->Vp,
-                          (size_t)T * c->Vp * 2, (size_t)c->V * 2, (size_t)B,
-                          cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+    // row T-1 of each sequence (B rows T * Vp apart), or all B*T rows (Vp apart)
+    std::vector<uint16_t> rows((size_t)nrows * c->V);
+    const bf16* src = all_rows ? c->logits : c->logits + (size_t)(T - 1) * c->Vp;
+    const size_t pitch = (all_rows ? (size_t)1 : (size_t)T) * c->Vp * 2;
+    if (cudaMemcpy2DAsync(rows.data(), (size_t)c->V * 2, src, pitch, (size_t)c->V * 2,
+                          (size_t)nrows, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
         return LLMGPU_E_CUDA;
     if ((rc = ctx_sync_check(c))) return rc;
     for (size_t i = 0; i < rows.size(); ++i) {
         const uint32_t bits = (uint32_t)rows[i] << 16;
         std::memcpy(&logits[i], &bits, sizeof(float));
     }
-    return (int64_t)B * c->V;
+    return nrows * c->V;
+}
+
+int64_t llmgpu_forward_logits(llmgpu_ctx* h, const int32_t* tokens, int B, int T, float* logits,
+                              int64_t cap) {
+    return forward_rows(h, tokens, B, T, logits, cap, false);
+}
+
+int64_t llmgpu_forward_logits_all(llmgpu_ctx* h, const int32_t* tokens, int B, int T,
+                                  float* logits, int64_t cap) {
+    return forward_rows(h, tokens, B, T, logits, cap, true);
 }
 
 int llmgpu_num_params(const llmgpu_ctx* h) {

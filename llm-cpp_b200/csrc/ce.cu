@@ -10,7 +10,7 @@ namespace llmgpu {
 
 namespace {
 
-constexpr int kCeThreads = 1024;
+constexpr int kCeThreads = 512;
 
 __device__ __forceinline__ float block_reduce(float v, float* sh, bool is_max) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -35,93 +35,100 @@ __device__ __forceinline__ float block_reduce(float v, float* sh, bool is_max) {
     return sh[32];
 }
 
-// Persistent over rows: CTA b takes rows b, b + grid, ... A row (Vp bf16) arrives by one
-// bulk copy into a shared buffer, is overwritten in place by its gradient, and leaves by one
-// bulk store, so the threads only do arithmetic. With two buffers (nbuf 2, rows up to half
-// the shared memory) the next row's copy runs while the current one is computed.
-__global__ void __launch_bounds__(kCeThreads, 1) ce_kernel(bf16* __restrict__ logits, int rows,
+// Combines two (max, sum of 2^((x - max) log2e)) pairs of the same row.
+__device__ __forceinline__ float2 lse_combine(float2 a, float2 b) {
+    constexpr float kLog2e = 1.4426950408889634f;
+    const float m = fmaxf(a.x, b.x);
+    const float sa = a.y == 0.f ? 0.f : a.y * ex2_approx((a.x - m) * kLog2e);
+    const float sb = b.y == 0.f ? 0.f : b.y * ex2_approx((b.x - m) * kLog2e);
+    return make_float2(m, sa + sb);
+}
+
+// Persistent over rows, two CTAs per SM: CTA b takes rows b, b + grid, ... A row (Vp bf16)
+// arrives by one bulk copy into the CTA's shared buffer, is overwritten in place by its
+// gradient and leaves by one bulk store, so the threads only do arithmetic; while one CTA of
+// an SM waits for its row, the other computes. Each row takes two passes over shared memory:
+// an online max / sum of exponentials (a thread rescales its running sum when its maximum
+// grows; the per-thread pairs meet in one block reduction), then the gradient.
+__global__ void __launch_bounds__(kCeThreads, 2) ce_kernel(bf16* __restrict__ logits, int rows,
                                                             int V, int Vp,
                                                             const int32_t* __restrict__ tokens,
                                                             float* __restrict__ row_loss,
-                                                            float scale, float smoothing,
-                                                            int nbuf, int* err) {
-    extern __shared__ __align__(128) uint8_t ce_smem[];  // nbuf x Vp bf16 (Vp % 8 == 0)
-    __shared__ float red[33];
+                                                            float scale, float smoothing, int* err) {
+    extern __shared__ __align__(128) uint8_t ce_smem[];  // Vp bf16 (Vp % 8 == 0)
+    __shared__ float2 red[kCeThreads / 32 + 1];
     __shared__ float s_tgt;
-    __shared__ __align__(8) uint64_t bar[2];
+    __shared__ __align__(8) uint64_t bar;
     const uint32_t row_bytes = (uint32_t)Vp * 2u;
     const int n8 = Vp >> 3;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
+        mbar_init(&bar, 1);
         fence_barrier_init();
     }
     __syncthreads();
     int row = blockIdx.x;
     if (row >= rows) return;
-    if (threadIdx.x == 0) {
-        mbar_arrive_expect_tx(&bar[0], row_bytes);
-        bulk_load_g2s(ce_smem, logits + (long long)row * Vp, row_bytes, &bar[0]);
-    }
+    uint4* srow = reinterpret_cast<uint4*>(ce_smem);
     const float off = (smoothing > 0.f && V > 1) ? smoothing / (float)(V - 1) : 0.f;
     const float on = 1.0f - smoothing;
+    constexpr float kLog2e = 1.4426950408889634f;
+    // groups of 8 columns: [0, nfull) all valid, then at most one partly valid group, then
+    // padding up to Vp
+    const int nfull = V >> 3, nval = (V + 7) >> 3;
     for (int it = 0; row < rows; ++it, row += gridDim.x) {
-        const int b = nbuf == 2 ? (it & 1) : 0;
-        uint4* srow = reinterpret_cast<uint4*>(ce_smem + (size_t)b * row_bytes);
         if (threadIdx.x == 0) {
-            // a buffer is refilled once the gradient store of its previous row has read it
-            const int next = row + gridDim.x;
-            if (nbuf == 2 && next < rows) {
-                bulk_wait_group_read<0>();
-                mbar_arrive_expect_tx(&bar[b ^ 1], row_bytes);
-                bulk_load_g2s(ce_smem + (size_t)(b ^ 1) * row_bytes,
-                              logits + (long long)next * Vp, row_bytes, &bar[b ^ 1]);
-            } else if (nbuf == 1 && it > 0) {
-                bulk_wait_group_read<0>();
-                mbar_arrive_expect_tx(&bar[0], row_bytes);
-                bulk_load_g2s(ce_smem, logits + (long long)row * Vp, row_bytes, &bar[0]);
-            }
+            // the buffer is refilled once the previous row's gradient store has read it
+            if (it > 0) bulk_wait_group_read<0>();
+            mbar_arrive_expect_tx(&bar, row_bytes);
+            bulk_load_g2s(ce_smem, logits + (long long)row * Vp, row_bytes, &bar);
         }
-        mbar_wait_bounded(&bar[b], (uint32_t)(nbuf == 2 ? (it >> 1) & 1 : it & 1), err,
-                          kDevTimeoutFull);
         int tgt = tokens[row] % V;
         if (tgt < 0) tgt += V;
-        // groups of 8 columns: [0, nfull) all valid, then at most one partly valid group,
-        // then padding up to Vp
-        const int nfull = V >> 3, nval = (V + 7) >> 3;
-        float mx = -FLT_MAX;
-        for (int i = threadIdx.x; i < nfull; i += blockDim.x) {
-            const uint4 u = srow[i];
-            mx = fmaxf(mx, fmaxf(fmaxf(fmaxf(bf16_lo(u.x), bf16_hi(u.x)),
-                                       fmaxf(bf16_lo(u.y), bf16_hi(u.y))),
-                                 fmaxf(fmaxf(bf16_lo(u.z), bf16_hi(u.z)),
-                                       fmaxf(bf16_lo(u.w), bf16_hi(u.w)))));
-        }
-        if (threadIdx.x == 0 && nval > nfull) {
-            const bf16* t = reinterpret_cast<const bf16*>(srow + nfull);
-            for (int c = nfull * 8; c < V; ++c) mx = fmaxf(mx, __bfloat162float(t[c - nfull * 8]));
-        }
-        if (threadIdx.x == 0) s_tgt = __bfloat162float(reinterpret_cast<const bf16*>(srow)[tgt]);
-        mx = block_reduce(mx, red, true);
-        // exp(x - m) = 2^(x log2e - m log2e)
-        constexpr float kLog2e = 1.4426950408889634f;
-        const float mxl = mx * kLog2e;
-        float se = 0.f;
+        mbar_wait_bounded(&bar, (uint32_t)(it & 1), err, kDevTimeoutFull);
+        float2 ms = make_float2(-FLT_MAX, 0.f);  // running (max, sum of 2^((x - max) log2e))
         for (int i = threadIdx.x; i < nfull; i += blockDim.x) {
             const uint4 u = srow[i];
             const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+            float m8 = fmaxf(fmaxf(fmaxf(bf16_lo(u.x), bf16_hi(u.x)), fmaxf(bf16_lo(u.y), bf16_hi(u.y))),
+                             fmaxf(fmaxf(bf16_lo(u.z), bf16_hi(u.z)), fmaxf(bf16_lo(u.w), bf16_hi(u.w))));
+            if (m8 > ms.x) {
+                ms.y = ms.y == 0.f ? 0.f : ms.y * ex2_approx((ms.x - m8) * kLog2e);
+                ms.x = m8;
+            }
+            const float ml = ms.x * kLog2e;
+            float acc = 0.f;
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-                se += ex2_approx(fmaf(bf16_lo(w[k]), kLog2e, -mxl)) +
-                      ex2_approx(fmaf(bf16_hi(w[k]), kLog2e, -mxl));
+                acc += ex2_approx(fmaf(bf16_lo(w[k]), kLog2e, -ml)) +
+                       ex2_approx(fmaf(bf16_hi(w[k]), kLog2e, -ml));
+            ms.y += acc;
         }
-        if (threadIdx.x == 0 && nval > nfull) {
-            const bf16* t = reinterpret_cast<const bf16*>(srow + nfull);
-            for (int c = nfull * 8; c < V; ++c)
-                se += ex2_approx(fmaf(__bfloat162float(t[c - nfull * 8]), kLog2e, -mxl));
+        if (threadIdx.x == 0) {
+            if (nval > nfull) {
+                const bf16* t = reinterpret_cast<const bf16*>(srow + nfull);
+                for (int c = nfull * 8; c < V; ++c)
+                    ms = lse_combine(ms, make_float2(__bfloat162float(t[c - nfull * 8]), 1.f));
+            }
+            s_tgt = __bfloat162float(reinterpret_cast<const bf16*>(srow)[tgt]);
         }
-        se = block_reduce(se, red, false);
-        const float lse = mx + logf(se);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+            ms = lse_combine(ms, make_float2(__shfl_xor_sync(0xffffffffu, ms.x, o),
+                                             __shfl_xor_sync(0xffffffffu, ms.y, o)));
+        if (lane == 0) red[warp] = ms;
+        __syncthreads();
+        if (warp == 0) {
+            ms = lane < (int)(blockDim.x >> 5) ? red[lane] : make_float2(-FLT_MAX, 0.f);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+                ms = lse_combine(ms, make_float2(__shfl_xor_sync(0xffffffffu, ms.x, o),
+                                                 __shfl_xor_sync(0xffffffffu, ms.y, o)));
+            if (lane == 0) red[kCeThreads / 32] = ms;
+        }
+        __syncthreads();
+        ms = red[kCeThreads / 32];
+        const float lse = ms.x + logf(ms.y);
         const float lsel = lse * kLog2e;
         if (threadIdx.x == 0) row_loss[row] = lse - s_tgt;
         // dlogits = (softmax - y) * scale; y = off everywhere but `on` at the target, and the
@@ -149,12 +156,15 @@ __global__ void __launch_bounds__(kCeThreads, 1) ce_kernel(bf16* __restrict__ lo
                 }
             }
             if (i == (tgt >> 3)) {  // the target column takes `on` instead of `off`
-                const int k = (tgt & 7) >> 1;
-                const float x = (tgt & 1) ? bf16_hi(w[k]) : bf16_lo(w[k]);
-                const float gt = (ex2_approx(fmaf(x, kLog2e, -lsel)) - on) * scale;
-                const float lo = (tgt & 1) ? bf16_lo(o[k]) : gt;
-                const float hi = (tgt & 1) ? gt : bf16_hi(o[k]);
-                o[k] = pack_bf16x2(lo, hi);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    if (k != ((tgt & 7) >> 1)) continue;
+                    const float x = (tgt & 1) ? bf16_hi(w[k]) : bf16_lo(w[k]);
+                    const float gt = (ex2_approx(fmaf(x, kLog2e, -lsel)) - on) * scale;
+                    const float lo = (tgt & 1) ? bf16_lo(o[k]) : gt;
+                    const float hi = (tgt & 1) ? gt : bf16_hi(o[k]);
+                    o[k] = pack_bf16x2(lo, hi);
+                }
             }
             srow[i] = make_uint4(o[0], o[1], o[2], o[3]);
         }
@@ -183,11 +193,11 @@ int cross_entropy_fwd_bwd(bf16* logits, int rows, int V, int Vp, const int32_t* 
                           int* err) {
     if ((Vp & 7) != 0 || V > Vp || rows <= 0) return -1;
     if ((reinterpret_cast<uintptr_t>(logits) & 15) != 0) return -3;
+    // one row per CTA in shared memory: two CTAs per SM for rows up to 110 KB (vocabularies
+    // up to 56,320), one for rows up to 220 KB
     constexpr size_t kMaxSmem = 220 * 1024;
-    const size_t row = (size_t)Vp * sizeof(bf16);
-    if (row > kMaxSmem) return -2;
-    const int nbuf = 2 * row <= kMaxSmem ? 2 : 1;
-    const size_t smem = nbuf * row;
+    const size_t smem = (size_t)Vp * sizeof(bf16);
+    if (smem > kMaxSmem) return -2;
     static bool set = false;
     if (!set) {
         cudaFuncSetAttribute(ce_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
@@ -196,9 +206,10 @@ int cross_entropy_fwd_bwd(bf16* logits, int rows, int V, int Vp, const int32_t* 
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int grid = rows < sms ? rows : sms;
+    const int per_sm = smem <= kMaxSmem / 2 ? 2 : 1;
+    const int grid = rows < per_sm * sms ? rows : per_sm * sms;
     ce_kernel<<<grid, kCeThreads, smem, s>>>(logits, rows, V, Vp, tokens, row_loss, scale,
-                                             smoothing, nbuf, err);
+                                             smoothing, err);
     return launch_status();
 }
 

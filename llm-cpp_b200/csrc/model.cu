@@ -1197,7 +1197,8 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
     mark(c, 1);
     if (c->logits_only) return 0;  // llmgpu_forward_logits reads them
     // ------------------------------------------------------------------ loss
-    KC(cross_entropy_fwd_bwd(c->logits, BT, V, Vp, c->d_tokens, c->d_row_loss, 1.0f / (float)BT,
+    KC(cross_entropy_fwd_bwd(c->logits, BT, V, Vp, c->d_tokens, c->d_row_loss,
+                             c->loss_scale / (float)BT,
                              c->smoothing, s, c->d_err));
     KC(mean_reduce(c->d_row_loss, BT, c->d_out, s));
     if (c->moe) KC(moe_add_aux(c->moe_aux, L, B, c->d_out, s));
@@ -1349,8 +1350,9 @@ int run_optimizer(Ctx* c, int K) {
     // data parallel: the gradient buckets were all-reduced (averaged) on the comm stream
     // during the last micro-batch's backward
     if (c->world > 1) CK(cudaStreamWaitEvent(s, c->ev_comm, 0));
-    if (K > 1) {
-        // train_step_accum averages the accumulated gradients (src/trainer.cpp:148-150)
+    if (K > 1 || c->loss_scale != 1.0f) {
+        // train_step_accum averages the accumulated gradients (src/trainer.cpp:148-150); a
+        // loss scale is divided out before the non-finite check and the clip (:103-105)
         KC(scale_inplace(c->g, c->n_floats, c->d_hp + 8, s));
     }
     mark(c, 4);
@@ -1375,7 +1377,7 @@ void prepare_step_scalars(Ctx* c, int K) {
     c->h_hp[5] = (float)(1.0 - std::pow((double)c->b1, (double)c->adam_t));
     c->h_hp[6] = (float)(1.0 - std::pow((double)c->b2, (double)c->adam_t));
     c->h_hp[7] = 1.0f;
-    c->h_hp[8] = 1.0f / (float)(K > 0 ? K : 1);
+    c->h_hp[8] = 1.0f / ((float)(K > 0 ? K : 1) * c->loss_scale);
 }
 
 int ctx_sync_check(Ctx* c) {

@@ -170,6 +170,7 @@ struct Ctx {
     int adam_t = 0;
     bool adam_init = false;
     float clip = 1.0f, smoothing = 0.0f;
+    float loss_scale = 1.0f;  // TrainConfig::loss_scale
     bool logits_only = false;  // forward stops after the lm head (llmgpu_forward_logits)
     int accum_k = 1, accum_count = 0;
     int step_count = 0, skipped = 0;

@@ -111,6 +111,13 @@ class Trainer:
         if rc:
             self._err("set_train", rc)
 
+    def set_loss_scale(self, scale):
+        """TrainConfig::loss_scale: loss gradient times `scale`, parameter gradients divided
+        by it before the clip."""
+        rc = self.lib.llmgpu_set_loss_scale(self.h, scale)
+        if rc:
+            self._err("set_loss_scale", rc)
+
     def set_graph(self, enable):
         self.lib.llmgpu_set_graph(self.h, int(enable))
 
@@ -166,6 +173,19 @@ class Trainer:
                                            out.size)
         if n < 0:
             self._err("forward_logits", n)
+        return out
+
+    def forward_logits_all(self, tokens):
+        """tokens int32 [B, T] -> float32 [B, T, V]: the logits of every position
+        (GPT::forward)."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        B, T = t.shape
+        out = np.empty((B, T, self.cfg.vocab_size), np.float32)
+        n = self.lib.llmgpu_forward_logits_all(
+            self.h, t.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), B, T,
+            out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), out.size)
+        if n < 0:
+            self._err("forward_logits_all", n)
         return out
 
     def generate(self, prompt, max_new_tokens, **sampling_args):

@@ -362,6 +362,8 @@ class Model:
         # test evaluate the restatement under exactly the routing another implementation
         # chose (routing is a discrete decision that rounding upstream can flip near ties).
         self.forced_routes = None
+        # TrainConfig::label_smoothing, applied by cross_entropy_backward (src/loss.cpp:26-40)
+        self.smoothing = 0.0
         self._seq = 0
         self._layer = 0
         self._routes = None
@@ -687,7 +689,7 @@ class Model:
         lm = p["wte"].T if cfg.tied else p["lm_head"]
         logits = hid @ lm
         loss = ce_loss(logits, tok) + aux_total
-        dlog = ce_backward(logits, tok)
+        dlog = ce_backward(logits, tok, self.smoothing)
         dlm = hid.T @ dlog
         if cfg.tied:
             G["wte"] += dlm.T

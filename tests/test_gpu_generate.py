@@ -28,10 +28,16 @@ def test_forward_logits_match_oracle(cuda, tied, rms):
     toks = np.random.default_rng(8).integers(0, cfg.vocab, size=(B, T)).astype(np.int32)
     got = tr.forward_logits(toks)
     model = go.Model(cfg, params)
-    want = np.stack([model.forward_backward(list(toks[b]))[2][T - 1] for b in range(B)])
+    every = np.stack([model.logits(list(toks[b])) for b in range(B)])
+    want = every[:, T - 1]
     # bf16 operands and bf16 logits on the device, fp64 in the oracle
     assert got.shape == (B, cfg.vocab)
     assert _rel(got, want) < 2e-2, _rel(got, want)
+    # every position (GPT::forward's [T, V]): llmgpu_forward_logits_all
+    allg = tr.forward_logits_all(toks)
+    assert allg.shape == (B, T, cfg.vocab)
+    assert _rel(allg, every) < 2e-2, _rel(allg, every)
+    np.testing.assert_array_equal(allg[:, T - 1], got)
     # the loss path is untouched: eval_loss after forward_logits is the same as before it
     l0 = tr.eval_loss(toks)
     tr.forward_logits(toks)

@@ -59,13 +59,16 @@ def test_norm_forward_backward(cuda, rms, C):
     assert _rel(ds, want_dx.sum(0)) < 1e-5
 
 
-# rows above the SM count run several rows per CTA through both shared buffers; a row wider
-# than half the shared memory (60032 bf16) takes the single-buffer path
-@pytest.mark.parametrize("V,Vp,rows", [(256, 256, 64), (50257, 50304, 64), (300, 384, 64),
-                                       (50257, 50304, 700), (60001, 60032, 400)])
-def test_cross_entropy(cuda, V, Vp, rows):
-    """loss = lse - logit[tgt]; dlogits = (softmax - onehot) * scale, zero in padding
-    (src/loss.cpp:6-40); targets are the tokens mod V."""
+# rows above the grid run several rows per CTA; a row wider than 110 KB (60032 bf16) runs
+# one CTA per SM instead of two; label smoothing per src/loss.cpp:26-40
+@pytest.mark.parametrize("V,Vp,rows,smoothing", [
+    (256, 256, 64, 0.0), (50257, 50304, 64, 0.0), (300, 384, 64, 0.0),
+    (50257, 50304, 700, 0.0), (60001, 60032, 400, 0.0), (256, 256, 300, 0.1),
+    (50257, 50304, 333, 0.05), (300, 384, 64, 0.2)])
+def test_cross_entropy(cuda, V, Vp, rows, smoothing):
+    """loss = lse - logit[tgt]; dlogits = (softmax - y) * scale with y = 1 - smoothing at the
+    target and smoothing / (V - 1) elsewhere, zero in padding (src/loss.cpp:6-40); targets
+    are the tokens mod V."""
     from llmgpu import ops
     g = torch.Generator().manual_seed(V + rows)
     logits = torch.zeros(rows, Vp)
@@ -74,15 +77,16 @@ def test_cross_entropy(cuda, V, Vp, rows):
     tok = torch.randint(-V, 2 * V, (rows,), generator=g, dtype=torch.int32)
     scale = 1.0 / rows
     d = l16.clone().to(cuda)
-    loss = ops.cross_entropy(d, V, tok.to(cuda), scale)
+    loss = ops.cross_entropy(d, V, tok.to(cuda), scale, smoothing)
     lf = l16.float()[:, :V].double()
     tgt = tok.long() % V
     lse = torch.logsumexp(lf, -1)
     want_loss = lse - lf[torch.arange(rows), tgt]
     assert torch.allclose(loss.cpu().double(), want_loss, rtol=1e-4, atol=1e-4)
     p = torch.softmax(lf, -1)
-    p[torch.arange(rows), tgt] -= 1
-    want = p * scale
+    y = torch.full_like(p, smoothing / (V - 1) if smoothing > 0 else 0.0)
+    y[torch.arange(rows), tgt] = 1.0 - smoothing
+    want = (p - y) * scale
     got = d.cpu().float()
     assert _rel(got[:, :V], want) < 1e-2
     assert torch.count_nonzero(got[:, V:]) == 0

@@ -222,6 +222,54 @@ def test_oracle_train_step(cuda, case):
     tr.close()
 
 
+def test_label_smoothing_step(cuda):
+    """TrainConfig::label_smoothing = 0.1: the loss is unchanged and the gradients follow
+    cross_entropy_backward with smoothed targets (src/loss.cpp:26-40), against the oracle."""
+    cfg = go.Cfg(vocab=512, n_layers=2, n_heads=4, n_embd=128, block_size=96)
+    params = go.init_params(cfg, seed=31)
+    toks = go.uniform_tokens(cfg.vocab, 2 * 96, seed=32).reshape(2, 96)
+    names = [n for n, _ in go.param_specs(cfg)]
+    tr = _trainer(cfg, 2, 96, params)
+    tr.set_train(grad_clip=1.0, label_smoothing=0.1)
+    model = go.Model(cfg, params)
+    model.smoothing = 0.1
+    st = go.AdamWState()
+    losses, raw, gnorm, _ = go.train_step(model, list(toks), st, clip=1.0)
+    loss, gn, skipped = tr.train_step(toks)
+    assert not skipped
+    assert abs(loss - np.mean(losses)) / np.mean(losses) < LOSS_RTOL
+    assert abs(gn - gnorm) / gnorm < GRAD_RTOL
+    _check_grads(tr, raw, names)
+    # the smoothing changes the head gradient visibly: not a no-op
+    plain = go.Model(cfg, params)
+    _, raw0, _, _ = go.train_step(plain, list(toks), go.AdamWState(), clip=1.0)
+    assert _rel(raw[0], raw0[0]) > 2 * GRAD_RTOL
+    tr.close()
+
+
+def test_loss_scale(cuda):
+    """TrainConfig::loss_scale (src/trainer.cpp:91,103-105): a power-of-two scale gives the
+    unscaled step bit for bit (every operation between the loss gradient and the unscaling is
+    linear, and the scale is exact); another scale agrees to rounding."""
+    cfg = go.Cfg(vocab=256, n_layers=2, n_heads=4, n_embd=128, block_size=64)
+    params = go.init_params(cfg, seed=51)
+    toks = go.uniform_tokens(cfg.vocab, 3 * 2 * 64, seed=52).reshape(3, 2, 64)
+    runs = []
+    for scale in (1.0, 1024.0, 3.0):
+        tr = _trainer(cfg, 2, 64, params)
+        tr.set_loss_scale(scale)
+        losses = [tr.train_step(toks[s])[0] for s in range(3)]
+        runs.append((losses, tr.params()))
+        tr.close()
+    (l1, p1), (l2, p2), (l3, p3) = runs
+    assert l1 == l2
+    for a, b in zip(p1, p2):
+        np.testing.assert_array_equal(a, b)
+    assert np.allclose(l1, l3, rtol=1e-6)
+    for a, b in zip(p1, p3):
+        assert _rel(b, a) < 1e-5
+
+
 def test_grad_accum_matches_batch(cuda):
     """train_step_accum with K calls of one sequence == one train_step over K sequences
     (src/trainer.cpp:127-169)."""
