@@ -34,7 +34,6 @@ CFG = dict(vocab_size=50257, n_layers=12, n_heads=12, n_embd=768, block_size=102
 B, T = 8, 1024
 HP = dict(lr=3e-4, b1=0.9, b2=0.95, eps=1e-8, wd=0.1)
 REF_T = 16          # tokens of the bounded CPU-reference sample (one sequence)
-PORT_T = 128        # tokens of the numpy-port CPU sample
 
 
 def algorithmic_flops_per_token(cfg=CFG, T=T):
@@ -46,8 +45,8 @@ def algorithmic_flops_per_token(cfg=CFG, T=T):
     return 6 * n_mm + 6 * L * T * C, n_mm
 
 
-# The other configurations of the path, for `--config` (reported in DESIGN.md; the default
-# line is GPT-2-small): model config, sequences per GPU, sequence length, workload text.
+# The other configurations of the path, for `--config` (the default line is GPT-2-small):
+# model config, sequences per GPU, sequence length, workload text.
 OTHER_CONFIGS = {
     "tiny": (dict(vocab_size=256, n_layers=4, n_heads=4, n_embd=128, block_size=128), 8, 128,
              "tiny char-level GPT (4L, n_embd 128, 4 heads, GELU FFN 512, vocab 256), seq 128, 8 seq/GPU"),
@@ -164,39 +163,25 @@ def ref_binary():
     return p if os.path.exists(p) else None
 
 
-def run_reference_cpu(steps, T_sample):
+def run_reference_cpu(steps, T_sample, model_cfg=CFG, B_sample=1, warmup=0, seed=1234):
     """The unmodified reference train step (oracle/_ref/ref_step, built from the reference
-    sources) on the host cores: `steps` optimizer steps of one sequence of T_sample tokens,
-    reference initialisation, constant LR. Returns (seconds per step list, threads)."""
+    sources) on all host cores: warmup + steps optimizer steps of Trainer::train_step_accum
+    over B_sample sequences of T_sample seeded Zipf(1.1) tokens, reference initialisation,
+    constant LR. Returns (seconds of each timed step, threads)."""
     threads = os.cpu_count() or 1
     with tempfile.TemporaryDirectory() as td:
         env = dict(os.environ, OMP_NUM_THREADS=str(threads))
-        args = [ref_binary(), "-", "-", "1", str(T_sample), td, f"steps={steps}", "timing_only=1",
-                f"vocab={CFG['vocab_size']}", f"layers={CFG['n_layers']}",
-                f"heads={CFG['n_heads']}", f"embd={CFG['n_embd']}", f"block={CFG['block_size']}"]
+        args = [ref_binary(), "-", "-", str(B_sample), str(T_sample), td,
+                f"steps={warmup + steps}", "timing_only=1", f"seed={seed}",
+                f"vocab={model_cfg['vocab_size']}", f"layers={model_cfg['n_layers']}",
+                f"heads={model_cfg['n_heads']}", f"embd={model_cfg['n_embd']}",
+                f"block={model_cfg['block_size']}", f"tied={int(model_cfg.get('weight_tying', True))}"]
         args += [f"{k}={v}" for k, v in HP.items()]
         subprocess.run(args, check=True, env=env, stdout=subprocess.DEVNULL,
                        stderr=subprocess.DEVNULL)
         with open(os.path.join(td, "timing.txt")) as f:
             times = [float(x) for x in f.read().split()]
-    return times, threads
-
-
-def run_port_cpu(T_sample):
-    """numpy restatement of the reference step (oracle/gpt_oracle.py, fp32) on one sequence
-    of T_sample tokens of the same model: forward, backward, clip, AdamW. Returns seconds."""
-    import numpy as np
-    sys.path.insert(0, ROOT)
-    from oracle import gpt_oracle as go
-    cfg = go.Cfg(vocab=CFG["vocab_size"], n_layers=CFG["n_layers"], n_heads=CFG["n_heads"],
-                 n_embd=CFG["n_embd"], block_size=CFG["block_size"])
-    params = go.init_params(cfg, seed=1)
-    toks = zipf_tokens(cfg.vocab, T_sample, 7)
-    model = go.Model(cfg, params, dtype=np.float32)
-    st = go.AdamWState(**HP)
-    t0 = time.perf_counter()
-    go.train_step(model, [toks], st, clip=1.0)
-    return time.perf_counter() - t0
+    return times[warmup:], threads
 
 
 # ------------------------------------------------------------------------------ reference arm
@@ -210,16 +195,19 @@ def reference_arm(args, rank, world):
         line["unavailable"] = "oracle/_ref/ref_step not built (needs the reference sources)"
         print(json.dumps(line))
         return 0
-    # One reference optimizer step over a single 16-token sequence of this model already
-    # takes ~80 s on 8 cores (naive single-threaded lm-head backward over V=50257 and an
-    # AdamW loop over 124M parameters), so the arm times at most 2 steps and no warm-up.
-    steps = max(1, min(args.steps, 2))
-    times, threads = run_reference_cpu(steps, REF_T)
-    per = sum(times) / len(times)
+    # One reference optimizer step over a single 16-token sequence of this model takes about
+    # 30 s on the host cores (a single-threaded lm-head backward over V=50257, three forward
+    # recomputes and an AdamW loop over 124M parameters): one warm-up step, then the median
+    # of at most three timed steps, so that the arm ends within a few minutes.
+    warm = min(args.warmup, 1)
+    steps = max(1, min(args.steps, 3))
+    times, threads = run_reference_cpu(steps, REF_T, warmup=warm)
+    per = statistics.median(times)
     value = REF_T / per
-    sample = (f"{steps} reference optimizer step(s), each over 1 sequence of {REF_T} tokens of "
-              f"the full 12-layer/768/50257 model (warm-up skipped: one step takes {per:.0f} s)")
-    line.update({"value": value, "steps": steps, "warmup": 0, "ms_per_step": per * 1e3,
+    sample = (f"{warm} warm-up + median of {steps} reference optimizer step(s) "
+              f"(Trainer::train_step_accum), each over 1 sequence of {REF_T} Zipf tokens of the "
+              f"full 12-layer/768/50257 model; {per:.1f} s per step")
+    line.update({"value": value, "steps": steps, "warmup": warm, "ms_per_step": per * 1e3,
                  "scaling": "weak", "vs_baseline": None,
                  "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads,
                                   "kind": "reference", "sample": sample},
@@ -241,8 +229,8 @@ def workload_config(n):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0,
@@ -371,15 +359,29 @@ def main():
             "clocks": clocks,
             "loss_last": losses[-1],
         }
-        if world == 1 and not args.no_cpu_baseline and workload is None:
+        if world == 1 and not args.no_cpu_baseline and ref_binary() is not None and \
+                (workload is None or args.config == "tiny"):
             try:
-                secs = run_port_cpu(PORT_T)
-                line["cpu_baseline"] = {
-                    "value": PORT_T / secs, "unit": "tokens/s", "cores": os.cpu_count(),
-                    "kind": "port",
-                    "sample": f"numpy fp32 restatement (oracle/gpt_oracle.py) of one optimizer "
-                              f"step over 1 sequence of {PORT_T} tokens of the same model "
-                              f"({secs:.1f} s)"}
+                if workload is None:
+                    # GPT-2-small: one optimizer step over one 16-token sequence (~30 s)
+                    times, threads = run_reference_cpu(1, REF_T)
+                    secs = times[0]
+                    line["cpu_baseline"] = {
+                        "value": REF_T / secs, "unit": "tokens/s", "cores": threads,
+                        "kind": "reference",
+                        "sample": f"the unmodified reference (oracle/_ref/ref_step) training "
+                                  f"one sequence of {REF_T} tokens of the same model for one "
+                                  f"optimizer step ({secs:.1f} s)"}
+                else:
+                    # the tiny configuration in full: 8 sequences of 128 tokens per step
+                    times, threads = run_reference_cpu(3, T, model_cfg, B_sample=B, warmup=1)
+                    secs = statistics.median(times)
+                    line["cpu_baseline"] = {
+                        "value": B * T / secs, "unit": "tokens/s", "cores": threads,
+                        "kind": "reference",
+                        "sample": f"the unmodified reference (oracle/_ref/ref_step): the whole "
+                                  f"step of {B} x {T} tokens, one warm-up and the median of 3 "
+                                  f"steps ({secs:.2f} s per step)"}
             except Exception as ex:  # the baseline is reported, never fatal
                 line["cpu_baseline"] = {"value": None, "error": str(ex)[:200]}
         print(json.dumps(line), flush=True)

@@ -134,6 +134,25 @@ int64_t llmgpu_forward_logits(llmgpu_ctx* ctx, const int32_t* tokens, int B, int
 int64_t llmgpu_forward_logits_all(llmgpu_ctx* ctx, const int32_t* tokens, int B, int T,
                                   float* logits, int64_t cap);
 
+/* KV-cached decoding on the device, as GPT::generate runs the transformer incrementally
+ * (src/model.cpp:393-474: MultiHeadAttention::forward_incremental src/attention.cpp:104-181
+ * with the KVCache of src/kv_cache.cpp). llmgpu_decode_prefill runs B prompts of T tokens
+ * through the forward, keeps every layer's keys and values, and returns each prompt's
+ * last-position logits (B*V floats); llmgpu_decode_step appends one token per sequence at the
+ * next position and returns that position's logits. All B sequences (B <= 8 and <= the
+ * context's max_batch) share one position, which stops at max_seq. llmgpu_decode_reset
+ * starts B empty sequences (the reference's empty prompt: its first logits are zeros).
+ * The caches hold the weights of the prefill: prefill again after a training step.
+ * Covered: the reference's transformer GPT (GELU FFN, LayerNorm or RMSNorm, tied or untied
+ * head, learned, sinusoidal or RoPE positions); other configurations return
+ * LLMGPU_E_UNSUPPORTED (the reference itself re-runs the whole sequence for Mamba). */
+int llmgpu_decode_reset(llmgpu_ctx* ctx, int B);
+int64_t llmgpu_decode_prefill(llmgpu_ctx* ctx, const int32_t* tokens, int B, int T,
+                              float* logits, int64_t cap);
+int64_t llmgpu_decode_step(llmgpu_ctx* ctx, const int32_t* tokens, int B, float* logits,
+                           int64_t cap);
+int llmgpu_decode_position(const llmgpu_ctx* ctx);
+
 /* Parameters in GPT::parameters() order (src/model.cpp:889-909). */
 int llmgpu_num_params(const llmgpu_ctx* ctx);           /* number of parameter tensors */
 size_t llmgpu_num_parameters(const llmgpu_ctx* ctx);     /* GPT::num_parameters() */
@@ -169,6 +188,15 @@ float llmgpu_last_grad_norm(const llmgpu_ctx* ctx);
 int llmgpu_last_timings(const llmgpu_ctx* ctx, float* ms6);
 /* Kernel launches issued by the last training step (library kernels counted). */
 int llmgpu_last_launches(const llmgpu_ctx* ctx);
+
+/* Data parallel: the longest a host call waits for a collective to complete before it
+ * aborts the communicator and returns LLMGPU_E_NCCL (a peer rank that stopped, a lost
+ * link), in seconds; default 600, or LLMGPU_COMM_TIMEOUT_S from the environment at
+ * llmgpu_create (which bounds the communicator's set-up the same way). After an abort the
+ * context's steps return LLMGPU_E_NCCL; parameters and checkpoints stay readable. The
+ * reference has no collectives (its data parallelism is mean_reduce_grads in one process,
+ * src/trainer.cpp:171-182); this bound replaces the wait a blocking collective would do. */
+int llmgpu_set_comm_timeout(llmgpu_ctx* ctx, double seconds);
 
 /* Executes steps as a captured CUDA graph when enable != 0 (default 1). */
 int llmgpu_set_graph(llmgpu_ctx* ctx, int enable);

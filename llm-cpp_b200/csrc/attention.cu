@@ -649,7 +649,7 @@ int rope_qk_inplace(bf16* qkv, int B, int T, int H, int hd, const float2* rope, 
 
 int attention_backward(const bf16* qkv, const bf16* out, const bf16* dout, const float* lse,
                        float* dvec, bf16* dqkv, int B, int T, int H, int hd, const float2* rope,
-                       cudaStream_t s, int* err, void* ds_work) {
+                       cudaStream_t s, int* err, void* ds_work, const float2* rope_back) {
     const float scale = 1.0f / sqrtf((float)hd);
     const long long n = (long long)B * T * H;
     const int rows_blocks = (int)(((long long)B * T + 7) / 8);
@@ -669,7 +669,8 @@ int attention_backward(const bf16* qkv, const bf16* out, const bf16* dout, const
         const int rc = launch_status();
         if (rc) return rc;
         if (!ds_work) return -5;  // the tcgen05 kernels need the dS scratch
-        return attention_backward_tc(qkv, dout, lse, dvec, dqkv, B, T, H, hd, ds_work, err, s);
+        return attention_backward_tc(qkv, dout, lse, dvec, dqkv, B, T, H, hd, ds_work, err, s,
+                                     rope_back);
     }
     dim3 grid((T + BLK - 1) / BLK, H, B);
     if (hd == 64) {
@@ -694,6 +695,11 @@ int attention_backward(const bf16* qkv, const bf16* out, const bf16* dout, const
                                                                 scale, rope);
     } else {
         return -1;
+    }
+    if (rope_back) {
+        const int rc = launch_status();
+        if (rc) return rc;
+        return rope_qk_inplace(dqkv, B, T, H, hd, rope_back, 1, s);
     }
     return launch_status();
 }

@@ -355,6 +355,23 @@ __device__ __forceinline__ void store_row64_bf16(bf16* dst, const uint32_t (&r)[
                            pack_bf16x2(__uint_as_float(r[8 * i + 6]) * mul, __uint_as_float(r[8 * i + 7]) * mul));
 }
 
+// dQ / dK of a row whose queries / keys were rotated by RoPE before the attention: the
+// gradient of the unrotated vector is the inverse rotation, pairs (2j, 2j+1) by the
+// (cos, sin) cs[j] of the row's position (r0: columns 0-31, r1: 32-63).
+__device__ __forceinline__ void rope_back_row64(uint32_t (&r0)[32], uint32_t (&r1)[32],
+                                                const float2* __restrict__ cs) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float2 a = cs[i], b = cs[16 + i];
+        const float x0 = __uint_as_float(r0[2 * i]), x1 = __uint_as_float(r0[2 * i + 1]);
+        r0[2 * i] = __float_as_uint(x0 * a.x + x1 * a.y);
+        r0[2 * i + 1] = __float_as_uint(x1 * a.x - x0 * a.y);
+        const float y0 = __uint_as_float(r1[2 * i]), y1 = __uint_as_float(r1[2 * i + 1]);
+        r1[2 * i] = __float_as_uint(y0 * b.x + y1 * b.y);
+        r1[2 * i + 1] = __float_as_uint(y1 * b.x - y0 * b.y);
+    }
+}
+
 // Work item `it` of a backward kernel: tile index counted from the longest end (the tile
 // with the most partner tiles first), head and sequence.
 struct BwdItem {
@@ -422,7 +439,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                             const __grid_constant__ CUtensorMap tm_lse,
                             const __grid_constant__ CUtensorMap tm_d,
                             const __grid_constant__ CUtensorMap tm_ds, bf16* __restrict__ dqkv,
-                            int B, int T, int H, float scale, int* __restrict__ err) {
+                            int B, int T, int H, float scale, const float2* __restrict__ rope,
+                            int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_u32 = smem_u32(smem_raw);
     uint8_t* sm = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
@@ -648,6 +666,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             tc_fence_before();
             mbar_arrive(k.acc_free);
             if (key < T) {
+                if (half == 1 && rope) rope_back_row64(r0, r1, rope + (long long)key * (kHD / 2));
                 bf16* dst = dqkv + ((long long)w.b * T + key) * 3LL * C + (half == 0 ? 2 * C : C) +
                             w.h * kHD;
                 store_row64_bf16(dst, r0, half == 0 ? 1.f : scale);
@@ -679,7 +698,8 @@ constexpr size_t kDqSmemBytes = 1024 + kDqBarOff + 256;
 __global__ void __launch_bounds__(kDqThreads, 1)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv,
                           const __grid_constant__ CUtensorMap tm_ds, bf16* __restrict__ dqkv,
-                          int B, int T, int H, float scale, int* __restrict__ err) {
+                          int B, int T, int H, float scale, const float2* __restrict__ rope,
+                          int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_u32 = smem_u32(smem_raw);
     uint8_t* sm = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
@@ -791,6 +811,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
             mbar_arrive(&acc_empty[acc]);
             const int q = qt * kRows + lq * 32 + lane;
             if (q < T) {
+                if (rope) rope_back_row64(r0, r1, rope + (long long)q * (kHD / 2));
                 bf16* dst = dqkv + ((long long)w.b * T + q) * 3LL * C + w.h * kHD;
                 store_row64_bf16(dst, r0, scale);
                 store_row64_bf16(dst + 32, r1, scale);
@@ -878,7 +899,7 @@ size_t attention_ds_bytes(int B, int T, int H) {
 
 int attention_backward_tc(const bf16* qkv, const bf16* dout, const float* lse, const float* dvec,
                           bf16* dqkv, int B, int T, int H, int hd, void* ds_work, int* err,
-                          cudaStream_t s) {
+                          cudaStream_t s, const float2* rope_back) {
     if (hd != kHD || B <= 0 || T <= 0 || H <= 0 || (T % 4) != 0 || !ds_work) return -1;
     const int C = H * hd;
     CUtensorMap tq, tdo, tl, td, tds_st, tds_ld;
@@ -933,11 +954,12 @@ int attention_backward_tc(const bf16* qkv, const bf16* dout, const float* lse, c
     const int items = ((T + kRows - 1) / kRows) * H * B;
     const int grid = items < sms ? items : sms;
     attn_bwd_dkdv_tc_kernel<<<grid, kBwdThreads, kDkdvSmemBytes, s>>>(tq, tdo, tl, td, tds_st, dqkv,
-                                                                      B, T, H, scale, err);
+                                                                      B, T, H, scale, rope_back,
+                                                                      err);
     int rc = launch_status();
     if (rc) return rc;
     attn_bwd_dq_tc_kernel<<<grid, kDqThreads, kDqSmemBytes, s>>>(tq, tds_ld, dqkv, B, T, H, scale,
-                                                                 err);
+                                                                 rope_back, err);
     return launch_status();
 }
 

@@ -60,6 +60,10 @@ int validate_bt(Ctx* c, int B, int T) {
 }
 
 int enqueue_step(Ctx* c, int B, int T, int accumulate, bool do_step, int K) {
+    if (c->comm_failed) {
+        c->err = "the communicator was aborted after an earlier collective failure";
+        return LLMGPU_E_NCCL;
+    }
     c->plan_cursor = 0;
     c->plan2_cursor = 0;
     c->prof_n = 0;
@@ -107,6 +111,10 @@ void capture_step(Ctx* c, int B, int T, int accumulate, bool do_step, int K) {
 
 // Runs one micro-batch (+ optimizer when `do_step`), eagerly or through the step graph.
 int run_step(Ctx* c, int B, int T, int accumulate, bool do_step, int K) {
+    if (c->comm_failed) {  // a captured step would replay collectives of the aborted communicator
+        c->err = "the communicator was aborted after an earlier collective failure";
+        return LLMGPU_E_NCCL;
+    }
     cudaMemsetAsync(c->d_out + 1, 0, sizeof(float) * 4, c->stream);
     if (do_step) prepare_step_scalars(c, K);
     const bool graphable = c->use_graph && !c->profile;
@@ -373,6 +381,65 @@ int64_t llmgpu_forward_logits_all(llmgpu_ctx* h, const int32_t* tokens, int B, i
     return forward_rows(h, tokens, B, T, logits, cap, true);
 }
 
+static int decode_check(llmgpu_ctx* h, int B) {
+    if (check_ctx(h)) return LLMGPU_E_ARG;
+    Ctx* c = h->c;
+    std::string why;
+    if (int rc = decode_supported(c, &why)) {
+        c->err = why;
+        return rc;
+    }
+    if (B < 1 || B > c->max_b || B > 8) {
+        c->err = "decode: B must be in [1, min(max_batch, 8)]";
+        return LLMGPU_E_ARG;
+    }
+    return decode_alloc(c);
+}
+
+int llmgpu_decode_reset(llmgpu_ctx* h, int B) {
+    if (int rc = decode_check(h, B)) return rc;
+    h->c->dec.B = B;
+    h->c->dec.pos = 0;
+    return 0;
+}
+
+int64_t llmgpu_decode_prefill(llmgpu_ctx* h, const int32_t* tokens, int B, int T, float* logits,
+                              int64_t cap) {
+    if (int rc = decode_check(h, B)) return rc;
+    Ctx* c = h->c;
+    const int64_t n = forward_rows(h, tokens, B, T, logits, cap, false);
+    if (n < 0) return n;
+    if (int rc = decode_fill(c, B, T)) return rc;
+    if (int rc = ctx_sync_check(c)) return rc;
+    return n;
+}
+
+int64_t llmgpu_decode_step(llmgpu_ctx* h, const int32_t* tokens, int B, float* logits,
+                           int64_t cap) {
+    if (check_ctx(h) || !tokens || !logits) return LLMGPU_E_ARG;
+    Ctx* c = h->c;
+    if (!c->dec.ready || B != c->dec.B) {
+        c->err = "decode: call llmgpu_decode_prefill or llmgpu_decode_reset with this B first";
+        return LLMGPU_E_ARG;
+    }
+    if (cap < (int64_t)B * c->V) return LLMGPU_E_ARG;
+    std::memcpy(c->h_tokens, tokens, sizeof(int32_t) * B);
+    if (cudaMemcpyAsync(c->dec.tokens, c->h_tokens, sizeof(int32_t) * B, cudaMemcpyHostToDevice,
+                        c->stream) != cudaSuccess)
+        return LLMGPU_E_CUDA;
+    if (int rc = decode_step(c, B)) return rc;
+    if (cudaMemcpy2DAsync(logits, (size_t)c->V * 4, c->dec.logits, (size_t)c->Vp * 4,
+                          (size_t)c->V * 4, (size_t)B, cudaMemcpyDeviceToHost, c->stream) !=
+        cudaSuccess)
+        return LLMGPU_E_CUDA;
+    if (int rc = ctx_sync_check(c)) return rc;
+    return (int64_t)B * c->V;
+}
+
+int llmgpu_decode_position(const llmgpu_ctx* h) {
+    return check_ctx(h) ? LLMGPU_E_ARG : (h->c->dec.ready ? h->c->dec.pos : 0);
+}
+
 int llmgpu_num_params(const llmgpu_ctx* h) {
     if (check_ctx(h)) return LLMGPU_E_ARG;
     return (int)h->c->params.size();
@@ -431,7 +498,7 @@ int llmgpu_set_param(llmgpu_ctx* h, int idx, const float* data, int64_t n) {
     if (copy_sync(c, c->p + p.offset, data, n * sizeof(float), cudaMemcpyHostToDevice))
         return LLMGPU_E_CUDA;
     refresh_shadows(c);
-    return cudaStreamSynchronize(c->stream) == cudaSuccess ? 0 : LLMGPU_E_CUDA;
+    return wait_stream(c, c->stream);
 }
 
 int llmgpu_save_binary(llmgpu_ctx* h, const char* path) {
@@ -501,6 +568,12 @@ int llmgpu_last_timings(const llmgpu_ctx* h, float* ms6) {
 }
 
 int llmgpu_last_launches(const llmgpu_ctx* h) { return check_ctx(h) ? LLMGPU_E_ARG : h->c->launches; }
+
+int llmgpu_set_comm_timeout(llmgpu_ctx* h, double seconds) {
+    if (check_ctx(h) || !(seconds > 0.0)) return LLMGPU_E_ARG;
+    h->c->comm_timeout_s = seconds;
+    return 0;
+}
 
 int llmgpu_set_graph(llmgpu_ctx* h, int enable) {
     if (check_ctx(h)) return LLMGPU_E_ARG;

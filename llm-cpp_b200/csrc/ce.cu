@@ -45,11 +45,12 @@ __device__ __forceinline__ float2 lse_combine(float2 a, float2 b) {
 }
 
 // Persistent over rows, two CTAs per SM: CTA b takes rows b, b + grid, ... A row (Vp bf16)
-// arrives by one bulk copy into the CTA's shared buffer, is overwritten in place by its
-// gradient and leaves by one bulk store, so the threads only do arithmetic; while one CTA of
-// an SM waits for its row, the other computes. Each row takes two passes over shared memory:
-// an online max / sum of exponentials (a thread rescales its running sum when its maximum
-// grows; the per-thread pairs meet in one block reduction), then the gradient.
+// sits in the CTA's shared buffer in two halves, each with its own bulk copy in and out: a
+// half is refilled with the next row as soon as its gradient store has read it, so the copies
+// overlap the arithmetic of the other half, and while one CTA of an SM waits the other
+// computes. Each row takes two passes over shared memory: an online max / sum of
+// exponentials (a thread rescales its running sum when its maximum grows; the per-thread
+// pairs meet in one block reduction), then the gradient, written in place.
 __global__ void __launch_bounds__(kCeThreads, 2) ce_kernel(bf16* __restrict__ logits, int rows,
                                                             int V, int Vp,
                                                             const int32_t* __restrict__ tokens,
@@ -58,12 +59,14 @@ __global__ void __launch_bounds__(kCeThreads, 2) ce_kernel(bf16* __restrict__ lo
     extern __shared__ __align__(128) uint8_t ce_smem[];  // Vp bf16 (Vp % 8 == 0)
     __shared__ float2 red[kCeThreads / 32 + 1];
     __shared__ float s_tgt;
-    __shared__ __align__(8) uint64_t bar;
-    const uint32_t row_bytes = (uint32_t)Vp * 2u;
+    __shared__ __align__(8) uint64_t bar[2];
     const int n8 = Vp >> 3;
+    const int h8 = n8 >> 1;  // uint4 groups in the first half
+    const uint32_t bytes0 = (uint32_t)h8 * 16u, bytes1 = (uint32_t)(n8 - h8) * 16u;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) {
-        mbar_init(&bar, 1);
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
         fence_barrier_init();
     }
     __syncthreads();
@@ -76,34 +79,44 @@ __global__ void __launch_bounds__(kCeThreads, 2) ce_kernel(bf16* __restrict__ lo
     // groups of 8 columns: [0, nfull) all valid, then at most one partly valid group, then
     // padding up to Vp
     const int nfull = V >> 3, nval = (V + 7) >> 3;
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bar[0], bytes0);
+        bulk_load_g2s(ce_smem, logits + (long long)row * Vp, bytes0, &bar[0]);
+    }
     for (int it = 0; row < rows; ++it, row += gridDim.x) {
         if (threadIdx.x == 0) {
-            // the buffer is refilled once the previous row's gradient store has read it
+            // the second half is refilled once the previous row's second-half store has read it
             if (it > 0) bulk_wait_group_read<0>();
-            mbar_arrive_expect_tx(&bar, row_bytes);
-            bulk_load_g2s(ce_smem, logits + (long long)row * Vp, row_bytes, &bar);
+            mbar_arrive_expect_tx(&bar[1], bytes1);
+            bulk_load_g2s(ce_smem + bytes0, logits + (long long)row * Vp + 8 * h8, bytes1, &bar[1]);
         }
         int tgt = tokens[row] % V;
         if (tgt < 0) tgt += V;
-        mbar_wait_bounded(&bar, (uint32_t)(it & 1), err, kDevTimeoutFull);
         float2 ms = make_float2(-FLT_MAX, 0.f);  // running (max, sum of 2^((x - max) log2e))
-        for (int i = threadIdx.x; i < nfull; i += blockDim.x) {
-            const uint4 u = srow[i];
-            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-            float m8 = fmaxf(fmaxf(fmaxf(bf16_lo(u.x), bf16_hi(u.x)), fmaxf(bf16_lo(u.y), bf16_hi(u.y))),
-                             fmaxf(fmaxf(bf16_lo(u.z), bf16_hi(u.z)), fmaxf(bf16_lo(u.w), bf16_hi(u.w))));
-            if (m8 > ms.x) {
-                ms.y = ms.y == 0.f ? 0.f : ms.y * ex2_approx((ms.x - m8) * kLog2e);
-                ms.x = m8;
-            }
-            const float ml = ms.x * kLog2e;
-            float acc = 0.f;
+        auto pass1 = [&](int i0, int i1) {
+            for (int i = i0 + (int)threadIdx.x; i < i1; i += blockDim.x) {
+                const uint4 u = srow[i];
+                const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+                const float m8 =
+                    fmaxf(fmaxf(fmaxf(bf16_lo(u.x), bf16_hi(u.x)), fmaxf(bf16_lo(u.y), bf16_hi(u.y))),
+                          fmaxf(fmaxf(bf16_lo(u.z), bf16_hi(u.z)), fmaxf(bf16_lo(u.w), bf16_hi(u.w))));
+                if (m8 > ms.x) {
+                    ms.y = ms.y == 0.f ? 0.f : ms.y * ex2_approx((ms.x - m8) * kLog2e);
+                    ms.x = m8;
+                }
+                const float ml = ms.x * kLog2e;
+                float acc = 0.f;
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-                acc += ex2_approx(fmaf(bf16_lo(w[k]), kLog2e, -ml)) +
-                       ex2_approx(fmaf(bf16_hi(w[k]), kLog2e, -ml));
-            ms.y += acc;
-        }
+                for (int k = 0; k < 4; ++k)
+                    acc += ex2_approx(fmaf(bf16_lo(w[k]), kLog2e, -ml)) +
+                           ex2_approx(fmaf(bf16_hi(w[k]), kLog2e, -ml));
+                ms.y += acc;
+            }
+        };
+        mbar_wait_bounded(&bar[0], (uint32_t)(it & 1), err, kDevTimeoutFull);
+        pass1(0, min(h8, nfull));
+        mbar_wait_bounded(&bar[1], (uint32_t)(it & 1), err, kDevTimeoutFull);
+        pass1(min(h8, nfull), nfull);
         if (threadIdx.x == 0) {
             if (nval > nfull) {
                 const bf16* t = reinterpret_cast<const bf16*>(srow + nfull);
@@ -134,45 +147,62 @@ __global__ void __launch_bounds__(kCeThreads, 2) ce_kernel(bf16* __restrict__ lo
         // dlogits = (softmax - y) * scale; y = off everywhere but `on` at the target, and the
         // padding columns get 0
         const float offs = off * scale;
-        for (int i = threadIdx.x; i < n8; i += blockDim.x) {
-            const uint4 u = srow[i];
-            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-            uint32_t o[4];
-            if (i < nfull) {
+        auto pass2 = [&](int i0, int i1) {
+            for (int i = i0 + (int)threadIdx.x; i < i1; i += blockDim.x) {
+                const uint4 u = srow[i];
+                const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+                uint32_t o[4];
+                if (i < nfull) {
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    o[k] = pack_bf16x2(ex2_approx(fmaf(bf16_lo(w[k]), kLog2e, -lsel)) * scale - offs,
-                                       ex2_approx(fmaf(bf16_hi(w[k]), kLog2e, -lsel)) * scale - offs);
-            } else {
+                    for (int k = 0; k < 4; ++k)
+                        o[k] = pack_bf16x2(ex2_approx(fmaf(bf16_lo(w[k]), kLog2e, -lsel)) * scale - offs,
+                                           ex2_approx(fmaf(bf16_hi(w[k]), kLog2e, -lsel)) * scale - offs);
+                } else {
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const int c = i * 8 + 2 * k;
-                    const float a =
-                        c < V ? ex2_approx(fmaf(bf16_lo(w[k]), kLog2e, -lsel)) * scale - offs : 0.f;
-                    const float bb =
-                        c + 1 < V ? ex2_approx(fmaf(bf16_hi(w[k]), kLog2e, -lsel)) * scale - offs
-                                  : 0.f;
-                    o[k] = pack_bf16x2(a, bb);
+                    for (int k = 0; k < 4; ++k) {
+                        const int c = i * 8 + 2 * k;
+                        const float a =
+                            c < V ? ex2_approx(fmaf(bf16_lo(w[k]), kLog2e, -lsel)) * scale - offs : 0.f;
+                        const float bb =
+                            c + 1 < V ? ex2_approx(fmaf(bf16_hi(w[k]), kLog2e, -lsel)) * scale - offs
+                                      : 0.f;
+                        o[k] = pack_bf16x2(a, bb);
+                    }
                 }
-            }
-            if (i == (tgt >> 3)) {  // the target column takes `on` instead of `off`
+                if (i == (tgt >> 3)) {  // the target column takes `on` instead of `off`
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    if (k != ((tgt & 7) >> 1)) continue;
-                    const float x = (tgt & 1) ? bf16_hi(w[k]) : bf16_lo(w[k]);
-                    const float gt = (ex2_approx(fmaf(x, kLog2e, -lsel)) - on) * scale;
-                    const float lo = (tgt & 1) ? bf16_lo(o[k]) : gt;
-                    const float hi = (tgt & 1) ? gt : bf16_hi(o[k]);
-                    o[k] = pack_bf16x2(lo, hi);
+                    for (int k = 0; k < 4; ++k) {
+                        if (k != ((tgt & 7) >> 1)) continue;
+                        const float x = (tgt & 1) ? bf16_hi(w[k]) : bf16_lo(w[k]);
+                        const float gt = (ex2_approx(fmaf(x, kLog2e, -lsel)) - on) * scale;
+                        const float lo = (tgt & 1) ? bf16_lo(o[k]) : gt;
+                        const float hi = (tgt & 1) ? gt : bf16_hi(o[k]);
+                        o[k] = pack_bf16x2(lo, hi);
+                    }
                 }
+                srow[i] = make_uint4(o[0], o[1], o[2], o[3]);
             }
-            srow[i] = make_uint4(o[0], o[1], o[2], o[3]);
-        }
+        };
+        pass2(0, h8);
         fence_proxy_async_smem();  // this thread's gradient writes before the bulk store
         __syncthreads();
         if (threadIdx.x == 0) {
-            bulk_store_s2g(logits + (long long)row * Vp, srow, row_bytes);
+            bulk_store_s2g(logits + (long long)row * Vp, srow, bytes0);
             bulk_commit_group();
+        }
+        pass2(h8, n8);
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            bulk_store_s2g(logits + (long long)row * Vp + 8 * h8, ce_smem + bytes0, bytes1);
+            bulk_commit_group();
+            // the first half is refilled with the next row once its store has read it
+            const int next = row + gridDim.x;
+            if (next < rows) {
+                bulk_wait_group_read<1>();
+                mbar_arrive_expect_tx(&bar[0], bytes0);
+                bulk_load_g2s(ce_smem, logits + (long long)next * Vp, bytes0, &bar[0]);
+            }
         }
     }
     if (threadIdx.x == 0) bulk_wait_group_all();

@@ -387,6 +387,21 @@ __device__ __forceinline__ void epilogue_input_tile(const GemmArgs& a, const CUt
     }
 }
 
+// Rotary embedding of one lane's 32 accumulator columns [col0, col0 + 32) of row m (a chunk
+// never straddles a head: rope_hd and col0 are multiples of 32).
+__device__ __forceinline__ void rope_chunk(const GemmArgs& a, int m, int col0, uint32_t (&r)[32]) {
+    if (col0 >= a.rope_cols || m >= a.M) return;
+    const int half = a.rope_hd >> 1;
+    const float2* cs = a.rope + (long long)(m % a.rope_T) * half + ((col0 % a.rope_hd) >> 1);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float2 w = cs[i];
+        const float x0 = __uint_as_float(r[2 * i]), x1 = __uint_as_float(r[2 * i + 1]);
+        r[2 * i] = __float_as_uint(x0 * w.x - x1 * w.y);
+        r[2 * i + 1] = __float_as_uint(x0 * w.y + x1 * w.x);
+    }
+}
+
 // One accumulator tile of one warp: rows [row0, row0+32), columns [n0, n0+NCOLS), TMEM
 // columns from tbase. `empty`: the tile had no k-blocks (writes zeros).
 template <int NCOLS>
@@ -415,6 +430,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
             } else {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) ra[j] = rb[j] = 0u;
+            }
+            if (a.rope) {
+                rope_chunk(a, row0 + lane, n0 + c * 32, ra);
+                rope_chunk(a, row0 + lane, n0 + (c + 1) * 32, rb);
             }
             uint8_t* box = w.stage + w.slot * kEpiSlotBytes;
             if (lane == 0) bulk_wait_group_read<1>();  // this box's previous store has read it
@@ -1357,6 +1376,10 @@ int gemm_make_plan(GemmPlan* plan, const void* A, long long lda, int a_mn_major,
     a.tma_epi = 0;
     if (std::getenv("LLMGPU_GEMM_DIRECT_EPILOGUE") == nullptr) a.tma_epi = plan_tma_epilogue(plan, a) ? 1 : 0;
     if (!a.tma_epi) plan->tmO = plan->tmX = CUtensorMap{};
+    // the rotary epilogue runs on the bf16 TMA store path only
+    if (a.rope && (a.epi != kEpiStoreBF16 || !a.tma_epi || a.rope_T <= 0 || a.rope_hd <= 0 ||
+                   (a.rope_hd % 32) != 0 || (a.rope_cols % 32) != 0))
+        return -9;
     plan->args = a;
     int rc;
     if (!a_mn_major)

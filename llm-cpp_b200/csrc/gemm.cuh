@@ -58,6 +58,12 @@ struct GemmArgs {
     int grp_mode;
     long long b_grp_rows;
     long long out_grp_stride;
+    // kEpiStoreBF16 through TMA: rotary embedding of the output columns [0, rope_cols) before
+    // the bf16 rounding. Pairs (2j, 2j+1) of each rope_hd-wide head of row m rotate by the
+    // (cos, sin) rope[(m % rope_T) * rope_hd / 2 + j] (the queries and keys of a QKV
+    // projection, RoPE applied per head). rope_hd and rope_cols are multiples of 32.
+    const float2* rope;
+    int rope_T, rope_hd, rope_cols;
 };
 
 enum GemmGroupMode : int { kGroupNone = 0, kGroupRows = 1, kGroupK = 2 };

@@ -85,13 +85,16 @@ int rope_qk_inplace(bf16* qkv, int B, int T, int H, int hd, const float2* rope, 
 // src/attention.cpp:183-363.
 // head_dim 64 without a fused rope and T % 4 == 0 runs on the tcgen05 kernels, which need
 // ds_work: attention_ds_bytes(B, T, H) bytes of scratch for the dS tiles.
+// rope_back (nullable): q and k in qkv were already rotated by this table ([T][hd/2] (cos, sin));
+// dq and dk are rotated back before they are written.
 int attention_backward(const bf16* qkv, const bf16* out, const bf16* dout, const float* lse,
                        float* dvec, bf16* dqkv, int B, int T, int H, int hd, const float2* rope,
-                       cudaStream_t s, int* err = nullptr, void* ds_work = nullptr);
+                       cudaStream_t s, int* err = nullptr, void* ds_work = nullptr,
+                       const float2* rope_back = nullptr);
 size_t attention_ds_bytes(int B, int T, int H);
 int attention_backward_tc(const bf16* qkv, const bf16* dout, const float* lse, const float* dvec,
                           bf16* dqkv, int B, int T, int H, int hd, void* ds_work, int* err,
-                          cudaStream_t s);
+                          cudaStream_t s, const float2* rope_back = nullptr);
 
 // ----------------------------------------------------------------- SwiGLU FFN
 // gated[r, j] = silu(h13[r, j]) * h13[r, F + j]   (src/transformer.cpp:22-30)

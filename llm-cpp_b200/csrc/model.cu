@@ -12,8 +12,10 @@
 // fp32 accumulation, and the weight gradients of a step are formed once for the whole batch.
 #include <nccl.h>
 
+#include <chrono>
 #include <cmath>
 #include <cstdio>
+#include <thread>
 #include <cstring>
 #include <fcntl.h>
 #include <fstream>
@@ -50,6 +52,41 @@ namespace {
     } while (0)
 
 inline int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+double now_s() {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch())
+        .count();
+}
+
+// Ends the communicator for good (its kernels in flight return) and marks the context.
+void abort_comm(Ctx* c) {
+    if (c->nccl) ncclCommAbort(reinterpret_cast<ncclComm_t>(c->nccl));
+    c->nccl = nullptr;
+    c->comm_failed = true;
+}
+
+// The communicator is non-blocking: a call may return ncclInProgress, and the next call may
+// only be made once ncclCommGetAsyncError reports success. Polls up to the context's timeout.
+int nccl_settle(Ctx* c, ncclResult_t r, const char* what, double timeout_s) {
+    const double deadline = now_s() + timeout_s;
+    ncclComm_t comm = reinterpret_cast<ncclComm_t>(c->nccl);
+    while (r == ncclInProgress) {
+        if (now_s() > deadline) {
+            c->err = std::string(what) + ": not finished after " + std::to_string(timeout_s) +
+                     " s (a peer rank did not take part); communicator aborted";
+            abort_comm(c);
+            return LLMGPU_E_NCCL;
+        }
+        std::this_thread::yield();
+        if (ncclCommGetAsyncError(comm, &r) != ncclSuccess) r = ncclSystemError;
+    }
+    if (r != ncclSuccess) {
+        c->err = std::string(what) + ": " + ncclGetErrorString(r) + "; communicator aborted";
+        abort_comm(c);
+        return LLMGPU_E_NCCL;
+    }
+    return 0;
+}
 
 void add_param(Ctx* c, const std::string& name, std::vector<int64_t> shape) {
     Param p;
@@ -407,12 +444,11 @@ int dalloc(Ctx* c, T** p, size_t n) {
 int copy_sync(Ctx* c, void* dst, const void* src, size_t bytes, cudaMemcpyKind kind) {
     if (bytes == 0) return 0;
     cudaError_t e = cudaMemcpyAsync(dst, src, bytes, kind, c->stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) {
         c->err = std::string("copy: ") + cudaGetErrorString(e);
         return LLMGPU_E_CUDA;
     }
-    return 0;
+    return wait_stream(c, c->stream);
 }
 
 // ---------------------------------------------------------------------------- shadows
@@ -802,14 +838,19 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
             return fail(c, "stream creation failed");
         ncclUniqueId id;
         std::memcpy(&id, uid, sizeof(id));
-        ncclComm_t comm;
+        ncclComm_t comm = nullptr;
         // NCCL's own CTA count by default; LLMGPU_NCCL_MAX_CTAS caps it (fewer CTAs leave more
-        // SMs to the backward the buckets overlap, but slow the last, unoverlapped bucket)
+        // SMs to the backward the buckets overlap, but slow the last, unoverlapped bucket).
+        // Non-blocking, so that no host call waits on a peer without a bound.
         ncclConfig_t ncfg = NCCL_CONFIG_INITIALIZER;
+        ncfg.blocking = 0;
         if (const char* e = std::getenv("LLMGPU_NCCL_MAX_CTAS")) ncfg.maxCTAs = std::atoi(e);
+        if (const char* e = std::getenv("LLMGPU_COMM_TIMEOUT_S")) c->comm_timeout_s = std::atof(e);
         ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &ncfg);
-        if (r != ncclSuccess) return fail(c, std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
         c->nccl = comm;
+        if (!comm && r != ncclSuccess)
+            return fail(c, std::string("ncclCommInitRankConfig: ") + ncclGetErrorString(r));
+        if (nccl_settle(c, r, "ncclCommInitRankConfig", c->comm_timeout_s)) return fail(c, "");
     }
     if (cudaDeviceSynchronize() != cudaSuccess) return fail(c, "device error during setup");
     return c;
@@ -817,9 +858,18 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
 
 void ctx_destroy(Ctx* c) {
     if (!c) return;
+    // a collective that never completes (a peer gone) would block the device sync below
+    if (c->nccl && c->stream && wait_stream(c, c->stream) == 0 && c->comm)
+        wait_stream(c, c->comm);
     cudaDeviceSynchronize();
+    decode_free(c);
     if (c->graph) cudaGraphExecDestroy(c->graph);
-    if (c->nccl) ncclCommDestroy(reinterpret_cast<ncclComm_t>(c->nccl));
+    if (c->nccl) {
+        ncclComm_t comm = reinterpret_cast<ncclComm_t>(c->nccl);
+        if (nccl_settle(c, ncclCommFinalize(comm), "ncclCommFinalize", c->comm_timeout_s) == 0)
+            ncclCommDestroy(comm);
+        c->nccl = nullptr;
+    }
     auto F = [](void* p) {
         if (p) cudaFree(p);
     };
@@ -1101,12 +1151,13 @@ int allreduce_bucket(Ctx* c, int64_t begin, int64_t end) {
     if (end <= begin) return 0;
     CK(cudaEventRecord(c->ev_grad, c->stream));
     CK(cudaStreamWaitEvent(c->comm, c->ev_grad, 0));
-    ncclResult_t r = ncclAllReduce(c->g + begin, c->g + begin, (size_t)(end - begin), ncclFloat,
-                                   ncclAvg, reinterpret_cast<ncclComm_t>(c->nccl), c->comm);
-    if (r != ncclSuccess) {
-        c->err = std::string("ncclAllReduce: ") + ncclGetErrorString(r);
+    if (!c->nccl) {
+        c->err = "the communicator was aborted after an earlier failure";
         return LLMGPU_E_NCCL;
     }
+    ncclResult_t r = ncclAllReduce(c->g + begin, c->g + begin, (size_t)(end - begin), ncclFloat,
+                                   ncclAvg, reinterpret_cast<ncclComm_t>(c->nccl), c->comm);
+    if (int rc = nccl_settle(c, r, "ncclAllReduce", c->comm_timeout_s)) return rc;
     c->launches++;
     return 0;
 }
@@ -1149,11 +1200,18 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
             continue;
         }
         KC(norm_forward(a.x, pp(b.ln1g), pp(b.ln1b), a.ln1, a.mean1, a.rstd1, BT, C, rms, s));
-        int rc = gemm(c, a.ln1, C, 0, c->wqkv16[l], 3 * C, 1, BT, 3 * C, C,
-                      epi_args(kEpiStoreBF16, a.qkv, 3 * C));
+        // RoPE on Q/K at head_dim 64: rotated in the QKV projection's epilogue (before the bf16
+        // rounding), so the tcgen05 attention takes q and k as they are
+        GemmArgs qa = epi_args(kEpiStoreBF16, a.qkv, 3 * C);
+        if (c->rope && hd == 64) {
+            qa.rope = c->rope;
+            qa.rope_T = T;
+            qa.rope_hd = hd;
+            qa.rope_cols = 2 * C;
+        }
+        int rc = gemm(c, a.ln1, C, 0, c->wqkv16[l], 3 * C, 1, BT, 3 * C, C, qa);
         if (rc) return rc;
-        if (c->rope && hd == 64) {  // rotate q, k in place; the tcgen05 kernel takes them as is
-            KC(rope_qk_inplace(a.qkv, B, T, H, hd, c->rope, 0, s));
+        if (c->rope && hd == 64) {
             KC(attention_forward(a.qkv, a.att, a.lse, B, T, H, hd, nullptr, s, c->d_err));
         } else {
             KC(attention_forward(a.qkv, a.att, a.lse, B, T, H, hd, c->rope, s, c->d_err));
@@ -1301,10 +1359,9 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
                             GemmCall{c->dy16, C, 0, c->wo16[l], C, 0, BT, C, C,
                                      epi_args(kEpiStoreBF16, c->datt, C), 1})))
             return rc;
-        if (c->rope && hd == 64) {  // q, k were rotated in place: rotate dq, dk back
+        if (c->rope && hd == 64) {  // q, k were rotated by the projection: dq, dk rotate back
             KC(attention_backward(a.qkv, a.att, c->datt, a.lse, c->dvec, c->dqkv, B, T, H, hd,
-                                  nullptr, s, c->d_err, c->attn_ds));
-            KC(rope_qk_inplace(c->dqkv, B, T, H, hd, c->rope, 1, s));
+                                  nullptr, s, c->d_err, c->attn_ds, c->rope));
         } else {
             KC(attention_backward(a.qkv, a.att, c->datt, a.lse, c->dvec, c->dqkv, B, T, H, hd,
                                   c->rope, s, c->d_err, c->attn_ds));
@@ -1380,9 +1437,45 @@ void prepare_step_scalars(Ctx* c, int K) {
     c->h_hp[8] = 1.0f / ((float)(K > 0 ? K : 1) * c->loss_scale);
 }
 
+int wait_stream(Ctx* c, cudaStream_t s) {
+    if (!c->nccl) {
+        const cudaError_t e = cudaStreamSynchronize(s);
+        if (e == cudaSuccess) return 0;
+        c->err = std::string("stream: ") + cudaGetErrorString(e);
+        return LLMGPU_E_CUDA;
+    }
+    ncclComm_t comm = reinterpret_cast<ncclComm_t>(c->nccl);
+    const double deadline = now_s() + c->comm_timeout_s;
+    for (;;) {
+        const cudaError_t e = cudaStreamQuery(s);
+        if (e == cudaSuccess) return 0;
+        if (e != cudaErrorNotReady) {
+            c->err = std::string("stream: ") + cudaGetErrorString(e);
+            return LLMGPU_E_CUDA;
+        }
+        ncclResult_t ar = ncclSuccess;
+        ncclCommGetAsyncError(comm, &ar);
+        const bool late = now_s() > deadline;
+        if ((ar != ncclSuccess && ar != ncclInProgress) || late) {
+            c->err = late ? "a collective did not complete within " +
+                                std::to_string(c->comm_timeout_s) +
+                                " s (a peer rank stopped taking part); communicator aborted"
+                          : std::string("collective failed: ") + ncclGetErrorString(ar) +
+                                "; communicator aborted";
+            abort_comm(c);
+            // the aborted communicator's kernels return; wait for the stream a bounded time
+            const double drain = now_s() + 30.0;
+            while (cudaStreamQuery(s) == cudaErrorNotReady && now_s() < drain)
+                std::this_thread::sleep_for(std::chrono::microseconds(200));
+            return LLMGPU_E_NCCL;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
 int ctx_sync_check(Ctx* c) {
     CK(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
-    CK(cudaStreamSynchronize(c->stream));
+    if (int rc = wait_stream(c, c->stream)) return rc;
     if (*c->h_err != 0) {
         c->err = "device-side wait timed out (code " + std::to_string(*c->h_err) + ")";
         return LLMGPU_E_DEVICE;
@@ -1572,8 +1665,7 @@ int load_binary(Ctx* c, const char* path) {
     if (copy_sync(c, c->p, host.data(), host.size() * sizeof(float), cudaMemcpyHostToDevice))
         return LLMGPU_E_CUDA;
     refresh_shadows(c);
-    CK(cudaStreamSynchronize(c->stream));
-    return 0;
+    return wait_stream(c, c->stream);
 }
 
 // Adam state persistence (src/optimizer.cpp:129-173): magic "ADAM", lr, b1, b2, eps, t,

@@ -77,6 +77,17 @@ struct MoeAct {
     float* yg = nullptr;     // [cap, C]  expert outputs
 };
 
+// KV-cached decoding (decode.cu): per layer K and V caches [max_b][max_t][C] bf16 and the
+// one-row activations of a decode step, allocated at the first decode call.
+struct DecodeState {
+    bool ready = false;
+    int max_b = 0, B = 0, pos = 0;
+    std::vector<bf16*> kc, vc;
+    float *x = nullptr, *y = nullptr, *stat = nullptr, *logits = nullptr;
+    bf16 *ln = nullptr, *qkv = nullptr, *att = nullptr, *act = nullptr;
+    int32_t* tokens = nullptr;
+};
+
 struct Ctx {
     llmgpu_config cfg{};
     int rank = 0, world = 1;
@@ -91,7 +102,12 @@ struct Ctx {
     cudaEvent_t ev_grad = nullptr, ev_comm = nullptr;
     std::vector<std::pair<int64_t, int64_t>> buckets;  // [begin, end) floats; index l = block l
     cudaEvent_t ev[6] = {};
-    void* nccl = nullptr;  // ncclComm_t
+    void* nccl = nullptr;  // ncclComm_t, created non-blocking
+    // host-side bound on any wait for a collective (a peer that stopped, a lost link): past
+    // it the communicator is aborted and the call returns LLMGPU_E_NCCL; the context is then
+    // unusable for steps (comm_failed)
+    double comm_timeout_s = 600.0;
+    bool comm_failed = false;
 
     std::vector<Param> params;
     std::vector<BlockIdx> blocks;
@@ -206,6 +222,8 @@ struct Ctx {
     int graph_launches = 0;
     int graph_seen = 0;  // consecutive eager runs with the current key (capture on the 2nd)
 
+    DecodeState dec;
+
     std::string err;
 };
 
@@ -220,6 +238,9 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
 // optimizer: (wait for the bucket all-reduces) -> scale by 1/K -> norm/clip -> AdamW
 int run_optimizer(Ctx* c, int K);
 int ctx_sync_check(Ctx* c);
+// Waits for stream `s` to drain. With a communicator it polls the communicator's
+// asynchronous error state and aborts it at the first error or past comm_timeout_s.
+int wait_stream(Ctx* c, cudaStream_t s);
 void prepare_step_scalars(Ctx* c, int K);
 int save_binary(Ctx* c, const char* path);
 int load_binary(Ctx* c, const char* path);
@@ -227,5 +248,11 @@ int save_adam(Ctx* c, const char* path);
 int load_adam(Ctx* c, const char* path);
 void refresh_shadows(Ctx* c);
 int copy_sync(Ctx* c, void* dst, const void* src, size_t bytes, cudaMemcpyKind kind);
+// KV-cached decoding (decode.cu)
+int decode_supported(const Ctx* c, std::string* why);
+int decode_alloc(Ctx* c);
+void decode_free(Ctx* c);
+int decode_fill(Ctx* c, int B, int T);
+int decode_step(Ctx* c, int B);
 
 }  // namespace llmgpu

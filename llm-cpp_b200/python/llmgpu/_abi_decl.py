@@ -31,6 +31,7 @@ SIGS = {
     "llmgpu_set_lr": ([c_vp, c_float], c_int),
     "llmgpu_set_train": ([c_vp, c_float, c_int, c_float], c_int),
     "llmgpu_set_loss_scale": ([c_vp, c_float], c_int),
+    "llmgpu_set_comm_timeout": ([c_vp, ctypes.c_double], c_int),
     "llmgpu_train_step": ([c_vp, P_i32, c_int, c_int, P_f32, P_f32], c_int),
     "llmgpu_train_step_accum": ([c_vp, P_i32, c_int, c_int, P_f32, P_int], c_int),
     "llmgpu_train_step_device": ([c_vp, c_vp, c_int, c_int, P_f32, P_f32], c_int),
@@ -38,6 +39,10 @@ SIGS = {
     "llmgpu_forward_logits": ([c_vp, P_i32, c_int, c_int, P_f32, ctypes.c_int64], ctypes.c_int64),
     "llmgpu_forward_logits_all": ([c_vp, P_i32, c_int, c_int, P_f32, ctypes.c_int64],
                                   ctypes.c_int64),
+    "llmgpu_decode_reset": ([c_vp, c_int], c_int),
+    "llmgpu_decode_prefill": ([c_vp, P_i32, c_int, c_int, P_f32, ctypes.c_int64], ctypes.c_int64),
+    "llmgpu_decode_step": ([c_vp, P_i32, c_int, P_f32, ctypes.c_int64], ctypes.c_int64),
+    "llmgpu_decode_position": ([c_vp], c_int),
     "llmgpu_num_params": ([c_vp], c_int),
     "llmgpu_num_parameters": ([c_vp], c_size_t),
     "llmgpu_param_info": ([c_vp, c_int, c_char_p, c_int, P_i64], c_int),

@@ -118,6 +118,13 @@ class Trainer:
         if rc:
             self._err("set_loss_scale", rc)
 
+    def set_comm_timeout(self, seconds):
+        """Bound (seconds) on any wait for a collective; past it the communicator is aborted
+        and the step raises LlmgpuError (LLMGPU_E_NCCL)."""
+        rc = self.lib.llmgpu_set_comm_timeout(self.h, float(seconds))
+        if rc:
+            self._err("set_comm_timeout", rc)
+
     def set_graph(self, enable):
         self.lib.llmgpu_set_graph(self.h, int(enable))
 
@@ -188,13 +195,58 @@ class Trainer:
             self._err("forward_logits_all", n)
         return out
 
-    def generate(self, prompt, max_new_tokens, **sampling_args):
-        """GPT::generate (src/model.cpp:393-474) on the device forward: greedy by default;
-        the reference's temperature / top-k / top-p / repetition-penalty options and its
-        one std::mt19937(42) stream, as in llmgpu.sampling.generate. Each token re-runs the
-        forward over the last max_seq tokens. Returns prompt + generated ids."""
+    # ------------------------------------------------------------------ KV-cached decoding
+    def decode_reset(self, B):
+        """Starts B empty sequences in the device KV caches."""
+        rc = self.lib.llmgpu_decode_reset(self.h, int(B))
+        if rc:
+            self._err("decode_reset", rc)
+
+    def decode_prefill(self, tokens):
+        """tokens int32 [B, T] -> float32 [B, V]: runs the prompts, keeps their keys and
+        values, returns each prompt's last-position logits."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        B, T = t.shape
+        out = np.empty((B, self.cfg.vocab_size), np.float32)
+        n = self.lib.llmgpu_decode_prefill(self.h, t.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                           B, T, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                           out.size)
+        if n < 0:
+            self._err("decode_prefill", n)
+        return out
+
+    def decode_step(self, tokens):
+        """tokens int32 [B] (one per sequence) -> float32 [B, V]: the logits of the position
+        the tokens were appended at."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32).ravel()
+        out = np.empty((t.size, self.cfg.vocab_size), np.float32)
+        n = self.lib.llmgpu_decode_step(self.h, t.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                        t.size, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                        out.size)
+        if n < 0:
+            self._err("decode_step", n)
+        return out
+
+    def decode_position(self):
+        return self.lib.llmgpu_decode_position(self.h)
+
+    def decode_supported(self):
+        c = self.cfg
+        return not (c.use_mamba or c.moe_experts or c.ffn_swiglu or c.rope_qk)
+
+    def generate(self, prompt, max_new_tokens, use_cache=True, **sampling_args):
+        """GPT::generate (src/model.cpp:393-474) on the device: greedy by default; the
+        reference's temperature / top-k / top-p / repetition-penalty options and its one
+        std::mt19937(42) stream, as in llmgpu.sampling.generate. With use_cache (and a
+        configuration the KV-cached decode covers) each new token runs one decode step against
+        the cached keys and values, as the reference's incremental forward does; otherwise, and
+        once the window slides past max_seq, the forward re-runs over the last max_seq tokens.
+        Returns prompt + generated ids."""
         from . import sampling
-        return sampling.generate(self.forward_logits, prompt, max_new_tokens, self.max_seq,
+        fwd = self.forward_logits
+        if use_cache and self.decode_supported():
+            fwd = _CachedForward(self)
+        return sampling.generate(fwd, prompt, max_new_tokens, self.max_seq,
                                  self.cfg.vocab_size, **sampling_args)
 
     # ------------------------------------------------------------------ parameters
@@ -329,3 +381,23 @@ class Trainer:
         if n < 0:
             self._err("moe_routing", n)
         return out
+
+
+class _CachedForward:
+    """Logits of the last position of a token window, through the KV caches: a window that
+    extends the previous one by one token is one decode step, any other window a prefill."""
+
+    def __init__(self, tr):
+        self.tr = tr
+        self.seen = None
+
+    def __call__(self, ctx):
+        toks = [int(t) for t in np.asarray(ctx)[0]]
+        if (self.seen is not None and len(toks) == len(self.seen) + 1
+                and toks[:-1] == self.seen):
+            out = self.tr.decode_step(np.asarray(toks[-1:], np.int32))
+        else:
+            out = self.tr.decode_prefill(np.asarray([toks], np.int32))
+        self.seen = toks
+        return out
+

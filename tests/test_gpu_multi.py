@@ -90,3 +90,85 @@ def test_two_gpu_data_parallel_matches_single_gpu():
         rel = np.linalg.norm(a.astype(np.float64) - b) / max(np.linalg.norm(b), 1e-30)
         assert rel < 1e-3, (one.param_info(i)[0], rel)
     one.close()
+
+
+def _stall_worker(rank, world, port, q, go_on):
+    """Two steps together; then rank 1 stops taking part (it stays alive, runs nothing) while
+    rank 0 (a) finds it missing through PeerWatch and (b) tries one more step, which must end
+    with the communicator timeout's error instead of waiting for good."""
+    import datetime
+    import sys
+    import time
+    import torch.distributed as dist
+    root = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+    sys.path.insert(0, os.path.join(root, "llm-cpp_b200", "python"))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      LLMGPU_COMM_TIMEOUT_S="60")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    from llmgpu.dist import PeerLost, PeerWatch
+    from llmgpu.trainer import LlmgpuError, Trainer, make_config, unique_id
+    obj = [unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    tr = Trainer(make_config(**CFG), B, T, rank=rank, world=world, uid=obj[0])
+    tr.set_adamw()
+    tr.set_train(grad_clip=1.0)
+    tr.set_comm_timeout(3.0)
+    watch = PeerWatch(dist.distributed_c10d._get_default_store(), rank, world, timeout_s=2.0,
+                      prefix="t/step")
+    toks = _tokens(world)
+    for s in range(2):
+        watch.arrive(s)
+        tr.train_step(toks[s, rank * B:(rank + 1) * B])
+    res = {}
+    if rank == 0:
+        t0 = time.time()
+        try:
+            watch.arrive(2)
+            res["watch"] = "arrived"
+        except PeerLost as e:
+            res["watch"] = ("lost", e.ranks, time.time() - t0)
+        t0 = time.time()
+        try:
+            tr.train_step(toks[0, :B])
+            res["step"] = "completed"
+        except LlmgpuError as e:
+            res["step"] = ("error", str(e), time.time() - t0)
+        try:  # the aborted context refuses steps at once and still reads out
+            tr.train_step(toks[0, :B])
+            res["again"] = "completed"
+        except LlmgpuError as e:
+            res["again"] = ("error", str(e))
+        res["param_ok"] = bool(np.isfinite(tr.get_param(0)).all())
+        q.put((rank, res))
+        go_on.set()
+    else:
+        go_on.wait(timeout=240)  # stopped: nothing of this rank is in flight meanwhile
+        q.put((rank, res))
+    tr.close()
+
+
+def test_stalled_peer_ends_in_an_error_not_a_hang():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import multiprocessing as mp
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    go_on = ctx.Event()
+    port = _port()
+    procs = [ctx.Process(target=_stall_worker, args=(r, world, port, q, go_on))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    r0 = res[0]
+    assert r0["watch"][0] == "lost" and r0["watch"][1] == [1], r0
+    assert r0["step"][0] == "error" and "communicator aborted" in r0["step"][1], r0
+    assert r0["step"][2] < 60.0, r0
+    assert r0["again"][0] == "error" and "aborted" in r0["again"][1], r0
+    assert r0["param_ok"]
