@@ -62,6 +62,13 @@ int llmgpu_op_gemm_splitk_noalloc(const void* A, long long lda, int a_mn_major, 
 /* x[b*T+t,:] = wte[tok mod V,:] + wpe[t,:] in fp32 (src/model.cpp:149-157). */
 int llmgpu_op_embed(const int32_t* tokens, const float* wte, const float* wpe, float* x, int B,
                     int T, int C, int V, void* stream);
+/* Embedding backward (src/model.cpp:314-322): wte_grad[tok mod V] += dx[row] for every token
+ * row (the rows of a repeated id summed in a fixed order, so the result is deterministic) and
+ * wpe_grad[t] (+)= sum_b dx[b*T + t] (accumulate_wpe). B*T <= 16384. `work` must hold
+ * llmgpu_op_embed_bwd_work(B, T, C) bytes. */
+long long llmgpu_op_embed_bwd_work(int B, int T, int C);
+int llmgpu_op_embed_bwd(const int32_t* tokens, const float* dx, float* wte_grad, float* wpe_grad,
+                        int B, int T, int C, int V, int accumulate_wpe, void* work, void* stream);
 /* LayerNorm (rms=0, src/tensor.cpp:388-413) / RMSNorm (rms=1, :604-623): fp32 rows in,
  * bf16 rows out, per-row mean and rstd saved. */
 int llmgpu_op_norm_fwd(const float* x, const float* gamma, const float* beta, void* y_bf16,

@@ -16,6 +16,7 @@ __global__ void __launch_bounds__(kNormThreads) grad_norm_kernel(const float* __
                                                                  long long n,
                                                                  double* __restrict__ partial,
                                                                  int* __restrict__ nonfinite) {
+    pdl_enter();
     __shared__ double red[kNormThreads / 32];
     float acc = 0.f;
     int bad = 0;
@@ -49,6 +50,7 @@ __global__ void __launch_bounds__(kNormThreads) grad_norm_kernel(const float* __
 __global__ void grad_norm_final_kernel(const double* __restrict__ partial, int nblocks,
                                        const int* __restrict__ nonfinite, float clip,
                                        float* __restrict__ scal) {
+    pdl_enter();
     __shared__ double red[32];
     double s = 0;
     for (int i = threadIdx.x; i < nblocks; i += blockDim.x) s += partial[i];
@@ -98,6 +100,7 @@ __global__ void __launch_bounds__(256) adamw_kernel(const AdamParam* __restrict_
                                                     float* __restrict__ m, float* __restrict__ v,
                                                     const float* __restrict__ scal,
                                                     const float* __restrict__ hp) {
+    pdl_enter();
     if (scal[3] != 0.0f) return;  // non-finite gradient: the step is skipped
     const AdamChunk ch = chunks[blockIdx.x];
     const AdamParam pr = params[ch.param];
@@ -158,6 +161,7 @@ __global__ void __launch_bounds__(256) adamw_kernel(const AdamParam* __restrict_
 __global__ void __launch_bounds__(256) shadow_kernel(const AdamParam* __restrict__ params,
                                                      const AdamChunk* __restrict__ chunks,
                                                      const float* __restrict__ p) {
+    pdl_enter();
     const AdamChunk ch = chunks[blockIdx.x];
     const AdamParam pr = params[ch.param];
     if (!pr.shadow) return;
@@ -174,6 +178,7 @@ __global__ void __launch_bounds__(256) shadow_kernel(const AdamParam* __restrict
 }
 
 __global__ void scale_kernel(float* x, long long n, const float* scale) {
+    pdl_enter();
     const float s = *scale;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x)
@@ -188,31 +193,31 @@ int grad_norm_partials(const float* g, long long n, double* partial, int* nonfin
                        cudaStream_t s) {
     if (nblocks != kNormBlocks) return -1;
     cudaMemsetAsync(nonfinite, 0, sizeof(int), s);
-    grad_norm_kernel<<<kNormBlocks, kNormThreads, 0, s>>>(g, n, partial, nonfinite);
+    launch_kernel(grad_norm_kernel, kNormBlocks, kNormThreads, 0, s, g, n, partial, nonfinite);
     return launch_status();
 }
 
 int grad_norm_finalize(const double* partial, int nblocks, const int* nonfinite, float clip,
                        float* scal, cudaStream_t s) {
-    grad_norm_final_kernel<<<1, 1024, 0, s>>>(partial, nblocks, nonfinite, clip, scal);
+    launch_kernel(grad_norm_final_kernel, 1, 1024, 0, s, partial, nblocks, nonfinite, clip, scal);
     return launch_status();
 }
 
 int adamw_update(const AdamParam* params, const AdamChunk* chunks, int nchunks, float* p,
                  const float* g, float* m, float* v, const float* scal, const float* hp,
                  cudaStream_t s) {
-    adamw_kernel<<<nchunks, 256, 0, s>>>(params, chunks, p, g, m, v, scal, hp);
+    launch_kernel(adamw_kernel, nchunks, 256, 0, s, params, chunks, p, g, m, v, scal, hp);
     return launch_status();
 }
 
 int write_shadows(const AdamParam* params, const AdamChunk* chunks, int nchunks, const float* p,
                   cudaStream_t s) {
-    shadow_kernel<<<nchunks, 256, 0, s>>>(params, chunks, p);
+    launch_kernel(shadow_kernel, nchunks, 256, 0, s, params, chunks, p);
     return launch_status();
 }
 
 int scale_inplace(float* x, long long n, const float* scale, cudaStream_t s) {
-    scale_kernel<<<592, 256, 0, s>>>(x, n, scale);
+    launch_kernel(scale_kernel, 592, 256, 0, s, x, n, scale);
     return launch_status();
 }
 

@@ -337,6 +337,7 @@ __global__ void __launch_bounds__(256) attn_dvec_rows_kernel(const bf16* __restr
                                                              const bf16* __restrict__ dout,
                                                              float* __restrict__ dvec, int B,
                                                              int T, int H) {
+    pdl_enter();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long row = blockIdx.x * 8LL + warp;  // b*T + t
     if (row >= (long long)B * T) return;
@@ -655,13 +656,13 @@ int attention_backward(const bf16* qkv, const bf16* out, const bf16* dout, const
     const int rows_blocks = (int)(((long long)B * T + 7) / 8);
     if (hd == 64 && H * 8 <= 128) {
         if (H * 8 <= 32)
-            attn_dvec_rows_kernel<8, 1><<<rows_blocks, 256, 0, s>>>(out, dout, dvec, B, T, H);
+            launch_kernel(attn_dvec_rows_kernel<8, 1>, rows_blocks, 256, 0, s, out, dout, dvec, B, T, H);
         else if (H * 8 <= 64)
-            attn_dvec_rows_kernel<8, 2><<<rows_blocks, 256, 0, s>>>(out, dout, dvec, B, T, H);
+            launch_kernel(attn_dvec_rows_kernel<8, 2>, rows_blocks, 256, 0, s, out, dout, dvec, B, T, H);
         else if (H * 8 <= 96)
-            attn_dvec_rows_kernel<8, 3><<<rows_blocks, 256, 0, s>>>(out, dout, dvec, B, T, H);
+            launch_kernel(attn_dvec_rows_kernel<8, 3>, rows_blocks, 256, 0, s, out, dout, dvec, B, T, H);
         else
-            attn_dvec_rows_kernel<8, 4><<<rows_blocks, 256, 0, s>>>(out, dout, dvec, B, T, H);
+            launch_kernel(attn_dvec_rows_kernel<8, 4>, rows_blocks, 256, 0, s, out, dout, dvec, B, T, H);
     } else {
         attn_dvec_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(out, dout, dvec, B, T, H, hd);
     }

@@ -103,6 +103,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
+    pdl_enter();  // first global-memory access follows
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -458,6 +459,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tmem_alloc(k.tmem_slot, kBwdTmem);
         tmem_relinquish();
     }
+    pdl_enter();  // first global-memory access follows
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -729,6 +731,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
         tmem_alloc(tmem_slot, 2 * kHD);
         tmem_relinquish();
     }
+    pdl_enter();  // first global-memory access follows
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -870,9 +873,8 @@ int attention_forward_tc(const CUtensorMap& tm, bf16* out, float* lse, int B, in
     });
     if (attr) return attr;
     const dim3 grid((T + kRows - 1) / kRows, H, B);
-    attn_fwd_tc_kernel<<<grid, kThreads, kSmemBytes, s>>>(tm, out, lse, T, H,
-                                                         1.4426950408889634f / sqrtf((float)hd), err);
-    return launch_status();
+    return launch_kernel(attn_fwd_tc_kernel, grid, kThreads, kSmemBytes, s, tm, out, lse, T, H,
+                         1.4426950408889634f / sqrtf((float)hd), err);
 }
 
 namespace {
@@ -953,14 +955,11 @@ int attention_backward_tc(const bf16* qkv, const bf16* dout, const float* lse, c
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int items = ((T + kRows - 1) / kRows) * H * B;
     const int grid = items < sms ? items : sms;
-    attn_bwd_dkdv_tc_kernel<<<grid, kBwdThreads, kDkdvSmemBytes, s>>>(tq, tdo, tl, td, tds_st, dqkv,
-                                                                      B, T, H, scale, rope_back,
-                                                                      err);
-    int rc = launch_status();
+    int rc = launch_kernel(attn_bwd_dkdv_tc_kernel, grid, kBwdThreads, kDkdvSmemBytes, s, tq, tdo,
+                           tl, td, tds_st, dqkv, B, T, H, scale, rope_back, err);
     if (rc) return rc;
-    attn_bwd_dq_tc_kernel<<<grid, kDqThreads, kDqSmemBytes, s>>>(tq, tds_ld, dqkv, B, T, H, scale,
-                                                                 rope_back, err);
-    return launch_status();
+    return launch_kernel(attn_bwd_dq_tc_kernel, grid, kDqThreads, kDqSmemBytes, s, tq, tds_ld, dqkv,
+                         B, T, H, scale, rope_back, err);
 }
 
 }  // namespace llmgpu

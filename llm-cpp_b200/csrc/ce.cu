@@ -56,6 +56,7 @@ __global__ void __launch_bounds__(kCeThreads, 2) ce_kernel(bf16* __restrict__ lo
                                                             const int32_t* __restrict__ tokens,
                                                             float* __restrict__ row_loss,
                                                             float scale, float smoothing, int* err) {
+    pdl_enter();
     extern __shared__ __align__(128) uint8_t ce_smem[];  // Vp bf16 (Vp % 8 == 0)
     __shared__ float2 red[kCeThreads / 32 + 1];
     __shared__ float s_tgt;
@@ -209,6 +210,7 @@ __global__ void __launch_bounds__(kCeThreads, 2) ce_kernel(bf16* __restrict__ lo
 }
 
 __global__ void mean_kernel(const float* __restrict__ v, int n, float* out) {
+    pdl_enter();
     __shared__ float red[33];
     float s = 0.f;
     for (int i = threadIdx.x; i < n; i += blockDim.x) s += v[i];
@@ -238,13 +240,13 @@ int cross_entropy_fwd_bwd(bf16* logits, int rows, int V, int Vp, const int32_t* 
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int per_sm = smem <= kMaxSmem / 2 ? 2 : 1;
     const int grid = rows < per_sm * sms ? rows : per_sm * sms;
-    ce_kernel<<<grid, kCeThreads, smem, s>>>(logits, rows, V, Vp, tokens, row_loss, scale,
+    launch_kernel(ce_kernel, grid, kCeThreads, smem, s, logits, rows, V, Vp, tokens, row_loss, scale,
                                              smoothing, err);
     return launch_status();
 }
 
 int mean_reduce(const float* v, int n, float* out, cudaStream_t s) {
-    mean_kernel<<<1, 1024, 0, s>>>(v, n, out);
+    launch_kernel(mean_kernel, 1, 1024, 0, s, v, n, out);
     return launch_status();
 }
 

@@ -10,6 +10,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace llmgpu {
 
 // Error codes written by kernels into the context's device error word.
@@ -462,6 +464,58 @@ __device__ __forceinline__ float gelu_tanh_grad(float v) {
     float sech2 = 1.0f - th * th;
     float inner = k * (1.0f + 3.0f * 0.044715f * v * v);
     return 0.5f * (1.0f + th) + 0.5f * v * sech2 * inner;
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// The GEMM kernels are launched with programmatic stream serialisation (when enabled): their
+// CTAs may be scheduled while the previous kernel of the stream is still running, set up
+// their barriers, TMEM and descriptors, and wait in pdl_wait() before the first access to
+// global memory until that kernel has completed and its writes are visible. Every kernel of
+// the step calls pdl_enter() first: the trigger in it lets a following GEMM start launching.
+// The other kernels keep plain stream order: their blocks launched early (while the kernel
+// before them finished) made the step slower. In a launch without the attribute both
+// instructions do nothing.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_enter() {
+    pdl_wait();
+    pdl_trigger();
+}
+
+// Process-wide switch for the GEMM launches: on unless the environment sets LLMGPU_PDL=0.
+bool pdl_enabled();
+
+// kernel<<<grid, block, smem, s>>>(args...) returning 0 or -(1000 + cudaError_t).
+template <typename... Exp, typename... Act>
+inline int launch_kernel(void (*kernel)(Exp...), dim3 grid, dim3 block, size_t smem,
+                         cudaStream_t s, Act&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Act>(args)...);
+    return e == cudaSuccess ? 0 : -(1000 + (int)e);
+}
+
+// The same with the programmatic-serialisation attribute when pdl_enabled() (GEMM kernels).
+template <typename... Exp, typename... Act>
+inline int launch_kernel_pdl(void (*kernel)(Exp...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t s, Act&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Act>(args)...);
+    return e == cudaSuccess ? 0 : -(1000 + (int)e);
 }
 
 }  // namespace llmgpu

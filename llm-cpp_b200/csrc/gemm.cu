@@ -583,6 +583,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
         tmem_relinquish();
     }
+    pdl_enter();  // barriers, TMEM and descriptors are set up while the previous kernel ends
     __shared__ int s_grp[kMaxGemmGroups + 1];
     if (args.grp_mode != kGroupNone)
         for (int i = threadIdx.x; i <= args.groups; i += blockDim.x) s_grp[i] = args.grp[i];
@@ -888,6 +889,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
         tmem_relinquish_pair();
     }
+    pdl_enter();  // barriers, TMEM and descriptors are set up while the previous kernel ends
     // row-group table of a grouped product (single products only)
     __shared__ int s_grp[kMaxGemmGroups + 1];
     if (NG == 1 && P.args[0].grp_mode != kGroupNone)
@@ -1060,6 +1062,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N,
                                      float* __restrict__ out, long long ldo, int col_group,
                                      long long group_stride, int accumulate) {
+    pdl_enter();
     const long long total4 = (long long)M * N / 4;
     const long long plane = (long long)M * N;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total4;
@@ -1094,6 +1097,7 @@ __global__ void splitk_reduce_scalar_kernel(const float* __restrict__ part, int 
                                             int N, float* __restrict__ out, long long ldo,
                                             int col_group, long long group_stride,
                                             int accumulate) {
+    pdl_enter();
     const long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     const long long plane = (long long)M * N;
     if (e >= plane) return;
@@ -1207,6 +1211,18 @@ bool plan_tma_epilogue(GemmPlan* plan, const GemmArgs& a) {
     return true;
 }
 
+}  // namespace
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("LLMGPU_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+namespace {
+
 template <int BN>
 int launch_bn(const GemmPlan& p, cudaStream_t stream) {
     static bool attr_set = false;
@@ -1216,9 +1232,8 @@ int launch_bn(const GemmPlan& p, cudaStream_t stream) {
             return -10;
         attr_set = true;
     }
-    gemm_bf16_tc_kernel<BN><<<p.grid, kGemmThreads, GemmCfg<BN>::SMEM, stream>>>(
-        p.tmA, p.tmB, p.tmO, p.tmX, p.args);
-    return launch_status();
+    return launch_kernel_pdl(gemm_bf16_tc_kernel<BN>, p.grid, kGemmThreads, GemmCfg<BN>::SMEM,
+                             stream, p.tmA, p.tmB, p.tmO, p.tmX, p.args);
 }
 
 int pair_set_attr() {
@@ -1272,16 +1287,17 @@ int launch_pair_params(const PairParams<NG>& P, int grid, cudaStream_t stream) {
     cfg.blockDim = dim3(kPairThreads, 1, 1);
     cfg.dynamicSmemBytes = PairCfg::SMEM;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, gemm_bf16_pair_kernel<NG>, P) != cudaSuccess)
-        return launch_status();
-    return launch_status();
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_bf16_pair_kernel<NG>, P);
+    return e == cudaSuccess ? 0 : -(1000 + (int)e);
 }
 
 int launch_pair(const GemmPlan& p, cudaStream_t stream) {
@@ -1518,15 +1534,14 @@ int gemm_splitk_reduce(const float* partial, int splits, int M, int N, float* ou
     if ((N % 4) != 0 || (ldo % 4) != 0 || (col_group != N && (col_group % 4) != 0) ||
         (group_stride % 4) != 0) {
         const long long total = (long long)M * N;
-        splitk_reduce_scalar_kernel<<<(int)((total + 255) / 256), 256, 0, stream>>>(
-            partial, splits, M, N, out, ldo, col_group, group_stride, accumulate);
+        launch_kernel(splitk_reduce_scalar_kernel, (int)((total + 255) / 256), 256, 0, stream, partial, splits, M, N, out, ldo, col_group, group_stride, accumulate);
         return launch_status();
     }
     long long total4 = (long long)M * N / 4;
     int threads = 256;
     long long blocks = (total4 + threads - 1) / threads;
     if (blocks > 148 * 16) blocks = 148 * 16;
-    splitk_reduce_kernel<<<(int)blocks, threads, 0, stream>>>(partial, splits, M, N, out, ldo,
+    launch_kernel(splitk_reduce_kernel, (int)blocks, threads, 0, stream, partial, splits, M, N, out, ldo,
                                                              col_group, group_stride, accumulate);
     return launch_status();
 }

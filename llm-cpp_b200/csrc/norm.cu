@@ -22,6 +22,7 @@ __global__ void __launch_bounds__(256) norm_fwd_kernel(const float* __restrict__
                                                        bf16* __restrict__ y, float* __restrict__ mean,
                                                        float* __restrict__ rstd, int rows, int C,
                                                        int rms) {
+    pdl_enter();
     const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -91,6 +92,7 @@ __global__ void __launch_bounds__(256) norm_bwd_kernel(
     const float* __restrict__ mean, const float* __restrict__ rstd,
     const float* __restrict__ resid_in, float* __restrict__ dx_f32, bf16* __restrict__ dx_bf16,
     float* __restrict__ partial, int rows, int C, int rms) {
+    pdl_enter();
     extern __shared__ float red[];  // [8][3][C]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nwarps_total = gridDim.x * 8;
@@ -190,6 +192,7 @@ __global__ void __launch_bounds__(1024) sum_parts_kernel(const float* __restrict
                                                          long long plane_off, int C, float* out0,
                                                          float* out1, float* out2,
                                                          int accumulate) {
+    pdl_enter();
     __shared__ float red[32][33];
     const int plane = blockIdx.y;
     float* out = plane == 0 ? out0 : (plane == 1 ? out1 : out2);
@@ -225,6 +228,7 @@ constexpr int kColsumGroups = 256;
 
 __global__ void colsum_stage1(const bf16* __restrict__ a, long long lda, int rows, int C,
                               float* __restrict__ work) {
+    pdl_enter();
     // blockIdx.x: 2048-column tile (256 threads x 8 columns); blockIdx.y: row group
     const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
     if (c0 >= C) return;
@@ -276,11 +280,11 @@ int norm_forward(const float* x, const float* gamma, const float* beta, bf16* y,
     if ((C & 3) != 0 || rows <= 0) return -1;
     const int blocks = (rows + 7) / 8;
     if (C <= 512)
-        norm_fwd_kernel<4><<<blocks, 256, 0, s>>>(x, gamma, beta, y, mean, rstd, rows, C, rms);
+        launch_kernel(norm_fwd_kernel<4>, blocks, 256, 0, s, x, gamma, beta, y, mean, rstd, rows, C, rms);
     else if (C <= 1024)
-        norm_fwd_kernel<8><<<blocks, 256, 0, s>>>(x, gamma, beta, y, mean, rstd, rows, C, rms);
+        launch_kernel(norm_fwd_kernel<8>, blocks, 256, 0, s, x, gamma, beta, y, mean, rstd, rows, C, rms);
     else if (C <= 2048)
-        norm_fwd_kernel<16><<<blocks, 256, 0, s>>>(x, gamma, beta, y, mean, rstd, rows, C, rms);
+        launch_kernel(norm_fwd_kernel<16>, blocks, 256, 0, s, x, gamma, beta, y, mean, rstd, rows, C, rms);
     else
         return -2;
     return launch_status();
@@ -309,9 +313,9 @@ int norm_backward(const float* dy, const float* x, const float* gamma, const flo
         cudaFuncSetAttribute(norm_bwd_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
         set = true;
     }
-#define NB_LAUNCH(MV)                                                                      \
-    norm_bwd_kernel<MV><<<grid, 256, smem, s>>>(dy, x, gamma, mean, rstd, resid_in, dx_f32, \
-                                                dx_bf16, partial, rows, C, rms)
+#define NB_LAUNCH(MV)                                                                   \
+    launch_kernel(norm_bwd_kernel<MV>, grid, 256, smem, s, dy, x, gamma, mean, rstd, resid_in, \
+                  dx_f32, dx_bf16, partial, rows, C, rms)
     if (C <= 128)
         NB_LAUNCH(1);
     else if (C <= 256)
@@ -331,7 +335,7 @@ int norm_backward(const float* dy, const float* x, const float* gamma, const flo
 int reduce_partials(const float* partial, int nparts, int C, float* out0, float* out1,
                     float* out2, int accumulate, cudaStream_t s) {
     dim3 grid((C + 31) / 32, 3);  // partials are [part][3][C]
-    sum_parts_kernel<<<grid, 1024, 0, s>>>(partial, nparts, 3LL * C, C, C, out0, out1, out2,
+    launch_kernel(sum_parts_kernel, grid, 1024, 0, s, partial, nparts, 3LL * C, C, C, out0, out1, out2,
                                            accumulate);
     return launch_status();
 }
@@ -341,8 +345,8 @@ size_t colsum_work_floats(int C) { return (size_t)kColsumGroups * C; }
 int colsum_bf16(const bf16* a, long long lda, int rows, int C, float* out, int accumulate,
                 float* work, cudaStream_t s) {
     dim3 g1((C + 2047) / 2048, kColsumGroups);
-    colsum_stage1<<<g1, 256, 0, s>>>(a, lda, rows, C, work);
-    sum_parts_kernel<<<dim3((C + 31) / 32, 1), 1024, 0, s>>>(work, kColsumGroups, C, 0, C, out,
+    launch_kernel(colsum_stage1, g1, 256, 0, s, a, lda, rows, C, work);
+    launch_kernel(sum_parts_kernel, dim3((C + 31) / 32, 1), 1024, 0, s, work, kColsumGroups, C, 0, C, out,
                                                              nullptr, nullptr, accumulate);
     return launch_status();
 }

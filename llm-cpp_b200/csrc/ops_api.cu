@@ -63,6 +63,25 @@ extern "C" int llmgpu_op_embed(const int32_t* tokens, const float* wte, const fl
     return embed_forward(tokens, wte, wpe, x, B, T, C, V, reinterpret_cast<cudaStream_t>(stream));
 }
 
+extern "C" long long llmgpu_op_embed_bwd_work(int B, int T, int C) {
+    const long long n = (long long)B * T;
+    return ((n * 8 + 255) / 256) * 256 + n * C * 4;
+}
+
+extern "C" int llmgpu_op_embed_bwd(const int32_t* tokens, const float* dx, float* wte_grad,
+                                   float* wpe_grad, int B, int T, int C, int V,
+                                   int accumulate_wpe, void* work, void* stream) {
+    const long long n = (long long)B * T;
+    if (B <= 0 || T <= 0 || C <= 0 || V <= 0 || n > 16384 || !work) return -1;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    uint64_t* keys = reinterpret_cast<uint64_t*>(work);
+    float* scratch = reinterpret_cast<float*>(reinterpret_cast<char*>(work) +
+                                              ((n * 8 + 255) / 256) * 256);
+    const int rc = embed_sort_keys(tokens, (int)n, V, keys, s);
+    if (rc) return rc;
+    return embed_backward(keys, dx, wte_grad, wpe_grad, B, T, C, accumulate_wpe, scratch, s);
+}
+
 extern "C" int llmgpu_op_norm_fwd(const float* x, const float* gamma, const float* beta,
                                   void* y_bf16, float* mean, float* rstd, int rows, int C, int rms,
                                   void* stream) {

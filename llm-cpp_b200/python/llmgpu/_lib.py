@@ -26,6 +26,9 @@ def _declare(lib):
                                    c_int, c_ll, c_int, c_vp, c_vp]
     lib.llmgpu_op_gemm.restype = c_int
     lib.llmgpu_op_embed.argtypes = [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp]
+    lib.llmgpu_op_embed_bwd_work.argtypes = [c_int, c_int, c_int]
+    lib.llmgpu_op_embed_bwd_work.restype = c_ll
+    lib.llmgpu_op_embed_bwd.argtypes = [c_vp, c_vp, c_vp, c_vp] + [c_int] * 5 + [c_vp, c_vp]
     lib.llmgpu_op_norm_fwd.argtypes = [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
                                        c_vp]
     lib.llmgpu_op_norm_bwd.argtypes = [c_vp] * 12 + [c_int, c_int, c_int, c_vp]

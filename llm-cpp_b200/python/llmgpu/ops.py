@@ -74,6 +74,17 @@ def embed(tokens, wte, wpe, B, T):
     return x
 
 
+def embed_bwd(tokens, dx, wte_grad, wpe_grad, B, T, accumulate_wpe=False):
+    """wte_grad[tok mod V] += dx rows; wpe_grad (+)= the batch sum of dx rows (in place)."""
+    lib = load()
+    V, C = wte_grad.shape
+    work = torch.empty(int(lib.llmgpu_op_embed_bwd_work(B, T, C)), dtype=torch.uint8,
+                       device=dx.device)
+    _sync_check(lib.llmgpu_op_embed_bwd(_ptr(tokens), _ptr(dx), _ptr(wte_grad), _ptr(wpe_grad),
+                                        B, T, C, V, int(accumulate_wpe), _ptr(work), _stream()),
+                "embed_bwd")
+
+
 def norm_fwd(x, gamma, beta, rms=False):
     lib = load()
     rows, C = x.shape

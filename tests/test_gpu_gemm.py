@@ -115,3 +115,17 @@ def test_gemm_large_persistent(cuda, bn):
     o = ops.gemm(a, b, M, N, K, epi=ops.EPI_F32, bn=bn)
     ref = a.float() @ b.float().t()
     assert _rel(o, ref) < 1e-4
+
+
+@pytest.mark.parametrize("K", [768, 3072])
+def test_gemm_residual_step_shapes(cuda, K):
+    """The training step's N = 768 products with the residual epilogue at 8192 token rows on
+    CTA pairs (attention output, K 768; FFN down, K 3072): 96 pair tiles in two waves."""
+    from llmgpu import ops
+    g = torch.Generator().manual_seed(K)
+    M, N = 8192, 768
+    a = _mk((M, K), g, 0.5).to(cuda)
+    b = _mk((K, N), g, 0.5).to(cuda)          # MN-major B, like x @ W
+    r = torch.randn(M, N, device=cuda)
+    o = ops.gemm(a, b, M, N, K, b_mn=True, bn=512, epi=ops.EPI_RESID, resid=r, ldr=N)
+    assert _rel(o, a.float() @ b.float() + r) < 1e-5

@@ -27,6 +27,33 @@ def test_embedding_gather_bit_exact(cuda):
     assert torch.equal(x.cpu(), want)
 
 
+@pytest.mark.parametrize("C", [96, 768])
+@pytest.mark.parametrize("accumulate_wpe", [False, True])
+def test_embedding_backward_repeated_ids(cuda, C, accumulate_wpe):
+    """wte_grad[tok mod V] += dx rows, wpe_grad (+)= sum over the batch (src/model.cpp:314-322).
+    One id fills 1500 of the 2048 rows (a run of 94 sixteen-row pieces: more than one
+    32-piece window of the run search), the rest are random ids, negative and past V
+    included; C 96 leaves lanes of the last column slice without a column."""
+    from llmgpu import ops
+    g = torch.Generator().manual_seed(C + accumulate_wpe)
+    B, T, V = 2, 1024, 300
+    tok = torch.randint(-400, 700, (B * T,), generator=g, dtype=torch.int32)
+    tok[torch.randperm(B * T, generator=g)[:1500]] = 7
+    dx = torch.randn(B * T, C, generator=g)
+    wte_g0 = torch.randn(V, C, generator=g)
+    wpe_g0 = torch.randn(T, C, generator=g)
+    wte_g, wpe_g = wte_g0.clone().to(cuda), wpe_g0.clone().to(cuda)
+    ops.embed_bwd(tok.to(cuda), dx.to(cuda), wte_g, wpe_g, B, T, accumulate_wpe)
+    want = wte_g0.double().index_add_(0, (tok.long() % V), dx.double())
+    assert _rel(wte_g.cpu(), want) < 1e-6
+    # the most repeated row: 1500 fp32 additions in pieces of 16
+    assert torch.allclose(wte_g.cpu()[7].double(), want[7], rtol=0, atol=2e-4)
+    # the batch sum over b in order (b = 0, then 1): exact in fp32
+    d3 = dx.reshape(B, T, C)
+    want_pe = (wpe_g0 + d3[0]) + d3[1] if accumulate_wpe else d3[0] + d3[1]
+    assert torch.equal(wpe_g.cpu(), want_pe)
+
+
 @pytest.mark.parametrize("rms", [False, True])
 @pytest.mark.parametrize("C", [128, 768, 1024])
 def test_norm_forward_backward(cuda, rms, C):
