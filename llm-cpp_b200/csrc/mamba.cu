@@ -18,14 +18,35 @@ namespace llmgpu {
 namespace {
 
 
-__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
-__device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + __expf(-v)); }
+__device__ __forceinline__ float silu_f(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
+__device__ __forceinline__ float sigmoid_f(float v) { return __fdividef(1.0f, 1.0f + __expf(-v)); }
 __device__ __forceinline__ float silu_grad_f(float v) {
     const float s = sigmoid_f(v);
     return s * (1.0f + v * (1.0f - s));
 }
-__device__ __forceinline__ float softplus_f(float v) { return log1pf(__expf(v)); }
-__device__ __forceinline__ float clamp_dt(float sp) { return fminf(fmaxf(sp, 0.001f), 0.1f); }
+// dt = clamp(softplus(x), 1e-3, 0.1) (src/mamba.cpp:120-135) and, for the backward, the
+// derivative of that w.r.t. x: sigmoid(x) where softplus(x) lies inside the clamp, else 0
+// (src/mamba.cpp:318-328). softplus(x) = log(1 + e) with e = e^x matters only where the clamp
+// keeps it, e in [1.0005e-3, 0.10517]: there log(1 + e) is its alternating series to the
+// e^8 term (remainder below 3e-9 relative, e < 0.11). Above e = 0.25 softplus exceeds 0.22
+// and the clamp gives 0.1 whatever its value.
+struct DtOf {
+    float dt, ddt;
+};
+__device__ __forceinline__ DtOf dt_of(float x) {
+    const float e = __expf(x);
+    float q = -0.125f;
+    q = fmaf(q, e, 1.0f / 7.0f);
+    q = fmaf(q, e, -1.0f / 6.0f);
+    q = fmaf(q, e, 0.2f);
+    q = fmaf(q, e, -0.25f);
+    q = fmaf(q, e, 1.0f / 3.0f);
+    q = fmaf(q, e, -0.5f);
+    q = fmaf(q, e, 1.0f);
+    const float sp = e > 0.25f ? 1.0f : q * e;
+    const bool inside = sp >= 0.001f && sp <= 0.1f;
+    return {fminf(fmaxf(sp, 0.001f), 0.1f), inside ? __fdividef(e, 1.0f + e) : 0.f};
+}
 
 // ---------------------------------------------------------------- conv forward
 // pre[t,d] = b[d] + sum_j w[d,j] x[t-(K-1)+j, d] within each sequence; u = silu(pre).
@@ -80,13 +101,14 @@ __global__ void conv_fwd_kernel(const bf16* __restrict__ proj, long long ldp, in
 
 // ---------------------------------------------------------------- scan staging
 // A block of kScanWarps warps owns CPB = kScanWarps * 32 / L consecutive channels of one
-// sequence; the L lanes of a channel hold S states each (state n*S + s in lane n), so
-// d_state 16 runs as 8 lanes x 2 states and all (sequence, channel) pairs of a Mamba layer
-// fit on the GPU at once. Time runs in chunks of kScanChunk steps; the block loads a chunk's
-// per-(step, channel) inputs and its per-(step, state) B and C into shared memory with
-// coalesced row segments, double buffered: the loads of the next chunk are issued into
-// registers before the recurrence of the current one runs, so the serial part of the scan
-// never waits on global memory.
+// sequence; the L lanes of a channel hold S states each (state n*S + s in lane n): d_state
+// 16 runs as 8 lanes x 2 states, and all (sequence, channel) pairs of a Mamba layer are
+// resident at once (one state per lane, with twice the warps, measured slower: more
+// instructions per state, and the scan is issue-bound at the bench shape). Time runs in chunks;
+// the block loads a chunk's per-(step, channel) inputs and its per-(step, state) B and C
+// into shared memory with coalesced row segments, double buffered: the loads of the next
+// chunk are issued into registers before the recurrence of the current one runs, so the
+// serial part of the scan does not wait on global memory.
 constexpr int kScanWarps = 4;
 template <int L, int S>
 struct ScanTile {
@@ -102,43 +124,64 @@ struct ScanTile {
                                                         // at different steps hit distinct banks
 };
 
-// v[M] held by each of the L lanes of a channel -> channel sums spread over the lanes:
-// lane n holds in v[0, kPer) the sums of entries [(n / kGroup) * kPer, ... + kPer), with
-// kPer = max(M / L, 1) and kGroup = max(L / M, 1) lanes holding each entry. Recursive
-// halving: every stage sends half of the remaining entries to the partner lane (M - M/L
-// shuffles for M >= L, instead of M*log2(L) for M butterflies), and the shuffles of a stage
-// are independent of one another.
-template <int L, int M>
-struct LaneSplit {
-    static constexpr int kPer = M >= L ? M / L : 1;
-    static constexpr int kGroup = M >= L ? 1 : L / M;
-};
-template <int L, int M>
-__device__ __forceinline__ void lane_reduce_scatter(float (&v)[M], int n) {
+// Sum of L values by a fixed pairwise tree (a short dependency chain; deterministic).
+template <int L>
+__device__ __forceinline__ float tree_sum(float (&v)[L]) {
 #pragma unroll
-    for (int o = L / 2, h = M / 2; o >= 1 && h >= 1; o >>= 1, h >>= 1) {
-        const bool up = (n & o) != 0;
+    for (int w = L / 2; w >= 1; w >>= 1)
 #pragma unroll
-        for (int k = 0; k < h; ++k) {
-            const float send = up ? v[k] : v[k + h];
-            const float keep = up ? v[k + h] : v[k];
-            v[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-        }
-    }
-    // M < L: lanes within a group still hold partial sums of the same entry
-#pragma unroll
-    for (int o = LaneSplit<L, M>::kGroup / 2; o >= 1; o >>= 1)
-        v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+        for (int k = 0; k < w; ++k) v[k] += v[k + w];
+    return v[0];
 }
 
 // ---------------------------------------------------------------- scan forward
+// exp(A dt) = 2^((A log2 e) dt): A is scaled by log2 e once per thread and the power of two
+// runs on the special-function unit (ex2.approx, flush-to-zero: decays below 2^-126 are 0).
+constexpr float kLog2e = 1.4426950408889634f;
+__device__ __forceinline__ float exp2_sfu(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// A lane's S consecutive state values to shared memory (one 8-byte store for S = 2).
+template <int S>
+__device__ __forceinline__ void store_states(float* p, const float (&v)[S]) {
+    if constexpr (S == 2) {
+        *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+    } else {
+#pragma unroll
+        for (int s = 0; s < S; ++s) p[s] = v[s];
+    }
+}
+
+// A lane's S consecutive state values from shared memory (one 8-byte load for S = 2).
+template <int S>
+__device__ __forceinline__ void load_states(const float* p, float (&v)[S]) {
+    if constexpr (S == 2) {
+        const float2 q = *reinterpret_cast<const float2*>(p);
+        v[0] = q.x;
+        v[1] = q.y;
+    } else {
+#pragma unroll
+        for (int s = 0; s < S; ++s) v[s] = p[s];
+    }
+}
+
 // The sequence is cut into gridDim.z segments of whole chunks, scanned side by side. The
 // recurrence is linear, so a segment's states are its own scan from h = 0 plus the state
 // entering it decayed by exp(A * (sum of dt so far in the segment)). PASS 0 scans each
 // segment from zero and keeps only its final state and its dt sum (seg_h [B][P][D][N],
 // seg_dt [B][P][D]); PASS 1 folds the earlier segments' results into the state entering its
-// segment, then scans it again writing y, the gated output and the saved chunk states. With
-// one segment, PASS 1 alone is the plain scan.
+// segment, then scans it again writing y, the gated output and the states every kScanChunk
+// steps. With one segment, PASS 1 alone is the plain scan.
+//
+// Time runs in chunks of TF steps (two or one kScanChunk). The block stages a chunk's
+// (dt, dt u) and (u, z) per (step, channel) and B, C per (step, state) in shared memory; the
+// inputs of the next chunk are loaded into registers while the current one runs. Per step a lane does S
+// states: a = 2^(A' dt), h = a h + B (dt u), p = sum_s C h. The L lanes of a channel then
+// add their p through shared memory: lane n of a channel sums, for its steps n, n + L, ...,
+// the L partials of that step (row pitch 33 floats: conflict-free) and writes y and the gate.
 template <int L, int S, int PASS>
 __global__ void __launch_bounds__(kScanWarps * 32) scan_fwd_kernel(
     const float* __restrict__ raw, const float* __restrict__ u, const float* __restrict__ xp,
@@ -147,42 +190,56 @@ __global__ void __launch_bounds__(kScanWarps * 32) scan_fwd_kernel(
     bf16* __restrict__ gated, float* __restrict__ hchk, float* __restrict__ seg_h,
     float* __restrict__ seg_dt, int T, int D, int N, int R) {
     using G = ScanTile<L, S>;
-    constexpr int CPB = G::kCPB, TC = G::kTC, EPT = G::kEPT, NT = G::kThreads, RW = G::kRow;
-    constexpr int NS = G::kNS, BPT = G::kBPT;
-    __shared__ float sDt[2][TC][RW], sU[2][TC][RW], sZ[2][TC][RW];
-    __shared__ __align__(16) float sB[2][TC][NS], sC[2][TC][NS];
+    constexpr int CPB = G::kCPB, CPW = G::kCPW, NT = G::kThreads, NS = G::kNS;
+    // 32-step chunks (states saved at both 16-step boundaries); 16 for 32-channel blocks,
+    // whose staging would not fit the 48 KB of static shared memory
+    constexpr int TF = CPB <= 16 ? 2 * kScanChunk : kScanChunk;
+    constexpr int EPT = TF * CPB / NT;            // (step, channel) items a thread stages
+    constexpr int BPT = (TF * NS + NT - 1) / NT;  // (step, state) items a thread stages
+    constexpr int KPER = TF / L;                  // steps whose output a lane writes
+    static_assert(TF * CPB % NT == 0 && TF % L == 0, "chunk tile must split evenly");
+    constexpr int P1 = PASS == 1 ? 2 : 1;
+    __shared__ float2 sDU[2][TF][CPB];  // (dt, dt * u)
+    __shared__ float2 sUZ[P1][PASS == 1 ? TF : 1][CPB];  // (u, z) for the outputs
+    __shared__ __align__(16) float sB[2][TF][NS];
+    __shared__ __align__(16) float sC[P1][PASS == 1 ? TF : 1][NS];
+    __shared__ float sRed[PASS == 1 ? kScanWarps : 1][PASS == 1 ? TF : 1][33];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n = lane % L, c = warp * G::kCPW + lane / L;
+    const int n = lane % L, ch = lane / L, c = warp * CPW + ch;
     const int d0 = blockIdx.x * CPB, d = d0 + c;
     const int b = blockIdx.y;
     const bool chan = d < D;
-    float A[S];
+    float A2[S];
 #pragma unroll
     for (int s = 0; s < S; ++s) {
         const int k = n * S + s;
-        A[s] = (chan && k < N) ? alog[(long long)d * N + k] : 0.f;
+        A2[s] = (chan && k < N) ? alog[(long long)d * N + k] * kLog2e : 0.f;
     }
     const float Ds = chan ? dskip[d] : 0.f;
-    const int nch = (T + TC - 1) / TC;
+    const int nch = (T + TF - 1) / TF;
+    const int nch16 = (T + kScanChunk - 1) / kScanChunk;
 
     float pr[EPT], pu[EPT], pz[EPT], pb[BPT], pc[BPT];
     auto fetch = [&](int t0) {
+        const long long row0 = (long long)b * T + t0;  // the chunk's first token row
+        const float* raw_c = raw + row0 * D + d0;
+        const float* u_c = u + row0 * D + d0;
+        const bf16* z_c = proj + row0 * ldp + d0;
+        const float* b_c = xp + row0 * ldx + R;
 #pragma unroll
         for (int e = 0; e < EPT; ++e) {
-            const int idx = tid + e * NT, i = idx / CPB, dd = d0 + idx % CPB;
-            const bool ok = t0 + i < T && dd < D;
-            const long long row = (long long)b * T + t0 + i;
-            pr[e] = ok ? raw[row * D + dd] : 0.f;
-            pu[e] = ok ? u[row * D + dd] : 0.f;
-            if (PASS == 1) pz[e] = ok ? __bfloat162float(proj[row * ldp + dd]) : 0.f;
+            const int idx = tid + e * NT, i = idx / CPB, cc = idx % CPB;
+            const bool ok = t0 + i < T && d0 + cc < D;
+            pr[e] = ok ? raw_c[i * D + cc] : 0.f;
+            pu[e] = ok ? u_c[i * D + cc] : 0.f;
+            if constexpr (PASS == 1) pz[e] = ok ? __bfloat162float(z_c[i * ldp + cc]) : 0.f;
         }
 #pragma unroll
         for (int e = 0; e < BPT; ++e) {
             const int idx = tid + e * NT, i = idx / NS, k = idx % NS;
-            const bool ok = idx < TC * NS && t0 + i < T && k < N;
-            const long long row = (long long)b * T + t0 + i;
-            pb[e] = ok ? xp[row * ldx + R + k] : 0.f;
-            if (PASS == 1) pc[e] = ok ? xp[row * ldx + R + N + k] : 0.f;
+            const bool ok = idx < TF * NS && t0 + i < T && k < N;
+            pb[e] = ok ? b_c[i * ldx + k] : 0.f;
+            if constexpr (PASS == 1) pc[e] = ok ? b_c[i * ldx + N + k] : 0.f;
         }
     };
     auto stage = [&](int buf, int t0) {
@@ -190,16 +247,16 @@ __global__ void __launch_bounds__(kScanWarps * 32) scan_fwd_kernel(
         for (int e = 0; e < EPT; ++e) {
             const int idx = tid + e * NT, i = idx / CPB, cc = idx % CPB;
             const bool ok = t0 + i < T && d0 + cc < D;
-            sDt[buf][i][cc] = ok ? clamp_dt(softplus_f(pr[e])) : 0.f;
-            sU[buf][i][cc] = pu[e];
-            if (PASS == 1) sZ[buf][i][cc] = pz[e];
+            const float dt = ok ? dt_of(pr[e]).dt : 0.f;
+            sDU[buf][i][cc] = make_float2(dt, dt * pu[e]);
+            if constexpr (PASS == 1) sUZ[buf][i][cc] = make_float2(pu[e], pz[e]);
         }
 #pragma unroll
         for (int e = 0; e < BPT; ++e) {
             const int idx = tid + e * NT;
-            if (idx < TC * NS) {
+            if (idx < TF * NS) {
                 sB[buf][idx / NS][idx % NS] = pb[e];
-                if (PASS == 1) sC[buf][idx / NS][idx % NS] = pc[e];
+                if constexpr (PASS == 1) sC[buf][idx / NS][idx % NS] = pc[e];
             }
         }
     };
@@ -220,58 +277,69 @@ __global__ void __launch_bounds__(kScanWarps * 32) scan_fwd_kernel(
             for (int s = 0; s < S; ++s) {
                 const int kk = n * S + s;
                 const float he = (chan && kk < N) ? seg_h[(bp * D + d) * N + kk] : 0.f;
-                h[s] = __expf(A[s] * dts) * h[s] + he;
+                h[s] = fmaf(exp2_sfu(A2[s] * dts), h[s], he);
             }
         }
     }
     float dtsum = 0.f;
-    if (k_begin < k_end) fetch(k_begin * TC);
+    if (k_begin < k_end) fetch(k_begin * TF);
     for (int k = k_begin; k < k_end; ++k) {
-        const int buf = k & 1, t0 = k * TC;
+        const int buf = k & 1, t0 = k * TF;
         stage(buf, t0);
         __syncthreads();
-        if (k + 1 < k_end) fetch(t0 + TC);
+        if (k + 1 < k_end) fetch(t0 + TF);
+        // steps past T were staged as dt = dt u = B = C = 0, which leaves h unchanged
         if constexpr (PASS == 0) {
-            // h from zero and the segment's dt sum only
 #pragma unroll
-            for (int i = 0; i < TC; ++i) {
-                const float dt = sDt[buf][i][c], uu = sU[buf][i][c];
-                dtsum += dt;
+            for (int i = 0; i < TF; ++i) {
+                const float2 dd = sDU[buf][i][c];
+                dtsum += dd.x;
 #pragma unroll
                 for (int s = 0; s < S; ++s)
-                    h[s] = __expf(A[s] * dt) * h[s] + sB[buf][i][n * S + s] * uu * dt;
+                    h[s] = fmaf(exp2_sfu(A2[s] * dd.x), h[s], sB[buf][i][n * S + s] * dd.y);
             }
         } else {
+            float p[TF];
 #pragma unroll
-            for (int s = 0; s < S; ++s)
-                if (chan && n * S + s < N)
-                    hchk[(((long long)b * nch + k) * D + d) * N + n * S + s] = h[s];
-            // steps past T were staged as dt = u = B = 0, which leaves h unchanged
-            float cs[TC];
+            for (int i = 0; i < TF; ++i) {
+                if (i % kScanChunk == 0 && t0 + i < T) {
+                    const int k16 = (t0 + i) / kScanChunk;
 #pragma unroll
-            for (int i = 0; i < TC; ++i) {
-                const float dt = sDt[buf][i][c], uu = sU[buf][i][c];
+                    for (int s = 0; s < S; ++s)
+                        if (chan && n * S + s < N)
+                            hchk[(((long long)b * nch16 + k16) * D + d) * N + n * S + s] = h[s];
+                }
+                const float2 dd = sDU[buf][i][c];
+                float bv[S], cv[S];
+                load_states<S>(&sB[buf][i][n * S], bv);
+                load_states<S>(&sC[buf][i][n * S], cv);
                 float acc = 0.f;
 #pragma unroll
                 for (int s = 0; s < S; ++s) {
-                    const float a = __expf(A[s] * dt);
-                    h[s] = a * h[s] + sB[buf][i][n * S + s] * uu * dt;
-                    acc += sC[buf][i][n * S + s] * h[s];
+                    h[s] = fmaf(exp2_sfu(A2[s] * dd.x), h[s], bv[s] * dd.y);
+                    acc = fmaf(cv[s], h[s], acc);
                 }
-                cs[i] = acc;
+                p[i] = acc;
             }
-            lane_reduce_scatter<L, TC>(cs, n);
-            using SP = LaneSplit<L, TC>;
 #pragma unroll
-            for (int j = 0; j < SP::kPer; ++j) {
-                const int i = (n / SP::kGroup) * SP::kPer + j;
-                if (chan && n % SP::kGroup == 0 && t0 + i < T) {
-                    const long long row = (long long)b * T + t0 + i;
-                    const float yv = cs[j] + Ds * sU[buf][i][c];
-                    y32[row * D + d] = yv;
-                    gated[row * D + d] = __float2bfloat16_rn(yv * silu_f(sZ[buf][i][c]));
+            for (int i = 0; i < TF; ++i) sRed[warp][i][lane] = p[i];
+            __syncwarp();
+#pragma unroll
+            for (int jj = 0; jj < KPER; ++jj) {
+                const int j = n + L * jj;
+                float part[L];
+#pragma unroll
+                for (int m = 0; m < L; ++m) part[m] = sRed[warp][j][ch * L + m];
+                float y = tree_sum<L>(part);
+                if (chan && t0 + j < T) {
+                    const long long row = (long long)b * T + t0 + j;
+                    const float2 uz = sUZ[buf][j][c];
+                    y = fmaf(Ds, uz.x, y);
+                    y32[row * D + d] = y;
+                    gated[row * D + d] = __float2bfloat16_rn(y * silu_f(uz.y));
                 }
             }
+            __syncwarp();  // the partials are read before the next chunk overwrites them
         }
     }
     if (PASS == 0) {
@@ -284,6 +352,34 @@ __global__ void __launch_bounds__(kScanWarps * 32) scan_fwd_kernel(
 }
 
 // ---------------------------------------------------------------- scan backward
+// Chunks of kScanChunk steps from the right. Per chunk a lane recomputes its states from the
+// saved h (keeping the decays a and the states in registers), then runs the reverse
+// recurrence: dh = dh' + dy C, dh' = dh a (for the step before), with per-lane sums over its
+// S states G = sum dh B and H = sum (dh a h_prev) A, and per-state terms dB = dh (dt u) and
+// dC = dy h. From the channel sums of G and H: du = G dt + dy D and ddt = H + G u. The L
+// lanes of a channel add G and H through shared memory like the forward's outputs; the dB
+// and dC terms go to a [channel][state] table and the block sums each (step, state) over its
+// channels in a fixed order (partials per channel group, reduced by dbc_reduce_kernel).
+template <int L, int S>
+struct ScanBwdSmem {
+    static constexpr int CPB = ScanTile<L, S>::kCPB, NS = ScanTile<L, S>::kNS;
+    static constexpr int TC = kScanChunk;
+    static constexpr size_t kDU = 0;                                      // float2 [2][TC][CPB]
+    static constexpr size_t kGU = kDU + sizeof(float2) * 2 * TC * CPB;    // float2 [2][TC][CPB]
+    static constexpr size_t kDf = kGU + sizeof(float2) * 2 * TC * CPB;    // float [2][TC][CPB]
+    static constexpr size_t kB = kDf + sizeof(float) * 2 * TC * CPB;      // float [2][TC][NS]
+    static constexpr size_t kC = kB + sizeof(float) * 2 * TC * NS;        // float [2][TC][NS]
+    static constexpr size_t kRed = kC + sizeof(float) * 2 * TC * NS;      // float2 [W][TC][33]
+    // dB/dC terms [2][TC][ROW]: a step's [channel][state] block, rows padded by 16 floats so
+    // that the block sum's reads of consecutive (step, state) pairs fall in distinct banks
+    static constexpr int ROW = CPB * NS + 16;
+    static constexpr size_t kP = kRed + sizeof(float) * kScanWarps * 2 * TC * 33;
+    static constexpr size_t kBytes = kP + sizeof(float) * 2 * TC * ROW;
+    static_assert(kB % 16 == 0 && kRed % 8 == 0 && kP % 16 == 0, "table alignment");
+};
+
+// Three blocks per SM (at most 170 registers a thread): the bench's four sequences of 96
+// channel groups make 384 blocks, which must all be resident.
 template <int L, int S>
 __global__ void __launch_bounds__(kScanWarps * 32, 3) scan_bwd_kernel(
     const float* __restrict__ raw, const float* __restrict__ u, const float* __restrict__ xp,
@@ -294,50 +390,67 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) scan_bwd_kernel(
     float* __restrict__ da_part, float* __restrict__ dd_part, const float* __restrict__ seg_dh,
     const float* __restrict__ seg_dt, int T, int D, int N, int R) {
     using G = ScanTile<L, S>;
-    constexpr int CPB = G::kCPB, TC = G::kTC, EPT = G::kEPT, NT = G::kThreads, RW = G::kRow;
-    constexpr int NS = G::kNS, BPT = G::kBPT;
-    __shared__ float sDt[2][TC][RW], sU[2][TC][RW], sDy[2][TC][RW];
+    using SM = ScanBwdSmem<L, S>;
+    constexpr int CPB = G::kCPB, CPW = G::kCPW, NT = G::kThreads, NS = G::kNS;
+    constexpr int TC = kScanChunk;
+    constexpr int EPT = TC * CPB / NT, BPT = (TC * NS + NT - 1) / NT, KPER = TC / L;
+    static_assert(TC * CPB % NT == 0 && TC % L == 0, "chunk tile must split evenly");
+    extern __shared__ __align__(16) unsigned char scan_smem[];
+    auto sDU = reinterpret_cast<float2(*)[TC][CPB]>(scan_smem + SM::kDU);  // (dt, dt u)
+    auto sGU = reinterpret_cast<float2(*)[TC][CPB]>(scan_smem + SM::kGU);  // (dy, u)
     // d(dt)/d(dt_raw): sigmoid(dt_raw) where softplus(dt_raw) lies inside the clamp, else 0
     // (src/mamba.cpp:318-328)
-    __shared__ float sDf[2][TC][RW];
-    __shared__ __align__(16) float sB[2][TC][NS], sC[2][TC][NS];
-    // per-channel dB, dC terms of the chunk, summed over the block's channels after it
-    __shared__ float sPB[TC][CPB][NS], sPC[TC][CPB][NS];
+    auto sDf = reinterpret_cast<float(*)[TC][CPB]>(scan_smem + SM::kDf);
+    auto sB = reinterpret_cast<float(*)[TC][NS]>(scan_smem + SM::kB);
+    auto sC = reinterpret_cast<float(*)[TC][NS]>(scan_smem + SM::kC);
+    auto sRed = reinterpret_cast<float2(*)[TC][33]>(scan_smem + SM::kRed);  // (G, H) partials
+    auto sP = reinterpret_cast<float(*)[TC][SM::ROW]>(scan_smem + SM::kP);  // [dB, dC]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n = lane % L, c = warp * G::kCPW + lane / L;
+    const int n = lane % L, ch = lane / L, c = warp * CPW + ch;
     const int d0 = blockIdx.x * CPB, d = d0 + c;
     const int b = blockIdx.y;
     const bool chan = d < D;
-    float A[S];
+    float A[S], A2[S];
 #pragma unroll
     for (int s = 0; s < S; ++s) {
         const int k = n * S + s;
         A[s] = (chan && k < N) ? alog[(long long)d * N + k] : 0.f;
+        A2[s] = A[s] * kLog2e;
     }
     const float Ds = chan ? dskip[d] : 0.f;
     const int nch = (T + TC - 1) / TC;
     const long long BT = (long long)gridDim.y * T;
 
-    float pr[EPT], pu[EPT], pg[EPT], pz[EPT], py[EPT], pb[BPT], pc[BPT];
+    float pr[EPT], pu[EPT], pg[EPT], pz[EPT], py[EPT], pb[BPT], pc[BPT], ph[S];
     auto fetch = [&](int t0) {
+        // the state saved at the chunk's start, loaded a chunk ahead like the inputs
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            const int kk = n * S + s;
+            ph[s] = (chan && kk < N)
+                        ? hchk[(((long long)b * nch + t0 / TC) * D + d) * N + kk] : 0.f;
+        }
+        const long long row0 = (long long)b * T + t0;  // the chunk's first token row
+        const long long o0 = row0 * D + d0;
+        const bf16* z_c = proj + row0 * ldp + d0;
+        const float* b_c = xp + row0 * ldx + R;
 #pragma unroll
         for (int e = 0; e < EPT; ++e) {
-            const int idx = tid + e * NT, i = idx / CPB, dd = d0 + idx % CPB;
-            const bool ok = t0 + i < T && dd < D;
-            const long long row = (long long)b * T + t0 + i;
-            pr[e] = ok ? raw[row * D + dd] : 0.f;
-            pu[e] = ok ? u[row * D + dd] : 0.f;
-            pg[e] = ok ? dgated[row * D + dd] : 0.f;
-            pz[e] = ok ? __bfloat162float(proj[row * ldp + dd]) : 0.f;
-            py[e] = ok ? y32[row * D + dd] : 0.f;
+            const int idx = tid + e * NT, i = idx / CPB, cc = idx % CPB;
+            const bool ok = t0 + i < T && d0 + cc < D;
+            const long long o = o0 + i * D + cc;
+            pr[e] = ok ? raw[o] : 0.f;
+            pu[e] = ok ? u[o] : 0.f;
+            pg[e] = ok ? dgated[o] : 0.f;
+            pz[e] = ok ? __bfloat162float(z_c[i * ldp + cc]) : 0.f;
+            py[e] = ok ? y32[o] : 0.f;
         }
 #pragma unroll
         for (int e = 0; e < BPT; ++e) {
             const int idx = tid + e * NT, i = idx / NS, k = idx % NS;
             const bool ok = idx < TC * NS && t0 + i < T && k < N;
-            const long long row = (long long)b * T + t0 + i;
-            pb[e] = ok ? xp[row * ldx + R + k] : 0.f;
-            pc[e] = ok ? xp[row * ldx + R + N + k] : 0.f;
+            pb[e] = ok ? b_c[i * ldx + k] : 0.f;
+            pc[e] = ok ? b_c[i * ldx + N + k] : 0.f;
         }
     };
     // also writes the x_z gradient, which needs no scan state
@@ -346,11 +459,11 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) scan_bwd_kernel(
         for (int e = 0; e < EPT; ++e) {
             const int idx = tid + e * NT, i = idx / CPB, cc = idx % CPB;
             const bool ok = t0 + i < T && d0 + cc < D;
-            const float sp = softplus_f(pr[e]);
-            sDt[buf][i][cc] = ok ? clamp_dt(sp) : 0.f;
-            sDf[buf][i][cc] = (ok && sp >= 0.001f && sp <= 0.1f) ? sigmoid_f(pr[e]) : 0.f;
-            sU[buf][i][cc] = pu[e];
-            sDy[buf][i][cc] = pg[e] * silu_f(pz[e]);      // d(loss)/d(y)
+            const DtOf v = dt_of(pr[e]);
+            const float dt = ok ? v.dt : 0.f;
+            sDU[buf][i][cc] = make_float2(dt, dt * pu[e]);
+            sGU[buf][i][cc] = make_float2(pg[e] * silu_f(pz[e]), pu[e]);  // d(loss)/d(y), u
+            sDf[buf][i][cc] = ok ? v.ddt : 0.f;
             if (ok) {
                 const long long row = (long long)b * T + t0 + i;
                 dproj[row * ldp + d0 + cc] = __float2bfloat16_rn(pg[e] * py[e] * silu_grad_f(pz[e]));
@@ -381,7 +494,7 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) scan_bwd_kernel(
         for (int s = 0; s < S; ++s) {
             const int kk = n * S + s;
             const float he = (chan && kk < N) ? seg_dh[(bp * D + d) * N + kk] : 0.f;
-            dh_next[s] = __expf(A[s] * dts) * dh_next[s] + he;
+            dh_next[s] = fmaf(exp2_sfu(A2[s] * dts), dh_next[s], he);
         }
     }
     float dD_acc = 0.f;
@@ -389,82 +502,97 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) scan_bwd_kernel(
     for (int k = k_end - 1; k >= k_begin; --k) {
         const int buf = k & 1, t0 = k * TC;
         stage(buf, t0);
+        float h_start[S], as[S][TC], hs[S][TC];
+#pragma unroll
+        for (int s = 0; s < S; ++s) h_start[s] = ph[s];
         __syncthreads();
         if (k > k_begin) fetch(t0 - TC);
-        // the chunk's states, recomputed from the ones saved at its start. Steps past T
-        // were staged as dt = u = B = C = dy = 0: h and dh pass through them unchanged and
-        // they add nothing to dA, dD, dB or dC; their du and ddt are not stored.
-        float h_start[S], hs[S][TC];
+        // The chunk's decays and states, recomputed from the state saved at its start. Steps
+        // past T were staged as dt = dt u = B = C = dy = 0: h and dh pass through them
+        // unchanged and they add nothing to dA, dD, dB or dC; their du and ddt are not stored.
 #pragma unroll
-        for (int s = 0; s < S; ++s) {
-            const int kk = n * S + s;
-            h_start[s] = (chan && kk < N) ? hchk[(((long long)b * nch + k) * D + d) * N + kk] : 0.f;
-            float h = h_start[s];
+        for (int i = 0; i < TC; ++i) {
+            const float2 dd = sDU[buf][i][c];
+            float bv[S];
+            load_states<S>(&sB[buf][i][n * S], bv);
 #pragma unroll
-            for (int i = 0; i < TC; ++i) {
-                const float dt = sDt[buf][i][c];
-                h = __expf(A[s] * dt) * h + sB[buf][i][n * S + s] * sU[buf][i][c] * dt;
-                hs[s][i] = h;
+            for (int s = 0; s < S; ++s) {
+                as[s][i] = exp2_sfu(A2[s] * dd.x);
+                hs[s][i] = fmaf(as[s][i], i > 0 ? hs[s][i - 1] : h_start[s], bv[s] * dd.y);
             }
         }
-        // the reverse pass in two halves of the chunk, each reduced over the lanes at its end
-        constexpr int HS = TC / 2;
-        using SP = LaneSplit<L, HS>;
+        // the reverse recurrence; per-lane G and H of every step, dB/dC terms per state
+        float gl[TC], hl[TC];
 #pragma unroll
-        for (int half = 1; half >= 0; --half) {
-            float du_c[HS], ddt_c[HS];
+        for (int i = TC - 1; i >= 0; --i) {
+            const float2 dd = sDU[buf][i][c];
+            const float2 gu = sGU[buf][i][c];
+            float gs = 0.f, hsum = 0.f, tb[S], tc[S];
+            float bv[S], cv[S];
+            load_states<S>(&sB[buf][i][n * S], bv);
+            load_states<S>(&sC[buf][i][n * S], cv);
 #pragma unroll
-            for (int j = HS - 1; j >= 0; --j) {
-                const int i = half * HS + j;
-                const float dyv = sDy[buf][i][c], uu = sU[buf][i][c], dt_t = sDt[buf][i][c];
-                float du_s = 0.f, ddt_s = 0.f;
-#pragma unroll
-                for (int s = 0; s < S; ++s) {
-                    const float Bv = sB[buf][i][n * S + s], Cv = sC[buf][i][n * S + s];
-                    const float a_t = __expf(A[s] * dt_t);
-                    const float h_t = hs[s][i];
-                    const float h_prev = i > 0 ? hs[s][i - 1] : h_start[s];
-                    const float dh = dh_next[s] + dyv * Cv;
-                    sPC[i][c][n * S + s] = dyv * h_t;
-                    sPB[i][c][n * S + s] = dh * uu * dt_t;
-                    du_s += dh * Bv * dt_t;
-                    ddt_s += dh * h_prev * a_t * A[s] + dh * Bv * uu;
-                    dA_acc[s] += dh * h_prev * a_t * dt_t;
-                    dh_next[s] = dh * a_t;
-                }
-                du_c[j] = du_s;
-                ddt_c[j] = ddt_s;
-                dD_acc += dyv * uu;
+            for (int s = 0; s < S; ++s) {
+                const float Bv = bv[s], Cv = cv[s];
+                const float h_prev = i > 0 ? hs[s][i - 1] : h_start[s];
+                const float dh = fmaf(gu.x, Cv, dh_next[s]);
+                tb[s] = dh * dd.y;        // dB term
+                tc[s] = gu.x * hs[s][i];  // dC term
+                gs = fmaf(dh, Bv, gs);
+                dh_next[s] = dh * as[s][i];
+                const float x = dh_next[s] * h_prev;
+                hsum = fmaf(x, A[s], hsum);
+                dA_acc[s] = fmaf(x, dd.x, dA_acc[s]);
             }
-            lane_reduce_scatter<L, HS>(du_c, n);
-            lane_reduce_scatter<L, HS>(ddt_c, n);
+            // [channel][state] rows: a warp's lanes store 32 consecutive floats (S = 1) or
+            // 8-byte pairs (S = 2), conflict-free either way
+            store_states<S>(&sP[0][i][c * NS + n * S], tb);
+            store_states<S>(&sP[1][i][c * NS + n * S], tc);
+            gl[i] = gs;
+            hl[i] = hsum;
+        }
 #pragma unroll
-            for (int j = 0; j < SP::kPer; ++j) {
-                const int i = half * HS + (n / SP::kGroup) * SP::kPer + j;
-                if (chan && n % SP::kGroup == 0 && t0 + i < T) {
-                    const long long row = (long long)b * T + t0 + i;
-                    du[row * D + d] = du_c[j] + sDy[buf][i][c] * Ds;
-                    draw[row * D + d] = ddt_c[j] * sDf[buf][i][c];
-                }
+        for (int i = 0; i < TC; ++i) sRed[warp][i][lane] = make_float2(gl[i], hl[i]);
+        __syncwarp();
+#pragma unroll
+        for (int jj = 0; jj < KPER; ++jj) {
+            const int j = n + L * jj;
+            float gp[L], hp[L];
+#pragma unroll
+            for (int m = 0; m < L; ++m) {
+                const float2 v = sRed[warp][j][ch * L + m];
+                gp[m] = v.x;
+                hp[m] = v.y;
+            }
+            const float gsum = tree_sum<L>(gp), hsum = tree_sum<L>(hp);
+            const float2 dd = sDU[buf][j][c];
+            const float2 gu = sGU[buf][j][c];
+            dD_acc = fmaf(gu.x, gu.y, dD_acc);
+            if (chan && t0 + j < T) {
+                const long long row = (long long)b * T + t0 + j;
+                du[row * D + d] = fmaf(gsum, dd.x, gu.x * Ds);
+                draw[row * D + d] = fmaf(gsum, gu.y, hsum) * sDf[buf][j][c];
             }
         }
         __syncthreads();
         // block partial over its channels (fixed order) -> dbc_part[blockIdx.x][2][B*T][N]
-        for (int kk = tid; kk < TC * N; kk += NT) {
-            const int i = kk / N, nn = kk - i * N;
+#pragma unroll
+        for (int k0 = 0; k0 < 2 * TC * NS; k0 += NT) {
+            const int kk = k0 + tid;
+            const int kind = kk / (TC * NS), i = (kk / NS) % TC, nn = kk % NS;
             const int t = t0 + i;
-            if (t >= T) continue;
-            float sb = 0.f, sc = 0.f;
-            for (int cc = 0; cc < CPB; ++cc) {
-                sb += sPB[i][cc][nn];
-                sc += sPC[i][cc][nn];
-            }
+            if (kk >= 2 * TC * NS || nn >= N || t >= T) continue;
+            float v[CPB];
+#pragma unroll
+            for (int cc = 0; cc < CPB; ++cc) v[cc] = sP[kind][i][cc * NS + nn];
+            const float sum = tree_sum<CPB>(v);
             const long long row = (long long)b * T + t;
-            float* part = dbc_part + (long long)blockIdx.x * 2 * BT * N;
-            part[row * N + nn] = sb;
-            part[BT * N + row * N + nn] = sc;
+            dbc_part[((long long)blockIdx.x * 2 + kind) * BT * N + row * N + nn] = sum;
         }
     }
+    // dD over the channel's lanes (each lane summed its own steps)
+#pragma unroll
+    for (int o = L / 2; o >= 1; o >>= 1) dD_acc += __shfl_xor_sync(0xffffffffu, dD_acc, o);
     // per (sequence, segment) partials [B * nseg][D][N] and [B * nseg][D]
     const long long bs = (long long)b * nseg + seg;
 #pragma unroll
@@ -492,11 +620,11 @@ __global__ void __launch_bounds__(kScanWarps * 32) scan_bwd_carry_kernel(
     const int d0 = blockIdx.x * CPB, d = d0 + c;
     const int b = blockIdx.y;
     const bool chan = d < D;
-    float A[S];
+    float A2[S];
 #pragma unroll
     for (int s = 0; s < S; ++s) {
         const int k = n * S + s;
-        A[s] = (chan && k < N) ? alog[(long long)d * N + k] : 0.f;
+        A2[s] = (chan && k < N) ? alog[(long long)d * N + k] * kLog2e : 0.f;
     }
     const int nch = (T + TC - 1) / TC;
     float pr[EPT], pg[EPT], pz[EPT], pc[BPT];
@@ -523,7 +651,7 @@ __global__ void __launch_bounds__(kScanWarps * 32) scan_bwd_carry_kernel(
         for (int e = 0; e < EPT; ++e) {
             const int idx = tid + e * NT, i = idx / CPB, cc = idx % CPB;
             const bool ok = t0 + i < T && d0 + cc < D;
-            sDt[buf][i][cc] = ok ? clamp_dt(softplus_f(pr[e])) : 0.f;
+            sDt[buf][i][cc] = ok ? dt_of(pr[e]).dt : 0.f;
             sDy[buf][i][cc] = pg[e] * silu_f(pz[e]);
         }
 #pragma unroll
@@ -551,7 +679,7 @@ __global__ void __launch_bounds__(kScanWarps * 32) scan_bwd_carry_kernel(
             dtsum += dt;
 #pragma unroll
             for (int s = 0; s < S; ++s)
-                dh_next[s] = (dh_next[s] + dyv * sC[buf][i][n * S + s]) * __expf(A[s] * dt);
+                dh_next[s] = fmaf(dyv, sC[buf][i][n * S + s], dh_next[s]) * exp2_sfu(A2[s] * dt);
         }
     }
     const long long bp = (long long)b * nseg + seg;
@@ -870,7 +998,15 @@ int launch_scan_bwd(const MambaDims& m, const float* raw, const float* u, const 
         int rc = launch_status();
         if (rc) return rc;
     }
-    scan_bwd_kernel<L, S><<<grid, kScanWarps * 32, 0, s>>>(
+    constexpr size_t smem = ScanBwdSmem<L, S>::kBytes;
+    static bool attr = false;  // per instantiation
+    if (!attr) {
+        const cudaError_t e = cudaFuncSetAttribute(
+            scan_bwd_kernel<L, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return -(1000 + (int)e);
+        attr = true;
+    }
+    scan_bwd_kernel<L, S><<<grid, kScanWarps * 32, smem, s>>>(
         raw, u, xp, m.ldx, alog, dskip, proj, m.ldp, y32, dgated, hchk, du, draw, dproj, dbc_part,
         da_part, dd_part, seg_dh, seg_dt, m.T, m.D, m.N, m.R);
     return launch_status();
