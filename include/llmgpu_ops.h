@@ -92,9 +92,15 @@ int llmgpu_op_cross_entropy(void* logits_bf16, int rows, int V, int Vp, const in
  * and dQ/dK are returned for the unrotated inputs. */
 int llmgpu_op_attention_fwd(const void* qkv, void* out, float* lse, int B, int T, int H, int hd,
                             const float* rope_cs, void* stream);
+/* The same forward with the backward's workspace (llmgpu_op_attention_bwd_work bytes): a
+ * head_dim below 64 (a multiple of 8) then also runs on the tcgen05 kernel, its heads
+ * zero-padded to 64 in the workspace (and rotated there when rope_cs is given). */
+int llmgpu_op_attention_fwd_ws(const void* qkv, void* out, float* lse, int B, int T, int H,
+                               int hd, const float* rope_cs, void* work, void* stream);
 /* The backward's `work` must hold llmgpu_op_attention_bwd_work(B, T, H, hd) bytes (the dS
- * tiles that the dK/dV kernel stores and the dQ kernel reads; 0 bytes when head_dim or the
- * rotation keep it off the tcgen05 kernels), 256-byte aligned. */
+ * tiles that the dK/dV kernel stores and the dQ kernel reads, and for a head_dim below 64 the
+ * zero-padded heads; 0 bytes when head_dim keeps it off the tcgen05 kernels), 256-byte
+ * aligned. */
 int llmgpu_op_attention_bwd(const void* qkv, const void* out, const void* dout, const float* lse,
                             float* dvec, void* dqkv, int B, int T, int H, int hd,
                             const float* rope_cs, void* work, void* stream);

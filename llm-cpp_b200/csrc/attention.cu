@@ -594,14 +594,129 @@ void set_smem(K kernel, int bytes) {
 
 }  // namespace
 
+namespace {
+// Heads of width hd < 64 as 64-wide heads for the tcgen05 kernels (attention_tc.cu): rows of
+// `parts` x H heads, [B*T][parts*H*hd] <-> [B*T][parts*H*64], zeros in dims hd..63. A thread
+// moves 8 consecutive dims (16 bytes) of one head. With `rope` ([T][hd/2] (cos, sin)), the
+// q and k parts (0 and 1) are rotated per pair (2j, 2j+1) on the way: forward when padding,
+// the transposed rotation when unpadding (gradients with respect to rotated q / k).
+constexpr int kPadHD = 64;
+
+__device__ __forceinline__ void rope8(float (&v)[8], const float2* tab, int t, int hd, int j0,
+                                      bool inverse) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float2 cs = tab[(long long)t * (hd / 2) + j0 + k];
+        const float sn = inverse ? -cs.y : cs.y;
+        const float x = v[2 * k], y = v[2 * k + 1];
+        v[2 * k] = x * cs.x - y * sn;
+        v[2 * k + 1] = x * sn + y * cs.x;
+    }
+}
+
+__global__ void pad_heads_kernel(const bf16* __restrict__ src, bf16* __restrict__ dst,
+                                 long long rows, int parts, int H, int hd, int T,
+                                 const float2* __restrict__ rope) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    const int per_row = parts * H * (kPadHD / 8);
+    if (i >= rows * per_row) return;
+    const long long row = i / per_row;
+    const int r = (int)(i - row * per_row);
+    const int c8 = r % (kPadHD / 8), head = r / (kPadHD / 8);  // head over parts * H
+    uint4 w = make_uint4(0u, 0u, 0u, 0u);
+    if (c8 * 8 < hd) {
+        w = *reinterpret_cast<const uint4*>(src + row * parts * H * hd + (long long)head * hd +
+                                            c8 * 8);
+        if (rope && head < 2 * H) {
+            const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+            float v[8];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                v[2 * k] = bf16_lo(u[k]);
+                v[2 * k + 1] = bf16_hi(u[k]);
+            }
+            rope8(v, rope, (int)(row % T), hd, c8 * 4, false);
+            w = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                           pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+        }
+    }
+    *reinterpret_cast<uint4*>(dst + row * parts * H * kPadHD + (long long)head * kPadHD +
+                              c8 * 8) = w;
+}
+
+__global__ void unpad_heads_kernel(const bf16* __restrict__ src, bf16* __restrict__ dst,
+                                   long long rows, int parts, int H, int hd, int T,
+                                   const float2* __restrict__ rope) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    const int per_row = parts * H * (hd / 8);
+    if (i >= rows * per_row) return;
+    const long long row = i / per_row;
+    const int r = (int)(i - row * per_row);
+    const int c8 = r % (hd / 8), head = r / (hd / 8);
+    uint4 w = *reinterpret_cast<const uint4*>(src + row * parts * H * kPadHD +
+                                              (long long)head * kPadHD + c8 * 8);
+    if (rope && head < 2 * H) {
+        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            v[2 * k] = bf16_lo(u[k]);
+            v[2 * k + 1] = bf16_hi(u[k]);
+        }
+        rope8(v, rope, (int)(row % T), hd, c8 * 4, true);
+        w = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                       pack_bf16x2(v[6], v[7]));
+    }
+    *reinterpret_cast<uint4*>(dst + row * parts * H * hd + (long long)head * hd + c8 * 8) = w;
+}
+
+bool pad_path(int hd) { return hd < kPadHD && hd >= 8 && hd % 8 == 0; }
+
+size_t pad_unit_bytes(int B, int T, int H) {  // one [B*T][H*64] bf16 plane, 256-byte multiple
+    return ((size_t)B * T * H * kPadHD * sizeof(bf16) + 255) / 256 * 256;
+}
+
+int pad_heads(const bf16* src, bf16* dst, int B, int T, int parts, int H, int hd,
+              const float2* rope, cudaStream_t s) {
+    const long long n = (long long)B * T * parts * H * (kPadHD / 8);
+    return launch_kernel(pad_heads_kernel, (unsigned)((n + 255) / 256), 256, 0, s, src, dst,
+                         (long long)B * T, parts, H, hd, T, rope);
+}
+
+int unpad_heads(const bf16* src, bf16* dst, int B, int T, int parts, int H, int hd,
+                const float2* rope, cudaStream_t s) {
+    const long long n = (long long)B * T * parts * H * (hd / 8);
+    return launch_kernel(unpad_heads_kernel, (unsigned)((n + 255) / 256), 256, 0, s, src, dst,
+                         (long long)B * T, parts, H, hd, T, rope);
+}
+}  // namespace
+
+size_t attention_work_bytes(int B, int T, int H, int hd) {
+    const size_t ds = (attention_ds_bytes(B, T, H) + 255) / 256 * 256;
+    return pad_path(hd) ? ds + 7 * pad_unit_bytes(B, T, H) : ds;
+}
+
 int attention_forward(const bf16* qkv, bf16* out, float* lse, int B, int T, int H, int hd,
-                      const float2* rope, cudaStream_t s, int* err) {
+                      const float2* rope, cudaStream_t s, int* err, void* work) {
     const float scale = 1.0f / sqrtf((float)hd);
     dim3 grid((T + BLK - 1) / BLK, H, B);
     if (hd == 64 && !rope) {
         CUtensorMap tm;
         if (attention_qkv_tmap(&tm, qkv, B, T, H * hd)) return -2;
-        return attention_forward_tc(tm, out, lse, B, T, H, hd, err, s);
+        return attention_forward_tc(tm, out, lse, B, T, H, hd, scale, err, s);
+    }
+    if (pad_path(hd) && work) {
+        // [q|k|v] and the output as 64-wide heads, after the dS region of the workspace
+        const size_t unit = pad_unit_bytes(B, T, H);
+        char* base = static_cast<char*>(work) + (attention_ds_bytes(B, T, H) + 255) / 256 * 256;
+        bf16* qkv64 = reinterpret_cast<bf16*>(base);
+        bf16* out64 = reinterpret_cast<bf16*>(base + 3 * unit);
+        int rc = pad_heads(qkv, qkv64, B, T, 3, H, hd, rope, s);
+        if (rc) return rc;
+        CUtensorMap tm;
+        if (attention_qkv_tmap(&tm, qkv64, B, T, H * kPadHD)) return -2;
+        if ((rc = attention_forward_tc(tm, out64, lse, B, T, H, kPadHD, scale, err, s))) return rc;
+        return unpad_heads(out64, out, B, T, 1, H, hd, nullptr, s);
     }
     if (hd == 64) {
         const int smem = 5 * BLK * 64 * 2;
@@ -670,8 +785,24 @@ int attention_backward(const bf16* qkv, const bf16* out, const bf16* dout, const
         const int rc = launch_status();
         if (rc) return rc;
         if (!ds_work) return -5;  // the tcgen05 kernels need the dS scratch
-        return attention_backward_tc(qkv, dout, lse, dvec, dqkv, B, T, H, hd, ds_work, err, s,
-                                     rope_back);
+        return attention_backward_tc(qkv, dout, lse, dvec, dqkv, B, T, H, hd, scale, ds_work, err,
+                                     s, rope_back);
+    }
+    if (pad_path(hd) && (T % 4) == 0 && ds_work) {
+        int rc = launch_status();
+        if (rc) return rc;
+        const size_t unit = pad_unit_bytes(B, T, H);
+        char* base = static_cast<char*>(ds_work) + (attention_ds_bytes(B, T, H) + 255) / 256 * 256;
+        bf16* qkv64 = reinterpret_cast<bf16*>(base);
+        bf16* dout64 = reinterpret_cast<bf16*>(base + 3 * unit);
+        bf16* dqkv64 = reinterpret_cast<bf16*>(base + 4 * unit);
+        if ((rc = pad_heads(qkv, qkv64, B, T, 3, H, hd, rope, s)) ||
+            (rc = pad_heads(dout, dout64, B, T, 1, H, hd, nullptr, s)) ||
+            (rc = attention_backward_tc(qkv64, dout64, lse, dvec, dqkv64, B, T, H, kPadHD, scale,
+                                        ds_work, err, s, nullptr)))
+            return rc;
+        // dq and dk rotate back with the table q and k were rotated by
+        return unpad_heads(dqkv64, dqkv, B, T, 3, H, hd, rope ? rope : rope_back, s);
     }
     dim3 grid((T + BLK - 1) / BLK, H, B);
     if (hd == 64) {

@@ -1,13 +1,13 @@
 // Causal flash attention forward on the 5th-generation tensor cores (head_dim 64).
 //
-// One CTA per (128-query tile, head, sequence), two CTAs per SM; 192 threads:
+// One CTA per (128-query tile, head, sequence), two CTAs per SM; 320 threads:
 //   warp 0     TMA producer: the Q tile once, then K and V tiles of 128 keys through two
 //              independent 2-deep rings (a K slot frees when its QK^T MMA is done, a V slot
 //              when its PV MMA is done)
 //   warp 1     TMEM allocator + MMA issuer: S_j = Q K_j^T into TMEM, then O += P_{j-1} V_{j-1}
 //              with P read straight from TMEM (the A-from-TMEM form of tcgen05.mma)
-//   warps 2-5  softmax: one query row per thread; warp w reads TMEM lanes 32*(w%4).. (the
-//              lane quarter a warp may access). Reads S_j, masks, keeps the
+//   warps 2-9  softmax: a query row per two threads (column half (w - 2) / 4); warp w reads
+//              TMEM lanes 32*(w%4).. (the lane quarter a warp may access). Reads S_j, masks, keeps the
 //              running max / sum in base 2, writes P_j (bf16 pairs) into TMEM, and rescales O
 //              in TMEM only when a row's running max grows by more than 2^8 (otherwise the
 //              stale max is kept: the final O / l is exact either way). At the end it writes
@@ -77,8 +77,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 1);
 
     const int nqb = (T + kRows - 1) / kRows;
-    const int qb = nqb - 1 - (int)blockIdx.x;    // longest (most keys) tiles first
-    const int h = blockIdx.y, b = blockIdx.z;
+    // blocks launch in x-fastest order: all (head, sequence) pairs of the longest query tile
+    // (most keys) first, the shortest last, so the last wave holds the shortest tiles
+    const int qb = nqb - 1 - (int)blockIdx.y;
+    const int h = (int)blockIdx.x % H, b = (int)blockIdx.x / H;
     const int C = H * kHD;
     const int q0 = qb * kRows;
     const int nkv = qb + 1;                      // causal: key tiles 0..qb
@@ -861,7 +863,7 @@ int attention_qkv_tmap(CUtensorMap* tm, const bf16* qkv, int B, int T, int C) {
 }
 
 int attention_forward_tc(const CUtensorMap& tm, bf16* out, float* lse, int B, int T, int H, int hd,
-                         int* err, cudaStream_t s) {
+                         float scale, int* err, cudaStream_t s) {
     if (hd != kHD || B <= 0 || T <= 0 || H <= 0) return -1;
     static int attr = -1;
     static std::once_flag once;
@@ -872,9 +874,9 @@ int attention_forward_tc(const CUtensorMap& tm, bf16* out, float* lse, int B, in
                    : -3;
     });
     if (attr) return attr;
-    const dim3 grid((T + kRows - 1) / kRows, H, B);
+    const dim3 grid(H * B, (T + kRows - 1) / kRows);
     return launch_kernel(attn_fwd_tc_kernel, grid, kThreads, kSmemBytes, s, tm, out, lse, T, H,
-                         1.4426950408889634f / sqrtf((float)hd), err);
+                         scale * kLog2ef, err);
 }
 
 namespace {
@@ -900,8 +902,8 @@ size_t attention_ds_bytes(int B, int T, int H) {
 }
 
 int attention_backward_tc(const bf16* qkv, const bf16* dout, const float* lse, const float* dvec,
-                          bf16* dqkv, int B, int T, int H, int hd, void* ds_work, int* err,
-                          cudaStream_t s, const float2* rope_back) {
+                          bf16* dqkv, int B, int T, int H, int hd, float scale, void* ds_work,
+                          int* err, cudaStream_t s, const float2* rope_back) {
     if (hd != kHD || B <= 0 || T <= 0 || H <= 0 || (T % 4) != 0 || !ds_work) return -1;
     const int C = H * hd;
     CUtensorMap tq, tdo, tl, td, tds_st, tds_ld;
@@ -949,7 +951,6 @@ int attention_backward_tc(const bf16* qkv, const bf16* dout, const float* lse, c
                    : -3;
     });
     if (attr) return attr;
-    const float scale = 1.0f / sqrtf((float)hd);
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -61,7 +61,7 @@ int validate_bt(Ctx* c, int B, int T) {
 
 int enqueue_step(Ctx* c, int B, int T, int accumulate, bool do_step, int K) {
     if (c->comm_failed) {
-        c->err = "the communicator was aborted after an earlier collective failure";
+        c->err = "the communicator was aborted (a collective failed or a peer is gone)";
         return LLMGPU_E_NCCL;
     }
     c->plan_cursor = 0;
@@ -112,7 +112,7 @@ void capture_step(Ctx* c, int B, int T, int accumulate, bool do_step, int K) {
 // Runs one micro-batch (+ optimizer when `do_step`), eagerly or through the step graph.
 int run_step(Ctx* c, int B, int T, int accumulate, bool do_step, int K) {
     if (c->comm_failed) {  // a captured step would replay collectives of the aborted communicator
-        c->err = "the communicator was aborted after an earlier collective failure";
+        c->err = "the communicator was aborted (a collective failed or a peer is gone)";
         return LLMGPU_E_NCCL;
     }
     cudaMemsetAsync(c->d_out + 1, 0, sizeof(float) * 4, c->stream);
@@ -573,6 +573,19 @@ int llmgpu_set_comm_timeout(llmgpu_ctx* h, double seconds) {
     if (check_ctx(h) || !(seconds > 0.0)) return LLMGPU_E_ARG;
     h->c->comm_timeout_s = seconds;
     return 0;
+}
+
+int llmgpu_abort_comm(llmgpu_ctx* h) {
+    if (check_ctx(h)) return LLMGPU_E_ARG;
+    Ctx* c = h->c;
+    if (!c->nccl) return 0;
+    int rc = wait_stream(c, c->stream);  // aborts by itself if the wait runs out
+    if (rc == 0 && c->comm) rc = wait_stream(c, c->comm);
+    if (c->nccl) {
+        abort_comm(c);
+        c->err = "communicator aborted on request (a peer rank is gone)";
+    }
+    return rc ? LLMGPU_E_NCCL : 0;
 }
 
 int llmgpu_set_graph(llmgpu_ctx* h, int enable) {

@@ -821,24 +821,48 @@ __device__ __forceinline__ PairShape pair_shape(const GemmArgs& a) {
     return s;
 }
 
-// Item i of cluster cid's work: product g, tile t of that product (split-major).
+// The work items of cluster cid in order: product g, tile t of that product (split-major).
+// With two products the items come from the cluster's list in the host-built table; the
+// entry of the next item is loaded while the current one is processed, so no role waits on
+// a global load at a tile boundary.
 template <int NG>
-__device__ __forceinline__ bool pair_item(const PairParams<NG>& P, int cid, int nclusters, int i,
-                                          int& g, int& t) {
-    if constexpr (NG == 1) {
-        const PairShape s = pair_shape(P.args[0]);
-        g = 0;
-        t = cid + i * nclusters;
-        return t < s.tiles_mn * P.args[0].splits;
-    } else {
-        const int* l = P.sched + (size_t)cid * P.sched_stride;
-        if (i >= l[0]) return false;
-        const int v = l[1 + i];
-        g = v >> 24;
-        t = v & 0xffffff;
-        return true;
+struct PairItems {
+    const int* list;
+    int n, i, next;
+    int cid, nclusters, total;
+    __device__ __forceinline__ PairItems(const PairParams<NG>& P, int cid_, int ncl) {
+        cid = cid_;
+        nclusters = ncl;
+        i = 0;
+        if constexpr (NG == 1) {
+            const PairShape s = pair_shape(P.args[0]);
+            total = s.tiles_mn * P.args[0].splits;
+            list = nullptr;
+            n = next = 0;
+        } else {
+            total = 0;
+            list = P.sched + (size_t)cid * P.sched_stride;
+            n = list[0];
+            next = n > 0 ? list[1] : 0;
+        }
     }
-}
+    __device__ __forceinline__ bool get(int& g, int& t) {
+        if constexpr (NG == 1) {
+            g = 0;
+            t = cid + i * nclusters;
+            ++i;
+            return t < total;
+        } else {
+            if (i >= n) return false;
+            const int v = next;
+            if (i + 1 < n) next = list[2 + i];
+            ++i;
+            g = v >> 24;
+            t = v & 0xffffff;
+            return true;
+        }
+    }
+};
 
 template <int NG>
 __global__ void __launch_bounds__(kPairThreads, 1)
@@ -908,7 +932,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             uint32_t phase = 0;
             bool ok = true;
             int g, t;
-            for (int i = 0; ok && pair_item(P, cid, nclusters, i, g, t); ++i) {
+            PairItems<NG> items(P, cid, nclusters);
+            while (ok && items.get(g, t)) {
                 const GemmArgs& args = P.args[g];
                 const PairShape sh = pair_shape(args);
                 const CUtensorMap* tmA = &P.tmA[g];
@@ -963,7 +988,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             uint32_t acc_phase = 0;
             bool ok = true;
             int g, t;
-            for (int i = 0; ok && pair_item(P, cid, nclusters, i, g, t); ++i) {
+            PairItems<NG> items(P, cid, nclusters);
+            while (ok && items.get(g, t)) {
                 const GemmArgs& args = P.args[g];
                 const PairShape sh = pair_shape(args);
                 const uint32_t idesc =
@@ -1023,7 +1049,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         int g, t;
-        for (int i = 0; pair_item(P, cid, nclusters, i, g, t); ++i) {
+        PairItems<NG> items(P, cid, nclusters);
+        while (items.get(g, t)) {
             const GemmArgs& args = P.args[g];
             const PairShape sh = pair_shape(args);
             int m_blk, n_blk, split, gi, kb0, kb1;
@@ -1433,40 +1460,61 @@ int gemm_pair_slots(int num_sms) { return pair_max_clusters(num_sms); }
 // resident pairs: each tile, longest first, goes to the pair with the least work so far
 // (ties: the lower pair), and every pair runs its tiles in the order they were given.
 // Cost of a tile: its k-blocks plus 4 for pipeline fill and epilogue.
-int gemm_make_plan2(GemmPlan2* plan, const GemmPlan& p0, const GemmPlan& p1, int num_sms) {
-    plan->sched = nullptr;
-    const GemmPlan* ps[2] = {&p0, &p1};
-    struct Unit {
-        int cost, g, t;
-    };
-    std::vector<Unit> units;
-    for (int g = 0; g < 2; ++g) {
-        const GemmArgs& a = ps[g]->args;
-        if (ps[g]->bn != kGemmPairTile || a.grp_mode != kGroupNone) return -50;
-        const int num_m = (a.M + PairCfg::BMP - 1) / PairCfg::BMP;
-        const int num_n = (a.N + PairCfg::BN - 1) / PairCfg::BN;
-        const int kblocks = (a.K + BK - 1) / BK;
-        const int tiles = num_m * num_n * a.splits;
-        if (tiles >= (1 << 24)) return -51;
-        for (int t = 0; t < tiles; ++t) {
-            const int split = t / (num_m * num_n);
-            const int kb0 = (int)((long long)split * kblocks / a.splits);
-            const int kb1 = (int)((long long)(split + 1) * kblocks / a.splits);
-            units.push_back(Unit{kb1 - kb0 + 4, g, t});
-        }
+namespace {
+
+int pair_tile_cost(int kblocks) { return kblocks + 4; }
+
+struct PairUnit {
+    int cost, g, t;
+};
+
+// Units of one product on pair tiles, `splits` ways over K.
+void pair_units(std::vector<PairUnit>& units, int g, int M, int N, int K, int splits) {
+    const int num_m = (M + PairCfg::BMP - 1) / PairCfg::BMP;
+    const int num_n = (N + PairCfg::BN - 1) / PairCfg::BN;
+    const int kblocks = (K + BK - 1) / BK;
+    const int tiles = num_m * num_n * splits;
+    for (int t = 0; t < tiles; ++t) {
+        const int split = t / (num_m * num_n);
+        const int kb0 = (int)((long long)split * kblocks / splits);
+        const int kb1 = (int)((long long)(split + 1) * kblocks / splits);
+        units.push_back(PairUnit{pair_tile_cost(kb1 - kb0), g, t});
     }
+}
+
+// Longest-first assignment of `units` to `ncl` pairs; returns the largest pair load.
+long long pair_lpt(std::vector<PairUnit>& units, int ncl, std::vector<std::vector<int>>* lists) {
     std::stable_sort(units.begin(), units.end(),
-                     [](const Unit& x, const Unit& y) { return x.cost > y.cost; });
-    const int ncl = std::min<int>(pair_max_clusters(num_sms), (int)units.size());
-    std::vector<std::vector<int>> lists(ncl);
+                     [](const PairUnit& x, const PairUnit& y) { return x.cost > y.cost; });
     std::vector<long long> load(ncl, 0);
-    for (const Unit& u : units) {
+    if (lists) lists->assign(ncl, {});
+    for (const PairUnit& u : units) {
         int best = 0;
         for (int c = 1; c < ncl; ++c)
             if (load[c] < load[best]) best = c;
         load[best] += u.cost;
-        lists[best].push_back((u.g << 24) | u.t);
+        if (lists) (*lists)[best].push_back((u.g << 24) | u.t);
     }
+    return *std::max_element(load.begin(), load.end());
+}
+
+}  // namespace
+
+int gemm_make_plan2(GemmPlan2* plan, const GemmPlan& p0, const GemmPlan& p1, int num_sms) {
+    plan->sched = nullptr;
+    const GemmPlan* ps[2] = {&p0, &p1};
+    std::vector<PairUnit> units;
+    for (int g = 0; g < 2; ++g) {
+        const GemmArgs& a = ps[g]->args;
+        if (ps[g]->bn != kGemmPairTile || a.grp_mode != kGroupNone) return -50;
+        const long long tiles = (long long)((a.M + PairCfg::BMP - 1) / PairCfg::BMP) *
+                                ((a.N + PairCfg::BN - 1) / PairCfg::BN) * a.splits;
+        if (tiles >= (1 << 24)) return -51;
+        pair_units(units, g, a.M, a.N, a.K, a.splits);
+    }
+    const int ncl = std::min<int>(pair_max_clusters(num_sms), (int)units.size());
+    std::vector<std::vector<int>> lists;
+    pair_lpt(units, ncl, &lists);
     size_t stride = 1;
     for (const auto& l : lists) stride = std::max(stride, l.size() + 1);
     std::vector<int> table((size_t)ncl * stride, 0);

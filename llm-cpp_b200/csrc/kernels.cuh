@@ -68,14 +68,17 @@ int mean_reduce(const float* v, int n, float* out, cudaStream_t s);
 // src/attention.cpp:35-102 / src/flash_attention.cpp:88-123.
 // rope (nullable): [T][hd/2] (cos, sin) table; when given, Q and K are rotated per head as
 // they are loaded and dQ/dK are rotated back before they are stored.
-// head_dim 64 without a fused rope runs on the tcgen05 kernel (attention_tc.cu); err
-// (nullable) receives the device error code of a timed-out wait.
+// head_dim 64 without a fused rope runs on the tcgen05 kernel (attention_tc.cu); so does a
+// head_dim below 64 (a multiple of 8) when `work` is given (attention_work_bytes): the heads
+// are zero-padded to 64 (rope, if any, applied while padding), which leaves scores and
+// outputs unchanged. err (nullable) receives the device error code of a timed-out wait.
 int attention_forward(const bf16* qkv, bf16* out, float* lse, int B, int T, int H, int hd,
-                      const float2* rope, cudaStream_t s, int* err = nullptr);
+                      const float2* rope, cudaStream_t s, int* err = nullptr,
+                      void* work = nullptr);
 // tcgen05 forward (head_dim 64) on a tensor map made by attention_qkv_tmap
 int attention_qkv_tmap(CUtensorMap* tm, const bf16* qkv, int B, int T, int C);
 int attention_forward_tc(const CUtensorMap& tm, bf16* out, float* lse, int B, int T, int H, int hd,
-                         int* err, cudaStream_t s);
+                         float scale, int* err, cudaStream_t s);
 // In-place RoPE of the q and k parts of qkv [B*T, 3C] (pairs 2j, 2j+1 of every head, table
 // [T][hd/2] of (cos, sin)); inverse != 0 applies the transposed rotation, which maps
 // gradients with respect to rotated q / k back to the unrotated ones.
@@ -84,7 +87,9 @@ int rope_qk_inplace(bf16* qkv, int B, int T, int H, int hd, const float2* rope, 
 // Backward: dqkv [B*T, 3C] bf16 from dout [B*T, C]; dvec [B, H, T] fp32 scratch.
 // src/attention.cpp:183-363.
 // head_dim 64 without a fused rope and T % 4 == 0 runs on the tcgen05 kernels, which need
-// ds_work: attention_ds_bytes(B, T, H) bytes of scratch for the dS tiles.
+// ds_work: attention_ds_bytes(B, T, H) bytes of scratch for the dS tiles; a head_dim below 64
+// (a multiple of 8) with T % 4 == 0 runs there too, zero-padded, when ds_work holds
+// attention_work_bytes(B, T, H, hd).
 // rope_back (nullable): q and k in qkv were already rotated by this table ([T][hd/2] (cos, sin));
 // dq and dk are rotated back before they are written.
 int attention_backward(const bf16* qkv, const bf16* out, const bf16* dout, const float* lse,
@@ -92,9 +97,11 @@ int attention_backward(const bf16* qkv, const bf16* out, const bf16* dout, const
                        cudaStream_t s, int* err = nullptr, void* ds_work = nullptr,
                        const float2* rope_back = nullptr);
 size_t attention_ds_bytes(int B, int T, int H);
+// dS tiles plus, for head_dim below 64, the zero-padded q|k|v, dout and dq|dk|dv
+size_t attention_work_bytes(int B, int T, int H, int hd);
 int attention_backward_tc(const bf16* qkv, const bf16* dout, const float* lse, const float* dvec,
-                          bf16* dqkv, int B, int T, int H, int hd, void* ds_work, int* err,
-                          cudaStream_t s, const float2* rope_back = nullptr);
+                          bf16* dqkv, int B, int T, int H, int hd, float scale, void* ds_work,
+                          int* err, cudaStream_t s, const float2* rope_back = nullptr);
 
 // ----------------------------------------------------------------- SwiGLU FFN
 // gated[r, j] = silu(h13[r, j]) * h13[r, F + j]   (src/transformer.cpp:22-30)

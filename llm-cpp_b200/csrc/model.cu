@@ -28,6 +28,13 @@
 
 namespace llmgpu {
 
+// Ends the communicator for good (its kernels in flight return) and marks the context.
+void abort_comm(Ctx* c) {
+    if (c->nccl) ncclCommAbort(reinterpret_cast<ncclComm_t>(c->nccl));
+    c->nccl = nullptr;
+    c->comm_failed = true;
+}
+
 namespace {
 
 #define CK(x)                                                                  \
@@ -58,12 +65,6 @@ double now_s() {
         .count();
 }
 
-// Ends the communicator for good (its kernels in flight return) and marks the context.
-void abort_comm(Ctx* c) {
-    if (c->nccl) ncclCommAbort(reinterpret_cast<ncclComm_t>(c->nccl));
-    c->nccl = nullptr;
-    c->comm_failed = true;
-}
 
 // The communicator is non-blocking: a call may return ncclInProgress, and the next call may
 // only be made once ncclCommGetAsyncError reports success. Polls up to the context's timeout.
@@ -754,7 +755,8 @@ Ctx* ctx_create(const llmgpu_config& cfg, int max_batch, int max_seq, int rank, 
         dalloc(c, &c->datt, (size_t)BT * C) || dalloc(c, &c->dqkv, (size_t)BT * 3 * C) ||
         dalloc(c, &c->dh, (size_t)BT * FH) || dalloc(c, &c->dvec, (size_t)BT * c->H) ||
         (!c->mamba &&
-         dalloc(c, &c->attn_ds, attention_ds_bytes(max_batch, max_seq, c->H) / sizeof(bf16))) ||
+         dalloc(c, &c->attn_ds,
+                attention_work_bytes(max_batch, max_seq, c->H, c->hd) / sizeof(bf16))) ||
         (c->swiglu && dalloc(c, &c->dact, (size_t)BT * F)) ||
         dalloc(c, &c->partial, (size_t)nparts * 3 * C) ||
         dalloc(c, &c->colwork, colsum_work_floats(F > C ? F : C)))
@@ -1212,9 +1214,11 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
         int rc = gemm(c, a.ln1, C, 0, c->wqkv16[l], 3 * C, 1, BT, 3 * C, C, qa);
         if (rc) return rc;
         if (c->rope && hd == 64) {
-            KC(attention_forward(a.qkv, a.att, a.lse, B, T, H, hd, nullptr, s, c->d_err));
+            KC(attention_forward(a.qkv, a.att, a.lse, B, T, H, hd, nullptr, s, c->d_err,
+                                 c->attn_ds));
         } else {
-            KC(attention_forward(a.qkv, a.att, a.lse, B, T, H, hd, c->rope, s, c->d_err));
+            KC(attention_forward(a.qkv, a.att, a.lse, B, T, H, hd, c->rope, s, c->d_err,
+                                 c->attn_ds));
         }
         GemmArgs r = epi_args(kEpiResidF32, a.y, C);
         r.resid = a.x;

@@ -241,6 +241,7 @@ int ctx_sync_check(Ctx* c);
 // Waits for stream `s` to drain. With a communicator it polls the communicator's
 // asynchronous error state and aborts it at the first error or past comm_timeout_s.
 int wait_stream(Ctx* c, cudaStream_t s);
+void abort_comm(Ctx* c);
 void prepare_step_scalars(Ctx* c, int K);
 int save_binary(Ctx* c, const char* path);
 int load_binary(Ctx* c, const char* path);

@@ -120,6 +120,14 @@ extern "C" int llmgpu_op_attention_fwd(const void* qkv, void* out, float* lse, i
                              reinterpret_cast<cudaStream_t>(stream));
 }
 
+extern "C" int llmgpu_op_attention_fwd_ws(const void* qkv, void* out, float* lse, int B, int T,
+                                          int H, int hd, const float* rope_cs, void* work,
+                                          void* stream) {
+    return attention_forward(reinterpret_cast<const bf16*>(qkv), reinterpret_cast<bf16*>(out), lse,
+                             B, T, H, hd, reinterpret_cast<const float2*>(rope_cs),
+                             reinterpret_cast<cudaStream_t>(stream), nullptr, work);
+}
+
 extern "C" int llmgpu_op_attention_bwd(const void* qkv, const void* out, const void* dout,
                                        const float* lse, float* dvec, void* dqkv, int B, int T,
                                        int H, int hd, const float* rope_cs, void* work,
@@ -132,8 +140,8 @@ extern "C" int llmgpu_op_attention_bwd(const void* qkv, const void* out, const v
 }
 
 extern "C" long long llmgpu_op_attention_bwd_work(int B, int T, int H, int hd) {
-    if (B <= 0 || T <= 0 || H <= 0 || hd != 64) return 0;
-    return (long long)attention_ds_bytes(B, T, H);
+    if (B <= 0 || T <= 0 || H <= 0 || hd > 64 || hd < 8 || hd % 8 != 0) return 0;
+    return (long long)attention_work_bytes(B, T, H, hd);
 }
 
 extern "C" int llmgpu_op_swiglu_fwd(const void* h13, void* gated, int rows, int F, void* stream) {

@@ -32,6 +32,7 @@ SIGS = {
     "llmgpu_set_train": ([c_vp, c_float, c_int, c_float], c_int),
     "llmgpu_set_loss_scale": ([c_vp, c_float], c_int),
     "llmgpu_set_comm_timeout": ([c_vp, ctypes.c_double], c_int),
+    "llmgpu_abort_comm": ([c_vp], c_int),
     "llmgpu_train_step": ([c_vp, P_i32, c_int, c_int, P_f32, P_f32], c_int),
     "llmgpu_train_step_accum": ([c_vp, P_i32, c_int, c_int, P_f32, P_int], c_int),
     "llmgpu_train_step_device": ([c_vp, c_vp, c_int, c_int, P_f32, P_f32], c_int),

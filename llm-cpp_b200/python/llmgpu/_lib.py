@@ -40,6 +40,8 @@ def _declare(lib):
                                             c_vp]
     lib.llmgpu_op_attention_bwd.argtypes = [c_vp] * 6 + [c_int, c_int, c_int, c_int, c_vp, c_vp,
                                                          c_vp]
+    lib.llmgpu_op_attention_fwd_ws.argtypes = [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int,
+                                               c_vp, c_vp, c_vp]
     lib.llmgpu_op_attention_bwd_work.argtypes = [c_int, c_int, c_int, c_int]
     lib.llmgpu_op_attention_bwd_work.restype = c_ll
     lib.llmgpu_op_swiglu_fwd.argtypes = [c_vp, c_vp, c_int, c_int, c_vp]
@@ -52,6 +54,7 @@ def _declare(lib):
                                            c_vp]
     for n in ("llmgpu_op_embed", "llmgpu_op_norm_fwd", "llmgpu_op_norm_bwd",
               "llmgpu_op_cross_entropy", "llmgpu_op_attention_fwd", "llmgpu_op_attention_bwd",
+              "llmgpu_op_attention_fwd_ws",
               "llmgpu_op_swiglu_fwd", "llmgpu_op_swiglu_bwd", "llmgpu_op_gemm_grouped",
               "llmgpu_op_moe_route", "llmgpu_op_moe_dispatch"):
         getattr(lib, n).restype = c_int

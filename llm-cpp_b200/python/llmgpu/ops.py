@@ -127,13 +127,23 @@ def rope_table(T, hd, theta, device):
     return torch.stack([ang.cos(), ang.sin()], -1).float().to(device).contiguous()
 
 
-def attention_fwd(qkv, B, T, H, hd, rope=None):
+def attention_fwd(qkv, B, T, H, hd, rope=None, workspace=True):
+    """Causal attention forward; with `workspace`, a head_dim below 64 runs zero-padded on the
+    tcgen05 kernel (llmgpu_op_attention_fwd_ws), else on the mma.sync kernel."""
     lib = load()
     C = H * hd
     out = torch.empty(B * T, C, dtype=torch.bfloat16, device=qkv.device)
     lse = torch.empty(B, H, T, device=qkv.device)
-    _sync_check(lib.llmgpu_op_attention_fwd(_ptr(qkv), _ptr(out), _ptr(lse), B, T, H, hd,
-                                            _ptr(rope), _stream()), "attention_fwd")
+    if workspace:
+        nbytes = int(lib.llmgpu_op_attention_bwd_work(B, T, H, hd))
+        work = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=qkv.device)
+        rc = lib.llmgpu_op_attention_fwd_ws(_ptr(qkv), _ptr(out), _ptr(lse), B, T, H, hd,
+                                            _ptr(rope), _ptr(work) if nbytes else None,
+                                            _stream())
+    else:
+        rc = lib.llmgpu_op_attention_fwd(_ptr(qkv), _ptr(out), _ptr(lse), B, T, H, hd,
+                                         _ptr(rope), _stream())
+    _sync_check(rc, "attention_fwd")
     return out, lse
 
 

@@ -125,6 +125,13 @@ class Trainer:
         if rc:
             self._err("set_comm_timeout", rc)
 
+    def abort_comm(self):
+        """Ends the communicator between steps once a peer is known to be gone (see
+        llmgpu.dist.PeerWatch); later steps raise LlmgpuError without launching."""
+        rc = self.lib.llmgpu_abort_comm(self.h)
+        if rc:
+            self._err("abort_comm", rc)
+
     def set_graph(self, enable):
         self.lib.llmgpu_set_graph(self.h, int(enable))
 

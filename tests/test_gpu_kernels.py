@@ -132,7 +132,7 @@ def _attn_ref(qkv, B, T, H, hd):
 
 @pytest.mark.parametrize("B,T,H,hd", [(2, 128, 4, 32), (1, 200, 2, 64), (2, 64, 12, 64),
                                       (1, 1024, 2, 64), (3, 33, 1, 32), (3, 300, 3, 64),
-                                      (2, 1024, 12, 64)])
+                                      (2, 1024, 12, 64), (2, 256, 3, 16), (1, 132, 2, 48)])
 def test_attention_forward_backward(cuda, B, T, H, hd):
     from llmgpu import ops
     g = torch.Generator().manual_seed(T * H + hd)
@@ -150,6 +150,19 @@ def test_attention_forward_backward(cuda, B, T, H, hd):
     for part in range(3):
         sl = slice(part * C, (part + 1) * C)
         assert _rel(dqkv[:, sl].float(), want[:, sl]) < 2e-2, part
+
+
+@pytest.mark.parametrize("B,T,H,hd", [(2, 128, 4, 32), (3, 33, 1, 32)])
+def test_attention_padded_heads_match_mma_kernel(cuda, B, T, H, hd):
+    """head_dim 32 on the tcgen05 kernel (heads zero-padded to 64) against the mma.sync
+    kernel on the same inputs: the padded dims add nothing to scores or outputs."""
+    from llmgpu import ops
+    g = torch.Generator().manual_seed(11 + T)
+    qkv = torch.randn(B * T, 3 * H * hd, generator=g).to(torch.bfloat16).to(cuda)
+    out_tc, lse_tc = ops.attention_fwd(qkv, B, T, H, hd)
+    out_mma, lse_mma = ops.attention_fwd(qkv, B, T, H, hd, workspace=False)
+    assert _rel(out_tc.float(), out_mma.float()) < 1e-2
+    assert torch.allclose(lse_tc, lse_mma, atol=2e-3, rtol=1e-3)
 
 
 def _rope_ref(x, B, T, H, hd, theta=10000.0):
