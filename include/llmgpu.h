@@ -198,12 +198,14 @@ int llmgpu_last_launches(const llmgpu_ctx* ctx);
  * src/trainer.cpp:171-182); this bound replaces the wait a blocking collective would do. */
 int llmgpu_set_comm_timeout(llmgpu_ctx* ctx, double seconds);
 
-/* Data parallel: ends the communicator between steps, after a rank has learned on the host
- * that a peer is gone (PeerWatch in the Python binding). Waits (bounded by the collective
- * timeout) for this rank's work in flight, then aborts the communicator; later steps return
- * LLMGPU_E_NCCL at once, without launching; parameters and checkpoints stay readable.
- * Returns 0, or LLMGPU_E_NCCL if the work in flight did not finish (it is aborted anyway).
- * No-op on a single-process context. */
+/* Data parallel: ends the use of the communicator between steps, after a rank has learned on
+ * the host that a peer is gone (PeerWatch in the Python binding). Waits (bounded by the
+ * collective timeout) for this rank's work in flight, then lets go of the communicator
+ * without a teardown that would wait on the missing peer (its resources are freed when the
+ * process exits); later steps return LLMGPU_E_NCCL at once, without launching; parameters
+ * and checkpoints stay readable and llmgpu_destroy returns. Returns 0, or LLMGPU_E_NCCL if
+ * the work in flight did not finish (the communicator is then aborted). No-op on a
+ * single-process context. */
 int llmgpu_abort_comm(llmgpu_ctx* ctx);
 
 /* Executes steps as a captured CUDA graph when enable != 0 (default 1). */

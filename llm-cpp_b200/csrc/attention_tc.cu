@@ -49,6 +49,14 @@ struct Smem {
 };
 constexpr size_t kSmemBytes = 1024 + Smem::TOTAL;
 
+// The n-th work item of this CTA in a persistent walk over items sorted longest first: rows
+// of gridDim.x items, taken left to right in even rows and right to left in odd ones, which
+// evens out the CTAs' totals (a plain stride gives the low CTAs the longest item of every row).
+__device__ __forceinline__ int snake_item(int n) {
+    const int g = (int)gridDim.x, b = (int)blockIdx.x;
+    return n * g + ((n & 1) ? g - 1 - b : b);
+}
+
 // Bounded wait by every lane of a warp with a warp-uniform result, so that the warp-collective
 // TMEM instructions after it are never reached by only part of the warp.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
@@ -474,7 +482,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             // ---------------- TMA producer: K, V of each item, then Q, dO, lse, D per tile
             bool ok = true;
             int g = 0;
-            for (int it = blockIdx.x, n = 0; it < items && ok; it += gridDim.x, ++n) {
+            for (int n = 0, it = snake_item(0); it < items && ok; ++n, it = snake_item(n)) {
                 const BwdItem w = bwd_item(it, H, B);
                 const int kt = w.tile, ns = nqb - kt, fb = n & 1;
                 if (!mbar_wait_bounded(&k.fix_empty[fb], ((n >> 1) & 1) ^ 1u, err,
@@ -535,14 +543,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 return true;
             };
             // walk the tiles: (n, s) of tile g, and of tile g + 1
-            int it = blockIdx.x, n = 0, s = 0;
+            int it = snake_item(0), n = 0, s = 0;
             int ns = it < items ? nqb - bwd_item(it, H, B).tile : 0;
             if (it < items) ok = issue_sdp(0, 0, 0, ns);
             for (int g = 0; it < items && ok; ++g) {
                 int it1 = it, n1 = n, s1 = s + 1, ns1 = ns;
                 if (s1 == ns) {
-                    it1 = it + gridDim.x;
                     n1 = n + 1;
+                    it1 = snake_item(n1);
                     s1 = 0;
                     ns1 = it1 < items ? nqb - bwd_item(it1, H, B).tile : 0;
                 }
@@ -585,7 +593,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
         bool ok = true;
         int g = 0;
-        for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+        for (int n = 0, it = snake_item(0); it < items && ok; it = snake_item(++n)) {
             const BwdItem w = bwd_item(it, H, B);
             const int kt = w.tile, ns = nqb - kt;
             const int key = kt * kRows + kr;
@@ -744,7 +752,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
         if (lane == 0) {
             bool ok = true;
             int g = 0;
-            for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+            for (int n = 0, it = snake_item(0); it < items && ok; it = snake_item(++n)) {
                 const BwdItem w = bwd_item(it, H, B);
                 const int qt = nqb - 1 - w.tile;
                 const int z0 = (w.b * H + w.h) * ntiles + ds_tile(qt, 0);
@@ -769,7 +777,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
             const uint32_t idesc = make_idesc_bf16(kRows, kHD, 1, 1);
             bool ok = true;
             int g = 0;
-            for (int it = blockIdx.x, n = 0; it < items && ok; it += gridDim.x, ++n) {
+            for (int n = 0, it = snake_item(0); it < items && ok; ++n, it = snake_item(n)) {
                 const int qt = nqb - 1 - bwd_item(it, H, B).tile;
                 const int acc = n & 1;
                 if (!mbar_wait_bounded(&acc_empty[acc], ((n >> 1) & 1) ^ 1u, err,
@@ -802,7 +810,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
         // ---------------- warps 2-5: TMEM lane quarter warp % 4, one query row per thread
         const int lq = warp & 3;
         const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
-        for (int it = blockIdx.x, n = 0; it < items; it += gridDim.x, ++n) {
+        for (int n = 0, it = snake_item(0); it < items; ++n, it = snake_item(n)) {
             const BwdItem w = bwd_item(it, H, B);
             const int qt = nqb - 1 - w.tile;
             const int acc = n & 1;

@@ -582,8 +582,12 @@ int llmgpu_abort_comm(llmgpu_ctx* h) {
     int rc = wait_stream(c, c->stream);  // aborts by itself if the wait runs out
     if (rc == 0 && c->comm) rc = wait_stream(c, c->comm);
     if (c->nccl) {
-        abort_comm(c);
-        c->err = "communicator aborted on request (a peer rank is gone)";
+        // Nothing of this rank is in flight, so no kernel needs the communicator's abort to
+        // return; its teardown would talk to the peer that is gone (on 2 x B200 the abort did
+        // not return within minutes). The context lets go of it; the process's exit frees it.
+        c->nccl = nullptr;
+        c->comm_failed = true;
+        c->err = "communicator released on request (a peer rank is gone)";
     }
     return rc ? LLMGPU_E_NCCL : 0;
 }

@@ -55,11 +55,11 @@ def test_embedding_backward_repeated_ids(cuda, C, accumulate_wpe):
 
 
 @pytest.mark.parametrize("rms", [False, True])
-@pytest.mark.parametrize("C", [128, 768, 1024])
-def test_norm_forward_backward(cuda, rms, C):
+@pytest.mark.parametrize("C,rows", [(128, 300), (768, 300), (1024, 300),
+                                    (768, 8192)])  # the GPT-2-small step's 8 x 1024 rows
+def test_norm_forward_backward(cuda, rms, C, rows):
     from llmgpu import ops
-    g = torch.Generator().manual_seed(C + rms)
-    rows = 300
+    g = torch.Generator().manual_seed(C + rms + rows)
     x = (torch.randn(rows, C, generator=g) * 2 + 0.5).to(cuda)
     gamma = (1 + 0.1 * torch.randn(C, generator=g)).to(cuda)
     beta = (0.1 * torch.randn(C, generator=g)).to(cuda)
