@@ -36,9 +36,11 @@ int norm_forward(const float* x, const float* gamma, const float* beta, bf16* y,
 // (dx_f32) and bf16 (dx_bf16, may be null). Per-CTA partial column sums are written to
 // `partial` [gridDim][3][C]: dgamma, dbeta, and the column sum of dx (used for the FFN
 // output-bias gradient of the block below). Returns the number of partial rows via *nparts.
+// A copy wait that gave up sets *err (when given) to kDevTimeoutFull.
 int norm_backward(const float* dy, const float* x, const float* gamma, const float* mean,
                   const float* rstd, const float* resid_in, float* dx_f32, bf16* dx_bf16,
-                  float* partial, int rows, int C, int rms, int* nparts, cudaStream_t s);
+                  float* partial, int rows, int C, int rms, int* nparts, cudaStream_t s,
+                  int* err = nullptr);
 int norm_backward_grid(int rows);
 // out[j*C + c] (+)= sum_p partial[p][j][c] for the selected planes j (mask bit j set), out
 // pointers per plane (null = skip).

@@ -1045,7 +1045,7 @@ int mamba_backward_layer(Ctx* c, int l, int B, int T, int acc) {
     // norm backward + residual (src/mamba.cpp:397-412); updates c->dres in place
     int nparts = 0;
     KC(norm_backward(c->dln, a.x, pp(b.norm_w), a.mean1, a.rstd1, c->dres, c->dres, c->dres16,
-                     c->partial, BT, C, rms, &nparts, s));
+                     c->partial, BT, C, rms, &nparts, s, c->d_err));
     KC(reduce_partials(c->partial, nparts, C, gp(b.norm_w), nullptr, nullptr, acc, s));
     return 0;
 }
@@ -1292,7 +1292,7 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
     }
     int nparts = 0;
     KC(norm_backward(c->dln, c->xL, pp(c->i_lnfg), c->meanf, c->rstdf, nullptr, c->dres,
-                     c->dres16, c->partial, BT, C, rms, &nparts, s));
+                     c->dres16, c->partial, BT, C, rms, &nparts, s, c->d_err));
     KC(reduce_partials(c->partial, nparts, C, gp(c->i_lnfg), rms ? nullptr : gp(c->i_lnfb),
                        c->blocks[L - 1].b2 >= 0 ? gp(c->blocks[L - 1].b2) : nullptr, acc, s));
     for (int l = L - 1; l >= 0; --l) {
@@ -1351,7 +1351,7 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
             KC(colsum_bf16(c->dh, F, BT, F, gp(b.b1), acc, c->colwork, s));
         }
         KC(norm_backward(c->dln, a.y, pp(b.ln2g), a.mean2, a.rstd2, c->dres, c->dy, c->dy16,
-                         c->partial, BT, C, rms, &nparts, s));
+                         c->partial, BT, C, rms, &nparts, s, c->d_err));
         KC(reduce_partials(c->partial, nparts, C, gp(b.ln2g), rms ? nullptr : gp(b.ln2b), nullptr,
                            acc, s));
         // ---- attention  (src/attention.cpp:183-363)
@@ -1381,7 +1381,7 @@ int run_fwd_bwd(Ctx* c, int B, int T, int accumulate, bool backward, bool reduce
                                      epi_args(kEpiStoreF32, c->dln, C), 1})))
             return rc;
         KC(norm_backward(c->dln, a.x, pp(b.ln1g), a.mean1, a.rstd1, c->dy, c->dres, c->dres16,
-                         c->partial, BT, C, rms, &nparts, s));
+                         c->partial, BT, C, rms, &nparts, s, c->d_err));
         KC(reduce_partials(c->partial, nparts, C, gp(b.ln1g), rms ? nullptr : gp(b.ln1b),
                            (l > 0 && c->blocks[l - 1].b2 >= 0) ? gp(c->blocks[l - 1].b2) : nullptr,
                            acc, s));

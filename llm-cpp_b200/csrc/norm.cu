@@ -1,5 +1,8 @@
-// LayerNorm / RMSNorm forward and backward (warp per row, 128-bit loads), deterministic
-// two-stage column reductions for the norm-parameter and bias gradients.
+// LayerNorm / RMSNorm forward (warp per row, 128-bit loads) and backward (rows streamed
+// through a shared-memory ring by bulk copies up to 1024 columns, warp per row above),
+// deterministic two-stage column reductions for the norm-parameter and bias gradients.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -183,6 +186,170 @@ __global__ void __launch_bounds__(256) norm_bwd_kernel(
     }
 }
 
+// The same backward with its inputs streamed through a ring of shared-memory stages by bulk
+// copies: one CTA per SM, a stage holds a group of 8 consecutive rows of dy, x and the
+// incoming residual gradient (three contiguous copies), and up to kNbStages - 1 groups are
+// in flight while the 8 warps work on the current one (a warp per row). The per-row work
+// alone kept too few bytes in flight to cover DRAM latency. Column partial sums stay in
+// registers across the CTA's rows (a lane owns fixed 4-column groups) and meet once, in
+// warp order, at the end: partial[blockIdx.x][3][C], the layout of norm_bwd_kernel.
+// dx may alias resid_in: a row is read (copied) before it is written, by the same CTA.
+constexpr int kNbStages = 4;
+constexpr int kNbRows = 8;  // rows per group = warps per CTA
+
+template <int MAXV>
+__global__ void __launch_bounds__(256, 1) norm_bwd_ring_kernel(
+    const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ gamma,
+    const float* __restrict__ mean, const float* __restrict__ rstd, const float* resid_in,
+    float* dx_f32, bf16* __restrict__ dx_bf16, float* __restrict__ partial, int rows, int C,
+    int rms, int nstages, int* err) {
+    pdl_enter();
+    extern __shared__ __align__(128) uint8_t nb_smem[];  // nstages x [3][8][C] floats
+    __shared__ __align__(8) uint64_t bar[kNbStages];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nv = C >> 2;
+    const int ngroups = (rows + kNbRows - 1) / kNbRows;
+    const size_t plane = (size_t)kNbRows * C;  // floats of one tensor in a stage
+    float* stages = reinterpret_cast<float*>(nb_smem);
+    const bool has_resid = resid_in != nullptr;
+    auto issue = [&](int g, int st) {  // thread 0: copy group g into stage st
+        const int r0 = g * kNbRows;
+        const int nr = min(kNbRows, rows - r0);
+        const uint32_t bytes = (uint32_t)nr * (uint32_t)C * 4u;
+        float* dst = stages + (size_t)st * 3 * plane;
+        mbar_arrive_expect_tx(&bar[st], bytes * (has_resid ? 3u : 2u));
+        bulk_load_g2s(dst, dy + (size_t)r0 * C, bytes, &bar[st]);
+        bulk_load_g2s(dst + plane, x + (size_t)r0 * C, bytes, &bar[st]);
+        if (has_resid) bulk_load_g2s(dst + 2 * plane, resid_in + (size_t)r0 * C, bytes, &bar[st]);
+    };
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < nstages; ++s) mbar_init(&bar[s], 1);
+        fence_barrier_init();
+        for (int j = 0, g = blockIdx.x; j < nstages && g < ngroups; ++j, g += gridDim.x)
+            issue(g, j);
+    }
+    float4 gv[MAXV], pg[MAXV], pb[MAXV], po[MAXV];
+    const float4* g4 = reinterpret_cast<const float4*>(gamma);
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int idx = lane + i * 32;
+        gv[i] = idx < nv ? g4[idx] : make_float4(0.f, 0.f, 0.f, 0.f);
+        pg[i] = pb[i] = po[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    __syncthreads();
+    const float invC = 1.0f / (float)C;
+    int st = 0;
+    uint32_t phase = 0;
+    for (int g = blockIdx.x; g < ngroups; g += gridDim.x) {
+        const int row = g * kNbRows + warp;
+        float mu = 0.f, r = 0.f;
+        if (row < rows) {
+            mu = mean[row];
+            r = rstd[row];
+        }
+        mbar_wait_bounded(&bar[st], phase, err, kDevTimeoutFull);
+        if (row < rows) {
+            const float* base = stages + (size_t)st * 3 * plane + (size_t)warp * C;
+            const float4* sd = reinterpret_cast<const float4*>(base);
+            const float4* sx = reinterpret_cast<const float4*>(base + plane);
+            const float4* sr = reinterpret_cast<const float4*>(base + 2 * plane);
+            float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+            for (int i = 0; i < MAXV; ++i) {
+                const int idx = lane + i * 32;
+                if (idx < nv) {
+                    const float4 d = sd[idx], xv = sx[idx], g = gv[i];
+                    const float gx = d.x * g.x, gy = d.y * g.y, gz = d.z * g.z, gw = d.w * g.w;
+                    if (!rms) {
+                        s1 += gx + gy + gz + gw;
+                        s2 += gx * (xv.x - mu) * r + gy * (xv.y - mu) * r +
+                              gz * (xv.z - mu) * r + gw * (xv.w - mu) * r;
+                    } else {
+                        s2 += gx * xv.x + gy * xv.y + gz * xv.z + gw * xv.w;
+                    }
+                }
+            }
+            s1 = warp_sum(s1);
+            s2 = warp_sum(s2);
+            const float m1 = s1 * invC, m2 = s2 * invC;
+            const float coef = rms ? s2 * r * r * r * invC : 0.f;
+            float4* o32 = reinterpret_cast<float4*>(dx_f32 + (size_t)row * C);
+            uint2* o16 = dx_bf16 ? reinterpret_cast<uint2*>(dx_bf16 + (size_t)row * C) : nullptr;
+#pragma unroll
+            for (int i = 0; i < MAXV; ++i) {
+                const int idx = lane + i * 32;
+                if (idx < nv) {
+                    const float4 d4 = sd[idx], x4 = sx[idx], g4v = gv[i];
+                    const float4 r4 = has_resid ? sr[idx] : make_float4(0.f, 0.f, 0.f, 0.f);
+                    const float dd[4] = {d4.x, d4.y, d4.z, d4.w};
+                    const float xx[4] = {x4.x, x4.y, x4.z, x4.w};
+                    const float gg[4] = {g4v.x, g4v.y, g4v.z, g4v.w};
+                    const float rr[4] = {r4.x, r4.y, r4.z, r4.w};
+                    float o[4], xh[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        xh[k] = (xx[k] - mu) * r;
+                        if (!rms)
+                            o[k] = r * (dd[k] * gg[k] - m1 - xh[k] * m2);
+                        else
+                            o[k] = dd[k] * gg[k] * r - xx[k] * coef;
+                        o[k] += rr[k];
+                    }
+                    o32[idx] = make_float4(o[0], o[1], o[2], o[3]);
+                    if (o16) o16[idx] = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+                    pg[i].x += dd[0] * xh[0];
+                    pg[i].y += dd[1] * xh[1];
+                    pg[i].z += dd[2] * xh[2];
+                    pg[i].w += dd[3] * xh[3];
+                    pb[i].x += dd[0];
+                    pb[i].y += dd[1];
+                    pb[i].z += dd[2];
+                    pb[i].w += dd[3];
+                    po[i].x += o[0];
+                    po[i].y += o[1];
+                    po[i].z += o[2];
+                    po[i].w += o[3];
+                }
+            }
+        }
+        __syncthreads();  // every warp is done with this stage
+        if (threadIdx.x == 0) {
+            const int gn = g + nstages * gridDim.x;
+            if (gn < ngroups) issue(gn, st);
+        }
+        if (++st == nstages) {
+            st = 0;
+            phase ^= 1u;
+        }
+    }
+    // Every copy issued was waited for: the stages are free for the CTA reduction,
+    // [8 warps][3][C] floats (one stage's size).
+    float4* red = reinterpret_cast<float4*>(stages);
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int idx = lane + i * 32;
+        if (idx < nv) {
+            red[(warp * 3 + 0) * nv + idx] = pg[i];
+            red[(warp * 3 + 1) * nv + idx] = pb[i];
+            red[(warp * 3 + 2) * nv + idx] = po[i];
+        }
+    }
+    __syncthreads();
+    float4* out = reinterpret_cast<float4*>(partial + (size_t)blockIdx.x * 3 * C);
+    for (int i = threadIdx.x; i < 3 * nv; i += blockDim.x) {
+        const int p = i / nv, c = i - p * nv;
+        float4 acc = red[p * nv + c];
+        for (int w = 1; w < kNbRows; ++w) {
+            const float4 v = red[(w * 3 + p) * nv + c];
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        out[i] = acc;  // i = p * nv + c: plane p, columns 4c..4c+3
+    }
+}
+
 // Sums nparts partial rows of C floats: out_y[c] = sum_p part[p * pstride + y * plane_off + c]
 // for planes y = blockIdx.y (a null output skips its plane). A block is 32 columns x 32 part
 // groups; group g adds parts g, g + 32, ... in order with four loads in flight, then the 32
@@ -275,6 +442,16 @@ __global__ void colsum_stage1(const bf16* __restrict__ a, long long lda, int row
 
 }  // namespace
 
+namespace {
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+int sm_count() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+}  // namespace
+
 int norm_forward(const float* x, const float* gamma, const float* beta, bf16* y, float* mean,
                  float* rstd, int rows, int C, int rms, cudaStream_t s) {
     if ((C & 3) != 0 || rows <= 0) return -1;
@@ -297,8 +474,48 @@ int norm_backward_grid(int rows) {
 
 int norm_backward(const float* dy, const float* x, const float* gamma, const float* mean,
                   const float* rstd, const float* resid_in, float* dx_f32, bf16* dx_bf16,
-                  float* partial, int rows, int C, int rms, int* nparts, cudaStream_t s) {
+                  float* partial, int rows, int C, int rms, int* nparts, cudaStream_t s,
+                  int* err) {
     if ((C & 3) != 0 || rows <= 0 || C > 2048) return -1;
+    // The ring kernel, where at least two stages of 8 rows fit in shared memory and every
+    // bulk-copy source is 16-byte aligned (rows start at multiples of 16 bytes as C % 4 == 0).
+    constexpr size_t kRingSmem = 226 * 1024;
+    const size_t stage_bytes = 3 * (size_t)kNbRows * C * sizeof(float);
+    const int nstages = (int)std::min<size_t>(kNbStages, kRingSmem / stage_bytes);
+    if (C <= 1024 && nstages >= 2 && aligned16(dy) && aligned16(x) &&
+        (!resid_in || aligned16(resid_in)) && aligned16(dx_f32) && aligned16(gamma)) {
+        static bool ring_set = false;
+        if (!ring_set) {
+            const int mx = (int)kRingSmem;
+            cudaFuncSetAttribute(norm_bwd_ring_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+            cudaFuncSetAttribute(norm_bwd_ring_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+            cudaFuncSetAttribute(norm_bwd_ring_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+            cudaFuncSetAttribute(norm_bwd_ring_kernel<6>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+            cudaFuncSetAttribute(norm_bwd_ring_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+            ring_set = true;
+        }
+        const int ngroups = (rows + kNbRows - 1) / kNbRows;
+        const int grid = std::min(sm_count(), ngroups);  // never above norm_backward_grid(rows)
+        // groups per CTA bound the stages; one stage still holds the final [8][3][C] sums
+        const int nst = std::min(nstages, (ngroups + grid - 1) / grid);
+        const size_t smem = (size_t)nst * stage_bytes;
+        if (nparts) *nparts = grid;
+#define NR_LAUNCH(MV)                                                                          \
+    launch_kernel(norm_bwd_ring_kernel<MV>, grid, 256, smem, s, dy, x, gamma, mean, rstd,      \
+                  resid_in, dx_f32, dx_bf16, partial, rows, C, rms, nst, err)
+        if (C <= 128)
+            NR_LAUNCH(1);
+        else if (C <= 256)
+            NR_LAUNCH(2);
+        else if (C <= 512)
+            NR_LAUNCH(4);
+        else if (C <= 768)
+            NR_LAUNCH(6);
+        else
+            NR_LAUNCH(8);
+#undef NR_LAUNCH
+        return launch_status();
+    }
     const int grid = norm_backward_grid(rows);
     const size_t smem = 8 * 3 * (size_t)C * sizeof(float);
     if (nparts) *nparts = grid;

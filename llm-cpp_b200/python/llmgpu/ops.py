@@ -96,10 +96,11 @@ def norm_fwd(x, gamma, beta, rms=False):
     return y, mean, rstd
 
 
-def norm_bwd(dy, x, gamma, mean, rstd, resid=None, rms=False):
+def norm_bwd(dy, x, gamma, mean, rstd, resid=None, rms=False, out=None):
+    """dx = resid + the norm's input gradient; `out` (may be `resid` itself) receives dx."""
     lib = load()
     rows, C = x.shape
-    dx = torch.empty_like(x)
+    dx = torch.empty_like(x) if out is None else out
     dx16 = torch.empty(rows, C, dtype=torch.bfloat16, device=x.device)
     dg, db, ds = (torch.empty(C, device=x.device) for _ in range(3))
     work = torch.empty(int(lib.llmgpu_op_norm_bwd_work(rows, C)), device=x.device)

@@ -86,6 +86,38 @@ def test_norm_forward_backward(cuda, rms, C, rows):
     assert _rel(ds, want_dx.sum(0)) < 1e-5
 
 
+@pytest.mark.parametrize("C,rows,form", [
+    (64, 77, "none"), (512, 1001, "inplace"), (768, 8192, "inplace"), (768, 8192, "none"),
+    (1024, 2049, "none"), (2048, 300, "inplace"), (1536, 600, "plain")])
+def test_norm_backward_forms(cuda, C, rows, form):
+    """The backward without an incoming residual gradient (the final norm), with dx written
+    over the residual gradient it reads (the Mamba block), ragged last 8-row groups, and
+    widths on both kernels (up to 1024 columns the shared-memory ring, above it the
+    per-warp kernel)."""
+    from llmgpu import ops
+    g = torch.Generator().manual_seed(C * 7 + rows)
+    x = (torch.randn(rows, C, generator=g) * 1.5 - 0.25).to(cuda)
+    gamma = (1 + 0.1 * torch.randn(C, generator=g)).to(cuda)
+    beta = (0.1 * torch.randn(C, generator=g)).to(cuda)
+    _, mean, rstd = ops.norm_fwd(x, gamma, beta, False)
+    dy = torch.randn(rows, C, generator=g).to(cuda)
+    resid = None if form == "none" else torch.randn(rows, C, generator=g).to(cuda)
+    resid0 = None if resid is None else resid.clone()
+    out = resid if form == "inplace" else None
+    dx, _, dg, db, ds = ops.norm_bwd(dy, x, gamma, mean, rstd, resid, False, out=out)
+    xd = x.double().requires_grad_(True)
+    mu = xd.mean(-1, keepdim=True)
+    xh = (xd - mu) / torch.sqrt(((xd - mu) ** 2).mean(-1, keepdim=True) + 1e-5)
+    (xh * gamma.double() + beta.double()).backward(dy.double())
+    want_dx = xd.grad + (0 if resid0 is None else resid0.double())
+    if form == "inplace":
+        assert dx.data_ptr() == resid.data_ptr()
+    assert _rel(dx, want_dx) < 1e-5
+    assert _rel(dg, (dy.double() * xh.detach()).sum(0)) < 1e-5
+    assert _rel(db, dy.double().sum(0)) < 1e-5
+    assert _rel(ds, want_dx.sum(0)) < 1e-5
+
+
 # rows above the grid run several rows per CTA; a row wider than 110 KB (60032 bf16) runs
 # one CTA per SM instead of two; label smoothing per src/loss.cpp:26-40
 @pytest.mark.parametrize("V,Vp,rows,smoothing", [
