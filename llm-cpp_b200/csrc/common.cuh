@@ -22,6 +22,7 @@ enum DeviceError : int {
     kDevTimeoutAcc = 3,       // epilogue waited too long for the accumulator
     kDevTimeoutAccFree = 4,   // MMA warp waited too long for a drained accumulator
     kDevBadShape = 5,
+    kDevTimeoutItem = 6,      // a GEMM role waited too long for its next work item
 };
 
 // Maximum time a device-side wait may spin before reporting an error (ns).
@@ -311,6 +312,10 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t cta_addr, uint32_t rank
 // All threads of both CTAs; divergent arrival allowed (no .aligned).
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// 32-bit store to shared memory of a CTA of this cluster (address from mapa_shared).
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)

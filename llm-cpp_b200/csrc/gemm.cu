@@ -797,6 +797,15 @@ __device__ __forceinline__ uint32_t pair_stage_bytes(const GemmArgs& a, int am, 
 // other's results). With NG = 1 cluster c takes tiles c, c + clusters, ...; with NG = 2 the
 // host's per-cluster lists in `sched` ([cluster][stride]: count, then items g << 24 | tile)
 // balance the two products' tiles over the pairs.
+//
+// With `queue` set (NG = 2), the units are handed out at run time instead: the leader CTA's
+// producer claims the next unit from queue[0] a few k-blocks before its current tile's loads
+// end and publishes it through a ring of kItemSlots slots in both CTAs' shared memory, and
+// every other role of the pair takes the units from the ring in the same order. Units are
+// numbered longest first: all units of product q_first, then those of the other product
+// (split-major tile order within a product). A pair whose SMs start late, held by another
+// kernel such as a collective, takes fewer units. queue[1] counts the pairs that have
+// finished claiming; the last one resets both counters for the next launch.
 template <int NG>
 struct PairParams {
     CUtensorMap tmA[NG];
@@ -806,6 +815,70 @@ struct PairParams {
     GemmArgs args[NG];
     const int* sched;
     int sched_stride;
+    int* queue;
+    int q_first;
+    int q_total[2];
+};
+
+constexpr int kItemSlots = 4;
+// roles that take each unit from the ring: the leader's MMA issuer and the follower's
+// producer, and every epilogue warp of both CTAs
+constexpr int kItemConsumers = 2 + 2 * kPairEpiWarps;
+// k-blocks before the end of a tile's loads at which the leader claims its next unit (the
+// claim's round trip to L2 overlaps these loads)
+constexpr int kClaimAhead = 4;
+
+// Unit number idx of the run-time queue as (product << 24 | tile), -1 past the last one.
+template <int NG>
+__device__ __forceinline__ int pair_queue_unit(const PairParams<NG>& P, int idx) {
+    const int f = P.q_first, n0 = P.q_total[f];
+    if (idx < n0) return (f << 24) | idx;
+    idx -= n0;
+    return idx < P.q_total[f ^ 1] ? (((f ^ 1) << 24) | idx) : -1;
+}
+
+// One role's view of the unit ring. Slot s of the ring carries units s, s + kItemSlots, ...;
+// `full` (one per slot, in each CTA) completes when the leader's producer has written the
+// slot in both CTAs, `empty` (one per slot, in the leader CTA) when all kItemConsumers roles
+// have read it.
+struct PairRing {
+    uint64_t* full;
+    uint64_t* empty;
+    int* slot;
+    uint32_t rank;
+    int i;
+    // A consumer's next unit; -1 when the list has ended or the wait gave up (error set).
+    // With warp_wide, all 32 lanes take the unit and lane 0 releases the slot.
+    __device__ __forceinline__ int take(int* err, bool warp_wide) {
+        const int s = i % kItemSlots;
+        const uint32_t parity = (uint32_t)(i / kItemSlots) & 1u;
+        ++i;
+        if (!mbar_wait_bounded_cluster(&full[s], parity, err, kDevTimeoutItem)) return -1;
+        const int v = *reinterpret_cast<volatile int*>(&slot[s]);
+        if (warp_wide) __syncwarp();
+        if (!warp_wide || (threadIdx.x & 31) == 0) {
+            if (rank == 0)
+                mbar_arrive(&empty[s]);
+            else
+                mbar_arrive_cluster(mapa_shared(smem_u32(&empty[s]), 0));
+        }
+        return v;
+    }
+    // The leader producer publishes unit v (-1 ends every role's list) once the slot's
+    // previous unit has been read by every consumer.
+    __device__ __forceinline__ bool put(int v, int* err) {
+        const int s = i % kItemSlots;
+        if (i >= kItemSlots &&
+            !mbar_wait_bounded(&empty[s], (uint32_t)(i / kItemSlots - 1) & 1u, err,
+                               kDevTimeoutItem))
+            return false;
+        ++i;
+        slot[s] = v;
+        st_shared_cluster_u32(mapa_shared(smem_u32(&slot[s]), 1), (uint32_t)v);
+        mbar_arrive(&full[s]);
+        mbar_arrive_cluster(mapa_shared(smem_u32(&full[s]), 1));
+        return true;
+    }
 };
 
 // Tile geometry of one product on 256 x 256 pair tiles.
@@ -890,11 +963,20 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const int cid = blockIdx.x >> 1;
     const int nclusters = gridDim.x >> 1;
     int* const err = P.args[0].err;
+    // run-time unit queue (dual launches): ring barriers [full x kItemSlots, empty x
+    // kItemSlots] and slots
+    const bool dyn = NG == 2 && P.queue != nullptr;
+    __shared__ __align__(8) uint64_t s_item_bar[2 * kItemSlots];
+    __shared__ int s_item[kItemSlots];
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < kItemSlots; ++s) {
+            mbar_init(&s_item_bar[s], 1);
+            mbar_init(&s_item_bar[kItemSlots + s], kItemConsumers);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&acc_full[i], 1);
@@ -933,7 +1015,24 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             bool ok = true;
             int g, t;
             PairItems<NG> items(P, cid, nclusters);
-            while (ok && items.get(g, t)) {
+            PairRing ring{s_item_bar, s_item_bar + kItemSlots, s_item, rank, 0};
+            const bool claimer = dyn && leader;
+            int pending = claimer ? atomicAdd(P.queue, 1) : 0;  // the leader's next unit
+            while (ok) {
+                if (dyn) {
+                    int v;
+                    if (leader) {
+                        v = pair_queue_unit(P, pending);
+                        if (!ring.put(v, err)) break;
+                    } else {
+                        v = ring.take(err, false);
+                    }
+                    if (v < 0) break;
+                    g = v >> 24;
+                    t = v & 0xffffff;
+                } else if (!items.get(g, t)) {
+                    break;
+                }
                 const GemmArgs& args = P.args[g];
                 const PairShape sh = pair_shape(args);
                 const CUtensorMap* tmA = &P.tmA[g];
@@ -947,7 +1046,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
                 const uint32_t all_bytes = leader ? pair_stage_bytes(args, m0, n0) +
                                                         pair_stage_bytes(args, m0 + 128, n0 + Cfg::BNH)
                                                   : 0u;
+                const int claim_at = kb1 - kClaimAhead > kb0 ? kb1 - kClaimAhead : kb0;
+                if (claimer && kb1 <= kb0) pending = atomicAdd(P.queue, 1);
                 for (int kb = kb0; kb < kb1; ++kb) {
+                    if (claimer && kb == claim_at) pending = atomicAdd(P.queue, 1);
                     if (!mbar_wait_bounded_cluster(&empty[stage], phase ^ 1u, err,
                                                    kDevTimeoutEmpty)) {
                         ok = false;
@@ -976,6 +1078,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
                     }
                 }
             }
+            // the last pair to finish claiming resets the counters for the next launch
+            if (claimer && atomicAdd(P.queue + 1, 1) == nclusters - 1) {
+                atomicExch(P.queue, 0);
+                atomicExch(P.queue + 1, 0);
+            }
             if (!ok) spin_ns(100000);  // error path: let copies in flight land first
         }
     } else if (warp == 1) {
@@ -989,7 +1096,16 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             bool ok = true;
             int g, t;
             PairItems<NG> items(P, cid, nclusters);
-            while (ok && items.get(g, t)) {
+            PairRing ring{s_item_bar, s_item_bar + kItemSlots, s_item, rank, 0};
+            while (ok) {
+                if (dyn) {
+                    const int v = ring.take(err, false);
+                    if (v < 0) break;
+                    g = v >> 24;
+                    t = v & 0xffffff;
+                } else if (!items.get(g, t)) {
+                    break;
+                }
                 const GemmArgs& args = P.args[g];
                 const PairShape sh = pair_shape(args);
                 const uint32_t idesc =
@@ -1050,7 +1166,16 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         uint32_t acc_phase = 0;
         int g, t;
         PairItems<NG> items(P, cid, nclusters);
-        while (items.get(g, t)) {
+        PairRing ring{s_item_bar, s_item_bar + kItemSlots, s_item, rank, 0};
+        while (true) {
+            if (dyn) {
+                const int v = ring.take(err, true);
+                if (v < 0) break;
+                g = v >> 24;
+                t = v & 0xffffff;
+            } else if (!items.get(g, t)) {
+                break;
+            }
             const GemmArgs& args = P.args[g];
             const PairShape sh = pair_shape(args);
             int m_blk, n_blk, split, gi, kb0, kb1;
@@ -1336,6 +1461,9 @@ int launch_pair(const GemmPlan& p, cudaStream_t stream) {
     P.args[0] = p.args;
     P.sched = nullptr;
     P.sched_stride = 0;
+    P.queue = nullptr;
+    P.q_first = 0;
+    P.q_total[0] = P.q_total[1] = 0;
     return launch_pair_params<1>(P, p.grid, stream);
 }
 
@@ -1500,8 +1628,19 @@ long long pair_lpt(std::vector<PairUnit>& units, int ncl, std::vector<std::vecto
 
 }  // namespace
 
+// LLMGPU_GEMM_QUEUE: "0" keeps every dual launch on the host's per-pair lists, "1" puts
+// every one on the run-time queue; unset, the caller decides.
+int pair_queue_override() {
+    static const int v = [] {
+        const char* e = getenv("LLMGPU_GEMM_QUEUE");
+        return (e && (e[0] == '0' || e[0] == '1')) ? e[0] - '0' : -1;
+    }();
+    return v;
+}
+
 int gemm_make_plan2(GemmPlan2* plan, const GemmPlan& p0, const GemmPlan& p1, int num_sms) {
     plan->sched = nullptr;
+    plan->queue = nullptr;
     const GemmPlan* ps[2] = {&p0, &p1};
     std::vector<PairUnit> units;
     for (int g = 0; g < 2; ++g) {
@@ -1513,11 +1652,18 @@ int gemm_make_plan2(GemmPlan2* plan, const GemmPlan& p0, const GemmPlan& p1, int
         pair_units(units, g, a.M, a.N, a.K, a.splits);
     }
     const int ncl = std::min<int>(pair_max_clusters(num_sms), (int)units.size());
+    // run-time queue order: the product with the longest units first
+    int qcost[2] = {0, 0}, qtotal[2] = {0, 0};
+    for (const PairUnit& u : units) {
+        qcost[u.g] = std::max(qcost[u.g], u.cost);
+        ++qtotal[u.g];
+    }
     std::vector<std::vector<int>> lists;
     pair_lpt(units, ncl, &lists);
     size_t stride = 1;
     for (const auto& l : lists) stride = std::max(stride, l.size() + 1);
-    std::vector<int> table((size_t)ncl * stride, 0);
+    // the per-pair lists, then the queue's two counters (zero between launches)
+    std::vector<int> table((size_t)ncl * stride + 2, 0);
     for (int c = 0; c < ncl; ++c) {
         table[(size_t)c * stride] = (int)lists[c].size();
         for (size_t i = 0; i < lists[c].size(); ++i) table[(size_t)c * stride + 1 + i] = lists[c][i];
@@ -1537,11 +1683,15 @@ int gemm_make_plan2(GemmPlan2* plan, const GemmPlan& p0, const GemmPlan& p1, int
     plan->p[1] = p1;
     plan->sched = d;
     plan->sched_stride = (int)stride;
+    plan->queue = d + (size_t)ncl * stride;
+    plan->q_first = qcost[1] > qcost[0] ? 1 : 0;
+    plan->q_total[0] = qtotal[0];
+    plan->q_total[1] = qtotal[1];
     plan->grid = 2 * ncl;
     return 0;
 }
 
-int gemm_run2(const GemmPlan2& plan, cudaStream_t stream) {
+int gemm_run2(const GemmPlan2& plan, cudaStream_t stream, bool queue) {
     PairParams<2> P;
     for (int g = 0; g < 2; ++g) {
         P.tmA[g] = plan.p[g].tmA;
@@ -1552,12 +1702,18 @@ int gemm_run2(const GemmPlan2& plan, cudaStream_t stream) {
     }
     P.sched = plan.sched;
     P.sched_stride = plan.sched_stride;
+    const int ov = pair_queue_override();
+    P.queue = (ov < 0 ? queue : ov == 1) ? plan.queue : nullptr;
+    P.q_first = plan.q_first;
+    P.q_total[0] = plan.q_total[0];
+    P.q_total[1] = plan.q_total[1];
     return launch_pair_params<2>(P, plan.grid, stream);
 }
 
 void gemm_free_plan2(GemmPlan2* plan) {
     if (plan->sched) cudaFree(plan->sched);
     plan->sched = nullptr;
+    plan->queue = nullptr;
 }
 
 int gemm_run(const GemmPlan& p, cudaStream_t stream) {

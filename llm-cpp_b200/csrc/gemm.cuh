@@ -106,9 +106,15 @@ struct GemmPlan2 {
     int grid;
     int* sched;
     int sched_stride;
+    int* queue;       // two device counters for the run-time unit queue (in the sched block)
+    int q_first;      // the product whose units are longest (handed out first)
+    int q_total[2];   // units of each product
 };
 int gemm_make_plan2(GemmPlan2* plan, const GemmPlan& p0, const GemmPlan& p1, int num_sms);
-int gemm_run2(const GemmPlan2& plan, cudaStream_t stream);
+// queue: hand the units out at run time (see PairParams) instead of the host's per-pair
+// lists. It pays where another kernel holds SMs during the launch (a data-parallel step's
+// all-reduce); LLMGPU_GEMM_QUEUE=0 or 1 overrides the caller's choice.
+int gemm_run2(const GemmPlan2& plan, cudaStream_t stream, bool queue);
 void gemm_free_plan2(GemmPlan2* plan);
 
 // Reduces split-K partials [splits][M][N] (fp32) into the final output with the
