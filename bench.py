@@ -34,6 +34,10 @@ CFG = dict(vocab_size=50257, n_layers=12, n_heads=12, n_embd=768, block_size=102
 B, T = 8, 1024
 HP = dict(lr=3e-4, b1=0.9, b2=0.95, eps=1e-8, wd=0.1)
 REF_T = 16          # tokens of the bounded CPU-reference sample (one sequence)
+# DRAM bytes read + written per GEMM launch of the GPT-2-small step, averaged over its 98
+# launches: one ncu capture of those launches (dram__bytes_read.sum + dram__bytes_write.sum,
+# cold caches) of `bench.py --steps 1 --warmup 1 --no-cpu-baseline`
+GEMM_TRAFFIC_BYTES = 107.6e6
 
 
 def algorithmic_flops_per_token(cfg=CFG, T=T):
@@ -352,7 +356,10 @@ def main():
                          "bound": "tensor", "achieved": gemm_tflops, "peak": peak_sus,
                          "unit": "TFLOP/s", "frac": gemm_tflops / peak_sus,
                          "peak_kind": f"{peak_kind} sustained bf16 (kernel timed inside a long step)",
-                         "traffic": None, "launches_per_step": glaunch / max(K, 1),
+                         "traffic": GEMM_TRAFFIC_BYTES if workload is None else None,
+                         "traffic_unit": "DRAM bytes read + written per GEMM launch, averaged "
+                                         "over the step's launches (one ncu capture, cold caches)",
+                         "launches_per_step": glaunch / max(K, 1),
                          "gemm_ms_per_step": gms / max(K, 1),
                          "flops_per_step": gflops / max(K, 1)},
             "phase_ms": timings,
