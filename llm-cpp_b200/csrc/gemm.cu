@@ -1245,6 +1245,58 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
     }
 }
 
+// The same reduction for a split count known at compile time: each thread takes two 4-column
+// groups per pass with all 2 x S plane loads issued before the first add (the planes are
+// summed in split order, as above).
+template <int S>
+__global__ void __launch_bounds__(256) splitk_reduce_s_kernel(
+    const float* __restrict__ part, int M, int N, float* __restrict__ out, long long ldo,
+    int col_group, long long group_stride, int accumulate) {
+    pdl_enter();
+    const long long total4 = (long long)M * N / 4;
+    const float4* p4 = reinterpret_cast<const float4*>(part);
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total4;
+         i += 2 * stride) {
+        const long long i2 = i + stride;
+        const bool two = i2 < total4;
+        float4 a[S], b[S];
+#pragma unroll
+        for (int k = 0; k < S; ++k) {
+            a[k] = p4[k * total4 + i];
+            if (two) b[k] = p4[k * total4 + i2];
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            if (h == 1 && !two) break;
+            const float4* v = h == 0 ? a : b;
+            float4 s = v[0];
+#pragma unroll
+            for (int k = 1; k < S; ++k) {
+                s.x += v[k].x;
+                s.y += v[k].y;
+                s.z += v[k].z;
+                s.w += v[k].w;
+            }
+            const long long e = (h == 0 ? i : i2) * 4;
+            const int m = (int)(e / N);
+            const int n = (int)(e - (long long)m * N);
+            const int g = n / col_group;
+            float* o = out + g * group_stride + m * ldo + (n - g * col_group);
+            if (accumulate) {
+                s.x += o[0];
+                s.y += o[1];
+                s.z += o[2];
+                s.w += o[3];
+            }
+            o[0] = s.x;
+            o[1] = s.y;
+            o[2] = s.z;
+            o[3] = s.w;
+        }
+    }
+}
+
 __global__ void splitk_reduce_scalar_kernel(const float* __restrict__ part, int splits, int M,
                                             int N, float* __restrict__ out, long long ldo,
                                             int col_group, long long group_stride,
@@ -1743,6 +1795,20 @@ int gemm_splitk_reduce(const float* partial, int splits, int M, int N, float* ou
     }
     long long total4 = (long long)M * N / 4;
     int threads = 256;
+    long long blocks2 = (total4 + 2 * threads - 1) / (2 * threads);
+    if (blocks2 > 148 * 8) blocks2 = 148 * 8;
+#define SR_LAUNCH(S)                                                                           \
+    launch_kernel(splitk_reduce_s_kernel<S>, (int)blocks2, threads, 0, stream, partial, M, N, \
+                  out, ldo, col_group, group_stride, accumulate)
+    switch (splits) {
+        case 2: SR_LAUNCH(2); return launch_status();
+        case 3: SR_LAUNCH(3); return launch_status();
+        case 4: SR_LAUNCH(4); return launch_status();
+        case 6: SR_LAUNCH(6); return launch_status();
+        case 8: SR_LAUNCH(8); return launch_status();
+        default: break;
+    }
+#undef SR_LAUNCH
     long long blocks = (total4 + threads - 1) / threads;
     if (blocks > 148 * 16) blocks = 148 * 16;
     launch_kernel(splitk_reduce_kernel, (int)blocks, threads, 0, stream, partial, splits, M, N, out, ldo,
