@@ -75,7 +75,8 @@ int llmgpu_op_norm_fwd(const float* x, const float* gamma, const float* beta, vo
                        float* mean, float* rstd, int rows, int C, int rms, void* stream);
 /* Norm backward (src/tensor.cpp:556-602 / :625-655): dx = resid + d/dx, written fp32 (and
  * bf16 if dx_bf16 != NULL); dgamma, dbeta (nullable) and the column sums of dx (nullable)
- * are written to their outputs. `work` must hold llmgpu_op_norm_bwd_work(rows, C) floats. */
+ * are written to their outputs. `work` must hold llmgpu_op_norm_bwd_work(rows, C) floats.
+ * dx may be resid itself (each row is read before it is written). */
 int llmgpu_op_norm_bwd(const float* dy, const float* x, const float* gamma, const float* mean,
                        const float* rstd, const float* resid, float* dx, void* dx_bf16,
                        float* dgamma, float* dbeta, float* dxsum, float* work, int rows, int C,
